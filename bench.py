@@ -1,0 +1,493 @@
+"""Benchmark of the fp32 GQA decode attention path on B200.
+
+Default workload (one line of JSON on rank 0): the 28-layer resident decode --
+per GPU one sequence, 28 layers of 12 q / 2 KV heads, d = 128, an fp32 KV cache
+of t_max = 4096 rows per layer (235 MB), and decode steps at positions
+3840..4095 (each step: RoPE + append + attention in all 28 layers; the window
+wraps after 256 steps).  A step is one replay of a CUDA graph holding the 28
+layer calls; inputs are resident in HBM.
+
+  value    KV-read GB/s: algorithmic K+V bytes (2048 B per attended row per
+           layer) of all ranks / max-over-ranks device time of the timed steps
+  e2e      the same metric through the C ABI with HOST buffers: each step
+           copies its 28 x 2048 fp32 q/k/v rows from pinned host memory,
+           replays the graph and copies the 28 x 1536 outputs back
+  roofline dominant kernel (decode_split_kernel) against the measured HBM peak
+  cpu_baseline  the reference's own CPU attention (oracle/_ref, compiled from
+           its sources) on this host's cores, on a bounded sample
+
+Multi-GPU (torchrun, one process per GPU): every rank decodes its own
+sequence (sharding by sequence, no collective on the data path); "scaling":
+"weak".  --impl reference runs the reference's CPU implementation instead
+(rank 0 only).  Other workloads (--workload batched|long|single) measure the
+remaining decode configurations.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "GQA decode attn: KV-read HBM GB/s (% of peak) and tok/s at 1/2/4/8 B200"
+N_Q, N_KV, D = 12, 2, 128
+ROW_BYTES = 2 * N_KV * D * 4  # K + V bytes of one attended position, all KV heads (2048)
+QKV_W, OUT_W = (N_Q + 2 * N_KV) * D, N_Q * D
+HBM_FALLBACK = 6650.0
+
+WORKLOADS = {
+    "resident28": dict(layers=28, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1),
+    "batched": dict(layers=1, seqs=64, len_lo=256, len_hi=8192, window=256),
+    "long": dict(layers=1, seqs=256, t_max=32768, window=64),
+    "single": dict(layers=1, t_max=512, pos_lo=511, pos_hi=512, seqs=1),
+}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK, "fallback"
+
+
+def profile_traffic(workload):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary."""
+    path = os.path.join(REPO, "profiles", f"traffic_{workload}.txt")
+    try:
+        vals = {}
+        for line in open(path):
+            if "=" in line and not line.startswith("#"):
+                k, v = line.split("=", 1)
+                vals[k.strip()] = v.strip()
+        return float(vals["bytes_per_launch"])
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML polling thread)
+# ---------------------------------------------------------------------------
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+            0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+            0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, device_index, period=0.002):
+        self.samples, self.reasons = [], 0
+        self.max_mhz = None
+        self.period = period
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report what we can
+            self._nv = None
+            self.error = str(e)
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self._nv:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        names = [n for b, n in _REASONS.items() if self.reasons & b and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus):
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    import torch
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU reference / baseline (oracle/_ref: the reference's own function)
+# ---------------------------------------------------------------------------
+def cpu_reference_run(steps, warmup, budget_s, pos_lo=3840, layers=28):
+    """Times the reference's cpu_attention_gqa_pipeline on the resident
+    workload: per step, its 28 layer calls (independent inputs) spread over all
+    host threads.  Returns (GB/s, cores, sample description, kind)."""
+    import __graft_entry__
+    orc = __graft_entry__.load_oracle()
+    cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    if orc.have_reference():
+        kind, T = "reference", orc.REF_T_MAX
+    else:
+        kind, T = "port", 4096
+    kcs = [rng.standard_normal((2, T, 128), dtype=np.float32) for _ in range(layers)]
+    vcs = [rng.standard_normal((2, T, 128), dtype=np.float32) for _ in range(layers)]
+    qkvs = [rng.standard_normal(QKV_W, dtype=np.float32) for _ in range(layers)]
+
+    def one_step(pos):
+        if kind == "reference":
+            orc.ref_bench_attention_many([q.copy() for q in qkvs], kcs, vcs, [pos] * layers,
+                                         [pos + 1] * layers, cores)
+        else:
+            orc.decode_batched([q.copy() for q in qkvs], kcs, vcs, [pos + 1] * layers,
+                               n_threads=cores)
+        return layers * ROW_BYTES * (pos + 1)
+
+    for i in range(warmup):
+        one_step(pos_lo + i % 256)
+    t0 = time.perf_counter()
+    done, nbytes = 0, 0
+    while done < steps:
+        nbytes += one_step(pos_lo + done % 256)
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    sample = (f"{done} decode step(s) x {layers} layers at positions {pos_lo}..{pos_lo + done - 1} "
+              f"(L = pos+1), layer calls spread over {cores} threads")
+    return nbytes / dt / 1e9, cores, sample, kind, done / dt
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    wl = WORKLOADS["resident28"]
+    gbs, cores, sample, kind, steps_per_s = cpu_reference_run(
+        args.steps, min(args.warmup, 2), budget_s=90.0, pos_lo=wl["pos_lo"])
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1000.0 / steps_per_s, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "tok_per_s": round(steps_per_s, 3),
+        "config": workload_config("resident28"),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(name):
+    if name == "resident28":
+        return {"workload": "resident28: 28-layer resident decode attention, 1 sequence per GPU, "
+                            "12 q / 2 KV heads, d=128, fp32 KV t_max=4096 per layer (235 MB), "
+                            "steps at positions 3840..4095 (window wraps)",
+                "layers": 28, "t_max": 4096, "positions": [3840, 4095], "global_batch": None,
+                "l2": "KV 235 MB per GPU > 126 MB L2, read cyclically; no flush",
+                "parallelism": "sequence-sharded replicas"}
+    if name == "batched":
+        return {"workload": "batched: 64 sequences, lengths U[256,8192] (seeded), fp32 KV, "
+                            "one new token per sequence per step", "seqs": 64,
+                "l2": "KV > 126 MB L2; no flush", "parallelism": "sequence-sharded"}
+    if name == "long":
+        return {"workload": "long: 256 sequences x 32768 fp32 KV rows (17.2 GB per layer)",
+                "seqs": 256, "t_max": 32768, "l2": "KV > L2; no flush",
+                "parallelism": "sequence-sharded"}
+    return {"workload": "single: one step, 12/2 heads, d=128, pos 511, seq_len 512",
+            "l2": "1 MB KV fits in L2 (latency-bound)"}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_resident(args, g, ctx, rank, world, local):
+    import torch
+    wl = WORKLOADS[args.workload]
+    L_layers, t_max, pos_lo, pos_hi = wl["layers"], wl["t_max"], wl["pos_lo"], wl["pos_hi"]
+    seed = 4242 + 1000 * rank
+    caches = torch.empty((L_layers, 2, 2, t_max, D), device="cuda")  # [layer][k/v][h][t][d]
+    ctx.fill_normal(caches, caches.numel(), seed, g.seeded.K_CACHE)
+    kvs = [g.kv_of(caches[l, 0], caches[l, 1]) for l in range(L_layers)]
+    n_slots = 8
+    qkv_slots = torch.empty((n_slots, L_layers, QKV_W), device="cuda")
+    ctx.fill_normal(qkv_slots, qkv_slots.numel(), seed, g.seeded.QKV)
+    out = torch.empty((L_layers, OUT_W), device="cuda")
+    d_pos = torch.tensor([pos_lo], dtype=torch.int32, device="cuda")
+    graphs = [ctx.graph_create_layers(kvs, qkv_slots[s], QKV_W, out, OUT_W, d_pos, advance=True,
+                                      wrap_lo=pos_lo, wrap_hi=pos_hi) for s in range(n_slots)]
+    # e2e: host-buffer steps through the C ABI (gqa_graph_step_host)
+    d_qkv_e2e = torch.empty((L_layers, QKV_W), device="cuda")
+    g_e2e = ctx.graph_create_layers(kvs, d_qkv_e2e, QKV_W, out, OUT_W, d_pos, advance=True,
+                                    wrap_lo=pos_lo, wrap_hi=pos_hi)
+    h_qkv = qkv_slots.cpu().pin_memory()
+    h_out = torch.empty((n_slots, L_layers, OUT_W)).pin_memory()
+    n_window = pos_hi - pos_lo
+
+    def step_bytes(i):
+        pos = pos_lo + i % n_window
+        return L_layers * ROW_BYTES * (pos + 1)
+
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        graphs[i % n_slots].launch(stream)
+    for i in range(args.warmup):
+        g_e2e.step_host(h_qkv[i % n_slots], h_out[i % n_slots], stream)
+    torch.cuda.synchronize()
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status set during warm-up")
+
+    # ---- kernel-only timed region ----
+    d_pos.fill_(pos_lo)
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            graphs[i % n_slots].launch(stream)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    total_bytes = sum(step_bytes(i) for i in range(args.steps))
+
+    # ---- e2e timed region (host buffers in, host buffers out) ----
+    d_pos.fill_(pos_lo)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        g_e2e.step_host(h_qkv[i % n_slots], h_out[i % n_slots], stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    t_e2e_local = e0.elapsed_time(e1) / 1e3
+    status = ctx.device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status} after the timed regions")
+
+    # mirrors the library's split plan for pos read from the device (planned for t_max)
+    n_sm = torch.cuda.get_device_properties(local).multi_processor_count
+    n_splits = min(-(-n_sm // N_KV), -(-t_max // 32))
+    kernels_per_step = L_layers * (2 if n_splits > 1 else 1) + 1
+    for gr in graphs + [g_e2e]:
+        gr.destroy()
+    return dict(t=t_local, t_e2e=t_e2e_local, bytes=total_bytes, clocks=clk.summary(),
+                launches=kernels_per_step * args.steps, launches_per_step=kernels_per_step,
+                h2d=L_layers * QKV_W * 4, d2h=L_layers * OUT_W * 4, tokens=args.steps,
+                dominant_launches=L_layers * args.steps)
+
+
+def run_batched(args, g, ctx, rank, world, local):
+    import torch
+    wl = WORKLOADS[args.workload]
+    seed = 777 + 1000 * rank
+    if args.workload == "batched":
+        n, window = wl["seqs"], wl["window"]
+        lens0 = [int(x) for x in g.seeded.uniform_int(seed, g.seeded.LENGTHS, n, wl["len_lo"],
+                                                      wl["len_hi"])]
+        t_max = wl["len_hi"] + window
+    else:
+        n, window, t_max = wl["seqs"], wl["window"], wl["t_max"]
+        lens0 = [t_max - window] * n
+    k = torch.empty((n, 2, t_max, D), device="cuda")
+    v = torch.empty((n, 2, t_max, D), device="cuda")
+    ctx.fill_normal(k, k.numel(), seed, g.seeded.K_CACHE)
+    ctx.fill_normal(v, v.numel(), seed, g.seeded.V_CACHE)
+    qkv = torch.empty((n, QKV_W), device="cuda")
+    ctx.fill_normal(qkv, qkv.numel(), seed, g.seeded.QKV)
+    out = torch.empty((n, OUT_W), device="cuda")
+    stride = 2 * t_max * D * 4
+    kp = torch.tensor([k.data_ptr() + s * stride for s in range(n)], dtype=torch.int64,
+                      device="cuda")
+    vp = torch.tensor([v.data_ptr() + s * stride for s in range(n)], dtype=torch.int64,
+                      device="cuda")
+    lens_base = torch.tensor(lens0, dtype=torch.int32, device="cuda")
+    dl = lens_base.clone()
+    max_len = max(lens0) + window - 1
+    ctx.reserve(n, max_len)
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        if i % window == 0:
+            dl.copy_(lens_base)
+        ctx.decode_batched(n, kp, vp, qkv, QKV_W, dl, max_len, out, OUT_W, stream)
+        dl.add_(1)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    total_bytes = sum(ROW_BYTES * (L + i % window) for i in range(args.steps) for L in lens0)
+    # e2e: q/k/v rows from pinned host memory, outputs back, every step
+    h_qkv = qkv.cpu().pin_memory()
+    h_out = torch.empty((n, OUT_W)).pin_memory()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        qkv.copy_(h_qkv, non_blocking=True)
+        step(i)
+        h_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    status = ctx.device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status}")
+    return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3, bytes=total_bytes,
+                clocks=clk.summary(), launches=2 * args.steps, launches_per_step=2,
+                h2d=n * QKV_W * 4, d2h=n * OUT_W * 4, tokens=n * args.steps,
+                dominant_launches=args.steps)
+
+
+def run_ours(args):
+    import torch
+    rank, world, local = dist_setup(args.gpus)
+    import __graft_entry__
+    g = __graft_entry__.load_package()
+    wl = WORKLOADS[args.workload]
+    t_max = wl.get("t_max") or (wl["len_hi"] + wl["window"])
+    ctx = g.Context(t_max=t_max, device=local)
+    if args.workload in ("resident28", "single"):
+        r = run_resident(args, g, ctx, rank, world, local)
+    else:
+        r = run_batched(args, g, ctx, rank, world, local)
+    t = max_over_ranks(r["t"], world)
+    t_e2e = max_over_ranks(r["t_e2e"], world)
+    total_bytes = sum_over_ranks(r["bytes"], world)
+    tokens = sum_over_ranks(r["tokens"], world)
+    peak, peak_kind = measured_peak()
+    gbs = total_bytes / t / 1e9
+    gbs_e2e = total_bytes / t_e2e / 1e9
+    per_gpu_bytes = r["bytes"] / r["dominant_launches"]
+    achieved = r["bytes"] / r["t"] / 1e9  # this rank's dominant-kernel bytes over its timed region
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cgbs, cores, sample, kind, _ = cpu_reference_run(10 ** 6, 1, budget_s=12.0)
+        cpu = {"value": round(cgbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+               "sample": sample}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t / args.steps * 1e3, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)",
+            "config": workload_config(args.workload),
+            "tok_per_s": round(tokens / t, 1),
+            "hbm_frac_of_measured": round(gbs / world / peak, 4),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_kind} hbm_gbs",
+                         "kernel": "decode_split_kernel",
+                         "algorithmic_bytes_per_launch": round(per_gpu_bytes),
+                         "duration_basis": "timed-region device time / launches of the "
+                                           "dominant kernel (includes its combine and gaps)",
+                         "traffic": profile_traffic(args.workload)},
+            "e2e": {"value": round(gbs_e2e, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
+                    "tok_per_s": round(tokens / t_e2e, 1)},
+            "gpu_launches": r["launches"],
+            "clocks": r["clocks"],
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="resident28")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,205 @@
+/*
+ * gqa.h -- C ABI of the B200 (sm_100a) grouped-query-attention decode path.
+ *
+ * Drop-in for the attention slice of the reference's resident Qwen2.5 decoder
+ * (fbetancourt-dev/macbook-hardware-linux-lab).  Plain C types only: device
+ * pointers are `float*`, streams are an opaque `void*` (a cudaStream_t; NULL is
+ * the legacy default stream).  Every call returns a gqa_status; nothing calls
+ * exit().  Calls are stream-ordered and asynchronous unless stated otherwise.
+ * One context per device; a context is not thread-safe (use one per thread or
+ * serialise), matching the reference's single in-order queue.  A context owns
+ * one split-KV scratch area, so its calls must not run concurrently on
+ * different streams; captured graphs keep using it (the context must outlive
+ * its graphs, and the scratch cannot grow while a graph exists).
+ *
+ * Shapes: head_dim 128, n_heads_q = 6 * n_heads_kv (Qwen2.5-1.5B: 12 / 2).
+ * KV cache per layer per sequence: [n_heads_kv][t_max][128] fp32, K stored
+ * after RoPE, exactly the reference's LayerKVDevice layout.
+ * qkv per token: [q (n_heads_q*128) | k (n_heads_kv*128) | v (n_heads_kv*128)].
+ */
+#ifndef GQA_B200_H
+#define GQA_B200_H
+
+#if defined(__GNUC__)
+#define GQA_API __attribute__((visibility("default")))
+#else
+#define GQA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct gqa_ctx gqa_ctx;
+typedef struct gqa_graph gqa_graph;
+typedef void *gqa_stream_t;
+
+typedef enum {
+    GQA_OK = 0,
+    GQA_ERR_INVALID_ARG = -1,  /* bad size, pointer, alignment or shape */
+    GQA_ERR_CUDA = -2,         /* a CUDA runtime call failed (see gqa_last_error_string) */
+    GQA_ERR_UNSUPPORTED = -3,  /* shape/config not built (e.g. head_dim != 128) */
+    GQA_ERR_DEVICE = -4,       /* a kernel flagged a problem (gqa_device_status) */
+    GQA_ERR_NO_MEMORY = -5,    /* allocation failed or not allowed while capturing */
+    GQA_ERR_TIMEOUT = -6       /* a bounded device wait gave up */
+} gqa_status;
+
+/* Model shape.  Replaces the reference's compile-time #defines
+ * (qwen_server.c:20-32: HEAD_DIM, N_HEADS_Q, N_HEADS_KV, T_MAX, ROPE_BASE). */
+typedef struct {
+    int n_heads_q;     /* 12 */
+    int n_heads_kv;    /* 2 */
+    int head_dim;      /* 128 (only value built) */
+    int t_max;         /* cache rows per KV head (reference: 4096) */
+    float rope_theta;  /* 1e6 */
+} gqa_config;
+
+/* One layer's resident KV cache: the reference's LayerKVDevice
+ * {k_cache, v_cache} (qwen_server.c:314-317), device pointers. */
+typedef struct {
+    float *k_cache;
+    float *v_cache;
+} gqa_layer_kv;
+
+/* ---- context ---------------------------------------------------------- */
+
+/* Creates a context on `device` (makes it current).  Replaces the OpenCL
+ * context/queue/program set-up of qwen_server.c:560-640. */
+GQA_API int gqa_create(const gqa_config *cfg, int device, gqa_ctx **out);
+GQA_API int gqa_destroy(gqa_ctx *ctx);
+
+/* Human-readable text of the last error on the calling thread. */
+GQA_API const char *gqa_last_error_string(void);
+
+/* Options.  GQA_OPT_PDL: 1 lets the library's own launches overlap their
+ * start with the previous kernel in the stream (programmatic dependent
+ * launch); KV rows below pos are then streamed before the previous kernel
+ * finishes, so the caller must not write those rows in the kernel launched
+ * immediately before.  Default 0 for single calls; the multi-layer step and
+ * graph APIs always use it between their own launches.
+ * GQA_OPT_TARGET_CTAS: CTAs one single-sequence decode aims for (default:
+ * the device's SM count). */
+enum { GQA_OPT_PDL = 1, GQA_OPT_TARGET_CTAS = 2 };
+GQA_API int gqa_set_option(gqa_ctx *ctx, int option, long long value);
+
+/* Pre-sizes the split-KV scratch for up to n_seq sequences of up to max_len
+ * tokens (call before stream capture; launches otherwise grow it on demand,
+ * which is refused while a capture is in progress). */
+GQA_API int gqa_reserve(gqa_ctx *ctx, int n_seq, int max_len);
+
+/* Reads and optionally clears the device status word (bitmask; 0 = fine).
+ * Synchronises the context's device. */
+GQA_API int gqa_device_status(gqa_ctx *ctx, int *status, int clear);
+
+/* ---- KV cache --------------------------------------------------------- */
+
+/* Allocates n_layers zero-filled caches of [n_heads_kv][t_max][128] fp32.
+ * Replaces qwen_server.c:646-647 (clCreateBuffer) and :671-676 (zero fill). */
+GQA_API int gqa_kv_alloc(gqa_ctx *ctx, int n_layers, gqa_layer_kv *out);
+GQA_API int gqa_kv_free(gqa_ctx *ctx, int n_layers, gqa_layer_kv *kv);
+
+/* ---- the layer call (the drop-in boundary) ---------------------------- */
+
+/* Attention slice of gpu_decoder_layer_step() (qwen_server.c:344-455, launches
+ * :446-450): RoPE (theta from cfg, half rotation) on q and k of the new token,
+ * append rotated k and raw v at row pos, attention of every q head over cache
+ * rows [0, seq_len), and the result written to qkv[0 : n_heads_q*128] as the
+ * reference's segment reduce does (qwen_server.c:402-404).  qkv[n_heads_q*128:]
+ * is left unchanged.  0 <= pos < t_max, 1 <= seq_len <= t_max (callers pass
+ * seq_len = pos + 1).  qkv and the caches must be 16-byte aligned. */
+GQA_API int gqa_layer_attention(gqa_ctx *ctx, gqa_stream_t stream, const gqa_layer_kv *kv, float *qkv,
+                        int pos, int seq_len);
+
+/* Same as gqa_layer_attention, result to a separate buffer out[n_heads_q*128]
+ * (qkv is then left unchanged). */
+GQA_API int gqa_layer_attention_out(gqa_ctx *ctx, gqa_stream_t stream, const gqa_layer_kv *kv,
+                            const float *qkv, int pos, int seq_len, float *out);
+
+/* The caller's per-token loop over layers (qwen_server.c:1021-1023,
+ * generate_stream.c:747-749): for each layer l, gqa_layer_attention_out on
+ * kv[l] with qkv + l*qkv_layer_stride -> out + l*out_layer_stride.  pos is read
+ * from device memory (*d_pos, seq_len = pos + 1); if advance is non-zero, *d_pos
+ * is incremented on the device after the last layer, wrapping to wrap_lo when
+ * it reaches wrap_hi (wrap_hi <= wrap_lo disables wrapping). */
+GQA_API int gqa_decode_layers(gqa_ctx *ctx, gqa_stream_t stream, int n_layers, const gqa_layer_kv *kv,
+                      const float *qkv, long long qkv_layer_stride, float *out,
+                      long long out_layer_stride, int *d_pos, int advance, int wrap_lo,
+                      int wrap_hi);
+
+/* gqa_decode_layers captured once into a CUDA graph and replayed by
+ * gqa_graph_launch (one launch = one decode step over all layers).  The
+ * pointers are baked into the graph. */
+GQA_API int gqa_graph_create_layers(gqa_ctx *ctx, int n_layers, const gqa_layer_kv *kv,
+                            const float *qkv, long long qkv_layer_stride, float *out,
+                            long long out_layer_stride, int *d_pos, int advance, int wrap_lo,
+                            int wrap_hi, gqa_graph **out_graph);
+GQA_API int gqa_graph_launch(gqa_graph *g, gqa_stream_t stream);
+GQA_API int gqa_graph_destroy(gqa_graph *g);
+
+/* One decode step with HOST buffers (the reference's write -> kernels ->
+ * read loop, attention_gqa_benchmark.c:531-545): copies h_qkv
+ * [n_layers][qkv_layer_stride] to d_qkv, replays g, copies d_out
+ * [n_layers][out_layer_stride] back to h_out.  Asynchronous on `stream`;
+ * pass page-locked host memory for the copies to overlap. */
+GQA_API int gqa_graph_step_host(gqa_graph *g, gqa_stream_t stream, const float *h_qkv, float *h_out);
+
+/* ---- kernel-level operations ------------------------------------------ */
+
+/* kernel_rope_and_kv_append (kernel_attention_gqa.cl:149-194): q[n_heads_q*128]
+ * rotated in place; k, v [n_heads_kv*128]; rotated k and v written to row pos.
+ * q, k, v must be the three consecutive slices of one qkv row, as the
+ * reference's sub-buffers are (qwen_server.c:664-669). */
+GQA_API int gqa_rope_kv_append(gqa_ctx *ctx, gqa_stream_t stream, const gqa_layer_kv *kv, float *q,
+                       const float *k, const float *v, int pos);
+
+/* Fused replacement of kernel_gqa_scores + kernel_softmax_gqa +
+ * kernel_gqa_value_combine_segmented + kernel_gqa_reduce_segments
+ * (kernel_attention_gqa.cl:202-397): attention of already-rotated q over
+ * cache rows [0, seq_len) -> out[n_heads_q*128]. */
+GQA_API int gqa_decode(gqa_ctx *ctx, gqa_stream_t stream, const gqa_layer_kv *kv, const float *q_rot,
+               int seq_len, float *out);
+
+/* Batched decode of n_seq independent sequences, one new token each: for
+ * sequence s, RoPE + append at pos = seq_lens[s] - 1 into k_caches[s] /
+ * v_caches[s], then attention over seq_lens[s] rows.  k_caches, v_caches,
+ * seq_lens are DEVICE arrays; qkv + s*qkv_stride is sequence s's qkv;
+ * results go to out + s*out_stride (out may equal qkv).  max_len bounds every
+ * seq_lens[s] (sizes the split plan). */
+GQA_API int gqa_decode_batched(gqa_ctx *ctx, gqa_stream_t stream, int n_seq, float *const *k_caches,
+                       float *const *v_caches, const float *qkv, long long qkv_stride,
+                       const int *seq_lens, int max_len, float *out, long long out_stride);
+
+/* Split-KV partial over cache rows [t_begin, t_end) for already-rotated q:
+ * per q head h, m[h] = max score (natural-log units, scores scaled by
+ * 1/sqrt(128)), l[h] = sum exp(s - m), o[h][:] = sum exp(s - m) v (not
+ * normalised).  An empty range yields m = -inf, l = 0. */
+GQA_API int gqa_decode_split_partial(gqa_ctx *ctx, gqa_stream_t stream, const gqa_layer_kv *kv,
+                             const float *q_rot, int t_begin, int t_end, float *m, float *l,
+                             float *o);
+
+/* Log-sum-exp combine of n_parts partials for n_rows rows (q heads):
+ * m, l: [n_parts][n_rows]; o: [n_parts][n_rows][128]; out: [n_rows][128] =
+ * sum_p e^(m_p - M) o_p / sum_p e^(m_p - M) l_p, M = max_p m_p.  Parts with
+ * l = 0 are ignored. */
+GQA_API int gqa_lse_combine(gqa_ctx *ctx, gqa_stream_t stream, int n_parts, int n_rows, const float *m,
+                    const float *l, const float *o, float *out);
+
+/* ---- utilities -------------------------------------------------------- */
+
+/* Fills dst[0..n) with seeded N(0,1) values (splitmix64 + Box-Muller;
+ * element e of stream (seed, stream_id) for e = offset .. offset+n-1). */
+GQA_API int gqa_fill_normal(gqa_ctx *ctx, gqa_stream_t stream, float *dst, long long n,
+                    unsigned long long seed, unsigned long long stream_id, long long offset);
+
+/* Inverse RoPE frequencies used by the kernels (host copy, head_dim/2
+ * floats): powf(theta, -2*i/head_dim) as in attention_gqa_benchmark.c:143. */
+GQA_API int gqa_inv_freq(const gqa_ctx *ctx, float *out);
+
+/* Version string of the library. */
+GQA_API const char *gqa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GQA_B200_H */

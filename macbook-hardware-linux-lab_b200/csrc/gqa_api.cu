@@ -1,0 +1,647 @@
+// C ABI of the GQA decode path (declared in include/gqa.h).
+//
+// The host side replaces the reference's clSetKernelArg/clEnqueueNDRangeKernel
+// plumbing in gpu_decoder_layer_step (qwen_server.c:344-455) with argument
+// validation, a split-KV plan and cudaLaunchKernelEx launches.  Errors are
+// returned as gqa_status codes with a thread-local message; nothing exits.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "gqa.h"
+#include "gqa_common.cuh"
+
+namespace gqa {
+size_t decode_smem_bytes();
+cudaError_t prepare_decode_kernels();
+cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cudaStream_t st,
+                                bool pdl);
+cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl);
+cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k_ptrs,
+                               float* const* v_ptrs, float* k_base, float* v_base,
+                               long long seq_stride, Lengths len, int t_max, int n_q, int n_kv,
+                               const float* inv_freq, int* status, int n_seq, cudaStream_t st,
+                               bool pdl);
+cudaError_t launch_advance_pos(int* pos, int wrap_lo, int wrap_hi, cudaStream_t st, bool pdl);
+cudaError_t launch_fill_normal(float* dst, long long n, uint64_t key, long long offset,
+                               int n_sm, cudaStream_t st);
+}  // namespace gqa
+
+using namespace gqa;
+
+struct gqa_ctx {
+  int device = 0;
+  int n_sm = 148;
+  gqa_config cfg{};
+  float h_inv_freq[kHalf];
+  float* inv_freq = nullptr;  // device [64]
+  int* status = nullptr;      // device
+  float* part_o = nullptr;    // split scratch
+  float* part_ml = nullptr;
+  long long cap_slots = 0;    // (q row x split) slots the scratch holds
+  int pdl = 0;
+  int target_ctas = 0;
+  int batch_chunk = 0;  // tokens per split in batched decode (0 = automatic)
+  int live_graphs = 0;  // graphs hold scratch pointers: no reallocation while > 0
+};
+
+struct gqa_graph {
+  gqa_ctx* ctx = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  const float* d_qkv = nullptr;
+  float* d_out = nullptr;
+  size_t qkv_bytes = 0;
+  size_t out_bytes = 0;
+};
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define GQA_CUDA(call)                                                                  \
+  do {                                                                                  \
+    cudaError_t e_ = (call);                                                            \
+    if (e_ != cudaSuccess)                                                              \
+      return fail(GQA_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));      \
+  } while (0)
+
+// Makes the context's device current for the duration of an API call.
+struct DeviceGuard {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) err = cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
+
+constexpr int kCtaQuant = 32;  // must match decode_split_kernel's range quantum
+
+bool is_capturing(cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess) return false;
+  return cs != cudaStreamCaptureStatusNone;
+}
+
+// Grows the split scratch to hold `slots` (row, split) partials.
+int ensure_scratch(gqa_ctx* c, long long slots, cudaStream_t st) {
+  if (slots <= c->cap_slots) return GQA_OK;
+  if (c->live_graphs > 0)
+    return fail(GQA_ERR_NO_MEMORY,
+                "split scratch too small (%lld slots needed, %lld held) and %d captured "
+                "graph(s) still use it; call gqa_reserve() before creating graphs",
+                slots, c->cap_slots, c->live_graphs);
+  if (is_capturing(st))
+    return fail(GQA_ERR_NO_MEMORY,
+                "split scratch too small (%lld slots needed, %lld held) while the stream is "
+                "being captured; call gqa_reserve() before capturing",
+                slots, c->cap_slots);
+  if (c->part_o) cudaFree(c->part_o);
+  if (c->part_ml) cudaFree(c->part_ml);
+  c->part_o = nullptr;
+  c->part_ml = nullptr;
+  c->cap_slots = 0;
+  if (cudaMalloc(&c->part_o, sizeof(float) * kHeadDim * (size_t)slots) != cudaSuccess ||
+      cudaMalloc(&c->part_ml, sizeof(float) * 2 * (size_t)slots) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(GQA_ERR_NO_MEMORY, "cudaMalloc of %lld split slots failed", slots);
+  }
+  c->cap_slots = slots;
+  return GQA_OK;
+}
+
+// Number of splits for a decode over `len` rows of `rows_kv` (sequence, KV
+// head) pairs: enough CTAs to cover the device once, never a split shorter
+// than 32 rows.
+int plan_splits_single(const gqa_ctx* c, int rows_kv, int len) {
+  const int target = c->target_ctas > 0 ? c->target_ctas : c->n_sm;
+  int want = ceil_div(target, rows_kv);
+  const int most = ceil_div(len, kCtaQuant);
+  if (want > most) want = most;
+  return want < 1 ? 1 : want;
+}
+
+int batch_chunk(const gqa_ctx* c, int max_len) {
+  if (c->batch_chunk > 0) return ((c->batch_chunk + kCtaQuant - 1) / kCtaQuant) * kCtaQuant;
+  return max_len > 8192 ? 1024 : 256;
+}
+
+DecodeParams base_params(gqa_ctx* c) {
+  DecodeParams p{};
+  p.t_max = c->cfg.t_max;
+  p.n_kv = c->cfg.n_heads_kv;
+  p.inv_freq = c->inv_freq;
+  p.q_scale = (1.0f / sqrtf((float)kHeadDim)) * 1.4426950408889634f;
+  p.status = c->status;
+  p.part_o = c->part_o;
+  p.part_ml = c->part_ml;
+  p.min_chunk = kCtaQuant;
+  p.lengths_stable = 1;
+  return p;
+}
+
+CombineParams combine_from_scratch(const gqa_ctx* c, int n_splits) {
+  CombineParams cp{};
+  cp.m = c->part_ml;
+  cp.l = c->part_ml + 1;
+  cp.o = c->part_o;
+  cp.ml_part_stride = 2;
+  cp.ml_row_stride = 2LL * n_splits;
+  cp.o_part_stride = kHeadDim;
+  cp.o_row_stride = (long long)kHeadDim * n_splits;
+  cp.n_parts = n_splits;
+  cp.rows_per_seq = c->cfg.n_heads_q;
+  return cp;
+}
+
+int check_kv(const gqa_ctx* c, const gqa_layer_kv* kv) {
+  if (!kv || !kv->k_cache || !kv->v_cache) return fail(GQA_ERR_INVALID_ARG, "null KV cache");
+  if (!aligned16(kv->k_cache) || !aligned16(kv->v_cache))
+    return fail(GQA_ERR_INVALID_ARG, "KV cache pointers must be 16-byte aligned");
+  (void)c;
+  return GQA_OK;
+}
+
+// One sequence: split kernel (+ combine when split), result to `out`.
+int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
+               Lengths len, int plan_len, bool fused, float* out, bool pdl_first,
+               bool lengths_stable) {
+  const int n_kv = c->cfg.n_heads_kv;
+  const int n_splits = plan_splits_single(c, n_kv, plan_len);
+  if (n_splits > 1) {
+    int rc = ensure_scratch(c, (long long)c->cfg.n_heads_q * n_splits, st);
+    if (rc != GQA_OK) return rc;
+  }
+  DecodeParams p = base_params(c);
+  p.k_base = kv->k_cache;
+  p.v_base = kv->v_cache;
+  p.qkv = qkv;
+  p.len = len;
+  p.lengths_stable = lengths_stable ? 1 : 0;
+  p.n_splits = n_splits;
+  p.out = out;
+  GQA_CUDA(launch_decode_split(p, 1, fused, st, pdl_first));
+  if (n_splits > 1) {
+    CombineParams cp = combine_from_scratch(c, n_splits);
+    cp.out = out;
+    GQA_CUDA(launch_combine(cp, 1, st, true));
+  }
+  return GQA_OK;
+}
+
+int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* kv,
+                const float* qkv, long long qkv_stride, float* out, long long out_stride,
+                int* d_pos, int advance, int wrap_lo, int wrap_hi) {
+  if (n_layers < 1 || !kv || !qkv || !out || !d_pos)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_decode_layers: null argument or n_layers < 1");
+  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
+  if (qkv_stride < (long long)(nq + 2 * nkv) * kHeadDim || out_stride < (long long)nq * kHeadDim)
+    return fail(GQA_ERR_INVALID_ARG, "layer strides smaller than one layer's qkv / output");
+  if ((qkv_stride & 3) || (out_stride & 3) || !aligned16(qkv) || !aligned16(out))
+    return fail(GQA_ERR_INVALID_ARG, "qkv/out and their layer strides must be 16-byte aligned");
+  for (int l = 0; l < n_layers; ++l) {
+    int rc = check_kv(c, &kv[l]);
+    if (rc != GQA_OK) return rc;
+  }
+  Lengths len{};
+  len.pos_dev = d_pos;
+  for (int l = 0; l < n_layers; ++l) {
+    // Layer 0 may follow the kernel that advanced *d_pos: it reads pos only
+    // after its dependency wait.  Later layers follow a combine/split of
+    // the previous layer, which never writes pos or this layer's cache.
+    int rc = run_single(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max, true,
+                        out + l * out_stride, /*pdl_first=*/true, /*lengths_stable=*/l > 0);
+    if (rc != GQA_OK) return rc;
+  }
+  if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
+  return GQA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gqa_last_error_string(void) { return g_err; }
+
+const char* gqa_version(void) { return "gqa-b200 0.1 (sm_100a)"; }
+
+int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
+  if (!cfg || !out) return fail(GQA_ERR_INVALID_ARG, "gqa_create: null argument");
+  *out = nullptr;
+  if (cfg->head_dim != kHeadDim)
+    return fail(GQA_ERR_UNSUPPORTED, "head_dim %d not built (only 128)", cfg->head_dim);
+  if (cfg->n_heads_kv < 1 || cfg->n_heads_q != 6 * cfg->n_heads_kv)
+    return fail(GQA_ERR_UNSUPPORTED, "n_heads_q must be 6 * n_heads_kv (got %d / %d)",
+                cfg->n_heads_q, cfg->n_heads_kv);
+  if (cfg->t_max < 1 || !(cfg->rope_theta > 0.f))
+    return fail(GQA_ERR_INVALID_ARG, "t_max must be >= 1 and rope_theta > 0");
+  if ((long long)cfg->n_heads_kv * cfg->t_max * kHeadDim > (1LL << 40))
+    return fail(GQA_ERR_INVALID_ARG, "cache too large");
+  int n_dev = 0;
+  GQA_CUDA(cudaGetDeviceCount(&n_dev));
+  if (device < 0 || device >= n_dev) return fail(GQA_ERR_INVALID_ARG, "no device %d", device);
+  DeviceGuard g(device);
+  if (g.err != cudaSuccess) return fail(GQA_ERR_CUDA, "cudaSetDevice: %s", cudaGetErrorString(g.err));
+  int major = 0, minor = 0;
+  GQA_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+  GQA_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+  if (major != 10 || minor != 0)
+    return fail(GQA_ERR_UNSUPPORTED, "built for sm_100a only; device is sm_%d%d", major, minor);
+
+  gqa_ctx* c = new gqa_ctx();
+  c->device = device;
+  c->cfg = *cfg;
+  cudaDeviceGetAttribute(&c->n_sm, cudaDevAttrMultiProcessorCount, device);
+  // attention_gqa_benchmark.c:143: powf(ROPE_BASE, -2.0f * (float)tid / (float)HEAD_DIM),
+  // evaluated once here with the host libm so the device multiplies the very
+  // same fp32 inverse frequency by pos.
+  for (int i = 0; i < kHalf; ++i)
+    c->h_inv_freq[i] = powf(cfg->rope_theta, -2.0f * (float)i / (float)kHeadDim);
+  cudaError_t e = prepare_decode_kernels();
+  if (e == cudaSuccess) e = cudaMalloc(&c->inv_freq, sizeof(float) * kHalf);
+  if (e == cudaSuccess) e = cudaMalloc(&c->status, sizeof(int));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(c->inv_freq, c->h_inv_freq, sizeof(float) * kHalf, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    gqa_destroy(c);
+    return fail(GQA_ERR_CUDA, "context set-up failed: %s", cudaGetErrorString(e));
+  }
+  *out = c;
+  return GQA_OK;
+}
+
+int gqa_destroy(gqa_ctx* c) {
+  if (!c) return GQA_OK;
+  DeviceGuard g(c->device);
+  if (c->inv_freq) cudaFree(c->inv_freq);
+  if (c->status) cudaFree(c->status);
+  if (c->part_o) cudaFree(c->part_o);
+  if (c->part_ml) cudaFree(c->part_ml);
+  delete c;
+  return GQA_OK;
+}
+
+int gqa_set_option(gqa_ctx* c, int option, long long value) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  switch (option) {
+    case GQA_OPT_PDL: c->pdl = value ? 1 : 0; return GQA_OK;
+    case GQA_OPT_TARGET_CTAS:
+      if (value < 0 || value > (1 << 20)) return fail(GQA_ERR_INVALID_ARG, "target CTAs out of range");
+      c->target_ctas = (int)value;
+      return GQA_OK;
+    case 3: /* GQA_OPT_BATCH_CHUNK (internal tuning knob) */
+      if (value < 0 || value > (1 << 20)) return fail(GQA_ERR_INVALID_ARG, "chunk out of range");
+      c->batch_chunk = (int)value;
+      return GQA_OK;
+    default: return fail(GQA_ERR_INVALID_ARG, "unknown option %d", option);
+  }
+}
+
+int gqa_reserve(gqa_ctx* c, int n_seq, int max_len) {
+  if (!c || n_seq < 1 || max_len < 1 || max_len > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_reserve: bad arguments");
+  DeviceGuard g(c->device);
+  const int single = plan_splits_single(c, c->cfg.n_heads_kv, max_len);
+  const int batched = ceil_div(max_len, batch_chunk(c, max_len));
+  const int splits = single > batched ? single : batched;
+  return ensure_scratch(c, (long long)n_seq * c->cfg.n_heads_q * splits, nullptr);
+}
+
+int gqa_device_status(gqa_ctx* c, int* status, int clear) {
+  if (!c || !status) return fail(GQA_ERR_INVALID_ARG, "null argument");
+  DeviceGuard g(c->device);
+  GQA_CUDA(cudaDeviceSynchronize());
+  GQA_CUDA(cudaMemcpy(status, c->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear) GQA_CUDA(cudaMemset(c->status, 0, sizeof(int)));
+  return GQA_OK;
+}
+
+int gqa_kv_alloc(gqa_ctx* c, int n_layers, gqa_layer_kv* out) {
+  if (!c || !out || n_layers < 1) return fail(GQA_ERR_INVALID_ARG, "gqa_kv_alloc: bad arguments");
+  DeviceGuard g(c->device);
+  const size_t bytes = sizeof(float) * (size_t)c->cfg.n_heads_kv * c->cfg.t_max * kHeadDim;
+  for (int l = 0; l < n_layers; ++l) out[l].k_cache = out[l].v_cache = nullptr;
+  for (int l = 0; l < n_layers; ++l) {
+    if (cudaMalloc(&out[l].k_cache, bytes) != cudaSuccess ||
+        cudaMalloc(&out[l].v_cache, bytes) != cudaSuccess ||
+        cudaMemset(out[l].k_cache, 0, bytes) != cudaSuccess ||
+        cudaMemset(out[l].v_cache, 0, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      gqa_kv_free(c, n_layers, out);
+      return fail(GQA_ERR_NO_MEMORY, "KV cache allocation failed at layer %d", l);
+    }
+  }
+  return GQA_OK;
+}
+
+int gqa_kv_free(gqa_ctx* c, int n_layers, gqa_layer_kv* kv) {
+  if (!c || !kv || n_layers < 0) return fail(GQA_ERR_INVALID_ARG, "gqa_kv_free: bad arguments");
+  DeviceGuard g(c->device);
+  for (int l = 0; l < n_layers; ++l) {
+    if (kv[l].k_cache) cudaFree(kv[l].k_cache);
+    if (kv[l].v_cache) cudaFree(kv[l].v_cache);
+    kv[l].k_cache = kv[l].v_cache = nullptr;
+  }
+  return GQA_OK;
+}
+
+int gqa_layer_attention_out(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
+                            const float* qkv, int pos, int seq_len, float* out) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  int rc = check_kv(c, kv);
+  if (rc != GQA_OK) return rc;
+  if (!qkv || !out || !aligned16(qkv) || !aligned16(out))
+    return fail(GQA_ERR_INVALID_ARG, "qkv/out must be non-null and 16-byte aligned");
+  if (pos < 0 || pos >= c->cfg.t_max || seq_len < 1 || seq_len > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "pos %d / seq_len %d outside [0, t_max=%d)", pos, seq_len,
+                c->cfg.t_max);
+  DeviceGuard g(c->device);
+  Lengths len{};
+  len.pos_imm = pos;
+  len.seqlen_imm = seq_len;
+  return run_single(c, (cudaStream_t)stream, kv, qkv, len, seq_len, true, out, c->pdl != 0,
+                    true);
+}
+
+int gqa_layer_attention(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, float* qkv,
+                        int pos, int seq_len) {
+  return gqa_layer_attention_out(c, stream, kv, qkv, pos, seq_len, qkv);
+}
+
+int gqa_decode_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers, const gqa_layer_kv* kv,
+                      const float* qkv, long long qkv_layer_stride, float* out,
+                      long long out_layer_stride, int* d_pos, int advance, int wrap_lo,
+                      int wrap_hi) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  DeviceGuard g(c->device);
+  return layers_impl(c, (cudaStream_t)stream, n_layers, kv, qkv, qkv_layer_stride, out,
+                     out_layer_stride, d_pos, advance, wrap_lo, wrap_hi);
+}
+
+int gqa_graph_create_layers(gqa_ctx* c, int n_layers, const gqa_layer_kv* kv, const float* qkv,
+                            long long qkv_layer_stride, float* out, long long out_layer_stride,
+                            int* d_pos, int advance, int wrap_lo, int wrap_hi,
+                            gqa_graph** out_graph) {
+  if (!c || !out_graph) return fail(GQA_ERR_INVALID_ARG, "null argument");
+  *out_graph = nullptr;
+  DeviceGuard g(c->device);
+  int rc = gqa_reserve(c, 1, c->cfg.t_max);
+  if (rc != GQA_OK) return rc;
+  cudaStream_t st;
+  GQA_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) {
+    cudaStreamDestroy(st);
+    return fail(GQA_ERR_CUDA, "cudaStreamBeginCapture: %s", cudaGetErrorString(e));
+  }
+  rc = layers_impl(c, st, n_layers, kv, qkv, qkv_layer_stride, out, out_layer_stride, d_pos,
+                   advance, wrap_lo, wrap_hi);
+  e = cudaStreamEndCapture(st, &graph);
+  cudaStreamDestroy(st);
+  if (rc != GQA_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return fail(GQA_ERR_CUDA, "cudaStreamEndCapture: %s", cudaGetErrorString(e));
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(graph);
+    return fail(GQA_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(e));
+  }
+  gqa_graph* gr = new gqa_graph();
+  c->live_graphs++;
+  gr->ctx = c;
+  gr->graph = graph;
+  gr->exec = exec;
+  gr->d_qkv = qkv;
+  gr->d_out = out;
+  gr->qkv_bytes = sizeof(float) * (size_t)qkv_layer_stride * n_layers;
+  gr->out_bytes = sizeof(float) * (size_t)out_layer_stride * n_layers;
+  *out_graph = gr;
+  return GQA_OK;
+}
+
+int gqa_graph_launch(gqa_graph* gr, gqa_stream_t stream) {
+  if (!gr) return fail(GQA_ERR_INVALID_ARG, "null graph");
+  DeviceGuard g(gr->ctx->device);
+  GQA_CUDA(cudaGraphLaunch(gr->exec, (cudaStream_t)stream));
+  return GQA_OK;
+}
+
+int gqa_graph_step_host(gqa_graph* gr, gqa_stream_t stream, const float* h_qkv, float* h_out) {
+  if (!gr || !h_qkv || !h_out) return fail(GQA_ERR_INVALID_ARG, "null argument");
+  DeviceGuard g(gr->ctx->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  GQA_CUDA(cudaMemcpyAsync((void*)gr->d_qkv, h_qkv, gr->qkv_bytes, cudaMemcpyHostToDevice, st));
+  GQA_CUDA(cudaGraphLaunch(gr->exec, st));
+  GQA_CUDA(cudaMemcpyAsync(h_out, gr->d_out, gr->out_bytes, cudaMemcpyDeviceToHost, st));
+  return GQA_OK;
+}
+
+int gqa_graph_destroy(gqa_graph* gr) {
+  if (!gr) return GQA_OK;
+  DeviceGuard g(gr->ctx->device);
+  if (gr->exec) cudaGraphExecDestroy(gr->exec);
+  if (gr->graph) cudaGraphDestroy(gr->graph);
+  gr->ctx->live_graphs--;
+  delete gr;
+  return GQA_OK;
+}
+
+int gqa_rope_kv_append(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, float* q,
+                       const float* k, const float* v, int pos) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  int rc = check_kv(c, kv);
+  if (rc != GQA_OK) return rc;
+  if (!q || !k || !v) return fail(GQA_ERR_INVALID_ARG, "null q/k/v");
+  if (pos < 0 || pos >= c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "pos %d outside [0, %d)", pos, c->cfg.t_max);
+  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
+  // The kernel addresses k and v relative to q (one qkv row); stage separate
+  // buffers through that layout only when they already are one row.
+  if (k != q + (long long)nq * kHeadDim || v != k + (long long)nkv * kHeadDim)
+    return fail(GQA_ERR_INVALID_ARG,
+                "q, k, v must be consecutive slices of one qkv row (k = q + n_heads_q*128, "
+                "v = k + n_heads_kv*128)");
+  DeviceGuard g(c->device);
+  Lengths len{};
+  len.pos_imm = pos;
+  len.seqlen_imm = pos + 1;
+  GQA_CUDA(launch_rope_append(q, 0, nullptr, nullptr, kv->k_cache, kv->v_cache, 0, len,
+                              c->cfg.t_max, nq, nkv, c->inv_freq, c->status, 1,
+                              (cudaStream_t)stream, c->pdl != 0));
+  return GQA_OK;
+}
+
+int gqa_decode(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, const float* q_rot,
+               int seq_len, float* out) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  int rc = check_kv(c, kv);
+  if (rc != GQA_OK) return rc;
+  if (!q_rot || !out || !aligned16(q_rot) || !aligned16(out))
+    return fail(GQA_ERR_INVALID_ARG, "q/out must be non-null and 16-byte aligned");
+  if (seq_len < 1 || seq_len > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "seq_len %d outside [1, %d]", seq_len, c->cfg.t_max);
+  DeviceGuard g(c->device);
+  Lengths len{};
+  len.pos_imm = seq_len - 1;
+  len.seqlen_imm = seq_len;
+  return run_single(c, (cudaStream_t)stream, kv, q_rot, len, seq_len, false, out, c->pdl != 0,
+                    true);
+}
+
+int gqa_decode_batched(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const* k_caches,
+                       float* const* v_caches, const float* qkv, long long qkv_stride,
+                       const int* seq_lens, int max_len, float* out, long long out_stride) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (n_seq < 1 || n_seq > 65535 || !k_caches || !v_caches || !qkv || !seq_lens || !out)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_decode_batched: null argument or n_seq out of range");
+  if (max_len < 1 || max_len > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "max_len %d outside [1, %d]", max_len, c->cfg.t_max);
+  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
+  if (qkv_stride < (long long)(nq + 2 * nkv) * kHeadDim || out_stride < (long long)nq * kHeadDim)
+    return fail(GQA_ERR_INVALID_ARG, "qkv/out strides smaller than one sequence's row");
+  if ((qkv_stride & 3) || (out_stride & 3) || !aligned16(qkv) || !aligned16(out))
+    return fail(GQA_ERR_INVALID_ARG, "qkv/out and their strides must be 16-byte aligned");
+  if (out != qkv && out < qkv + qkv_stride * n_seq && qkv < out + out_stride * n_seq)
+    return fail(GQA_ERR_INVALID_ARG, "out overlaps qkv without being equal to it");
+  DeviceGuard g(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int chunk = batch_chunk(c, max_len);
+  const int n_splits = ceil_div(max_len, chunk);
+  if (n_splits > 65535) return fail(GQA_ERR_INVALID_ARG, "too many splits");
+  if (n_splits > 1) {
+    int rc = ensure_scratch(c, (long long)n_seq * nq * n_splits, st);
+    if (rc != GQA_OK) return rc;
+  }
+  // In-place output: the split kernels read q of their own sequence before
+  // the combine overwrites it (separate launches), so out == qkv is safe.
+  DecodeParams p = base_params(c);
+  p.k_ptrs = k_caches;
+  p.v_ptrs = v_caches;
+  p.qkv = qkv;
+  p.qkv_stride = qkv_stride;
+  p.len.seq_lens = seq_lens;
+  p.lengths_stable = 0;
+  p.n_splits = n_splits;
+  p.min_chunk = chunk;
+  p.out = out;
+  p.out_stride = out_stride;
+  GQA_CUDA(launch_decode_split(p, n_seq, true, st, c->pdl != 0));
+  if (n_splits > 1) {
+    CombineParams cp = combine_from_scratch(c, n_splits);
+    cp.out = out;
+    cp.out_stride = out_stride;
+    GQA_CUDA(launch_combine(cp, n_seq, st, true));
+  }
+  return GQA_OK;
+}
+
+int gqa_decode_split_partial(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
+                             const float* q_rot, int t_begin, int t_end, float* m, float* l,
+                             float* o) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  int rc = check_kv(c, kv);
+  if (rc != GQA_OK) return rc;
+  if (!q_rot || !m || !l || !o || !aligned16(q_rot))
+    return fail(GQA_ERR_INVALID_ARG, "null argument or unaligned q");
+  if (t_begin < 0 || t_end < t_begin || t_end > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "range [%d, %d) outside [0, %d]", t_begin, t_end,
+                c->cfg.t_max);
+  DeviceGuard g(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int nq = c->cfg.n_heads_q;
+  CombineParams cp{};
+  int n_splits = 0;
+  if (t_end > t_begin) {
+    n_splits = plan_splits_single(c, c->cfg.n_heads_kv, t_end - t_begin);
+    rc = ensure_scratch(c, (long long)nq * n_splits, st);
+    if (rc != GQA_OK) return rc;
+    DecodeParams p = base_params(c);
+    p.k_base = kv->k_cache;
+    p.v_base = kv->v_cache;
+    p.qkv = q_rot;
+    p.len.pos_imm = t_end - 1;
+    p.len.seqlen_imm = t_end;
+    p.t_begin = t_begin;
+    p.t_end = t_end;
+    p.n_splits = n_splits;
+    p.out = nullptr;  // always write partials
+    GQA_CUDA(launch_decode_split(p, 1, false, st, c->pdl != 0));
+    cp = combine_from_scratch(c, n_splits);
+  } else {
+    cp.rows_per_seq = nq;
+  }
+  cp.n_parts = n_splits;
+  cp.out = o;
+  cp.out_m = m;
+  cp.out_l = l;
+  GQA_CUDA(launch_combine(cp, 1, st, true));
+  return GQA_OK;
+}
+
+int gqa_lse_combine(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows, const float* m,
+                    const float* l, const float* o, float* out) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (n_parts < 0 || n_parts > 4096 || n_rows < 1 || n_rows > 65535 || !m || !l || !o || !out)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_lse_combine: bad arguments");
+  DeviceGuard g(c->device);
+  CombineParams cp{};
+  cp.m = m;
+  cp.l = l;
+  cp.o = o;
+  cp.ml_part_stride = n_rows;
+  cp.ml_row_stride = 1;
+  cp.o_part_stride = (long long)n_rows * kHeadDim;
+  cp.o_row_stride = kHeadDim;
+  cp.n_parts = n_parts;
+  cp.rows_per_seq = n_rows;
+  cp.out = out;
+  GQA_CUDA(launch_combine(cp, 1, (cudaStream_t)stream, c->pdl != 0));
+  return GQA_OK;
+}
+
+int gqa_fill_normal(gqa_ctx* c, gqa_stream_t stream, float* dst, long long n,
+                    unsigned long long seed, unsigned long long stream_id, long long offset) {
+  if (!c || !dst || n < 0 || offset < 0) return fail(GQA_ERR_INVALID_ARG, "bad arguments");
+  if (n == 0) return GQA_OK;
+  DeviceGuard g(c->device);
+  // Stream key: splitmix64 finaliser of seed ^ (stream_id * odd constant);
+  // identical to seeded.stream_key() on the host.
+  uint64_t z = (uint64_t)seed ^ ((uint64_t)stream_id * 0xD1B54A32D192ED03ULL);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  z = z ^ (z >> 31);
+  GQA_CUDA(launch_fill_normal(dst, n, z, offset, c->n_sm, (cudaStream_t)stream));
+  return GQA_OK;
+}
+
+int gqa_inv_freq(const gqa_ctx* c, float* out) {
+  if (!c || !out) return fail(GQA_ERR_INVALID_ARG, "null argument");
+  memcpy(out, c->h_inv_freq, sizeof(c->h_inv_freq));
+  return GQA_OK;
+}
+
+}  // extern "C"

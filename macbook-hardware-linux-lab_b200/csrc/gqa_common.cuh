@@ -1,0 +1,178 @@
+// Shared definitions for the sm_100a GQA attention kernels.
+//
+// Shapes follow the reference's Qwen2.5-1.5B attention (compute/attention-gqa-
+// resident/attention_gqa_benchmark.c:15-22): head_dim 128, 6 query heads per KV
+// head, KV cache laid out [n_kv][t_max][128] fp32 per layer per sequence
+// (kernel_attention_gqa.cl:153-154, qwen_server.c:314-317).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace gqa {
+
+constexpr int kHeadDim = 128;
+constexpr int kHalf = kHeadDim / 2;
+constexpr int kRowBytes = kHeadDim * 4;  // one fp32 K or V row
+
+// Device status bits, OR-ed into the context's status word by kernels that
+// detect a problem they cannot report through a return value.
+enum : int {
+  kStatusBadLength = 1 << 0,    // a device-side pos / seq_len was out of range
+  kStatusWaitTimeout = 1 << 1,  // an mbarrier wait ran out of its budget
+  kStatusBadSplit = 1 << 2,     // split bookkeeping inconsistent
+};
+
+// ---------------------------------------------------------------------------
+// PTX helpers (mbarrier, bulk async copy, programmatic dependent launch)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after ~`budget` SM clock cycles and returns false.
+// Every wait in these kernels is bounded so that a lost transfer can never
+// hang the GPU; the caller records kStatusWaitTimeout and drains.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                                                  long long budget) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - start > budget) return false;
+  }
+  return true;
+}
+
+// Global -> shared bulk copy (no tensor map, no multicast) completing on `bar`.
+// Both addresses must be 16-byte aligned and `bytes` a multiple of 16.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// Programmatic dependent launch.  `wait` blocks until the preceding grid in
+// the stream has completed and its memory is visible; it is a no-op when the
+// kernel was launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Kernel parameter blocks
+// ---------------------------------------------------------------------------
+
+// Where the token count of each sequence comes from.
+//   pos_dev != nullptr : pos = *pos_dev, seq_len = pos + 1 (one sequence;
+//                        used by graph replays that advance pos on device)
+//   seq_lens != nullptr: seq_len = seq_lens[s], pos = seq_len - 1
+//   otherwise          : pos = pos_imm, seq_len = seqlen_imm
+struct Lengths {
+  const int* pos_dev;
+  const int* seq_lens;
+  int pos_imm;
+  int seqlen_imm;
+};
+
+struct DecodeParams {
+  // KV caches.  Per sequence s the cache is k_ptrs[s] (device array of
+  // pointers) or, when k_ptrs is null, k_base + s * seq_stride.
+  float* const* k_ptrs;
+  float* const* v_ptrs;
+  float* k_base;
+  float* v_base;
+  long long seq_stride;  // floats between consecutive sequences' caches
+  int t_max;             // cache rows per KV head (row stride t_max * 128)
+  int n_kv;              // KV heads
+
+  // Inputs.  For sequence s, q = qkv + s*qkv_stride holds n_kv*G heads of
+  // 128 floats; in the fused mode k and v of the new token follow q.
+  const float* qkv;
+  long long qkv_stride;
+
+  Lengths len;
+  // 1 when the lengths (and cache rows below pos) are not written by the
+  // kernel launched immediately before this one, so the fused kernel may read
+  // them and start streaming the cache before its dependency wait.
+  int lengths_stable;
+  int t_begin;   // first cache row attended (0 except for KV-range shards)
+  int t_end;     // if > 0: attend rows [t_begin, t_end) instead of [t_begin, seq_len)
+
+  int n_splits;  // grid.x
+  int min_chunk;  // tokens; every split covers a multiple of 32 tokens
+
+  const float* inv_freq;  // [64] RoPE inverse frequencies
+  float q_scale;          // softmax scale * log2(e), folded into q
+
+  // Split outputs: part_o [n_seq][n_q][n_splits][128] (un-normalised),
+  // part_ml [n_seq][n_q][n_splits][2] = (m in natural-log units, l).
+  float* part_o;
+  float* part_ml;
+
+  // Final output when n_splits == 1 (normalised), row stride per sequence.
+  float* out;
+  long long out_stride;
+
+  int* status;
+};
+
+struct CombineParams {
+  const float* m;  // m[p * ml_part_stride + r * ml_row_stride]
+  const float* l;
+  const float* o;  // o[p * o_part_stride + r * o_row_stride + d]
+  long long ml_part_stride, ml_row_stride;
+  long long o_part_stride, o_row_stride;
+  int n_parts;
+  int rows_per_seq;  // q heads per sequence
+  // Output: row r = (seq, h) -> out + seq*out_stride + h*128.
+  float* out;
+  long long out_stride;
+  // When out_m/out_l are set, the combined triple (M, L, un-normalised O) is
+  // written instead of O / L (a partial over the union of the parts).
+  float* out_m;
+  float* out_l;
+};
+
+}  // namespace gqa

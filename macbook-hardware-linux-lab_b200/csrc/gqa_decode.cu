@@ -1,0 +1,662 @@
+// fp32 GQA decode attention for sm_100a.
+//
+// Replaces the reference's five decode launches (kernel_attention_gqa.cl:149-397:
+// RoPE+append, scores, softmax, segmented PV, segment reduce) by
+//   decode_split_kernel : RoPE of q and of the new k (optional), KV append,
+//                         QK^T, online softmax and PV over one token range of
+//                         one KV head for all 6 query heads of its group, so
+//                         every K/V byte is read from HBM exactly once;
+//   combine_kernel      : log-sum-exp merge of the per-range partials.
+//
+// Memory path.  Each CTA owns a contiguous token range of one KV head; each of
+// its 4 warps owns a contiguous quarter of that range and streams it through a
+// private 3-stage ring in shared memory with cp.async.bulk (1-D TMA: one copy
+// per K tile and one per V tile, 8 rows = 4 KB each, evict-first L2 hint).
+// Consecutive cache rows are contiguous ([h][t][128] layout), so a tile is
+// one linear copy; no tensor map and no multicast is needed.
+//
+// Compute path (per warp, per 8-token stage).  Lane l holds dims 4l..4l+3 of
+// the 6 (scaled, rotated) q heads.  QK^T gives 48 partial dot products per
+// lane; a butterfly reduce-scatter (5 exchange rounds, 48 shuffles in total)
+// leaves each lane 3 complete scores.  Softmax runs in the log2 domain with a
+// lazily updated running max (rescale only when a score exceeds the max by
+// more than 2^8), p is staged through a 256-byte per-warp buffer and PV
+// accumulates o[6][4] per lane.  Warps are merged in shared memory at the end.
+#include "gqa_common.cuh"
+
+#include <math_constants.h>
+
+namespace gqa {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;  // == kHeadDim: one thread per dim in the epilogue
+constexpr int kStageTok = 8;
+constexpr int kStages = 3;
+constexpr int kCtaQuant = kWarps * kStageTok;  // CTA ranges are multiples of 32 tokens
+constexpr float kRescaleThresh = 8.0f;         // log2 units
+constexpr long long kWaitBudget = 2000000000LL;  // ~1 s of SM clocks per wait
+constexpr float kLn2 = 0.6931471805599453f;
+
+static_assert(kThreads == kHeadDim, "epilogue maps one thread per head dim");
+
+template <int G>
+struct DecodeSmem {
+  float k[kWarps][kStages][kStageTok * kHeadDim];
+  float v[kWarps][kStages][kStageTok * kHeadDim];
+  float q[G][kHeadDim];
+  float newk[kHeadDim];
+  float newv[kHeadDim];
+  float cs[kHalf][2];
+  float p[kWarps][kStageTok][8];
+  float wm[kWarps][G];
+  float wl[kWarps][G];
+  uint64_t full[kWarps][kStages];
+  int err;
+};
+
+__device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
+__device__ __forceinline__ int round_up_i(int a, int b) { return ceil_div_i(a, b) * b; }
+
+// Token range of split `split` when [t_begin, t_end) is cut into n_splits
+// chunks of a multiple of kCtaQuant tokens (at least min_chunk).  Shared by
+// the host planner (mirrored in gqa_api.cu) and the kernels.
+__device__ __forceinline__ int chunk_tokens(int len, int n_splits, int min_chunk) {
+  int c = round_up_i(ceil_div_i(len, n_splits), kCtaQuant);
+  return c > min_chunk ? c : min_chunk;
+}
+
+__device__ __forceinline__ void resolve_lengths(const Lengths& L, int seq, int& pos,
+                                                int& seq_len) {
+  if (L.pos_dev) {
+    pos = *L.pos_dev;
+    seq_len = pos + 1;
+  } else if (L.seq_lens) {
+    seq_len = L.seq_lens[seq];
+    pos = seq_len - 1;
+  } else {
+    pos = L.pos_imm;
+    seq_len = L.seqlen_imm;
+  }
+}
+
+// Butterfly reduce-scatter step: N values -> N/2, lanes with bit OFF set keep
+// the upper half.  After the steps 16,8,4,2 on 48 values, lane keeps original
+// indices base..base+2 with base = 24*b4 + 12*b3 + 6*b2 + 3*b1.
+template <int N, int OFF>
+__device__ __forceinline__ void bfly_halve(float (&v)[48], int lane) {
+  const bool up = (lane & OFF) != 0;
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    const float send = up ? v[i] : v[i + N / 2];
+    const float keep = up ? v[i + N / 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
+  }
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+
+template <int G, bool FUSED>
+__global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeParams p) {
+  static_assert(G == 6, "the lane/score ownership map below is written for 6 q heads per KV head");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  DecodeSmem<G>& sm = *reinterpret_cast<DecodeSmem<G>*>(smem_raw);
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int split = blockIdx.x, hkv = blockIdx.y, seq = blockIdx.z;
+  const int n_q = p.n_kv * G;
+
+  // Only the fused kernel streams the cache before its dependency wait, and
+  // only when the host marked the lengths as stable (not produced by the
+  // preceding kernel, e.g. the device pos advanced at the end of a step).
+  // The unfused kernel usually follows rope_append, which writes row pos.
+  const bool early = FUSED && p.lengths_stable != 0;
+  if (!early) pdl_wait();
+
+  int pos, seq_len;
+  resolve_lengths(p.len, seq, pos, seq_len);
+  const int r_end = p.t_end > 0 ? p.t_end : seq_len;
+  const bool bad = seq_len < 1 || seq_len > p.t_max || pos < 0 || pos >= p.t_max ||
+                   p.t_begin < 0 || r_end > p.t_max || p.t_begin >= r_end;
+  if (bad) {
+    if (early) pdl_wait();
+    if (tid == 0) atomicOr(p.status, kStatusBadLength);
+    return;
+  }
+
+  const int len = r_end - p.t_begin;
+  const int chunk = chunk_tokens(len, p.n_splits, p.min_chunk);
+  const int c0 = p.t_begin + split * chunk;
+  const int c1 = min(c0 + chunk, r_end);
+  const long long prow = ((long long)seq * n_q + hkv * G) * p.n_splits + split;
+
+  if (c0 >= r_end) {
+    // Empty split (short sequence in a batch planned for the longest one).
+    if (early) pdl_wait();
+    pdl_launch_dependents();
+    if (tid < G) {
+      p.part_ml[(prow + (long long)tid * p.n_splits) * 2 + 0] = -CUDART_INF_F;
+      p.part_ml[(prow + (long long)tid * p.n_splits) * 2 + 1] = 0.f;
+    }
+    return;
+  }
+
+  const int ctoks = c1 - c0;
+  const int wchunk = round_up_i(ceil_div_i(ctoks, kWarps), kStageTok);
+  const int w0 = c0 + warp * wchunk;
+  const int w1 = min(w0 + wchunk, c1);
+  const int n_tok = max(w1 - w0, 0);
+  const int n_it = ceil_div_i(n_tok, kStageTok);
+
+  float* kc;
+  float* vc;
+  if (p.k_ptrs) {
+    kc = p.k_ptrs[seq];
+    vc = p.v_ptrs[seq];
+  } else {
+    kc = p.k_base + (long long)seq * p.seq_stride;
+    vc = p.v_base + (long long)seq * p.seq_stride;
+  }
+  kc += (long long)hkv * p.t_max * kHeadDim;
+  vc += (long long)hkv * p.t_max * kHeadDim;
+
+  if (tid == 0) sm.err = 0;
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) mbar_init(&sm.full[warp][s], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+
+  const uint64_t policy = l2_policy_evict_first();
+  auto issue = [&](int stage, int it) {
+    const int t = w0 + it * kStageTok;
+    const int nt = min(kStageTok, w1 - t);
+    const uint32_t bytes = (uint32_t)nt * kRowBytes;
+    mbar_arrive_expect_tx(&sm.full[warp][stage], 2 * bytes);
+    bulk_copy_g2s(sm.k[warp][stage], kc + (long long)t * kHeadDim, bytes, &sm.full[warp][stage],
+                  policy);
+    bulk_copy_g2s(sm.v[warp][stage], vc + (long long)t * kHeadDim, bytes, &sm.full[warp][stage],
+                  policy);
+  };
+  // Cache rows before pos are not written by the preceding kernel: stream
+  // them before waiting on it.
+  if (lane == 0) {
+    for (int s = 0; s < kStages && s < n_it; ++s) issue(s, s);
+  }
+
+  if (early) pdl_wait();
+  pdl_launch_dependents();
+
+  // ---- q (and the new k/v row) into shared memory -------------------------
+  const float* qin = p.qkv + (long long)seq * p.qkv_stride;
+  if (FUSED) {
+    if (tid < kHalf) {
+      float sn, cs;
+      sincosf((float)pos * p.inv_freq[tid], &sn, &cs);
+      sm.cs[tid][0] = cs;
+      sm.cs[tid][1] = sn;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < G * kHalf; idx += kThreads) {
+      const int h = idx / kHalf, i = idx % kHalf;
+      const float* qh = qin + (long long)(hkv * G + h) * kHeadDim;
+      const float q0 = qh[i], q1 = qh[i + kHalf];
+      const float c = sm.cs[i][0], s = sm.cs[i][1];
+      sm.q[h][i] = (q0 * c - q1 * s) * p.q_scale;
+      sm.q[h][i + kHalf] = (q0 * s + q1 * c) * p.q_scale;
+    }
+    if (tid < kHalf) {
+      const float* kin = qin + (long long)n_q * kHeadDim + (long long)hkv * kHeadDim;
+      const float* vin = qin + (long long)(n_q + p.n_kv) * kHeadDim + (long long)hkv * kHeadDim;
+      const float c = sm.cs[tid][0], s = sm.cs[tid][1];
+      const float k0 = kin[tid], k1 = kin[tid + kHalf];
+      sm.newk[tid] = k0 * c - k1 * s;
+      sm.newk[tid + kHalf] = k0 * s + k1 * c;
+      sm.newv[tid] = vin[tid];
+      sm.newv[tid + kHalf] = vin[tid + kHalf];
+    }
+  } else {
+    for (int idx = tid; idx < G * kHeadDim; idx += kThreads) {
+      const int h = idx / kHeadDim, d = idx % kHeadDim;
+      sm.q[h][d] = qin[(long long)(hkv * G + h) * kHeadDim + d] * p.q_scale;
+    }
+  }
+  __syncthreads();
+
+  // The new row is written by the warp whose range holds pos (after that
+  // stage's copy has landed, so the stale row it replaced was already read),
+  // or by split 0 / warp 0 when pos is outside the attended range.
+  if (FUSED && split == 0 && warp == 0 && !(pos >= p.t_begin && pos < r_end)) {
+    reinterpret_cast<float4*>(kc + (long long)pos * kHeadDim)[lane] =
+        reinterpret_cast<const float4*>(sm.newk)[lane];
+    reinterpret_cast<float4*>(vc + (long long)pos * kHeadDim)[lane] =
+        reinterpret_cast<const float4*>(sm.newv)[lane];
+  }
+
+  float qr[G][4];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    const float4 t = reinterpret_cast<const float4*>(sm.q[h])[lane];
+    qr[h][0] = t.x; qr[h][1] = t.y; qr[h][2] = t.z; qr[h][3] = t.w;
+  }
+
+  float o[G][4];
+  float m[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    m[h] = -CUDART_INF_F;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[h][j] = 0.f;
+  }
+  float lown[3] = {0.f, 0.f, 0.f};
+  const int b1 = (lane >> 1) & 1;
+  const int tt = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+  const int hb = 3 * b1;
+  int consumed = 0;
+  bool failed = false;
+
+  for (int it = 0; it < n_it; ++it) {
+    const int s = it % kStages;
+    const uint32_t par = (uint32_t)(it / kStages) & 1u;
+    bool ok = mbar_wait_bounded(&sm.full[warp][s], par, kWaitBudget);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) {
+      failed = true;
+      break;
+    }
+    consumed = it + 1;
+    const int t0 = w0 + it * kStageTok;
+    const int nt = min(kStageTok, w1 - t0);
+    const float* ks = sm.k[warp][s];
+    const float* vs = sm.v[warp][s];
+
+    if (FUSED && pos >= t0 && pos < t0 + nt) {
+      reinterpret_cast<float4*>(kc + (long long)pos * kHeadDim)[lane] =
+          reinterpret_cast<const float4*>(sm.newk)[lane];
+      reinterpret_cast<float4*>(vc + (long long)pos * kHeadDim)[lane] =
+          reinterpret_cast<const float4*>(sm.newv)[lane];
+    }
+
+    // ---- scores: 8 tokens x 6 heads, reduced over the 32 lanes ----
+    float part[48];
+#pragma unroll
+    for (int t = 0; t < kStageTok; ++t) {
+      if (t < nt) {
+        const float* kr = (FUSED && t0 + t == pos) ? sm.newk : ks + t * kHeadDim;
+        const float4 kv = reinterpret_cast<const float4*>(kr)[lane];
+#pragma unroll
+        for (int h = 0; h < G; ++h)
+          part[t * G + h] = qr[h][0] * kv.x + qr[h][1] * kv.y + qr[h][2] * kv.z + qr[h][3] * kv.w;
+      } else {
+#pragma unroll
+        for (int h = 0; h < G; ++h) part[t * G + h] = 0.f;
+      }
+    }
+    bfly_halve<48, 16>(part, lane);
+    bfly_halve<24, 8>(part, lane);
+    bfly_halve<12, 4>(part, lane);
+    bfly_halve<6, 2>(part, lane);
+#pragma unroll
+    for (int i = 0; i < 3; ++i) part[i] += __shfl_xor_sync(0xffffffffu, part[i], 1);
+
+    float sc[3];
+    const bool valid = tt < nt;
+#pragma unroll
+    for (int i = 0; i < 3; ++i) sc[i] = valid ? part[i] : -CUDART_INF_F;
+
+    // ---- online softmax with lazy max update ----
+    float mo[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) mo[i] = b1 ? m[3 + i] : m[i];
+    const bool exceed = sc[0] > mo[0] + kRescaleThresh || sc[1] > mo[1] + kRescaleThresh ||
+                        sc[2] > mo[2] + kRescaleThresh;
+    if (__any_sync(0xffffffffu, exceed)) {
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float mine = ((h / 3) == b1) ? sc[h % 3] : -CUDART_INF_F;
+        const float mnew = fmaxf(m[h], warp_max(mine));
+        const float alpha = (mnew == -CUDART_INF_F) ? 1.f : exp2f(m[h] - mnew);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[h][j] *= alpha;
+        if ((h / 3) == b1) lown[h % 3] *= alpha;
+        m[h] = mnew;
+      }
+#pragma unroll
+      for (int i = 0; i < 3; ++i) mo[i] = b1 ? m[3 + i] : m[i];
+    }
+    float pv[3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) pv[i] = exp2f(sc[i] - mo[i]);
+    if ((lane & 1) == 0) {
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        lown[i] += pv[i];
+        sm.p[warp][tt][hb + i] = pv[i];
+      }
+    }
+    __syncwarp();
+
+    // ---- o += p . V ----
+#pragma unroll
+    for (int t = 0; t < kStageTok; ++t) {
+      if (t < nt) {
+        const float4 pa = *reinterpret_cast<const float4*>(&sm.p[warp][t][0]);
+        const float2 pb = *reinterpret_cast<const float2*>(&sm.p[warp][t][4]);
+        const float* vr = (FUSED && t0 + t == pos) ? sm.newv : vs + t * kHeadDim;
+        const float4 vv = reinterpret_cast<const float4*>(vr)[lane];
+        const float pr[6] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y};
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          o[h][0] += pr[h] * vv.x;
+          o[h][1] += pr[h] * vv.y;
+          o[h][2] += pr[h] * vv.z;
+          o[h][3] += pr[h] * vv.w;
+        }
+      }
+    }
+    __syncwarp();
+    if (it + kStages < n_it && lane == 0) {
+      fence_proxy_async_smem();
+      issue(s, it + kStages);
+    }
+  }
+
+  if (failed) {
+    // Drain whatever this warp still has in flight (bounded), then report.
+    const int issued = min(n_it, consumed + kStages);
+    for (int it = consumed; it < issued; ++it)
+      (void)mbar_wait_bounded(&sm.full[warp][it % kStages], (uint32_t)(it / kStages) & 1u,
+                              kWaitBudget / 16);
+    if (lane == 0) {
+      atomicOr(p.status, kStatusWaitTimeout);
+      atomicOr(&sm.err, 1);
+    }
+  }
+
+  // ---- per-warp (m, l, o) -> shared memory ----
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    float x = lown[i];
+    x += __shfl_xor_sync(0xffffffffu, x, 1);
+    x += __shfl_xor_sync(0xffffffffu, x, 4);
+    x += __shfl_xor_sync(0xffffffffu, x, 8);
+    x += __shfl_xor_sync(0xffffffffu, x, 16);
+    lown[i] = x;
+  }
+  if (lane == 0 || lane == 2) {
+#pragma unroll
+    for (int i = 0; i < 3; ++i) sm.wl[warp][hb + i] = lown[i];
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) sm.wm[warp][h] = m[h];
+  }
+  // Each warp reuses stage 0 of its own ring (all its copies have landed).
+  float* ow = sm.k[warp][0];
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+    reinterpret_cast<float4*>(ow + h * kHeadDim)[lane] =
+        make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
+  __syncthreads();
+  if (sm.err) return;
+
+  // ---- merge the 4 warps; thread tid owns head dim d = tid ----
+  const int d = tid;
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm.wm[w][h]);
+    float Lsum = 0.f, O = 0.f;
+    if (M != -CUDART_INF_F) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float mw = sm.wm[w][h];
+        if (mw != -CUDART_INF_F) {
+          const float a = exp2f(mw - M);
+          Lsum += a * sm.wl[w][h];
+          O += a * sm.k[w][0][h * kHeadDim + d];
+        }
+      }
+    }
+    if (p.out != nullptr && p.n_splits == 1) {
+      p.out[(long long)seq * p.out_stride + (long long)(hkv * G + h) * kHeadDim + d] =
+          Lsum > 0.f ? O / Lsum : 0.f;
+    } else {
+      const long long r = prow + (long long)h * p.n_splits;
+      p.part_o[r * kHeadDim + d] = O;
+      if (d == 0) {
+        p.part_ml[r * 2 + 0] = M * kLn2;  // natural-log units outside this kernel
+        p.part_ml[r * 2 + 1] = Lsum;
+      }
+    }
+  }
+}
+
+// Log-sum-exp merge of n_parts partials per output row (one CTA per row, one
+// thread per head dim).  Parts with l == 0 or m == -inf carry no weight and
+// their o is never read.
+__global__ void __launch_bounds__(kHeadDim) combine_kernel(const CombineParams c) {
+  extern __shared__ float sw[];  // [n_parts] weights, then [n_parts] l
+  __shared__ float red[kHeadDim / 32];
+  __shared__ float s_M;
+  const int h = blockIdx.x, seq = blockIdx.y, d = threadIdx.x;
+  const long long r = (long long)seq * c.rows_per_seq + h;
+  // Let the next kernel (the next layer's split kernel) start streaming its
+  // own cache now; it waits for this grid before it reads or writes anything
+  // this grid touches.
+  pdl_launch_dependents();
+  pdl_wait();
+
+  float mx = -CUDART_INF_F;
+  for (int i = d; i < c.n_parts; i += kHeadDim) {
+    const float mi = c.m[i * c.ml_part_stride + r * c.ml_row_stride];
+    const float li = c.l[i * c.ml_part_stride + r * c.ml_row_stride];
+    sw[i] = mi;
+    sw[c.n_parts + i] = li;
+    if (li > 0.f) mx = fmaxf(mx, mi);
+  }
+  mx = warp_max(mx);
+  if ((d & 31) == 0) red[d >> 5] = mx;
+  __syncthreads();
+  if (d == 0) {
+    float M = red[0];
+    for (int w = 1; w < kHeadDim / 32; ++w) M = fmaxf(M, red[w]);
+    s_M = M;
+  }
+  __syncthreads();
+  const float M = s_M;
+  for (int i = d; i < c.n_parts; i += kHeadDim) {
+    const float li = sw[c.n_parts + i];
+    sw[i] = (li > 0.f && M != -CUDART_INF_F) ? expf(sw[i] - M) : 0.f;
+  }
+  __syncthreads();
+
+  float L = 0.f, O = 0.f;
+  const float* op = c.o + r * c.o_row_stride + d;
+  int i = 0;
+  for (; i + 4 <= c.n_parts; i += 4) {
+    float w[4], ov[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) w[u] = sw[i + u];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) ov[u] = w[u] != 0.f ? op[(long long)(i + u) * c.o_part_stride] : 0.f;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      L += w[u] * sw[c.n_parts + i + u];
+      O += w[u] * ov[u];
+    }
+  }
+  for (; i < c.n_parts; ++i) {
+    const float w = sw[i];
+    if (w != 0.f) {
+      L += w * sw[c.n_parts + i];
+      O += w * op[(long long)i * c.o_part_stride];
+    }
+  }
+  float* dst = c.out + (long long)seq * c.out_stride + (long long)h * kHeadDim;
+  if (c.out_m) {
+    dst[d] = O;
+    if (d == 0) {
+      c.out_m[r] = M;
+      c.out_l[r] = L;
+    }
+  } else {
+    dst[d] = L > 0.f ? O / L : 0.f;
+  }
+}
+
+// RoPE on every q head (in place) and every k head of one new token per
+// sequence, with the rotated k and raw v written to cache row pos: the
+// reference's kernel_rope_and_kv_append (kernel_attention_gqa.cl:149-194) for
+// a batch of sequences.  One CTA per sequence, one thread per rotation pair.
+__global__ void __launch_bounds__(kHalf) rope_append_kernel(
+    float* qkv, long long qkv_stride, float* const* k_ptrs, float* const* v_ptrs, float* k_base,
+    float* v_base, long long seq_stride, Lengths len, int t_max, int n_q, int n_kv,
+    const float* inv_freq, int* status) {
+  const int seq = blockIdx.x, i = threadIdx.x;
+  pdl_wait();
+  pdl_launch_dependents();
+  int pos, seq_len;
+  resolve_lengths(len, seq, pos, seq_len);
+  if (pos < 0 || pos >= t_max) {
+    if (i == 0) atomicOr(status, kStatusBadLength);
+    return;
+  }
+  float* q = qkv + (long long)seq * qkv_stride;
+  const float* k = q + (long long)n_q * kHeadDim;
+  const float* v = k + (long long)n_kv * kHeadDim;
+  float* kc = k_ptrs ? k_ptrs[seq] : k_base + (long long)seq * seq_stride;
+  float* vc = v_ptrs ? v_ptrs[seq] : v_base + (long long)seq * seq_stride;
+  float sn, cs;
+  sincosf((float)pos * inv_freq[i], &sn, &cs);
+  for (int h = 0; h < n_q; ++h) {
+    float* qh = q + (long long)h * kHeadDim;
+    const float q0 = qh[i], q1 = qh[i + kHalf];
+    qh[i] = q0 * cs - q1 * sn;
+    qh[i + kHalf] = q0 * sn + q1 * cs;
+  }
+  for (int h = 0; h < n_kv; ++h) {
+    const float k0 = k[h * kHeadDim + i], k1 = k[h * kHeadDim + i + kHalf];
+    const long long row = ((long long)h * t_max + pos) * kHeadDim;
+    kc[row + i] = k0 * cs - k1 * sn;
+    kc[row + i + kHalf] = k0 * sn + k1 * cs;
+    vc[row + i] = v[h * kHeadDim + i];
+    vc[row + i + kHalf] = v[h * kHeadDim + i + kHalf];
+  }
+}
+
+// Advances the device-side position after a replayed decode step, wrapping
+// from wrap_hi back to wrap_lo (a fixed window of positions can then be
+// replayed indefinitely).
+__global__ void advance_pos_kernel(int* pos, int wrap_lo, int wrap_hi) {
+  pdl_wait();
+  int nxt = *pos + 1;
+  if (wrap_hi > wrap_lo && nxt >= wrap_hi) nxt = wrap_lo;
+  *pos = nxt;
+}
+
+// Seeded N(0,1) fill: element i is one half of the Box-Muller pair i/2 drawn
+// from two counter-indexed splitmix64 outputs.  The same sequence is produced
+// on the host by the package's seeded.py, so device-filled and host-filled
+// tensors of the same (seed, stream) hold the same distribution; bit-equality
+// with the host is not promised (double-precision log/cos may differ in the
+// last ulp).
+__device__ __forceinline__ uint64_t splitmix_mix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+  return z ^ (z >> 31);
+}
+
+__global__ void fill_normal_kernel(float* dst, long long n, uint64_t key, long long offset) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const long long e = i + offset;
+    const uint64_t j = (uint64_t)(e >> 1);
+    const uint64_t r1 = splitmix_mix(key + (2 * j + 1) * 0x9E3779B97F4A7C15ULL);
+    const uint64_t r2 = splitmix_mix(key + (2 * j + 2) * 0x9E3779B97F4A7C15ULL);
+    const double u1 = ((double)(r1 >> 11) + 1.0) * (1.0 / 9007199254740992.0);
+    const double u2 = (double)(r2 >> 11) * (1.0 / 9007199254740992.0);
+    const double rad = sqrt(-2.0 * log(u1));
+    const double ang = 6.283185307179586 * u2;
+    dst[i] = (float)((e & 1) ? rad * sin(ang) : rad * cos(ang));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host-side launchers (C++; the C ABI in gqa_api.cu validates and calls these)
+// ---------------------------------------------------------------------------
+size_t decode_smem_bytes() { return sizeof(DecodeSmem<6>); }
+
+static cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t st, bool pdl, void** args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+cudaError_t prepare_decode_kernels() {
+  const int smem = (int)decode_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute((const void*)decode_split_kernel<6, true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute((const void*)decode_split_kernel<6, false>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
+cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cudaStream_t st,
+                                bool pdl) {
+  dim3 grid(p.n_splits, p.n_kv, n_seq);
+  DecodeParams copy = p;
+  void* args[] = {&copy};
+  const void* fn = fused ? (const void*)decode_split_kernel<6, true>
+                         : (const void*)decode_split_kernel<6, false>;
+  return launch_ex(fn, grid, dim3(kThreads), decode_smem_bytes(), st, pdl, args);
+}
+
+cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl) {
+  dim3 grid(c.rows_per_seq, n_seq);
+  CombineParams copy = c;
+  void* args[] = {&copy};
+  return launch_ex((const void*)combine_kernel, grid, dim3(kHeadDim),
+                   sizeof(float) * 2 * (size_t)c.n_parts, st, pdl, args);
+}
+
+cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k_ptrs,
+                               float* const* v_ptrs, float* k_base, float* v_base,
+                               long long seq_stride, Lengths len, int t_max, int n_q, int n_kv,
+                               const float* inv_freq, int* status, int n_seq, cudaStream_t st,
+                               bool pdl) {
+  void* args[] = {&qkv, &qkv_stride, (void*)&k_ptrs, (void*)&v_ptrs, &k_base, &v_base,
+                  &seq_stride, &len, &t_max, &n_q, &n_kv, (void*)&inv_freq, &status};
+  return launch_ex((const void*)rope_append_kernel, dim3(n_seq), dim3(kHalf), 0, st, pdl, args);
+}
+
+cudaError_t launch_advance_pos(int* pos, int wrap_lo, int wrap_hi, cudaStream_t st, bool pdl) {
+  void* args[] = {&pos, &wrap_lo, &wrap_hi};
+  return launch_ex((const void*)advance_pos_kernel, dim3(1), dim3(1), 0, st, pdl, args);
+}
+
+cudaError_t launch_fill_normal(float* dst, long long n, uint64_t key, long long offset,
+                               int n_sm, cudaStream_t st) {
+  long long blocks = (n + 255) / 256;
+  const long long cap = (long long)n_sm * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  fill_normal_kernel<<<(unsigned)blocks, 256, 0, st>>>(dst, n, key, offset);
+  return cudaGetLastError();
+}
+
+}  // namespace gqa

@@ -1,0 +1,304 @@
+"""ctypes binding of the C ABI declared in include/gqa.h.
+
+This is the host-side mirror of the reference's layer-call API for the
+attention slice: ``Context.layer_attention(kv, qkv, pos, seq_len)`` has the
+argument meaning of gpu_decoder_layer_step (qwen_server.c:344-455, attention
+launches :446-450) -- q/k/v of the new token in, KV cache appended at ``pos``,
+attention over ``seq_len`` rows, ``attn_out`` written over ``qkv[0:1536]``.
+Where the reference exits on a failed OpenCL call (CHECK_CL, qwen_server.c:53-58),
+every call here raises :class:`GqaError` carrying the library's status code
+and message; the process keeps running.
+
+Device memory, streams and pinned host buffers are plain pointers; torch
+tensors are accepted wherever a pointer is expected (their ``data_ptr()``) and
+torch's current stream is used when no stream is given.  There is no CPU
+fallback: if the CUDA library is not built, :func:`lib` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libgqa_b200.so")
+HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "gqa.h")
+
+GQA_OK = 0
+GQA_ERR_INVALID_ARG = -1
+GQA_ERR_CUDA = -2
+GQA_ERR_UNSUPPORTED = -3
+GQA_ERR_DEVICE = -4
+GQA_ERR_NO_MEMORY = -5
+GQA_ERR_TIMEOUT = -6
+
+GQA_OPT_PDL = 1
+GQA_OPT_TARGET_CTAS = 2
+GQA_OPT_BATCH_CHUNK = 3
+
+STATUS_BAD_LENGTH = 1
+STATUS_WAIT_TIMEOUT = 2
+
+
+class GqaError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"gqa error {code}: {message}")
+        self.code = code
+
+
+class Config(ctypes.Structure):
+    _fields_ = [("n_heads_q", ctypes.c_int), ("n_heads_kv", ctypes.c_int),
+                ("head_dim", ctypes.c_int), ("t_max", ctypes.c_int),
+                ("rope_theta", ctypes.c_float)]
+
+
+class LayerKV(ctypes.Structure):
+    """One layer's cache: the reference's LayerKVDevice {k_cache, v_cache}."""
+    _fields_ = [("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p)]
+
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_ll = ctypes.c_longlong
+_ull = ctypes.c_ulonglong
+
+# name -> argtypes (restype is int unless listed in _RESTYPES)
+_SIGNATURES = {
+    "gqa_create": [ctypes.POINTER(Config), _i, ctypes.POINTER(_vp)],
+    "gqa_destroy": [_vp],
+    "gqa_last_error_string": [],
+    "gqa_set_option": [_vp, _i, _ll],
+    "gqa_reserve": [_vp, _i, _i],
+    "gqa_device_status": [_vp, ctypes.POINTER(_i), _i],
+    "gqa_kv_alloc": [_vp, _i, ctypes.POINTER(LayerKV)],
+    "gqa_kv_free": [_vp, _i, ctypes.POINTER(LayerKV)],
+    "gqa_layer_attention": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i],
+    "gqa_layer_attention_out": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _vp],
+    "gqa_decode_layers": [_vp, _vp, _i, ctypes.POINTER(LayerKV), _vp, _ll, _vp, _ll, _vp, _i,
+                          _i, _i],
+    "gqa_graph_create_layers": [_vp, _i, ctypes.POINTER(LayerKV), _vp, _ll, _vp, _ll, _vp, _i,
+                                _i, _i, ctypes.POINTER(_vp)],
+    "gqa_graph_launch": [_vp, _vp],
+    "gqa_graph_step_host": [_vp, _vp, _vp, _vp],
+    "gqa_graph_destroy": [_vp],
+    "gqa_rope_kv_append": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _vp, _vp, _i],
+    "gqa_decode": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _vp],
+    "gqa_decode_batched": [_vp, _vp, _i, _vp, _vp, _vp, _ll, _vp, _i, _vp, _ll],
+    "gqa_decode_split_partial": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _vp, _vp, _vp],
+    "gqa_lse_combine": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
+    "gqa_fill_normal": [_vp, _vp, _vp, _ll, _ull, _ull, _ll],
+    "gqa_inv_freq": [_vp, ctypes.POINTER(ctypes.c_float)],
+    "gqa_version": [],
+}
+_RESTYPES = {"gqa_last_error_string": ctypes.c_char_p, "gqa_version": ctypes.c_char_p}
+
+_lib = None
+
+
+def header_functions(path: str = HEADER_PATH) -> list[str]:
+    """Names of the functions declared in include/gqa.h."""
+    text = open(path).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gqa_[a-z0-9_]+)\s*\(", text)))
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded CUDA library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise GqaError(GQA_ERR_UNSUPPORTED,
+                           f"CUDA library {LIB_PATH} is not built; run __graft_entry__.build()")
+        h = ctypes.CDLL(LIB_PATH)
+        for name, args in _SIGNATURES.items():
+            fn = getattr(h, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        _lib = h
+    return _lib
+
+
+def last_error() -> str:
+    return (lib().gqa_last_error_string() or b"").decode()
+
+
+def _check(rc: int) -> None:
+    if rc != GQA_OK:
+        raise GqaError(rc, last_error())
+
+
+def _ptr(x) -> int | None:
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    raise TypeError(f"cannot take a device pointer of {type(x)}")
+
+
+def _stream(s) -> int | None:
+    if s is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(s, int):
+        return s
+    return s.cuda_stream
+
+
+def kv_of(k_cache, v_cache) -> LayerKV:
+    return LayerKV(_ptr(k_cache), _ptr(v_cache))
+
+
+def _kv_array(kvs) -> ctypes.Array:
+    if isinstance(kvs, LayerKV):
+        kvs = [kvs]
+    arr = (LayerKV * len(kvs))()
+    for i, kv in enumerate(kvs):
+        arr[i] = kv
+    return arr
+
+
+class Graph:
+    """A captured multi-layer decode step (gqa_graph_create_layers)."""
+
+    def __init__(self, handle: int, keep: tuple):
+        self._h = handle
+        self._keep = keep  # keeps the ctypes arrays alive
+
+    def launch(self, stream=None) -> None:
+        _check(lib().gqa_graph_launch(self._h, _stream(stream)))
+
+    def step_host(self, h_qkv, h_out, stream=None) -> None:
+        _check(lib().gqa_graph_step_host(self._h, _stream(stream), _ptr(h_qkv), _ptr(h_out)))
+
+    def destroy(self) -> None:
+        if self._h:
+            lib().gqa_graph_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+class Context:
+    """One gqa_ctx on one device (see include/gqa.h for every call)."""
+
+    def __init__(self, n_heads_q: int = 12, n_heads_kv: int = 2, head_dim: int = 128,
+                 t_max: int = 4096, rope_theta: float = 1e6, device: int = 0):
+        self.cfg = Config(n_heads_q, n_heads_kv, head_dim, t_max, rope_theta)
+        h = _vp()
+        _check(lib().gqa_create(ctypes.byref(self.cfg), device, ctypes.byref(h)))
+        self._h = h.value
+        self.device = device
+        self.n_heads_q, self.n_heads_kv, self.head_dim, self.t_max = (
+            n_heads_q, n_heads_kv, head_dim, t_max)
+
+    # -- lifetime / options -------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().gqa_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_option(self, option: int, value: int) -> None:
+        _check(lib().gqa_set_option(self._h, option, value))
+
+    def reserve(self, n_seq: int, max_len: int) -> None:
+        _check(lib().gqa_reserve(self._h, n_seq, max_len))
+
+    def device_status(self, clear: bool = True) -> int:
+        st = _i(0)
+        _check(lib().gqa_device_status(self._h, ctypes.byref(st), 1 if clear else 0))
+        return st.value
+
+    def inv_freq(self) -> np.ndarray:
+        buf = (ctypes.c_float * (self.head_dim // 2))()
+        _check(lib().gqa_inv_freq(self._h, buf))
+        return np.frombuffer(buf, dtype=np.float32).copy()
+
+    # -- KV cache -----------------------------------------------------------
+    def kv_alloc(self, n_layers: int) -> list[LayerKV]:
+        arr = (LayerKV * n_layers)()
+        _check(lib().gqa_kv_alloc(self._h, n_layers, arr))
+        return [arr[i] for i in range(n_layers)]
+
+    def kv_free(self, kvs) -> None:
+        arr = _kv_array(kvs)
+        _check(lib().gqa_kv_free(self._h, len(arr), arr))
+
+    # -- layer call ---------------------------------------------------------
+    def layer_attention(self, kv: LayerKV, qkv, pos: int, seq_len: int, stream=None) -> None:
+        _check(lib().gqa_layer_attention(self._h, _stream(stream), ctypes.byref(kv), _ptr(qkv),
+                                         pos, seq_len))
+
+    def layer_attention_out(self, kv: LayerKV, qkv, pos: int, seq_len: int, out,
+                            stream=None) -> None:
+        _check(lib().gqa_layer_attention_out(self._h, _stream(stream), ctypes.byref(kv),
+                                             _ptr(qkv), pos, seq_len, _ptr(out)))
+
+    def decode_layers(self, kvs, qkv, qkv_stride: int, out, out_stride: int, d_pos,
+                      advance: bool = False, wrap_lo: int = 0, wrap_hi: int = 0,
+                      stream=None) -> None:
+        arr = _kv_array(kvs)
+        _check(lib().gqa_decode_layers(self._h, _stream(stream), len(arr), arr, _ptr(qkv),
+                                       qkv_stride, _ptr(out), out_stride, _ptr(d_pos),
+                                       1 if advance else 0, wrap_lo, wrap_hi))
+
+    def graph_create_layers(self, kvs, qkv, qkv_stride: int, out, out_stride: int, d_pos,
+                            advance: bool = True, wrap_lo: int = 0, wrap_hi: int = 0) -> Graph:
+        arr = _kv_array(kvs)
+        h = _vp()
+        _check(lib().gqa_graph_create_layers(self._h, len(arr), arr, _ptr(qkv), qkv_stride,
+                                             _ptr(out), out_stride, _ptr(d_pos),
+                                             1 if advance else 0, wrap_lo, wrap_hi,
+                                             ctypes.byref(h)))
+        return Graph(h.value, (arr,))
+
+    # -- kernel-level operations ---------------------------------------------
+    def rope_kv_append(self, kv: LayerKV, q, k, v, pos: int, stream=None) -> None:
+        _check(lib().gqa_rope_kv_append(self._h, _stream(stream), ctypes.byref(kv), _ptr(q),
+                                        _ptr(k), _ptr(v), pos))
+
+    def decode(self, kv: LayerKV, q_rot, seq_len: int, out, stream=None) -> None:
+        _check(lib().gqa_decode(self._h, _stream(stream), ctypes.byref(kv), _ptr(q_rot), seq_len,
+                                _ptr(out)))
+
+    def decode_batched(self, n_seq: int, k_ptrs, v_ptrs, qkv, qkv_stride: int, seq_lens,
+                       max_len: int, out, out_stride: int, stream=None) -> None:
+        _check(lib().gqa_decode_batched(self._h, _stream(stream), n_seq, _ptr(k_ptrs),
+                                        _ptr(v_ptrs), _ptr(qkv), qkv_stride, _ptr(seq_lens),
+                                        max_len, _ptr(out), out_stride))
+
+    def decode_split_partial(self, kv: LayerKV, q_rot, t_begin: int, t_end: int, m, l, o,
+                             stream=None) -> None:
+        _check(lib().gqa_decode_split_partial(self._h, _stream(stream), ctypes.byref(kv),
+                                              _ptr(q_rot), t_begin, t_end, _ptr(m), _ptr(l),
+                                              _ptr(o)))
+
+    def lse_combine(self, n_parts: int, n_rows: int, m, l, o, out, stream=None) -> None:
+        _check(lib().gqa_lse_combine(self._h, _stream(stream), n_parts, n_rows, _ptr(m), _ptr(l),
+                                     _ptr(o), _ptr(out)))
+
+    def fill_normal(self, dst, n: int, seed: int, stream_id: int, offset: int = 0,
+                    stream=None) -> None:
+        _check(lib().gqa_fill_normal(self._h, _stream(stream), _ptr(dst), n, seed, stream_id,
+                                     offset))

@@ -1,0 +1,110 @@
+"""Seeded synthetic inputs shared by the tests, the fixtures and the bench.
+
+Every tensor is drawn from a named stream of one 64-bit seed: element ``e`` of
+stream ``(seed, stream_id)`` is one half of the Box-Muller pair ``e // 2``
+whose two uniforms are the splitmix64 outputs number ``e - e % 2`` and
+``e - e % 2 + 1`` of the stream key (splitmix64: Steele, Lea, Flood, "Fast
+splittable pseudorandom number generators", OOPSLA 2014; Box-Muller in double
+precision, then rounded to fp32).  Being counter-based, any slice can be
+generated on its own; ``gqa_fill_normal`` in the library produces the same
+streams on the device.
+
+The reference seeds glibc ``rand()`` with 42 and draws uniform values
+(compute/attention-gqa-resident/attention_gqa_benchmark.c:350-369); the
+workloads here ask for N(0, 1) q/k/v and caches instead, so the generator is
+our own.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+_GOLDEN = np.uint64(0x9E3779B97F4A7C15)
+_M1 = np.uint64(0xBF58476D1CE4E5B9)
+_M2 = np.uint64(0x94D049BB133111EB)
+_STREAM_MUL = 0xD1B54A32D192ED03
+_MASK = (1 << 64) - 1
+
+# Stream ids used across tests and the bench, so that the same seed names the
+# same tensor everywhere.
+QKV, K_CACHE, V_CACHE, LENGTHS, PREFILL_Q, PREFILL_K, PREFILL_V = 1, 2, 3, 4, 5, 6, 7
+
+
+def _mix(z: np.ndarray) -> np.ndarray:
+    z = (z ^ (z >> np.uint64(30))) * _M1
+    z = (z ^ (z >> np.uint64(27))) * _M2
+    return z ^ (z >> np.uint64(31))
+
+
+def _mix_int(z: int) -> int:
+    z &= _MASK
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _MASK
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _MASK
+    return z ^ (z >> 31)
+
+
+def stream_key(seed: int, stream_id: int) -> int:
+    """Key of stream ``stream_id`` of ``seed`` (same formula as gqa_fill_normal)."""
+    return _mix_int((seed & _MASK) ^ ((stream_id * _STREAM_MUL) & _MASK))
+
+
+def uniform_u64(seed: int, stream_id: int, n: int, offset: int = 0) -> np.ndarray:
+    """splitmix64 outputs number offset .. offset+n-1 of the stream."""
+    key = np.uint64(stream_key(seed, stream_id))
+    idx = np.arange(offset, offset + n, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        return _mix(key + (idx + np.uint64(1)) * _GOLDEN)
+
+
+def normal(seed: int, stream_id: int, n: int, offset: int = 0) -> np.ndarray:
+    """fp32 N(0, 1) values number offset .. offset+n-1 of the stream."""
+    if n <= 0:
+        return np.zeros(0, dtype=np.float32)
+    first_pair = offset // 2
+    last_pair = (offset + n - 1) // 2
+    n_pairs = last_pair - first_pair + 1
+    r = uniform_u64(seed, stream_id, 2 * n_pairs, 2 * first_pair)
+    r1 = r[0::2]
+    r2 = r[1::2]
+    u1 = ((r1 >> np.uint64(11)).astype(np.float64) + 1.0) * (1.0 / 9007199254740992.0)
+    u2 = (r2 >> np.uint64(11)).astype(np.float64) * (1.0 / 9007199254740992.0)
+    rad = np.sqrt(-2.0 * np.log(u1))
+    ang = 6.283185307179586 * u2
+    out = np.empty(2 * n_pairs, dtype=np.float64)
+    out[0::2] = rad * np.cos(ang)
+    out[1::2] = rad * np.sin(ang)
+    start = offset - 2 * first_pair
+    return out[start:start + n].astype(np.float32)
+
+
+def uniform_int(seed: int, stream_id: int, n: int, lo: int, hi: int) -> np.ndarray:
+    """n integers uniform in [lo, hi] (inclusive), by 128-bit multiply-shift."""
+    r = uniform_u64(seed, stream_id, n)
+    span = hi - lo + 1
+    return np.array([lo + ((int(x) * span) >> 64) for x in r], dtype=np.int64)
+
+
+def grid_uniform(seed: int, stream_id: int, n: int) -> np.ndarray:
+    """Values on the grid {-1.00, -0.99, ..., 0.99}: the distribution of the
+    reference benchmark's cache contents (attention_gqa_benchmark.c:366-369),
+    drawn from our own generator instead of glibc rand()."""
+    r = uniform_u64(seed, stream_id, n)
+    return ((r % np.uint64(200)).astype(np.int64) - 100).astype(np.float32) * np.float32(0.01)
+
+
+def decode_inputs(seed: int, t_max: int = 4096, n_heads_q: int = 12, n_heads_kv: int = 2,
+                  dist: str = "normal"):
+    """(qkv [n_q*128 + 2*n_kv*128], k_cache, v_cache [n_kv][t_max][128]) for one
+    layer of one sequence.  dist "normal": everything N(0,1); "grid": q/k/v
+    N(0,1) and the caches on the reference benchmark's uniform grid."""
+    n_qkv = (n_heads_q + 2 * n_heads_kv) * 128
+    qkv = normal(seed, QKV, n_qkv)
+    n = n_heads_kv * t_max * 128
+    if dist == "normal":
+        kc = normal(seed, K_CACHE, n)
+        vc = normal(seed, V_CACHE, n)
+    elif dist == "grid":
+        kc = grid_uniform(seed, K_CACHE, n)
+        vc = grid_uniform(seed, V_CACHE, n)
+    else:
+        raise ValueError(dist)
+    return qkv, kc.reshape(n_heads_kv, t_max, 128), vc.reshape(n_heads_kv, t_max, 128)

@@ -1,0 +1,220 @@
+"""ctypes access to the oracle -- TEST INFRASTRUCTURE ONLY.
+
+Imported only by tests/, __graft_entry__.smoke() and the cpu_baseline leg of
+bench.py, as the checker (never as the thing measured or shipped).
+
+* ``liboracle.so``      -- gqa_oracle.c, the C restatement of the reference's
+                           fp32 attention with run-time shapes (any t_max).
+* ``_ref/libgqa_ref_bench.so`` / ``_ref/libgqa_ref_layer.so`` -- the
+  reference's own cpu_attention_gqa_pipeline (attention_gqa_benchmark.c:109-216)
+  and cpu_decoder_layer_step (test_28_layers_real.c:192-318), compiled
+  unmodified from its sources by oracle/Makefile.  They exist only where the
+  reference sources were present at build time; REF_T_MAX = 4096 is their
+  compile-time cache stride.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_BENCH_SO = os.path.join(HERE, "_ref", "libgqa_ref_bench.so")
+REF_LAYER_SO = os.path.join(HERE, "_ref", "libgqa_ref_layer.so")
+REF_T_MAX = 4096
+
+_f = ctypes.c_float
+_i = ctypes.c_int
+_fp = ctypes.POINTER(ctypes.c_float)
+_ip = ctypes.POINTER(ctypes.c_int)
+_fpp = ctypes.POINTER(_fp)
+
+_libs: dict[str, ctypes.CDLL] = {}
+
+
+def build() -> None:
+    """make -C oracle (restatement always; the reference only if its sources exist)."""
+    import subprocess
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _load(path: str) -> ctypes.CDLL:
+    if path not in _libs:
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} not built (run make -C oracle)")
+        _libs[path] = ctypes.CDLL(path)
+    return _libs[path]
+
+
+def have_reference() -> bool:
+    return os.path.exists(REF_BENCH_SO) and os.path.exists(REF_LAYER_SO)
+
+
+def _fptr(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_fp)
+
+
+def _lib():
+    lib = _load(ORACLE_SO)
+    if not getattr(lib, "_typed", False):
+        lib.oracle_inv_freq.argtypes = [_f, _i, _fp]
+        lib.oracle_rope_kv_append.argtypes = [_fp, _fp, _fp, _fp, _fp, _i, _i, _i, _i, _i, _f]
+        lib.oracle_attention.argtypes = [_fp, _fp, _fp, _i, _i, _i, _i, _i, _fp]
+        lib.oracle_layer_attention.argtypes = [_fp, _fp, _fp, _i, _i, _i, _i, _i, _i, _f]
+        lib.oracle_decode_batched.argtypes = [_i, _fpp, _fpp, _fpp, _ip, _i, _i, _i, _i, _f, _fpp,
+                                              _i]
+        lib.oracle_attention_batched.argtypes = [_i, _fpp, _fpp, _fpp, _ip, _i, _i, _i, _i, _fpp,
+                                                 _i]
+        lib.oracle_attention_partial.argtypes = [_fp, _fp, _fp, _i, _i, _i, _i, _i, _i, _fp, _fp,
+                                                 _fp]
+        lib.oracle_lse_combine.argtypes = [_i, _fp, _fp, _fp, _i, _i, _fp]
+        lib.oracle_prefill_rows.argtypes = [_fp, _fp, _fp, _i, _i, _i, _i, _i, _f, _fp, _fp, _ip,
+                                            _i, _fp, _i]
+        for fn in (lib.oracle_inv_freq, lib.oracle_rope_kv_append, lib.oracle_attention,
+                   lib.oracle_layer_attention, lib.oracle_decode_batched,
+                   lib.oracle_attention_batched, lib.oracle_attention_partial,
+                   lib.oracle_lse_combine, lib.oracle_prefill_rows):
+            fn.restype = None
+        lib._typed = True
+    return lib
+
+
+def inv_freq(rope_base: float = 1e6, head_dim: int = 128) -> np.ndarray:
+    out = np.zeros(head_dim // 2, dtype=np.float32)
+    _lib().oracle_inv_freq(rope_base, head_dim, _fptr(out))
+    return out
+
+
+def layer_attention(qkv: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, pos: int,
+                    seq_len: int, n_heads_q: int = 12, n_heads_kv: int = 2,
+                    rope_base: float = 1e6) -> None:
+    """In place: caches [n_kv][t_max][128] get row pos, qkv[:n_q*128] becomes attn_out."""
+    t_max = k_cache.shape[1]
+    _lib().oracle_layer_attention(_fptr(qkv), _fptr(k_cache), _fptr(v_cache), pos, seq_len, t_max,
+                                  n_heads_q, n_heads_kv, 128, rope_base)
+
+
+def rope_kv_append(q, k, v, k_cache, v_cache, pos, n_heads_q=12, n_heads_kv=2, rope_base=1e6):
+    t_max = k_cache.shape[1]
+    _lib().oracle_rope_kv_append(_fptr(q), _fptr(k), _fptr(v), _fptr(k_cache), _fptr(v_cache),
+                                 pos, t_max, n_heads_q, n_heads_kv, 128, rope_base)
+
+
+def attention(q, k_cache, v_cache, seq_len, n_heads_q=12, n_heads_kv=2) -> np.ndarray:
+    out = np.zeros(n_heads_q * 128, dtype=np.float32)
+    _lib().oracle_attention(_fptr(q), _fptr(k_cache), _fptr(v_cache), seq_len, k_cache.shape[1],
+                            n_heads_q, n_heads_kv, 128, _fptr(out))
+    return out
+
+
+def _ptr_array(arrs):
+    return (_fp * len(arrs))(*[_fptr(a) for a in arrs])
+
+
+def decode_batched(qkv: list, k_caches: list, v_caches: list, seq_lens, n_heads_q=12,
+                   n_heads_kv=2, rope_base=1e6, n_threads=None) -> list:
+    """One new token per sequence; caches appended in place; returns attn_out per sequence."""
+    n = len(qkv)
+    outs = [np.zeros(n_heads_q * 128, dtype=np.float32) for _ in range(n)]
+    lens = (ctypes.c_int * n)(*[int(x) for x in seq_lens])
+    _lib().oracle_decode_batched(n, _ptr_array(qkv), _ptr_array(k_caches), _ptr_array(v_caches),
+                                 lens, k_caches[0].shape[1], n_heads_q, n_heads_kv, 128, rope_base,
+                                 _ptr_array(outs), n_threads or os.cpu_count())
+    return outs
+
+
+def attention_batched(q: list, k_caches: list, v_caches: list, seq_lens, n_heads_q=12,
+                      n_heads_kv=2, n_threads=None) -> list:
+    n = len(q)
+    outs = [np.zeros(n_heads_q * 128, dtype=np.float32) for _ in range(n)]
+    lens = (ctypes.c_int * n)(*[int(x) for x in seq_lens])
+    _lib().oracle_attention_batched(n, _ptr_array(q), _ptr_array(k_caches), _ptr_array(v_caches),
+                                    lens, k_caches[0].shape[1], n_heads_q, n_heads_kv, 128,
+                                    _ptr_array(outs), n_threads or os.cpu_count())
+    return outs
+
+
+def attention_partial(q, k_cache, v_cache, t_begin, t_end, n_heads_q=12, n_heads_kv=2):
+    m = np.zeros(n_heads_q, dtype=np.float32)
+    l = np.zeros(n_heads_q, dtype=np.float32)
+    o = np.zeros(n_heads_q * 128, dtype=np.float32)
+    _lib().oracle_attention_partial(_fptr(q), _fptr(k_cache), _fptr(v_cache), t_begin, t_end,
+                                    k_cache.shape[1], n_heads_q, n_heads_kv, 128, _fptr(m),
+                                    _fptr(l), _fptr(o))
+    return m, l, o
+
+
+def lse_combine(m: np.ndarray, l: np.ndarray, o: np.ndarray) -> np.ndarray:
+    """m, l: [parts][rows]; o: [parts][rows][128] -> [rows][128]."""
+    n_parts, n_rows = m.shape
+    out = np.zeros((n_rows, 128), dtype=np.float32)
+    _lib().oracle_lse_combine(n_parts, _fptr(np.ascontiguousarray(m)),
+                              _fptr(np.ascontiguousarray(l)), _fptr(np.ascontiguousarray(o)),
+                              n_rows, 128, _fptr(out))
+    return out
+
+
+def prefill_rows(q, k, v, rows, n_heads_q=12, n_heads_kv=2, rope_base=1e6, n_threads=None):
+    """Causal attention rows of one sequence (q/k/v [S][heads*128], pre-RoPE)."""
+    S = q.shape[0]
+    kc = np.zeros((n_heads_kv, S, 128), dtype=np.float32)
+    vc = np.zeros((n_heads_kv, S, 128), dtype=np.float32)
+    rows_c = (ctypes.c_int * len(rows))(*[int(r) for r in rows])
+    out = np.zeros((len(rows), n_heads_q * 128), dtype=np.float32)
+    _lib().oracle_prefill_rows(_fptr(q), _fptr(k), _fptr(v), S, S, n_heads_q, n_heads_kv, 128,
+                               rope_base, _fptr(kc), _fptr(vc), rows_c, len(rows), _fptr(out),
+                               n_threads or os.cpu_count())
+    return out, kc, vc
+
+
+# ---- the reference itself (compiled from its sources) ----------------------
+
+def _ref_lib(path, prefix):
+    lib = _load(path)
+    fn = getattr(lib, prefix + "_attention")
+    if fn.argtypes is None:
+        fn.argtypes = [_fp, _fp, _fp, _i, _i, _fp]
+        fn.restype = _i
+    return lib
+
+
+def ref_bench_attention(qkv: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, pos: int,
+                        seq_len: int) -> np.ndarray:
+    """cpu_attention_gqa_pipeline with q/k/v injected; caches [2][4096][128] updated in place."""
+    assert k_cache.shape == (2, REF_T_MAX, 128) and v_cache.shape == (2, REF_T_MAX, 128)
+    out = np.zeros(1536, dtype=np.float32)
+    rc = _ref_lib(REF_BENCH_SO, "ref_bench").ref_bench_attention(
+        _fptr(qkv), _fptr(k_cache), _fptr(v_cache), pos, seq_len, _fptr(out))
+    if rc != 0:
+        raise ValueError("reference rejected pos/seq_len")
+    return out
+
+
+def ref_bench_attention_many(qkv: list, k_caches: list, v_caches: list, pos: list,
+                             seq_len: list, n_threads: int) -> list:
+    lib = _load(REF_BENCH_SO)
+    fn = lib.ref_bench_attention_many
+    if fn.argtypes is None:
+        fn.argtypes = [_i, _fpp, _fpp, _fpp, _ip, _ip, _fpp, _i]
+        fn.restype = _i
+    n = len(qkv)
+    outs = [np.zeros(1536, dtype=np.float32) for _ in range(n)]
+    rc = fn(n, _ptr_array(qkv), _ptr_array(k_caches), _ptr_array(v_caches),
+            (ctypes.c_int * n)(*pos), (ctypes.c_int * n)(*seq_len), _ptr_array(outs), n_threads)
+    if rc != 0:
+        raise ValueError("reference rejected pos/seq_len")
+    return outs
+
+
+def ref_layer_attention(qkv, k_cache, v_cache, pos, seq_len) -> np.ndarray:
+    """cpu_decoder_layer_step's attention slice (weights chosen so y_out == attn_out)."""
+    assert k_cache.shape == (2, REF_T_MAX, 128)
+    out = np.zeros(1536, dtype=np.float32)
+    rc = _ref_lib(REF_LAYER_SO, "ref_layer").ref_layer_attention(
+        _fptr(qkv), _fptr(k_cache), _fptr(v_cache), pos, seq_len, _fptr(out))
+    if rc != 0:
+        raise ValueError("reference rejected pos/seq_len")
+    return out

@@ -1,0 +1,76 @@
+/*
+ * TEST INFRASTRUCTURE (oracle) -- never linked into the product library.
+ *
+ * Compiles the decoder-layer CPU reference cpu_decoder_layer_step() from
+ * compute/gguf-real-weights-loader/test_28_layers_real.c:192-318 unmodified
+ * (the Makefile passes the file's path as REF_LAYER_SRC).  Its attention slice
+ * (:219-289) is the production caller's math: same RoPE/append as the
+ * standalone benchmark, but the softmax normaliser is 1/sum (:276) instead of
+ * 1/(sum + 1e-12) (attention_gqa_benchmark.c:195).
+ *
+ * The layer only returns the post-FFN residual, so we choose weights that
+ * make that residual equal to the attention output exactly:
+ *   x_in = 0, W_qkv = 0 with bias = [q | k | v]  -> qkv = bias       (:211-213)
+ *   W_o = identity (nibble 9 on the diagonal, 8 elsewhere, fp16 scale 1.0)
+ *                                                -> r = attn_out + 0  (:291-296)
+ *   W_gate = W_up = W_down = 0                  -> y_out = r          (:309-317)
+ * Every product with a zero weight is +-0 and every sum with it is exact, so
+ * y_out == attn_out bit for bit.
+ */
+#include <pthread.h>
+
+#define main gqa_reference_layer_main_unused
+#include REF_LAYER_SRC
+#undef main
+
+static LayerWeightsHost g_w;
+static float g_x0[D_MODEL];
+static pthread_once_t g_once = PTHREAD_ONCE_INIT;
+
+static block_q4_0 *alloc_blocks(size_t rows, size_t cols, int identity) {
+    size_t nb = cols / 32;
+    block_q4_0 *b = (block_q4_0 *)malloc(sizeof(block_q4_0) * rows * nb);
+    for (size_t i = 0; i < rows * nb; i++) {
+        b[i].d = 0x3C00; /* fp16 1.0 */
+        memset(b[i].qs, 0x88, sizeof(b[i].qs));
+    }
+    if (identity) {
+        for (size_t r = 0; r < rows; r++) {
+            block_q4_0 *blk = &b[r * nb + r / 32];
+            int j = (int)(r % 32);
+            /* low nibble of qs[j] is weight j, high nibble of qs[j-16] is weight j */
+            if (j < 16) blk->qs[j] = 0x89;
+            else blk->qs[j - 16] = 0x98;
+        }
+    }
+    return b;
+}
+
+static float g_bias_unused[D_QKV];
+
+static void init_weights(void) {
+    g_w.gamma_attn = (float *)malloc(sizeof(float) * D_MODEL);
+    g_w.gamma_ffn = (float *)malloc(sizeof(float) * D_MODEL);
+    for (int i = 0; i < D_MODEL; i++) { g_w.gamma_attn[i] = 1.0f; g_w.gamma_ffn[i] = 1.0f; g_x0[i] = 0.0f; }
+    g_w.b_qkv = g_bias_unused;
+    g_w.W_qkv = alloc_blocks(D_QKV, D_MODEL, 0);
+    g_w.W_o = alloc_blocks(D_MODEL, D_MODEL, 1);
+    g_w.W_gate = alloc_blocks(D_FFN, D_MODEL, 0);
+    g_w.W_up = alloc_blocks(D_FFN, D_MODEL, 0);
+    g_w.W_down = alloc_blocks(D_MODEL, D_FFN, 0);
+}
+
+int ref_layer_t_max(void) { return T_MAX; }
+
+/* qkv_in [2048] (pre-RoPE q|k|v); caches [2][4096][128] updated at row pos;
+ * attn_out [1536]. */
+int ref_layer_attention(const float *qkv_in, float *k_cache, float *v_cache,
+                        int pos, int seq_len, float *attn_out) {
+    if (pos < 0 || pos >= T_MAX || seq_len < 1 || seq_len > T_MAX) return -1;
+    pthread_once(&g_once, init_weights);
+    LayerWeightsHost w = g_w;
+    w.b_qkv = (float *)qkv_in; /* read-only inside the reference */
+    LayerKVHost kv = { k_cache, v_cache };
+    cpu_decoder_layer_step(g_x0, &w, &kv, pos, seq_len, attn_out);
+    return 0;
+}
