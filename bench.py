@@ -331,7 +331,8 @@ def run_resident(args, g, ctx, rank, world, local):
 
     # mirrors the library's split plan for pos read from the device (planned for t_max)
     n_sm = torch.cuda.get_device_properties(local).multi_processor_count
-    n_splits = min(-(-n_sm // N_KV), -(-t_max // 32))
+    target = args.target_ctas or n_sm
+    n_splits = min(-(-target // N_KV), -(-t_max // g.gqa.VARIANT_QUANT[args.variant]))
     kernels_per_step = L_layers * (2 if n_splits > 1 else 1) + 1
     for gr in graphs + [g_e2e]:
         gr.destroy()
@@ -421,6 +422,12 @@ def run_ours(args):
     wl = WORKLOADS[args.workload]
     t_max = wl.get("t_max") or (wl["len_hi"] + wl["window"])
     ctx = g.Context(t_max=t_max, device=local)
+    if args.variant:
+        ctx.set_option(g.gqa.GQA_OPT_KERNEL_VARIANT, args.variant)
+    if args.target_ctas:
+        ctx.set_option(g.gqa.GQA_OPT_TARGET_CTAS, args.target_ctas)
+    if args.batch_chunk:
+        ctx.set_option(g.gqa.GQA_OPT_BATCH_CHUNK, args.batch_chunk)
     if args.workload in ("resident28", "single"):
         r = run_resident(args, g, ctx, rank, world, local)
     else:
@@ -446,7 +453,9 @@ def run_ours(args):
             "ms_per_step": round(t / args.steps * 1e3, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)",
-            "config": workload_config(args.workload),
+            "config": dict(workload_config(args.workload), kernel_variant=args.variant,
+                           target_ctas=args.target_ctas or None,
+                           batch_chunk=args.batch_chunk or None),
             "tok_per_s": round(tokens / t, 1),
             "hbm_frac_of_measured": round(gbs / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
@@ -480,6 +489,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="resident28")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # tuning knobs (defaults are the library's own choices)
+    ap.add_argument("--variant", type=int, default=0, help=argparse.SUPPRESS)
+    ap.add_argument("--target-ctas", type=int, default=0, help=argparse.SUPPRESS)
+    ap.add_argument("--batch-chunk", type=int, default=0, help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -170,9 +170,11 @@ GQA_API int gqa_decode_batched(gqa_ctx *ctx, gqa_stream_t stream, int n_seq, flo
                        const int *seq_lens, int max_len, float *out, long long out_stride);
 
 /* Split-KV partial over cache rows [t_begin, t_end) for already-rotated q:
- * per q head h, m[h] = max score (natural-log units, scores scaled by
- * 1/sqrt(128)), l[h] = sum exp(s - m), o[h][:] = sum exp(s - m) v (not
- * normalised).  An empty range yields m = -inf, l = 0. */
+ * per q head h, a reference value m[h] (natural-log units; scores are
+ * q.k / sqrt(128)), l[h] = sum exp(s - m) and o[h][:] = sum exp(s - m) v (not
+ * normalised).  m is at most the maximum score and trails it by at most
+ * 8 ln 2; (m, l, o) is exact up to that common factor, which a log-sum-exp
+ * combine removes.  An empty range yields m = -inf, l = 0, o = 0. */
 GQA_API int gqa_decode_split_partial(gqa_ctx *ctx, gqa_stream_t stream, const gqa_layer_kv *kv,
                              const float *q_rot, int t_begin, int t_end, float *m, float *l,
                              float *o);

@@ -17,7 +17,9 @@ namespace gqa {
 size_t decode_smem_bytes();
 cudaError_t prepare_decode_kernels();
 cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cudaStream_t st,
-                                bool pdl);
+                                bool pdl, int variant);
+int decode_variant_count();
+int decode_variant_quant(int variant);
 cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl);
 cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k_ptrs,
                                float* const* v_ptrs, float* k_base, float* v_base,
@@ -45,6 +47,7 @@ struct gqa_ctx {
   int target_ctas = 0;
   int batch_chunk = 0;  // tokens per split in batched decode (0 = automatic)
   int live_graphs = 0;  // graphs hold scratch pointers: no reallocation while > 0
+  int variant = 0;      // decode kernel shape (tuning knob)
 };
 
 struct gqa_graph {
@@ -94,7 +97,6 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
-constexpr int kCtaQuant = 32;  // must match decode_split_kernel's range quantum
 
 bool is_capturing(cudaStream_t st) {
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
@@ -135,14 +137,15 @@ int ensure_scratch(gqa_ctx* c, long long slots, cudaStream_t st) {
 int plan_splits_single(const gqa_ctx* c, int rows_kv, int len) {
   const int target = c->target_ctas > 0 ? c->target_ctas : c->n_sm;
   int want = ceil_div(target, rows_kv);
-  const int most = ceil_div(len, kCtaQuant);
+  const int most = ceil_div(len, decode_variant_quant(c->variant));
   if (want > most) want = most;
   return want < 1 ? 1 : want;
 }
 
 int batch_chunk(const gqa_ctx* c, int max_len) {
-  if (c->batch_chunk > 0) return ((c->batch_chunk + kCtaQuant - 1) / kCtaQuant) * kCtaQuant;
-  return max_len > 8192 ? 1024 : 256;
+  const int q = decode_variant_quant(c->variant);
+  const int want = c->batch_chunk > 0 ? c->batch_chunk : (max_len > 8192 ? 1024 : 256);
+  return ((want + q - 1) / q) * q;
 }
 
 DecodeParams base_params(gqa_ctx* c) {
@@ -154,7 +157,7 @@ DecodeParams base_params(gqa_ctx* c) {
   p.status = c->status;
   p.part_o = c->part_o;
   p.part_ml = c->part_ml;
-  p.min_chunk = kCtaQuant;
+  p.min_chunk = decode_variant_quant(c->variant);
   p.lengths_stable = 1;
   return p;
 }
@@ -199,7 +202,7 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
   p.lengths_stable = lengths_stable ? 1 : 0;
   p.n_splits = n_splits;
   p.out = out;
-  GQA_CUDA(launch_decode_split(p, 1, fused, st, pdl_first));
+  GQA_CUDA(launch_decode_split(p, 1, fused, st, pdl_first, c->variant));
   if (n_splits > 1) {
     CombineParams cp = combine_from_scratch(c, n_splits);
     cp.out = out;
@@ -312,6 +315,11 @@ int gqa_set_option(gqa_ctx* c, int option, long long value) {
     case 3: /* GQA_OPT_BATCH_CHUNK (internal tuning knob) */
       if (value < 0 || value > (1 << 20)) return fail(GQA_ERR_INVALID_ARG, "chunk out of range");
       c->batch_chunk = (int)value;
+      return GQA_OK;
+    case 4: /* GQA_OPT_KERNEL_VARIANT (internal tuning knob) */
+      if (value < 0 || value >= decode_variant_count())
+        return fail(GQA_ERR_INVALID_ARG, "kernel variant out of range");
+      c->variant = (int)value;
       return GQA_OK;
     default: return fail(GQA_ERR_INVALID_ARG, "unknown option %d", option);
   }
@@ -549,7 +557,7 @@ int gqa_decode_batched(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const*
   p.min_chunk = chunk;
   p.out = out;
   p.out_stride = out_stride;
-  GQA_CUDA(launch_decode_split(p, n_seq, true, st, c->pdl != 0));
+  GQA_CUDA(launch_decode_split(p, n_seq, true, st, c->pdl != 0, c->variant));
   if (n_splits > 1) {
     CombineParams cp = combine_from_scratch(c, n_splits);
     cp.out = out;
@@ -589,7 +597,7 @@ int gqa_decode_split_partial(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv
     p.t_end = t_end;
     p.n_splits = n_splits;
     p.out = nullptr;  // always write partials
-    GQA_CUDA(launch_decode_split(p, 1, false, st, c->pdl != 0));
+    GQA_CUDA(launch_decode_split(p, 1, false, st, c->pdl != 0, c->variant));
     cp = combine_from_scratch(c, n_splits);
   } else {
     cp.rows_per_seq = nq;

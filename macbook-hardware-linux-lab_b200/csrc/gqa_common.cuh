@@ -140,8 +140,9 @@ struct DecodeParams {
   int t_begin;   // first cache row attended (0 except for KV-range shards)
   int t_end;     // if > 0: attend rows [t_begin, t_end) instead of [t_begin, seq_len)
 
-  int n_splits;  // grid.x
-  int min_chunk;  // tokens; every split covers a multiple of 32 tokens
+  int n_splits;   // grid.x
+  int min_chunk;  // tokens; every split covers a multiple of `quant` tokens
+  int quant;      // set by the launcher from the kernel shape
 
   const float* inv_freq;  // [64] RoPE inverse frequencies
   float q_scale;          // softmax scale * log2(e), folded into q

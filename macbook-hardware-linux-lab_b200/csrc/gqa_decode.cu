@@ -28,29 +28,26 @@
 
 namespace gqa {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;  // == kHeadDim: one thread per dim in the epilogue
-constexpr int kStageTok = 8;
-constexpr int kStages = 3;
-constexpr int kCtaQuant = kWarps * kStageTok;  // CTA ranges are multiples of 32 tokens
-constexpr float kRescaleThresh = 8.0f;         // log2 units
+constexpr float kRescaleThresh = 8.0f;           // log2 units
 constexpr long long kWaitBudget = 2000000000LL;  // ~1 s of SM clocks per wait
 constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kG = 6;                            // q heads per KV head
 
-static_assert(kThreads == kHeadDim, "epilogue maps one thread per head dim");
-
-template <int G>
+// Kernel shape: NW streaming warps per CTA, each with a private ring of NS
+// stages of ST cache rows (K and V).  Instantiated shapes are listed in
+// decode_variant(); the host picks one per launch.
+template <int NW, int ST, int NS>
 struct DecodeSmem {
-  float k[kWarps][kStages][kStageTok * kHeadDim];
-  float v[kWarps][kStages][kStageTok * kHeadDim];
-  float q[G][kHeadDim];
+  float k[NW][NS][ST * kHeadDim];
+  float v[NW][NS][ST * kHeadDim];
+  float q[kG][kHeadDim];
   float newk[kHeadDim];
   float newv[kHeadDim];
   float cs[kHalf][2];
-  float p[kWarps][kStageTok][8];
-  float wm[kWarps][G];
-  float wl[kWarps][G];
-  uint64_t full[kWarps][kStages];
+  float p[NW][ST][8];
+  float wm[NW][kG];
+  float wl[NW][kG];
+  uint64_t full[NW][NS];
   int err;
 };
 
@@ -58,10 +55,10 @@ __device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b
 __device__ __forceinline__ int round_up_i(int a, int b) { return ceil_div_i(a, b) * b; }
 
 // Token range of split `split` when [t_begin, t_end) is cut into n_splits
-// chunks of a multiple of kCtaQuant tokens (at least min_chunk).  Shared by
-// the host planner (mirrored in gqa_api.cu) and the kernels.
-__device__ __forceinline__ int chunk_tokens(int len, int n_splits, int min_chunk) {
-  int c = round_up_i(ceil_div_i(len, n_splits), kCtaQuant);
+// chunks of a multiple of `quant` tokens (at least min_chunk).  The host
+// planner (gqa_api.cu) uses the same rule.
+__device__ __forceinline__ int chunk_tokens(int len, int n_splits, int min_chunk, int quant) {
+  int c = round_up_i(ceil_div_i(len, n_splits), quant);
   return c > min_chunk ? c : min_chunk;
 }
 
@@ -79,11 +76,14 @@ __device__ __forceinline__ void resolve_lengths(const Lengths& L, int seq, int& 
   }
 }
 
-// Butterfly reduce-scatter step: N values -> N/2, lanes with bit OFF set keep
-// the upper half.  After the steps 16,8,4,2 on 48 values, lane keeps original
-// indices base..base+2 with base = 24*b4 + 12*b3 + 6*b2 + 3*b1.
+// Reduce-scatter of ST*6 partial dot products (index t*6 + h) over the 32
+// lanes.  H = log2(2*ST) halving rounds at lane offsets 16, 8, ... leave each
+// lane 3 complete-over-the-upper-bits sums; the remaining offsets are summed
+// directly.  Lane ends up owning token t = lane >> (6 - H) and heads
+// h0..h0+2 with h0 = 3 * ((lane >> (5 - H)) & 1); the 2^(5-H) lanes that differ
+// only in the lowest bits hold identical copies.
 template <int N, int OFF>
-__device__ __forceinline__ void bfly_halve(float (&v)[48], int lane) {
+__device__ __forceinline__ void bfly_halve(float* v, int lane) {
   const bool up = (lane & OFF) != 0;
 #pragma unroll
   for (int i = 0; i < N / 2; ++i) {
@@ -93,17 +93,55 @@ __device__ __forceinline__ void bfly_halve(float (&v)[48], int lane) {
   }
 }
 
+template <int ST>
+struct Bfly {
+  static constexpr int H = ST == 8 ? 4 : ST == 4 ? 3 : ST == 2 ? 2 : -1;
+  static_assert(H > 0, "ST must be 2, 4 or 8");
+  static constexpr int kLowBits = 5 - H;  // duplicate-copy bits
+  __device__ __forceinline__ static void run(float* v, int lane) {
+    bfly_halve<ST * 6, 16>(v, lane);
+    if constexpr (H >= 2) bfly_halve<ST * 3, 8>(v, lane);
+    if constexpr (H >= 3) bfly_halve<ST * 3 / 2, 4>(v, lane);
+    if constexpr (H >= 4) bfly_halve<ST * 3 / 4, 2>(v, lane);
+#pragma unroll
+    for (int off = 1 << (kLowBits - 1); off > 0; off >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 3; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], off);
+    }
+  }
+  __device__ __forceinline__ static int token(int lane) { return lane >> (6 - H); }
+  __device__ __forceinline__ static int head0(int lane) { return 3 * ((lane >> (5 - H)) & 1); }
+  __device__ __forceinline__ static bool owner(int lane) {
+    return (lane & ((1 << kLowBits) - 1)) == 0;
+  }
+};
+
 __device__ __forceinline__ float warp_max(float x) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
   return x;
 }
 
-template <int G, bool FUSED>
-__global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeParams p) {
-  static_assert(G == 6, "the lane/score ownership map below is written for 6 q heads per KV head");
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+
+template <int NW>
+struct MinBlocks {
+  static constexpr int value = NW >= 8 ? 2 : 3;
+};
+
+template <int NW, int ST, int NS, bool FUSED>
+__global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
+    decode_split_kernel(const DecodeParams p) {
+  constexpr int G = kG;
+  constexpr int NT = NW * 32;
+  static_assert(NT % kHeadDim == 0, "epilogue maps threads onto head dims");
+  using B = Bfly<ST>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  DecodeSmem<G>& sm = *reinterpret_cast<DecodeSmem<G>*>(smem_raw);
+  DecodeSmem<NW, ST, NS>& sm = *reinterpret_cast<DecodeSmem<NW, ST, NS>*>(smem_raw);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x, hkv = blockIdx.y, seq = blockIdx.z;
@@ -128,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
   }
 
   const int len = r_end - p.t_begin;
-  const int chunk = chunk_tokens(len, p.n_splits, p.min_chunk);
+  const int chunk = chunk_tokens(len, p.n_splits, p.min_chunk, p.quant);
   const int c0 = p.t_begin + split * chunk;
   const int c1 = min(c0 + chunk, r_end);
   const long long prow = ((long long)seq * n_q + hkv * G) * p.n_splits + split;
@@ -145,11 +183,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
   }
 
   const int ctoks = c1 - c0;
-  const int wchunk = round_up_i(ceil_div_i(ctoks, kWarps), kStageTok);
+  const int wchunk = round_up_i(ceil_div_i(ctoks, NW), ST);
   const int w0 = c0 + warp * wchunk;
   const int w1 = min(w0 + wchunk, c1);
   const int n_tok = max(w1 - w0, 0);
-  const int n_it = ceil_div_i(n_tok, kStageTok);
+  const int n_it = ceil_div_i(n_tok, ST);
 
   float* kc;
   float* vc;
@@ -166,15 +204,15 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
   if (tid == 0) sm.err = 0;
   if (lane == 0) {
 #pragma unroll
-    for (int s = 0; s < kStages; ++s) mbar_init(&sm.full[warp][s], 1);
+    for (int s = 0; s < NS; ++s) mbar_init(&sm.full[warp][s], 1);
     fence_barrier_init();
   }
   __syncwarp();
 
   const uint64_t policy = l2_policy_evict_first();
   auto issue = [&](int stage, int it) {
-    const int t = w0 + it * kStageTok;
-    const int nt = min(kStageTok, w1 - t);
+    const int t = w0 + it * ST;
+    const int nt = min(ST, w1 - t);
     const uint32_t bytes = (uint32_t)nt * kRowBytes;
     mbar_arrive_expect_tx(&sm.full[warp][stage], 2 * bytes);
     bulk_copy_g2s(sm.k[warp][stage], kc + (long long)t * kHeadDim, bytes, &sm.full[warp][stage],
@@ -185,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
   // Cache rows before pos are not written by the preceding kernel: stream
   // them before waiting on it.
   if (lane == 0) {
-    for (int s = 0; s < kStages && s < n_it; ++s) issue(s, s);
+    for (int s = 0; s < NS && s < n_it; ++s) issue(s, s);
   }
 
   if (early) pdl_wait();
@@ -201,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
       sm.cs[tid][1] = sn;
     }
     __syncthreads();
-    for (int idx = tid; idx < G * kHalf; idx += kThreads) {
+    for (int idx = tid; idx < G * kHalf; idx += NT) {
       const int h = idx / kHalf, i = idx % kHalf;
       const float* qh = qin + (long long)(hkv * G + h) * kHeadDim;
       const float q0 = qh[i], q1 = qh[i + kHalf];
@@ -220,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
       sm.newv[tid + kHalf] = vin[tid + kHalf];
     }
   } else {
-    for (int idx = tid; idx < G * kHeadDim; idx += kThreads) {
+    for (int idx = tid; idx < G * kHeadDim; idx += NT) {
       const int h = idx / kHeadDim, d = idx % kHeadDim;
       sm.q[h][d] = qin[(long long)(hkv * G + h) * kHeadDim + d] * p.q_scale;
     }
@@ -253,15 +291,16 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
     for (int j = 0; j < 4; ++j) o[h][j] = 0.f;
   }
   float lown[3] = {0.f, 0.f, 0.f};
-  const int b1 = (lane >> 1) & 1;
-  const int tt = ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
-  const int hb = 3 * b1;
+  const int tt = B::token(lane);
+  const int hb = B::head0(lane);
+  const bool hi = hb != 0;
+  const bool own = B::owner(lane);
   int consumed = 0;
   bool failed = false;
 
   for (int it = 0; it < n_it; ++it) {
-    const int s = it % kStages;
-    const uint32_t par = (uint32_t)(it / kStages) & 1u;
+    const int s = it % NS;
+    const uint32_t par = (uint32_t)(it / NS) & 1u;
     bool ok = mbar_wait_bounded(&sm.full[warp][s], par, kWaitBudget);
     ok = __all_sync(0xffffffffu, ok);
     if (!ok) {
@@ -269,8 +308,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
       break;
     }
     consumed = it + 1;
-    const int t0 = w0 + it * kStageTok;
-    const int nt = min(kStageTok, w1 - t0);
+    const int t0 = w0 + it * ST;
+    const int nt = min(ST, w1 - t0);
     const float* ks = sm.k[warp][s];
     const float* vs = sm.v[warp][s];
 
@@ -281,10 +320,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
           reinterpret_cast<const float4*>(sm.newv)[lane];
     }
 
-    // ---- scores: 8 tokens x 6 heads, reduced over the 32 lanes ----
-    float part[48];
+    // ---- scores: ST tokens x 6 heads, reduced over the 32 lanes ----
+    float part[ST * G];
 #pragma unroll
-    for (int t = 0; t < kStageTok; ++t) {
+    for (int t = 0; t < ST; ++t) {
       if (t < nt) {
         const float* kr = (FUSED && t0 + t == pos) ? sm.newk : ks + t * kHeadDim;
         const float4 kv = reinterpret_cast<const float4*>(kr)[lane];
@@ -296,12 +335,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
         for (int h = 0; h < G; ++h) part[t * G + h] = 0.f;
       }
     }
-    bfly_halve<48, 16>(part, lane);
-    bfly_halve<24, 8>(part, lane);
-    bfly_halve<12, 4>(part, lane);
-    bfly_halve<6, 2>(part, lane);
-#pragma unroll
-    for (int i = 0; i < 3; ++i) part[i] += __shfl_xor_sync(0xffffffffu, part[i], 1);
+    B::run(part, lane);
 
     float sc[3];
     const bool valid = tt < nt;
@@ -311,27 +345,27 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
     // ---- online softmax with lazy max update ----
     float mo[3];
 #pragma unroll
-    for (int i = 0; i < 3; ++i) mo[i] = b1 ? m[3 + i] : m[i];
+    for (int i = 0; i < 3; ++i) mo[i] = hi ? m[3 + i] : m[i];
     const bool exceed = sc[0] > mo[0] + kRescaleThresh || sc[1] > mo[1] + kRescaleThresh ||
                         sc[2] > mo[2] + kRescaleThresh;
     if (__any_sync(0xffffffffu, exceed)) {
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float mine = ((h / 3) == b1) ? sc[h % 3] : -CUDART_INF_F;
+        const float mine = ((h / 3) == (hi ? 1 : 0)) ? sc[h % 3] : -CUDART_INF_F;
         const float mnew = fmaxf(m[h], warp_max(mine));
         const float alpha = (mnew == -CUDART_INF_F) ? 1.f : exp2f(m[h] - mnew);
 #pragma unroll
         for (int j = 0; j < 4; ++j) o[h][j] *= alpha;
-        if ((h / 3) == b1) lown[h % 3] *= alpha;
+        if ((h / 3) == (hi ? 1 : 0)) lown[h % 3] *= alpha;
         m[h] = mnew;
       }
 #pragma unroll
-      for (int i = 0; i < 3; ++i) mo[i] = b1 ? m[3 + i] : m[i];
+      for (int i = 0; i < 3; ++i) mo[i] = hi ? m[3 + i] : m[i];
     }
     float pv[3];
 #pragma unroll
     for (int i = 0; i < 3; ++i) pv[i] = exp2f(sc[i] - mo[i]);
-    if ((lane & 1) == 0) {
+    if (own) {
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
         lown[i] += pv[i];
@@ -342,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
 
     // ---- o += p . V ----
 #pragma unroll
-    for (int t = 0; t < kStageTok; ++t) {
+    for (int t = 0; t < ST; ++t) {
       if (t < nt) {
         const float4 pa = *reinterpret_cast<const float4*>(&sm.p[warp][t][0]);
         const float2 pb = *reinterpret_cast<const float2*>(&sm.p[warp][t][4]);
@@ -359,17 +393,17 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
       }
     }
     __syncwarp();
-    if (it + kStages < n_it && lane == 0) {
+    if (it + NS < n_it && lane == 0) {
       fence_proxy_async_smem();
-      issue(s, it + kStages);
+      issue(s, it + NS);
     }
   }
 
   if (failed) {
     // Drain whatever this warp still has in flight (bounded), then report.
-    const int issued = min(n_it, consumed + kStages);
+    const int issued = min(n_it, consumed + NS);
     for (int it = consumed; it < issued; ++it)
-      (void)mbar_wait_bounded(&sm.full[warp][it % kStages], (uint32_t)(it / kStages) & 1u,
+      (void)mbar_wait_bounded(&sm.full[warp][it % NS], (uint32_t)(it / NS) & 1u,
                               kWaitBudget / 16);
     if (lane == 0) {
       atomicOr(p.status, kStatusWaitTimeout);
@@ -379,23 +413,16 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
 
   // ---- per-warp (m, l, o) -> shared memory ----
 #pragma unroll
-  for (int i = 0; i < 3; ++i) {
-    float x = lown[i];
-    x += __shfl_xor_sync(0xffffffffu, x, 1);
-    x += __shfl_xor_sync(0xffffffffu, x, 4);
-    x += __shfl_xor_sync(0xffffffffu, x, 8);
-    x += __shfl_xor_sync(0xffffffffu, x, 16);
-    lown[i] = x;
+  for (int h = 0; h < G; ++h) {
+    const float mine = ((h / 3) == (hi ? 1 : 0)) ? lown[h % 3] : 0.f;
+    const float lsum = warp_sum(mine);
+    if (lane == 0) {
+      sm.wl[warp][h] = lsum;
+      sm.wm[warp][h] = m[h];
+    }
   }
-  if (lane == 0 || lane == 2) {
-#pragma unroll
-    for (int i = 0; i < 3; ++i) sm.wl[warp][hb + i] = lown[i];
-  }
-  if (lane == 0) {
-#pragma unroll
-    for (int h = 0; h < G; ++h) sm.wm[warp][h] = m[h];
-  }
-  // Each warp reuses stage 0 of its own ring (all its copies have landed).
+  // Each warp reuses stage 0 of its own K ring (all its copies have landed).
+  static_assert(NS * ST * kHeadDim >= G * kHeadDim, "K ring too small for the epilogue");
   float* ow = sm.k[warp][0];
 #pragma unroll
   for (int h = 0; h < G; ++h)
@@ -404,22 +431,27 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
   __syncthreads();
   if (sm.err) return;
 
-  // ---- merge the 4 warps; thread tid owns head dim d = tid ----
-  const int d = tid;
+  // ---- merge the warps; thread owns head dim d of heads hg*GPT .. ----
+  constexpr int NGRP = NT / kHeadDim;             // thread groups
+  constexpr int GPT = (G + NGRP - 1) / NGRP;      // heads per group
+  const int d = tid % kHeadDim;
+  const int hg = tid / kHeadDim;
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
+  for (int hh = 0; hh < GPT; ++hh) {
+    const int h = hg * GPT + hh;
+    if (h >= G) break;
     float M = -CUDART_INF_F;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm.wm[w][h]);
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm.wm[w][h]);
     float Lsum = 0.f, O = 0.f;
     if (M != -CUDART_INF_F) {
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
+      for (int w = 0; w < NW; ++w) {
         const float mw = sm.wm[w][h];
         if (mw != -CUDART_INF_F) {
           const float a = exp2f(mw - M);
           Lsum += a * sm.wl[w][h];
-          O += a * sm.k[w][0][h * kHeadDim + d];
+          O += a * (&sm.k[w][0][0])[h * kHeadDim + d];
         }
       }
     }
@@ -437,9 +469,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const DecodeP
   }
 }
 
-// Log-sum-exp merge of n_parts partials per output row (one CTA per row, one
-// thread per head dim).  Parts with l == 0 or m == -inf carry no weight and
-// their o is never read.
+// Log-sum-exp merge of n_parts partials per output row.  One CTA per row and
+// one thread per head dim; the partial vectors are read with kCombineILP
+// independent loads in flight per thread, so a row costs about one L2 round
+// trip per kCombineILP parts.  Parts with l == 0 or m == -inf carry no weight
+// and their o is never read.
+constexpr int kCombineILP = 16;
+
 __global__ void __launch_bounds__(kHeadDim) combine_kernel(const CombineParams c) {
   extern __shared__ float sw[];  // [n_parts] weights, then [n_parts] l
   __shared__ float red[kHeadDim / 32];
@@ -476,28 +512,26 @@ __global__ void __launch_bounds__(kHeadDim) combine_kernel(const CombineParams c
   }
   __syncthreads();
 
-  float L = 0.f, O = 0.f;
   const float* op = c.o + r * c.o_row_stride + d;
-  int i = 0;
-  for (; i + 4 <= c.n_parts; i += 4) {
-    float w[4], ov[4];
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float L = 0.f;
+  for (int i0 = 0; i0 < c.n_parts; i0 += kCombineILP) {
+    float ov[kCombineILP];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) w[u] = sw[i + u];
+    for (int u = 0; u < kCombineILP; ++u) {
+      const int i = i0 + u;
+      ov[u] = (i < c.n_parts && sw[i] != 0.f) ? __ldcg(op + (long long)i * c.o_part_stride) : 0.f;
+    }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) ov[u] = w[u] != 0.f ? op[(long long)(i + u) * c.o_part_stride] : 0.f;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      L += w[u] * sw[c.n_parts + i + u];
-      O += w[u] * ov[u];
+    for (int u = 0; u < kCombineILP; ++u) {
+      const int i = i0 + u;
+      if (i < c.n_parts) {
+        acc[u & 3] += sw[i] * ov[u];
+        L += sw[i] * sw[c.n_parts + i];
+      }
     }
   }
-  for (; i < c.n_parts; ++i) {
-    const float w = sw[i];
-    if (w != 0.f) {
-      L += w * sw[c.n_parts + i];
-      O += w * op[(long long)i * c.o_part_stride];
-    }
-  }
+  const float O = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   float* dst = c.out + (long long)seq * c.out_stride + (long long)h * kHeadDim;
   if (c.out_m) {
     dst[d] = O;
@@ -590,7 +624,41 @@ __global__ void fill_normal_kernel(float* dst, long long n, uint64_t key, long l
 // ---------------------------------------------------------------------------
 // Host-side launchers (C++; the C ABI in gqa_api.cu validates and calls these)
 // ---------------------------------------------------------------------------
-size_t decode_smem_bytes() { return sizeof(DecodeSmem<6>); }
+// Instantiated kernel shapes (warps, rows per stage, stages).  Variant 0 is
+// the default; the others exist for tuning and are selected per context.
+struct Variant {
+  const void* fused;
+  const void* unfused;
+  int threads;
+  int quant;
+  size_t smem;
+};
+
+template <int NW, int ST, int NS>
+static Variant make_variant() {
+  Variant v;
+  v.fused = (const void*)decode_split_kernel<NW, ST, NS, true>;
+  v.unfused = (const void*)decode_split_kernel<NW, ST, NS, false>;
+  v.threads = NW * 32;
+  v.quant = NW * ST > 32 ? NW * ST : 32;
+  v.smem = sizeof(DecodeSmem<NW, ST, NS>);
+  return v;
+}
+
+static const Variant& decode_variant(int i) {
+  static const Variant table[] = {
+      make_variant<8, 4, 3>(),  // 0: 256 threads, 12 KB ring per warp, 2 CTAs/SM
+      make_variant<4, 8, 3>(),  // 1: 128 threads, 24 KB ring per warp, 2 CTAs/SM
+      make_variant<4, 4, 4>(),  // 2: 128 threads, 16 KB ring per warp, 3 CTAs/SM
+      make_variant<8, 8, 2>(),  // 3: 256 threads, 32 KB ring per warp, 1 CTA/SM
+      make_variant<8, 2, 4>(),  // 4: 256 threads,  8 KB ring per warp, 2-3 CTAs/SM
+  };
+  constexpr int n = sizeof(table) / sizeof(table[0]);
+  return table[(i >= 0 && i < n) ? i : 0];
+}
+
+int decode_variant_count() { return 5; }
+int decode_variant_quant(int i) { return decode_variant(i).quant; }
 
 static cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem,
                              cudaStream_t st, bool pdl, void** args) {
@@ -608,22 +676,26 @@ static cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem,
 }
 
 cudaError_t prepare_decode_kernels() {
-  const int smem = (int)decode_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute((const void*)decode_split_kernel<6, true>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute((const void*)decode_split_kernel<6, false>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  for (int i = 0; i < decode_variant_count(); ++i) {
+    const Variant& v = decode_variant(i);
+    cudaError_t e = cudaFuncSetAttribute(v.fused, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)v.smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(v.unfused, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)v.smem);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cudaStream_t st,
-                                bool pdl) {
+                                bool pdl, int variant) {
+  const Variant& v = decode_variant(variant);
   dim3 grid(p.n_splits, p.n_kv, n_seq);
   DecodeParams copy = p;
+  copy.quant = v.quant;
   void* args[] = {&copy};
-  const void* fn = fused ? (const void*)decode_split_kernel<6, true>
-                         : (const void*)decode_split_kernel<6, false>;
-  return launch_ex(fn, grid, dim3(kThreads), decode_smem_bytes(), st, pdl, args);
+  return launch_ex(fused ? v.fused : v.unfused, grid, dim3(v.threads), v.smem, st, pdl, args);
 }
 
 cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl) {

@@ -137,10 +137,12 @@ def test_split_partial_matches_oracle(pkg, orc, cuda, ctx4096, t_begin, t_end):
     if t_end == t_begin:
         assert np.all(np.isneginf(gm)) and np.all(gl == 0) and np.all(go == 0)
         return
-    # partials are defined up to a common factor e^(m_gpu - m_ref): compare normalised
-    assert np.abs(gm - m).max() < 1e-4
-    scale = np.exp(gm - m).astype(np.float64)
-    assert np.abs(gl / scale - l).max() / l.max() < 1e-4
+    # A partial (m, l, o) is defined up to a common factor: (m', l e^(m-m'), o e^(m-m'))
+    # is the same partial.  The kernel's m is a running reference that trails the
+    # true maximum by at most 8 log2 units (its lazy rescale threshold).
+    assert np.all(gm <= m + 1e-5) and np.all(gm >= m - 8 * np.log(2) - 1e-5)
+    scale = np.exp((gm - m).astype(np.float64))
+    assert np.abs(gl * scale - l).max() / l.max() < 1e-4
     assert nerr((go.reshape(12, 128) / (gl[:, None])).reshape(-1),
                 (o.reshape(12, 128) / l[:, None]).reshape(-1)) <= TOL
 
@@ -297,8 +299,6 @@ def test_graph_step_host_buffers(pkg, orc, cuda):
         orc.layer_attention(q, caches[l][1].copy(), caches[l][2].copy(), pos0, pos0 + 1)
         ref.append(q[:1536])
     with pkg.Context(t_max=t_max) as ctx:
-        kvs = [pkg.kv_of(to_dev(torch, c[1]), to_dev(torch, c[2])) for c in caches]
-        keep = [(kv.k_cache, kv.v_cache) for kv in kvs]
         tensors = [(to_dev(torch, c[1]), to_dev(torch, c[2])) for c in caches]
         kvs = [pkg.kv_of(k, v) for k, v in tensors]
         d_qkv = torch.empty((n_layers, 2048), device="cuda")
@@ -311,7 +311,6 @@ def test_graph_step_host_buffers(pkg, orc, cuda):
         torch.cuda.synchronize()
         assert nerr(h_out.numpy().reshape(-1), np.stack(ref).reshape(-1)) <= TOL
         g.destroy()
-        del keep
 
 
 def test_invalid_arguments_raise(pkg, cuda, ctx4096):
@@ -347,3 +346,40 @@ def test_device_side_bad_position_sets_status(pkg, cuda):
         assert st & pkg.gqa.STATUS_BAD_LENGTH
         assert ctx.device_status() == 0
         assert float(k.abs().sum()) == 0.0
+
+
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
+def test_every_kernel_variant_matches_oracle(pkg, orc, cuda, variant):
+    """Each instantiated kernel shape gives the same results (fused single
+    sequence at several lengths, unfused partials, and a ragged batch)."""
+    torch = cuda
+    t_max = 2048
+    with pkg.Context(t_max=t_max) as ctx:
+        ctx.set_option(pkg.gqa.GQA_OPT_KERNEL_VARIANT, variant)
+        for pos, seq_len in [(0, 1), (37, 38), (700, 701), (2047, 2048), (900, 20)]:
+            qkv, kc, vc = pkg.seeded.decode_inputs(3000 + pos + variant, t_max)
+            rq, rk, rv = qkv.copy(), kc.copy(), vc.copy()
+            orc.layer_attention(rq, rk, rv, pos, seq_len)
+            d_qkv, d_k, d_v = to_dev(torch, qkv), to_dev(torch, kc), to_dev(torch, vc)
+            ctx.layer_attention(pkg.kv_of(d_k, d_v), d_qkv, pos, seq_len)
+            torch.cuda.synchronize()
+            assert nerr(d_qkv[:1536].cpu().numpy(), rq[:1536]) <= TOL, (variant, pos, seq_len)
+            assert np.abs(d_k[:, pos].cpu().numpy() - rk[:, pos]).max() <= 1e-5
+        lens = [1, 64, 65, 1999, 300]
+        qkv, kc, vc = _batched_case(pkg, torch, lens, t_max, 900 + variant)
+        ref = orc.decode_batched([qkv[s].copy() for s in range(len(lens))],
+                                 [kc[s].copy() for s in range(len(lens))],
+                                 [vc[s].copy() for s in range(len(lens))], lens)
+        d_qkv, d_k, d_v = to_dev(torch, qkv), to_dev(torch, kc), to_dev(torch, vc)
+        stride = 2 * t_max * 128 * 4
+        kp = torch.tensor([d_k.data_ptr() + s * stride for s in range(len(lens))],
+                          dtype=torch.int64, device="cuda")
+        vp = torch.tensor([d_v.data_ptr() + s * stride for s in range(len(lens))],
+                          dtype=torch.int64, device="cuda")
+        dl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+        out = torch.empty((len(lens), 1536), device="cuda")
+        ctx.decode_batched(len(lens), kp, vp, d_qkv, 2048, dl, max(lens), out, 1536)
+        torch.cuda.synchronize()
+        for s in range(len(lens)):
+            assert nerr(out[s].cpu().numpy(), ref[s]) <= TOL, (variant, s)
+        assert ctx.device_status() == 0
