@@ -48,6 +48,7 @@ struct gqa_ctx {
   int batch_chunk = 0;  // tokens per split in batched decode (0 = automatic)
   int live_graphs = 0;  // graphs hold scratch pointers: no reallocation while > 0
   int variant = 0;      // decode kernel shape (tuning knob)
+  int layers_pdl = 1;   // programmatic dependent launch inside the layer loop
 };
 
 struct gqa_graph {
@@ -206,7 +207,7 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
   if (n_splits > 1) {
     CombineParams cp = combine_from_scratch(c, n_splits);
     cp.out = out;
-    GQA_CUDA(launch_combine(cp, 1, st, true));
+    GQA_CUDA(launch_combine(cp, 1, st, c->layers_pdl != 0));
   }
   return GQA_OK;
 }
@@ -232,7 +233,8 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
     // after its dependency wait.  Later layers follow a combine/split of
     // the previous layer, which never writes pos or this layer's cache.
     int rc = run_single(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max, true,
-                        out + l * out_stride, /*pdl_first=*/true, /*lengths_stable=*/l > 0);
+                        out + l * out_stride, /*pdl_first=*/c->layers_pdl != 0,
+                        /*lengths_stable=*/l > 0);
     if (rc != GQA_OK) return rc;
   }
   if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
@@ -315,6 +317,9 @@ int gqa_set_option(gqa_ctx* c, int option, long long value) {
     case 3: /* GQA_OPT_BATCH_CHUNK (internal tuning knob) */
       if (value < 0 || value > (1 << 20)) return fail(GQA_ERR_INVALID_ARG, "chunk out of range");
       c->batch_chunk = (int)value;
+      return GQA_OK;
+    case 5: /* GQA_OPT_LAYERS_PDL (internal tuning knob) */
+      c->layers_pdl = value ? 1 : 0;
       return GQA_OK;
     case 4: /* GQA_OPT_KERNEL_VARIANT (internal tuning knob) */
       if (value < 0 || value >= decode_variant_count())

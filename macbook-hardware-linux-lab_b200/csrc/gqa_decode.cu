@@ -40,13 +40,13 @@ template <int NW, int ST, int NS>
 struct DecodeSmem {
   float k[NW][NS][ST * kHeadDim];
   float v[NW][NS][ST * kHeadDim];
-  float q[kG][kHeadDim];
-  float newk[kHeadDim];
-  float newv[kHeadDim];
   float cs[kHalf][2];
   float p[NW][ST][8];
   float wm[NW][kG];
   float wl[NW][kG];
+  float wa[NW][kG];  // per-warp merge weights
+  float hm[kG];      // CTA max per head (log2 units)
+  float hl[kG];      // CTA sum per head
   uint64_t full[NW][NS];
   int err;
 };
@@ -226,60 +226,80 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     for (int s = 0; s < NS && s < n_it; ++s) issue(s, s);
   }
 
-  if (early) pdl_wait();
-  pdl_launch_dependents();
-
-  // ---- q (and the new k/v row) into shared memory -------------------------
-  const float* qin = p.qkv + (long long)seq * p.qkv_stride;
-  if (FUSED) {
+  // RoPE angle table (cos, sin per rotation pair).  When pos is known before
+  // the dependency wait, it is built while the previous kernel finishes.
+  auto rope_table = [&]() {
     if (tid < kHalf) {
       float sn, cs;
-      sincosf((float)pos * p.inv_freq[tid], &sn, &cs);
+      sincosf((float)pos * __ldg(p.inv_freq + tid), &sn, &cs);
       sm.cs[tid][0] = cs;
       sm.cs[tid][1] = sn;
     }
-    __syncthreads();
-    for (int idx = tid; idx < G * kHalf; idx += NT) {
-      const int h = idx / kHalf, i = idx % kHalf;
-      const float* qh = qin + (long long)(hkv * G + h) * kHeadDim;
-      const float q0 = qh[i], q1 = qh[i + kHalf];
-      const float c = sm.cs[i][0], s = sm.cs[i][1];
-      sm.q[h][i] = (q0 * c - q1 * s) * p.q_scale;
-      sm.q[h][i + kHalf] = (q0 * s + q1 * c) * p.q_scale;
-    }
-    if (tid < kHalf) {
-      const float* kin = qin + (long long)n_q * kHeadDim + (long long)hkv * kHeadDim;
-      const float* vin = qin + (long long)(n_q + p.n_kv) * kHeadDim + (long long)hkv * kHeadDim;
-      const float c = sm.cs[tid][0], s = sm.cs[tid][1];
-      const float k0 = kin[tid], k1 = kin[tid + kHalf];
-      sm.newk[tid] = k0 * c - k1 * s;
-      sm.newk[tid + kHalf] = k0 * s + k1 * c;
-      sm.newv[tid] = vin[tid];
-      sm.newv[tid + kHalf] = vin[tid + kHalf];
-    }
-  } else {
-    for (int idx = tid; idx < G * kHeadDim; idx += NT) {
-      const int h = idx / kHeadDim, d = idx % kHeadDim;
-      sm.q[h][d] = qin[(long long)(hkv * G + h) * kHeadDim + d] * p.q_scale;
-    }
-  }
-  __syncthreads();
+  };
+  if (FUSED && early) rope_table();
+  if (early) pdl_wait();
+  pdl_launch_dependents();
+  if (FUSED && !early) rope_table();
 
-  // The new row is written by the warp whose range holds pos (after that
-  // stage's copy has landed, so the stale row it replaced was already read),
-  // or by split 0 / warp 0 when pos is outside the attended range.
-  if (FUSED && split == 0 && warp == 0 && !(pos >= p.t_begin && pos < r_end)) {
-    reinterpret_cast<float4*>(kc + (long long)pos * kHeadDim)[lane] =
-        reinterpret_cast<const float4*>(sm.newk)[lane];
-    reinterpret_cast<float4*>(vc + (long long)pos * kHeadDim)[lane] =
-        reinterpret_cast<const float4*>(sm.newv)[lane];
+  // ---- q (and the new k/v row) straight into registers --------------------
+  // Lane l holds dims 4l..4l+3 of every head; the RoPE partner dims (+-64)
+  // live in lane l^16, one shuffle away.
+  const float* qin = p.qkv + (long long)seq * p.qkv_stride;
+  float4 qv[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+    qv[h] = __ldcg(reinterpret_cast<const float4*>(qin + (long long)(hkv * G + h) * kHeadDim) +
+                   lane);
+  const bool pos_attended = pos >= p.t_begin && pos < r_end;
+  const bool row_writer = FUSED && (pos_attended ? (pos >= w0 && pos < w1)
+                                                 : (split == 0 && warp == 0));
+  float4 nk = make_float4(0.f, 0.f, 0.f, 0.f), nv = nk;
+  if (row_writer) {
+    nk = __ldcg(reinterpret_cast<const float4*>(qin + (long long)(n_q + hkv) * kHeadDim) + lane);
+    nv = __ldcg(reinterpret_cast<const float4*>(qin + (long long)(n_q + p.n_kv + hkv) *
+                                                kHeadDim) + lane);
   }
+  if (FUSED) __syncthreads();  // angle table complete
 
   float qr[G][4];
+  if (FUSED) {
+    float c[4], sn[4];
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    const float4 t = reinterpret_cast<const float4*>(sm.q[h])[lane];
-    qr[h][0] = t.x; qr[h][1] = t.y; qr[h][2] = t.z; qr[h][3] = t.w;
+    for (int j = 0; j < 4; ++j) {
+      const float2 t = *reinterpret_cast<const float2*>(sm.cs[4 * (lane & 15) + j]);
+      c[j] = t.x;
+      sn[j] = t.y;
+    }
+    const bool lo = lane < 16;
+    // lo lanes: x' = x c - y s (dims < 64); hi lanes: x' = y s + x c (dims >= 64),
+    // with y the partner value: the reference's half rotation.
+    auto rot = [&](float x, int j) {
+      const float y = __shfl_xor_sync(0xffffffffu, x, 16);
+      return lo ? (x * c[j] - y * sn[j]) : (y * sn[j] + x * c[j]);
+    };
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      qr[h][0] = rot(qv[h].x, 0) * p.q_scale;
+      qr[h][1] = rot(qv[h].y, 1) * p.q_scale;
+      qr[h][2] = rot(qv[h].z, 2) * p.q_scale;
+      qr[h][3] = rot(qv[h].w, 3) * p.q_scale;
+    }
+    if (row_writer) {
+      nk = make_float4(rot(nk.x, 0), rot(nk.y, 1), rot(nk.z, 2), rot(nk.w, 3));
+      if (!pos_attended) {
+        // Not read by this launch: store it right away.
+        reinterpret_cast<float4*>(kc + (long long)pos * kHeadDim)[lane] = nk;
+        reinterpret_cast<float4*>(vc + (long long)pos * kHeadDim)[lane] = nv;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      qr[h][0] = qv[h].x * p.q_scale;
+      qr[h][1] = qv[h].y * p.q_scale;
+      qr[h][2] = qv[h].z * p.q_scale;
+      qr[h][3] = qv[h].w * p.q_scale;
+    }
   }
 
   float o[G][4];
@@ -313,11 +333,12 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     const float* ks = sm.k[warp][s];
     const float* vs = sm.v[warp][s];
 
-    if (FUSED && pos >= t0 && pos < t0 + nt) {
-      reinterpret_cast<float4*>(kc + (long long)pos * kHeadDim)[lane] =
-          reinterpret_cast<const float4*>(sm.newk)[lane];
-      reinterpret_cast<float4*>(vc + (long long)pos * kHeadDim)[lane] =
-          reinterpret_cast<const float4*>(sm.newv)[lane];
+    // The row at pos is replaced by the new token's (registers); its cache
+    // copy is written only after this stage's transfer has landed.
+    const bool pos_here = row_writer && pos >= t0 && pos < t0 + nt;
+    if (pos_here) {
+      reinterpret_cast<float4*>(kc + (long long)pos * kHeadDim)[lane] = nk;
+      reinterpret_cast<float4*>(vc + (long long)pos * kHeadDim)[lane] = nv;
     }
 
     // ---- scores: ST tokens x 6 heads, reduced over the 32 lanes ----
@@ -325,8 +346,8 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
 #pragma unroll
     for (int t = 0; t < ST; ++t) {
       if (t < nt) {
-        const float* kr = (FUSED && t0 + t == pos) ? sm.newk : ks + t * kHeadDim;
-        const float4 kv = reinterpret_cast<const float4*>(kr)[lane];
+        float4 kv = reinterpret_cast<const float4*>(ks + t * kHeadDim)[lane];
+        if (pos_here && t0 + t == pos) kv = nk;
 #pragma unroll
         for (int h = 0; h < G; ++h)
           part[t * G + h] = qr[h][0] * kv.x + qr[h][1] * kv.y + qr[h][2] * kv.z + qr[h][3] * kv.w;
@@ -349,10 +370,17 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     const bool exceed = sc[0] > mo[0] + kRescaleThresh || sc[1] > mo[1] + kRescaleThresh ||
                         sc[2] > mo[2] + kRescaleThresh;
     if (__any_sync(0xffffffffu, exceed)) {
+      float mx[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) mx[h] = ((h / 3) == (hi ? 1 : 0)) ? sc[h % 3] : -CUDART_INF_F;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+        for (int h = 0; h < G; ++h) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
+      }
 #pragma unroll
       for (int h = 0; h < G; ++h) {
-        const float mine = ((h / 3) == (hi ? 1 : 0)) ? sc[h % 3] : -CUDART_INF_F;
-        const float mnew = fmaxf(m[h], warp_max(mine));
+        const float mnew = fmaxf(m[h], mx[h]);
         const float alpha = (mnew == -CUDART_INF_F) ? 1.f : exp2f(m[h] - mnew);
 #pragma unroll
         for (int j = 0; j < 4; ++j) o[h][j] *= alpha;
@@ -380,8 +408,8 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
       if (t < nt) {
         const float4 pa = *reinterpret_cast<const float4*>(&sm.p[warp][t][0]);
         const float2 pb = *reinterpret_cast<const float2*>(&sm.p[warp][t][4]);
-        const float* vr = (FUSED && t0 + t == pos) ? sm.newv : vs + t * kHeadDim;
-        const float4 vv = reinterpret_cast<const float4*>(vr)[lane];
+        float4 vv = reinterpret_cast<const float4*>(vs + t * kHeadDim)[lane];
+        if (pos_here && t0 + t == pos) vv = nv;
         const float pr[6] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y};
 #pragma unroll
         for (int h = 0; h < G; ++h) {
@@ -412,18 +440,24 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   }
 
   // ---- per-warp (m, l, o) -> shared memory ----
+  float lx[G];
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    const float mine = ((h / 3) == (hi ? 1 : 0)) ? lown[h % 3] : 0.f;
-    const float lsum = warp_sum(mine);
-    if (lane == 0) {
-      sm.wl[warp][h] = lsum;
+  for (int h = 0; h < G; ++h) lx[h] = ((h / 3) == (hi ? 1 : 0)) ? lown[h % 3] : 0.f;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) lx[h] += __shfl_xor_sync(0xffffffffu, lx[h], off);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      sm.wl[warp][h] = lx[h];
       sm.wm[warp][h] = m[h];
     }
   }
   // Each warp reuses stage 0 of its own K ring (all its copies have landed).
   static_assert(NS * ST * kHeadDim >= G * kHeadDim, "K ring too small for the epilogue");
-  float* ow = sm.k[warp][0];
+  float* ow = &sm.k[warp][0][0];
 #pragma unroll
   for (int h = 0; h < G; ++h)
     reinterpret_cast<float4*>(ow + h * kHeadDim)[lane] =
@@ -431,7 +465,24 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   __syncthreads();
   if (sm.err) return;
 
-  // ---- merge the warps; thread owns head dim d of heads hg*GPT .. ----
+  // ---- merge the warps: weights once per (warp, head), then one pass ----
+  if (tid < G) {
+    const int h = tid;
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm.wm[w][h]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float mw = sm.wm[w][h];
+      const float a = (mw == -CUDART_INF_F) ? 0.f : exp2f(mw - M);
+      sm.wa[w][h] = a;
+      L += a * sm.wl[w][h];
+    }
+    sm.hm[h] = M;
+    sm.hl[h] = L;
+  }
+  __syncthreads();
   constexpr int NGRP = NT / kHeadDim;             // thread groups
   constexpr int GPT = (G + NGRP - 1) / NGRP;      // heads per group
   const int d = tid % kHeadDim;
@@ -440,21 +491,16 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   for (int hh = 0; hh < GPT; ++hh) {
     const int h = hg * GPT + hh;
     if (h >= G) break;
-    float M = -CUDART_INF_F;
+    float ov[NW];
 #pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm.wm[w][h]);
-    float Lsum = 0.f, O = 0.f;
-    if (M != -CUDART_INF_F) {
+    for (int w = 0; w < NW; ++w) ov[w] = (&sm.k[w][0][0])[h * kHeadDim + d];
+    float O = 0.f;
 #pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float mw = sm.wm[w][h];
-        if (mw != -CUDART_INF_F) {
-          const float a = exp2f(mw - M);
-          Lsum += a * sm.wl[w][h];
-          O += a * (&sm.k[w][0][0])[h * kHeadDim + d];
-        }
-      }
+    for (int w = 0; w < NW; ++w) {
+      const float a = sm.wa[w][h];
+      O += (a != 0.f) ? a * ov[w] : 0.f;
     }
+    const float M = sm.hm[h], Lsum = sm.hl[h];
     if (p.out != nullptr && p.n_splits == 1) {
       p.out[(long long)seq * p.out_stride + (long long)(hkv * G + h) * kHeadDim + d] =
           Lsum > 0.f ? O / Lsum : 0.f;
@@ -469,18 +515,20 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   }
 }
 
-// Log-sum-exp merge of n_parts partials per output row.  One CTA per row and
-// one thread per head dim; the partial vectors are read with kCombineILP
-// independent loads in flight per thread, so a row costs about one L2 round
-// trip per kCombineILP parts.  Parts with l == 0 or m == -inf carry no weight
-// and their o is never read.
-constexpr int kCombineILP = 16;
+// Log-sum-exp merge of n_parts partials per output row.  One CTA per row:
+// kCombGroups groups of 128 threads (one per head dim) take interleaved
+// subsets of the parts, each issuing all of a batch's m, l and o loads before
+// using any of them (one L2 round trip per batch of kCombBatch parts per
+// group), then the groups are merged in shared memory.  Parts with l == 0
+// carry no weight; their o is selected away, never multiplied.
+constexpr int kCombGroups = 4;
+constexpr int kCombBatch = 16;
 
-__global__ void __launch_bounds__(kHeadDim) combine_kernel(const CombineParams c) {
-  extern __shared__ float sw[];  // [n_parts] weights, then [n_parts] l
-  __shared__ float red[kHeadDim / 32];
-  __shared__ float s_M;
-  const int h = blockIdx.x, seq = blockIdx.y, d = threadIdx.x;
+__global__ void __launch_bounds__(kHeadDim * kCombGroups) combine_kernel(const CombineParams c) {
+  __shared__ float s_o[kCombGroups][kHeadDim];
+  __shared__ float s_m[kCombGroups], s_l[kCombGroups];
+  const int h = blockIdx.x, seq = blockIdx.y;
+  const int d = threadIdx.x % kHeadDim, g = threadIdx.x / kHeadDim;
   const long long r = (long long)seq * c.rows_per_seq + h;
   // Let the next kernel (the next layer's split kernel) start streaming its
   // own cache now; it waits for this grid before it reads or writes anything
@@ -488,59 +536,61 @@ __global__ void __launch_bounds__(kHeadDim) combine_kernel(const CombineParams c
   pdl_launch_dependents();
   pdl_wait();
 
-  float mx = -CUDART_INF_F;
-  for (int i = d; i < c.n_parts; i += kHeadDim) {
-    const float mi = c.m[i * c.ml_part_stride + r * c.ml_row_stride];
-    const float li = c.l[i * c.ml_part_stride + r * c.ml_row_stride];
-    sw[i] = mi;
-    sw[c.n_parts + i] = li;
-    if (li > 0.f) mx = fmaxf(mx, mi);
+  float M = -CUDART_INF_F, L = 0.f, O = 0.f;
+  for (int i0 = g; i0 < c.n_parts; i0 += kCombGroups * kCombBatch) {
+    float mv[kCombBatch], lv[kCombBatch], ov[kCombBatch];
+#pragma unroll
+    for (int u = 0; u < kCombBatch; ++u) {
+      const int i = i0 + u * kCombGroups;
+      const bool ok = i < c.n_parts;
+      mv[u] = ok ? __ldcg(c.m + i * c.ml_part_stride + r * c.ml_row_stride) : -CUDART_INF_F;
+      lv[u] = ok ? __ldcg(c.l + i * c.ml_part_stride + r * c.ml_row_stride) : 0.f;
+      ov[u] = ok ? __ldcg(c.o + i * c.o_part_stride + r * c.o_row_stride + d) : 0.f;
+    }
+    float bm = M;
+#pragma unroll
+    for (int u = 0; u < kCombBatch; ++u)
+      if (lv[u] > 0.f) bm = fmaxf(bm, mv[u]);
+    if (bm == -CUDART_INF_F) continue;
+    const float sc = (M == -CUDART_INF_F) ? 0.f : expf(M - bm);
+    L *= sc;
+    O *= sc;
+#pragma unroll
+    for (int u = 0; u < kCombBatch; ++u) {
+      const float w = lv[u] > 0.f ? expf(mv[u] - bm) : 0.f;
+      L += w * lv[u];
+      O += (w != 0.f) ? w * ov[u] : 0.f;
+    }
+    M = bm;
   }
-  mx = warp_max(mx);
-  if ((d & 31) == 0) red[d >> 5] = mx;
-  __syncthreads();
+  s_o[g][d] = O;
   if (d == 0) {
-    float M = red[0];
-    for (int w = 1; w < kHeadDim / 32; ++w) M = fmaxf(M, red[w]);
-    s_M = M;
+    s_m[g] = M;
+    s_l[g] = L;
   }
   __syncthreads();
-  const float M = s_M;
-  for (int i = d; i < c.n_parts; i += kHeadDim) {
-    const float li = sw[c.n_parts + i];
-    sw[i] = (li > 0.f && M != -CUDART_INF_F) ? expf(sw[i] - M) : 0.f;
-  }
-  __syncthreads();
-
-  const float* op = c.o + r * c.o_row_stride + d;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  float L = 0.f;
-  for (int i0 = 0; i0 < c.n_parts; i0 += kCombineILP) {
-    float ov[kCombineILP];
+  if (g != 0) return;
+  float Mt = -CUDART_INF_F;
 #pragma unroll
-    for (int u = 0; u < kCombineILP; ++u) {
-      const int i = i0 + u;
-      ov[u] = (i < c.n_parts && sw[i] != 0.f) ? __ldcg(op + (long long)i * c.o_part_stride) : 0.f;
-    }
+  for (int k = 0; k < kCombGroups; ++k) Mt = fmaxf(Mt, s_m[k]);
+  float Lt = 0.f, Ot = 0.f;
+  if (Mt != -CUDART_INF_F) {
 #pragma unroll
-    for (int u = 0; u < kCombineILP; ++u) {
-      const int i = i0 + u;
-      if (i < c.n_parts) {
-        acc[u & 3] += sw[i] * ov[u];
-        L += sw[i] * sw[c.n_parts + i];
-      }
+    for (int k = 0; k < kCombGroups; ++k) {
+      const float w = (s_m[k] == -CUDART_INF_F) ? 0.f : expf(s_m[k] - Mt);
+      Lt += w * s_l[k];
+      Ot += (w != 0.f) ? w * s_o[k][d] : 0.f;
     }
   }
-  const float O = (acc[0] + acc[1]) + (acc[2] + acc[3]);
   float* dst = c.out + (long long)seq * c.out_stride + (long long)h * kHeadDim;
   if (c.out_m) {
-    dst[d] = O;
+    dst[d] = Ot;
     if (d == 0) {
-      c.out_m[r] = M;
-      c.out_l[r] = L;
+      c.out_m[r] = Mt;
+      c.out_l[r] = Lt;
     }
   } else {
-    dst[d] = L > 0.f ? O / L : 0.f;
+    dst[d] = Lt > 0.f ? Ot / Lt : 0.f;
   }
 }
 
@@ -702,8 +752,8 @@ cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, b
   dim3 grid(c.rows_per_seq, n_seq);
   CombineParams copy = c;
   void* args[] = {&copy};
-  return launch_ex((const void*)combine_kernel, grid, dim3(kHeadDim),
-                   sizeof(float) * 2 * (size_t)c.n_parts, st, pdl, args);
+  return launch_ex((const void*)combine_kernel, grid, dim3(kHeadDim * kCombGroups), 0, st, pdl,
+                   args);
 }
 
 cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k_ptrs,
