@@ -186,6 +186,24 @@ GQA_API int gqa_decode_split_partial(gqa_ctx *ctx, gqa_stream_t stream, const gq
 GQA_API int gqa_lse_combine(gqa_ctx *ctx, gqa_stream_t stream, int n_parts, int n_rows, const float *m,
                     const float *l, const float *o, float *out);
 
+/* ---- layer call without allocation ------------------------------------ */
+
+/* gqa_layer_attention for callers that cannot allocate device memory when
+ * they run (host callbacks, plugins whose framework owns all device memory,
+ * allocation-free capture set-ups).  No counterpart in the reference.  It
+ * needs no context: it runs on the calling thread's current device, and its
+ * split-KV scratch is a static device array inside the library (about
+ * 2.03 MiB per device that loads the library, held until exit, room for 4096
+ * q-head x split partials; a call needing more is rejected with
+ * GQA_ERR_INVALID_ARG).  The first call on a device, and any call with a new
+ * rope_theta, does a one-time set-up that includes a synchronous copy, so make
+ * it before any stream capture.  Calls share the array: calls on one device
+ * that may overlap on the GPU race and must be ordered by the caller.  It
+ * calls no cudaMalloc, cudaFree or allocating library routine. */
+GQA_API int gqa_layer_attention_static(const gqa_config *cfg, gqa_stream_t stream,
+                                       const gqa_layer_kv *kv, float *qkv, int pos,
+                                       int seq_len);
+
 /* ---- utilities -------------------------------------------------------- */
 
 /* Fills dst[0..n) with seeded N(0,1) values (splitmix64 + Box-Muller;

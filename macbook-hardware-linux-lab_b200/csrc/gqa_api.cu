@@ -243,6 +243,17 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
 
 }  // namespace
 
+namespace gqa {
+// Records an error message for gqa_last_error_string() from other units.
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+}  // namespace gqa
+
 extern "C" {
 
 const char* gqa_last_error_string(void) { return g_err; }

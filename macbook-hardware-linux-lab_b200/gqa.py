@@ -94,6 +94,8 @@ _SIGNATURES = {
     "gqa_fill_normal": [_vp, _vp, _vp, _ll, _ull, _ull, _ll],
     "gqa_inv_freq": [_vp, ctypes.POINTER(ctypes.c_float)],
     "gqa_version": [],
+    "gqa_layer_attention_static": [ctypes.POINTER(Config), _vp, ctypes.POINTER(LayerKV), _vp, _i,
+                                   _i],
 }
 _RESTYPES = {"gqa_last_error_string": ctypes.c_char_p, "gqa_version": ctypes.c_char_p}
 
