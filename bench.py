@@ -214,8 +214,9 @@ def cpu_reference_run(steps, warmup, budget_s, pos_lo=3840, layers=28):
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    sample = (f"{done} decode step(s) x {layers} layers at positions {pos_lo}..{pos_lo + done - 1} "
-              f"(L = pos+1), layer calls spread over {cores} threads")
+    sample = (f"{done} decode step(s) x {layers} layers at positions {pos_lo}.."
+              f"{pos_lo + min(done, 256) - 1} (L = pos+1, window of 256 wraps), layer calls "
+              f"spread over {cores} threads")
     return nbytes / dt / 1e9, cores, sample, kind, done / dt
 
 
@@ -332,7 +333,8 @@ def run_resident(args, g, ctx, rank, world, local):
     # mirrors the library's split plan for pos read from the device (planned for t_max)
     n_sm = torch.cuda.get_device_properties(local).multi_processor_count
     target = args.target_ctas or n_sm
-    n_splits = min(-(-target // N_KV), -(-t_max // g.gqa.VARIANT_QUANT[args.variant]))
+    quant = g.gqa.VARIANT_QUANT[3 if args.variant < 0 else args.variant]
+    n_splits = min(-(-target // N_KV), -(-t_max // quant))
     kernels_per_step = L_layers * (2 if n_splits > 1 else 1) + 1
     for gr in graphs + [g_e2e]:
         gr.destroy()
@@ -422,7 +424,7 @@ def run_ours(args):
     wl = WORKLOADS[args.workload]
     t_max = wl.get("t_max") or (wl["len_hi"] + wl["window"])
     ctx = g.Context(t_max=t_max, device=local)
-    if args.variant:
+    if args.variant >= 0:
         ctx.set_option(g.gqa.GQA_OPT_KERNEL_VARIANT, args.variant)
     if args.target_ctas:
         ctx.set_option(g.gqa.GQA_OPT_TARGET_CTAS, args.target_ctas)
@@ -453,7 +455,8 @@ def run_ours(args):
             "ms_per_step": round(t / args.steps * 1e3, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)",
-            "config": dict(workload_config(args.workload), kernel_variant=args.variant,
+            "config": dict(workload_config(args.workload),
+                           kernel_variant="auto" if args.variant < 0 else args.variant,
                            target_ctas=args.target_ctas or None,
                            batch_chunk=args.batch_chunk or None),
             "tok_per_s": round(tokens / t, 1),
@@ -490,7 +493,7 @@ def main():
     ap.add_argument("--workload", choices=list(WORKLOADS), default="resident28")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     # tuning knobs (defaults are the library's own choices)
-    ap.add_argument("--variant", type=int, default=0, help=argparse.SUPPRESS)
+    ap.add_argument("--variant", type=int, default=-1, help=argparse.SUPPRESS)
     ap.add_argument("--target-ctas", type=int, default=0, help=argparse.SUPPRESS)
     ap.add_argument("--batch-chunk", type=int, default=0, help=argparse.SUPPRESS)
     args = ap.parse_args()

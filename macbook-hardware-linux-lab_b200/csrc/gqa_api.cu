@@ -47,8 +47,18 @@ struct gqa_ctx {
   int target_ctas = 0;
   int batch_chunk = 0;  // tokens per split in batched decode (0 = automatic)
   int live_graphs = 0;  // graphs hold scratch pointers: no reallocation while > 0
-  int variant = 0;      // decode kernel shape (tuning knob)
+  // Decode kernel shapes (csrc/gqa_decode.cu variant table).  Measured on
+  // B200: one sequence (few long CTAs, latency-bound) runs best with 8 warps
+  // x 8-row stages (variant 3); batches and long caches (many CTAs,
+  // bandwidth-bound) with 8 warps x 4-row stages (variant 0).
+  int variant = -1;     // -1: per path as above; otherwise forced (tuning knob)
   int layers_pdl = 1;   // programmatic dependent launch inside the layer loop
+  // Cluster reduction for single-sequence launches.  Off by default: on B200
+  // it measured slower than the separate combine kernel (cluster start skew
+  // and ~1 us per dependent global round trip for the arrival counter and
+  // the final merge).
+  int cluster = 0;
+  int* counters = nullptr;  // [kMaxCounters] arrival counters, kept at zero
 };
 
 struct gqa_graph {
@@ -96,6 +106,9 @@ struct DeviceGuard {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+constexpr int kCluster = 8;             // CTAs per cluster in the cluster reduction
+constexpr int kMaxCounters = 1 << 16;   // (sequence, KV head) arrival counters
+
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
 
@@ -135,16 +148,19 @@ int ensure_scratch(gqa_ctx* c, long long slots, cudaStream_t st) {
 // Number of splits for a decode over `len` rows of `rows_kv` (sequence, KV
 // head) pairs: enough CTAs to cover the device once, never a split shorter
 // than 32 rows.
+int single_variant(const gqa_ctx* c) { return c->variant >= 0 ? c->variant : 3; }
+int batch_variant(const gqa_ctx* c) { return c->variant >= 0 ? c->variant : 0; }
+
 int plan_splits_single(const gqa_ctx* c, int rows_kv, int len) {
   const int target = c->target_ctas > 0 ? c->target_ctas : c->n_sm;
   int want = ceil_div(target, rows_kv);
-  const int most = ceil_div(len, decode_variant_quant(c->variant));
+  const int most = ceil_div(len, decode_variant_quant(single_variant(c)));
   if (want > most) want = most;
   return want < 1 ? 1 : want;
 }
 
 int batch_chunk(const gqa_ctx* c, int max_len) {
-  const int q = decode_variant_quant(c->variant);
+  const int q = decode_variant_quant(batch_variant(c));
   const int want = c->batch_chunk > 0 ? c->batch_chunk : (max_len > 8192 ? 1024 : 256);
   return ((want + q - 1) / q) * q;
 }
@@ -158,7 +174,7 @@ DecodeParams base_params(gqa_ctx* c) {
   p.status = c->status;
   p.part_o = c->part_o;
   p.part_ml = c->part_ml;
-  p.min_chunk = decode_variant_quant(c->variant);
+  p.min_chunk = decode_variant_quant(single_variant(c));
   p.lengths_stable = 1;
   return p;
 }
@@ -190,7 +206,10 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
                Lengths len, int plan_len, bool fused, float* out, bool pdl_first,
                bool lengths_stable) {
   const int n_kv = c->cfg.n_heads_kv;
-  const int n_splits = plan_splits_single(c, n_kv, plan_len);
+  int n_splits = plan_splits_single(c, n_kv, plan_len);
+  // Enough splits for whole clusters: reduce in-kernel (no combine launch).
+  const bool use_cluster = fused && c->cluster && n_splits >= kCluster && n_kv <= kMaxCounters;
+  if (use_cluster) n_splits = ((n_splits + kCluster - 1) / kCluster) * kCluster;
   if (n_splits > 1) {
     int rc = ensure_scratch(c, (long long)c->cfg.n_heads_q * n_splits, st);
     if (rc != GQA_OK) return rc;
@@ -203,8 +222,10 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
   p.lengths_stable = lengths_stable ? 1 : 0;
   p.n_splits = n_splits;
   p.out = out;
-  GQA_CUDA(launch_decode_split(p, 1, fused, st, pdl_first, c->variant));
-  if (n_splits > 1) {
+  p.cluster = use_cluster ? kCluster : 0;
+  p.counters = c->counters;
+  GQA_CUDA(launch_decode_split(p, 1, fused, st, pdl_first, single_variant(c)));
+  if (n_splits > 1 && !use_cluster) {
     CombineParams cp = combine_from_scratch(c, n_splits);
     cp.out = out;
     GQA_CUDA(launch_combine(cp, 1, st, c->layers_pdl != 0));
@@ -295,6 +316,8 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   cudaError_t e = prepare_decode_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->inv_freq, sizeof(float) * kHalf);
   if (e == cudaSuccess) e = cudaMalloc(&c->status, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kMaxCounters);
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * kMaxCounters);
   if (e == cudaSuccess)
     e = cudaMemcpy(c->inv_freq, c->h_inv_freq, sizeof(float) * kHalf, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(int));
@@ -311,6 +334,7 @@ int gqa_destroy(gqa_ctx* c) {
   DeviceGuard g(c->device);
   if (c->inv_freq) cudaFree(c->inv_freq);
   if (c->status) cudaFree(c->status);
+  if (c->counters) cudaFree(c->counters);
   if (c->part_o) cudaFree(c->part_o);
   if (c->part_ml) cudaFree(c->part_ml);
   delete c;
@@ -332,9 +356,12 @@ int gqa_set_option(gqa_ctx* c, int option, long long value) {
     case 5: /* GQA_OPT_LAYERS_PDL (internal tuning knob) */
       c->layers_pdl = value ? 1 : 0;
       return GQA_OK;
+    case 6: /* GQA_OPT_CLUSTER (internal tuning knob) */
+      c->cluster = value ? 1 : 0;
+      return GQA_OK;
     case 4: /* GQA_OPT_KERNEL_VARIANT (internal tuning knob) */
-      if (value < 0 || value >= decode_variant_count())
-        return fail(GQA_ERR_INVALID_ARG, "kernel variant out of range");
+      if (value < -1 || value >= decode_variant_count())
+        return fail(GQA_ERR_INVALID_ARG, "kernel variant out of range (-1 = automatic)");
       c->variant = (int)value;
       return GQA_OK;
     default: return fail(GQA_ERR_INVALID_ARG, "unknown option %d", option);
@@ -345,7 +372,8 @@ int gqa_reserve(gqa_ctx* c, int n_seq, int max_len) {
   if (!c || n_seq < 1 || max_len < 1 || max_len > c->cfg.t_max)
     return fail(GQA_ERR_INVALID_ARG, "gqa_reserve: bad arguments");
   DeviceGuard g(c->device);
-  const int single = plan_splits_single(c, c->cfg.n_heads_kv, max_len);
+  const int single = ((plan_splits_single(c, c->cfg.n_heads_kv, max_len) + kCluster - 1) /
+                      kCluster) * kCluster;
   const int batched = ceil_div(max_len, batch_chunk(c, max_len));
   const int splits = single > batched ? single : batched;
   return ensure_scratch(c, (long long)n_seq * c->cfg.n_heads_q * splits, nullptr);
@@ -573,7 +601,7 @@ int gqa_decode_batched(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const*
   p.min_chunk = chunk;
   p.out = out;
   p.out_stride = out_stride;
-  GQA_CUDA(launch_decode_split(p, n_seq, true, st, c->pdl != 0, c->variant));
+  GQA_CUDA(launch_decode_split(p, n_seq, true, st, c->pdl != 0, batch_variant(c)));
   if (n_splits > 1) {
     CombineParams cp = combine_from_scratch(c, n_splits);
     cp.out = out;
@@ -613,7 +641,7 @@ int gqa_decode_split_partial(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv
     p.t_end = t_end;
     p.n_splits = n_splits;
     p.out = nullptr;  // always write partials
-    GQA_CUDA(launch_decode_split(p, 1, false, st, c->pdl != 0, c->variant));
+    GQA_CUDA(launch_decode_split(p, 1, false, st, c->pdl != 0, single_variant(c)));
     cp = combine_from_scratch(c, n_splits);
   } else {
     cp.rows_per_seq = nq;

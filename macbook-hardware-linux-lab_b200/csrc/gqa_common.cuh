@@ -96,6 +96,28 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
 // the stream has completed and its memory is visible; it is a no-op when the
 // kernel was launched without the programmatic-serialization attribute.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Thread-block cluster helpers (distributed shared memory reads only).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+// Address of `p` (this CTA's shared memory) in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_map(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr(p)), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
@@ -157,6 +179,15 @@ struct DecodeParams {
   long long out_stride;
 
   int* status;
+
+  // Cluster reduction (single-sequence launches only).  When cluster > 1 the
+  // grid is launched in clusters of `cluster` CTAs along the split axis; the
+  // clusters reduce through distributed shared memory, write one partial
+  // per cluster to part_o/part_ml, and the last CTA of each (sequence, KV
+  // head) -- found with counters[seq * n_kv + hkv], which must start at zero
+  // and is left at zero -- merges them into `out`.
+  int cluster;
+  int* counters;
 };
 
 struct CombineParams {

@@ -41,12 +41,14 @@ struct DecodeSmem {
   float k[NW][NS][ST * kHeadDim];
   float v[NW][NS][ST * kHeadDim];
   float cs[kHalf][2];
+  float q[kG][kHeadDim];  // raw (pre-RoPE) q of the group, staged once per CTA
   float p[NW][ST][8];
   float wm[NW][kG];
   float wl[NW][kG];
-  float wa[NW][kG];  // per-warp merge weights
-  float hm[kG];      // CTA max per head (log2 units)
-  float hl[kG];      // CTA sum per head
+  float wa[NW][kG];   // per-warp merge weights
+  float wla[NW][kG];  // weight * l per warp
+  float hm[kG];       // CTA max per head (log2 units)
+  float hl[kG];       // CTA sum per head (cluster reduction input)
   uint64_t full[NW][NS];
   int err;
 };
@@ -130,10 +132,118 @@ __device__ __forceinline__ float warp_sum(float x) {
 
 template <int NW>
 struct MinBlocks {
-  static constexpr int value = NW >= 8 ? 2 : 3;
+  static constexpr int value = NW >= 16 ? 1 : NW >= 8 ? 2 : 3;
 };
 
-template <int NW, int ST, int NS, bool FUSED>
+// Cluster reduction of the per-CTA partials of one (sequence, KV head):
+// cluster CTA r merges outputs [r*96, r*96+96) of the 6x128 over the cluster's
+// CTAs through distributed shared memory and writes them as the cluster's
+// partial; the last CTA to finish (arrival counter) merges all clusters'
+// partials into the output and resets the counter.  Every thread of every CTA
+// of the cluster calls this (it holds two cluster barriers).
+template <int NT>
+__device__ __forceinline__ void cluster_epilogue(const DecodeParams& p, float (*co)[kHeadDim],
+                                                 float* cm, float* cl, int seq, int hkv) {
+  constexpr int G = kG;
+  constexpr int kOut = G * kHeadDim;  // 768 outputs per (sequence, KV head)
+  const int tid = threadIdx.x;
+  const int CL = p.cluster;
+  const uint32_t rank = cluster_ctarank();
+  const int n_cl = gridDim.x / CL;
+  const int cl_id = blockIdx.x / CL;
+  const int n_q = p.n_kv * G;
+  __shared__ int s_last;
+  __syncthreads();
+  cluster_sync();  // every CTA's (cm, cl, co) is in place
+  const int per = kOut / CL;
+  for (int t = tid; t < per; t += NT) {
+    const int idx = (int)rank * per + t;
+    const int h = idx / kHeadDim, d = idx % kHeadDim;
+    float mv[8], lv[8], ov[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      if (c < CL) {
+        mv[c] = ld_cluster_f32(cluster_map(&cm[h], c));
+        lv[c] = ld_cluster_f32(cluster_map(&cl[h], c));
+        ov[c] = ld_cluster_f32(cluster_map(&co[h][d], c));
+      } else {
+        mv[c] = -CUDART_INF_F;
+        lv[c] = 0.f;
+        ov[c] = 0.f;
+      }
+    }
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      if (lv[c] > 0.f) M = fmaxf(M, mv[c]);
+    float L = 0.f, O = 0.f;
+    if (M != -CUDART_INF_F) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float w = lv[c] > 0.f ? exp2f(mv[c] - M) : 0.f;
+        L += w * lv[c];
+        O += (w != 0.f) ? w * ov[c] : 0.f;
+      }
+    }
+    const long long r = ((long long)seq * n_q + hkv * G + h) * n_cl + cl_id;
+    p.part_o[r * kHeadDim + d] = O;
+    if (d == 0) {
+      p.part_ml[r * 2 + 0] = M;  // log2 units: consumed only below
+      p.part_ml[r * 2 + 1] = L;
+    }
+  }
+  cluster_sync();  // remote reads done before any CTA of the cluster exits
+
+  // Arrival count over all CTAs of this (sequence, KV head).
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const int old = atomicAdd(&p.counters[seq * p.n_kv + hkv], 1);
+    s_last = (old == (int)gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // All of an output's cluster partials are loaded before any is used (one
+  // L2 round trip per batch of kFinalBatch clusters).
+  constexpr int kFinalBatch = 16;
+  for (int idx = tid; idx < kOut; idx += NT) {
+    const int h = idx / kHeadDim, d = idx % kHeadDim;
+    const long long r0 = ((long long)seq * n_q + hkv * G + h) * n_cl;
+    float M = -CUDART_INF_F, L = 0.f, O = 0.f;
+    for (int c0 = 0; c0 < n_cl; c0 += kFinalBatch) {
+      float mv[kFinalBatch], lv[kFinalBatch], ov[kFinalBatch];
+#pragma unroll
+      for (int u = 0; u < kFinalBatch; ++u) {
+        const bool ok = c0 + u < n_cl;
+        const long long r = r0 + c0 + u;
+        mv[u] = ok ? __ldcg(p.part_ml + r * 2) : -CUDART_INF_F;
+        lv[u] = ok ? __ldcg(p.part_ml + r * 2 + 1) : 0.f;
+        ov[u] = ok ? __ldcg(p.part_o + r * kHeadDim + d) : 0.f;
+      }
+      float bm = M;
+#pragma unroll
+      for (int u = 0; u < kFinalBatch; ++u)
+        if (lv[u] > 0.f) bm = fmaxf(bm, mv[u]);
+      if (bm == -CUDART_INF_F) continue;
+      const float sc = (M == -CUDART_INF_F) ? 0.f : exp2f(M - bm);
+      L *= sc;
+      O *= sc;
+#pragma unroll
+      for (int u = 0; u < kFinalBatch; ++u) {
+        const float w = lv[u] > 0.f ? exp2f(mv[u] - bm) : 0.f;
+        L += w * lv[u];
+        O += (w != 0.f) ? w * ov[u] : 0.f;
+      }
+      M = bm;
+    }
+    p.out[(long long)seq * p.out_stride + (long long)(hkv * G + h) * kHeadDim + d] =
+        L > 0.f ? O / L : 0.f;
+  }
+  if (tid == 0) p.counters[seq * p.n_kv + hkv] = 0;
+}
+
+template <int NW, int ST, int NS, bool FUSED, bool CLUSTER = false>
 __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     decode_split_kernel(const DecodeParams p) {
   constexpr int G = kG;
@@ -171,8 +281,10 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   const int c1 = min(c0 + chunk, r_end);
   const long long prow = ((long long)seq * n_q + hkv * G) * p.n_splits + split;
 
-  if (c0 >= r_end) {
+  if (!CLUSTER && c0 >= r_end) {
     // Empty split (short sequence in a batch planned for the longest one).
+    // (In cluster mode empty CTAs run through with no rows: they must still
+    // take part in the cluster barriers.)
     if (early) pdl_wait();
     pdl_launch_dependents();
     if (tid < G) {
@@ -182,7 +294,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     return;
   }
 
-  const int ctoks = c1 - c0;
+  const int ctoks = max(c1 - c0, 0);
   const int wchunk = round_up_i(ceil_div_i(ctoks, NW), ST);
   const int w0 = c0 + warp * wchunk;
   const int w1 = min(w0 + wchunk, c1);
@@ -245,22 +357,31 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   // Lane l holds dims 4l..4l+3 of every head; the RoPE partner dims (+-64)
   // live in lane l^16, one shuffle away.
   const float* qin = p.qkv + (long long)seq * p.qkv_stride;
-  float4 qv[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-    qv[h] = __ldcg(reinterpret_cast<const float4*>(qin + (long long)(hkv * G + h) * kHeadDim) +
-                   lane);
+  // One cooperative load of the group's q (6 x 128 floats) per CTA.
+  {
+    const float4* qg = reinterpret_cast<const float4*>(qin + (long long)hkv * G * kHeadDim);
+    for (int i = tid; i < G * kHeadDim / 4; i += NT)
+      reinterpret_cast<float4*>(&sm.q[0][0])[i] = __ldcg(qg + i);
+  }
   const bool pos_attended = pos >= p.t_begin && pos < r_end;
   const bool row_writer = FUSED && (pos_attended ? (pos >= w0 && pos < w1)
                                                  : (split == 0 && warp == 0));
-  float4 nk = make_float4(0.f, 0.f, 0.f, 0.f), nv = nk;
+  float4 nk = make_float4(0.f, 0.f, 0.f, 0.f), nv = nk, nkp = nk;
   if (row_writer) {
-    nk = __ldcg(reinterpret_cast<const float4*>(qin + (long long)(n_q + hkv) * kHeadDim) + lane);
+    const float4* kh = reinterpret_cast<const float4*>(qin + (long long)(n_q + hkv) * kHeadDim);
+    nk = __ldcg(kh + lane);
+    nkp = __ldcg(kh + (lane ^ 16));
     nv = __ldcg(reinterpret_cast<const float4*>(qin + (long long)(n_q + p.n_kv + hkv) *
                                                 kHeadDim) + lane);
   }
-  if (FUSED) __syncthreads();  // angle table complete
+  __syncthreads();  // q staged, angle table complete
 
+  float4 qv[G], qp[G];  // own dims and the RoPE partner dims (+-64)
+#pragma unroll
+  for (int h = 0; h < G; ++h) {
+    qv[h] = reinterpret_cast<const float4*>(sm.q[h])[lane];
+    qp[h] = reinterpret_cast<const float4*>(sm.q[h])[lane ^ 16];
+  }
   float qr[G][4];
   if (FUSED) {
     float c[4], sn[4];
@@ -273,19 +394,19 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     const bool lo = lane < 16;
     // lo lanes: x' = x c - y s (dims < 64); hi lanes: x' = y s + x c (dims >= 64),
     // with y the partner value: the reference's half rotation.
-    auto rot = [&](float x, int j) {
-      const float y = __shfl_xor_sync(0xffffffffu, x, 16);
+    auto rot = [&](float x, float y, int j) {
       return lo ? (x * c[j] - y * sn[j]) : (y * sn[j] + x * c[j]);
     };
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      qr[h][0] = rot(qv[h].x, 0) * p.q_scale;
-      qr[h][1] = rot(qv[h].y, 1) * p.q_scale;
-      qr[h][2] = rot(qv[h].z, 2) * p.q_scale;
-      qr[h][3] = rot(qv[h].w, 3) * p.q_scale;
+      qr[h][0] = rot(qv[h].x, qp[h].x, 0) * p.q_scale;
+      qr[h][1] = rot(qv[h].y, qp[h].y, 1) * p.q_scale;
+      qr[h][2] = rot(qv[h].z, qp[h].z, 2) * p.q_scale;
+      qr[h][3] = rot(qv[h].w, qp[h].w, 3) * p.q_scale;
     }
     if (row_writer) {
-      nk = make_float4(rot(nk.x, 0), rot(nk.y, 1), rot(nk.z, 2), rot(nk.w, 3));
+      nk = make_float4(rot(nk.x, nkp.x, 0), rot(nk.y, nkp.y, 1), rot(nk.z, nkp.z, 2),
+                       rot(nk.w, nkp.w, 3));
       if (!pos_attended) {
         // Not read by this launch: store it right away.
         reinterpret_cast<float4*>(kc + (long long)pos * kHeadDim)[lane] = nk;
@@ -310,7 +431,9 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[h][j] = 0.f;
   }
-  float lown[3] = {0.f, 0.f, 0.f};
+  float lsum[G];  // uniform across the warp (accumulated from the broadcast p)
+#pragma unroll
+  for (int h = 0; h < G; ++h) lsum[h] = 0.f;
   const int tt = B::token(lane);
   const int hb = B::head0(lane);
   const bool hi = hb != 0;
@@ -364,6 +487,13 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     for (int i = 0; i < 3; ++i) sc[i] = valid ? part[i] : -CUDART_INF_F;
 
     // ---- online softmax with lazy max update ----
+    if (it == 0) {
+      // Seed the running max with token 0's scores (always a valid token):
+      // six broadcasts instead of a full reduction.
+      const int src_hi = 1 << (5 - B::H);  // first lane holding heads 3..5 of token 0
+#pragma unroll
+      for (int h = 0; h < G; ++h) m[h] = __shfl_sync(0xffffffffu, sc[h % 3], h < 3 ? 0 : src_hi);
+    }
     float mo[3];
 #pragma unroll
     for (int i = 0; i < 3; ++i) mo[i] = hi ? m[3 + i] : m[i];
@@ -384,7 +514,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
         const float alpha = (mnew == -CUDART_INF_F) ? 1.f : exp2f(m[h] - mnew);
 #pragma unroll
         for (int j = 0; j < 4; ++j) o[h][j] *= alpha;
-        if ((h / 3) == (hi ? 1 : 0)) lown[h % 3] *= alpha;
+        lsum[h] *= alpha;
         m[h] = mnew;
       }
 #pragma unroll
@@ -395,10 +525,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     for (int i = 0; i < 3; ++i) pv[i] = exp2f(sc[i] - mo[i]);
     if (own) {
 #pragma unroll
-      for (int i = 0; i < 3; ++i) {
-        lown[i] += pv[i];
-        sm.p[warp][tt][hb + i] = pv[i];
-      }
+      for (int i = 0; i < 3; ++i) sm.p[warp][tt][hb + i] = pv[i];
     }
     __syncwarp();
 
@@ -413,6 +540,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
         const float pr[6] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y};
 #pragma unroll
         for (int h = 0; h < G; ++h) {
+          lsum[h] += pr[h];
           o[h][0] += pr[h] * vv.x;
           o[h][1] += pr[h] * vv.y;
           o[h][2] += pr[h] * vv.z;
@@ -440,18 +568,10 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   }
 
   // ---- per-warp (m, l, o) -> shared memory ----
-  float lx[G];
-#pragma unroll
-  for (int h = 0; h < G; ++h) lx[h] = ((h / 3) == (hi ? 1 : 0)) ? lown[h % 3] : 0.f;
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-#pragma unroll
-    for (int h = 0; h < G; ++h) lx[h] += __shfl_xor_sync(0xffffffffu, lx[h], off);
-  }
   if (lane == 0) {
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      sm.wl[warp][h] = lx[h];
+      sm.wl[warp][h] = lsum[h];
       sm.wm[warp][h] = m[h];
     }
   }
@@ -463,24 +583,19 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     reinterpret_cast<float4*>(ow + h * kHeadDim)[lane] =
         make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
   __syncthreads();
-  if (sm.err) return;
+  if (!CLUSTER && sm.err) return;
 
   // ---- merge the warps: weights once per (warp, head), then one pass ----
-  if (tid < G) {
-    const int h = tid;
+  if (tid < NW * G) {
+    const int h = tid % G, w = tid / G;
     float M = -CUDART_INF_F;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm.wm[w][h]);
-    float L = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) {
-      const float mw = sm.wm[w][h];
-      const float a = (mw == -CUDART_INF_F) ? 0.f : exp2f(mw - M);
-      sm.wa[w][h] = a;
-      L += a * sm.wl[w][h];
-    }
-    sm.hm[h] = M;
-    sm.hl[h] = L;
+    for (int k = 0; k < NW; ++k) M = fmaxf(M, sm.wm[k][h]);
+    const float mw = sm.wm[w][h];
+    const float a = (mw == -CUDART_INF_F) ? 0.f : exp2f(mw - M);
+    sm.wa[w][h] = a;
+    sm.wla[w][h] = a * sm.wl[w][h];
+    if (w == 0) sm.hm[h] = M;
   }
   __syncthreads();
   constexpr int NGRP = NT / kHeadDim;             // thread groups
@@ -500,8 +615,16 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
       const float a = sm.wa[w][h];
       O += (a != 0.f) ? a * ov[w] : 0.f;
     }
-    const float M = sm.hm[h], Lsum = sm.hl[h];
-    if (p.out != nullptr && p.n_splits == 1) {
+    float Lsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) Lsum += sm.wla[w][h];
+    const float M = sm.hm[h];
+    if constexpr (CLUSTER) {
+      // Keep this CTA's partial in its own shared memory (the q staging area
+      // is free by now) for the cluster reduction below.
+      sm.q[h][d] = O;
+      if (d == 0) sm.hl[h] = (sm.err || M == -CUDART_INF_F) ? 0.f : Lsum;
+    } else if (p.out != nullptr && p.n_splits == 1) {
       p.out[(long long)seq * p.out_stride + (long long)(hkv * G + h) * kHeadDim + d] =
           Lsum > 0.f ? O / Lsum : 0.f;
     } else {
@@ -513,6 +636,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
       }
     }
   }
+  if constexpr (CLUSTER) cluster_epilogue<NT>(p, sm.q, sm.hm, sm.hl, seq, hkv);
 }
 
 // Log-sum-exp merge of n_parts partials per output row.  One CTA per row:
@@ -679,6 +803,7 @@ __global__ void fill_normal_kernel(float* dst, long long n, uint64_t key, long l
 struct Variant {
   const void* fused;
   const void* unfused;
+  const void* fused_cluster;
   int threads;
   int quant;
   size_t smem;
@@ -689,6 +814,7 @@ static Variant make_variant() {
   Variant v;
   v.fused = (const void*)decode_split_kernel<NW, ST, NS, true>;
   v.unfused = (const void*)decode_split_kernel<NW, ST, NS, false>;
+  v.fused_cluster = (const void*)decode_split_kernel<NW, ST, NS, true, true>;
   v.threads = NW * 32;
   v.quant = NW * ST > 32 ? NW * ST : 32;
   v.smem = sizeof(DecodeSmem<NW, ST, NS>);
@@ -702,12 +828,14 @@ static const Variant& decode_variant(int i) {
       make_variant<4, 4, 4>(),  // 2: 128 threads, 16 KB ring per warp, 3 CTAs/SM
       make_variant<8, 8, 2>(),  // 3: 256 threads, 32 KB ring per warp, 1 CTA/SM
       make_variant<8, 2, 4>(),  // 4: 256 threads,  8 KB ring per warp, 2-3 CTAs/SM
+      make_variant<16, 4, 2>(), // 5: 512 threads,  8 KB ring per warp, 1 CTA/SM
+      make_variant<16, 2, 3>(), // 6: 512 threads,  6 KB ring per warp, 1 CTA/SM
   };
   constexpr int n = sizeof(table) / sizeof(table[0]);
   return table[(i >= 0 && i < n) ? i : 0];
 }
 
-int decode_variant_count() { return 5; }
+int decode_variant_count() { return 7; }
 int decode_variant_quant(int i) { return decode_variant(i).quant; }
 
 static cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem,
@@ -733,6 +861,9 @@ cudaError_t prepare_decode_kernels() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(v.unfused, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)v.smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(v.fused_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)v.smem);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -745,6 +876,24 @@ cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cu
   DecodeParams copy = p;
   copy.quant = v.quant;
   void* args[] = {&copy};
+  if (p.cluster > 1) {
+    if (!fused || p.n_splits % p.cluster != 0 || p.cluster > 8) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(v.threads);
+    cfg.dynamicSmemBytes = v.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)p.cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelExC(&cfg, v.fused_cluster, args);
+  }
   return launch_ex(fused ? v.fused : v.unfused, grid, dim3(v.threads), v.smem, st, pdl, args);
 }
 

@@ -348,7 +348,7 @@ def test_device_side_bad_position_sets_status(pkg, cuda):
         assert float(k.abs().sum()) == 0.0
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6])
 def test_every_kernel_variant_matches_oracle(pkg, orc, cuda, variant):
     """Each instantiated kernel shape gives the same results (fused single
     sequence at several lengths, unfused partials, and a ragged batch)."""
@@ -382,4 +382,27 @@ def test_every_kernel_variant_matches_oracle(pkg, orc, cuda, variant):
         torch.cuda.synchronize()
         for s in range(len(lens)):
             assert nerr(out[s].cpu().numpy(), ref[s]) <= TOL, (variant, s)
+        assert ctx.device_status() == 0
+
+
+@pytest.mark.parametrize("variant", [0, 3, 5])
+@pytest.mark.parametrize("cluster", [0, 1])
+def test_cluster_reduction_matches_oracle(pkg, orc, cuda, variant, cluster):
+    """Single-sequence decode with and without the in-kernel cluster reduction
+    (several lengths, repeated calls so the arrival counters are reused)."""
+    torch = cuda
+    t_max = 4096
+    with pkg.Context(t_max=t_max) as ctx:
+        ctx.set_option(pkg.gqa.GQA_OPT_KERNEL_VARIANT, variant)
+        ctx.set_option(6, cluster)
+        for pos, seq_len in [(4095, 4096), (3000, 3001), (300, 301), (256, 257), (4000, 2000)]:
+            for rep in range(2):
+                qkv, kc, vc = pkg.seeded.decode_inputs(7000 + pos + rep, t_max)
+                rq, rk, rv = qkv.copy(), kc.copy(), vc.copy()
+                orc.layer_attention(rq, rk, rv, pos, seq_len)
+                d_qkv, d_k, d_v = to_dev(torch, qkv), to_dev(torch, kc), to_dev(torch, vc)
+                ctx.layer_attention(pkg.kv_of(d_k, d_v), d_qkv, pos, seq_len)
+                torch.cuda.synchronize()
+                assert nerr(d_qkv[:1536].cpu().numpy(), rq[:1536]) <= TOL, (pos, seq_len, rep)
+                assert np.abs(d_k[:, pos].cpu().numpy() - rk[:, pos]).max() <= 1e-5
         assert ctx.device_status() == 0
