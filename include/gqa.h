@@ -179,12 +179,33 @@ GQA_API int gqa_decode_split_partial(gqa_ctx *ctx, gqa_stream_t stream, const gq
                              const float *q_rot, int t_begin, int t_end, float *m, float *l,
                              float *o);
 
+/* One KV-range shard of a decode step (a long sequence split over GPUs by
+ * cache rows).  This shard holds global rows [shard_begin, shard_begin +
+ * shard_rows) at local rows [0, shard_rows) of kv.  qkv is the new token's
+ * row (q|k|v before RoPE, the same on every shard) at global position pos.
+ * q is rotated for pos; if pos falls in this shard, its rotated k and raw v
+ * are written at local row pos - shard_begin.  Output: the partial (m, l, o)
+ * of gqa_decode_split_partial over the shard's rows up to pos (m = -inf,
+ * l = 0, o = 0 if none), ready for gqa_lse_combine across shards.  The
+ * reference has no multi-GPU path; this replaces its single-queue split-K
+ * segments (kernel_attention_gqa.cl:340-397) at the scale of several GPUs. */
+GQA_API int gqa_decode_kv_shard(gqa_ctx *ctx, gqa_stream_t stream, const gqa_layer_kv *kv,
+                                const float *qkv, int pos, int shard_begin, int shard_rows,
+                                float *m, float *l, float *o);
+
 /* Log-sum-exp combine of n_parts partials for n_rows rows (q heads):
  * m, l: [n_parts][n_rows]; o: [n_parts][n_rows][128]; out: [n_rows][128] =
  * sum_p e^(m_p - M) o_p / sum_p e^(m_p - M) l_p, M = max_p m_p.  Parts with
  * l = 0 are ignored. */
 GQA_API int gqa_lse_combine(gqa_ctx *ctx, gqa_stream_t stream, int n_parts, int n_rows, const float *m,
                     const float *l, const float *o, float *out);
+
+/* gqa_lse_combine for partials packed one part after another, each part
+ * [m (n_rows) | l (n_rows) | o (n_rows*128)] at part_stride floats from the
+ * previous: the layout of gqa_decode_kv_shard outputs written to
+ * (buf, buf + n_rows, buf + 2*n_rows) and all-gathered across GPUs. */
+GQA_API int gqa_lse_combine_packed(gqa_ctx *ctx, gqa_stream_t stream, int n_parts, int n_rows,
+                                   const float *packed, long long part_stride, float *out);
 
 /* ---- layer call without allocation ------------------------------------ */
 

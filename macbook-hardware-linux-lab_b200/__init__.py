@@ -11,6 +11,6 @@ ctypes binding and the host-side helpers for sharding across GPUs.
 The directory name contains hyphens, so it is loaded by path (see
 ``__graft_entry__.load_package``) under the module name ``gqa_b200``.
 """
-from . import seeded  # noqa: F401
+from . import seeded, shard  # noqa: F401
 from .gqa import (Context, GqaError, Graph, LayerKV, kv_of, lib, last_error,  # noqa: F401
                   header_functions)

@@ -654,6 +654,56 @@ int gqa_decode_split_partial(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv
   return GQA_OK;
 }
 
+int gqa_decode_kv_shard(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
+                        const float* qkv, int pos, int shard_begin, int shard_rows, float* m,
+                        float* l, float* o) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  int rc = check_kv(c, kv);
+  if (rc != GQA_OK) return rc;
+  if (!qkv || !m || !l || !o || !aligned16(qkv))
+    return fail(GQA_ERR_INVALID_ARG, "null argument or unaligned qkv");
+  if (pos < 0 || shard_begin < 0 || shard_rows < 0 || shard_rows > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "pos %d / shard [%d, +%d) invalid (t_max %d)", pos,
+                shard_begin, shard_rows, c->cfg.t_max);
+  DeviceGuard g(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int nq = c->cfg.n_heads_q;
+  // Rows of this shard that the new token attends: global [shard_begin, pos].
+  long long attended = (long long)pos + 1 - shard_begin;
+  if (attended > shard_rows) attended = shard_rows;
+  if (attended < 0) attended = 0;
+  const bool owns = pos >= shard_begin && pos < shard_begin + shard_rows;
+  CombineParams cp{};
+  int n_splits = 0;
+  if (attended > 0) {
+    n_splits = plan_splits_single(c, c->cfg.n_heads_kv, (int)attended);
+    rc = ensure_scratch(c, (long long)nq * n_splits, st);
+    if (rc != GQA_OK) return rc;
+    DecodeParams p = base_params(c);
+    p.k_base = kv->k_cache;
+    p.v_base = kv->v_cache;
+    p.qkv = qkv;
+    p.rope_override = 1;
+    p.rope_pos = pos;
+    p.skip_append = owns ? 0 : 1;
+    p.len.pos_imm = owns ? pos - shard_begin : 0;
+    p.len.seqlen_imm = (int)attended;
+    p.t_end = (int)attended;
+    p.n_splits = n_splits;
+    p.out = nullptr;  // partials only
+    GQA_CUDA(launch_decode_split(p, 1, true, st, c->pdl != 0, single_variant(c)));
+    cp = combine_from_scratch(c, n_splits);
+  } else {
+    cp.rows_per_seq = nq;
+  }
+  cp.n_parts = n_splits;
+  cp.out = o;
+  cp.out_m = m;
+  cp.out_l = l;
+  GQA_CUDA(launch_combine(cp, 1, st, true));
+  return GQA_OK;
+}
+
 int gqa_lse_combine(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows, const float* m,
                     const float* l, const float* o, float* out) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
@@ -667,6 +717,28 @@ int gqa_lse_combine(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows, co
   cp.ml_part_stride = n_rows;
   cp.ml_row_stride = 1;
   cp.o_part_stride = (long long)n_rows * kHeadDim;
+  cp.o_row_stride = kHeadDim;
+  cp.n_parts = n_parts;
+  cp.rows_per_seq = n_rows;
+  cp.out = out;
+  GQA_CUDA(launch_combine(cp, 1, (cudaStream_t)stream, c->pdl != 0));
+  return GQA_OK;
+}
+
+int gqa_lse_combine_packed(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows,
+                           const float* packed, long long part_stride, float* out) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (n_parts < 0 || n_parts > 4096 || n_rows < 1 || n_rows > 65535 || !packed || !out ||
+      part_stride < (long long)n_rows * (2 + kHeadDim))
+    return fail(GQA_ERR_INVALID_ARG, "gqa_lse_combine_packed: bad arguments");
+  DeviceGuard g(c->device);
+  CombineParams cp{};
+  cp.m = packed;
+  cp.l = packed + n_rows;
+  cp.o = packed + 2 * n_rows;
+  cp.ml_part_stride = part_stride;
+  cp.ml_row_stride = 1;
+  cp.o_part_stride = part_stride;
   cp.o_row_stride = kHeadDim;
   cp.n_parts = n_parts;
   cp.rows_per_seq = n_rows;

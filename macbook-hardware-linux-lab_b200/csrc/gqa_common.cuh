@@ -159,6 +159,14 @@ struct DecodeParams {
   // kernel launched immediately before this one, so the fused kernel may read
   // them and start streaming the cache before its dependency wait.
   int lengths_stable;
+  // KV-range shards: with rope_override set, the angle of the new token's
+  // RoPE is taken at rope_pos (its global position) while `pos` is the row
+  // index in this shard's cache; skip_append makes the fused kernel neither
+  // write nor substitute the new row (the shard does not hold it).  All zero
+  // (the default of a zero-initialised block) keeps the plain behaviour.
+  int rope_override;
+  int rope_pos;
+  int skip_append;
   int t_begin;   // first cache row attended (0 except for KV-range shards)
   int t_end;     // if > 0: attend rows [t_begin, t_end) instead of [t_begin, seq_len)
 

@@ -267,7 +267,8 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   int pos, seq_len;
   resolve_lengths(p.len, seq, pos, seq_len);
   const int r_end = p.t_end > 0 ? p.t_end : seq_len;
-  const bool bad = seq_len < 1 || seq_len > p.t_max || pos < 0 || pos >= p.t_max ||
+  const bool has_row = FUSED && p.skip_append == 0;  // this launch holds the new token's row
+  const bool bad = seq_len < 1 || seq_len > p.t_max || (has_row && (pos < 0 || pos >= p.t_max)) ||
                    p.t_begin < 0 || r_end > p.t_max || p.t_begin >= r_end;
   if (bad) {
     if (early) pdl_wait();
@@ -343,7 +344,8 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   auto rope_table = [&]() {
     if (tid < kHalf) {
       float sn, cs;
-      sincosf((float)pos * __ldg(p.inv_freq + tid), &sn, &cs);
+      const int angle_pos = p.rope_override ? p.rope_pos : pos;
+      sincosf((float)angle_pos * __ldg(p.inv_freq + tid), &sn, &cs);
       sm.cs[tid][0] = cs;
       sm.cs[tid][1] = sn;
     }
@@ -364,8 +366,8 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
       reinterpret_cast<float4*>(&sm.q[0][0])[i] = __ldcg(qg + i);
   }
   const bool pos_attended = pos >= p.t_begin && pos < r_end;
-  const bool row_writer = FUSED && (pos_attended ? (pos >= w0 && pos < w1)
-                                                 : (split == 0 && warp == 0));
+  const bool row_writer = has_row && (pos_attended ? (pos >= w0 && pos < w1)
+                                                   : (split == 0 && warp == 0));
   float4 nk = make_float4(0.f, 0.f, 0.f, 0.f), nv = nk, nkp = nk;
   if (row_writer) {
     const float4* kh = reinterpret_cast<const float4*>(qin + (long long)(n_q + hkv) * kHeadDim);

@@ -91,6 +91,8 @@ _SIGNATURES = {
     "gqa_decode_batched": [_vp, _vp, _i, _vp, _vp, _vp, _ll, _vp, _i, _vp, _ll],
     "gqa_decode_split_partial": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _vp, _vp, _vp],
     "gqa_lse_combine": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
+    "gqa_decode_kv_shard": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _i, _vp, _vp, _vp],
+    "gqa_lse_combine_packed": [_vp, _vp, _i, _i, _vp, _ll, _vp],
     "gqa_fill_normal": [_vp, _vp, _vp, _ll, _ull, _ull, _ll],
     "gqa_inv_freq": [_vp, ctypes.POINTER(ctypes.c_float)],
     "gqa_version": [],
@@ -299,9 +301,19 @@ class Context:
                                               _ptr(q_rot), t_begin, t_end, _ptr(m), _ptr(l),
                                               _ptr(o)))
 
+    def decode_kv_shard(self, kv: LayerKV, qkv, pos: int, shard_begin: int, shard_rows: int,
+                        m, l, o, stream=None) -> None:
+        _check(lib().gqa_decode_kv_shard(self._h, _stream(stream), ctypes.byref(kv), _ptr(qkv),
+                                         pos, shard_begin, shard_rows, _ptr(m), _ptr(l), _ptr(o)))
+
     def lse_combine(self, n_parts: int, n_rows: int, m, l, o, out, stream=None) -> None:
         _check(lib().gqa_lse_combine(self._h, _stream(stream), n_parts, n_rows, _ptr(m), _ptr(l),
                                      _ptr(o), _ptr(out)))
+
+    def lse_combine_packed(self, n_parts: int, n_rows: int, packed, part_stride: int, out,
+                           stream=None) -> None:
+        _check(lib().gqa_lse_combine_packed(self._h, _stream(stream), n_parts, n_rows,
+                                            _ptr(packed), part_stride, _ptr(out)))
 
     def fill_normal(self, dst, n: int, seed: int, stream_id: int, offset: int = 0,
                     stream=None) -> None:
