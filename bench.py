@@ -48,6 +48,7 @@ WORKLOADS = {
     "batched": dict(layers=1, seqs=64, len_lo=256, len_hi=8192, window=256),
     "long": dict(layers=1, seqs=256, t_max=32768, window=64),
     "single": dict(layers=1, t_max=512, pos_lo=511, pos_hi=512, seqs=1),
+    "long1": dict(layers=1, seqs=1, t_max=32768, window=64),
 }
 
 
@@ -258,6 +259,11 @@ def workload_config(name):
         return {"workload": "long: 256 sequences x 32768 fp32 KV rows (17.2 GB per layer)",
                 "seqs": 256, "t_max": 32768, "l2": "KV > L2; no flush",
                 "parallelism": "sequence-sharded"}
+    if name == "long1":
+        return {"workload": "long1: one sequence, 32768 fp32 KV rows (67 MB per layer) split by "
+                            "KV range across the GPUs, partials all-gathered (NCCL) and "
+                            "LSE-combined every step", "seqs": 1, "t_max": 32768,
+                "l2": "KV > L2 at 1-2 GPUs; no flush", "parallelism": "kv-range split"}
     return {"workload": "single: one step, 12/2 heads, d=128, pos 511, seq_len 512",
             "l2": "1 MB KV fits in L2 (latency-bound)"}
 
@@ -349,13 +355,17 @@ def run_batched(args, g, ctx, rank, world, local):
     wl = WORKLOADS[args.workload]
     seed = 777 + 1000 * rank
     if args.workload == "batched":
-        n, window = wl["seqs"], wl["window"]
-        lens0 = [int(x) for x in g.seeded.uniform_int(seed, g.seeded.LENGTHS, n, wl["len_lo"],
-                                                      wl["len_hi"])]
+        n_all, window = wl["seqs"], wl["window"]
+        lens_all = [int(x) for x in g.seeded.uniform_int(777, g.seeded.LENGTHS, n_all,
+                                                         wl["len_lo"], wl["len_hi"])]
         t_max = wl["len_hi"] + window
     else:
-        n, window, t_max = wl["seqs"], wl["window"], wl["t_max"]
-        lens0 = [t_max - window] * n
+        n_all, window, t_max = wl["seqs"], wl["window"], wl["t_max"]
+        lens_all = [t_max - window] * n_all
+    # Sequences are dealt to ranks (longest first to the least-loaded rank).
+    mine = g.shard.plan_sequence_shards(lens_all, world)[rank]
+    lens0 = [lens_all[i] for i in mine]
+    n = len(lens0)
     k = torch.empty((n, 2, t_max, D), device="cuda")
     v = torch.empty((n, 2, t_max, D), device="cuda")
     ctx.fill_normal(k, k.numel(), seed, g.seeded.K_CACHE)
@@ -416,6 +426,61 @@ def run_batched(args, g, ctx, rank, world, local):
                 dominant_launches=args.steps)
 
 
+def run_long1(args, g, ctx, rank, world, local):
+    import torch
+    wl = WORKLOADS["long1"]
+    T, window = wl["t_max"], wl["window"]
+    b, n = g.shard.plan_kv_ranges(T, world)[rank]
+    seed = 5151
+    k = torch.empty((N_KV, max(n, 1), D), device="cuda")
+    v = torch.empty((N_KV, max(n, 1), D), device="cuda")
+    for h in range(N_KV):  # this rank's rows of the one seeded global cache
+        ctx.fill_normal(k[h], n * D, seed, g.seeded.K_CACHE, offset=(h * T + b) * D)
+        ctx.fill_normal(v[h], n * D, seed, g.seeded.V_CACHE, offset=(h * T + b) * D)
+    qkv = torch.empty(QKV_W, device="cuda")
+    ctx.fill_normal(qkv, QKV_W, seed, g.seeded.QKV)
+    out = torch.empty(OUT_W, device="cuda")
+    dec = g.shard.KvShardDecoder(ctx, k, v, b, n)
+    pos0 = T - window
+    stream = torch.cuda.current_stream()
+
+    def my_bytes(i):
+        pos = pos0 + i % window
+        return ROW_BYTES * max(0, min(n, pos + 1 - b))
+
+    for i in range(args.warmup):
+        dec.step(qkv, pos0 + i % window, out)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            dec.step(qkv, pos0 + i % window, out)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    h_qkv = qkv.cpu().pin_memory()
+    h_out = torch.empty(OUT_W).pin_memory()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        qkv.copy_(h_qkv, non_blocking=True)
+        dec.step(qkv, pos0 + i % window, out)
+        h_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status set")
+    return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3,
+                bytes=sum(my_bytes(i) for i in range(args.steps)), clocks=clk.summary(),
+                launches=2 * args.steps, launches_per_step=2, h2d=QKV_W * 4, d2h=OUT_W * 4,
+                tokens=args.steps / world, dominant_launches=args.steps)
+
+
 def run_ours(args):
     import torch
     rank, world, local = dist_setup(args.gpus)
@@ -423,6 +488,8 @@ def run_ours(args):
     g = __graft_entry__.load_package()
     wl = WORKLOADS[args.workload]
     t_max = wl.get("t_max") or (wl["len_hi"] + wl["window"])
+    if args.workload == "long1":
+        t_max = max(n for _, n in g.shard.plan_kv_ranges(t_max, world))
     ctx = g.Context(t_max=t_max, device=local)
     if args.variant >= 0:
         ctx.set_option(g.gqa.GQA_OPT_KERNEL_VARIANT, args.variant)
@@ -432,6 +499,8 @@ def run_ours(args):
         ctx.set_option(g.gqa.GQA_OPT_BATCH_CHUNK, args.batch_chunk)
     if args.workload in ("resident28", "single"):
         r = run_resident(args, g, ctx, rank, world, local)
+    elif args.workload == "long1":
+        r = run_long1(args, g, ctx, rank, world, local)
     else:
         r = run_batched(args, g, ctx, rank, world, local)
     t = max_over_ranks(r["t"], world)
@@ -453,7 +522,8 @@ def run_ours(args):
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t / args.steps * 1e3, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "weak" if args.workload in ("resident28", "single") else "strong",
+            "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)",
             "config": dict(workload_config(args.workload),
                            kernel_variant="auto" if args.variant < 0 else args.variant,

@@ -65,6 +65,8 @@ def all_gather_partials(packed, group=None):
     into a [world, width] tensor in rank order."""
     import torch
     import torch.distributed as dist
+    if not dist.is_available() or not dist.is_initialized():
+        return packed.view(1, -1)  # a single process: nothing to exchange
     world = dist.get_world_size(group)
     flat = torch.empty(world * packed.numel(), dtype=packed.dtype, device=packed.device)
     dist.all_gather_into_tensor(flat, packed.contiguous().view(-1), group=group)
