@@ -26,6 +26,8 @@
 
 #include <math_constants.h>
 
+#include <type_traits>
+
 namespace gqa {
 
 constexpr float kRescaleThresh = 8.0f;           // log2 units
@@ -44,7 +46,7 @@ struct DecodeSmem {
   float q[kG][kHeadDim];  // raw (pre-RoPE) q of the group, staged once per CTA
   float p[NW][ST][8];
   float wm[NW][kG];
-  float wl[NW][kG];
+  float lp[NW][ST][8];  // per-warp l partials, one row per owner token
   float wa[NW][kG];   // per-warp merge weights
   float wla[NW][kG];  // weight * l per warp
   float hm[kG];       // CTA max per head (log2 units)
@@ -111,6 +113,25 @@ struct Bfly {
       for (int i = 0; i < 3; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], off);
     }
   }
+  // Select-free form: each exchange keeps positions [0, N/2) and sends
+  // [N/2, N); correct when partials are stored in the lane-permuted order
+  // described at the call site.
+  template <int N, int OFF>
+  __device__ __forceinline__ static void halve_permuted(float* v) {
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i + N / 2], OFF);
+  }
+  __device__ __forceinline__ static void run_permuted(float* v) {
+    halve_permuted<ST * 6, 16>(v);
+    if constexpr (H >= 2) halve_permuted<ST * 3, 8>(v);
+    if constexpr (H >= 3) halve_permuted<ST * 3 / 2, 4>(v);
+    if constexpr (H >= 4) halve_permuted<ST * 3 / 4, 2>(v);
+#pragma unroll
+    for (int off = 1 << (kLowBits - 1); off > 0; off >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 3; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], off);
+    }
+  }
   __device__ __forceinline__ static int token(int lane) { return lane >> (6 - H); }
   __device__ __forceinline__ static int head0(int lane) { return 3 * ((lane >> (5 - H)) & 1); }
   __device__ __forceinline__ static bool owner(int lane) {
@@ -130,9 +151,17 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
-template <int NW>
+// CTAs per SM the register budget is sized for: as many as the shared memory
+// footprint (two K/V rings of NW x NS x ST rows) lets reside, but never so
+// many that a thread gets fewer than 128 registers (the loop holds 24 q, 24 o
+// and up to 48 partial-sum registers) and at most 3.
+template <int NW, int ST, int NS>
 struct MinBlocks {
-  static constexpr int value = NW >= 16 ? 1 : NW >= 8 ? 2 : 3;
+  static constexpr int kRingBytes = 2 * NW * NS * ST * kRowBytes;
+  static constexpr int kBySmem = (227 * 1024) / (kRingBytes + 8 * 1024);
+  static constexpr int kByRegs = 16 / NW;  // 65536 / (NW * 32 * 128)
+  static constexpr int kMin = kBySmem < kByRegs ? kBySmem : kByRegs;
+  static constexpr int value = kMin < 1 ? 1 : (kMin > 3 ? 3 : kMin);
 };
 
 // Cluster reduction of the per-CTA partials of one (sequence, KV head):
@@ -244,7 +273,7 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeParams& p, float (*
 }
 
 template <int NW, int ST, int NS, bool FUSED, bool CLUSTER = false>
-__global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
+__global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     decode_split_kernel(const DecodeParams p) {
   constexpr int G = kG;
   constexpr int NT = NW * 32;
@@ -433,13 +462,20 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[h][j] = 0.f;
   }
-  float lsum[G];  // uniform across the warp (accumulated from the broadcast p)
-#pragma unroll
-  for (int h = 0; h < G; ++h) lsum[h] = 0.f;
-  const int tt = B::token(lane);
-  const int hb = B::head0(lane);
+  const int tt = B::token(lane);     // token this lane's scores belong to
+  const int hb = B::head0(lane);     // first of this lane's three heads
   const bool hi = hb != 0;
-  const bool own = B::owner(lane);
+  const bool own = B::owner(lane);   // one lane per (token, head triple) writes p
+  // Partials are stored in a lane-dependent order -- position (tp, hp) holds
+  // token tp ^ tt and head hp with its triple swapped when `hi` -- so that
+  // every butterfly exchange keeps the lower half and sends the upper half
+  // with no select (Bfly::run_permuted).  The q registers are swapped once.
+  float qs[G][4];
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) qs[h][j] = hi ? qr[(h + 3) % G][j] : qr[h][j];
+  float lown[3] = {0.f, 0.f, 0.f};  // this owner lane's share of l for its heads
   int consumed = 0;
   bool failed = false;
 
@@ -455,33 +491,39 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     consumed = it + 1;
     const int t0 = w0 + it * ST;
     const int nt = min(ST, w1 - t0);
-    const float* ks = sm.k[warp][s];
-    const float* vs = sm.v[warp][s];
+    float* ks = sm.k[warp][s];
+    float* vs = sm.v[warp][s];
 
-    // The row at pos is replaced by the new token's (registers); its cache
-    // copy is written only after this stage's transfer has landed.
-    const bool pos_here = row_writer && pos >= t0 && pos < t0 + nt;
-    if (pos_here) {
+    // The row at pos is the new token's: put it into the landed stage (the
+    // stale copy the transfer brought in is overwritten) and into the cache.
+    if (row_writer && pos >= t0 && pos < t0 + nt) {
+      reinterpret_cast<float4*>(ks + (pos - t0) * kHeadDim)[lane] = nk;
+      reinterpret_cast<float4*>(vs + (pos - t0) * kHeadDim)[lane] = nv;
       reinterpret_cast<float4*>(kc + (long long)pos * kHeadDim)[lane] = nk;
       reinterpret_cast<float4*>(vc + (long long)pos * kHeadDim)[lane] = nv;
+      __syncwarp();
     }
 
     // ---- scores: ST tokens x 6 heads, reduced over the 32 lanes ----
     float part[ST * G];
+    auto scores = [&](auto full) {
 #pragma unroll
-    for (int t = 0; t < ST; ++t) {
-      if (t < nt) {
-        float4 kv = reinterpret_cast<const float4*>(ks + t * kHeadDim)[lane];
-        if (pos_here && t0 + t == pos) kv = nk;
+      for (int tp = 0; tp < ST; ++tp) {
+        const int t = tp ^ tt;
+        if (decltype(full)::value || t < nt) {
+          const float4 kv = reinterpret_cast<const float4*>(ks + t * kHeadDim)[lane];
 #pragma unroll
-        for (int h = 0; h < G; ++h)
-          part[t * G + h] = qr[h][0] * kv.x + qr[h][1] * kv.y + qr[h][2] * kv.z + qr[h][3] * kv.w;
-      } else {
+          for (int h = 0; h < G; ++h)
+            part[tp * G + h] =
+                qs[h][0] * kv.x + qs[h][1] * kv.y + qs[h][2] * kv.z + qs[h][3] * kv.w;
+        } else {
 #pragma unroll
-        for (int h = 0; h < G; ++h) part[t * G + h] = 0.f;
+          for (int h = 0; h < G; ++h) part[tp * G + h] = 0.f;
+        }
       }
-    }
-    B::run(part, lane);
+    };
+    if (nt == ST) scores(std::true_type{}); else scores(std::false_type{});
+    B::run_permuted(part);
 
     float sc[3];
     const bool valid = tt < nt;
@@ -516,7 +558,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
         const float alpha = (mnew == -CUDART_INF_F) ? 1.f : exp2f(m[h] - mnew);
 #pragma unroll
         for (int j = 0; j < 4; ++j) o[h][j] *= alpha;
-        lsum[h] *= alpha;
+        if ((h / 3) == (hi ? 1 : 0)) lown[h % 3] *= alpha;
         m[h] = mnew;
       }
 #pragma unroll
@@ -527,29 +569,33 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     for (int i = 0; i < 3; ++i) pv[i] = exp2f(sc[i] - mo[i]);
     if (own) {
 #pragma unroll
-      for (int i = 0; i < 3; ++i) sm.p[warp][tt][hb + i] = pv[i];
+      for (int i = 0; i < 3; ++i) {
+        lown[i] += pv[i];
+        sm.p[warp][tt][hb + i] = pv[i];
+      }
     }
     __syncwarp();
 
     // ---- o += p . V ----
+    auto pv_acc = [&](auto full) {
 #pragma unroll
-    for (int t = 0; t < ST; ++t) {
-      if (t < nt) {
-        const float4 pa = *reinterpret_cast<const float4*>(&sm.p[warp][t][0]);
-        const float2 pb = *reinterpret_cast<const float2*>(&sm.p[warp][t][4]);
-        float4 vv = reinterpret_cast<const float4*>(vs + t * kHeadDim)[lane];
-        if (pos_here && t0 + t == pos) vv = nv;
-        const float pr[6] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y};
+      for (int t = 0; t < ST; ++t) {
+        if (decltype(full)::value || t < nt) {
+          const float4 pa = *reinterpret_cast<const float4*>(&sm.p[warp][t][0]);
+          const float2 pb = *reinterpret_cast<const float2*>(&sm.p[warp][t][4]);
+          const float4 vv = reinterpret_cast<const float4*>(vs + t * kHeadDim)[lane];
+          const float pr[6] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y};
 #pragma unroll
-        for (int h = 0; h < G; ++h) {
-          lsum[h] += pr[h];
-          o[h][0] += pr[h] * vv.x;
-          o[h][1] += pr[h] * vv.y;
-          o[h][2] += pr[h] * vv.z;
-          o[h][3] += pr[h] * vv.w;
+          for (int h = 0; h < G; ++h) {
+            o[h][0] += pr[h] * vv.x;
+            o[h][1] += pr[h] * vv.y;
+            o[h][2] += pr[h] * vv.z;
+            o[h][3] += pr[h] * vv.w;
+          }
         }
       }
-    }
+    };
+    if (nt == ST) pv_acc(std::true_type{}); else pv_acc(std::false_type{});
     __syncwarp();
     if (it + NS < n_it && lane == 0) {
       fence_proxy_async_smem();
@@ -570,12 +616,13 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
   }
 
   // ---- per-warp (m, l, o) -> shared memory ----
+  if (own) {
+#pragma unroll
+    for (int i = 0; i < 3; ++i) sm.lp[warp][tt][hb + i] = lown[i];
+  }
   if (lane == 0) {
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      sm.wl[warp][h] = lsum[h];
-      sm.wm[warp][h] = m[h];
-    }
+    for (int h = 0; h < G; ++h) sm.wm[warp][h] = m[h];
   }
   // Each warp reuses stage 0 of its own K ring (all its copies have landed).
   static_assert(NS * ST * kHeadDim >= G * kHeadDim, "K ring too small for the epilogue");
@@ -595,8 +642,11 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW>::value)
     for (int k = 0; k < NW; ++k) M = fmaxf(M, sm.wm[k][h]);
     const float mw = sm.wm[w][h];
     const float a = (mw == -CUDART_INF_F) ? 0.f : exp2f(mw - M);
+    float lw = 0.f;  // warp w's l for head h: the sum over its owner lanes, in token order
+#pragma unroll
+    for (int t = 0; t < ST; ++t) lw += sm.lp[w][t][h];
     sm.wa[w][h] = a;
-    sm.wla[w][h] = a * sm.wl[w][h];
+    sm.wla[w][h] = a == 0.f ? 0.f : a * lw;
     if (w == 0) sm.hm[h] = M;
   }
   __syncthreads();
