@@ -207,6 +207,21 @@ GQA_API int gqa_lse_combine(gqa_ctx *ctx, gqa_stream_t stream, int n_parts, int 
 GQA_API int gqa_lse_combine_packed(gqa_ctx *ctx, gqa_stream_t stream, int n_parts, int n_rows,
                                    const float *packed, long long part_stride, float *out);
 
+/* ---- prefill ---------------------------------------------------------- */
+
+/* Causal attention over whole prompts on the tensor cores (bf16 operands,
+ * fp32 accumulation).  The reference has no prefill: it runs the prompt
+ * through the decode layer call one token at a time (qwen_server.c:957-964);
+ * this computes the same rows at once.  qkv: [n_seq][seq_len][q|k|v] fp32
+ * before RoPE, token s at position s; out: [n_seq][seq_len][n_heads_q*128]
+ * fp32.  When k_caches / v_caches (DEVICE arrays of n_seq cache pointers) are
+ * given, rows [0, seq_len) of each cache receive the rotated K and raw V in
+ * fp32, as the token-by-token path would leave them.  seq_len must be a
+ * multiple of 128.  Accuracy: bf16 operands, about 1e-2 of the output RMS. */
+GQA_API int gqa_prefill_bf16(gqa_ctx *ctx, gqa_stream_t stream, int n_seq, int seq_len,
+                             const float *qkv, float *out, float *const *k_caches,
+                             float *const *v_caches);
+
 /* ---- layer call without allocation ------------------------------------ */
 
 /* gqa_layer_attention for callers that cannot allocate device memory when

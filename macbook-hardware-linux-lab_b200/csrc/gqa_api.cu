@@ -10,6 +10,8 @@
 #include <cstring>
 #include <vector>
 
+#include <cuda_bf16.h>
+
 #include "gqa.h"
 #include "gqa_common.cuh"
 
@@ -29,6 +31,12 @@ cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k
 cudaError_t launch_advance_pos(int* pos, int wrap_lo, int wrap_hi, cudaStream_t st, bool pdl);
 cudaError_t launch_fill_normal(float* dst, long long n, uint64_t key, long long offset,
                                int n_sm, cudaStream_t st);
+cudaError_t prepare_prefill_kernels();
+cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, int S, int n_q,
+                           int n_kv, const float* inv_freq, __nv_bfloat16* qimg,
+                           __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
+                           float* const* v_caches, int t_max, float* out, int* status,
+                           cudaStream_t st);
 }  // namespace gqa
 
 using namespace gqa;
@@ -59,6 +67,8 @@ struct gqa_ctx {
   // the final merge).
   int cluster = 0;
   int* counters = nullptr;  // [kMaxCounters] arrival counters, kept at zero
+  __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
+  size_t prefill_cap = 0;                // elements
 };
 
 struct gqa_graph {
@@ -314,6 +324,7 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   for (int i = 0; i < kHalf; ++i)
     c->h_inv_freq[i] = powf(cfg->rope_theta, -2.0f * (float)i / (float)kHeadDim);
   cudaError_t e = prepare_decode_kernels();
+  if (e == cudaSuccess) e = prepare_prefill_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->inv_freq, sizeof(float) * kHalf);
   if (e == cudaSuccess) e = cudaMalloc(&c->status, sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kMaxCounters);
@@ -335,6 +346,7 @@ int gqa_destroy(gqa_ctx* c) {
   if (c->inv_freq) cudaFree(c->inv_freq);
   if (c->status) cudaFree(c->status);
   if (c->counters) cudaFree(c->counters);
+  if (c->prefill_img) cudaFree(c->prefill_img);
   if (c->part_o) cudaFree(c->part_o);
   if (c->part_ml) cudaFree(c->part_ml);
   delete c;
@@ -744,6 +756,48 @@ int gqa_lse_combine_packed(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_r
   cp.rows_per_seq = n_rows;
   cp.out = out;
   GQA_CUDA(launch_combine(cp, 1, (cudaStream_t)stream, c->pdl != 0));
+  return GQA_OK;
+}
+
+int gqa_prefill_bf16(gqa_ctx* c, gqa_stream_t stream, int n_seq, int seq_len, const float* qkv,
+                     float* out, float* const* k_caches, float* const* v_caches) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (n_seq < 1 || n_seq > 65535 || !qkv || !out)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_prefill_bf16: null argument or n_seq out of range");
+  if (seq_len < 128 || seq_len % 128 != 0 || seq_len > 65535 * 128)
+    return fail(GQA_ERR_UNSUPPORTED, "gqa_prefill_bf16: seq_len %d must be a positive multiple of 128",
+                seq_len);
+  if ((k_caches == nullptr) != (v_caches == nullptr))
+    return fail(GQA_ERR_INVALID_ARG, "give both cache arrays or neither");
+  if (k_caches && seq_len > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "seq_len %d exceeds the cache capacity t_max %d", seq_len,
+                c->cfg.t_max);
+  if (!aligned16(qkv) || !aligned16(out))
+    return fail(GQA_ERR_INVALID_ARG, "qkv/out must be 16-byte aligned");
+  DeviceGuard g(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
+  const size_t per = (size_t)n_seq * seq_len * kHeadDim;
+  const size_t need = per * (size_t)(nq + 2 * nkv);
+  if (need > c->prefill_cap) {
+    if (is_capturing(st) || c->live_graphs > 0)
+      return fail(GQA_ERR_NO_MEMORY, "prefill scratch must grow outside capture / live graphs");
+    if (c->prefill_img) cudaFree(c->prefill_img);
+    c->prefill_img = nullptr;
+    c->prefill_cap = 0;
+    if (cudaMalloc(&c->prefill_img, need * sizeof(__nv_bfloat16)) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(GQA_ERR_NO_MEMORY, "cudaMalloc of %zu bytes of prefill scratch failed",
+                  need * sizeof(__nv_bfloat16));
+    }
+    c->prefill_cap = need;
+  }
+  __nv_bfloat16* qimg = c->prefill_img;
+  __nv_bfloat16* kimg = qimg + per * nq;
+  __nv_bfloat16* vimg = kimg + per * nkv;
+  GQA_CUDA(launch_prefill(qkv, (long long)seq_len * (nq + 2 * nkv) * kHeadDim, n_seq, seq_len, nq,
+                          nkv, c->inv_freq, qimg, kimg, vimg, k_caches, v_caches, c->cfg.t_max,
+                          out, c->status, st));
   return GQA_OK;
 }
 

@@ -93,6 +93,7 @@ _SIGNATURES = {
     "gqa_lse_combine": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
     "gqa_decode_kv_shard": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _i, _vp, _vp, _vp],
     "gqa_lse_combine_packed": [_vp, _vp, _i, _i, _vp, _ll, _vp],
+    "gqa_prefill_bf16": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
     "gqa_fill_normal": [_vp, _vp, _vp, _ll, _ull, _ull, _ll],
     "gqa_inv_freq": [_vp, ctypes.POINTER(ctypes.c_float)],
     "gqa_version": [],
@@ -314,6 +315,11 @@ class Context:
                            stream=None) -> None:
         _check(lib().gqa_lse_combine_packed(self._h, _stream(stream), n_parts, n_rows,
                                             _ptr(packed), part_stride, _ptr(out)))
+
+    def prefill_bf16(self, n_seq: int, seq_len: int, qkv, out, k_ptrs=None, v_ptrs=None,
+                     stream=None) -> None:
+        _check(lib().gqa_prefill_bf16(self._h, _stream(stream), n_seq, seq_len, _ptr(qkv),
+                                      _ptr(out), _ptr(k_ptrs), _ptr(v_ptrs)))
 
     def fill_normal(self, dst, n: int, seed: int, stream_id: int, offset: int = 0,
                     stream=None) -> None:
