@@ -49,7 +49,10 @@ WORKLOADS = {
     "long": dict(layers=1, seqs=256, t_max=32768, window=64),
     "single": dict(layers=1, t_max=512, pos_lo=511, pos_hi=512, seqs=1),
     "long1": dict(layers=1, seqs=1, t_max=32768, window=64),
+    "prefill": dict(layers=1, seqs=8, t_max=2048),
 }
+
+PREFILL_METRIC = "GQA causal prefill: bf16 tensor-core TFLOP/s (fp32 accumulation)"
 
 
 def measured_peak():
@@ -259,6 +262,11 @@ def workload_config(name):
         return {"workload": "long: 256 sequences x 32768 fp32 KV rows (17.2 GB per layer)",
                 "seqs": 256, "t_max": 32768, "l2": "KV > L2; no flush",
                 "parallelism": "sequence-sharded"}
+    if name == "prefill":
+        return {"workload": "prefill: 8 sequences x 2048 tokens, 12 q / 2 KV heads, d=128, RoPE "
+                            "theta 1e6, fp32 inputs cast to bf16, causal, fp32 accumulation",
+                "seqs": 8, "seq_len": 2048, "flops_per_step": "4*B*Hq*d*S*(S+1)/2",
+                "l2": "inputs 134 MB > L2; no flush", "parallelism": "sequence-sharded"}
     if name == "long1":
         return {"workload": "long1: one sequence, 32768 fp32 KV rows (67 MB per layer) split by "
                             "KV range across the GPUs, partials all-gathered (NCCL) and "
@@ -481,6 +489,49 @@ def run_long1(args, g, ctx, rank, world, local):
                 tokens=args.steps / world, dominant_launches=args.steps)
 
 
+def run_prefill(args, g, ctx, rank, world, local):
+    import torch
+    wl = WORKLOADS["prefill"]
+    mine = g.shard.plan_sequence_shards([wl["t_max"]] * wl["seqs"], world)[rank]
+    n, S = len(mine), wl["t_max"]
+    x = torch.empty((max(n, 1), S, QKV_W), device="cuda")
+    ctx.fill_normal(x, x.numel(), 9090 + rank, g.seeded.PREFILL_Q)
+    out = torch.empty((max(n, 1), S, OUT_W), device="cuda")
+    stream = torch.cuda.current_stream()
+    flops = 4.0 * N_Q * D * S * (S + 1) / 2 * n
+    for _ in range(args.warmup):
+        ctx.prefill_bf16(n, S, x, out)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            ctx.prefill_bf16(n, S, x, out)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    h_x = x.cpu().pin_memory()
+    h_out = torch.empty(out.shape).pin_memory()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        x.copy_(h_x, non_blocking=True)
+        ctx.prefill_bf16(n, S, x, out)
+        h_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status set")
+    return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3, flops=flops * args.steps,
+                clocks=clk.summary(), launches=2 * args.steps, launches_per_step=2,
+                h2d=x.numel() * 4, d2h=out.numel() * 4, tokens=n * S * args.steps,
+                dominant_launches=args.steps)
+
+
 def run_ours(args):
     import torch
     rank, world, local = dist_setup(args.gpus)
@@ -497,6 +548,9 @@ def run_ours(args):
         ctx.set_option(g.gqa.GQA_OPT_TARGET_CTAS, args.target_ctas)
     if args.batch_chunk:
         ctx.set_option(g.gqa.GQA_OPT_BATCH_CHUNK, args.batch_chunk)
+    if args.workload == "prefill":
+        return report_prefill(args, run_prefill(args, g, ctx, rank, world, local), ctx, rank,
+                              world)
     if args.workload in ("resident28", "single"):
         r = run_resident(args, g, ctx, rank, world, local)
     elif args.workload == "long1":
@@ -545,6 +599,42 @@ def run_ours(args):
             "gpu_launches": r["launches"],
             "clocks": r["clocks"],
             "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def report_prefill(args, r, ctx, rank, world):
+    t = max_over_ranks(r["t"], world)
+    t_e2e = max_over_ranks(r["t_e2e"], world)
+    flops = sum_over_ranks(r["flops"], world)
+    tokens = sum_over_ranks(r["tokens"], world)
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peak, src = float(json.load(f)["bf16_tflops_sustained"]), "measured bf16_tflops_sustained"
+    except Exception:
+        peak, src = 1400.0, "fallback sustained"
+    tf = flops / t / 1e12
+    if rank == 0:
+        line = {
+            "metric": PREFILL_METRIC, "value": round(tf, 1), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t / args.steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded N(0,1) q/k/v (gqa_fill_normal)",
+            "config": workload_config("prefill"), "tok_per_s": round(tokens / t, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tf / world, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(tf / world / peak, 4),
+                         "peak_source": src, "kernel": "prefill_attn_kernel (+ prep kernel)",
+                         "algorithmic_flops_per_step": 4.0 * N_Q * D * 2048 * 2049 / 2 * 8,
+                         "traffic": None},
+            "e2e": {"value": round(flops / t_e2e / 1e12, 1), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+            "gpu_launches": r["launches"], "clocks": r["clocks"], "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)
     ctx.close()
