@@ -32,8 +32,10 @@ cudaError_t launch_advance_pos(int* pos, int wrap_lo, int wrap_hi, cudaStream_t 
 cudaError_t launch_fill_normal(float* dst, long long n, uint64_t key, long long offset,
                                int n_sm, cudaStream_t st);
 cudaError_t prepare_prefill_kernels();
+cudaError_t launch_prefill_rope_table(const float* inv_freq, float2* cs, int n_pos,
+                                      cudaStream_t st);
 cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, int S, int n_q,
-                           int n_kv, const float* inv_freq, __nv_bfloat16* qimg,
+                           int n_kv, const float2* rope_cs, __nv_bfloat16* qimg,
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
                            cudaStream_t st);
@@ -69,6 +71,8 @@ struct gqa_ctx {
   int* counters = nullptr;  // [kMaxCounters] arrival counters, kept at zero
   __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
   size_t prefill_cap = 0;                // elements
+  float2* rope_cs = nullptr;             // prefill RoPE table [rope_cap][64] (cos, sin)
+  int rope_cap = 0;                      // positions in the table
 };
 
 struct gqa_graph {
@@ -347,6 +351,7 @@ int gqa_destroy(gqa_ctx* c) {
   if (c->status) cudaFree(c->status);
   if (c->counters) cudaFree(c->counters);
   if (c->prefill_img) cudaFree(c->prefill_img);
+  if (c->rope_cs) cudaFree(c->rope_cs);
   if (c->part_o) cudaFree(c->part_o);
   if (c->part_ml) cudaFree(c->part_ml);
   delete c;
@@ -792,11 +797,27 @@ int gqa_prefill_bf16(gqa_ctx* c, gqa_stream_t stream, int n_seq, int seq_len, co
     }
     c->prefill_cap = need;
   }
+  if (seq_len > c->rope_cap) {
+    // The table covers max(seq_len, t_max) positions and is filled once, on
+    // the caller's stream, when it is (re)allocated.
+    if (is_capturing(st) || c->live_graphs > 0)
+      return fail(GQA_ERR_NO_MEMORY, "prefill RoPE table must grow outside capture / live graphs");
+    const int cap = seq_len > c->cfg.t_max ? seq_len : c->cfg.t_max;
+    if (c->rope_cs) cudaFree(c->rope_cs);
+    c->rope_cs = nullptr;
+    c->rope_cap = 0;
+    if (cudaMalloc(&c->rope_cs, sizeof(float2) * (size_t)cap * (kHeadDim / 2)) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(GQA_ERR_NO_MEMORY, "cudaMalloc of the prefill RoPE table failed");
+    }
+    GQA_CUDA(launch_prefill_rope_table(c->inv_freq, c->rope_cs, cap, st));
+    c->rope_cap = cap;
+  }
   __nv_bfloat16* qimg = c->prefill_img;
   __nv_bfloat16* kimg = qimg + per * nq;
   __nv_bfloat16* vimg = kimg + per * nkv;
   GQA_CUDA(launch_prefill(qkv, (long long)seq_len * (nq + 2 * nkv) * kHeadDim, n_seq, seq_len, nq,
-                          nkv, c->inv_freq, qimg, kimg, vimg, k_caches, v_caches, c->cfg.t_max,
+                          nkv, c->rope_cs, qimg, kimg, vimg, k_caches, v_caches, c->cfg.t_max,
                           out, c->status, st));
   return GQA_OK;
 }

@@ -40,8 +40,8 @@ constexpr int kPT = 128;                          // tile rows (queries or keys)
 constexpr int kImgElems = kPT * kHeadDim;         // one tile image (bf16 elements)
 constexpr int kImgBytes = kImgElems * 2;          // 32 KB
 constexpr int kKBlockElems = kPT * 64;            // one 64-wide K block (16 KB)
-constexpr int kPrefillThreads = 192;              // warps 0-3 softmax, 4 loader, 5 MMA
-constexpr int kTmemCols = 512;                    // S0 | S1 | O (| unused)
+constexpr int kPrefillThreads = 320;              // warps 0-7 softmax, 8 loader, 9 MMA
+constexpr int kTmemCols = 512;                    // S_A | S_B | O_A | O_B
 constexpr long long kPrefillWaitBudget = 2000000000LL;
 
 // Element offset of (row r, k) in a 128 x 128 bf16 K-major image with the
@@ -138,6 +138,132 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       : "memory");
 }
 
+// 128 consecutive fp32 columns of this thread's TMEM lane, waited in the same statement.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128]) {
+  uint32_t r[128];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x128.b32 {"
+      "%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, "
+      "%32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, "
+      "%64, %65, %66, %67, %68, %69, %70, %71, %72, %73, %74, %75, %76, %77, %78, %79, "
+      "%80, %81, %82, %83, %84, %85, %86, %87, %88, %89, %90, %91, %92, %93, %94, %95, "
+      "%96, %97, %98, %99, %100, %101, %102, %103, %104, %105, %106, %107, %108, %109, %110, %111, "
+      "%112, %113, %114, %115, %116, %117, %118, %119, %120, %121, %122, %123, %124, %125, %126, %127}, [%128];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]),
+        "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+        "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]),
+        "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]),
+        "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+        "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]),
+        "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]),
+        "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+        "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 64 consecutive 32-bit columns of this thread's TMEM lane, waited in the same statement.
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&v)[64]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {"
+      "%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, "
+      "%33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, "
+      "%49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64};\n\t"
+      "tcgen05.wait::st.sync.aligned;"
+      ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+        "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+        "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]),
+        "r"(v[32]), "r"(v[33]), "r"(v[34]), "r"(v[35]), "r"(v[36]), "r"(v[37]), "r"(v[38]), "r"(v[39]),
+        "r"(v[40]), "r"(v[41]), "r"(v[42]), "r"(v[43]), "r"(v[44]), "r"(v[45]), "r"(v[46]), "r"(v[47]),
+        "r"(v[48]), "r"(v[49]), "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]), "r"(v[55]),
+        "r"(v[56]), "r"(v[57]), "r"(v[58]), "r"(v[59]), "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63])
+      : "memory");
+}
+
+// max of three (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two non-negative finite floats to a bf16 pair (lo = a) with integer ops,
+// rounding to nearest (ties away from zero), so the conversion runs on the
+// integer pipe instead of the one ex2 uses.
+__device__ __forceinline__ uint32_t pack_bf16_pos(float a, float b) {
+  return __byte_perm(__float_as_uint(a) + 0x8000u, __float_as_uint(b) + 0x8000u, 0x7632);
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int n_threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n_threads) : "memory");
+}
+
+// Packed fp32 pair arithmetic (one f32x2 instruction for two lanes of work).
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
+                                      float c0, float c1) {
+  asm("{\n\t.reg .b64 a, b, c, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+      "fma.rn.f32x2 d, a, b, c;\n\t"
+      "mov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\t"
+      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "add.rn.f32x2 d, a, b;\n\t"
+      "mov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// 2^x for a pair on the FMA pipe, for x <= 2^22 (x below -125 is clamped;
+// 2^-125 is as good as 0 for a softmax weight).  Range reduction x = n + f,
+// n = round(x) taken from the low mantissa bits of x + 1.5 * 2^23, f in
+// [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted to relative error on
+// [-1/2, 1/2] (Lawson's iteratively reweighted least squares, max relative
+// error 7.5e-5, far below the bf16 rounding of P); 2^n added to the exponent
+// field.  Generator: csrc/fit_exp2_poly.py.
+constexpr float kExp2C0 = 0.9999281167984009f;
+constexpr float kExp2C1 = 0.6932609677314758f;
+constexpr float kExp2C2 = 0.24261054396629333f;
+constexpr float kExp2C3 = 0.05517132207751274f;
+constexpr float kRoundShift = 12582912.0f;  // 1.5 * 2^23
+
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  x0 = fmaxf(x0, -125.f);
+  x1 = fmaxf(x1, -125.f);
+  float t0, t1, n0, n1, f0, f1, r0, r1;
+  fadd2(t0, t1, x0, x1, kRoundShift, kRoundShift);    // n in the low mantissa bits
+  fadd2(n0, n1, t0, t1, -kRoundShift, -kRoundShift);  // n = round(x)
+  ffma2(f0, f1, n0, n1, -1.f, -1.f, x0, x1);          // f = x - n (exact)
+  ffma2(r0, r1, kExp2C3, kExp2C3, f0, f1, kExp2C2, kExp2C2);
+  ffma2(r0, r1, r0, r1, f0, f1, kExp2C1, kExp2C1);
+  ffma2(r0, r1, r0, r1, f0, f1, kExp2C0, kExp2C0);
+  y0 = __uint_as_float(__float_as_uint(r0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(r1) + (__float_as_uint(t1) << 23));
+}
+
+// Of every four key pairs, this many take exp2_poly2 and the rest the MUFU
+// ex2 (16 lanes per clock per SM), so the two pipes share the softmax work.
+constexpr int kPolyPairs = 1;
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -147,12 +273,22 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // ---------------------------------------------------------------------------
 // Prep: RoPE, bf16, swizzled tile images, cache append
 // ---------------------------------------------------------------------------
+// RoPE table for the prefill: cs[pos][i] = (cos, sin) of pos * inv_freq[i],
+// the angle formed in fp32 exactly as the decode kernels form it.
+__global__ void prefill_rope_table_kernel(const float* inv_freq, float2* cs, int n_pos) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n_pos * kHalf) return;
+  float sn, c;
+  sincosf((float)(idx / kHalf) * inv_freq[idx % kHalf], &sn, &c);
+  cs[idx] = make_float2(c, sn);
+}
+
 struct PrefillPrepParams {
   const float* qkv;      // [n_seq][S][(n_q + 2 n_kv) * 128]
   long long seq_stride;  // floats between sequences
   int S;
   int n_q, n_kv;
-  const float* inv_freq;
+  const float2* rope_cs; // [>= S][64] (cos, sin)
   __nv_bfloat16* qimg;   // [n_seq][n_q][S/128] images
   __nv_bfloat16* kimg;   // [n_seq][n_kv][S/128] images
   __nv_bfloat16* vimg;   // [n_seq][n_kv][S/128] images (transposed)
@@ -161,54 +297,92 @@ struct PrefillPrepParams {
   int t_max;
 };
 
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  __nv_bfloat162 b = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+// One block per (head slot, 128-token tile, sequence).  Head slots 0..n_q-1
+// are q heads, then n_kv k heads, then n_kv v heads.  Every thread produces
+// whole 16-byte chunks (8 bf16) of the swizzled image, so image stores are
+// 16-byte vectors; reads of the fp32 rows are 32-byte pieces of one row
+// across neighbouring threads.
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrefillPrepParams p) {
-  __shared__ float cs[kHalf][2];
-  const int s = blockIdx.x, seq = blockIdx.y, tid = threadIdx.x;
-  if (tid < kHalf) {
-    float sn, c;
-    sincosf((float)s * p.inv_freq[tid], &sn, &c);
-    cs[tid][0] = c;
-    cs[tid][1] = sn;
-  }
-  __syncthreads();
+  const int unit = blockIdx.x, tile = blockIdx.y, seq = blockIdx.z, tid = threadIdx.x;
   const int width = (p.n_q + 2 * p.n_kv) * kHeadDim;
-  const float* row = p.qkv + (long long)seq * p.seq_stride + (long long)s * width;
   const int n_tiles = p.S / kPT;
-  const int tile = s / kPT, r = s % kPT;
-  float* kc = p.k_caches ? p.k_caches[seq] : nullptr;
-  float* vc = p.v_caches ? p.v_caches[seq] : nullptr;
-  // q and k heads: one rotation pair per thread-iteration
-  for (int idx = tid; idx < (p.n_q + p.n_kv) * kHalf; idx += blockDim.x) {
-    const int hh = idx / kHalf, i = idx % kHalf;
-    const float x0 = row[hh * kHeadDim + i], x1 = row[hh * kHeadDim + i + kHalf];
-    const float c = cs[i][0], sn = cs[i][1];
-    const float y0 = x0 * c - x1 * sn;
-    const float y1 = x0 * sn + x1 * c;
-    if (hh < p.n_q) {
-      __nv_bfloat16* img =
-          p.qimg + ((long long)(seq * p.n_q + hh) * n_tiles + tile) * kImgElems;
-      img[sw_offset(r, i)] = __float2bfloat16_rn(y0);
-      img[sw_offset(r, i + kHalf)] = __float2bfloat16_rn(y1);
-    } else {
-      const int kh = hh - p.n_q;
-      __nv_bfloat16* img =
-          p.kimg + ((long long)(seq * p.n_kv + kh) * n_tiles + tile) * kImgElems;
-      img[sw_offset(r, i)] = __float2bfloat16_rn(y0);
-      img[sw_offset(r, i + kHalf)] = __float2bfloat16_rn(y1);
+  const float* base = p.qkv + (long long)seq * p.seq_stride + (long long)tile * kPT * width +
+                      (long long)unit * kHeadDim;
+  if (unit < p.n_q + p.n_kv) {
+    // q or k head: rotate pairs (i, i + 64); item = (row r, chunk c of 8 pairs)
+    const bool is_q = unit < p.n_q;
+    const int kh = unit - p.n_q;
+    __nv_bfloat16* img =
+        is_q ? p.qimg + ((long long)(seq * p.n_q + unit) * n_tiles + tile) * kImgElems
+             : p.kimg + ((long long)(seq * p.n_kv + kh) * n_tiles + tile) * kImgElems;
+    float* kc = (!is_q && p.k_caches) ? p.k_caches[seq] : nullptr;
+    for (int item = tid; item < kPT * 8; item += blockDim.x) {
+      const int r = item >> 3, c = item & 7;
+      const int pos = tile * kPT + r;
+      const float* row = base + (long long)r * width;
+      const float4 a0 = *reinterpret_cast<const float4*>(row + 8 * c);
+      const float4 a1 = *reinterpret_cast<const float4*>(row + 8 * c + 4);
+      const float4 b0 = *reinterpret_cast<const float4*>(row + kHalf + 8 * c);
+      const float4 b1 = *reinterpret_cast<const float4*>(row + kHalf + 8 * c + 4);
+      const float4* csp = reinterpret_cast<const float4*>(p.rope_cs + (long long)pos * kHalf + 8 * c);
+      const float4 t0 = csp[0], t1 = csp[1], t2 = csp[2], t3 = csp[3];  // (cos, sin) x 8
+      const float x0[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float x1[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      const float co[8] = {t0.x, t0.z, t1.x, t1.z, t2.x, t2.z, t3.x, t3.z};
+      const float si[8] = {t0.y, t0.w, t1.y, t1.w, t2.y, t2.w, t3.y, t3.w};
+      float y0[8], y1[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        y0[e] = x0[e] * co[e] - x1[e] * si[e];
+        y1[e] = x0[e] * si[e] + x1[e] * co[e];
+      }
+      *reinterpret_cast<uint4*>(img + sw_offset(r, 8 * c)) =
+          make_uint4(bf16x2_rn(y0[0], y0[1]), bf16x2_rn(y0[2], y0[3]), bf16x2_rn(y0[4], y0[5]),
+                     bf16x2_rn(y0[6], y0[7]));
+      *reinterpret_cast<uint4*>(img + sw_offset(r, kHalf + 8 * c)) =
+          make_uint4(bf16x2_rn(y1[0], y1[1]), bf16x2_rn(y1[2], y1[3]), bf16x2_rn(y1[4], y1[5]),
+                     bf16x2_rn(y1[6], y1[7]));
       if (kc) {
-        float* dst = kc + ((long long)kh * p.t_max + s) * kHeadDim;
-        dst[i] = y0;
-        dst[i + kHalf] = y1;
+        float* dst = kc + ((long long)kh * p.t_max + pos) * kHeadDim;
+        if ((reinterpret_cast<uintptr_t>(kc) & 15) == 0) {
+          *reinterpret_cast<float4*>(dst + 8 * c) = make_float4(y0[0], y0[1], y0[2], y0[3]);
+          *reinterpret_cast<float4*>(dst + 8 * c + 4) = make_float4(y0[4], y0[5], y0[6], y0[7]);
+          *reinterpret_cast<float4*>(dst + kHalf + 8 * c) = make_float4(y1[0], y1[1], y1[2], y1[3]);
+          *reinterpret_cast<float4*>(dst + kHalf + 8 * c + 4) =
+              make_float4(y1[4], y1[5], y1[6], y1[7]);
+        } else {  // a cache that is only 4-byte aligned
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            dst[8 * c + e] = y0[e];
+            dst[kHalf + 8 * c + e] = y1[e];
+          }
+        }
       }
     }
-  }
-  // v heads: transposed image (row = head dim, K = key within the tile)
-  for (int idx = tid; idx < p.n_kv * kHeadDim; idx += blockDim.x) {
-    const int kh = idx / kHeadDim, d = idx % kHeadDim;
-    const float x = row[(p.n_q + p.n_kv + kh) * kHeadDim + d];
-    __nv_bfloat16* img = p.vimg + ((long long)(seq * p.n_kv + kh) * n_tiles + tile) * kImgElems;
-    img[sw_offset(d, r)] = __float2bfloat16_rn(x);
-    if (vc) vc[((long long)kh * p.t_max + s) * kHeadDim + d] = x;
+  } else {
+    // v head: transposed image, row = head dim d, K = token; item = (d, 8 tokens)
+    const int vh = unit - p.n_q - p.n_kv;
+    __nv_bfloat16* img = p.vimg + ((long long)(seq * p.n_kv + vh) * n_tiles + tile) * kImgElems;
+    float* vc = p.v_caches ? p.v_caches[seq] : nullptr;
+    for (int item = tid; item < kPT * (kPT / 8); item += blockDim.x) {
+      const int d = item & (kHeadDim - 1), rg = item >> 7;
+      float x[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = base[(long long)(8 * rg + e) * width + d];
+      *reinterpret_cast<uint4*>(img + sw_offset(d, 8 * rg)) =
+          make_uint4(bf16x2_rn(x[0], x[1]), bf16x2_rn(x[2], x[3]), bf16x2_rn(x[4], x[5]),
+                     bf16x2_rn(x[6], x[7]));
+      if (vc) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          vc[((long long)vh * p.t_max + tile * kPT + 8 * rg + e) * kHeadDim + d] = x[e];
+      }
+    }
   }
 }
 
@@ -226,18 +400,75 @@ struct PrefillAttnParams {
   int* status;
 };
 
+// One CTA serves two q heads of one KV group on the same 128-token query tile,
+// so every K / V^T tile it stages feeds two S = QK^T and two O += PV MMAs.
 struct PrefillSmem {
-  __nv_bfloat16 q[kImgElems];
-  __nv_bfloat16 k[2][kImgElems];
-  __nv_bfloat16 vt[2][kImgElems];
-  __nv_bfloat16 p[kImgElems];
-  uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], s_empty[2], p_full, o_done;
+  __nv_bfloat16 q[2][kImgElems];   // the two Q tiles (head 2h, 2h+1)
+  __nv_bfloat16 k[2][kImgElems];   // K tile ring
+  __nv_bfloat16 vt[2][kImgElems];  // V^T tile ring
+  uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full[2], p_full[2], o_final[2], drain;
   uint32_t tmem_base;
   int err;
 };
 
 constexpr size_t prefill_smem_bytes() { return sizeof(PrefillSmem) + 1024; }  // + alignment slack
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps in the barrier unit (until the phase completes or the hint runs out)
+// instead of spinning, so a waiting warp leaves the issue slots of its
+// scheduler to the softmax warp that shares it.
+constexpr uint32_t kSuspendHintNs = 20000;
+
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that also gives up as soon as another role has raised `err`.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* err) {
+  if (mbar_try_wait_suspend(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait_suspend(bar, parity)) {
+    if (*err) return false;
+    if (clock64() - start > kPrefillWaitBudget) {
+      atomicOr((int*)err, 1);
+      return false;
+    }
+  }
+  return true;
+}
+
+// O += P.V with P (bf16, M = 128 query rows x K = 16 keys) read from tensor
+// memory: row = TMEM lane, two consecutive keys per 32-bit column.
+__device__ __forceinline__ void umma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                                 bool acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(kIdescBf16M128N128), "r"((uint32_t)acc));
+}
+
+// Tensor memory plan (512 columns, all 128 lanes): S of head g in columns
+// [128 g, 128 g + 128), O of head g in [256 + 128 g, 384 + 128 g).  P of head g
+// (bf16 pairs) overwrites the first 64 columns of its own S once the softmax
+// thread has read that S row into registers; the next S MMA of head g is
+// issued after the P.V MMA that reads it, and tcgen05.mma operations of one
+// thread execute in issue order.
+//
+// MMA issue order per key tile j (heads A = 0, B = 1):
+//   PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)
+// so the softmax of one head always overlaps two MMAs of the other.  The
+// commit that signals S_g(j+1) also covers PV_g(j): when the softmax thread of
+// head g sees S, its O row is final up to key tile j and may be rescaled.
 __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const PrefillAttnParams p) {
   extern __shared__ unsigned char smem_raw[];
   // The swizzled operand images need 1 KB alignment.
@@ -245,25 +476,31 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_tiles = p.S / kPT;
-  const int i = n_tiles - 1 - (int)blockIdx.x;  // heaviest (longest causal) tiles first
-  const int hq = blockIdx.y, seq = blockIdx.z;
-  const int kvh = hq / (p.n_q / p.n_kv);
+  // The query tile is the slowest grid dimension, longest causal tiles first,
+  // so the block scheduler hands out the heavy work before the light tail.
+  const int i = n_tiles - 1 - (int)blockIdx.z;
+  const int pair = blockIdx.x, seq = blockIdx.y;
+  const int hq0 = 2 * pair;
+  const int kvh = hq0 / (p.n_q / p.n_kv);
   const int n_kv_tiles = i + 1;
+  volatile int* err = &sm.err;
 
   if (tid == 0) {
     mbar_init(&sm.q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.s_empty[s], 128);
+      mbar_init(&sm.p_full[s], 4);  // one arrival per softmax warp
+      mbar_init(&sm.o_final[s], 1);
     }
-    mbar_init(&sm.p_full, 128);
-    mbar_init(&sm.o_done, 1);
+    mbar_init(&sm.drain, 1);
     sm.err = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                  ::"r"(smem_addr(&sm.tmem_base)), "r"(kTmemCols) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -272,180 +509,225 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
-  const uint32_t tmem_s[2] = {tmem, tmem + 128};
-  const uint32_t tmem_o = tmem + 256;
 
-  const long long q_off = ((long long)(seq * p.n_q + hq) * n_tiles + i) * kImgElems;
   const long long kv_base = (long long)(seq * p.n_kv + kvh) * n_tiles * kImgElems;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---- loader ----
     if (lane == 0) {
       const uint64_t policy = l2_policy_evict_first();
-      mbar_arrive_expect_tx(&sm.q_full, kImgBytes);
-      bulk_copy_g2s(sm.q, p.qimg + q_off, kImgBytes, &sm.q_full, policy);
+      mbar_arrive_expect_tx(&sm.q_full, 2 * kImgBytes);
+      for (int g = 0; g < 2; ++g) {
+        const long long q_off = ((long long)(seq * p.n_q + hq0 + g) * n_tiles + i) * kImgElems;
+        bulk_copy_g2s(sm.q[g], p.qimg + q_off, kImgBytes, &sm.q_full, policy);
+      }
+      int k_issued = 0, v_issued = 0;
       for (int j = 0; j < n_kv_tiles; ++j) {
         const int st = j & 1;
-        if (j >= 2 && !mbar_wait_bounded(&sm.kv_empty[st], ((j >> 1) - 1) & 1,
-                                         kPrefillWaitBudget)) {
-          atomicOr(&sm.err, 1);
-          break;
-        }
-        mbar_arrive_expect_tx(&sm.kv_full[st], 2 * kImgBytes);
+        const uint32_t reuse = ((j >> 1) - 1) & 1;
         // K and V tiles are re-read by the other q heads of the group: keep them in L2.
+        if (j >= 2 && !wait_or_abort(&sm.k_empty[st], reuse, err)) break;
+        mbar_arrive_expect_tx(&sm.k_full[st], kImgBytes);
         asm volatile(
             "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
             ::"r"(smem_addr(sm.k[st])), "l"(p.kimg + kv_base + (long long)j * kImgElems),
-              "r"(kImgBytes), "r"(smem_addr(&sm.kv_full[st])) : "memory");
+              "r"(kImgBytes), "r"(smem_addr(&sm.k_full[st])) : "memory");
+        ++k_issued;
+        if (j >= 2 && !wait_or_abort(&sm.v_empty[st], reuse, err)) break;
+        mbar_arrive_expect_tx(&sm.v_full[st], kImgBytes);
         asm volatile(
             "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
             ::"r"(smem_addr(sm.vt[st])), "l"(p.vimg + kv_base + (long long)j * kImgElems),
-              "r"(kImgBytes), "r"(smem_addr(&sm.kv_full[st])) : "memory");
+              "r"(kImgBytes), "r"(smem_addr(&sm.v_full[st])) : "memory");
+        ++v_issued;
+      }
+      if (*err) {
+        // Let the copies already issued land before the CTA's shared memory
+        // can be handed to another CTA (copies always complete).
+        mbar_wait_bounded(&sm.q_full, 0, kPrefillWaitBudget);
+        for (int j = k_issued - 2; j < k_issued; ++j)
+          if (j >= 0) mbar_wait_bounded(&sm.k_full[j & 1], (j >> 1) & 1, kPrefillWaitBudget);
+        for (int j = v_issued - 2; j < v_issued; ++j)
+          if (j >= 0) mbar_wait_bounded(&sm.v_full[j & 1], (j >> 1) & 1, kPrefillWaitBudget);
       }
     }
     __syncwarp();  // the other lanes wait here, so the warp reaches the block barrier converged
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---- MMA issuer ----
     if (lane == 0) {
-      bool ok = mbar_wait_bounded(&sm.q_full, 0, kPrefillWaitBudget);
-      const uint32_t q_addr = smem_addr(sm.q);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait_bounded(&sm.kv_full[st], (j >> 1) & 1, kPrefillWaitBudget)) return false;
-        if (j >= 2 && !mbar_wait_bounded(&sm.s_empty[st], ((j >> 1) - 1) & 1, kPrefillWaitBudget))
-          return false;
-        tc_fence_after();
-        const uint32_t k_addr = smem_addr(sm.k[st]);
+      const uint32_t q_addr[2] = {smem_addr(sm.q[0]), smem_addr(sm.q[1])};
+      auto issue_s = [&](int g, int j) {
+        const uint32_t k_addr = smem_addr(sm.k[j & 1]);
 #pragma unroll
         for (int ks = 0; ks < kHeadDim / 16; ++ks) {
           const uint32_t off = (ks >> 2) * (kKBlockElems * 2) + (ks & 3) * 32;
-          umma_bf16(tmem_s[st], umma_smem_desc(q_addr + off), umma_smem_desc(k_addr + off), ks > 0);
+          umma_bf16(tmem + 128 * g, umma_smem_desc(q_addr[g] + off),
+                    umma_smem_desc(k_addr + off), ks > 0);
         }
-        umma_commit(&sm.s_full[st]);
-        return true;
+        umma_commit(&sm.s_full[g]);
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_kv_tiles; ++j) {
-        if (j + 1 < n_kv_tiles && !issue_s(j + 1)) { ok = false; break; }
-        if (!mbar_wait_bounded(&sm.p_full, j & 1, kPrefillWaitBudget)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t p_addr = smem_addr(sm.p);
+      auto issue_pv = [&](int g, int j) {
         const uint32_t v_addr = smem_addr(sm.vt[j & 1]);
 #pragma unroll
         for (int ks = 0; ks < kPT / 16; ++ks) {
           const uint32_t off = (ks >> 2) * (kKBlockElems * 2) + (ks & 3) * 32;
-          umma_bf16(tmem_o, umma_smem_desc(p_addr + off), umma_smem_desc(v_addr + off),
-                    j > 0 || ks > 0);
+          umma_bf16_tmem_a(tmem + 256 + 128 * g, tmem + 128 * g + ks * 8,
+                           umma_smem_desc(v_addr + off), j > 0 || ks > 0);
         }
-        umma_commit(&sm.o_done);
-        umma_commit(&sm.kv_empty[j & 1]);
+      };
+      bool ok = wait_or_abort(&sm.q_full, 0, err) && wait_or_abort(&sm.k_full[0], 0, err);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&sm.k_empty[0]);
       }
-      if (!ok) atomicOr(&sm.err, 1);
+      for (int j = 0; ok && j < n_kv_tiles; ++j) {
+        const bool more = j + 1 < n_kv_tiles;
+        const int sn = (j + 1) & 1;
+        const uint32_t pn = ((j + 1) >> 1) & 1;
+        if (!wait_or_abort(&sm.p_full[0], j & 1, err) ||
+            !wait_or_abort(&sm.v_full[j & 1], (j >> 1) & 1, err)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!wait_or_abort(&sm.k_full[sn], pn, err)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(0, j + 1);
+        } else {
+          umma_commit(&sm.o_final[0]);
+        }
+        if (!wait_or_abort(&sm.p_full[1], j & 1, err)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(&sm.v_empty[j & 1]);
+        if (more) {
+          issue_s(1, j + 1);
+          umma_commit(&sm.k_empty[sn]);
+        } else {
+          umma_commit(&sm.o_final[1]);
+        }
+      }
+      // Whatever happened, no MMA may still be running when TMEM is freed.
+      umma_commit(&sm.drain);
+      mbar_wait_bounded(&sm.drain, 0, kPrefillWaitBudget);
     }
     __syncwarp();
   } else {
-    // ---- softmax: thread tid owns query row tid of the tile (TMEM lane tid) ----
-    const int r = tid;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    // ---- softmax: warps 4g..4g+3 serve head g; thread owns query row r ----
+    const int g = warp >> 2, r = tid & 127;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + lane_off + 128 * g;
+    const uint32_t t_o = tmem + lane_off + 256 + 128 * g;
+    const float sc = p.scale_log2;
     float m = -CUDART_INF_F, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_kv_tiles && ok; ++j) {
-      const int st = j & 1;
+    for (int j = 0; j < n_kv_tiles; ++j) {
       // Waits are voted so the warp stays converged for the warp-collective
       // tensor-memory loads and stores.
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(&sm.s_full[st], (j >> 1) & 1,
-                                                     kPrefillWaitBudget));
+      ok = __all_sync(0xffffffffu, wait_or_abort(&sm.s_full[g], j & 1, err));
       if (!ok) break;
       tc_fence_after();
       float s[kPT];
+      tmem_ld128(t_s, s);
+      if (j == i) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(tmem_s[st] + lane_off + c * 32, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = v[e];
+        for (int c = 0; c < kPT; ++c)
+          if (c > r) s[c] = -CUDART_INF_F;  // causal: keys after the query
       }
-      tc_fence_before();
-      mbar_arrive(&sm.s_empty[st]);
-      const bool diag = (j == i);
-      float rowmax = -CUDART_INF_F;
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
 #pragma unroll
-      for (int c = 0; c < kPT; ++c) {
-        float x = s[c] * p.scale_log2;
-        if (diag && c > r) x = -CUDART_INF_F;  // causal: keys after the query
-        s[c] = x;
-        rowmax = fmaxf(rowmax, x);
+      for (int c = 4; c < kPT; c += 8) {
+        mx0 = fmax3(mx0, s[c], s[c + 1]);
+        mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
+        mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
+        mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
       }
-      const bool move = (j == 0) || rowmax > m + 8.0f;
-      const float m_new = move ? fmaxf(m, rowmax) : m;
-      const float alpha = (move && j > 0) ? fast_exp2(m - m_new) : 1.f;
-      m = m_new;
-      float sum = 0.f;
-      uint32_t packed[kPT / 2];
+      const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sc;
+      float alpha = 1.f;
+      if (j == 0 || mt > m + 8.0f) {  // lazy: move the reference max only by > 2^8
+        const float mn = fmaxf(m, mt);
+        if (j > 0) alpha = fast_exp2(m - mn);
+        m = mn;
+      }
+      const float nm = -m;
+      float sum0 = 0.f, sum1 = 0.f;
+      uint32_t pk[kPT / 2];
 #pragma unroll
       for (int c = 0; c < kPT; c += 2) {
-        const float p0 = fast_exp2(s[c] - m), p1 = fast_exp2(s[c + 1] - m);
-        sum += p0 + p1;
-        __nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-        packed[c / 2] = *reinterpret_cast<uint32_t*>(&b2);
+        float x0, x1, p0, p1;
+        ffma2(x0, x1, s[c], s[c + 1], sc, sc, nm, nm);
+        if (((c >> 1) & 3) < kPolyPairs) {
+          exp2_poly2(x0, x1, p0, p1);
+        } else {
+          p0 = fast_exp2(x0);
+          p1 = fast_exp2(x1);
+        }
+        fadd2(sum0, sum1, sum0, sum1, p0, p1);
+        pk[c / 2] = pack_bf16_pos(p0, p1);
       }
-      l = l * alpha + sum;
-      // P.V of the previous tile must be done: O is then current and P free.
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait_bounded(&sm.o_done, (j - 1) & 1, kPrefillWaitBudget));
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      tmem_st64(t_s, pk);
+      l = l * alpha + (sum0 + sum1);
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float v[32];
-            tmem_ld32(tmem_o + lane_off + c * 32, v);
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(t_o + c * 32, v);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] *= alpha;
-            tmem_st32(tmem_o + lane_off + c * 32, v);
-          }
+          for (int e = 0; e < 32; ++e) v[e] *= alpha;
+          tmem_st32(t_o + c * 32, v);
         }
       }
-      // P row -> swizzled operand image (8 bf16 = 16 B per store)
-#pragma unroll
-      for (int ch = 0; ch < kPT / 8; ++ch) {
-        const int k0 = ch * 8;
-        uint4 val = make_uint4(packed[k0 / 2], packed[k0 / 2 + 1], packed[k0 / 2 + 2],
-                               packed[k0 / 2 + 3]);
-        *reinterpret_cast<uint4*>(&sm.p[sw_offset(r, k0)]) = val;
-      }
-      fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&sm.p_full);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.p_full[g]);
     }
-    const bool fin = __all_sync(0xffffffffu, ok && mbar_wait_bounded(&sm.o_done,
-                                                                     (n_kv_tiles - 1) & 1,
-                                                                     kPrefillWaitBudget));
+    const bool fin = __all_sync(0xffffffffu, ok && wait_or_abort(&sm.o_final[g], 0, err));
+    float* stage = reinterpret_cast<float*>(g == 0 ? &sm.k[0][0] : &sm.q[0][0]);
     if (fin) {
+      // Epilogue through shared memory: once o_final of head g fired, every
+      // S MMA has completed, so head 0 stages its O tile in the K ring and
+      // head 1 in the Q tiles (64 KB each).  Staging layout: four 16 KB
+      // column blocks of 128 rows x 32 floats, the 16-byte chunk k of row r
+      // at chunk k ^ (r % 8), so both the row-wise writes here and the
+      // chunk-wise reads below touch each bank once per 128 bytes.
       tc_fence_after();
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
-      float* dst = p.out + ((long long)seq * p.S + (long long)i * kPT + r) * p.n_q * kHeadDim +
-                   (long long)hq * kHeadDim;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float v[32];
-        tmem_ld32(tmem_o + lane_off + c * 32, v);
+        tmem_ld32(t_o + c * 32, v);
+        float* row = stage + c * (kPT * 32) + r * 32;
 #pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4*>(dst + c * 32 + e) =
-              make_float4(v[e] * inv_l, v[e + 1] * inv_l, v[e + 2] * inv_l, v[e + 3] * inv_l);
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float4*>(row + ((k ^ (r & 7)) << 2)) =
+              make_float4(v[4 * k] * inv_l, v[4 * k + 1] * inv_l, v[4 * k + 2] * inv_l,
+                          v[4 * k + 3] * inv_l);
       }
     } else {
       atomicOr(&sm.err, 1);
     }
+    // All 128 threads of the head reach this barrier on every path; a warp
+    // that failed raised err before it, so no thread copies unwritten rows.
+    named_barrier_sync(1 + g, 128);
+    if (*err == 0) {
+      // Coalesced copy-out: warp w writes rows 32w..32w+31, one 512-byte row
+      // per instruction (lane = 16-byte chunk of the row).
+      float* dst = p.out + ((long long)seq * p.S + (long long)i * kPT) * p.n_q * kHeadDim +
+                   (long long)(hq0 + g) * kHeadDim + lane * 4;
+      const float* src = stage + (lane >> 3) * (kPT * 32);
+#pragma unroll 4
+      for (int rr = (warp & 3) * 32; rr < (warp & 3) * 32 + 32; ++rr)
+        *reinterpret_cast<float4*>(dst + (long long)rr * p.n_q * kHeadDim) =
+            *reinterpret_cast<const float4*>(src + rr * 32 + (((lane & 7) ^ (rr & 7)) << 2));
+    }
   }
 
-  // ---- teardown: make sure no MMA is still writing, then free TMEM ----
+  // ---- teardown: the MMA warp drained its MMAs; free TMEM ----
   tc_fence_before();
   __syncthreads();
   if (sm.err && tid == 0) atomicOr(p.status, kStatusWaitTimeout);
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
                  ::"r"(tmem), "r"(kTmemCols) : "memory");
@@ -462,8 +744,15 @@ cudaError_t prepare_prefill_kernels() {
                               (int)prefill_smem_bytes());
 }
 
+cudaError_t launch_prefill_rope_table(const float* inv_freq, float2* cs, int n_pos,
+                                      cudaStream_t st) {
+  const int n = n_pos * kHalf;
+  prefill_rope_table_kernel<<<(n + 255) / 256, 256, 0, st>>>(inv_freq, cs, n_pos);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, int S, int n_q,
-                           int n_kv, const float* inv_freq, __nv_bfloat16* qimg,
+                           int n_kv, const float2* rope_cs, __nv_bfloat16* qimg,
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
                            cudaStream_t st) {
@@ -473,14 +762,14 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
   pp.S = S;
   pp.n_q = n_q;
   pp.n_kv = n_kv;
-  pp.inv_freq = inv_freq;
+  pp.rope_cs = rope_cs;
   pp.qimg = qimg;
   pp.kimg = kimg;
   pp.vimg = vimg;
   pp.k_caches = k_caches;
   pp.v_caches = v_caches;
   pp.t_max = t_max;
-  prefill_prep_kernel<<<dim3(S, n_seq), 256, 0, st>>>(pp);
+  prefill_prep_kernel<<<dim3(n_q + 2 * n_kv, S / kPT, n_seq), 256, 0, st>>>(pp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   PrefillAttnParams ap{};
@@ -493,7 +782,8 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
   ap.n_kv = n_kv;
   ap.scale_log2 = (1.0f / sqrtf((float)kHeadDim)) * 1.4426950408889634f;
   ap.status = status;
-  prefill_attn_kernel<<<dim3(S / kPT, n_q, n_seq), kPrefillThreads, prefill_smem_bytes(), st>>>(ap);
+  prefill_attn_kernel<<<dim3(n_q / 2, n_seq, S / kPT), kPrefillThreads, prefill_smem_bytes(),
+                        st>>>(ap);
   return cudaGetLastError();
 }
 
