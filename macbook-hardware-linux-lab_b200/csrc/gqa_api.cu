@@ -38,7 +38,7 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
                            int n_kv, const float2* rope_cs, __nv_bfloat16* qimg,
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
-                           cudaStream_t st);
+                           int n_sm, cudaStream_t st);
 }  // namespace gqa
 
 using namespace gqa;
@@ -818,7 +818,7 @@ int gqa_prefill_bf16(gqa_ctx* c, gqa_stream_t stream, int n_seq, int seq_len, co
   __nv_bfloat16* vimg = kimg + per * nkv;
   GQA_CUDA(launch_prefill(qkv, (long long)seq_len * (nq + 2 * nkv) * kHeadDim, n_seq, seq_len, nq,
                           nkv, c->rope_cs, qimg, kimg, vimg, k_caches, v_caches, c->cfg.t_max,
-                          out, c->status, st));
+                          out, c->status, c->n_sm, st));
   return GQA_OK;
 }
 

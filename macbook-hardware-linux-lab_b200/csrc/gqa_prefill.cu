@@ -202,11 +202,10 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Two non-negative finite floats to a bf16 pair (lo = a) with integer ops,
-// rounding to nearest (ties away from zero), so the conversion runs on the
-// integer pipe instead of the one ex2 uses.
-__device__ __forceinline__ uint32_t pack_bf16_pos(float a, float b) {
-  return __byte_perm(__float_as_uint(a) + 0x8000u, __float_as_uint(b) + 0x8000u, 0x7632);
+// Two floats to a bf16 pair (lo = a), round to nearest even.
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 b2 = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&b2);
 }
 
 __device__ __forceinline__ void named_barrier_sync(int id, int n_threads) {
@@ -232,37 +231,6 @@ __device__ __forceinline__ void fadd2(float& d0, float& d1, float a0, float a1, 
       : "=f"(d0), "=f"(d1)
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
-
-// 2^x for a pair on the FMA pipe, for x <= 2^22 (x below -125 is clamped;
-// 2^-125 is as good as 0 for a softmax weight).  Range reduction x = n + f,
-// n = round(x) taken from the low mantissa bits of x + 1.5 * 2^23, f in
-// [-1/2, 1/2]; 2^f by a degree-3 polynomial fitted to relative error on
-// [-1/2, 1/2] (Lawson's iteratively reweighted least squares, max relative
-// error 7.5e-5, far below the bf16 rounding of P); 2^n added to the exponent
-// field.  Generator: csrc/fit_exp2_poly.py.
-constexpr float kExp2C0 = 0.9999281167984009f;
-constexpr float kExp2C1 = 0.6932609677314758f;
-constexpr float kExp2C2 = 0.24261054396629333f;
-constexpr float kExp2C3 = 0.05517132207751274f;
-constexpr float kRoundShift = 12582912.0f;  // 1.5 * 2^23
-
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
-  x0 = fmaxf(x0, -125.f);
-  x1 = fmaxf(x1, -125.f);
-  float t0, t1, n0, n1, f0, f1, r0, r1;
-  fadd2(t0, t1, x0, x1, kRoundShift, kRoundShift);    // n in the low mantissa bits
-  fadd2(n0, n1, t0, t1, -kRoundShift, -kRoundShift);  // n = round(x)
-  ffma2(f0, f1, n0, n1, -1.f, -1.f, x0, x1);          // f = x - n (exact)
-  ffma2(r0, r1, kExp2C3, kExp2C3, f0, f1, kExp2C2, kExp2C2);
-  ffma2(r0, r1, r0, r1, f0, f1, kExp2C1, kExp2C1);
-  ffma2(r0, r1, r0, r1, f0, f1, kExp2C0, kExp2C0);
-  y0 = __uint_as_float(__float_as_uint(r0) + (__float_as_uint(t0) << 23));
-  y1 = __uint_as_float(__float_as_uint(r1) + (__float_as_uint(t1) << 23));
-}
-
-// Of every four key pairs, this many take exp2_poly2 and the rest the MUFU
-// ex2 (16 lanes per clock per SM), so the two pipes share the softmax work.
-constexpr int kPolyPairs = 1;
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -396,17 +364,22 @@ struct PrefillAttnParams {
   float* out;            // [n_seq][S][n_q * 128]
   int S;
   int n_q, n_kv;
+  int n_seq;
   float scale_log2;      // softmax scale * log2(e)
   int* status;
 };
 
-// One CTA serves two q heads of one KV group on the same 128-token query tile,
-// so every K / V^T tile it stages feeds two S = QK^T and two O += PV MMAs.
+// A work item is (128-token query tile, pair of q heads of one KV group,
+// sequence): both heads share every K / V^T tile the CTA stages, which feeds
+// two S = QK^T and two O += PV MMAs.  The kernel is persistent: one CTA per
+// SM walks a list of items, so the Q load of the next item and the output
+// stores of the last one overlap the MMAs.
 struct PrefillSmem {
   __nv_bfloat16 q[2][kImgElems];   // the two Q tiles (head 2h, 2h+1)
   __nv_bfloat16 k[2][kImgElems];   // K tile ring
   __nv_bfloat16 vt[2][kImgElems];  // V^T tile ring
-  uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2];
+  float stage[8][32 * 32];         // per softmax warp: 32 rows x 32 floats of output
+  uint64_t q_full[2], q_empty[2], k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full[2], p_full[2], o_final[2], drain;
   uint32_t tmem_base;
   int err;
@@ -457,6 +430,23 @@ __device__ __forceinline__ void umma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tme
       ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(kIdescBf16M128N128), "r"((uint32_t)acc));
 }
 
+// Items in decreasing causal length (query tile n_tiles-1 first).  Item k of
+// CTA b in round r is r * G + b for even r and r * G + (G - 1 - b) for odd r:
+// the snake evens out the per-CTA sum of causal lengths.
+struct PrefillItem {
+  int i, pair, seq;
+};
+
+__device__ __forceinline__ int prefill_item_index(int round, int b, int G) {
+  return round * G + ((round & 1) ? G - 1 - b : b);
+}
+
+__device__ __forceinline__ PrefillItem prefill_item(int k, int n_tiles, int n_pairs, int n_seq) {
+  const int per_tile = n_pairs * n_seq;
+  const int t = k / per_tile, rem = k % per_tile;
+  return PrefillItem{n_tiles - 1 - t, rem % n_pairs, rem / n_pairs};
+}
+
 // Tensor memory plan (512 columns, all 128 lanes): S of head g in columns
 // [128 g, 128 g + 128), O of head g in [256 + 128 g, 384 + 128 g).  P of head g
 // (bf16 pairs) overwrites the first 64 columns of its own S once the softmax
@@ -464,11 +454,16 @@ __device__ __forceinline__ void umma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tme
 // issued after the P.V MMA that reads it, and tcgen05.mma operations of one
 // thread execute in issue order.
 //
-// MMA issue order per key tile j (heads A = 0, B = 1):
-//   PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)
-// so the softmax of one head always overlaps two MMAs of the other.  The
-// commit that signals S_g(j+1) also covers PV_g(j): when the softmax thread of
-// head g sees S, its O row is final up to key tile j and may be rescaled.
+// The MMA warp walks the key tiles of all its items as one sequence t and
+// issues, per t (heads A = 0, B = 1):
+//   PV_A(t), S_A(t+1), PV_B(t), S_B(t+1)
+// where t+1 may be the first tile of the next item (other Q, other causal
+// range).  The softmax of one head thus always overlaps two MMAs of the other,
+// and the commit that signals S_g(t+1) also covers PV_g(t): when the softmax
+// thread sees S its O row is final up to tile t and may be rescaled.  The
+// next item's first P.V (which overwrites O with accumulate = 0) is issued
+// only after the softmax warps signalled that P, and they read O for the
+// epilogue before they produce it.
 __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const PrefillAttnParams p) {
   extern __shared__ unsigned char smem_raw[];
   // The swizzled operand images need 1 KB alignment.
@@ -476,18 +471,16 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_tiles = p.S / kPT;
-  // The query tile is the slowest grid dimension, longest causal tiles first,
-  // so the block scheduler hands out the heavy work before the light tail.
-  const int i = n_tiles - 1 - (int)blockIdx.z;
-  const int pair = blockIdx.x, seq = blockIdx.y;
-  const int hq0 = 2 * pair;
-  const int kvh = hq0 / (p.n_q / p.n_kv);
-  const int n_kv_tiles = i + 1;
+  const int n_pairs = p.n_q / 2;
+  const int n_items = n_tiles * n_pairs * p.n_seq;
+  const int G = gridDim.x, b = blockIdx.x;
+  const int group = p.n_q / p.n_kv;
   volatile int* err = &sm.err;
 
   if (tid == 0) {
-    mbar_init(&sm.q_full, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.q_full[s], 1);
+      mbar_init(&sm.q_empty[s], 1);
       mbar_init(&sm.k_full[s], 1);
       mbar_init(&sm.k_empty[s], 1);
       mbar_init(&sm.v_full[s], 1);
@@ -510,103 +503,149 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  const long long kv_base = (long long)(seq * p.n_kv + kvh) * n_tiles * kImgElems;
-
   if (warp == 8) {
     // ---- loader ----
     if (lane == 0) {
       const uint64_t policy = l2_policy_evict_first();
-      mbar_arrive_expect_tx(&sm.q_full, 2 * kImgBytes);
-      for (int g = 0; g < 2; ++g) {
-        const long long q_off = ((long long)(seq * p.n_q + hq0 + g) * n_tiles + i) * kImgElems;
-        bulk_copy_g2s(sm.q[g], p.qimg + q_off, kImgBytes, &sm.q_full, policy);
-      }
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < n_kv_tiles; ++j) {
-        const int st = j & 1;
-        const uint32_t reuse = ((j >> 1) - 1) & 1;
-        // K and V tiles are re-read by the other q heads of the group: keep them in L2.
-        if (j >= 2 && !wait_or_abort(&sm.k_empty[st], reuse, err)) break;
-        mbar_arrive_expect_tx(&sm.k_full[st], kImgBytes);
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-            ::"r"(smem_addr(sm.k[st])), "l"(p.kimg + kv_base + (long long)j * kImgElems),
-              "r"(kImgBytes), "r"(smem_addr(&sm.k_full[st])) : "memory");
-        ++k_issued;
-        if (j >= 2 && !wait_or_abort(&sm.v_empty[st], reuse, err)) break;
-        mbar_arrive_expect_tx(&sm.v_full[st], kImgBytes);
-        asm volatile(
-            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-            ::"r"(smem_addr(sm.vt[st])), "l"(p.vimg + kv_base + (long long)j * kImgElems),
-              "r"(kImgBytes), "r"(smem_addr(&sm.v_full[st])) : "memory");
-        ++v_issued;
+      int kv = 0, q_issued = 0, k_issued = 0, v_issued = 0;
+      bool ok = true;
+      for (int rd = 0; ok; ++rd) {
+        const int k = prefill_item_index(rd, b, G);
+        if (k >= n_items) break;
+        const PrefillItem it = prefill_item(k, n_tiles, n_pairs, p.n_seq);
+        const int kvh = (2 * it.pair) / group;
+        for (int g = 0; g < 2 && ok; ++g) {
+          if (rd > 0 && !wait_or_abort(&sm.q_empty[g], (rd - 1) & 1, err)) { ok = false; break; }
+          const long long q_off =
+              ((long long)(it.seq * p.n_q + 2 * it.pair + g) * n_tiles + it.i) * kImgElems;
+          mbar_arrive_expect_tx(&sm.q_full[g], kImgBytes);
+          bulk_copy_g2s(sm.q[g], p.qimg + q_off, kImgBytes, &sm.q_full[g], policy);
+          ++q_issued;
+        }
+        const long long kv_base = (long long)(it.seq * p.n_kv + kvh) * n_tiles * kImgElems;
+        for (int j = 0; j <= it.i && ok; ++j, ++kv) {
+          const int st = kv & 1;
+          const uint32_t reuse = ((kv >> 1) - 1) & 1;
+          // K and V tiles are re-read by the other q heads of the group: keep them in L2.
+          if (kv >= 2 && !wait_or_abort(&sm.k_empty[st], reuse, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&sm.k_full[st], kImgBytes);
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+              ::"r"(smem_addr(sm.k[st])), "l"(p.kimg + kv_base + (long long)j * kImgElems),
+                "r"(kImgBytes), "r"(smem_addr(&sm.k_full[st])) : "memory");
+          ++k_issued;
+          if (kv >= 2 && !wait_or_abort(&sm.v_empty[st], reuse, err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&sm.v_full[st], kImgBytes);
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+              ::"r"(smem_addr(sm.vt[st])), "l"(p.vimg + kv_base + (long long)j * kImgElems),
+                "r"(kImgBytes), "r"(smem_addr(&sm.v_full[st])) : "memory");
+          ++v_issued;
+        }
       }
       if (*err) {
         // Let the copies already issued land before the CTA's shared memory
         // can be handed to another CTA (copies always complete).
-        mbar_wait_bounded(&sm.q_full, 0, kPrefillWaitBudget);
-        for (int j = k_issued - 2; j < k_issued; ++j)
-          if (j >= 0) mbar_wait_bounded(&sm.k_full[j & 1], (j >> 1) & 1, kPrefillWaitBudget);
-        for (int j = v_issued - 2; j < v_issued; ++j)
-          if (j >= 0) mbar_wait_bounded(&sm.v_full[j & 1], (j >> 1) & 1, kPrefillWaitBudget);
+        for (int n = q_issued - 2; n < q_issued; ++n)
+          if (n >= 0) mbar_wait_bounded(&sm.q_full[n & 1], (n >> 1) & 1, kPrefillWaitBudget);
+        for (int n = k_issued - 2; n < k_issued; ++n)
+          if (n >= 0) mbar_wait_bounded(&sm.k_full[n & 1], (n >> 1) & 1, kPrefillWaitBudget);
+        for (int n = v_issued - 2; n < v_issued; ++n)
+          if (n >= 0) mbar_wait_bounded(&sm.v_full[n & 1], (n >> 1) & 1, kPrefillWaitBudget);
       }
     }
     __syncwarp();  // the other lanes wait here, so the warp reaches the block barrier converged
   } else if (warp == 9) {
     // ---- MMA issuer ----
     if (lane == 0) {
-      const uint32_t q_addr[2] = {smem_addr(sm.q[0]), smem_addr(sm.q[1])};
-      auto issue_s = [&](int g, int j) {
-        const uint32_t k_addr = smem_addr(sm.k[j & 1]);
+      auto issue_s = [&](int g, int kv) {
+        const uint32_t q_addr = smem_addr(sm.q[g]);
+        const uint32_t k_addr = smem_addr(sm.k[kv & 1]);
 #pragma unroll
         for (int ks = 0; ks < kHeadDim / 16; ++ks) {
           const uint32_t off = (ks >> 2) * (kKBlockElems * 2) + (ks & 3) * 32;
-          umma_bf16(tmem + 128 * g, umma_smem_desc(q_addr[g] + off),
+          umma_bf16(tmem + 128 * g, umma_smem_desc(q_addr + off),
                     umma_smem_desc(k_addr + off), ks > 0);
         }
         umma_commit(&sm.s_full[g]);
       };
-      auto issue_pv = [&](int g, int j) {
-        const uint32_t v_addr = smem_addr(sm.vt[j & 1]);
+      auto issue_pv = [&](int g, int kv, bool acc) {
+        const uint32_t v_addr = smem_addr(sm.vt[kv & 1]);
 #pragma unroll
         for (int ks = 0; ks < kPT / 16; ++ks) {
           const uint32_t off = (ks >> 2) * (kKBlockElems * 2) + (ks & 3) * 32;
           umma_bf16_tmem_a(tmem + 256 + 128 * g, tmem + 128 * g + ks * 8,
-                           umma_smem_desc(v_addr + off), j > 0 || ks > 0);
+                           umma_smem_desc(v_addr + off), acc || ks > 0);
         }
       };
-      bool ok = wait_or_abort(&sm.q_full, 0, err) && wait_or_abort(&sm.k_full[0], 0, err);
+      // Position in the flat tile sequence: item round rd, tile j of it, and
+      // the running K/V tile index kv.
+      int rd = 0, kv = 0;
+      int k = prefill_item_index(0, b, G);
+      bool ok = k < n_items;
+      PrefillItem it{};
       if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-        umma_commit(&sm.k_empty[0]);
-      }
-      for (int j = 0; ok && j < n_kv_tiles; ++j) {
-        const bool more = j + 1 < n_kv_tiles;
-        const int sn = (j + 1) & 1;
-        const uint32_t pn = ((j + 1) >> 1) & 1;
-        if (!wait_or_abort(&sm.p_full[0], j & 1, err) ||
-            !wait_or_abort(&sm.v_full[j & 1], (j >> 1) & 1, err)) { ok = false; break; }
-        tc_fence_after();
-        issue_pv(0, j);
-        if (more) {
-          if (!wait_or_abort(&sm.k_full[sn], pn, err)) { ok = false; break; }
+        it = prefill_item(k, n_tiles, n_pairs, p.n_seq);
+        ok = wait_or_abort(&sm.q_full[0], 0, err) && wait_or_abort(&sm.k_full[0], 0, err);
+        if (ok) {
           tc_fence_after();
-          issue_s(0, j + 1);
-        } else {
-          umma_commit(&sm.o_final[0]);
+          issue_s(0, 0);
+          if (it.i == 0) umma_commit(&sm.q_empty[0]);
+          ok = wait_or_abort(&sm.q_full[1], 0, err);
         }
-        if (!wait_or_abort(&sm.p_full[1], j & 1, err)) { ok = false; break; }
+        if (ok) {
+          tc_fence_after();
+          issue_s(1, 0);
+          if (it.i == 0) umma_commit(&sm.q_empty[1]);
+          umma_commit(&sm.k_empty[0]);
+        }
+      }
+      int j = 0;
+      while (ok) {
+        // the tile after (rd, j): same item, or the first tile of the next one
+        int rd_n = rd, j_n = j + 1;
+        PrefillItem it_n = it;
+        bool more = true;
+        if (j_n > it.i) {
+          rd_n = rd + 1;
+          j_n = 0;
+          const int kn = prefill_item_index(rd_n, b, G);
+          more = kn < n_items;
+          if (more) it_n = prefill_item(kn, n_tiles, n_pairs, p.n_seq);
+        }
+        const int kv_n = kv + 1;
+        const bool last_of_item = (j == it.i);
+        const bool n_last = more && (j_n == it_n.i);  // tile t+1 is the last of its item
+        if (!wait_or_abort(&sm.p_full[0], kv & 1, err) ||
+            !wait_or_abort(&sm.v_full[kv & 1], (kv >> 1) & 1, err)) { ok = false; break; }
         tc_fence_after();
-        issue_pv(1, j);
-        umma_commit(&sm.v_empty[j & 1]);
+        issue_pv(0, kv, j > 0);
+        if (last_of_item) umma_commit(&sm.o_final[0]);
         if (more) {
-          issue_s(1, j + 1);
-          umma_commit(&sm.k_empty[sn]);
-        } else {
-          umma_commit(&sm.o_final[1]);
+          if ((j_n == 0 && !wait_or_abort(&sm.q_full[0], rd_n & 1, err)) ||
+              !wait_or_abort(&sm.k_full[kv_n & 1], (kv_n >> 1) & 1, err)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(0, kv_n);
+          if (n_last) umma_commit(&sm.q_empty[0]);
         }
+        if (!wait_or_abort(&sm.p_full[1], kv & 1, err)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(1, kv, j > 0);
+        umma_commit(&sm.v_empty[kv & 1]);
+        if (last_of_item) umma_commit(&sm.o_final[1]);
+        if (more) {
+          if (j_n == 0 && !wait_or_abort(&sm.q_full[1], rd_n & 1, err)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(1, kv_n);
+          if (n_last) umma_commit(&sm.q_empty[1]);
+          umma_commit(&sm.k_empty[kv_n & 1]);
+        } else {
+          break;
+        }
+        rd = rd_n;
+        j = j_n;
+        it = it_n;
+        kv = kv_n;
       }
       // Whatever happened, no MMA may still be running when TMEM is freed.
       umma_commit(&sm.drain);
@@ -620,107 +659,115 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
     const uint32_t t_s = tmem + lane_off + 128 * g;
     const uint32_t t_o = tmem + lane_off + 256 + 128 * g;
     const float sc = p.scale_log2;
-    float m = -CUDART_INF_F, l = 0.f;
+    float* slice = sm.stage[warp];
+    int tc = 0;  // S tiles of this head so far (s_full / p_full parity)
     bool ok = true;
-    for (int j = 0; j < n_kv_tiles; ++j) {
-      // Waits are voted so the warp stays converged for the warp-collective
-      // tensor-memory loads and stores.
-      ok = __all_sync(0xffffffffu, wait_or_abort(&sm.s_full[g], j & 1, err));
+    for (int rd = 0; ok; ++rd) {
+      const int k = prefill_item_index(rd, b, G);
+      if (k >= n_items) break;
+      const PrefillItem it = prefill_item(k, n_tiles, n_pairs, p.n_seq);
+      float m = -CUDART_INF_F, l = 0.f;
+      for (int j = 0; j <= it.i; ++j, ++tc) {
+        // Waits are voted so the warp stays converged for the warp-collective
+        // tensor-memory loads and stores.
+        ok = __all_sync(0xffffffffu, wait_or_abort(&sm.s_full[g], tc & 1, err));
+        if (!ok) break;
+        tc_fence_after();
+        // Weights against the running reference max m.  The row max is taken
+        // only on the first tile of the item, or when the weights of this
+        // tile sum past 2^8 in some row of the warp (a score moved well above
+        // m; the sum also catches an overflow): then the S rows are loaded
+        // again, m moves to the row max, the tile is recomputed, and l and
+        // the O row are rescaled.  Otherwise no max pass is spent on the tile.
+        float alpha = 1.f, sum0 = 0.f, sum1 = 0.f;
+        uint32_t pk[kPT / 2];
+        bool fresh = (j == 0);
+#pragma unroll 1
+        for (int pass = 0; pass < 2; ++pass) {
+          float s[kPT];
+          tmem_ld128(t_s, s);
+          if (j == it.i) {
+#pragma unroll
+            for (int c = 0; c < kPT; ++c)
+              if (c > r) s[c] = -CUDART_INF_F;  // causal: keys after the query
+          }
+          if (fresh) {
+            float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+            for (int c = 4; c < kPT; c += 8) {
+              mx0 = fmax3(mx0, s[c], s[c + 1]);
+              mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
+              mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
+              mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
+            }
+            const float mn = fmaxf(m, fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sc);
+            if (j > 0) alpha = fast_exp2(m - mn);
+            m = mn;
+          }
+          const float nm = -m;
+          sum0 = 0.f;
+          sum1 = 0.f;
+#pragma unroll
+          for (int c = 0; c < kPT; c += 2) {
+            float x0, x1;
+            ffma2(x0, x1, s[c], s[c + 1], sc, sc, nm, nm);
+            const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+            fadd2(sum0, sum1, sum0, sum1, p0, p1);
+            pk[c / 2] = pack_bf16(p0, p1);
+          }
+          if (fresh || !__any_sync(0xffffffffu, !(sum0 + sum1 <= 256.f))) break;
+          fresh = true;
+        }
+        __syncwarp();
+        tmem_st64(t_s, pk);
+        l = l * alpha + (sum0 + sum1);
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            tmem_ld32(t_o + c * 32, v);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] *= alpha;
+            tmem_st32(t_o + c * 32, v);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_full[g]);
+      }
+      if (!ok) break;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&sm.o_final[g], rd & 1, err));
       if (!ok) break;
       tc_fence_after();
-      float s[kPT];
-      tmem_ld128(t_s, s);
-      if (j == i) {
-#pragma unroll
-        for (int c = 0; c < kPT; ++c)
-          if (c > r) s[c] = -CUDART_INF_F;  // causal: keys after the query
-      }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
-#pragma unroll
-      for (int c = 4; c < kPT; c += 8) {
-        mx0 = fmax3(mx0, s[c], s[c + 1]);
-        mx1 = fmax3(mx1, s[c + 2], s[c + 3]);
-        mx2 = fmax3(mx2, s[c + 4], s[c + 5]);
-        mx3 = fmax3(mx3, s[c + 6], s[c + 7]);
-      }
-      const float mt = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sc;
-      float alpha = 1.f;
-      if (j == 0 || mt > m + 8.0f) {  // lazy: move the reference max only by > 2^8
-        const float mn = fmaxf(m, mt);
-        if (j > 0) alpha = fast_exp2(m - mn);
-        m = mn;
-      }
-      const float nm = -m;
-      float sum0 = 0.f, sum1 = 0.f;
-      uint32_t pk[kPT / 2];
-#pragma unroll
-      for (int c = 0; c < kPT; c += 2) {
-        float x0, x1, p0, p1;
-        ffma2(x0, x1, s[c], s[c + 1], sc, sc, nm, nm);
-        if (((c >> 1) & 3) < kPolyPairs) {
-          exp2_poly2(x0, x1, p0, p1);
-        } else {
-          p0 = fast_exp2(x0);
-          p1 = fast_exp2(x1);
-        }
-        fadd2(sum0, sum1, sum0, sum1, p0, p1);
-        pk[c / 2] = pack_bf16_pos(p0, p1);
-      }
-      tmem_st64(t_s, pk);
-      l = l * alpha + (sum0 + sum1);
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(t_o + c * 32, v);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] *= alpha;
-          tmem_st32(t_o + c * 32, v);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sm.p_full[g]);
-    }
-    const bool fin = __all_sync(0xffffffffu, ok && wait_or_abort(&sm.o_final[g], 0, err));
-    float* stage = reinterpret_cast<float*>(g == 0 ? &sm.k[0][0] : &sm.q[0][0]);
-    if (fin) {
-      // Epilogue through shared memory: once o_final of head g fired, every
-      // S MMA has completed, so head 0 stages its O tile in the K ring and
-      // head 1 in the Q tiles (64 KB each).  Staging layout: four 16 KB
-      // column blocks of 128 rows x 32 floats, the 16-byte chunk k of row r
-      // at chunk k ^ (r % 8), so both the row-wise writes here and the
-      // chunk-wise reads below touch each bank once per 128 bytes.
-      tc_fence_after();
+      // The O row leaves tensor memory here, before this warp signals the
+      // next item's first P (whose P.V overwrites O).
+      float o[kPT];
+      tmem_ld128(t_o, o);
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
+      // Output through this warp's 4 KB slice, a quarter of the columns at a
+      // time: each lane writes 32 floats of its row (16-byte chunk c at
+      // c ^ (row % 8)), then the warp stores 4 rows x 128 B per instruction.
+      float* dst = p.out + ((long long)it.seq * p.S + (long long)it.i * kPT + (warp & 3) * 32) *
+                               p.n_q * kHeadDim +
+                   (long long)(2 * it.pair + g) * kHeadDim;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(t_o + c * 32, v);
-        float* row = stage + c * (kPT * 32) + r * 32;
+      for (int qc = 0; qc < 4; ++qc) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          *reinterpret_cast<float4*>(row + ((k ^ (r & 7)) << 2)) =
-              make_float4(v[4 * k] * inv_l, v[4 * k + 1] * inv_l, v[4 * k + 2] * inv_l,
-                          v[4 * k + 3] * inv_l);
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<float4*>(slice + lane * 32 + ((c ^ (lane & 7)) << 2)) =
+              make_float4(o[32 * qc + 4 * c] * inv_l, o[32 * qc + 4 * c + 1] * inv_l,
+                          o[32 * qc + 4 * c + 2] * inv_l, o[32 * qc + 4 * c + 3] * inv_l);
+        __syncwarp();
+#pragma unroll
+        for (int mr = 0; mr < 8; ++mr) {
+          const int rr = 4 * mr + (lane >> 3), ch = lane & 7;
+          *reinterpret_cast<float4*>(dst + (long long)rr * p.n_q * kHeadDim + 32 * qc + 4 * ch) =
+              *reinterpret_cast<const float4*>(slice + rr * 32 + ((ch ^ (rr & 7)) << 2));
+        }
+        __syncwarp();
       }
-    } else {
-      atomicOr(&sm.err, 1);
     }
-    // All 128 threads of the head reach this barrier on every path; a warp
-    // that failed raised err before it, so no thread copies unwritten rows.
-    named_barrier_sync(1 + g, 128);
-    if (*err == 0) {
-      // Coalesced copy-out: warp w writes rows 32w..32w+31, one 512-byte row
-      // per instruction (lane = 16-byte chunk of the row).
-      float* dst = p.out + ((long long)seq * p.S + (long long)i * kPT) * p.n_q * kHeadDim +
-                   (long long)(hq0 + g) * kHeadDim + lane * 4;
-      const float* src = stage + (lane >> 3) * (kPT * 32);
-#pragma unroll 4
-      for (int rr = (warp & 3) * 32; rr < (warp & 3) * 32 + 32; ++rr)
-        *reinterpret_cast<float4*>(dst + (long long)rr * p.n_q * kHeadDim) =
-            *reinterpret_cast<const float4*>(src + rr * 32 + (((lane & 7) ^ (rr & 7)) << 2));
-    }
+    if (!ok) atomicOr(&sm.err, 1);
   }
 
   // ---- teardown: the MMA warp drained its MMAs; free TMEM ----
@@ -755,7 +802,7 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
                            int n_kv, const float2* rope_cs, __nv_bfloat16* qimg,
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
-                           cudaStream_t st) {
+                           int n_sm, cudaStream_t st) {
   PrefillPrepParams pp{};
   pp.qkv = qkv;
   pp.seq_stride = seq_stride;
@@ -780,10 +827,12 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
   ap.S = S;
   ap.n_q = n_q;
   ap.n_kv = n_kv;
+  ap.n_seq = n_seq;
   ap.scale_log2 = (1.0f / sqrtf((float)kHeadDim)) * 1.4426950408889634f;
   ap.status = status;
-  prefill_attn_kernel<<<dim3(n_q / 2, n_seq, S / kPT), kPrefillThreads, prefill_smem_bytes(),
-                        st>>>(ap);
+  const long long n_items = (long long)(S / kPT) * (n_q / 2) * n_seq;
+  const int grid = (int)(n_items < n_sm ? n_items : n_sm);
+  prefill_attn_kernel<<<grid, kPrefillThreads, prefill_smem_bytes(), st>>>(ap);
   return cudaGetLastError();
 }
 
