@@ -38,7 +38,7 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
                            int n_kv, const float2* rope_cs, __nv_bfloat16* qimg,
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
-                           int n_sm, cudaStream_t st);
+                           int* sched, int n_sm, cudaStream_t st);
 }  // namespace gqa
 
 using namespace gqa;
@@ -68,7 +68,7 @@ struct gqa_ctx {
   // and ~1 us per dependent global round trip for the arrival counter and
   // the final merge).
   int cluster = 0;
-  int* counters = nullptr;  // [kMaxCounters] arrival counters, kept at zero
+  int* counters = nullptr;  // [kMaxCounters + 2] arrival / item counters, kept at zero
   __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
   size_t prefill_cap = 0;                // elements
   float2* rope_cs = nullptr;             // prefill RoPE table [rope_cap][64] (cos, sin)
@@ -122,6 +122,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 constexpr int kCluster = 8;             // CTAs per cluster in the cluster reduction
 constexpr int kMaxCounters = 1 << 16;   // (sequence, KV head) arrival counters
+// Two counters past the decode range: the prefill's dynamic item counter and
+// its CTA-done counter (both zero between launches).
+constexpr int kPrefillSchedSlot = kMaxCounters;
 
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
@@ -331,8 +334,8 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess) e = prepare_prefill_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->inv_freq, sizeof(float) * kHalf);
   if (e == cudaSuccess) e = cudaMalloc(&c->status, sizeof(int));
-  if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kMaxCounters);
-  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * kMaxCounters);
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * (kMaxCounters + 2));
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * (kMaxCounters + 2));
   if (e == cudaSuccess)
     e = cudaMemcpy(c->inv_freq, c->h_inv_freq, sizeof(float) * kHalf, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(int));
@@ -818,7 +821,7 @@ int gqa_prefill_bf16(gqa_ctx* c, gqa_stream_t stream, int n_seq, int seq_len, co
   __nv_bfloat16* vimg = kimg + per * nkv;
   GQA_CUDA(launch_prefill(qkv, (long long)seq_len * (nq + 2 * nkv) * kHeadDim, n_seq, seq_len, nq,
                           nkv, c->rope_cs, qimg, kimg, vimg, k_caches, v_caches, c->cfg.t_max,
-                          out, c->status, c->n_sm, st));
+                          out, c->status, c->counters + kPrefillSchedSlot, c->n_sm, st));
   return GQA_OK;
 }
 

@@ -29,6 +29,8 @@
 //
 // Every wait is bounded; on a timeout the CTA raises a status bit, drains
 // what it issued and frees its tensor memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <math_constants.h>
 
@@ -358,6 +360,9 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrefillPrepPara
 // Attention
 // ---------------------------------------------------------------------------
 struct PrefillAttnParams {
+  // out as a 2-D fp32 tensor (columns n_q * 128, rows n_seq * S), stored
+  // through 32 x 32 boxes with the 128-byte swizzle.
+  CUtensorMap out_map;
   const __nv_bfloat16* qimg;
   const __nv_bfloat16* kimg;
   const __nv_bfloat16* vimg;
@@ -367,6 +372,7 @@ struct PrefillAttnParams {
   int n_seq;
   float scale_log2;      // softmax scale * log2(e)
   int* status;
+  int* sched;            // [2] next item, CTAs done; zero between launches
 };
 
 // A work item is (128-token query tile, pair of q heads of one KV group,
@@ -379,6 +385,8 @@ struct PrefillSmem {
   __nv_bfloat16 k[2][kImgElems];   // K tile ring
   __nv_bfloat16 vt[2][kImgElems];  // V^T tile ring
   float stage[8][32 * 32];         // per softmax warp: 32 rows x 32 floats of output
+  int item_ring[4];                // item ids handed out by the loader (-1: none left)
+  uint64_t item_full[4], item_empty[4];
   uint64_t q_full[2], q_empty[2], k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full[2], p_full[2], o_final[2], drain;
   uint32_t tmem_base;
@@ -430,15 +438,23 @@ __device__ __forceinline__ void umma_bf16_tmem_a(uint32_t d_tmem, uint32_t a_tme
       ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(kIdescBf16M128N128), "r"((uint32_t)acc));
 }
 
-// Items in decreasing causal length (query tile n_tiles-1 first).  Item k of
-// CTA b in round r is r * G + b for even r and r * G + (G - 1 - b) for odd r:
-// the snake evens out the per-CTA sum of causal lengths.
+// Items are numbered in decreasing causal length (query tile n_tiles-1 first)
+// and handed out dynamically: the loader of a CTA takes the next number from a
+// global counter when it is ready for another item, so SMs that finish early
+// take more of the short tail items.  The loader publishes each number in a
+// 4-slot ring that the MMA thread and the eight softmax warps read in order.
 struct PrefillItem {
   int i, pair, seq;
 };
 
-__device__ __forceinline__ int prefill_item_index(int round, int b, int G) {
-  return round * G + ((round & 1) ? G - 1 - b : b);
+constexpr int kItemConsumers = 9;  // the MMA thread and one arrival per softmax warp
+
+// Number n of this CTA's item sequence (blocks until the loader published it);
+// -1 when none is left.  `ok` turns false on a timeout or another role's error.
+__device__ __forceinline__ int item_take(PrefillSmem& sm, int n, volatile int* err, bool& ok) {
+  const int slot = n & 3;
+  ok = wait_or_abort(&sm.item_full[slot], (n >> 2) & 1, err);
+  return ok ? *reinterpret_cast<volatile int*>(&sm.item_ring[slot]) : -1;
 }
 
 __device__ __forceinline__ PrefillItem prefill_item(int k, int n_tiles, int n_pairs, int n_seq) {
@@ -464,7 +480,8 @@ __device__ __forceinline__ PrefillItem prefill_item(int k, int n_tiles, int n_pa
 // next item's first P.V (which overwrites O with accumulate = 0) is issued
 // only after the softmax warps signalled that P, and they read O for the
 // epilogue before they produce it.
-__global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const PrefillAttnParams p) {
+__global__ void __launch_bounds__(kPrefillThreads, 1)
+    prefill_attn_kernel(const __grid_constant__ PrefillAttnParams p) {
   extern __shared__ unsigned char smem_raw[];
   // The swizzled operand images need 1 KB alignment.
   PrefillSmem& sm = *reinterpret_cast<PrefillSmem*>(
@@ -473,11 +490,14 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
   const int n_tiles = p.S / kPT;
   const int n_pairs = p.n_q / 2;
   const int n_items = n_tiles * n_pairs * p.n_seq;
-  const int G = gridDim.x, b = blockIdx.x;
   const int group = p.n_q / p.n_kv;
   volatile int* err = &sm.err;
 
   if (tid == 0) {
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(&sm.item_full[s], 1);
+      mbar_init(&sm.item_empty[s], kItemConsumers);
+    }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.q_full[s], 1);
       mbar_init(&sm.q_empty[s], 1);
@@ -510,8 +530,16 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
       int kv = 0, q_issued = 0, k_issued = 0, v_issued = 0;
       bool ok = true;
       for (int rd = 0; ok; ++rd) {
-        const int k = prefill_item_index(rd, b, G);
-        if (k >= n_items) break;
+        const int slot = rd & 3;
+        if (rd >= 4 && !wait_or_abort(&sm.item_empty[slot], ((rd >> 2) - 1) & 1, err)) {
+          ok = false;
+          break;
+        }
+        int k = atomicAdd(p.sched, 1);
+        if (k >= n_items) k = -1;
+        sm.item_ring[slot] = k;
+        mbar_arrive(&sm.item_full[slot]);  // release: the ring entry is visible to the waiters
+        if (k < 0) break;
         const PrefillItem it = prefill_item(k, n_tiles, n_pairs, p.n_seq);
         const int kvh = (2 * it.pair) / group;
         for (int g = 0; g < 2 && ok; ++g) {
@@ -581,8 +609,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
       // Position in the flat tile sequence: item round rd, tile j of it, and
       // the running K/V tile index kv.
       int rd = 0, kv = 0;
-      int k = prefill_item_index(0, b, G);
-      bool ok = k < n_items;
+      bool ok = true;
+      int k = item_take(sm, 0, err, ok);
+      if (ok) mbar_arrive(&sm.item_empty[0]);
+      ok = ok && k >= 0;
       PrefillItem it{};
       if (ok) {
         it = prefill_item(k, n_tiles, n_pairs, p.n_seq);
@@ -609,8 +639,10 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
         if (j_n > it.i) {
           rd_n = rd + 1;
           j_n = 0;
-          const int kn = prefill_item_index(rd_n, b, G);
-          more = kn < n_items;
+          const int kn = item_take(sm, rd_n, err, ok);
+          if (!ok) break;
+          mbar_arrive(&sm.item_empty[rd_n & 3]);
+          more = kn >= 0;
           if (more) it_n = prefill_item(kn, n_tiles, n_pairs, p.n_seq);
         }
         const int kv_n = kv + 1;
@@ -663,8 +695,12 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
     int tc = 0;  // S tiles of this head so far (s_full / p_full parity)
     bool ok = true;
     for (int rd = 0; ok; ++rd) {
-      const int k = prefill_item_index(rd, b, G);
-      if (k >= n_items) break;
+      int k = item_take(sm, rd, err, ok);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.item_empty[rd & 3]);
+      if (k < 0) break;
       const PrefillItem it = prefill_item(k, n_tiles, n_pairs, p.n_seq);
       float m = -CUDART_INF_F, l = 0.f;
       for (int j = 0; j <= it.i; ++j, ++tc) {
@@ -746,34 +782,50 @@ __global__ void __launch_bounds__(kPrefillThreads, 1) prefill_attn_kernel(const 
       const float inv_l = l > 0.f ? 1.f / l : 0.f;
       // Output through this warp's 4 KB slice, a quarter of the columns at a
       // time: each lane writes 32 floats of its row (16-byte chunk c at
-      // c ^ (row % 8)), then the warp stores 4 rows x 128 B per instruction.
-      float* dst = p.out + ((long long)it.seq * p.S + (long long)it.i * kPT + (warp & 3) * 32) *
-                               p.n_q * kHeadDim +
-                   (long long)(2 * it.pair + g) * kHeadDim;
+      // c ^ (row % 8), the 128-byte swizzle), then one lane hands the 32 x 32
+      // box to the tensor-store engine.  The slice is rewritten only after the
+      // previous store has read it.
+      const int x0 = (2 * it.pair + g) * kHeadDim;
+      const int y0 = it.seq * p.S + it.i * kPT + (warp & 3) * 32;
 #pragma unroll
       for (int qc = 0; qc < 4; ++qc) {
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        __syncwarp();
 #pragma unroll
         for (int c = 0; c < 8; ++c)
           *reinterpret_cast<float4*>(slice + lane * 32 + ((c ^ (lane & 7)) << 2)) =
               make_float4(o[32 * qc + 4 * c] * inv_l, o[32 * qc + 4 * c + 1] * inv_l,
                           o[32 * qc + 4 * c + 2] * inv_l, o[32 * qc + 4 * c + 3] * inv_l);
+        fence_proxy_async_smem();
         __syncwarp();
-#pragma unroll
-        for (int mr = 0; mr < 8; ++mr) {
-          const int rr = 4 * mr + (lane >> 3), ch = lane & 7;
-          *reinterpret_cast<float4*>(dst + (long long)rr * p.n_q * kHeadDim + 32 * qc + 4 * ch) =
-              *reinterpret_cast<const float4*>(slice + rr * 32 + ((ch ^ (rr & 7)) << 2));
+        if (lane == 0) {
+          asm volatile(
+              "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+              ::"l"(reinterpret_cast<uint64_t>(&p.out_map)), "r"(x0 + 32 * qc), "r"(y0),
+                "r"(smem_addr(slice)) : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
         }
-        __syncwarp();
       }
     }
+    // The CTA's shared memory must outlive the stores that read it.
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
     if (!ok) atomicOr(&sm.err, 1);
   }
 
   // ---- teardown: the MMA warp drained its MMAs; free TMEM ----
   tc_fence_before();
   __syncthreads();
-  if (sm.err && tid == 0) atomicOr(p.status, kStatusWaitTimeout);
+  if (tid == 0) {
+    if (sm.err) atomicOr(p.status, kStatusWaitTimeout);
+    // The last CTA out returns the item counter to zero for the next launch
+    // (every loader has taken its last number before its CTA gets here).
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
+      atomicExch(p.sched, 0);
+      atomicExch(p.sched + 1, 0);
+    }
+  }
   if (warp == 9) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
@@ -791,6 +843,19 @@ cudaError_t prepare_prefill_kernels() {
                               (int)prefill_smem_bytes());
 }
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }();
+  return fn;
+}
+
 cudaError_t launch_prefill_rope_table(const float* inv_freq, float2* cs, int n_pos,
                                       cudaStream_t st) {
   const int n = n_pos * kHalf;
@@ -802,7 +867,7 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
                            int n_kv, const float2* rope_cs, __nv_bfloat16* qimg,
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
-                           int n_sm, cudaStream_t st) {
+                           int* sched, int n_sm, cudaStream_t st) {
   PrefillPrepParams pp{};
   pp.qkv = qkv;
   pp.seq_stride = seq_stride;
@@ -820,6 +885,16 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   PrefillAttnParams ap{};
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {(cuuint64_t)n_q * kHeadDim, (cuuint64_t)n_seq * S};
+  const cuuint64_t strides[1] = {(cuuint64_t)n_q * kHeadDim * sizeof(float)};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  if (encode(&ap.out_map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
   ap.qimg = qimg;
   ap.kimg = kimg;
   ap.vimg = vimg;
@@ -830,6 +905,7 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
   ap.n_seq = n_seq;
   ap.scale_log2 = (1.0f / sqrtf((float)kHeadDim)) * 1.4426950408889634f;
   ap.status = status;
+  ap.sched = sched;
   const long long n_items = (long long)(S / kPT) * (n_q / 2) * n_seq;
   const int grid = (int)(n_items < n_sm ? n_items : n_sm);
   prefill_attn_kernel<<<grid, kPrefillThreads, prefill_smem_bytes(), st>>>(ap);
