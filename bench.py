@@ -631,7 +631,8 @@ def report_prefill(args, r, ctx, rank, world):
                          "unit": "TFLOP/s", "frac": round(tf / world / peak, 4),
                          "peak_source": src, "kernel": "prefill_attn_kernel (+ prep kernel)",
                          "algorithmic_flops_per_step": 4.0 * N_Q * D * 2048 * 2049 / 2 * 8,
-                         "traffic": None},
+                         "achieved_scope": "whole step (prep + attention kernels)",
+                         "traffic": profile_traffic("prefill")},
             "e2e": {"value": round(flops / t_e2e / 1e12, 1), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
             "gpu_launches": r["launches"], "clocks": r["clocks"], "cpu_baseline": None,
