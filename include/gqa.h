@@ -207,6 +207,36 @@ GQA_API int gqa_lse_combine(gqa_ctx *ctx, gqa_stream_t stream, int n_parts, int 
 GQA_API int gqa_lse_combine_packed(gqa_ctx *ctx, gqa_stream_t stream, int n_parts, int n_rows,
                                    const float *packed, long long part_stride, float *out);
 
+/* ---- KV-range split over several GPUs, merged through peer memory ------ */
+
+/* One GPU's member of a group of `world` GPUs (one process or thread each)
+ * that decode one sequence with its cache rows split in contiguous ranges.
+ * gqa_exchange_create allocates this GPU's inbox and writes its CUDA IPC
+ * handle (GQA_IPC_HANDLE_BYTES bytes) to ipc_handle; the caller gathers every
+ * rank's handle (in rank order) and passes the array to gqa_exchange_open,
+ * which maps the peers' inboxes (a handle equal to the caller's own maps to
+ * its own inbox).  The reference runs on one GPU and has no
+ * counterpart; the merge it extends is its split-K segment reduce
+ * (kernel_attention_gqa.cl:378-397). */
+#define GQA_IPC_HANDLE_BYTES 64
+typedef struct gqa_exchange gqa_exchange;
+GQA_API int gqa_exchange_create(gqa_ctx *ctx, int rank, int world, gqa_exchange **out,
+                                void *ipc_handle);
+GQA_API int gqa_exchange_open(gqa_exchange *x, const void *handles);
+GQA_API int gqa_exchange_destroy(gqa_exchange *x);
+
+/* gqa_decode_kv_shard followed by the cross-GPU merge in one kernel: every
+ * rank of the group calls it for the same step (same qkv row and pos) with
+ * its own range; each writes its merged (m, l, o) per q head into every
+ * rank's inbox over NVLink, waits (bounded, ~1 s) for the others', and
+ * writes the complete attention output [n_heads_q][128] to out.  All ranks
+ * must make the same sequence of calls; a peer that does not arrive sets the
+ * wait-timeout bit (2) of the device status word (gqa_device_status) and
+ * leaves out unwritten, and the group must then be destroyed. */
+GQA_API int gqa_decode_kv_shard_exchange(gqa_ctx *ctx, gqa_exchange *x, gqa_stream_t stream,
+                                         const gqa_layer_kv *kv, const float *qkv, int pos,
+                                         int shard_begin, int shard_rows, float *out);
+
 /* ---- prefill ---------------------------------------------------------- */
 
 /* Causal attention over whole prompts on the tensor cores (bf16 operands,

@@ -39,9 +39,32 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
                            int* sched, int n_sm, cudaStream_t st);
+size_t exchange_inbox_bytes(int world, int n_rows);
+size_t exchange_flag_bytes(int world, int n_rows);
+cudaError_t launch_exchange_combine(const CombineParams& local, float* const* inbox,
+                                    unsigned* const* flags, unsigned* epoch, int rank, int world,
+                                    float* out, int* status, cudaStream_t st, bool pdl);
 }  // namespace gqa
 
 using namespace gqa;
+
+constexpr int kMaxExchangeWorld = 64;
+
+// Peer-memory exchange group of one GPU (gqa_exchange_*).  The inbox and
+// its flags live in one allocation exported through CUDA IPC.
+struct gqa_exchange {
+  gqa_ctx* ctx = nullptr;  // compared, never dereferenced after creation
+  int device = 0;
+  int rank = 0, world = 1, n_rows = 0;
+  void* base = nullptr;                    // local inbox | flags
+  cudaIpcMemHandle_t own{};                // handle of base
+  size_t flags_offset = 0;
+  void* peer[kMaxExchangeWorld] = {};      // mapped peer allocations (self: base)
+  float** d_inbox = nullptr;               // device [world]
+  unsigned** d_flags = nullptr;            // device [world]
+  unsigned* epoch = nullptr;               // device [n_rows]
+  bool opened = false;
+};
 
 struct gqa_ctx {
   int device = 0;
@@ -276,6 +299,50 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
     if (rc != GQA_OK) return rc;
   }
   if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
+  return GQA_OK;
+}
+
+// Runs the split kernel of one KV shard (rows [shard_begin, shard_begin +
+// shard_rows) of the sequence, global position pos) and describes its
+// partials in *cp for a merge (cp->n_parts = 0 when the shard attends no row).
+int shard_partials(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv, int pos,
+                   int shard_begin, int shard_rows, CombineParams* cp) {
+  int rc = check_kv(c, kv);
+  if (rc != GQA_OK) return rc;
+  if (!qkv || !aligned16(qkv)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned qkv");
+  if (pos < 0 || shard_begin < 0 || shard_rows < 0 || shard_rows > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "pos %d / shard [%d, +%d) invalid (t_max %d)", pos,
+                shard_begin, shard_rows, c->cfg.t_max);
+  const int nq = c->cfg.n_heads_q;
+  // Rows of this shard that the new token attends: global [shard_begin, pos].
+  long long attended = (long long)pos + 1 - shard_begin;
+  if (attended > shard_rows) attended = shard_rows;
+  if (attended < 0) attended = 0;
+  const bool owns = pos >= shard_begin && pos < shard_begin + shard_rows;
+  *cp = CombineParams{};
+  int n_splits = 0;
+  if (attended > 0) {
+    n_splits = plan_splits_single(c, c->cfg.n_heads_kv, (int)attended);
+    rc = ensure_scratch(c, (long long)nq * n_splits, st);
+    if (rc != GQA_OK) return rc;
+    DecodeParams p = base_params(c);
+    p.k_base = kv->k_cache;
+    p.v_base = kv->v_cache;
+    p.qkv = qkv;
+    p.rope_override = 1;
+    p.rope_pos = pos;
+    p.skip_append = owns ? 0 : 1;
+    p.len.pos_imm = owns ? pos - shard_begin : 0;
+    p.len.seqlen_imm = (int)attended;
+    p.t_end = (int)attended;
+    p.n_splits = n_splits;
+    p.out = nullptr;  // partials only
+    GQA_CUDA(launch_decode_split(p, 1, true, st, c->pdl != 0, single_variant(c)));
+    *cp = combine_from_scratch(c, n_splits);
+  } else {
+    cp->rows_per_seq = nq;
+  }
+  cp->n_parts = n_splits;
   return GQA_OK;
 }
 
@@ -678,49 +745,109 @@ int gqa_decode_kv_shard(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
                         const float* qkv, int pos, int shard_begin, int shard_rows, float* m,
                         float* l, float* o) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
-  int rc = check_kv(c, kv);
-  if (rc != GQA_OK) return rc;
-  if (!qkv || !m || !l || !o || !aligned16(qkv))
-    return fail(GQA_ERR_INVALID_ARG, "null argument or unaligned qkv");
-  if (pos < 0 || shard_begin < 0 || shard_rows < 0 || shard_rows > c->cfg.t_max)
-    return fail(GQA_ERR_INVALID_ARG, "pos %d / shard [%d, +%d) invalid (t_max %d)", pos,
-                shard_begin, shard_rows, c->cfg.t_max);
+  if (!m || !l || !o) return fail(GQA_ERR_INVALID_ARG, "null argument");
   DeviceGuard g(c->device);
   cudaStream_t st = (cudaStream_t)stream;
-  const int nq = c->cfg.n_heads_q;
-  // Rows of this shard that the new token attends: global [shard_begin, pos].
-  long long attended = (long long)pos + 1 - shard_begin;
-  if (attended > shard_rows) attended = shard_rows;
-  if (attended < 0) attended = 0;
-  const bool owns = pos >= shard_begin && pos < shard_begin + shard_rows;
   CombineParams cp{};
-  int n_splits = 0;
-  if (attended > 0) {
-    n_splits = plan_splits_single(c, c->cfg.n_heads_kv, (int)attended);
-    rc = ensure_scratch(c, (long long)nq * n_splits, st);
-    if (rc != GQA_OK) return rc;
-    DecodeParams p = base_params(c);
-    p.k_base = kv->k_cache;
-    p.v_base = kv->v_cache;
-    p.qkv = qkv;
-    p.rope_override = 1;
-    p.rope_pos = pos;
-    p.skip_append = owns ? 0 : 1;
-    p.len.pos_imm = owns ? pos - shard_begin : 0;
-    p.len.seqlen_imm = (int)attended;
-    p.t_end = (int)attended;
-    p.n_splits = n_splits;
-    p.out = nullptr;  // partials only
-    GQA_CUDA(launch_decode_split(p, 1, true, st, c->pdl != 0, single_variant(c)));
-    cp = combine_from_scratch(c, n_splits);
-  } else {
-    cp.rows_per_seq = nq;
-  }
-  cp.n_parts = n_splits;
+  int rc = shard_partials(c, st, kv, qkv, pos, shard_begin, shard_rows, &cp);
+  if (rc != GQA_OK) return rc;
   cp.out = o;
   cp.out_m = m;
   cp.out_l = l;
   GQA_CUDA(launch_combine(cp, 1, st, true));
+  return GQA_OK;
+}
+
+int gqa_exchange_create(gqa_ctx* c, int rank, int world, gqa_exchange** out, void* ipc_handle) {
+  if (!c || !out || !ipc_handle) return fail(GQA_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (world < 1 || world > kMaxExchangeWorld || rank < 0 || rank >= world)
+    return fail(GQA_ERR_INVALID_ARG, "rank %d / world %d invalid (world <= %d)", rank, world,
+                kMaxExchangeWorld);
+  DeviceGuard g(c->device);
+  gqa_exchange* x = new gqa_exchange();
+  x->ctx = c;
+  x->device = c->device;
+  x->rank = rank;
+  x->world = world;
+  x->n_rows = c->cfg.n_heads_q;
+  x->flags_offset = (exchange_inbox_bytes(world, x->n_rows) + 255) & ~(size_t)255;
+  const size_t bytes = x->flags_offset + exchange_flag_bytes(world, x->n_rows);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaMalloc(&x->base, bytes);
+  if (e == cudaSuccess) e = cudaMemset(x->base, 0, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&x->epoch, sizeof(unsigned) * x->n_rows);
+  if (e == cudaSuccess) e = cudaMemset(x->epoch, 0, sizeof(unsigned) * x->n_rows);
+  if (e == cudaSuccess) e = cudaMalloc(&x->d_inbox, sizeof(float*) * world);
+  if (e == cudaSuccess) e = cudaMalloc(&x->d_flags, sizeof(unsigned*) * world);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, x->base);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    gqa_exchange_destroy(x);
+    return fail(GQA_ERR_CUDA, "gqa_exchange_create: %s", cudaGetErrorString(e));
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  x->own = h;
+  *out = x;
+  return GQA_OK;
+}
+
+int gqa_exchange_open(gqa_exchange* x, const void* handles) {
+  if (!x || !handles) return fail(GQA_ERR_INVALID_ARG, "null argument");
+  if (x->opened) return fail(GQA_ERR_INVALID_ARG, "exchange already opened");
+  DeviceGuard g(x->device);
+  float* inbox[kMaxExchangeWorld];
+  unsigned* flags[kMaxExchangeWorld];
+  for (int r = 0; r < x->world; ++r) {
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const char*>(handles) + (size_t)r * GQA_IPC_HANDLE_BYTES, sizeof(h));
+    if (r == x->rank || memcmp(&h, &x->own, sizeof(h)) == 0) {
+      // This process's own inbox (a handle cannot be opened by its exporter).
+      x->peer[r] = x->base;
+    } else {
+      cudaError_t e = cudaIpcOpenMemHandle(&x->peer[r], h, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        x->peer[r] = nullptr;
+        cudaGetLastError();
+        return fail(GQA_ERR_CUDA, "opening the inbox of rank %d: %s", r, cudaGetErrorString(e));
+      }
+    }
+    inbox[r] = static_cast<float*>(x->peer[r]);
+    flags[r] = reinterpret_cast<unsigned*>(static_cast<char*>(x->peer[r]) + x->flags_offset);
+  }
+  GQA_CUDA(cudaMemcpy(x->d_inbox, inbox, sizeof(float*) * x->world, cudaMemcpyHostToDevice));
+  GQA_CUDA(cudaMemcpy(x->d_flags, flags, sizeof(unsigned*) * x->world, cudaMemcpyHostToDevice));
+  x->opened = true;
+  return GQA_OK;
+}
+
+int gqa_decode_kv_shard_exchange(gqa_ctx* c, gqa_exchange* x, gqa_stream_t stream,
+                                 const gqa_layer_kv* kv, const float* qkv, int pos,
+                                 int shard_begin, int shard_rows, float* out) {
+  if (!c || !x || !out) return fail(GQA_ERR_INVALID_ARG, "null argument");
+  if (x->ctx != c || !x->opened)
+    return fail(GQA_ERR_INVALID_ARG, "exchange belongs to another context or is not opened");
+  if (!aligned16(out)) return fail(GQA_ERR_INVALID_ARG, "out must be 16-byte aligned");
+  DeviceGuard g(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  CombineParams cp{};
+  int rc = shard_partials(c, st, kv, qkv, pos, shard_begin, shard_rows, &cp);
+  if (rc != GQA_OK) return rc;
+  GQA_CUDA(launch_exchange_combine(cp, x->d_inbox, x->d_flags, x->epoch, x->rank, x->world, out,
+                                   c->status, st, true));
+  return GQA_OK;
+}
+
+int gqa_exchange_destroy(gqa_exchange* x) {
+  if (!x) return GQA_OK;
+  DeviceGuard g(x->device);
+  for (int r = 0; r < x->world; ++r)
+    if (x->peer[r] && x->peer[r] != x->base) cudaIpcCloseMemHandle(x->peer[r]);
+  if (x->d_inbox) cudaFree(x->d_inbox);
+  if (x->d_flags) cudaFree(x->d_flags);
+  if (x->epoch) cudaFree(x->epoch);
+  if (x->base) cudaFree(x->base);
+  delete x;
   return GQA_OK;
 }
 

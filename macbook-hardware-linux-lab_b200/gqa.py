@@ -93,6 +93,11 @@ _SIGNATURES = {
     "gqa_lse_combine": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
     "gqa_decode_kv_shard": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _i, _vp, _vp, _vp],
     "gqa_lse_combine_packed": [_vp, _vp, _i, _i, _vp, _ll, _vp],
+    "gqa_exchange_create": [_vp, _i, _i, ctypes.POINTER(_vp), _vp],
+    "gqa_exchange_open": [_vp, _vp],
+    "gqa_exchange_destroy": [_vp],
+    "gqa_decode_kv_shard_exchange": [_vp, _vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _i,
+                                     _vp],
     "gqa_prefill_bf16": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
     "gqa_fill_normal": [_vp, _vp, _vp, _ll, _ull, _ull, _ll],
     "gqa_inv_freq": [_vp, ctypes.POINTER(ctypes.c_float)],
@@ -187,6 +192,49 @@ class Graph:
     def destroy(self) -> None:
         if self._h:
             lib().gqa_graph_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+IPC_HANDLE_BYTES = 64
+
+
+class Exchange:
+    """This GPU's member of a group that decodes one sequence with its KV
+    rows split across GPUs and merges the partials through peer memory
+    (gqa_exchange_create / _open / gqa_decode_kv_shard_exchange).
+
+    `handle` (bytes) is this GPU's inbox handle; gather every rank's handle
+    in rank order and pass the list to open()."""
+
+    def __init__(self, ctx: "Context", rank: int, world: int):
+        h = _vp()
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        _check(lib().gqa_exchange_create(ctx._h, rank, world, ctypes.byref(h), buf))
+        self._h = h.value
+        self.ctx, self.rank, self.world = ctx, rank, world
+        self.handle = buf.raw
+
+    def open(self, handles) -> None:
+        blob = b"".join(bytes(x) for x in handles)
+        if len(blob) != self.world * IPC_HANDLE_BYTES:
+            raise ValueError("need one handle of IPC_HANDLE_BYTES per rank")
+        _check(lib().gqa_exchange_open(self._h, blob))
+
+    def step(self, kv, qkv, pos: int, shard_begin: int, shard_rows: int, out,
+             stream=None) -> None:
+        _check(lib().gqa_decode_kv_shard_exchange(self.ctx._h, self._h, _stream(stream),
+                                                  ctypes.byref(kv), _ptr(qkv), pos, shard_begin,
+                                                  shard_rows, _ptr(out)))
+
+    def destroy(self) -> None:
+        if getattr(self, "_h", None):
+            lib().gqa_exchange_destroy(self._h)
             self._h = None
 
     def __del__(self):

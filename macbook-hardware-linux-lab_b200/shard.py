@@ -10,9 +10,12 @@ module adds the two ways the decode step shards:
   collective;
 * by KV range -- one long sequence's cache rows are cut into contiguous
   ranges, one per GPU; each GPU produces a partial (m, l, o) per q head over
-  its rows (gqa_decode_kv_shard), the partials are all-gathered and merged
-  with a log-sum-exp combine (gqa_lse_combine_packed) -- the cross-GPU form of
-  the reference's split-K segment reduce (kernel_attention_gqa.cl:378-397).
+  its rows and the partials are merged with a log-sum-exp combine -- the
+  cross-GPU form of the reference's split-K segment reduce
+  (kernel_attention_gqa.cl:378-397).  KvShardExchangeDecoder does the
+  exchange and merge in one kernel over peer memory (NVLink stores and
+  flags); KvShardDecoder all-gathers the partials with the process group's
+  collective (NCCL) and merges them in a second kernel.
 """
 from __future__ import annotations
 
@@ -97,3 +100,35 @@ class KvShardDecoder:
                                  base + 8 * n)
         gathered = all_gather_partials(self.part, self.group)
         self.ctx.lse_combine_packed(gathered.shape[0], n, gathered, self.width, out)
+
+
+class KvShardExchangeDecoder:
+    """KvShardDecoder with the exchange done by the merging kernel itself:
+    each rank stores its merged partial into every rank's inbox over NVLink
+    and merges the world partials once their flags are up
+    (gqa_decode_kv_shard_exchange).  The process group is used once, to swap
+    the inbox handles; the data path uses no collective."""
+
+    def __init__(self, ctx, k_local, v_local, begin: int, rows: int, group=None):
+        import torch.distributed as dist
+        from .gqa import Exchange, kv_of
+        if dist.is_available() and dist.is_initialized():
+            rank, world = dist.get_rank(group), dist.get_world_size(group)
+        else:
+            rank, world = 0, 1
+        self.ctx, self.begin, self.rows = ctx, begin, rows
+        self.kv = kv_of(k_local, v_local)
+        self._keep = (k_local, v_local)
+        self.exchange = Exchange(ctx, rank, world)
+        handles = [self.exchange.handle]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, self.exchange.handle, group=group)
+        self.exchange.open(handles)
+
+    def step(self, qkv, pos: int, out, stream=None) -> None:
+        """qkv: the new token's [q|k|v] row (same on every rank); out: [n_q*128]."""
+        self.exchange.step(self.kv, qkv, pos, self.begin, self.rows, out, stream)
+
+    def close(self) -> None:
+        self.exchange.destroy()

@@ -2,7 +2,10 @@
 
 First on one GPU with the shards emulated (each shard's rows copied to its own
 cache, partials combined with gqa_lse_combine_packed), then across 2 GPUs
-with NCCL (skipped when fewer GPUs are visible)."""
+with NCCL, and the peer-memory exchange (gqa_decode_kv_shard_exchange): on
+one GPU as a group of one (several steps, both inbox parities), its bounded
+wait when a peer never arrives, and across 2 GPUs (skipped when fewer GPUs
+are visible)."""
 import datetime
 import os
 import socket
@@ -106,3 +109,113 @@ def test_kv_shards_over_two_gpus_nccl(pkg, orc, cuda):
     orc.layer_attention(rq, kc, vc, 8191, 8192)
     for r in range(2):
         assert nerr(res[r], rq[:1536]) <= TOL
+
+
+def _oracle_steps(pkg, orc, seed, t_max, positions):
+    """Oracle outputs for consecutive decode steps of one sequence, each step
+    appending its row (the same qkv row at each position)."""
+    qkv, kc, vc = pkg.seeded.decode_inputs(seed, t_max)
+    rk, rv, outs = kc.copy(), vc.copy(), []
+    for pos in positions:
+        rq = qkv.copy()
+        orc.layer_attention(rq, rk, rv, pos, pos + 1)
+        outs.append(rq[:1536].copy())
+    return qkv, kc, vc, outs
+
+
+def test_exchange_group_of_one_steps(pkg, orc, cuda):
+    torch = cuda
+    t_max, positions = 8192, [6000, 6001, 6002, 6003]
+    qkv, kc, vc, ref = _oracle_steps(pkg, orc, 31, t_max, positions)
+    with pkg.Context(t_max=t_max) as ctx:
+        k = torch.from_numpy(kc).cuda()
+        v = torch.from_numpy(vc).cuda()
+        dec = pkg.shard.KvShardExchangeDecoder(ctx, k, v, 0, t_max)
+        d_qkv = torch.from_numpy(qkv).cuda()
+        out = torch.empty(1536, device="cuda")
+        for pos, r in zip(positions, ref):
+            dec.step(d_qkv, pos, out)
+            torch.cuda.synchronize()
+            assert ctx.device_status() == 0
+            assert nerr(out.cpu().numpy(), r) <= TOL
+        dec.close()
+
+
+def test_exchange_absent_peer_times_out(pkg, cuda):
+    """A group of two whose second rank never runs: the kernel's wait for its
+    flag gives up after its budget (~1 s), raises the wait-timeout status bit
+    and leaves the output unwritten; the GPU stays usable."""
+    torch = cuda
+    t_max = 1024
+    qkv, kc, vc = pkg.seeded.decode_inputs(5, t_max)
+    with pkg.Context(t_max=t_max) as ctx:
+        x = pkg.gqa.Exchange(ctx, 0, 2)
+        x.open([x.handle, x.handle])  # the absent rank's inbox maps to our own
+        k = torch.from_numpy(kc).cuda()
+        v = torch.from_numpy(vc).cuda()
+        out = torch.full((1536,), 7.0, device="cuda")
+        x.step(pkg.kv_of(k, v), torch.from_numpy(qkv).cuda(), 700, 0, t_max, out)
+        torch.cuda.synchronize()
+        st = ctx.device_status()
+        assert st & pkg.gqa.STATUS_WAIT_TIMEOUT
+        assert bool((out == 7.0).all())
+        x.destroy()
+        # the context still works afterwards
+        out2 = torch.empty(1536, device="cuda")
+        ctx.layer_attention_out(pkg.kv_of(k, v), torch.from_numpy(qkv).cuda(), 700, 701, out2)
+        torch.cuda.synchronize()
+        assert ctx.device_status() == 0
+
+
+def _exchange_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    # gloo only swaps the inbox handles; the data path is the kernel's NVLink stores
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    import __graft_entry__
+    g = __graft_entry__.load_package()
+    t_max, positions = 8192, [8188, 8189, 8190, 8191]
+    qkv, kc, vc = g.seeded.decode_inputs(78, t_max)
+    b, n = g.shard.plan_kv_ranges(t_max, world)[rank]
+    outs = []
+    with g.Context(t_max=n, device=rank) as ctx:
+        k = torch.from_numpy(np.ascontiguousarray(kc[:, b:b + n])).cuda()
+        v = torch.from_numpy(np.ascontiguousarray(vc[:, b:b + n])).cuda()
+        dec = g.shard.KvShardExchangeDecoder(ctx, k, v, b, n)
+        d_qkv = torch.from_numpy(qkv).cuda()
+        out = torch.empty(1536, device="cuda")
+        for pos in positions:
+            dec.step(d_qkv, pos, out)
+            torch.cuda.synchronize()
+            outs.append(out.cpu().numpy().copy())
+        status = ctx.device_status()
+        dist.barrier()  # no rank unmaps its inbox while a peer may still write to it
+        dec.close()
+        q.put((rank, status, outs))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_kv_shards_over_two_gpus_exchange(pkg, orc, cuda):
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {r: (st, outs) for r, st, outs in (q.get(timeout=300) for _ in range(2))}
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    _, _, _, ref = _oracle_steps(pkg, orc, 78, 8192, [8188, 8189, 8190, 8191])
+    for r in range(2):
+        st, outs = res[r]
+        assert st == 0
+        for got, want in zip(outs, ref):
+            assert nerr(got, want) <= TOL
