@@ -246,7 +246,7 @@ def run_reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(name):
+def workload_config(name, exchange="peer"):
     if name == "resident28":
         return {"workload": "resident28: 28-layer resident decode attention, 1 sequence per GPU, "
                             "12 q / 2 KV heads, d=128, fp32 KV t_max=4096 per layer (235 MB), "
@@ -268,10 +268,13 @@ def workload_config(name):
                 "seqs": 8, "seq_len": 2048, "flops_per_step": "4*B*Hq*d*S*(S+1)/2",
                 "l2": "inputs 134 MB > L2; no flush", "parallelism": "sequence-sharded"}
     if name == "long1":
+        how = ("merged partials exchanged by one kernel over NVLink peer memory (IPC inboxes, "
+               "epoch flags) and LSE-combined" if exchange == "peer" else
+               "partials all-gathered (NCCL) and LSE-combined")
         return {"workload": "long1: one sequence, 32768 fp32 KV rows (67 MB per layer) split by "
-                            "KV range across the GPUs, partials all-gathered (NCCL) and "
-                            "LSE-combined every step", "seqs": 1, "t_max": 32768,
-                "l2": "KV > L2 at 1-2 GPUs; no flush", "parallelism": "kv-range split"}
+                            "KV range across the GPUs, " + how + " every step", "seqs": 1,
+                "t_max": 32768, "l2": "KV > L2 at 1-2 GPUs; no flush",
+                "parallelism": "kv-range split", "exchange": exchange}
     return {"workload": "single: one step, 12/2 heads, d=128, pos 511, seq_len 512",
             "l2": "1 MB KV fits in L2 (latency-bound)"}
 
@@ -448,7 +451,12 @@ def run_long1(args, g, ctx, rank, world, local):
     qkv = torch.empty(QKV_W, device="cuda")
     ctx.fill_normal(qkv, QKV_W, seed, g.seeded.QKV)
     out = torch.empty(OUT_W, device="cuda")
-    dec = g.shard.KvShardDecoder(ctx, k, v, b, n)
+    if args.exchange == "peer":
+        dec = g.shard.KvShardExchangeDecoder(ctx, k, v, b, n)
+        per_step = 2  # split kernel + exchange-merge kernel
+    else:
+        dec = g.shard.KvShardDecoder(ctx, k, v, b, n)
+        per_step = 3  # split + local merge + merge of the gathered partials (NCCL not counted)
     pos0 = T - window
     stream = torch.cuda.current_stream()
 
@@ -456,15 +464,34 @@ def run_long1(args, g, ctx, rank, world, local):
         pos = pos0 + i % window
         return ROW_BYTES * max(0, min(n, pos + 1 - b))
 
+    ctx.reserve(1, max(n, 1))  # split scratch for every position, before any capture
     for i in range(args.warmup):
         dec.step(qkv, pos0 + i % window, out)
     torch.cuda.synchronize()
+    graph = None
+    if args.exchange == "peer":
+        # One CUDA graph holds the window's steps (positions pos0 .. pos0+window-1); the
+        # exchange's step epoch lives on the device, so every replay is a new set of steps.
+        # The NCCL arm stays eager (its collective is issued from the host).
+        if args.steps % window:
+            raise SystemExit(f"long1 with the peer exchange times whole windows: --steps must be "
+                             f"a multiple of {window}")
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(window):
+                dec.step(qkv, pos0 + i, out)
+        graph.replay()
+        torch.cuda.synchronize()
     barrier(world)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         ev0.record(stream)
-        for i in range(args.steps):
-            dec.step(qkv, pos0 + i % window, out)
+        if graph is not None:
+            for _ in range(args.steps // window):
+                graph.replay()
+        else:
+            for i in range(args.steps):
+                dec.step(qkv, pos0 + i % window, out)
         ev1.record(stream)
         torch.cuda.synchronize()
     barrier(world)
@@ -483,10 +510,14 @@ def run_long1(args, g, ctx, rank, world, local):
     barrier(world)
     if ctx.device_status() != 0:
         raise RuntimeError("device status set")
+    if args.exchange == "peer":
+        barrier(world)  # no rank unmaps its inbox while a peer may still store into it
+        del graph
+        dec.close()
     return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3,
                 bytes=sum(my_bytes(i) for i in range(args.steps)), clocks=clk.summary(),
-                launches=2 * args.steps, launches_per_step=2, h2d=QKV_W * 4, d2h=OUT_W * 4,
-                tokens=args.steps / world, dominant_launches=args.steps)
+                launches=per_step * args.steps, launches_per_step=per_step, h2d=QKV_W * 4,
+                d2h=OUT_W * 4, tokens=args.steps / world, dominant_launches=args.steps)
 
 
 def run_prefill(args, g, ctx, rank, world, local):
@@ -579,7 +610,7 @@ def run_ours(args):
             "scaling": "weak" if args.workload in ("resident28", "single") else "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)",
-            "config": dict(workload_config(args.workload),
+            "config": dict(workload_config(args.workload, args.exchange),
                            kernel_variant="auto" if args.variant < 0 else args.variant,
                            target_ctas=args.target_ctas or None,
                            batch_chunk=args.batch_chunk or None),
@@ -657,6 +688,7 @@ def main():
     ap.add_argument("--variant", type=int, default=-1, help=argparse.SUPPRESS)
     ap.add_argument("--target-ctas", type=int, default=0, help=argparse.SUPPRESS)
     ap.add_argument("--batch-chunk", type=int, default=0, help=argparse.SUPPRESS)
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer", help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

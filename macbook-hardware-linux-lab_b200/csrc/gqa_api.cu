@@ -40,28 +40,25 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
                            float* const* v_caches, int t_max, float* out, int* status,
                            int* sched, int n_sm, cudaStream_t st);
 size_t exchange_inbox_bytes(int world, int n_rows);
-size_t exchange_flag_bytes(int world, int n_rows);
-cudaError_t launch_exchange_combine(const CombineParams& local, float* const* inbox,
-                                    unsigned* const* flags, unsigned* epoch, int rank, int world,
-                                    float* out, int* status, cudaStream_t st, bool pdl);
+cudaError_t launch_exchange_combine(const CombineParams& local, uint2* const* inbox,
+                                    unsigned* epoch, int rank, int world, float* out, int* status,
+                                    cudaStream_t st, bool pdl);
 }  // namespace gqa
 
 using namespace gqa;
 
 constexpr int kMaxExchangeWorld = 64;
 
-// Peer-memory exchange group of one GPU (gqa_exchange_*).  The inbox and
-// its flags live in one allocation exported through CUDA IPC.
+// Peer-memory exchange group of one GPU (gqa_exchange_*).  The inbox is one
+// allocation exported through CUDA IPC.
 struct gqa_exchange {
   gqa_ctx* ctx = nullptr;  // compared, never dereferenced after creation
   int device = 0;
   int rank = 0, world = 1, n_rows = 0;
-  void* base = nullptr;                    // local inbox | flags
+  void* base = nullptr;                    // local inbox
   cudaIpcMemHandle_t own{};                // handle of base
-  size_t flags_offset = 0;
   void* peer[kMaxExchangeWorld] = {};      // mapped peer allocations (self: base)
-  float** d_inbox = nullptr;               // device [world]
-  unsigned** d_flags = nullptr;            // device [world]
+  uint2** d_inbox = nullptr;               // device [world]
   unsigned* epoch = nullptr;               // device [n_rows]
   bool opened = false;
 };
@@ -771,15 +768,13 @@ int gqa_exchange_create(gqa_ctx* c, int rank, int world, gqa_exchange** out, voi
   x->rank = rank;
   x->world = world;
   x->n_rows = c->cfg.n_heads_q;
-  x->flags_offset = (exchange_inbox_bytes(world, x->n_rows) + 255) & ~(size_t)255;
-  const size_t bytes = x->flags_offset + exchange_flag_bytes(world, x->n_rows);
+  const size_t bytes = exchange_inbox_bytes(world, x->n_rows);
   cudaIpcMemHandle_t h;
   cudaError_t e = cudaMalloc(&x->base, bytes);
   if (e == cudaSuccess) e = cudaMemset(x->base, 0, bytes);
   if (e == cudaSuccess) e = cudaMalloc(&x->epoch, sizeof(unsigned) * x->n_rows);
   if (e == cudaSuccess) e = cudaMemset(x->epoch, 0, sizeof(unsigned) * x->n_rows);
-  if (e == cudaSuccess) e = cudaMalloc(&x->d_inbox, sizeof(float*) * world);
-  if (e == cudaSuccess) e = cudaMalloc(&x->d_flags, sizeof(unsigned*) * world);
+  if (e == cudaSuccess) e = cudaMalloc(&x->d_inbox, sizeof(uint2*) * world);
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, x->base);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
@@ -796,8 +791,7 @@ int gqa_exchange_open(gqa_exchange* x, const void* handles) {
   if (!x || !handles) return fail(GQA_ERR_INVALID_ARG, "null argument");
   if (x->opened) return fail(GQA_ERR_INVALID_ARG, "exchange already opened");
   DeviceGuard g(x->device);
-  float* inbox[kMaxExchangeWorld];
-  unsigned* flags[kMaxExchangeWorld];
+  uint2* inbox[kMaxExchangeWorld];
   for (int r = 0; r < x->world; ++r) {
     cudaIpcMemHandle_t h;
     memcpy(&h, static_cast<const char*>(handles) + (size_t)r * GQA_IPC_HANDLE_BYTES, sizeof(h));
@@ -812,11 +806,9 @@ int gqa_exchange_open(gqa_exchange* x, const void* handles) {
         return fail(GQA_ERR_CUDA, "opening the inbox of rank %d: %s", r, cudaGetErrorString(e));
       }
     }
-    inbox[r] = static_cast<float*>(x->peer[r]);
-    flags[r] = reinterpret_cast<unsigned*>(static_cast<char*>(x->peer[r]) + x->flags_offset);
+    inbox[r] = static_cast<uint2*>(x->peer[r]);
   }
-  GQA_CUDA(cudaMemcpy(x->d_inbox, inbox, sizeof(float*) * x->world, cudaMemcpyHostToDevice));
-  GQA_CUDA(cudaMemcpy(x->d_flags, flags, sizeof(unsigned*) * x->world, cudaMemcpyHostToDevice));
+  GQA_CUDA(cudaMemcpy(x->d_inbox, inbox, sizeof(uint2*) * x->world, cudaMemcpyHostToDevice));
   x->opened = true;
   return GQA_OK;
 }
@@ -833,8 +825,8 @@ int gqa_decode_kv_shard_exchange(gqa_ctx* c, gqa_exchange* x, gqa_stream_t strea
   CombineParams cp{};
   int rc = shard_partials(c, st, kv, qkv, pos, shard_begin, shard_rows, &cp);
   if (rc != GQA_OK) return rc;
-  GQA_CUDA(launch_exchange_combine(cp, x->d_inbox, x->d_flags, x->epoch, x->rank, x->world, out,
-                                   c->status, st, true));
+  GQA_CUDA(launch_exchange_combine(cp, x->d_inbox, x->epoch, x->rank, x->world, out, c->status,
+                                   st, true));
   return GQA_OK;
 }
 
@@ -844,7 +836,6 @@ int gqa_exchange_destroy(gqa_exchange* x) {
   for (int r = 0; r < x->world; ++r)
     if (x->peer[r] && x->peer[r] != x->base) cudaIpcCloseMemHandle(x->peer[r]);
   if (x->d_inbox) cudaFree(x->d_inbox);
-  if (x->d_flags) cudaFree(x->d_flags);
   if (x->epoch) cudaFree(x->epoch);
   if (x->base) cudaFree(x->base);
   delete x;

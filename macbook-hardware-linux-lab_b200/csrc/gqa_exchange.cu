@@ -7,10 +7,12 @@
 //   1. merges this GPU's split partials into one (m, l, o) for the head
 //      (the same log-sum-exp merge as combine_kernel);
 //   2. stores that triple straight into the inbox of every GPU of the group
-//      (peer memory mapped through CUDA IPC, plain stores over NVLink) and
-//      raises a per-(source, head) flag there with a system-scope release;
-//   3. waits (bounded) until every source's flag for this step is up in its
-//      own inbox, and merges the world triples into the head's output.
+//      (peer memory mapped through CUDA IPC, stores over NVLink), each value
+//      as one 8-byte word {value, step epoch};
+//   3. polls (bounded) its own inbox until every source's words carry this
+//      step's epoch, and merges the world triples into the head's output.
+// An aligned 8-byte store is never seen half-written, so a word whose epoch
+// is current holds its value: no fence and no separate flag is needed.
 // This is the reference's split-K segment reduce (kernel_attention_gqa.cl:
 // 378-397) stretched over several GPUs, with the all-gather done by the
 // merging kernel itself instead of a collective library call.
@@ -18,7 +20,7 @@
 // Steps are told apart by a per-head epoch kept on the device (so graph
 // replays advance it); inbox slots alternate by epoch parity.  A GPU cannot
 // run two steps ahead of a peer: its step e+1 waits for the peer's step-e+1
-// flags, which the peer raises only after its step-e kernel (and every read
+// words, which the peer stores only after its step-e kernel (and every read
 // of the slots it reuses) has finished.
 #include "gqa_common.cuh"
 
@@ -26,36 +28,49 @@
 
 namespace gqa {
 
-constexpr int kExSlot = 132;        // floats per (source, head) slot: m, l, o[128], pad to 16 B
+constexpr int kExSlot = 130;        // 8-byte words per (source, head) slot: m, l, o[128]
 constexpr int kExGroups = 4;        // local merge: groups of 128 threads over the split parts
 constexpr int kExBatch = 16;        // parts loaded per group before any is used
 constexpr long long kExWaitBudget = 2000000000LL;  // ~1 s of SM clocks
 
 struct ExchangeParams {
   CombineParams local;          // this GPU's split partials (n_parts may be 0)
-  float* const* inbox;          // [world] -> that GPU's slots [2][world][n_rows][kExSlot]
-  unsigned* const* flags;       // [world] -> that GPU's flags [2][world][n_rows]
+  uint2* const* inbox;          // [world] -> that GPU's slots [2][world][n_rows][kExSlot]
   unsigned* epoch;              // [n_rows] steps done by this GPU, per head
   int rank, world;
   float* out;                   // [n_rows][128]
   int* status;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// One word {value, epoch}, stored and loaded whole at system scope.
+__device__ __forceinline__ void st_word(uint2* p, float v, unsigned e) {
+  asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)),
+               "r"(e) : "memory");
 }
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint2 ld_word(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p)
+               : "memory");
   return v;
+}
+
+// Value of word p once its epoch reaches e; false if that takes past deadline.
+__device__ __forceinline__ bool wait_word(const uint2* p, unsigned e, long long deadline,
+                                          float& v) {
+  uint2 w = ld_word(p);
+  while ((int)(w.y - e) < 0) {
+    if (clock64() > deadline) return false;
+    w = ld_word(p);
+  }
+  v = __uint_as_float(w.x);
+  return true;
 }
 
 __global__ void __launch_bounds__(kHeadDim * kExGroups) exchange_combine_kernel(
     const ExchangeParams x) {
   __shared__ float s_o[kExGroups][kHeadDim];
   __shared__ float s_m[kExGroups], s_l[kExGroups];
-  __shared__ int s_ok;
   const CombineParams& c = x.local;
   const int h = blockIdx.x, n_rows = c.rows_per_seq;
   const int d = threadIdx.x % kHeadDim, g = threadIdx.x / kHeadDim;
@@ -95,7 +110,6 @@ __global__ void __launch_bounds__(kHeadDim * kExGroups) exchange_combine_kernel(
     s_m[g] = M;
     s_l[g] = L;
   }
-  if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
 
   const unsigned e = x.epoch[h] + 1u;  // only this CTA advances epoch[h]
@@ -117,83 +131,61 @@ __global__ void __launch_bounds__(kHeadDim * kExGroups) exchange_combine_kernel(
     }
     const long long slot = ((long long)(par * x.world + x.rank) * n_rows + h) * kExSlot;
     for (int dst = 0; dst < x.world; ++dst) {
-      float* p = x.inbox[dst] + slot;
-      p[2 + d] = Ot;
+      uint2* p = x.inbox[dst] + slot;
+      st_word(p + 2 + d, Ot, e);
       if (d == 0) {
-        p[0] = Mt;
-        p[1] = Lt;
+        st_word(p, Mt, e);
+        st_word(p + 1, Lt, e);
       }
     }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int dst = 0; dst < x.world; ++dst)
-      st_release_sys(x.flags[dst] + (par * x.world + x.rank) * n_rows + h, e);
   }
 
-  // ---- 3. wait for every source's triple of this step (thread = source) ----
-  if (threadIdx.x < x.world) {
-    const unsigned* f = x.flags[x.rank] + (par * x.world + threadIdx.x) * n_rows + h;
-    if ((int)(ld_acquire_sys(f) - e) < 0) {
-      const long long start = clock64();
-      while ((int)(ld_acquire_sys(f) - e) < 0) {
-        if (clock64() - start > kExWaitBudget) {
-          s_ok = 0;
-          break;
-        }
+  // ---- 3./4. wait for every source's words of this step and merge them ----
+  bool ok = true;
+  float Ow = 0.f, Lw = 0.f;
+  if (g == 0) {
+    const uint2* base = x.inbox[x.rank] + (long long)par * x.world * n_rows * kExSlot +
+                        (long long)h * kExSlot;
+    const long long src_stride = (long long)n_rows * kExSlot;
+    const long long deadline = clock64() + kExWaitBudget;
+    float Mw = -CUDART_INF_F;
+    for (int s = 0; s < x.world && ok; ++s) {
+      float ms, ls;
+      ok = wait_word(base + s * src_stride, e, deadline, ms) &&
+           wait_word(base + s * src_stride + 1, e, deadline, ls);
+      if (ok && ls > 0.f) Mw = fmaxf(Mw, ms);
+    }
+    for (int s = 0; s < x.world && ok; ++s) {
+      float ms, ls, os;
+      ok = wait_word(base + s * src_stride, e, deadline, ms) &&
+           wait_word(base + s * src_stride + 1, e, deadline, ls) &&
+           wait_word(base + s * src_stride + 2 + d, e, deadline, os);
+      if (ok && ls > 0.f) {
+        const float w = expf(ms - Mw);
+        Lw += w * ls;
+        Ow += w * os;
       }
     }
   }
-  __syncthreads();
-  if (!s_ok) {
+  if (!__syncthreads_and(ok)) {
     // A peer did not arrive: report it, leave out and epoch untouched.
     if (threadIdx.x == 0) atomicOr(x.status, kStatusWaitTimeout);
     return;
   }
-
-  // ---- 4. merge the world triples from this GPU's inbox ----
-  if (g == 0) {
-    const float* base = x.inbox[x.rank] + (long long)par * x.world * n_rows * kExSlot +
-                        (long long)h * kExSlot;
-    const long long src_stride = (long long)n_rows * kExSlot;
-    float Mw = -CUDART_INF_F;
-    for (int s = 0; s < x.world; ++s) {
-      const float ls = __ldcg(base + s * src_stride + 1);
-      if (ls > 0.f) Mw = fmaxf(Mw, __ldcg(base + s * src_stride));
-    }
-    float Lw = 0.f, Ow = 0.f;
-    if (Mw != -CUDART_INF_F) {
-      for (int s = 0; s < x.world; ++s) {
-        const float* p = base + s * src_stride;
-        const float ls = __ldcg(p + 1);
-        if (ls > 0.f) {
-          const float w = expf(__ldcg(p) - Mw);
-          Lw += w * ls;
-          Ow += w * __ldcg(p + 2 + d);
-        }
-      }
-    }
-    x.out[(long long)h * kHeadDim + d] = Lw > 0.f ? Ow / Lw : 0.f;
-  }
+  if (g == 0) x.out[(long long)h * kHeadDim + d] = Lw > 0.f ? Ow / Lw : 0.f;
   if (threadIdx.x == 0) x.epoch[h] = e;
 }
 
 size_t exchange_inbox_bytes(int world, int n_rows) {
-  return sizeof(float) * 2ull * world * n_rows * kExSlot;
+  return sizeof(uint2) * 2ull * world * n_rows * kExSlot;
 }
 
-size_t exchange_flag_bytes(int world, int n_rows) {
-  return sizeof(unsigned) * 2ull * world * n_rows;
-}
-
-cudaError_t launch_exchange_combine(const CombineParams& local, float* const* inbox,
-                                    unsigned* const* flags, unsigned* epoch, int rank, int world,
-                                    float* out, int* status, cudaStream_t st, bool pdl) {
+cudaError_t launch_exchange_combine(const CombineParams& local, uint2* const* inbox,
+                                    unsigned* epoch, int rank, int world, float* out, int* status,
+                                    cudaStream_t st, bool pdl) {
   ExchangeParams x{};
   x.local = local;
   x.inbox = inbox;
-  x.flags = flags;
   x.epoch = epoch;
   x.rank = rank;
   x.world = world;
