@@ -14,6 +14,7 @@
 
 #include "gqa.h"
 #include "gqa_common.cuh"
+#include "gqa_merge.cuh"
 
 namespace gqa {
 size_t decode_smem_bytes();
@@ -47,7 +48,7 @@ cudaError_t launch_exchange_combine(const CombineParams& local, uint2* const* in
 
 using namespace gqa;
 
-constexpr int kMaxExchangeWorld = 64;
+constexpr int kMaxExchangeWorld = 32;  // = kExMaxWorld of the exchange kernel
 
 // Peer-memory exchange group of one GPU (gqa_exchange_*).  The inbox is one
 // allocation exported through CUDA IPC.
@@ -193,12 +194,15 @@ int plan_splits_single(const gqa_ctx* c, int rows_kv, int len) {
   int want = ceil_div(target, rows_kv);
   const int most = ceil_div(len, decode_variant_quant(single_variant(c)));
   if (want > most) want = most;
+  if (want > kMergeMaxParts) want = kMergeMaxParts;  // the merge's weight table
   return want < 1 ? 1 : want;
 }
 
 int batch_chunk(const gqa_ctx* c, int max_len) {
   const int q = decode_variant_quant(batch_variant(c));
-  const int want = c->batch_chunk > 0 ? c->batch_chunk : (max_len > 8192 ? 1024 : 256);
+  int want = c->batch_chunk > 0 ? c->batch_chunk : (max_len > 8192 ? 1024 : 256);
+  const int least = ceil_div(max_len, kMergeMaxParts);  // at most kMergeMaxParts splits
+  if (want < least) want = least;
   return ((want + q - 1) / q) * q;
 }
 

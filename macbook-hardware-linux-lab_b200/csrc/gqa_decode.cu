@@ -23,6 +23,7 @@
 // more than 2^8), p is staged through a 256-byte per-warp buffer and PV
 // accumulates o[6][4] per lane.  Warps are merged in shared memory at the end.
 #include "gqa_common.cuh"
+#include "gqa_merge.cuh"
 
 #include <math_constants.h>
 
@@ -138,18 +139,6 @@ struct Bfly {
     return (lane & ((1 << kLowBits) - 1)) == 0;
   }
 };
-
-__device__ __forceinline__ float warp_max(float x) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
-  return x;
-}
-
-__device__ __forceinline__ float warp_sum(float x) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-  return x;
-}
 
 // CTAs per SM the register budget is sized for: as many as the shared memory
 // footprint (two K/V rings of NW x NS x ST rows) lets reside, but never so
@@ -691,18 +680,10 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   if constexpr (CLUSTER) cluster_epilogue<NT>(p, sm.q, sm.hm, sm.hl, seq, hkv);
 }
 
-// Log-sum-exp merge of n_parts partials per output row.  One CTA per row:
-// kCombGroups groups of 128 threads (one per head dim) take interleaved
-// subsets of the parts, each issuing all of a batch's m, l and o loads before
-// using any of them (one L2 round trip per batch of kCombBatch parts per
-// group), then the groups are merged in shared memory.  Parts with l == 0
-// carry no weight; their o is selected away, never multiplied.
-constexpr int kCombGroups = 4;
-constexpr int kCombBatch = 16;
-
-__global__ void __launch_bounds__(kHeadDim * kCombGroups) combine_kernel(const CombineParams c) {
-  __shared__ float s_o[kCombGroups][kHeadDim];
-  __shared__ float s_m[kCombGroups], s_l[kCombGroups];
+// Log-sum-exp merge of n_parts partials per output row (merge_partials in
+// gqa_merge.cuh): one CTA of kMergeGroups x 128 threads per row.
+__global__ void __launch_bounds__(kHeadDim * kMergeGroups) combine_kernel(const CombineParams c) {
+  __shared__ MergeSmem sm;
   const int h = blockIdx.x, seq = blockIdx.y;
   const int d = threadIdx.x % kHeadDim, g = threadIdx.x / kHeadDim;
   const long long r = (long long)seq * c.rows_per_seq + h;
@@ -711,62 +692,18 @@ __global__ void __launch_bounds__(kHeadDim * kCombGroups) combine_kernel(const C
   // this grid touches.
   pdl_launch_dependents();
   pdl_wait();
-
-  float M = -CUDART_INF_F, L = 0.f, O = 0.f;
-  for (int i0 = g; i0 < c.n_parts; i0 += kCombGroups * kCombBatch) {
-    float mv[kCombBatch], lv[kCombBatch], ov[kCombBatch];
-#pragma unroll
-    for (int u = 0; u < kCombBatch; ++u) {
-      const int i = i0 + u * kCombGroups;
-      const bool ok = i < c.n_parts;
-      mv[u] = ok ? __ldcg(c.m + i * c.ml_part_stride + r * c.ml_row_stride) : -CUDART_INF_F;
-      lv[u] = ok ? __ldcg(c.l + i * c.ml_part_stride + r * c.ml_row_stride) : 0.f;
-      ov[u] = ok ? __ldcg(c.o + i * c.o_part_stride + r * c.o_row_stride + d) : 0.f;
-    }
-    float bm = M;
-#pragma unroll
-    for (int u = 0; u < kCombBatch; ++u)
-      if (lv[u] > 0.f) bm = fmaxf(bm, mv[u]);
-    if (bm == -CUDART_INF_F) continue;
-    const float sc = (M == -CUDART_INF_F) ? 0.f : expf(M - bm);
-    L *= sc;
-    O *= sc;
-#pragma unroll
-    for (int u = 0; u < kCombBatch; ++u) {
-      const float w = lv[u] > 0.f ? expf(mv[u] - bm) : 0.f;
-      L += w * lv[u];
-      O += (w != 0.f) ? w * ov[u] : 0.f;
-    }
-    M = bm;
-  }
-  s_o[g][d] = O;
-  if (d == 0) {
-    s_m[g] = M;
-    s_l[g] = L;
-  }
-  __syncthreads();
+  float M, L, O;
+  merge_partials(c, r, sm, M, L, O);
   if (g != 0) return;
-  float Mt = -CUDART_INF_F;
-#pragma unroll
-  for (int k = 0; k < kCombGroups; ++k) Mt = fmaxf(Mt, s_m[k]);
-  float Lt = 0.f, Ot = 0.f;
-  if (Mt != -CUDART_INF_F) {
-#pragma unroll
-    for (int k = 0; k < kCombGroups; ++k) {
-      const float w = (s_m[k] == -CUDART_INF_F) ? 0.f : expf(s_m[k] - Mt);
-      Lt += w * s_l[k];
-      Ot += (w != 0.f) ? w * s_o[k][d] : 0.f;
-    }
-  }
   float* dst = c.out + (long long)seq * c.out_stride + (long long)h * kHeadDim;
   if (c.out_m) {
-    dst[d] = Ot;
+    dst[d] = O;
     if (d == 0) {
-      c.out_m[r] = Mt;
-      c.out_l[r] = Lt;
+      c.out_m[r] = M;
+      c.out_l[r] = L;
     }
   } else {
-    dst[d] = Lt > 0.f ? Ot / Lt : 0.f;
+    dst[d] = L > 0.f ? O / L : 0.f;
   }
 }
 
@@ -953,7 +890,7 @@ cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, b
   dim3 grid(c.rows_per_seq, n_seq);
   CombineParams copy = c;
   void* args[] = {&copy};
-  return launch_ex((const void*)combine_kernel, grid, dim3(kHeadDim * kCombGroups), 0, st, pdl,
+  return launch_ex((const void*)combine_kernel, grid, dim3(kHeadDim * kMergeGroups), 0, st, pdl,
                    args);
 }
 

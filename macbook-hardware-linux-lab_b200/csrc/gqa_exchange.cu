@@ -5,7 +5,7 @@
 // Each GPU runs the split kernel over its range (gqa_decode.cu), then this
 // kernel, one CTA per q head:
 //   1. merges this GPU's split partials into one (m, l, o) for the head
-//      (the same log-sum-exp merge as combine_kernel);
+//      (merge_partials, as in combine_kernel);
 //   2. stores that triple straight into the inbox of every GPU of the group
 //      (peer memory mapped through CUDA IPC, stores over NVLink), each value
 //      as one 8-byte word {value, step epoch};
@@ -23,15 +23,17 @@
 // words, which the peer stores only after its step-e kernel (and every read
 // of the slots it reuses) has finished.
 #include "gqa_common.cuh"
+#include "gqa_merge.cuh"
 
 #include <math_constants.h>
 
 namespace gqa {
 
 constexpr int kExSlot = 130;        // 8-byte words per (source, head) slot: m, l, o[128]
-constexpr int kExGroups = 4;        // local merge: groups of 128 threads over the split parts
-constexpr int kExBatch = 16;        // parts loaded per group before any is used
+constexpr int kExGroups = kMergeGroups;  // groups of 128 threads
 constexpr long long kExWaitBudget = 2000000000LL;  // ~1 s of SM clocks
+constexpr int kExMaxWorld = 32;
+constexpr int kExPerGroup = kExMaxWorld / kExGroups;  // sources gathered by one group
 
 struct ExchangeParams {
   CombineParams local;          // this GPU's split partials (n_parts may be 0)
@@ -55,22 +57,23 @@ __device__ __forceinline__ uint2 ld_word(const uint2* p) {
   return v;
 }
 
-// Value of word p once its epoch reaches e; false if that takes past deadline.
-__device__ __forceinline__ bool wait_word(const uint2* p, unsigned e, long long deadline,
-                                          float& v) {
-  uint2 w = ld_word(p);
+// Reloads word w from p until its epoch reaches e; false if that takes past
+// the deadline.
+__device__ __forceinline__ bool settle_word(const uint2* p, unsigned e, long long deadline,
+                                            uint2& w) {
   while ((int)(w.y - e) < 0) {
     if (clock64() > deadline) return false;
     w = ld_word(p);
   }
-  v = __uint_as_float(w.x);
   return true;
 }
 
 __global__ void __launch_bounds__(kHeadDim * kExGroups) exchange_combine_kernel(
     const ExchangeParams x) {
+  __shared__ MergeSmem sm;
   __shared__ float s_o[kExGroups][kHeadDim];
   __shared__ float s_m[kExGroups], s_l[kExGroups];
+  __shared__ float s_wm[kExMaxWorld], s_wl[kExMaxWorld];  // every source's m and l
   const CombineParams& c = x.local;
   const int h = blockIdx.x, n_rows = c.rows_per_seq;
   const int d = threadIdx.x % kHeadDim, g = threadIdx.x / kHeadDim;
@@ -78,57 +81,14 @@ __global__ void __launch_bounds__(kHeadDim * kExGroups) exchange_combine_kernel(
   pdl_wait();
 
   // ---- 1. merge this GPU's split partials (m in natural-log units) ----
-  float M = -CUDART_INF_F, L = 0.f, O = 0.f;
-  for (int i0 = g; i0 < c.n_parts; i0 += kExGroups * kExBatch) {
-    float mv[kExBatch], lv[kExBatch], ov[kExBatch];
-#pragma unroll
-    for (int u = 0; u < kExBatch; ++u) {
-      const int i = i0 + u * kExGroups;
-      const bool in = i < c.n_parts;
-      mv[u] = in ? __ldcg(c.m + i * c.ml_part_stride + h * c.ml_row_stride) : -CUDART_INF_F;
-      lv[u] = in ? __ldcg(c.l + i * c.ml_part_stride + h * c.ml_row_stride) : 0.f;
-      ov[u] = in ? __ldcg(c.o + i * c.o_part_stride + h * c.o_row_stride + d) : 0.f;
-    }
-    float bm = M;
-#pragma unroll
-    for (int u = 0; u < kExBatch; ++u)
-      if (lv[u] > 0.f) bm = fmaxf(bm, mv[u]);
-    if (bm == -CUDART_INF_F) continue;
-    const float sc = (M == -CUDART_INF_F) ? 0.f : expf(M - bm);
-    L *= sc;
-    O *= sc;
-#pragma unroll
-    for (int u = 0; u < kExBatch; ++u) {
-      const float w = lv[u] > 0.f ? expf(mv[u] - bm) : 0.f;
-      L += w * lv[u];
-      O += (w != 0.f) ? w * ov[u] : 0.f;
-    }
-    M = bm;
-  }
-  s_o[g][d] = O;
-  if (d == 0) {
-    s_m[g] = M;
-    s_l[g] = L;
-  }
-  __syncthreads();
+  float Mt = -CUDART_INF_F, Lt = 0.f, Ot = 0.f;
+  merge_partials(c, h, sm, Mt, Lt, Ot);
 
   const unsigned e = x.epoch[h] + 1u;  // only this CTA advances epoch[h]
   const int par = e & 1u;
 
   // ---- 2. publish (M, L, O) of this GPU to every GPU's inbox ----
   if (g == 0) {
-    float Mt = -CUDART_INF_F;
-#pragma unroll
-    for (int k = 0; k < kExGroups; ++k) Mt = fmaxf(Mt, s_m[k]);
-    float Lt = 0.f, Ot = 0.f;
-    if (Mt != -CUDART_INF_F) {
-#pragma unroll
-      for (int k = 0; k < kExGroups; ++k) {
-        const float w = (s_m[k] == -CUDART_INF_F) ? 0.f : expf(s_m[k] - Mt);
-        Lt += w * s_l[k];
-        Ot += (w != 0.f) ? w * s_o[k][d] : 0.f;
-      }
-    }
     const long long slot = ((long long)(par * x.world + x.rank) * n_rows + h) * kExSlot;
     for (int dst = 0; dst < x.world; ++dst) {
       uint2* p = x.inbox[dst] + slot;
@@ -140,39 +100,77 @@ __global__ void __launch_bounds__(kHeadDim * kExGroups) exchange_combine_kernel(
     }
   }
 
-  // ---- 3./4. wait for every source's words of this step and merge them ----
+  // ---- 3./4. gather every source's words of this step and merge them ----
+  // The o words of a thread's sources (spread over the 4 groups) are all
+  // loaded before any is checked; meanwhile one thread per (source, m or l)
+  // settles those words into shared memory.  Stale words are re-polled.
+  const uint2* base = x.inbox[x.rank] + (long long)par * x.world * n_rows * kExSlot +
+                      (long long)h * kExSlot;
+  const long long src_stride = (long long)n_rows * kExSlot;
+  uint2 wo[kExPerGroup];
+#pragma unroll
+  for (int k = 0; k < kExPerGroup; ++k) {
+    const int src = g + k * kExGroups;
+    if (src < x.world) wo[k] = ld_word(base + src * src_stride + 2 + d);
+  }
+  const long long deadline = clock64() + kExWaitBudget;
   bool ok = true;
-  float Ow = 0.f, Lw = 0.f;
-  if (g == 0) {
-    const uint2* base = x.inbox[x.rank] + (long long)par * x.world * n_rows * kExSlot +
-                        (long long)h * kExSlot;
-    const long long src_stride = (long long)n_rows * kExSlot;
-    const long long deadline = clock64() + kExWaitBudget;
-    float Mw = -CUDART_INF_F;
-    for (int s = 0; s < x.world && ok; ++s) {
-      float ms, ls;
-      ok = wait_word(base + s * src_stride, e, deadline, ms) &&
-           wait_word(base + s * src_stride + 1, e, deadline, ls);
-      if (ok && ls > 0.f) Mw = fmaxf(Mw, ms);
-    }
-    for (int s = 0; s < x.world && ok; ++s) {
-      float ms, ls, os;
-      ok = wait_word(base + s * src_stride, e, deadline, ms) &&
-           wait_word(base + s * src_stride + 1, e, deadline, ls) &&
-           wait_word(base + s * src_stride + 2 + d, e, deadline, os);
-      if (ok && ls > 0.f) {
-        const float w = expf(ms - Mw);
-        Lw += w * ls;
-        Ow += w * os;
+  if (threadIdx.x < 2 * x.world) {
+    const int src = threadIdx.x % x.world, which = threadIdx.x / x.world;  // 0: m, 1: l
+    const uint2* p = base + src * src_stride + which;
+    uint2 w = ld_word(p);
+    ok = settle_word(p, e, deadline, w);
+    (which ? s_wl : s_wm)[src] = __uint_as_float(w.x);
+  }
+  if (!__syncthreads_and(ok)) {
+    if (threadIdx.x == 0) atomicOr(x.status, kStatusWaitTimeout);
+    return;
+  }
+  float Mg = -CUDART_INF_F;
+#pragma unroll
+  for (int k = 0; k < kExPerGroup; ++k) {
+    const int src = g + k * kExGroups;
+    if (src < x.world && s_wl[src] > 0.f) Mg = fmaxf(Mg, s_wm[src]);
+  }
+  float Lg = 0.f, Og = 0.f;
+#pragma unroll
+  for (int k = 0; k < kExPerGroup; ++k) {
+    const int src = g + k * kExGroups;
+    if (src < x.world && ok) {
+      ok = settle_word(base + src * src_stride + 2 + d, e, deadline, wo[k]);
+      if (s_wl[src] > 0.f) {
+        const float w = expf(s_wm[src] - Mg);
+        Lg += w * s_wl[src];
+        Og += w * __uint_as_float(wo[k].x);
       }
     }
+  }
+  __syncthreads();  // the publish step above has finished reading s_m / s_l / s_o
+  s_o[g][d] = Og;
+  if (d == 0) {
+    s_m[g] = Mg;
+    s_l[g] = Lg;
   }
   if (!__syncthreads_and(ok)) {
     // A peer did not arrive: report it, leave out and epoch untouched.
     if (threadIdx.x == 0) atomicOr(x.status, kStatusWaitTimeout);
     return;
   }
-  if (g == 0) x.out[(long long)h * kHeadDim + d] = Lw > 0.f ? Ow / Lw : 0.f;
+  if (g == 0) {
+    float Mw = -CUDART_INF_F;
+#pragma unroll
+    for (int k = 0; k < kExGroups; ++k) Mw = fmaxf(Mw, s_m[k]);
+    float Lw = 0.f, Ow = 0.f;
+    if (Mw != -CUDART_INF_F) {
+#pragma unroll
+      for (int k = 0; k < kExGroups; ++k) {
+        const float w = (s_m[k] == -CUDART_INF_F) ? 0.f : expf(s_m[k] - Mw);
+        Lw += w * s_l[k];
+        Ow += (w != 0.f) ? w * s_o[k][d] : 0.f;
+      }
+    }
+    x.out[(long long)h * kHeadDim + d] = Lw > 0.f ? Ow / Lw : 0.f;
+  }
   if (threadIdx.x == 0) x.epoch[h] = e;
 }
 
