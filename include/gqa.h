@@ -237,6 +237,42 @@ GQA_API int gqa_decode_kv_shard_exchange(gqa_ctx *ctx, gqa_exchange *x, gqa_stre
                                          const gqa_layer_kv *kv, const float *qkv, int pos,
                                          int shard_begin, int shard_rows, float *out);
 
+/* ---- the attention half of the decoder layer ---------------------------- */
+
+/* Q4_0 blocks as in the reference (block_q4_0, attention_gqa_benchmark.c:
+ * 26-29): 32 weights in 18 bytes, an IEEE fp16 scale d then 16 bytes of
+ * 4-bit codes; weight j < 16 = d * ((qs[j] & 15) - 8), weight j + 16 =
+ * d * ((qs[j] >> 4) - 8).  A matrix is row-major: rows one after another,
+ * each row d_model / 32 blocks. */
+#define GQA_Q4_0_BLOCK_BYTES 18
+
+/* Device pointers of one layer's attention weights (16-byte aligned). */
+typedef struct {
+    const void *w_qkv;   /* Q4_0 [(n_heads_q + 2 n_heads_kv) * 128][d_model / 32] */
+    const float *b_qkv;  /* [(n_heads_q + 2 n_heads_kv) * 128] */
+    const void *w_o;     /* Q4_0 [d_model][d_model / 32] */
+    const float *gamma;  /* [d_model] weight of the attention RMSNorm */
+} gqa_block_weights;
+
+/* state += W_o * attention(RoPE(W_qkv * rmsnorm(state, gamma) + b_qkv)):
+ * the attention half of gpu_decoder_layer_step (qwen_server.c:444-453:
+ * k_rmsnorm_attn, k_qkv_gemv, the five attention kernels, k_wo_residual),
+ * with the KV append at pos as in gqa_layer_attention.  d_model =
+ * n_heads_q * 128 must be 1536; the RMSNorm epsilon is the reference's 1e-6.
+ * state: [d_model] device floats, updated in place. */
+GQA_API int gqa_attention_block(gqa_ctx *ctx, gqa_stream_t stream, const gqa_block_weights *w,
+                                const gqa_layer_kv *kv, float *state, int pos, int seq_len);
+
+/* gqa_attention_block for n_layers layers in a row (one state, the token's
+ * position read from device memory d_pos, seq_len = *d_pos + 1), the token
+ * loop of qwen_server.c:1021-1023 without the FFN half; with advance != 0 the
+ * position is incremented on the device afterwards (wrapping to wrap_lo at
+ * wrap_hi when wrap_hi > 0).  Capturable in a CUDA graph. */
+GQA_API int gqa_attention_block_layers(gqa_ctx *ctx, gqa_stream_t stream, int n_layers,
+                                       const gqa_block_weights *w, const gqa_layer_kv *kv,
+                                       float *state, int *d_pos, int advance, int wrap_lo,
+                                       int wrap_hi);
+
 /* ---- prefill ---------------------------------------------------------- */
 
 /* Causal attention over whole prompts on the tensor cores (bf16 operands,

@@ -12,5 +12,5 @@ The directory name contains hyphens, so it is loaded by path (see
 ``__graft_entry__.load_package``) under the module name ``gqa_b200``.
 """
 from . import seeded, shard  # noqa: F401
-from .gqa import (Context, GqaError, Graph, LayerKV, kv_of, lib, last_error,  # noqa: F401
-                  header_functions)
+from .gqa import (BlockWeights, Context, Exchange, GqaError, Graph, LayerKV,  # noqa: F401
+                  block_weights_of, header_functions, kv_of, last_error, lib)

@@ -40,6 +40,13 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
                            int* sched, int n_sm, cudaStream_t st);
+int q4_row_bytes();
+int block_d_model();
+cudaError_t launch_qkv_gemv(const void* w, const float* bias, const float* gamma,
+                            const float* state, float* qkv, int M, int* status, cudaStream_t st,
+                            bool pdl);
+cudaError_t launch_wo_gemv(const void* w, const float* attn, float* state, int M, int* status,
+                           cudaStream_t st, bool pdl);
 size_t exchange_inbox_bytes(int world, int n_rows);
 cudaError_t launch_exchange_combine(const CombineParams& local, uint2* const* inbox,
                                     unsigned* epoch, int rank, int world, float* out, int* status,
@@ -90,6 +97,8 @@ struct gqa_ctx {
   // the final merge).
   int cluster = 0;
   int* counters = nullptr;  // [kMaxCounters + 2] arrival / item counters, kept at zero
+  float* blk_qkv = nullptr;   // attention block workspace: qkv of the token
+  float* blk_attn = nullptr;  // attention block workspace: attention output
   __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
   size_t prefill_cap = 0;                // elements
   float2* rope_cs = nullptr;             // prefill RoPE table [rope_cap][64] (cos, sin)
@@ -303,6 +312,31 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
   return GQA_OK;
 }
 
+// One attention block: QKV projection (with RMSNorm) -> split-KV attention
+// (RoPE + append fused) and merge -> Wo projection into the state.
+int check_block_weights(const gqa_ctx* c, const gqa_block_weights* w) {
+  if (!w || !w->w_qkv || !w->b_qkv || !w->w_o || !w->gamma)
+    return fail(GQA_ERR_INVALID_ARG, "null block weight pointer");
+  if (c->cfg.n_heads_q * kHeadDim != block_d_model())
+    return fail(GQA_ERR_UNSUPPORTED, "attention block built for d_model %d (n_heads_q * 128 = %d)",
+                block_d_model(), c->cfg.n_heads_q * kHeadDim);
+  if (!aligned16(w->w_qkv) || !aligned16(w->w_o) || !aligned16(w->b_qkv) || !aligned16(w->gamma))
+    return fail(GQA_ERR_INVALID_ARG, "block weights must be 16-byte aligned");
+  return GQA_OK;
+}
+
+int block_impl(gqa_ctx* c, cudaStream_t st, const gqa_block_weights* w, const gqa_layer_kv* kv,
+               float* state, Lengths len, int plan_len, bool pdl_first, bool lengths_stable) {
+  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
+  GQA_CUDA(launch_qkv_gemv(w->w_qkv, w->b_qkv, w->gamma, state, c->blk_qkv,
+                           (nq + 2 * nkv) * kHeadDim, c->status, st, pdl_first));
+  int rc = run_single(c, st, kv, c->blk_qkv, len, plan_len, true, c->blk_attn, true,
+                      lengths_stable);
+  if (rc != GQA_OK) return rc;
+  GQA_CUDA(launch_wo_gemv(w->w_o, c->blk_attn, state, nq * kHeadDim, c->status, st, true));
+  return GQA_OK;
+}
+
 // Runs the split kernel of one KV shard (rows [shard_begin, shard_begin +
 // shard_rows) of the sequence, global position pos) and describes its
 // partials in *cp for a merge (cp->n_parts = 0 when the shard attends no row).
@@ -402,6 +436,9 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess) e = prepare_prefill_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->inv_freq, sizeof(float) * kHalf);
   if (e == cudaSuccess) e = cudaMalloc(&c->status, sizeof(int));
+  if (e == cudaSuccess)
+    e = cudaMalloc(&c->blk_qkv, sizeof(float) * (cfg->n_heads_q + 2 * cfg->n_heads_kv) * kHeadDim);
+  if (e == cudaSuccess) e = cudaMalloc(&c->blk_attn, sizeof(float) * cfg->n_heads_q * kHeadDim);
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * (kMaxCounters + 2));
   if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * (kMaxCounters + 2));
   if (e == cudaSuccess)
@@ -421,6 +458,8 @@ int gqa_destroy(gqa_ctx* c) {
   if (c->inv_freq) cudaFree(c->inv_freq);
   if (c->status) cudaFree(c->status);
   if (c->counters) cudaFree(c->counters);
+  if (c->blk_qkv) cudaFree(c->blk_qkv);
+  if (c->blk_attn) cudaFree(c->blk_attn);
   if (c->prefill_img) cudaFree(c->prefill_img);
   if (c->rope_cs) cudaFree(c->rope_cs);
   if (c->part_o) cudaFree(c->part_o);
@@ -756,6 +795,51 @@ int gqa_decode_kv_shard(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
   cp.out_m = m;
   cp.out_l = l;
   GQA_CUDA(launch_combine(cp, 1, st, true));
+  return GQA_OK;
+}
+
+int gqa_attention_block(gqa_ctx* c, gqa_stream_t stream, const gqa_block_weights* w,
+                        const gqa_layer_kv* kv, float* state, int pos, int seq_len) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  int rc = check_block_weights(c, w);
+  if (rc != GQA_OK) return rc;
+  rc = check_kv(c, kv);
+  if (rc != GQA_OK) return rc;
+  if (!state || !aligned16(state)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned state");
+  if (pos < 0 || pos >= c->cfg.t_max || seq_len < 1 || seq_len > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "pos %d / seq_len %d out of range (t_max %d)", pos, seq_len,
+                c->cfg.t_max);
+  DeviceGuard g(c->device);
+  Lengths len{};
+  len.pos_imm = pos;
+  len.seqlen_imm = seq_len;
+  return block_impl(c, (cudaStream_t)stream, w, kv, state, len, seq_len, c->pdl != 0, false);
+}
+
+int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
+                               const gqa_block_weights* w, const gqa_layer_kv* kv, float* state,
+                               int* d_pos, int advance, int wrap_lo, int wrap_hi) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (n_layers < 1 || !w || !kv || !d_pos || !state || !aligned16(state))
+    return fail(GQA_ERR_INVALID_ARG, "gqa_attention_block_layers: bad arguments");
+  for (int l = 0; l < n_layers; ++l) {
+    int rc = check_block_weights(c, &w[l]);
+    if (rc == GQA_OK) rc = check_kv(c, &kv[l]);
+    if (rc != GQA_OK) return rc;
+  }
+  DeviceGuard g(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Lengths len{};
+  len.pos_dev = d_pos;
+  for (int l = 0; l < n_layers; ++l) {
+    // Layer 0 may follow the kernel that advanced *d_pos; its split kernel
+    // reads pos only after its wait.  Every later kernel starts after layer
+    // 0's split kernel has passed its wait.
+    int rc = block_impl(c, st, &w[l], &kv[l], state, len, c->cfg.t_max,
+                        c->layers_pdl != 0, l > 0);
+    if (rc != GQA_OK) return rc;
+  }
+  if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
   return GQA_OK;
 }
 

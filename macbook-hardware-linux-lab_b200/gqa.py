@@ -57,6 +57,11 @@ class Config(ctypes.Structure):
                 ("rope_theta", ctypes.c_float)]
 
 
+class BlockWeights(ctypes.Structure):
+    _fields_ = [("w_qkv", ctypes.c_void_p), ("b_qkv", ctypes.c_void_p),
+                ("w_o", ctypes.c_void_p), ("gamma", ctypes.c_void_p)]
+
+
 class LayerKV(ctypes.Structure):
     """One layer's cache: the reference's LayerKVDevice {k_cache, v_cache}."""
     _fields_ = [("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p)]
@@ -93,6 +98,10 @@ _SIGNATURES = {
     "gqa_lse_combine": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
     "gqa_decode_kv_shard": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _i, _vp, _vp, _vp],
     "gqa_lse_combine_packed": [_vp, _vp, _i, _i, _vp, _ll, _vp],
+    "gqa_attention_block": [_vp, _vp, ctypes.POINTER(BlockWeights), ctypes.POINTER(LayerKV), _vp,
+                            _i, _i],
+    "gqa_attention_block_layers": [_vp, _vp, _i, ctypes.POINTER(BlockWeights),
+                                   ctypes.POINTER(LayerKV), _vp, _vp, _i, _i, _i],
     "gqa_exchange_create": [_vp, _i, _i, ctypes.POINTER(_vp), _vp],
     "gqa_exchange_open": [_vp, _vp],
     "gqa_exchange_destroy": [_vp],
@@ -165,6 +174,11 @@ def _stream(s) -> int | None:
 
 def kv_of(k_cache, v_cache) -> LayerKV:
     return LayerKV(_ptr(k_cache), _ptr(v_cache))
+
+
+def block_weights_of(w_qkv, b_qkv, w_o, gamma) -> BlockWeights:
+    """BlockWeights of device tensors (Q4_0 byte tensors and float tensors)."""
+    return BlockWeights(_ptr(w_qkv), _ptr(b_qkv), _ptr(w_o), _ptr(gamma))
 
 
 def _kv_array(kvs) -> ctypes.Array:
@@ -358,6 +372,20 @@ class Context:
     def lse_combine(self, n_parts: int, n_rows: int, m, l, o, out, stream=None) -> None:
         _check(lib().gqa_lse_combine(self._h, _stream(stream), n_parts, n_rows, _ptr(m), _ptr(l),
                                      _ptr(o), _ptr(out)))
+
+    def attention_block(self, w: "BlockWeights", kv: LayerKV, state, pos: int, seq_len: int,
+                        stream=None) -> None:
+        _check(lib().gqa_attention_block(self._h, _stream(stream), ctypes.byref(w),
+                                         ctypes.byref(kv), _ptr(state), pos, seq_len))
+
+    def attention_block_layers(self, weights, kvs, state, d_pos, advance: bool = False,
+                               wrap_lo: int = 0, wrap_hi: int = 0, stream=None) -> None:
+        n = len(weights)
+        warr = (BlockWeights * n)(*weights)
+        karr = (LayerKV * n)(*kvs)
+        _check(lib().gqa_attention_block_layers(self._h, _stream(stream), n, warr, karr,
+                                                _ptr(state), _ptr(d_pos), int(advance), wrap_lo,
+                                                wrap_hi))
 
     def lse_combine_packed(self, n_parts: int, n_rows: int, packed, part_stride: int, out,
                            stream=None) -> None:

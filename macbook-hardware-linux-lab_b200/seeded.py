@@ -27,6 +27,9 @@ _MASK = (1 << 64) - 1
 # Stream ids used across tests and the bench, so that the same seed names the
 # same tensor everywhere.
 QKV, K_CACHE, V_CACHE, LENGTHS, PREFILL_Q, PREFILL_K, PREFILL_V = 1, 2, 3, 4, 5, 6, 7
+W_QKV, B_QKV, W_O, GAMMA, STATE = 8, 9, 10, 11, 12
+
+Q4_0_BLOCK_BYTES = 18
 
 
 def _mix(z: np.ndarray) -> np.ndarray:
@@ -108,3 +111,44 @@ def decode_inputs(seed: int, t_max: int = 4096, n_heads_q: int = 12, n_heads_kv:
     else:
         raise ValueError(dist)
     return qkv, kc.reshape(n_heads_kv, t_max, 128), vc.reshape(n_heads_kv, t_max, 128)
+
+
+def q4_0_matrix(seed: int, stream_id: int, rows: int, cols: int, scale: float) -> np.ndarray:
+    """A Q4_0 matrix [rows][cols / 32 blocks] as bytes (the reference's
+    block_q4_0: little-endian fp16 scale, then 16 bytes of 4-bit codes).
+    Block b takes splitmix64 outputs 3b .. 3b+2 of the stream: the first sets
+    d = scale * (0.5 + u), u uniform in [0, 1), the other two are the codes."""
+    nb = rows * (cols // 32)
+    u = uniform_u64(seed, stream_id, 3 * nb)
+    frac = (u[0::3] >> np.uint64(11)).astype(np.float64) / float(1 << 53)
+    d = (scale * (0.5 + frac)).astype(np.float16)
+    out = np.empty((nb, Q4_0_BLOCK_BYTES), dtype=np.uint8)
+    out[:, 0:2] = d.view(np.uint8).reshape(nb, 2)
+    out[:, 2:] = np.stack([u[1::3], u[2::3]], axis=1).astype("<u8").view(np.uint8).reshape(nb, 16)
+    return out.reshape(-1)
+
+
+def q4_0_dequant(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """Dense float32 [rows][cols] of a Q4_0 byte matrix (w = d * (code - 8))."""
+    b = np.asarray(blocks, dtype=np.uint8).reshape(rows * (cols // 32), Q4_0_BLOCK_BYTES)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
+    q = b[:, 2:].astype(np.int32)
+    w = np.concatenate([(q & 15) - 8, (q >> 4) - 8], axis=1).astype(np.float32) * d
+    return w.reshape(rows, cols)
+
+
+def attention_block_inputs(seed: int, t_max: int = 4096, d_model: int = 1536, n_heads_kv: int = 2):
+    """(state, w_qkv, b_qkv, w_o, gamma, k_cache, v_cache) of one layer's
+    attention block: state, caches N(0, 1); Q4_0 weights scaled so each
+    projection has unit-RMS rows; b_qkv ~ N(0, 0.1^2); gamma ~ 1 + N(0, 0.1^2)."""
+    n_qkv = d_model + 2 * n_heads_kv * 128
+    scale = 1.0 / (4.6 * np.sqrt(d_model))  # RMS of (code - 8) is ~4.6
+    state = normal(seed, STATE, d_model)
+    w_qkv = q4_0_matrix(seed, W_QKV, n_qkv, d_model, scale)
+    b_qkv = (0.1 * normal(seed, B_QKV, n_qkv)).astype(np.float32)
+    w_o = q4_0_matrix(seed, W_O, d_model, d_model, scale)
+    gamma = (1.0 + 0.1 * normal(seed, GAMMA, d_model)).astype(np.float32)
+    n = n_heads_kv * t_max * 128
+    kc = normal(seed, K_CACHE, n).reshape(n_heads_kv, t_max, 128)
+    vc = normal(seed, V_CACHE, n).reshape(n_heads_kv, t_max, 128)
+    return state, w_qkv, b_qkv, w_o, gamma, kc, vc

@@ -218,3 +218,28 @@ def ref_layer_attention(qkv, k_cache, v_cache, pos, seq_len) -> np.ndarray:
     if rc != 0:
         raise ValueError("reference rejected pos/seq_len")
     return out
+
+
+def ref_attention_block(x_in, w_qkv, b_qkv, w_o, gamma, k_cache, v_cache, pos, seq_len) -> np.ndarray:
+    """The reference's cpu_decoder_layer_step with zero FFN weights: x_in +
+    W_o * attn(RoPE(W_qkv * rmsnorm(x_in, gamma) + b_qkv)).  w_qkv / w_o are
+    Q4_0 byte arrays ([2048][48] and [1536][48] blocks of 18 bytes); caches
+    [2][4096][128] are updated in place at row pos."""
+    assert k_cache.shape == (2, REF_T_MAX, 128) and v_cache.shape == (2, REF_T_MAX, 128)
+    w_qkv = np.ascontiguousarray(w_qkv, dtype=np.uint8)
+    w_o = np.ascontiguousarray(w_o, dtype=np.uint8)
+    assert w_qkv.size == 2048 * 48 * 18 and w_o.size == 1536 * 48 * 18
+    lib = _load(REF_LAYER_SO)
+    fn = lib.ref_attention_block
+    if fn.argtypes is None:
+        _vp = ctypes.c_void_p
+        fn.argtypes = [_fp, _vp, _fp, _vp, _fp, _fp, _fp, _i, _i, _fp]
+        fn.restype = _i
+    out = np.zeros(1536, dtype=np.float32)
+    rc = fn(_fptr(np.ascontiguousarray(x_in, dtype=np.float32)), w_qkv.ctypes.data,
+            _fptr(np.ascontiguousarray(b_qkv, dtype=np.float32)), w_o.ctypes.data,
+            _fptr(np.ascontiguousarray(gamma, dtype=np.float32)), _fptr(k_cache), _fptr(v_cache),
+            pos, seq_len, _fptr(out))
+    if rc != 0:
+        raise ValueError("reference rejected pos/seq_len")
+    return out

@@ -74,3 +74,24 @@ int ref_layer_attention(const float *qkv_in, float *k_cache, float *v_cache,
     cpu_decoder_layer_step(g_x0, &w, &kv, pos, seq_len, attn_out);
     return 0;
 }
+
+/* The attention half of the layer with caller-given weights:
+ *   y_out = x_in + W_o * attn(RoPE(W_qkv * rmsnorm(x_in, gamma) + b_qkv))
+ * (test_28_layers_real.c:199-296).  The FFN weights stay all zero, so the
+ * layer's FFN adds exactly 0 (:298-317) and y_out is the attention half bit
+ * for bit.  w_qkv: [2048][48] block_q4_0, w_o: [1536][48]; caches
+ * [2][4096][128] updated at row pos. */
+int ref_attention_block(const float *x_in, const void *w_qkv, const float *b_qkv,
+                        const void *w_o, const float *gamma, float *k_cache, float *v_cache,
+                        int pos, int seq_len, float *y_out) {
+    if (pos < 0 || pos >= T_MAX || seq_len < 1 || seq_len > T_MAX) return -1;
+    pthread_once(&g_once, init_weights);
+    LayerWeightsHost w = g_w;
+    w.W_qkv = (block_q4_0 *)w_qkv;
+    w.b_qkv = (float *)b_qkv;
+    w.W_o = (block_q4_0 *)w_o;
+    w.gamma_attn = (float *)gamma;
+    LayerKVHost kv = { k_cache, v_cache };
+    cpu_decoder_layer_step(x_in, &w, &kv, pos, seq_len, y_out);
+    return 0;
+}
