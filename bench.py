@@ -50,7 +50,13 @@ WORKLOADS = {
     "single": dict(layers=1, t_max=512, pos_lo=511, pos_hi=512, seqs=1),
     "long1": dict(layers=1, seqs=1, t_max=32768, window=64),
     "prefill": dict(layers=1, seqs=8, t_max=2048),
+    "block28": dict(layers=28, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1),
 }
+
+BLOCK_METRIC = ("GQA attention block (RMSNorm, Q4_0 QKV + bias, attention, Q4_0 Wo + residual): "
+                "HBM GB/s of KV + weights and tok/s")
+Q4_ROW = (1536 // 32) * 18  # bytes of one Q4_0 row of d_model = 1536 inputs
+BLOCK_WEIGHT_BYTES = (QKV_W + OUT_W) * Q4_ROW + (QKV_W + OUT_W) * 4  # W_qkv, W_o, b_qkv, gamma
 
 PREFILL_METRIC = "GQA causal prefill: bf16 tensor-core TFLOP/s (fp32 accumulation)"
 
@@ -247,6 +253,14 @@ def run_reference_arm(args):
 
 
 def workload_config(name, exchange="peer"):
+    if name == "block28":
+        return {"workload": "block28: 28 attention blocks per token (RMSNorm, Q4_0 QKV 2048x1536 + "
+                            "bias, RoPE/append + GQA attention over fp32 KV t_max=4096, Q4_0 Wo "
+                            "1536x1536 + residual), 1 sequence per GPU, positions 3840..4095",
+                "layers": 28, "t_max": 4096, "positions": [3840, 4095],
+                "bytes_per_layer": "2048*(pos+1) KV + %d weights" % BLOCK_WEIGHT_BYTES,
+                "l2": "KV 235 MB + weights 87 MB per GPU > 126 MB L2; no flush",
+                "parallelism": "sequence-sharded replicas"}
     if name == "resident28":
         return {"workload": "resident28: 28-layer resident decode attention, 1 sequence per GPU, "
                             "12 q / 2 KV heads, d=128, fp32 KV t_max=4096 per layer (235 MB), "
@@ -359,6 +373,121 @@ def run_resident(args, g, ctx, rank, world, local):
                 launches=kernels_per_step * args.steps, launches_per_step=kernels_per_step,
                 h2d=L_layers * QKV_W * 4, d2h=L_layers * OUT_W * 4, tokens=args.steps,
                 dominant_launches=L_layers * args.steps)
+
+
+def run_block(args, g, ctx, rank, world, local):
+    import torch
+    wl = WORKLOADS["block28"]
+    L_layers, t_max, pos_lo, pos_hi = wl["layers"], wl["t_max"], wl["pos_lo"], wl["pos_hi"]
+    seed = 5353 + 1000 * rank
+    caches = torch.empty((L_layers, 2, 2, t_max, D), device="cuda")
+    ctx.fill_normal(caches, caches.numel(), seed, g.seeded.K_CACHE)
+    kvs = [g.kv_of(caches[l, 0], caches[l, 1]) for l in range(L_layers)]
+    scale = 1.0 / (4.6 * np.sqrt(OUT_W))
+    keep, ws = [], []
+    for l in range(L_layers):
+        wq = torch.from_numpy(g.seeded.q4_0_matrix(seed + l, g.seeded.W_QKV, QKV_W, OUT_W, scale))
+        wo = torch.from_numpy(g.seeded.q4_0_matrix(seed + l, g.seeded.W_O, OUT_W, OUT_W, scale))
+        bq = torch.from_numpy(0.1 * g.seeded.normal(seed + l, g.seeded.B_QKV, QKV_W))
+        gm = torch.from_numpy(1.0 + 0.1 * g.seeded.normal(seed + l, g.seeded.GAMMA, OUT_W))
+        dev = [wq.cuda(), bq.float().cuda(), wo.cuda(), gm.float().cuda()]
+        keep += dev
+        ws.append(g.block_weights_of(*dev))
+    state0 = torch.empty(OUT_W, device="cuda")
+    ctx.fill_normal(state0, OUT_W, seed, g.seeded.STATE)
+    state = state0.clone()
+    d_pos = torch.tensor([pos_lo], dtype=torch.int32, device="cuda")
+    ctx.reserve(1, t_max)
+    n_window = pos_hi - pos_lo
+
+    def step_bytes(i):
+        pos = pos_lo + i % n_window
+        return L_layers * (ROW_BYTES * (pos + 1) + BLOCK_WEIGHT_BYTES)
+
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        ctx.attention_block_layers(ws, kvs, state, d_pos, True, pos_lo, pos_hi)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    with torch.cuda.stream(cap):
+        with torch.cuda.graph(graph, stream=cap):
+            ctx.attention_block_layers(ws, kvs, state, d_pos, True, pos_lo, pos_hi)
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status set during warm-up")
+
+    d_pos.fill_(pos_lo)
+    state.copy_(state0)
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    total_bytes = sum(step_bytes(i) for i in range(args.steps))
+
+    # e2e: the token's residual state from pinned host memory in, the state out
+    h_state = state0.cpu().pin_memory()
+    h_out = torch.empty(OUT_W).pin_memory()
+    d_pos.fill_(pos_lo)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        state.copy_(h_state, non_blocking=True)
+        graph.replay()
+        h_out.copy_(state, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status set after the timed regions")
+    del graph
+    # per layer: QKV GEMV, split, combine, Wo GEMV; plus the position advance
+    per_step = 4 * L_layers + 1
+    return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3, bytes=total_bytes,
+                clocks=clk.summary(), launches=per_step * args.steps,
+                launches_per_step=per_step, h2d=OUT_W * 4, d2h=OUT_W * 4, tokens=args.steps,
+                dominant_launches=L_layers * args.steps, metric=BLOCK_METRIC,
+                kernel="decode_split_kernel + gemv_q4_kernel (one attention block)",
+                data="synthetic: seeded N(0,1) state and KV caches, seeded Q4_0 weights "
+                     "(scales for unit-RMS projections)")
+
+
+def cpu_block_run(budget_s, pos_lo=3840, layers=28):
+    """The reference's decoder-layer step with zero FFN weights (the attention
+    block) on the host cores: per step its 28 layer calls in a row, each with
+    the reference's OpenMP GEMVs and serial attention."""
+    import __graft_entry__
+    g = __graft_entry__.load_package()
+    orc = __graft_entry__.load_oracle()
+    if not orc.have_reference():
+        return None
+    blocks = [g.seeded.attention_block_inputs(900 + l) for l in range(layers)]
+    state = blocks[0][0].copy()
+    t0 = time.perf_counter()
+    done, nbytes = 0, 0
+    while True:
+        pos = pos_lo + done % 256
+        for L in blocks:
+            state = orc.ref_attention_block(state, L[1], L[2], L[3], L[4], L[5], L[6], pos, pos + 1)
+        nbytes += layers * (ROW_BYTES * (pos + 1) + BLOCK_WEIGHT_BYTES)
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    sample = (f"{done} token step(s) x {layers} attention blocks at positions {pos_lo}.."
+              f"{pos_lo + min(done, 256) - 1}, the reference's OpenMP GEMVs on "
+              f"{os.cpu_count()} threads, attention serial")
+    return nbytes / dt / 1e9, os.cpu_count() or 1, sample, "reference", done / dt
 
 
 def run_batched(args, g, ctx, rank, world, local):
@@ -582,7 +711,9 @@ def run_ours(args):
     if args.workload == "prefill":
         return report_prefill(args, run_prefill(args, g, ctx, rank, world, local), ctx, rank,
                               world)
-    if args.workload in ("resident28", "single"):
+    if args.workload == "block28":
+        r = run_block(args, g, ctx, rank, world, local)
+    elif args.workload in ("resident28", "single"):
         r = run_resident(args, g, ctx, rank, world, local)
     elif args.workload == "long1":
         r = run_long1(args, g, ctx, rank, world, local)
@@ -599,17 +730,23 @@ def run_ours(args):
     achieved = r["bytes"] / r["t"] / 1e9  # this rank's dominant-kernel bytes over its timed region
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cgbs, cores, sample, kind, _ = cpu_reference_run(10 ** 6, 1, budget_s=12.0)
-        cpu = {"value": round(cgbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
-               "sample": sample}
+        if args.workload == "block28":
+            res = cpu_block_run(budget_s=12.0)
+        else:
+            res = cpu_reference_run(10 ** 6, 1, budget_s=12.0)
+        if res is not None:
+            cgbs, cores, sample, kind, _ = res
+            cpu = {"value": round(cgbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+                   "sample": sample}
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world,
+            "metric": r.get("metric", METRIC), "value": round(gbs, 2), "unit": "GB/s",
+            "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t / args.steps * 1e3, 5), "higher_is_better": True,
-            "scaling": "weak" if args.workload in ("resident28", "single") else "strong",
+            "scaling": "weak" if args.workload in ("resident28", "single", "block28") else "strong",
             "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)",
+            "data": r.get("data", "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)"),
             "config": dict(workload_config(args.workload, args.exchange),
                            kernel_variant="auto" if args.variant < 0 else args.variant,
                            target_ctas=args.target_ctas or None,
@@ -619,7 +756,7 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_kind} hbm_gbs",
-                         "kernel": "decode_split_kernel",
+                         "kernel": r.get("kernel", "decode_split_kernel"),
                          "algorithmic_bytes_per_launch": round(per_gpu_bytes),
                          "duration_basis": "timed-region device time / launches of the "
                                            "dominant kernel (includes its combine and gaps)",

@@ -17,10 +17,13 @@
 // d * ((qs[j] >> 4) - 8).  A row of d_model = 1536 inputs is 48 blocks =
 // 864 bytes (a multiple of 16, so rows are whole 1-D bulk copies).
 //
-// Each CTA owns 16 consecutive output rows.  It copies their weights into
-// shared memory before its programmatic-dependency wait (the weights do not
-// depend on the previous kernel), then reads the input vector, and 16
-// threads per row each take 3 blocks; the 16 partial sums meet by shuffles.
+// Each CTA owns 8 consecutive output rows, one warp per row.  It copies
+// their weights into shared memory (and the QKV kernel its RMSNorm weights
+// into registers) before its programmatic-dependency wait -- the weights do
+// not depend on the previous kernel -- then reads the input vector.  Lane
+// 2i + h of a row's warp takes, in each of 3 passes, the low (h = 0) or high
+// (h = 1) nibbles of block i + 16 * pass, i.e. 16 weights, with 16-bit code
+// loads and float4 loads of the input; the 32 partial sums meet by shuffles.
 #include <cuda_fp16.h>
 
 #include "gqa_common.cuh"
@@ -30,9 +33,10 @@ namespace gqa {
 constexpr int kQ4BlockBytes = 18;
 constexpr int kDModel = 1536;                                // inputs per row
 constexpr int kQ4RowBytes = (kDModel / 32) * kQ4BlockBytes;  // 864
-constexpr int kGemvRows = 16;                                // rows per CTA
-constexpr int kGemvThreads = 256;                            // 16 threads per row
-constexpr int kGemvBlocksPerThread = (kDModel / 32) / 16;    // 3
+constexpr int kGemvRows = 8;                                 // rows per CTA, a warp each
+constexpr int kGemvThreads = 32 * kGemvRows;
+constexpr int kGemvPasses = (kDModel / 32) / 16;             // 3 (16 blocks per pass)
+constexpr int kGemvInPerThread = kDModel / kGemvThreads;     // 6
 constexpr float kRmsEps = 1e-6f;                             // EPSILON of the reference
 constexpr long long kGemvWaitBudget = 2000000000LL;
 
@@ -48,7 +52,7 @@ struct GemvParams {
 
 struct GemvSmem {
   alignas(128) uint8_t w[kGemvRows * kQ4RowBytes];
-  float z[kDModel];
+  alignas(16) float z[kDModel];
   float red[kGemvThreads / 32];
   uint64_t full;
 };
@@ -61,8 +65,8 @@ __device__ __forceinline__ float q4_weight(uint32_t code) {
 template <bool kQKV>
 __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams p) {
   __shared__ GemvSmem sm;
-  const int tid = threadIdx.x, r0 = blockIdx.x * kGemvRows;
-  const int row = tid >> 4, sub = tid & 15;
+  const int tid = threadIdx.x, row = tid >> 5, lane = tid & 31;
+  const int r0 = blockIdx.x * kGemvRows;
   if (tid == 0) {
     mbar_init(&sm.full, 1);
     fence_barrier_init();
@@ -75,30 +79,36 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
         ::"r"(smem_addr(sm.w)), "l"(p.w + (size_t)r0 * kQ4RowBytes),
           "r"(kGemvRows * kQ4RowBytes), "r"(smem_addr(&sm.full)) : "memory");
   }
-  const float bias = (kQKV && sub == 0) ? p.bias[r0 + row] : 0.f;
+  float gm[kGemvInPerThread];
+  if (kQKV) {
+#pragma unroll
+    for (int k = 0; k < kGemvInPerThread; ++k) gm[k] = p.gamma[tid + k * kGemvThreads];
+  }
+  const float bias = (kQKV && lane == 0) ? p.bias[r0 + row] : 0.f;
   pdl_launch_dependents();
   pdl_wait();
 
   // ---- the input vector (RMSNorm'ed for the QKV projection) ----
+  float xv[kGemvInPerThread];
+#pragma unroll
+  for (int k = 0; k < kGemvInPerThread; ++k) xv[k] = p.x[tid + k * kGemvThreads];
   if (kQKV) {
     float ss = 0.f;
-    for (int i = tid; i < kDModel; i += kGemvThreads) {
-      const float v = p.x[i];
-      sm.z[i] = v;
-      ss += v * v;
-    }
+#pragma unroll
+    for (int k = 0; k < kGemvInPerThread; ++k) ss += xv[k] * xv[k];
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    if ((tid & 31) == 0) sm.red[tid >> 5] = ss;
+    if (lane == 0) sm.red[row] = ss;
     __syncthreads();
     float tot = 0.f;
 #pragma unroll
     for (int k = 0; k < kGemvThreads / 32; ++k) tot += sm.red[k];
     const float scale = 1.0f / sqrtf(tot / (float)kDModel + kRmsEps);
-    for (int i = tid; i < kDModel; i += kGemvThreads) sm.z[i] = sm.z[i] * scale * p.gamma[i];
-  } else {
-    for (int i = tid; i < kDModel; i += kGemvThreads) sm.z[i] = p.x[i];
+#pragma unroll
+    for (int k = 0; k < kGemvInPerThread; ++k) xv[k] = xv[k] * scale * gm[k];
   }
+#pragma unroll
+  for (int k = 0; k < kGemvInPerThread; ++k) sm.z[tid + k * kGemvThreads] = xv[k];
   __syncthreads();
 
   // ---- weights landed? (bounded wait; the copy always completes) ----
@@ -107,27 +117,34 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
     return;
   }
 
-  // ---- 16 threads per row, blocks sub, sub + 16, sub + 32 ----
+  // ---- one warp per row: lane = (block within the pass, nibble half) ----
   const uint8_t* wrow = sm.w + row * kQ4RowBytes;
+  const int half = lane & 1, shift = 4 * half;
   float acc = 0.f;
 #pragma unroll
-  for (int k = 0; k < kGemvBlocksPerThread; ++k) {
-    const int b = sub + 16 * k;
+  for (int pass = 0; pass < kGemvPasses; ++pass) {
+    const int b = (lane >> 1) + 16 * pass;
     const uint8_t* blk = wrow + b * kQ4BlockBytes;
     const float d = __half2float(*reinterpret_cast<const __half*>(blk));
-    const float* z = sm.z + 32 * b;
-    float a0 = 0.f, a1 = 0.f;
+    const uint16_t* qs = reinterpret_cast<const uint16_t*>(blk + 2);
+    const float4* z4 = reinterpret_cast<const float4*>(sm.z + 32 * b + 16 * half);
+    float a = 0.f;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t q = blk[2 + j];
-      a0 = fmaf(q4_weight(q & 15u), z[j], a0);
-      a1 = fmaf(q4_weight(q >> 4), z[16 + j], a1);
+    for (int m = 0; m < 4; ++m) {
+      const float4 z = z4[m];
+      const uint32_t v0 = qs[2 * m], v1 = qs[2 * m + 1];
+      // weights 4m .. 4m+3 of this half: byte 4m+e holds weight 4m+e (low
+      // nibble, half 0) or 16+4m+e (high nibble, half 1)
+      a = fmaf(q4_weight((v0 >> shift) & 15u), z.x, a);
+      a = fmaf(q4_weight((v0 >> (8 + shift)) & 15u), z.y, a);
+      a = fmaf(q4_weight((v1 >> shift) & 15u), z.z, a);
+      a = fmaf(q4_weight((v1 >> (8 + shift)) & 15u), z.w, a);
     }
-    acc = fmaf(d, a0 + a1, acc);
+    acc = fmaf(d, a, acc);
   }
 #pragma unroll
-  for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (sub == 0) {
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
     if (kQKV)
       p.y[r0 + row] = acc + bias;
     else
