@@ -85,8 +85,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
     for (int k = 0; k < kGemvInPerThread; ++k) gm[k] = p.gamma[tid + k * kGemvThreads];
   }
   const float bias = (kQKV && lane == 0) ? p.bias[r0 + row] : 0.f;
-  pdl_launch_dependents();
+  // Dependents are released only once this grid runs for real: launched
+  // earlier, their waiting CTAs would hold SM space this grid needs.
   pdl_wait();
+  pdl_launch_dependents();
+  // The residual this row adds to, loaded now rather than after the dot product.
+  const float resid = (!kQKV && lane == 0) ? p.y[r0 + row] : 0.f;
 
   // ---- the input vector (RMSNorm'ed for the QKV projection) ----
   float xv[kGemvInPerThread];
@@ -148,7 +152,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
     if (kQKV)
       p.y[r0 + row] = acc + bias;
     else
-      p.y[r0 + row] += acc;
+      p.y[r0 + row] = resid + acc;
   }
 }
 

@@ -687,11 +687,13 @@ __global__ void __launch_bounds__(kHeadDim * kMergeGroups) combine_kernel(const 
   const int h = blockIdx.x, seq = blockIdx.y;
   const int d = threadIdx.x % kHeadDim, g = threadIdx.x / kHeadDim;
   const long long r = (long long)seq * c.rows_per_seq + h;
-  // Let the next kernel (the next layer's split kernel) start streaming its
-  // own cache now; it waits for this grid before it reads or writes anything
-  // this grid touches.
-  pdl_launch_dependents();
+  // The next kernel is released once this grid runs (after its wait), not
+  // before: released earlier, its CTAs would sit in their own wait holding
+  // SM space the split kernel still running ahead of this one needs (a
+  // trace showed the next grid's tail stretched by ~5 us).  It waits for
+  // this grid before it reads or writes anything this grid touches.
   pdl_wait();
+  pdl_launch_dependents();
   float M, L, O;
   merge_partials(c, r, sm, M, L, O);
   if (g != 0) return;
