@@ -51,12 +51,17 @@ WORKLOADS = {
     "long1": dict(layers=1, seqs=1, t_max=32768, window=64),
     "prefill": dict(layers=1, seqs=8, t_max=2048),
     "block28": dict(layers=28, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1),
+    "layer28": dict(layers=28, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1),
 }
 
 BLOCK_METRIC = ("GQA attention block (RMSNorm, Q4_0 QKV + bias, attention, Q4_0 Wo + residual): "
                 "HBM GB/s of KV + weights and tok/s")
 Q4_ROW = (1536 // 32) * 18  # bytes of one Q4_0 row of d_model = 1536 inputs
 BLOCK_WEIGHT_BYTES = (QKV_W + OUT_W) * Q4_ROW + (QKV_W + OUT_W) * 4  # W_qkv, W_o, b_qkv, gamma
+D_FFN = 8960
+FFN_WEIGHT_BYTES = 2 * D_FFN * Q4_ROW + OUT_W * (D_FFN // 32) * 18 + OUT_W * 4  # gate, up, down, gamma
+LAYER_METRIC = ("decoder layer step (attention block + RMSNorm/SwiGLU/down FFN, Q4_0): HBM GB/s "
+                "of KV + weights and tok/s")
 
 PREFILL_METRIC = "GQA causal prefill: bf16 tensor-core TFLOP/s (fp32 accumulation)"
 
@@ -253,6 +258,16 @@ def run_reference_arm(args):
 
 
 def workload_config(name, exchange="peer"):
+    if name == "layer28":
+        return {"workload": "layer28: 28 whole decoder layers per token (attention block as in "
+                            "block28, then RMSNorm, Q4_0 gate/up 8960x1536 with SiLU, Q4_0 down "
+                            "1536x8960 + residual), 1 sequence per GPU, positions 3840..4095, "
+                            "no LM head",
+                "layers": 28, "t_max": 4096, "positions": [3840, 4095],
+                "bytes_per_layer": "2048*(pos+1) KV + %d weights"
+                                   % (BLOCK_WEIGHT_BYTES + FFN_WEIGHT_BYTES),
+                "l2": "KV 235 MB + weights 737 MB per GPU > 126 MB L2; no flush",
+                "parallelism": "sequence-sharded replicas"}
     if name == "block28":
         return {"workload": "block28: 28 attention blocks per token (RMSNorm, Q4_0 QKV 2048x1536 + "
                             "bias, RoPE/append + GQA attention over fp32 KV t_max=4096, Q4_0 Wo "
@@ -377,14 +392,15 @@ def run_resident(args, g, ctx, rank, world, local):
 
 def run_block(args, g, ctx, rank, world, local):
     import torch
-    wl = WORKLOADS["block28"]
+    full = args.workload == "layer28"
+    wl = WORKLOADS[args.workload]
     L_layers, t_max, pos_lo, pos_hi = wl["layers"], wl["t_max"], wl["pos_lo"], wl["pos_hi"]
     seed = 5353 + 1000 * rank
     caches = torch.empty((L_layers, 2, 2, t_max, D), device="cuda")
     ctx.fill_normal(caches, caches.numel(), seed, g.seeded.K_CACHE)
     kvs = [g.kv_of(caches[l, 0], caches[l, 1]) for l in range(L_layers)]
     scale = 1.0 / (4.6 * np.sqrt(OUT_W))
-    keep, ws = [], []
+    keep, ws, fws = [], [], []
     for l in range(L_layers):
         wq = torch.from_numpy(g.seeded.q4_0_matrix(seed + l, g.seeded.W_QKV, QKV_W, OUT_W, scale))
         wo = torch.from_numpy(g.seeded.q4_0_matrix(seed + l, g.seeded.W_O, OUT_W, OUT_W, scale))
@@ -393,6 +409,10 @@ def run_block(args, g, ctx, rank, world, local):
         dev = [wq.cuda(), bq.float().cuda(), wo.cuda(), gm.float().cuda()]
         keep += dev
         ws.append(g.block_weights_of(*dev))
+        if full:
+            fdev = [torch.from_numpy(a).cuda() for a in g.seeded.ffn_block_inputs(seed + l)]
+            keep += fdev
+            fws.append(g.ffn_weights_of(*fdev))
     state0 = torch.empty(OUT_W, device="cuda")
     ctx.fill_normal(state0, OUT_W, seed, g.seeded.STATE)
     state = state0.clone()
@@ -400,20 +420,28 @@ def run_block(args, g, ctx, rank, world, local):
     ctx.reserve(1, t_max)
     n_window = pos_hi - pos_lo
 
+    w_bytes = BLOCK_WEIGHT_BYTES + (FFN_WEIGHT_BYTES if full else 0)
+
     def step_bytes(i):
         pos = pos_lo + i % n_window
-        return L_layers * (ROW_BYTES * (pos + 1) + BLOCK_WEIGHT_BYTES)
+        return L_layers * (ROW_BYTES * (pos + 1) + w_bytes)
+
+    def token_step():
+        if full:
+            ctx.decoder_layers(ws, fws, kvs, state, d_pos, True, pos_lo, pos_hi)
+        else:
+            ctx.attention_block_layers(ws, kvs, state, d_pos, True, pos_lo, pos_hi)
 
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
-        ctx.attention_block_layers(ws, kvs, state, d_pos, True, pos_lo, pos_hi)
+        token_step()
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     cap = torch.cuda.Stream()
     cap.wait_stream(stream)
     with torch.cuda.stream(cap):
         with torch.cuda.graph(graph, stream=cap):
-            ctx.attention_block_layers(ws, kvs, state, d_pos, True, pos_lo, pos_hi)
+            token_step()
     torch.cuda.synchronize()
     graph.replay()
     torch.cuda.synchronize()
@@ -451,40 +479,50 @@ def run_block(args, g, ctx, rank, world, local):
     if ctx.device_status() != 0:
         raise RuntimeError("device status set after the timed regions")
     del graph
-    # per layer: QKV GEMV, split, combine, Wo GEMV; plus the position advance
-    per_step = 4 * L_layers + 1
+    # per layer: QKV GEMV, split, combine, Wo GEMV (+ gate/up, down); plus the position advance
+    per_step = (6 if full else 4) * L_layers + 1
     return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3, bytes=total_bytes,
                 clocks=clk.summary(), launches=per_step * args.steps,
                 launches_per_step=per_step, h2d=OUT_W * 4, d2h=OUT_W * 4, tokens=args.steps,
-                dominant_launches=L_layers * args.steps, metric=BLOCK_METRIC,
-                kernel="decode_split_kernel + gemv_q4_kernel (one attention block)",
+                dominant_launches=L_layers * args.steps,
+                metric=LAYER_METRIC if full else BLOCK_METRIC,
+                kernel="decode_split_kernel + gemv_q4_kernel (one %s)"
+                       % ("decoder layer" if full else "attention block"),
                 data="synthetic: seeded N(0,1) state and KV caches, seeded Q4_0 weights "
                      "(scales for unit-RMS projections)")
 
 
-def cpu_block_run(budget_s, pos_lo=3840, layers=28):
-    """The reference's decoder-layer step with zero FFN weights (the attention
-    block) on the host cores: per step its 28 layer calls in a row, each with
-    the reference's OpenMP GEMVs and serial attention."""
+def cpu_block_run(budget_s, pos_lo=3840, layers=28, full=False):
+    """The reference's decoder-layer step on the host cores -- with zero FFN
+    weights (the attention block) or whole -- per step its 28 layer calls in a
+    row, each with the reference's OpenMP GEMVs and serial attention."""
     import __graft_entry__
     g = __graft_entry__.load_package()
     orc = __graft_entry__.load_oracle()
     if not orc.have_reference():
         return None
     blocks = [g.seeded.attention_block_inputs(900 + l) for l in range(layers)]
+    ffns = [g.seeded.ffn_block_inputs(900 + l) for l in range(layers)] if full else None
     state = blocks[0][0].copy()
+    w_bytes = BLOCK_WEIGHT_BYTES + (FFN_WEIGHT_BYTES if full else 0)
     t0 = time.perf_counter()
     done, nbytes = 0, 0
     while True:
         pos = pos_lo + done % 256
-        for L in blocks:
-            state = orc.ref_attention_block(state, L[1], L[2], L[3], L[4], L[5], L[6], pos, pos + 1)
-        nbytes += layers * (ROW_BYTES * (pos + 1) + BLOCK_WEIGHT_BYTES)
+        for l, L in enumerate(blocks):
+            if full:
+                state = orc.ref_decoder_layer(state, (L[1], L[2], L[3], L[4]), ffns[l], L[5], L[6],
+                                              pos, pos + 1)
+            else:
+                state = orc.ref_attention_block(state, L[1], L[2], L[3], L[4], L[5], L[6], pos,
+                                                pos + 1)
+        nbytes += layers * (ROW_BYTES * (pos + 1) + w_bytes)
         done += 1
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    sample = (f"{done} token step(s) x {layers} attention blocks at positions {pos_lo}.."
+    what = "decoder layers" if full else "attention blocks"
+    sample = (f"{done} token step(s) x {layers} {what} at positions {pos_lo}.."
               f"{pos_lo + min(done, 256) - 1}, the reference's OpenMP GEMVs on "
               f"{os.cpu_count()} threads, attention serial")
     return nbytes / dt / 1e9, os.cpu_count() or 1, sample, "reference", done / dt
@@ -711,7 +749,7 @@ def run_ours(args):
     if args.workload == "prefill":
         return report_prefill(args, run_prefill(args, g, ctx, rank, world, local), ctx, rank,
                               world)
-    if args.workload == "block28":
+    if args.workload in ("block28", "layer28"):
         r = run_block(args, g, ctx, rank, world, local)
     elif args.workload in ("resident28", "single"):
         r = run_resident(args, g, ctx, rank, world, local)
@@ -730,8 +768,8 @@ def run_ours(args):
     achieved = r["bytes"] / r["t"] / 1e9  # this rank's dominant-kernel bytes over its timed region
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        if args.workload == "block28":
-            res = cpu_block_run(budget_s=12.0)
+        if args.workload in ("block28", "layer28"):
+            res = cpu_block_run(budget_s=12.0, full=args.workload == "layer28")
         else:
             res = cpu_reference_run(10 ** 6, 1, budget_s=12.0)
         if res is not None:
@@ -744,7 +782,8 @@ def run_ours(args):
             "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t / args.steps * 1e3, 5), "higher_is_better": True,
-            "scaling": "weak" if args.workload in ("resident28", "single", "block28") else "strong",
+            "scaling": "weak" if args.workload in ("resident28", "single", "block28", "layer28")
+            else "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": r.get("data", "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)"),
             "config": dict(workload_config(args.workload, args.exchange),

@@ -273,6 +273,30 @@ GQA_API int gqa_attention_block_layers(gqa_ctx *ctx, gqa_stream_t stream, int n_
                                        float *state, int *d_pos, int advance, int wrap_lo,
                                        int wrap_hi);
 
+/* Device pointers of one layer's FFN weights (16-byte aligned). */
+typedef struct {
+    const void *w_gate;  /* Q4_0 [d_ffn][d_model / 32] */
+    const void *w_up;    /* Q4_0 [d_ffn][d_model / 32] */
+    const void *w_down;  /* Q4_0 [d_model][d_ffn / 32] */
+    const float *gamma;  /* [d_model] weight of the FFN RMSNorm */
+} gqa_ffn_weights;
+
+/* state += W_down * (silu(W_gate * z) * (W_up * z)), z = rmsnorm(state, gamma):
+ * the FFN half of gpu_decoder_layer_step (qwen_server.c k_rmsnorm_ffn,
+ * k_swiglu_fused, k_down_res; CPU test_28_layers_real.c:298-317), with the
+ * reference's stable SiLU.  d_model = 1536, d_ffn = 8960. */
+GQA_API int gqa_ffn_block(gqa_ctx *ctx, gqa_stream_t stream, const gqa_ffn_weights *w,
+                          float *state);
+
+/* The whole decoder layer (attention block, then FFN block) for n_layers
+ * layers of one token, position on the device as in
+ * gqa_attention_block_layers: the reference's per-token loop over
+ * gpu_decoder_layer_step (qwen_server.c:1021-1023).  Capturable. */
+GQA_API int gqa_decoder_layers(gqa_ctx *ctx, gqa_stream_t stream, int n_layers,
+                               const gqa_block_weights *attn, const gqa_ffn_weights *ffn,
+                               const gqa_layer_kv *kv, float *state, int *d_pos, int advance,
+                               int wrap_lo, int wrap_hi);
+
 /* ---- prefill ---------------------------------------------------------- */
 
 /* Causal attention over whole prompts on the tensor cores (bf16 operands,

@@ -40,8 +40,14 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
                            int* sched, int n_sm, cudaStream_t st);
-int q4_row_bytes();
 int block_d_model();
+int block_d_ffn();
+cudaError_t prepare_block_kernels();
+cudaError_t launch_gateup_gemv(const void* w_gate, const void* w_up, const float* gamma,
+                               const float* state, float* h, int* status, cudaStream_t st,
+                               bool pdl);
+cudaError_t launch_down_gemv(const void* w_down, const float* h, float* state, int* status,
+                             cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_gemv(const void* w, const float* bias, const float* gamma,
                             const float* state, float* qkv, int M, int* status, cudaStream_t st,
                             bool pdl);
@@ -99,6 +105,7 @@ struct gqa_ctx {
   int* counters = nullptr;  // [kMaxCounters + 2] arrival / item counters, kept at zero
   float* blk_qkv = nullptr;   // attention block workspace: qkv of the token
   float* blk_attn = nullptr;  // attention block workspace: attention output
+  float* blk_h = nullptr;     // FFN workspace: silu(gate) * up
   __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
   size_t prefill_cap = 0;                // elements
   float2* rope_cs = nullptr;             // prefill RoPE table [rope_cap][64] (cos, sin)
@@ -337,6 +344,24 @@ int block_impl(gqa_ctx* c, cudaStream_t st, const gqa_block_weights* w, const gq
   return GQA_OK;
 }
 
+int check_ffn_weights(const gqa_ctx* c, const gqa_ffn_weights* w) {
+  if (!w || !w->w_gate || !w->w_up || !w->w_down || !w->gamma)
+    return fail(GQA_ERR_INVALID_ARG, "null FFN weight pointer");
+  if (c->cfg.n_heads_q * kHeadDim != block_d_model())
+    return fail(GQA_ERR_UNSUPPORTED, "FFN block built for d_model %d", block_d_model());
+  if (!aligned16(w->w_gate) || !aligned16(w->w_up) || !aligned16(w->w_down) ||
+      !aligned16(w->gamma))
+    return fail(GQA_ERR_INVALID_ARG, "FFN weights must be 16-byte aligned");
+  return GQA_OK;
+}
+
+int ffn_impl(gqa_ctx* c, cudaStream_t st, const gqa_ffn_weights* w, float* state, bool pdl_first) {
+  GQA_CUDA(launch_gateup_gemv(w->w_gate, w->w_up, w->gamma, state, c->blk_h, c->status, st,
+                              pdl_first));
+  GQA_CUDA(launch_down_gemv(w->w_down, c->blk_h, state, c->status, st, true));
+  return GQA_OK;
+}
+
 // Runs the split kernel of one KV shard (rows [shard_begin, shard_begin +
 // shard_rows) of the sequence, global position pos) and describes its
 // partials in *cp for a merge (cp->n_parts = 0 when the shard attends no row).
@@ -439,6 +464,8 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess)
     e = cudaMalloc(&c->blk_qkv, sizeof(float) * (cfg->n_heads_q + 2 * cfg->n_heads_kv) * kHeadDim);
   if (e == cudaSuccess) e = cudaMalloc(&c->blk_attn, sizeof(float) * cfg->n_heads_q * kHeadDim);
+  if (e == cudaSuccess) e = cudaMalloc(&c->blk_h, sizeof(float) * block_d_ffn());
+  if (e == cudaSuccess) e = prepare_block_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * (kMaxCounters + 2));
   if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * (kMaxCounters + 2));
   if (e == cudaSuccess)
@@ -460,6 +487,7 @@ int gqa_destroy(gqa_ctx* c) {
   if (c->counters) cudaFree(c->counters);
   if (c->blk_qkv) cudaFree(c->blk_qkv);
   if (c->blk_attn) cudaFree(c->blk_attn);
+  if (c->blk_h) cudaFree(c->blk_h);
   if (c->prefill_img) cudaFree(c->prefill_img);
   if (c->rope_cs) cudaFree(c->rope_cs);
   if (c->part_o) cudaFree(c->part_o);
@@ -837,6 +865,43 @@ int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
     // 0's split kernel has passed its wait.
     int rc = block_impl(c, st, &w[l], &kv[l], state, len, c->cfg.t_max,
                         c->layers_pdl != 0, l > 0);
+    if (rc != GQA_OK) return rc;
+  }
+  if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
+  return GQA_OK;
+}
+
+int gqa_ffn_block(gqa_ctx* c, gqa_stream_t stream, const gqa_ffn_weights* w, float* state) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  int rc = check_ffn_weights(c, w);
+  if (rc != GQA_OK) return rc;
+  if (!state || !aligned16(state)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned state");
+  DeviceGuard g(c->device);
+  return ffn_impl(c, (cudaStream_t)stream, w, state, c->pdl != 0);
+}
+
+int gqa_decoder_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers, const gqa_block_weights* attn,
+                       const gqa_ffn_weights* ffn, const gqa_layer_kv* kv, float* state,
+                       int* d_pos, int advance, int wrap_lo, int wrap_hi) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (n_layers < 1 || !attn || !ffn || !kv || !d_pos || !state || !aligned16(state))
+    return fail(GQA_ERR_INVALID_ARG, "gqa_decoder_layers: bad arguments");
+  for (int l = 0; l < n_layers; ++l) {
+    int rc = check_block_weights(c, &attn[l]);
+    if (rc == GQA_OK) rc = check_ffn_weights(c, &ffn[l]);
+    if (rc == GQA_OK) rc = check_kv(c, &kv[l]);
+    if (rc != GQA_OK) return rc;
+  }
+  DeviceGuard g(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  Lengths len{};
+  len.pos_dev = d_pos;
+  for (int l = 0; l < n_layers; ++l) {
+    // Layer 0's split kernel reads pos only after its wait (see
+    // gqa_attention_block_layers); every later kernel starts after it.
+    int rc = block_impl(c, st, &attn[l], &kv[l], state, len, c->cfg.t_max, c->layers_pdl != 0,
+                        l > 0);
+    if (rc == GQA_OK) rc = ffn_impl(c, st, &ffn[l], state, true);
     if (rc != GQA_OK) return rc;
   }
   if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));

@@ -62,6 +62,11 @@ class BlockWeights(ctypes.Structure):
                 ("w_o", ctypes.c_void_p), ("gamma", ctypes.c_void_p)]
 
 
+class FfnWeights(ctypes.Structure):
+    _fields_ = [("w_gate", ctypes.c_void_p), ("w_up", ctypes.c_void_p),
+                ("w_down", ctypes.c_void_p), ("gamma", ctypes.c_void_p)]
+
+
 class LayerKV(ctypes.Structure):
     """One layer's cache: the reference's LayerKVDevice {k_cache, v_cache}."""
     _fields_ = [("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p)]
@@ -102,6 +107,9 @@ _SIGNATURES = {
                             _i, _i],
     "gqa_attention_block_layers": [_vp, _vp, _i, ctypes.POINTER(BlockWeights),
                                    ctypes.POINTER(LayerKV), _vp, _vp, _i, _i, _i],
+    "gqa_ffn_block": [_vp, _vp, ctypes.POINTER(FfnWeights), _vp],
+    "gqa_decoder_layers": [_vp, _vp, _i, ctypes.POINTER(BlockWeights), ctypes.POINTER(FfnWeights),
+                           ctypes.POINTER(LayerKV), _vp, _vp, _i, _i, _i],
     "gqa_exchange_create": [_vp, _i, _i, ctypes.POINTER(_vp), _vp],
     "gqa_exchange_open": [_vp, _vp],
     "gqa_exchange_destroy": [_vp],
@@ -179,6 +187,11 @@ def kv_of(k_cache, v_cache) -> LayerKV:
 def block_weights_of(w_qkv, b_qkv, w_o, gamma) -> BlockWeights:
     """BlockWeights of device tensors (Q4_0 byte tensors and float tensors)."""
     return BlockWeights(_ptr(w_qkv), _ptr(b_qkv), _ptr(w_o), _ptr(gamma))
+
+
+def ffn_weights_of(w_gate, w_up, w_down, gamma) -> FfnWeights:
+    """FfnWeights of device tensors (Q4_0 byte tensors and a float tensor)."""
+    return FfnWeights(_ptr(w_gate), _ptr(w_up), _ptr(w_down), _ptr(gamma))
 
 
 def _kv_array(kvs) -> ctypes.Array:
@@ -386,6 +399,16 @@ class Context:
         _check(lib().gqa_attention_block_layers(self._h, _stream(stream), n, warr, karr,
                                                 _ptr(state), _ptr(d_pos), int(advance), wrap_lo,
                                                 wrap_hi))
+
+    def ffn_block(self, w: "FfnWeights", state, stream=None) -> None:
+        _check(lib().gqa_ffn_block(self._h, _stream(stream), ctypes.byref(w), _ptr(state)))
+
+    def decoder_layers(self, attn, ffn, kvs, state, d_pos, advance: bool = False,
+                       wrap_lo: int = 0, wrap_hi: int = 0, stream=None) -> None:
+        n = len(attn)
+        _check(lib().gqa_decoder_layers(self._h, _stream(stream), n, (BlockWeights * n)(*attn),
+                                        (FfnWeights * n)(*ffn), (LayerKV * n)(*kvs), _ptr(state),
+                                        _ptr(d_pos), int(advance), wrap_lo, wrap_hi))
 
     def lse_combine_packed(self, n_parts: int, n_rows: int, packed, part_stride: int, out,
                            stream=None) -> None:

@@ -28,6 +28,7 @@ _MASK = (1 << 64) - 1
 # same tensor everywhere.
 QKV, K_CACHE, V_CACHE, LENGTHS, PREFILL_Q, PREFILL_K, PREFILL_V = 1, 2, 3, 4, 5, 6, 7
 W_QKV, B_QKV, W_O, GAMMA, STATE = 8, 9, 10, 11, 12
+W_GATE, W_UP, W_DOWN, GAMMA_FFN = 13, 14, 15, 16
 
 Q4_0_BLOCK_BYTES = 18
 
@@ -152,3 +153,15 @@ def attention_block_inputs(seed: int, t_max: int = 4096, d_model: int = 1536, n_
     kc = normal(seed, K_CACHE, n).reshape(n_heads_kv, t_max, 128)
     vc = normal(seed, V_CACHE, n).reshape(n_heads_kv, t_max, 128)
     return state, w_qkv, b_qkv, w_o, gamma, kc, vc
+
+
+def ffn_block_inputs(seed: int, d_model: int = 1536, d_ffn: int = 8960):
+    """(w_gate, w_up, w_down, gamma_ffn) of one layer's FFN: Q4_0 weights
+    scaled for unit-RMS projection rows; gamma ~ 1 + N(0, 0.1^2)."""
+    s_in = 1.0 / (4.6 * np.sqrt(d_model))
+    s_down = 1.0 / (4.6 * np.sqrt(d_ffn))
+    w_gate = q4_0_matrix(seed, W_GATE, d_ffn, d_model, s_in)
+    w_up = q4_0_matrix(seed, W_UP, d_ffn, d_model, s_in)
+    w_down = q4_0_matrix(seed, W_DOWN, d_model, d_ffn, s_down)
+    gamma = (1.0 + 0.1 * normal(seed, GAMMA_FFN, d_model)).astype(np.float32)
+    return w_gate, w_up, w_down, gamma

@@ -243,3 +243,29 @@ def ref_attention_block(x_in, w_qkv, b_qkv, w_o, gamma, k_cache, v_cache, pos, s
     if rc != 0:
         raise ValueError("reference rejected pos/seq_len")
     return out
+
+
+def ref_decoder_layer(x_in, attn, ffn, k_cache, v_cache, pos, seq_len) -> np.ndarray:
+    """The reference's cpu_decoder_layer_step with all weights given:
+    attn = (w_qkv, b_qkv, w_o, gamma_attn), ffn = (w_gate, w_up, w_down,
+    gamma_ffn) as Q4_0 byte arrays / float arrays; caches [2][4096][128]
+    updated in place at row pos."""
+    assert k_cache.shape == (2, REF_T_MAX, 128) and v_cache.shape == (2, REF_T_MAX, 128)
+    w_qkv, b_qkv, w_o, g_a = attn
+    w_gate, w_up, w_down, g_f = ffn
+    arrs = [np.ascontiguousarray(a, dtype=np.uint8) for a in (w_qkv, w_o, w_gate, w_up, w_down)]
+    assert arrs[2].size == 8960 * 48 * 18 and arrs[4].size == 1536 * 280 * 18
+    lib = _load(REF_LAYER_SO)
+    fn = lib.ref_decoder_layer
+    if fn.argtypes is None:
+        _vp = ctypes.c_void_p
+        fn.argtypes = [_fp, _vp, _fp, _vp, _fp, _vp, _vp, _vp, _fp, _fp, _fp, _i, _i, _fp]
+        fn.restype = _i
+    f32 = lambda a: _fptr(np.ascontiguousarray(a, dtype=np.float32))
+    out = np.zeros(1536, dtype=np.float32)
+    rc = fn(f32(x_in), arrs[0].ctypes.data, f32(b_qkv), arrs[1].ctypes.data, f32(g_a),
+            arrs[2].ctypes.data, arrs[3].ctypes.data, arrs[4].ctypes.data, f32(g_f),
+            _fptr(k_cache), _fptr(v_cache), pos, seq_len, _fptr(out))
+    if rc != 0:
+        raise ValueError("reference rejected pos/seq_len")
+    return out

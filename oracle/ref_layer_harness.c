@@ -95,3 +95,25 @@ int ref_attention_block(const float *x_in, const void *w_qkv, const float *b_qkv
     cpu_decoder_layer_step(x_in, &w, &kv, pos, seq_len, y_out);
     return 0;
 }
+
+/* The whole decoder layer with caller-given weights (test_28_layers_real.c:
+ * 192-318): w_gate, w_up [8960][48] and w_down [1536][280] block_q4_0. */
+int ref_decoder_layer(const float *x_in, const void *w_qkv, const float *b_qkv, const void *w_o,
+                      const float *gamma_attn, const void *w_gate, const void *w_up,
+                      const void *w_down, const float *gamma_ffn, float *k_cache, float *v_cache,
+                      int pos, int seq_len, float *y_out) {
+    if (pos < 0 || pos >= T_MAX || seq_len < 1 || seq_len > T_MAX) return -1;
+    LayerWeightsHost w;
+    memset(&w, 0, sizeof(w));
+    w.W_qkv = (block_q4_0 *)w_qkv;
+    w.b_qkv = (float *)b_qkv;
+    w.W_o = (block_q4_0 *)w_o;
+    w.gamma_attn = (float *)gamma_attn;
+    w.W_gate = (block_q4_0 *)w_gate;
+    w.W_up = (block_q4_0 *)w_up;
+    w.W_down = (block_q4_0 *)w_down;
+    w.gamma_ffn = (float *)gamma_ffn;
+    LayerKVHost kv = { k_cache, v_cache };
+    cpu_decoder_layer_step(x_in, &w, &kv, pos, seq_len, y_out);
+    return 0;
+}

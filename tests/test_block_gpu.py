@@ -101,3 +101,73 @@ def test_attention_block_rejects_bad_weights(pkg, cuda):
         bad = pkg.BlockWeights(buf.data_ptr() + 2, f.data_ptr(), buf.data_ptr(), f.data_ptr())
         with pytest.raises(pkg.GqaError):
             ctx.attention_block(bad, pkg.kv_of(k, k), state, 5, 6)
+
+
+def _ffn_device(torch, pkg, wg, wu, wd, gf):
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    dev = [t(wg), t(wu), t(wd), t(gf)]
+    return dev, pkg.ffn_weights_of(*dev)
+
+
+def test_ffn_block_matches_reference(pkg, orc, cuda):
+    """The FFN half alone: the reference layer with a zero attention half
+    (W_qkv = 0, b_qkv = 0, W_o = 0 add exactly 0) is x + FFN(x)."""
+    torch = cuda
+    x, _, _, _, gamma_a, kc, vc = pkg.seeded.attention_block_inputs(31)
+    wg, wu, wd, gf = pkg.seeded.ffn_block_inputs(31)
+    zq = np.zeros(2048 * 48 * 18, np.uint8)
+    zo = np.zeros(1536 * 48 * 18, np.uint8)
+    want = orc.ref_decoder_layer(x, (zq, np.zeros(2048, np.float32), zo, gamma_a),
+                                 (wg, wu, wd, gf), kc.copy(), vc.copy(), 10, 11)
+    with pkg.Context(t_max=4096) as ctx:
+        keep, w = _ffn_device(torch, pkg, wg, wu, wd, gf)
+        state = torch.from_numpy(x).cuda()
+        ctx.ffn_block(w, state)
+        torch.cuda.synchronize()
+        assert ctx.device_status() == 0
+        assert nerr(state.cpu().numpy() - x, want - x) <= TOL
+
+
+def test_decoder_layers_match_reference(pkg, orc, cuda):
+    """Two whole layers per token, two tokens (the second from a CUDA graph
+    replay), position on the device."""
+    torch = cuda
+    n_layers, pos0 = 2, 1500
+    attn = [pkg.seeded.attention_block_inputs(80 + l) for l in range(n_layers)]
+    ffn = [pkg.seeded.ffn_block_inputs(80 + l) for l in range(n_layers)]
+    x0 = attn[0][0]
+    caches = [(A[5].copy(), A[6].copy()) for A in attn]
+    state, want = x0.copy(), []
+    for step in range(2):
+        for l in range(n_layers):
+            A = attn[l]
+            state = orc.ref_decoder_layer(state, (A[1], A[2], A[3], A[4]), ffn[l], caches[l][0],
+                                          caches[l][1], pos0 + step, pos0 + step + 1)
+        want.append(state.copy())
+    with pkg.Context(t_max=4096) as ctx:
+        keep, aw, fw, kvs = [], [], [], []
+        for l in range(n_layers):
+            d1, w1 = _device(torch, pkg, *attn[l][:5])
+            d2, w2 = _ffn_device(torch, pkg, *ffn[l])
+            k, v = torch.from_numpy(attn[l][5]).cuda(), torch.from_numpy(attn[l][6]).cuda()
+            keep += d1 + d2 + [k, v]
+            aw.append(w1)
+            fw.append(w2)
+            kvs.append(pkg.kv_of(k, v))
+        d_pos = torch.tensor([pos0], dtype=torch.int32, device="cuda")
+        st = torch.from_numpy(x0).cuda()
+        ctx.decoder_layers(aw, fw, kvs, st, d_pos, advance=True)
+        torch.cuda.synchronize()
+        assert nerr(st.cpu().numpy() - x0, want[0] - x0) <= TOL
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                ctx.decoder_layers(aw, fw, kvs, st, d_pos, advance=True)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        assert ctx.device_status() == 0
+        assert nerr(st.cpu().numpy() - want[0], want[1] - want[0]) <= TOL
+        del g

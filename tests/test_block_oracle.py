@@ -70,3 +70,37 @@ def test_block_oracle_matches_dense_restatement(pkg, orc):
     want = x + (pkg.seeded.q4_0_dequant(wo, 1536, 1536).astype(np.float64) @ qkv[:1536])
     delta, wdelta = y - x, want - x
     assert np.abs(delta - wdelta).max() / np.sqrt(np.mean(wdelta ** 2)) <= 1e-4
+
+
+def _silu(x):
+    return np.where(x >= 0, x / (1 + np.exp(-np.abs(x))), x * np.exp(-np.abs(x)) / (1 + np.exp(-np.abs(x))))
+
+
+def test_layer_oracle_ffn_matches_dense_restatement(pkg, orc):
+    """With W_qkv = 0, b_qkv = 0, W_o = 0 the attention half adds exactly 0, so
+    the reference layer is x + FFN(x); against a float64 restatement."""
+    if not orc.have_reference():
+        pytest.skip("reference not compiled")
+    x, _, _, _, gamma_a, kc, vc = pkg.seeded.attention_block_inputs(21)
+    zq = np.zeros(2048 * 48 * 18, np.uint8)
+    zo = np.zeros(1536 * 48 * 18, np.uint8)
+    wg, wu, wd, gf = pkg.seeded.ffn_block_inputs(21)
+    y = orc.ref_decoder_layer(x, (zq, np.zeros(2048, np.float32), zo, gamma_a), (wg, wu, wd, gf),
+                              kc.copy(), vc.copy(), 100, 101)
+    z = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2) + 1e-6) * gf
+    g = pkg.seeded.q4_0_dequant(wg, 8960, 1536).astype(np.float64) @ z
+    u = pkg.seeded.q4_0_dequant(wu, 8960, 1536).astype(np.float64) @ z
+    want = x + pkg.seeded.q4_0_dequant(wd, 1536, 8960).astype(np.float64) @ (_silu(g) * u)
+    assert np.abs((y - x) - (want - x)).max() / np.sqrt(np.mean((want - x) ** 2)) <= 1e-4
+
+
+def test_layer_oracle_without_ffn_is_the_block_oracle(pkg, orc):
+    if not orc.have_reference():
+        pytest.skip("reference not compiled")
+    x, wq, bq, wo, gamma, kc, vc = pkg.seeded.attention_block_inputs(22)
+    zg = np.zeros(8960 * 48 * 18, np.uint8)
+    zd = np.zeros(1536 * 280 * 18, np.uint8)
+    y1 = orc.ref_decoder_layer(x, (wq, bq, wo, gamma), (zg, zg, zd, np.ones(1536, np.float32)),
+                               kc.copy(), vc.copy(), 700, 701)
+    y2 = orc.ref_attention_block(x, wq, bq, wo, gamma, kc.copy(), vc.copy(), 700, 701)
+    assert np.array_equal(y1, y2)
