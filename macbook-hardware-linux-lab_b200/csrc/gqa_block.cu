@@ -20,13 +20,17 @@
 // so a CTA's rows are whole 1-D bulk copies).
 //
 // Each CTA owns 8 consecutive output rows, one warp per row (two rows --
-// gate and up -- for kGateUp).  It copies their weights into shared memory
-// (and the RMSNorm weights into registers) before its programmatic-dependency
-// wait -- the weights do not depend on the previous kernel -- then reads the
-// input vector.  Lane 2i + h of a row's warp takes, in each pass, the low
-// (h = 0) or high (h = 1) nibbles of block i + 16 * pass, i.e. 16 weights,
-// with 16-bit code loads and float4 loads of the input; the 32 partial sums
-// meet by shuffles.  Dependents are released after the wait, not before.
+// gate and up -- for kGateUp; for kDown 4 rows, two warps per row, each
+// taking half of K).  It copies their weights into shared memory (and the
+// RMSNorm weights into registers) before its programmatic-dependency wait --
+// the weights do not depend on the previous kernel -- then reads the input
+// vector into shared memory, block b's 32 values rotated by 4b so that the
+// 16 blocks a warp reads at once start on different banks.  Lane 2i + h takes,
+// in each pass, the low (h = 0) or high (h = 1) nibbles of block i + 16 * pass,
+// i.e. 16 weights: the block's scale and codes come from five aligned 32-bit
+// shared loads (the 18-byte blocks sit at 2 or 0 mod 4), the inputs from four
+// float4 loads; the 32 partial sums meet by shuffles.  Dependents are released
+// after the wait, not before.
 #include <cuda_fp16.h>
 
 #include "gqa_common.cuh"
@@ -61,7 +65,9 @@ struct GemvShape {
   static constexpr int K = kMode == kDown ? kDFfn : kDModel;
   static constexpr int kRowBytes = q4_row_bytes_of(K);
   static constexpr int kMats = kMode == kGateUp ? 2 : 1;
-  static constexpr int kWBytes = kMats * kGemvRows * kRowBytes;
+  static constexpr int kSplitK = kMode == kDown ? 2 : 1;       // warps per row
+  static constexpr int kRows = kGemvRows / kSplitK;            // rows per CTA
+  static constexpr int kWBytes = kMats * kRows * kRowBytes + 16;  // + tail for 32-bit reads
   static constexpr int kInPerThread = K / kGemvThreads;
   static constexpr int kBlocks = K / 32;
   static constexpr bool kNorm = kMode == kQkv || kMode == kGateUp;
@@ -82,28 +88,45 @@ __device__ __forceinline__ float silu_ref(float x) {
   return x * ex / (1.0f + ex);
 }
 
-// Dot product of one Q4_0 row held in shared memory with z, by one warp.
-template <int kBlocks>
-__device__ __forceinline__ float warp_row_dot(const uint8_t* wrow, const float* z, int lane) {
+// Shared-memory index of input j: block j / 32 rotated by 4 per block.
+__device__ __forceinline__ int z_index(int j) {
+  const int b = j >> 5;
+  return (b << 5) + (((j & 31) + 4 * b) & 31);
+}
+
+// Dot product of blocks [b_begin, b_end) of one Q4_0 row held in shared
+// memory (row start 16-byte aligned) with z, by one warp.
+__device__ __forceinline__ float warp_row_dot(const uint8_t* wrow, const float* z, int lane,
+                                              int b_begin, int b_end) {
   const int half = lane & 1, shift = 4 * half;
   float acc = 0.f;
 #pragma unroll 3
-  for (int b = lane >> 1; b < kBlocks; b += 16) {
-    const uint8_t* blk = wrow + b * kQ4BlockBytes;
-    const float d = __half2float(*reinterpret_cast<const __half*>(blk));
-    const uint16_t* qs = reinterpret_cast<const uint16_t*>(blk + 2);
-    const float4* z4 = reinterpret_cast<const float4*>(z + 32 * b + 16 * half);
+  for (int b = b_begin + (lane >> 1); b < b_end; b += 16) {
+    // Block b spans bytes [18b, 18b + 18); words from the 4-byte boundary at
+    // or below 18b: an even block starts on it, an odd one 2 bytes past it.
+    const int off = b * kQ4BlockBytes;
+    const uint32_t* wp = reinterpret_cast<const uint32_t*>(wrow + (off & ~3));
+    const uint32_t w0 = wp[0], w1 = wp[1], w2 = wp[2], w3 = wp[3], w4 = wp[4];
+    const bool odd = (off & 3) != 0;
+    const float d = __half2float(__ushort_as_half((unsigned short)(odd ? (w0 >> 16) : w0)));
+    // codes byte 4m .. 4m+3 (block bytes 2 + 4m ..): word m+1 for an odd
+    // block, the upper half of word m and lower half of word m+1 otherwise
+    const uint32_t q[4] = {odd ? w1 : __funnelshift_r(w0, w1, 16),
+                           odd ? w2 : __funnelshift_r(w1, w2, 16),
+                           odd ? w3 : __funnelshift_r(w2, w3, 16),
+                           odd ? w4 : __funnelshift_r(w3, w4, 16)};
+    const int zb = b << 5;
     float a = 0.f;
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
-      const float4 zz = z4[m];
-      const uint32_t v0 = qs[2 * m], v1 = qs[2 * m + 1];
+      const float4 zz =
+          *reinterpret_cast<const float4*>(z + zb + ((16 * half + 4 * m + 4 * b) & 31));
       // weights 4m .. 4m+3 of this half: byte 4m+e holds weight 4m+e (low
       // nibble, half 0) or 16+4m+e (high nibble, half 1)
-      a = fmaf(q4_weight((v0 >> shift) & 15u), zz.x, a);
-      a = fmaf(q4_weight((v0 >> (8 + shift)) & 15u), zz.y, a);
-      a = fmaf(q4_weight((v1 >> shift) & 15u), zz.z, a);
-      a = fmaf(q4_weight((v1 >> (8 + shift)) & 15u), zz.w, a);
+      a = fmaf(q4_weight((q[m] >> shift) & 15u), zz.x, a);
+      a = fmaf(q4_weight((q[m] >> (8 + shift)) & 15u), zz.y, a);
+      a = fmaf(q4_weight((q[m] >> (16 + shift)) & 15u), zz.z, a);
+      a = fmaf(q4_weight((q[m] >> (24 + shift)) & 15u), zz.w, a);
     }
     acc = fmaf(d, a, acc);
   }
@@ -120,21 +143,22 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
   float* sz = reinterpret_cast<float*>(gemv_smem + S::kWBytes);
   float* red = sz + S::K;
   uint64_t* full = reinterpret_cast<uint64_t*>(red + 16);
-  const int tid = threadIdx.x, row = tid >> 5, lane = tid & 31;
-  const int r0 = blockIdx.x * kGemvRows;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row = warp / S::kSplitK, part = warp % S::kSplitK;
+  const int r0 = blockIdx.x * S::kRows;
   if (tid == 0) {
     mbar_init(full, 1);
     fence_barrier_init();
   }
   __syncthreads();
   if (tid == 0) {
-    mbar_arrive_expect_tx(full, S::kWBytes);
+    mbar_arrive_expect_tx(full, S::kMats * S::kRows * S::kRowBytes);
     for (int mat = 0; mat < S::kMats; ++mat) {
       const uint8_t* src = (mat == 0 ? p.w : p.w2) + (size_t)r0 * S::kRowBytes;
       asm volatile(
           "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-          ::"r"(smem_addr(sw + mat * kGemvRows * S::kRowBytes)), "l"(src),
-            "r"(kGemvRows * S::kRowBytes), "r"(smem_addr(full)) : "memory");
+          ::"r"(smem_addr(sw + mat * S::kRows * S::kRowBytes)), "l"(src),
+            "r"(S::kRows * S::kRowBytes), "r"(smem_addr(full)) : "memory");
     }
   }
   float gm[S::kInPerThread];
@@ -142,13 +166,13 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
 #pragma unroll
     for (int k = 0; k < S::kInPerThread; ++k) gm[k] = p.gamma[tid + k * kGemvThreads];
   }
-  const float bias = (kMode == kQkv && lane == 0) ? p.bias[r0 + row] : 0.f;
+  const float bias = (kMode == kQkv && lane == 0 && part == 0) ? p.bias[r0 + row] : 0.f;
   // Dependents are released only once this grid runs for real: launched
   // earlier, their waiting CTAs would hold SM space this grid needs.
   pdl_wait();
   pdl_launch_dependents();
   // The residual this row adds to, loaded now rather than after the dot product.
-  const float resid = (S::kAdd && lane == 0) ? p.y[r0 + row] : 0.f;
+  const float resid = (S::kAdd && lane == 0 && part == 0) ? p.y[r0 + row] : 0.f;
 
   // ---- the input vector (RMSNorm'ed for the QKV and gate/up projections) ----
   float xv[S::kInPerThread];
@@ -160,7 +184,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
     for (int k = 0; k < S::kInPerThread; ++k) ss += xv[k] * xv[k];
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    if (lane == 0) red[row] = ss;
+    if (lane == 0) red[warp] = ss;
     __syncthreads();
     float tot = 0.f;
 #pragma unroll
@@ -170,19 +194,29 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
     for (int k = 0; k < S::kInPerThread; ++k) xv[k] = xv[k] * scale * gm[k];
   }
 #pragma unroll
-  for (int k = 0; k < S::kInPerThread; ++k) sz[tid + k * kGemvThreads] = xv[k];
+  for (int k = 0; k < S::kInPerThread; ++k) sz[z_index(tid + k * kGemvThreads)] = xv[k];
   __syncthreads();
 
   // ---- weights landed? (bounded wait; the copy always completes) ----
-  if (!mbar_wait_bounded(full, 0, kGemvWaitBudget)) {
+  // The decision is made for the whole CTA, which synchronises again below.
+  if (!__syncthreads_and(mbar_wait_bounded(full, 0, kGemvWaitBudget))) {
     if (tid == 0) atomicOr(p.status, kStatusWaitTimeout);
     return;
   }
 
-  const float acc = warp_row_dot<S::kBlocks>(sw + row * S::kRowBytes, sz, lane);
+  constexpr int kPartBlocks = S::kBlocks / S::kSplitK;
+  float acc = warp_row_dot(sw + row * S::kRowBytes, sz, lane, part * kPartBlocks,
+                           (part + 1) * kPartBlocks);
+  if (S::kSplitK > 1) {
+    // the other half of the row's blocks, from the partner warp
+    if (lane == 0) red[8 + warp] = acc;
+    __syncthreads();
+    if (part != 0) return;
+    if (lane == 0) acc += red[8 + warp + 1];
+  }
   float out;
   if (kMode == kGateUp) {
-    const float up = warp_row_dot<S::kBlocks>(sw + (kGemvRows + row) * S::kRowBytes, sz, lane);
+    const float up = warp_row_dot(sw + (S::kRows + row) * S::kRowBytes, sz, lane, 0, S::kBlocks);
     out = silu_ref(acc) * up;
   } else if (kMode == kQkv) {
     out = acc + bias;
@@ -194,9 +228,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
 
 template <int kMode>
 static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t st, bool pdl) {
-  if (p.M % kGemvRows) return cudaErrorInvalidValue;
+  if (p.M % GemvShape<kMode>::kRows) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.M / kGemvRows);
+  cfg.gridDim = dim3(p.M / GemvShape<kMode>::kRows);
   cfg.blockDim = dim3(kGemvThreads);
   cfg.dynamicSmemBytes = GemvShape<kMode>::kSmem;
   cfg.stream = st;
