@@ -52,6 +52,8 @@ WORKLOADS = {
     "prefill": dict(layers=1, seqs=8, t_max=2048),
     "block28": dict(layers=28, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1),
     "layer28": dict(layers=28, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1),
+    "head": dict(layers=0, t_max=1, seqs=1, vocab=151936),
+    "token28": dict(layers=28, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1, vocab=151936),
 }
 
 BLOCK_METRIC = ("GQA attention block (RMSNorm, Q4_0 QKV + bias, attention, Q4_0 Wo + residual): "
@@ -64,6 +66,12 @@ LAYER_METRIC = ("decoder layer step (attention block + RMSNorm/SwiGLU/down FFN, 
                 "of KV + weights and tok/s")
 
 PREFILL_METRIC = "GQA causal prefill: bf16 tensor-core TFLOP/s (fp32 accumulation)"
+VOCAB = 151936
+HEAD_BYTES = VOCAB * 1260 + OUT_W * 4 * 2  # Q6_K output.weight, gamma_output, state
+HEAD_METRIC = ("Q6_K LM head (output RMSNorm, 151936x1536 GEMV, greedy pick): HBM GB/s of "
+               "weights and logits/s")
+TOKEN_METRIC = ("whole-model greedy decode step (Q4_0 embedding, 28 decoder layers, Q6_K LM head, "
+                "pick): tok/s and HBM GB/s of KV + weights")
 
 
 def measured_peak():
@@ -258,6 +266,23 @@ def run_reference_arm(args):
 
 
 def workload_config(name, exchange="peer"):
+    if name == "head":
+        return {"workload": "head: output RMSNorm + Q6_K LM head 151936x1536 (191 MB) + greedy "
+                            "pick, one token's state per step",
+                "vocab": VOCAB, "bytes_per_step": HEAD_BYTES,
+                "l2": "two copies of the head weights used alternately (383 MB > 126 MB L2); "
+                      "no flush",
+                "parallelism": "replicas"}
+    if name == "token28":
+        return {"workload": "token28: one greedy decode step of the whole model per step -- Q4_0 "
+                            "embedding of the previous pick, 28 decoder layers as in layer28, "
+                            "output RMSNorm, Q6_K LM head 151936x1536, pick -- token and position "
+                            "kept on the device, one CUDA graph per step",
+                "layers": 28, "t_max": 4096, "positions": [3840, 4095], "vocab": VOCAB,
+                "bytes_per_step": "28*(2048*(pos+1) + %d) + %d"
+                                  % (BLOCK_WEIGHT_BYTES + FFN_WEIGHT_BYTES, HEAD_BYTES + Q4_ROW),
+                "l2": "KV 235 MB + weights 928 MB per GPU > 126 MB L2; no flush",
+                "parallelism": "sequence-sharded replicas"}
     if name == "layer28":
         return {"workload": "layer28: 28 whole decoder layers per token (attention block as in "
                             "block28, then RMSNorm, Q4_0 gate/up 8960x1536 with SiLU, Q4_0 down "
@@ -490,6 +515,177 @@ def run_block(args, g, ctx, rank, world, local):
                        % ("decoder layer" if full else "attention block"),
                 data="synthetic: seeded N(0,1) state and KV caches, seeded Q4_0 weights "
                      "(scales for unit-RMS projections)")
+
+
+def run_head(args, g, ctx, rank, world, local):
+    """The LM head alone ("head") or the whole greedy decode step ("token28")."""
+    import torch
+    wl = WORKLOADS[args.workload]
+    whole = args.workload == "token28"
+    seed = 6464 + 1000 * rank
+    s = g.seeded
+    w_head, gamma_out, embd = s.head_inputs(seed, VOCAB, OUT_W)
+    n_copies = 1 if whole else 2
+    packed = []
+    raw = torch.from_numpy(w_head).cuda()
+    for _ in range(n_copies):
+        p = torch.empty(g.Context.lm_head_packed_bytes(VOCAB), dtype=torch.uint8, device="cuda")
+        ctx.lm_head_pack(raw, VOCAB, p)
+        packed.append(p)
+    del raw
+    d_gamma = torch.from_numpy(gamma_out).cuda()
+    d_embd = torch.from_numpy(embd).cuda()
+    d_tok = torch.tensor([17], dtype=torch.int32, device="cuda")
+    logits = torch.empty(VOCAB, device="cuda")
+    state0 = torch.empty(OUT_W, device="cuda")
+    ctx.fill_normal(state0, OUT_W, seed, s.STATE)
+    state = state0.clone()
+    keep = []
+    if whole:
+        L_layers, t_max, pos_lo, pos_hi = wl["layers"], wl["t_max"], wl["pos_lo"], wl["pos_hi"]
+        caches = torch.empty((L_layers, 2, 2, t_max, D), device="cuda")
+        ctx.fill_normal(caches, caches.numel(), seed, s.K_CACHE)
+        kvs = [g.kv_of(caches[l, 0], caches[l, 1]) for l in range(L_layers)]
+        scale = 1.0 / (4.6 * np.sqrt(OUT_W))
+        ws, fws = [], []
+        for l in range(L_layers):
+            wq = s.q4_0_matrix(seed + l, s.W_QKV, QKV_W, OUT_W, scale)
+            wo = s.q4_0_matrix(seed + l, s.W_O, OUT_W, OUT_W, scale)
+            bq = (0.1 * s.normal(seed + l, s.B_QKV, QKV_W)).astype(np.float32)
+            gm = (1.0 + 0.1 * s.normal(seed + l, s.GAMMA, OUT_W)).astype(np.float32)
+            dev = [torch.from_numpy(a).cuda() for a in (wq, bq, wo, gm)]
+            fdev = [torch.from_numpy(a).cuda() for a in s.ffn_block_inputs(seed + l)]
+            keep += dev + fdev
+            ws.append(g.block_weights_of(*dev))
+            fws.append(g.ffn_weights_of(*fdev))
+        model = g.ModelHandle(ws, fws, kvs, d_embd, d_gamma, packed[0], VOCAB)
+        d_pos = torch.tensor([pos_lo], dtype=torch.int32, device="cuda")
+        ctx.reserve(1, t_max)
+        n_window = pos_hi - pos_lo
+        w_bytes = BLOCK_WEIGHT_BYTES + FFN_WEIGHT_BYTES
+
+        def step_bytes(i):
+            pos = pos_lo + i % n_window
+            return L_layers * (ROW_BYTES * (pos + 1) + w_bytes) + HEAD_BYTES + Q4_ROW
+
+        def graph_body(i):
+            ctx.decode_token(model, state, d_tok, d_pos, logits, pos_lo, pos_hi)
+    else:
+        def step_bytes(i):
+            return HEAD_BYTES
+
+        def graph_body(i):
+            ctx.lm_head(packed[i % n_copies], VOCAB, d_gamma, state, logits, d_tok)
+
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        graph_body(i)
+    torch.cuda.synchronize()
+    graphs = []
+    cap = torch.cuda.Stream()
+    cap.wait_stream(stream)
+    for i in range(n_copies):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(gr, stream=cap):
+                graph_body(i)
+        graphs.append(gr)
+    torch.cuda.synchronize()
+    for gr in graphs:
+        gr.replay()
+    torch.cuda.synchronize()
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status set during warm-up")
+    if whole:
+        d_pos.fill_(pos_lo)
+    d_tok.fill_(17)
+    state.copy_(state0)
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for i in range(args.steps):
+            graphs[i % n_copies].replay()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    t_local = ev0.elapsed_time(ev1) / 1e3
+    total_bytes = sum(step_bytes(i) for i in range(args.steps))
+
+    # e2e: the previous token in from pinned host memory, the pick out
+    h_tok = torch.tensor([17], dtype=torch.int32).pin_memory()
+    h_out = torch.empty(1, dtype=torch.int32).pin_memory()
+    if whole:
+        d_pos.fill_(pos_lo)
+    state.copy_(state0)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        d_tok.copy_(h_tok, non_blocking=True)
+        graphs[i % n_copies].replay()
+        h_out.copy_(d_tok, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    if ctx.device_status() != 0:
+        raise RuntimeError("device status set after the timed regions")
+    del graphs
+    # embedding, per layer 6 kernels, head, position advance
+    per_step = (1 + 6 * wl["layers"] + 2) if whole else 1
+    return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3, bytes=total_bytes,
+                clocks=clk.summary(), launches=per_step * args.steps,
+                launches_per_step=per_step, h2d=4, d2h=4, tokens=args.steps,
+                dominant_launches=args.steps,
+                metric=TOKEN_METRIC if whole else HEAD_METRIC,
+                kernel="whole decode step" if whole else "lm_head_kernel",
+                head_bytes=HEAD_BYTES,
+                data="synthetic: seeded Q6_K head (uniform codes/scales, fp16 d ~ 2^-12), seeded "
+                     "Q4_0 embedding/layer weights, N(0,1) state and KV caches")
+
+
+def cpu_head_run(budget_s, whole=False, pos_lo=3840, layers=28):
+    """The reference's CPU path on the host cores: its Q6_K GEMV
+    (cpu_gemv_q6_k_ref, OpenMP over rows) after the output norm, with the
+    pick; for the whole step also the embedding lookup and its decoder-layer
+    step 28 times (OpenMP GEMVs, serial attention)."""
+    import __graft_entry__
+    g = __graft_entry__.load_package()
+    orc = __graft_entry__.load_oracle()
+    if not orc.have_reference():
+        return None
+    s = g.seeded
+    w_head = s.q6_k_matrix(901, s.W_HEAD, VOCAB)
+    gamma = (1.0 + 0.1 * s.normal(901, s.GAMMA_OUT, OUT_W)).astype(np.float32)
+    state = s.normal(901, s.STATE, OUT_W)
+    if whole:
+        table = s.q4_0_matrix(901, s.TOKEN_EMBD, VOCAB, OUT_W, 1.0 / 4.6)
+        blocks = [s.attention_block_inputs(900 + l) for l in range(layers)]
+        ffns = [s.ffn_block_inputs(900 + l) for l in range(layers)]
+    tok = 17
+    t0 = time.perf_counter()
+    done, nbytes = 0, 0
+    while True:
+        if whole:
+            pos = pos_lo + done % 256
+            x = orc.ref_token_embedding(table, tok)
+            for l, L in enumerate(blocks):
+                x = orc.ref_decoder_layer(x, (L[1], L[2], L[3], L[4]), ffns[l], L[5], L[6], pos,
+                                          pos + 1)
+            nbytes += layers * (ROW_BYTES * (pos + 1) + BLOCK_WEIGHT_BYTES + FFN_WEIGHT_BYTES)
+            _, tok = orc.ref_lm_head(x, gamma, w_head)
+            nbytes += HEAD_BYTES + Q4_ROW
+        else:
+            _, tok = orc.ref_lm_head(state, gamma, w_head)
+            nbytes += HEAD_BYTES
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    what = ("whole decode step(s): embedding, 28 decoder layers, output norm, Q6_K head, pick"
+            if whole else "LM head call(s): output norm, Q6_K GEMV over 151936 rows, pick")
+    sample = (f"{done} {what}; the reference's OpenMP GEMVs on {os.cpu_count()} threads")
+    return nbytes / dt / 1e9, os.cpu_count() or 1, sample, "reference", done / dt
 
 
 def cpu_block_run(budget_s, pos_lo=3840, layers=28, full=False):
@@ -751,6 +947,8 @@ def run_ours(args):
                               world)
     if args.workload in ("block28", "layer28"):
         r = run_block(args, g, ctx, rank, world, local)
+    elif args.workload in ("head", "token28"):
+        r = run_head(args, g, ctx, rank, world, local)
     elif args.workload in ("resident28", "single"):
         r = run_resident(args, g, ctx, rank, world, local)
     elif args.workload == "long1":
@@ -770,6 +968,8 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if args.workload in ("block28", "layer28"):
             res = cpu_block_run(budget_s=12.0, full=args.workload == "layer28")
+        elif args.workload in ("head", "token28"):
+            res = cpu_head_run(budget_s=12.0, whole=args.workload == "token28")
         else:
             res = cpu_reference_run(10 ** 6, 1, budget_s=12.0)
         if res is not None:
@@ -782,7 +982,8 @@ def run_ours(args):
             "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t / args.steps * 1e3, 5), "higher_is_better": True,
-            "scaling": "weak" if args.workload in ("resident28", "single", "block28", "layer28")
+            "scaling": "weak" if args.workload in ("resident28", "single", "block28", "layer28",
+                                                   "head", "token28")
             else "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": r.get("data", "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)"),

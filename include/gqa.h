@@ -297,6 +297,72 @@ GQA_API int gqa_decoder_layers(gqa_ctx *ctx, gqa_stream_t stream, int n_layers,
                                const gqa_layer_kv *kv, float *state, int *d_pos, int advance,
                                int wrap_lo, int wrap_hi);
 
+/* ---- token embedding, LM head and the whole decode step --------------- */
+
+#define GQA_Q6_K_BLOCK_BYTES 210  /* block_q6_K: 256 weights */
+
+/* Bytes that gqa_lm_head_pack writes for n_rows rows of 1536 inputs: the
+ * size of the GGUF tensor itself, n_rows * 1260. */
+GQA_API long long gqa_lm_head_packed_bytes(int n_rows);
+
+/* Lays a Q6_K matrix out for gqa_lm_head.  q6k: device, n_rows rows of
+ * 1536 / 256 superblocks of 210 bytes (block_q6_K, test_gemv_q6_k.c:21-26),
+ * the bytes of the GGUF tensor output.weight that qwen_server.c uploads whole
+ * (:586-588, d_W_head); packed: device, 16-byte aligned,
+ * gqa_lm_head_packed_bytes(n_rows).  The same bytes in four planes (ql, qh,
+ * scales, d) whose rows are aligned; run once when the weights are loaded. */
+GQA_API int gqa_lm_head_pack(gqa_ctx *ctx, gqa_stream_t stream, const void *q6k, int n_rows,
+                             void *packed);
+
+/* logits[r] = sum_j W[r][j] * z[j] with z = rmsnorm(state) * gamma (epsilon
+ * 1e-6): k_output_norm and the gemv_q6_k LM head of qwen_server.c:1025-1044
+ * (CPU: test_full_model_logits.c:944-958).  When token is given, *token
+ * (device int) receives the greedy pick of the host loop at
+ * qwen_server.c:998-1005: the first row whose logit is the largest one above
+ * -1e30 (NaN never wins), 0 if there is none.  logits may be NULL when only
+ * the pick is wanted; at least one of logits and token must be given.  A
+ * context runs one head at a time (its pick scratch is shared). */
+GQA_API int gqa_lm_head(gqa_ctx *ctx, gqa_stream_t stream, const void *packed, int n_rows,
+                        const float *gamma, const float *state, float *logits, int *token);
+
+/* state = row *d_token of a Q4_0 embedding table [n_rows][1536 / 32 blocks]
+ * (device, the bytes of token_embd.weight): get_token_embedding
+ * (qwen_server.c:188-201) done on the device, so that the token id never
+ * leaves it.  An id outside [0, n_rows) sets GQA_STATUS_BAD_TOKEN in the
+ * device status word and leaves state unchanged. */
+GQA_API int gqa_token_embedding(gqa_ctx *ctx, gqa_stream_t stream, const void *table, int n_rows,
+                                const int *d_token, float *state);
+
+/* Device status bits (gqa_device_status). */
+#define GQA_STATUS_BAD_LENGTH 1   /* a device-side pos / seq_len was out of range */
+#define GQA_STATUS_WAIT_TIMEOUT 2 /* a bounded device wait gave up */
+#define GQA_STATUS_BAD_TOKEN 8    /* a device-side token id was outside the vocabulary */
+
+/* Everything one decode step of the whole model reads (device pointers in
+ * host arrays). */
+typedef struct {
+    int n_layers;
+    const gqa_block_weights *attn;  /* [n_layers] */
+    const gqa_ffn_weights *ffn;     /* [n_layers] */
+    const gqa_layer_kv *kv;         /* [n_layers] */
+    const void *token_embd;         /* Q4_0 [vocab][48 blocks] */
+    const float *gamma_output;      /* [1536] output_norm.weight */
+    const void *lm_head;            /* gqa_lm_head_pack layout of output.weight */
+    int vocab;                      /* rows of token_embd and of the head */
+} gqa_model;
+
+/* One greedy decode step of the whole model without leaving the device: the
+ * token loop of qwen_server.c:1016-1046 -- embedding of *d_token, n_layers
+ * decoder layers at position *d_pos, output norm, LM head, greedy pick -- with
+ * the pick written back to *d_token and *d_pos advanced (wrapping to wrap_lo
+ * at wrap_hi when wrap_hi > 0), so that steps chain on the device and one step
+ * can be captured as a graph.  state: [1536] device workspace; logits: [vocab]
+ * device, or NULL.  The end-of-generation check (:1008) and the position
+ * limit (:1014) stay with the caller, which reads *d_token. */
+GQA_API int gqa_decode_token(gqa_ctx *ctx, gqa_stream_t stream, const gqa_model *model,
+                             float *state, int *d_token, int *d_pos, float *logits, int wrap_lo,
+                             int wrap_hi);
+
 /* ---- prefill ---------------------------------------------------------- */
 
 /* Causal attention over whole prompts on the tensor cores (bf16 operands,

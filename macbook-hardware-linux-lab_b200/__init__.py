@@ -13,5 +13,5 @@ The directory name contains hyphens, so it is loaded by path (see
 """
 from . import seeded, shard  # noqa: F401
 from .gqa import (BlockWeights, Context, Exchange, FfnWeights, GqaError, Graph,  # noqa: F401
-                  LayerKV, block_weights_of, ffn_weights_of, header_functions, kv_of, last_error,
-                  lib)
+                  LayerKV, Model, ModelHandle, block_weights_of, ffn_weights_of, header_functions,
+                  kv_of, last_error, lib)

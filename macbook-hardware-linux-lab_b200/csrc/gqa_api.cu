@@ -57,6 +57,15 @@ size_t exchange_inbox_bytes(int world, int n_rows);
 cudaError_t launch_exchange_combine(const CombineParams& local, uint2* const* inbox,
                                     unsigned* epoch, int rank, int world, float* out, int* status,
                                     cudaStream_t st, bool pdl);
+size_t lm_head_packed_bytes(long long n_rows);
+int lm_head_grid(int n_sm);
+size_t lm_head_best_bytes(int grid);
+cudaError_t launch_q6k_pack(const void* src, int n_rows, void* dst, cudaStream_t st);
+cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, const float* state,
+                           float* logits, int* token, void* best, unsigned* done, int grid,
+                           cudaStream_t st, bool pdl);
+cudaError_t launch_embed_q4(const void* table, int n_rows, const int* token, float* state,
+                            int* status, cudaStream_t st, bool pdl);
 }  // namespace gqa
 
 using namespace gqa;
@@ -102,10 +111,12 @@ struct gqa_ctx {
   // and ~1 us per dependent global round trip for the arrival counter and
   // the final merge).
   int cluster = 0;
-  int* counters = nullptr;  // [kMaxCounters + 2] arrival / item counters, kept at zero
+  int* counters = nullptr;  // [kCounterSlots] arrival / item counters, kept at zero
   float* blk_qkv = nullptr;   // attention block workspace: qkv of the token
   float* blk_attn = nullptr;  // attention block workspace: attention output
   float* blk_h = nullptr;     // FFN workspace: silu(gate) * up
+  void* head_best = nullptr;  // LM head: per-CTA greedy picks
+  int head_grid = 0;          // LM head CTAs
   __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
   size_t prefill_cap = 0;                // elements
   float2* rope_cs = nullptr;             // prefill RoPE table [rope_cap][64] (cos, sin)
@@ -162,6 +173,9 @@ constexpr int kMaxCounters = 1 << 16;   // (sequence, KV head) arrival counters
 // Two counters past the decode range: the prefill's dynamic item counter and
 // its CTA-done counter (both zero between launches).
 constexpr int kPrefillSchedSlot = kMaxCounters;
+// The LM head's CTA arrival counter (zero between launches).
+constexpr int kHeadDoneSlot = kMaxCounters + 2;
+constexpr int kCounterSlots = kMaxCounters + 3;
 
 int ceil_div(long long a, long long b) { return (int)((a + b - 1) / b); }
 
@@ -355,6 +369,15 @@ int check_ffn_weights(const gqa_ctx* c, const gqa_ffn_weights* w) {
   return GQA_OK;
 }
 
+int check_head(const gqa_ctx* c, const void* packed, int n_rows, const float* gamma) {
+  if (c->cfg.n_heads_q * kHeadDim != block_d_model())
+    return fail(GQA_ERR_UNSUPPORTED, "LM head built for d_model %d", block_d_model());
+  if (!packed || !gamma || n_rows < 1)
+    return fail(GQA_ERR_INVALID_ARG, "LM head: null weights or n_rows %d", n_rows);
+  if (!aligned16(packed) || !aligned16(gamma))
+    return fail(GQA_ERR_INVALID_ARG, "LM head weights must be 16-byte aligned");
+  return GQA_OK;
+}
 int ffn_impl(gqa_ctx* c, cudaStream_t st, const gqa_ffn_weights* w, float* state, bool pdl_first) {
   GQA_CUDA(launch_gateup_gemv(w->w_gate, w->w_up, w->gamma, state, c->blk_h, c->status, st,
                               pdl_first));
@@ -466,8 +489,12 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->blk_attn, sizeof(float) * cfg->n_heads_q * kHeadDim);
   if (e == cudaSuccess) e = cudaMalloc(&c->blk_h, sizeof(float) * block_d_ffn());
   if (e == cudaSuccess) e = prepare_block_kernels();
-  if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * (kMaxCounters + 2));
-  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * (kMaxCounters + 2));
+  if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kCounterSlots);
+  if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * kCounterSlots);
+  if (e == cudaSuccess) {
+    c->head_grid = lm_head_grid(c->n_sm);
+    e = cudaMalloc(&c->head_best, lm_head_best_bytes(c->head_grid));
+  }
   if (e == cudaSuccess)
     e = cudaMemcpy(c->inv_freq, c->h_inv_freq, sizeof(float) * kHalf, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(int));
@@ -488,6 +515,7 @@ int gqa_destroy(gqa_ctx* c) {
   if (c->blk_qkv) cudaFree(c->blk_qkv);
   if (c->blk_attn) cudaFree(c->blk_attn);
   if (c->blk_h) cudaFree(c->blk_h);
+  if (c->head_best) cudaFree(c->head_best);
   if (c->prefill_img) cudaFree(c->prefill_img);
   if (c->rope_cs) cudaFree(c->rope_cs);
   if (c->part_o) cudaFree(c->part_o);
@@ -905,6 +933,81 @@ int gqa_decoder_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers, const gqa_
     if (rc != GQA_OK) return rc;
   }
   if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
+  return GQA_OK;
+}
+
+long long gqa_lm_head_packed_bytes(int n_rows) {
+  return n_rows < 1 ? 0 : (long long)lm_head_packed_bytes(n_rows);
+}
+
+int gqa_lm_head_pack(gqa_ctx* c, gqa_stream_t stream, const void* q6k, int n_rows, void* packed) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (!q6k || !packed || n_rows < 1)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_lm_head_pack: null buffer or n_rows %d", n_rows);
+  if (!aligned16(packed)) return fail(GQA_ERR_INVALID_ARG, "packed head must be 16-byte aligned");
+  DeviceGuard g(c->device);
+  GQA_CUDA(launch_q6k_pack(q6k, n_rows, packed, (cudaStream_t)stream));
+  return GQA_OK;
+}
+
+int gqa_lm_head(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
+                const float* gamma, const float* state, float* logits, int* token) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  int rc = check_head(c, packed, n_rows, gamma);
+  if (rc != GQA_OK) return rc;
+  if (!state || !aligned16(state)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned state");
+  if (!logits && !token) return fail(GQA_ERR_INVALID_ARG, "gqa_lm_head: no output requested");
+  DeviceGuard g(c->device);
+  GQA_CUDA(launch_lm_head(packed, n_rows, gamma, state, logits, token, c->head_best,
+                          reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot), c->head_grid,
+                          (cudaStream_t)stream, c->pdl != 0));
+  return GQA_OK;
+}
+
+int gqa_token_embedding(gqa_ctx* c, gqa_stream_t stream, const void* table, int n_rows,
+                        const int* d_token, float* state) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (c->cfg.n_heads_q * kHeadDim != block_d_model())
+    return fail(GQA_ERR_UNSUPPORTED, "embedding built for d_model %d", block_d_model());
+  if (!table || !d_token || !state || n_rows < 1)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_token_embedding: null argument or n_rows %d", n_rows);
+  DeviceGuard g(c->device);
+  GQA_CUDA(launch_embed_q4(table, n_rows, d_token, state, c->status, (cudaStream_t)stream,
+                           c->pdl != 0));
+  return GQA_OK;
+}
+
+int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float* state,
+                     int* d_token, int* d_pos, float* logits, int wrap_lo, int wrap_hi) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (!m || m->n_layers < 1 || !m->attn || !m->ffn || !m->kv || !m->token_embd || !d_token ||
+      !d_pos || !state || !aligned16(state))
+    return fail(GQA_ERR_INVALID_ARG, "gqa_decode_token: bad arguments");
+  int rc = check_head(c, m->lm_head, m->vocab, m->gamma_output);
+  if (rc != GQA_OK) return rc;
+  for (int l = 0; l < m->n_layers; ++l) {
+    rc = check_block_weights(c, &m->attn[l]);
+    if (rc == GQA_OK) rc = check_ffn_weights(c, &m->ffn[l]);
+    if (rc == GQA_OK) rc = check_kv(c, &m->kv[l]);
+    if (rc != GQA_OK) return rc;
+  }
+  DeviceGuard g(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool pdl = c->layers_pdl != 0;
+  GQA_CUDA(launch_embed_q4(m->token_embd, m->vocab, d_token, state, c->status, st, pdl));
+  Lengths len{};
+  len.pos_dev = d_pos;
+  for (int l = 0; l < m->n_layers; ++l) {
+    // Layer 0's split kernel reads pos only after its wait (see
+    // gqa_attention_block_layers); every later kernel starts after it.
+    rc = block_impl(c, st, &m->attn[l], &m->kv[l], state, len, c->cfg.t_max, pdl, l > 0);
+    if (rc == GQA_OK) rc = ffn_impl(c, st, &m->ffn[l], state, pdl);
+    if (rc != GQA_OK) return rc;
+  }
+  GQA_CUDA(launch_lm_head(m->lm_head, m->vocab, m->gamma_output, state, logits, d_token,
+                          c->head_best, reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot),
+                          c->head_grid, st, pdl));
+  GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, pdl));
   return GQA_OK;
 }
 

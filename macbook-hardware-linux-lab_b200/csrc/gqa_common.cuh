@@ -21,6 +21,7 @@ enum : int {
   kStatusBadLength = 1 << 0,    // a device-side pos / seq_len was out of range
   kStatusWaitTimeout = 1 << 1,  // an mbarrier wait ran out of its budget
   kStatusBadSplit = 1 << 2,     // split bookkeeping inconsistent
+  kStatusBadToken = 1 << 3,     // a device-side token id was outside the vocabulary
 };
 
 // ---------------------------------------------------------------------------

@@ -43,6 +43,7 @@ VARIANT_QUANT = {0: 32, 1: 32, 2: 32, 3: 64, 4: 32, 5: 64, 6: 32}
 
 STATUS_BAD_LENGTH = 1
 STATUS_WAIT_TIMEOUT = 2
+STATUS_BAD_TOKEN = 8
 
 
 class GqaError(RuntimeError):
@@ -70,6 +71,14 @@ class FfnWeights(ctypes.Structure):
 class LayerKV(ctypes.Structure):
     """One layer's cache: the reference's LayerKVDevice {k_cache, v_cache}."""
     _fields_ = [("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p)]
+
+
+class Model(ctypes.Structure):
+    """gqa_model: everything one whole-model decode step reads."""
+    _fields_ = [("n_layers", ctypes.c_int), ("attn", ctypes.POINTER(BlockWeights)),
+                ("ffn", ctypes.POINTER(FfnWeights)), ("kv", ctypes.POINTER(LayerKV)),
+                ("token_embd", ctypes.c_void_p), ("gamma_output", ctypes.c_void_p),
+                ("lm_head", ctypes.c_void_p), ("vocab", ctypes.c_int)]
 
 
 _vp = ctypes.c_void_p
@@ -115,6 +124,11 @@ _SIGNATURES = {
     "gqa_exchange_destroy": [_vp],
     "gqa_decode_kv_shard_exchange": [_vp, _vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _i,
                                      _vp],
+    "gqa_lm_head_packed_bytes": [_i],
+    "gqa_lm_head_pack": [_vp, _vp, _vp, _i, _vp],
+    "gqa_lm_head": [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp],
+    "gqa_token_embedding": [_vp, _vp, _vp, _i, _vp, _vp],
+    "gqa_decode_token": [_vp, _vp, ctypes.POINTER(Model), _vp, _vp, _vp, _vp, _i, _i],
     "gqa_prefill_bf16": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
     "gqa_fill_normal": [_vp, _vp, _vp, _ll, _ull, _ull, _ll],
     "gqa_inv_freq": [_vp, ctypes.POINTER(ctypes.c_float)],
@@ -122,7 +136,8 @@ _SIGNATURES = {
     "gqa_layer_attention_static": [ctypes.POINTER(Config), _vp, ctypes.POINTER(LayerKV), _vp, _i,
                                    _i],
 }
-_RESTYPES = {"gqa_last_error_string": ctypes.c_char_p, "gqa_version": ctypes.c_char_p}
+_RESTYPES = {"gqa_last_error_string": ctypes.c_char_p, "gqa_version": ctypes.c_char_p,
+             "gqa_lm_head_packed_bytes": ctypes.c_longlong}
 
 _lib = None
 
@@ -271,6 +286,20 @@ class Exchange:
             pass
 
 
+class ModelHandle:
+    """A gqa_model together with the ctypes arrays it points into."""
+
+    def __init__(self, attn, ffn, kvs, token_embd, gamma_output, lm_head_packed, vocab: int):
+        n = len(attn)
+        assert len(ffn) == n and len(kvs) == n
+        self._attn = (BlockWeights * n)(*attn)
+        self._ffn = (FfnWeights * n)(*ffn)
+        self._kv = (LayerKV * n)(*kvs)
+        self._keep = (token_embd, gamma_output, lm_head_packed)
+        self.struct = Model(n, self._attn, self._ffn, self._kv, _ptr(token_embd),
+                            _ptr(gamma_output), _ptr(lm_head_packed), vocab)
+
+
 class Context:
     """One gqa_ctx on one device (see include/gqa.h for every call)."""
 
@@ -409,6 +438,30 @@ class Context:
         _check(lib().gqa_decoder_layers(self._h, _stream(stream), n, (BlockWeights * n)(*attn),
                                         (FfnWeights * n)(*ffn), (LayerKV * n)(*kvs), _ptr(state),
                                         _ptr(d_pos), int(advance), wrap_lo, wrap_hi))
+
+    # ---- the model's ends and the whole decode step ----
+
+    @staticmethod
+    def lm_head_packed_bytes(n_rows: int) -> int:
+        return int(lib().gqa_lm_head_packed_bytes(n_rows))
+
+    def lm_head_pack(self, q6k, n_rows: int, packed, stream=None) -> None:
+        _check(lib().gqa_lm_head_pack(self._h, _stream(stream), _ptr(q6k), n_rows, _ptr(packed)))
+
+    def lm_head(self, packed, n_rows: int, gamma, state, logits=None, token=None,
+                stream=None) -> None:
+        _check(lib().gqa_lm_head(self._h, _stream(stream), _ptr(packed), n_rows, _ptr(gamma),
+                                 _ptr(state), _ptr(logits), _ptr(token)))
+
+    def token_embedding(self, table, n_rows: int, d_token, state, stream=None) -> None:
+        _check(lib().gqa_token_embedding(self._h, _stream(stream), _ptr(table), n_rows,
+                                         _ptr(d_token), _ptr(state)))
+
+    def decode_token(self, model: "ModelHandle", state, d_token, d_pos, logits=None,
+                     wrap_lo: int = 0, wrap_hi: int = 0, stream=None) -> None:
+        _check(lib().gqa_decode_token(self._h, _stream(stream), ctypes.byref(model.struct),
+                                      _ptr(state), _ptr(d_token), _ptr(d_pos), _ptr(logits),
+                                      wrap_lo, wrap_hi))
 
     def lse_combine_packed(self, n_parts: int, n_rows: int, packed, part_stride: int, out,
                            stream=None) -> None:

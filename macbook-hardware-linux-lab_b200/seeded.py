@@ -29,8 +29,10 @@ _MASK = (1 << 64) - 1
 QKV, K_CACHE, V_CACHE, LENGTHS, PREFILL_Q, PREFILL_K, PREFILL_V = 1, 2, 3, 4, 5, 6, 7
 W_QKV, B_QKV, W_O, GAMMA, STATE = 8, 9, 10, 11, 12
 W_GATE, W_UP, W_DOWN, GAMMA_FFN = 13, 14, 15, 16
+W_HEAD, GAMMA_OUT, TOKEN_EMBD, HEAD_X = 17, 18, 19, 20
 
 Q4_0_BLOCK_BYTES = 18
+Q6_K_BLOCK_BYTES = 210
 
 
 def _mix(z: np.ndarray) -> np.ndarray:
@@ -136,6 +138,63 @@ def q4_0_dequant(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
     q = b[:, 2:].astype(np.int32)
     w = np.concatenate([(q & 15) - 8, (q >> 4) - 8], axis=1).astype(np.float32) * d
     return w.reshape(rows, cols)
+
+
+def q6_k_matrix(seed: int, stream_id: int, rows: int, cols: int = 1536,
+                scale: float = 2.0 ** -12) -> np.ndarray:
+    """A Q6_K matrix [rows][cols / 256 superblocks] as bytes (the reference's
+    block_q6_K: ql[128], qh[64], int8 scales[16], little-endian fp16 d).
+    Superblock s takes splitmix64 outputs 27s .. 27s+26: the first 26 give
+    bytes 0..207 (codes and scales, uniform), the last d = scale * (0.5 + u),
+    u uniform in [0, 1).  With the default scale, d stays a normal fp16 and
+    rows dotted with a unit-RMS input give logits of about 13 RMS."""
+    nb = rows * (cols // 256)
+    u = uniform_u64(seed, stream_id, 27 * nb).reshape(nb, 27)
+    out = np.empty((nb, Q6_K_BLOCK_BYTES), dtype=np.uint8)
+    out[:, :208] = np.ascontiguousarray(u[:, :26]).astype("<u8").view(np.uint8).reshape(nb, 208)
+    frac = (u[:, 26] >> np.uint64(11)).astype(np.float64) / float(1 << 53)
+    d = (scale * (0.5 + frac)).astype(np.float16)
+    out[:, 208:] = d.view(np.uint8).reshape(nb, 2)
+    return out.reshape(-1)
+
+
+def q6_k_dequant(blocks: np.ndarray, rows: int, cols: int = 1536) -> np.ndarray:
+    """Dense float32 [rows][cols] of a Q6_K byte matrix, in the reference's
+    arithmetic: weight (n, c, l) of a superblock = (d * scales[8n + 2c + l/16])
+    * (code - 32), code = ((ql[64n + 32(c & 1) + l] >> 4(c >> 1)) & 15)
+    | ((qh[32n + l] >> 2c) & 3) << 4 (test_gemv_q6_k.c:46-74)."""
+    b = np.asarray(blocks, dtype=np.uint8).reshape(rows * (cols // 256), Q6_K_BLOCK_BYTES)
+    ql = b[:, :128].astype(np.int32)
+    qh = b[:, 128:192].astype(np.int32)
+    sc = b[:, 192:208].view(np.int8).astype(np.float32)
+    d = b[:, 208:210].copy().view(np.float16).astype(np.float32)[:, 0]
+    y = np.empty((b.shape[0], 256), dtype=np.float32)
+    l = np.arange(32)
+    for n in range(2):
+        for c in range(4):
+            lo = (ql[:, 64 * n + 32 * (c & 1) + l] >> (4 * (c >> 1))) & 15
+            hi = (qh[:, 32 * n + l] >> (2 * c)) & 3
+            code = (lo | (hi << 4)) - 32
+            ds = d[:, None] * sc[:, 8 * n + 2 * c + l // 16]
+            y[:, 128 * n + 32 * c + l] = ds * code.astype(np.float32)
+    return y.reshape(rows, cols)
+
+
+def q6_k_planes(blocks: np.ndarray, rows: int) -> np.ndarray:
+    """The byte layout gqa_lm_head_pack writes: ql [rows][768], qh [rows][384],
+    scales [rows][96], d [rows][12] (superblock order kept within each plane)."""
+    b = np.asarray(blocks, dtype=np.uint8).reshape(rows, 6, Q6_K_BLOCK_BYTES)
+    return np.concatenate([b[:, :, :128].reshape(-1), b[:, :, 128:192].reshape(-1),
+                           b[:, :, 192:208].reshape(-1), b[:, :, 208:].reshape(-1)])
+
+
+def head_inputs(seed: int, vocab: int = 151936, d_model: int = 1536):
+    """(w_head Q6_K bytes, gamma_out, token_embd Q4_0 bytes) of the model's
+    ends: gamma_out ~ 1 + N(0, 0.1^2); embedding rows of unit RMS."""
+    w_head = q6_k_matrix(seed, W_HEAD, vocab, d_model)
+    gamma = (1.0 + 0.1 * normal(seed, GAMMA_OUT, d_model)).astype(np.float32)
+    embd = q4_0_matrix(seed, TOKEN_EMBD, vocab, d_model, 1.0 / 4.6)
+    return w_head, gamma, embd
 
 
 def attention_block_inputs(seed: int, t_max: int = 4096, d_model: int = 1536, n_heads_kv: int = 2):

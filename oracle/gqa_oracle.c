@@ -21,7 +21,9 @@
  *                               OpenMP-parallel over (sequence, q head); each
  *                               head's arithmetic is identical to the serial loop.
  */
+#include <immintrin.h>
 #include <math.h>
+#include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
 #include <omp.h>
@@ -309,4 +311,52 @@ void oracle_prefill_rows(const float *q, const float *k, const float *v, int S, 
         free(scores);
     }
     free(qrot);
+}
+
+/* ---- around the decoder layers: embedding, output norm, greedy pick ---- */
+
+/* fp16 -> fp32 as the reference converts it (fp16_to_float,
+ * qwen_server.c:66-68: _cvtsh_ss, F16C). */
+static float oracle_fp16_to_float(uint16_t h) { return _cvtsh_ss(h); }
+
+/* get_token_embedding (qwen_server.c:188-201): row `token` of a Q4_0 table of
+ * d_model / 32 blocks of 18 bytes, x[32b + j] = ((qs[j] & 15) - 8) * d and
+ * x[32b + j + 16] = ((qs[j] >> 4) - 8) * d. */
+void oracle_token_embedding(const uint8_t *table, int d_model, int token, float *x) {
+    int nb = d_model / 32;
+    const uint8_t *row = table + (size_t)token * nb * 18;
+    for (int b = 0; b < nb; b++) {
+        const uint8_t *blk = row + 18 * b;
+        float d = oracle_fp16_to_float((uint16_t)(blk[0] | (blk[1] << 8)));
+        for (int j = 0; j < 16; j++) {
+            uint8_t q = blk[2 + j];
+            x[b * 32 + j] = (float)((int)(q & 0x0F) - 8) * d;
+            x[b * 32 + j + 16] = (float)((int)(q >> 4) - 8) * d;
+        }
+    }
+}
+
+/* The output RMSNorm of the whole-model check (test_full_model_logits.c:
+ * 944-948): fp32 sum of squares in index order, scale = 1 / sqrtf(sum / n +
+ * eps), z = x * scale * gamma. */
+void oracle_output_norm(const float *x, const float *gamma, int n, float eps, float *z) {
+    float sum_sq = 0.0f;
+    for (int i = 0; i < n; i++) sum_sq += x[i] * x[i];
+    float scale = 1.0f / sqrtf((sum_sq / (float)n) + eps);
+    for (int i = 0; i < n; i++) z[i] = x[i] * scale * gamma[i];
+}
+
+/* The server's greedy pick (qwen_server.c:998-1005): best_val starts at
+ * -1e30, a logit replaces it only when strictly larger, so the first row of
+ * the maximum wins, NaN never does, and 0 comes back when nothing beats -1e30. */
+int oracle_greedy_pick(const float *logits, int n) {
+    int best_tok = 0;
+    float best_val = -1e30f;
+    for (int i = 0; i < n; i++) {
+        if (logits[i] > best_val) {
+            best_val = logits[i];
+            best_tok = i;
+        }
+    }
+    return best_tok;
 }

@@ -5,9 +5,12 @@ bench.py, as the checker (never as the thing measured or shipped).
 
 * ``liboracle.so``      -- gqa_oracle.c, the C restatement of the reference's
                            fp32 attention with run-time shapes (any t_max).
-* ``_ref/libgqa_ref_bench.so`` / ``_ref/libgqa_ref_layer.so`` -- the
-  reference's own cpu_attention_gqa_pipeline (attention_gqa_benchmark.c:109-216)
-  and cpu_decoder_layer_step (test_28_layers_real.c:192-318), compiled
+* ``_ref/libgqa_ref_bench.so`` / ``_ref/libgqa_ref_layer.so`` /
+  ``_ref/libgqa_ref_head.so`` / ``_ref/libgqa_ref_model.so`` -- the
+  reference's own cpu_attention_gqa_pipeline (attention_gqa_benchmark.c:
+  109-216), cpu_decoder_layer_step (test_28_layers_real.c:192-318), Q6_K
+  LM-head GEMV cpu_gemv_q6_k_ref (test_gemv_q6_k.c:46-94) and token embedding
+  lookup get_token_embedding (test_full_model_logits.c:584-597), compiled
   unmodified from its sources by oracle/Makefile.  They exist only where the
   reference sources were present at build time; REF_T_MAX = 4096 is their
   compile-time cache stride.
@@ -23,6 +26,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_BENCH_SO = os.path.join(HERE, "_ref", "libgqa_ref_bench.so")
 REF_LAYER_SO = os.path.join(HERE, "_ref", "libgqa_ref_layer.so")
+REF_HEAD_SO = os.path.join(HERE, "_ref", "libgqa_ref_head.so")
+REF_MODEL_SO = os.path.join(HERE, "_ref", "libgqa_ref_model.so")
 REF_T_MAX = 4096
 
 _f = ctypes.c_float
@@ -49,7 +54,7 @@ def _load(path: str) -> ctypes.CDLL:
 
 
 def have_reference() -> bool:
-    return os.path.exists(REF_BENCH_SO) and os.path.exists(REF_LAYER_SO)
+    return all(os.path.exists(p) for p in (REF_BENCH_SO, REF_LAYER_SO, REF_HEAD_SO, REF_MODEL_SO))
 
 
 def _fptr(a: np.ndarray):
@@ -269,3 +274,108 @@ def ref_decoder_layer(x_in, attn, ffn, k_cache, v_cache, pos, seq_len) -> np.nda
     if rc != 0:
         raise ValueError("reference rejected pos/seq_len")
     return out
+
+
+# ---- around the decoder layers: embedding, output norm, LM head, pick -------
+
+Q6_K_ROW_BYTES = 1260  # 6 superblocks of 210 bytes per 1536-wide row
+
+
+def token_embedding(table: np.ndarray, token: int, d_model: int = 1536) -> np.ndarray:
+    """get_token_embedding (qwen_server.c:188-201), restated in gqa_oracle.c."""
+    table = np.ascontiguousarray(table, dtype=np.uint8)
+    assert 0 <= token and (token + 1) * (d_model // 32) * 18 <= table.size
+    fn = _lib().oracle_token_embedding
+    if fn.argtypes is None:
+        fn.argtypes = [ctypes.c_void_p, _i, _i, _fp]
+        fn.restype = None
+    out = np.zeros(d_model, dtype=np.float32)
+    fn(table.ctypes.data, d_model, token, _fptr(out))
+    return out
+
+
+def output_norm(x: np.ndarray, gamma: np.ndarray, eps: float = 1e-6) -> np.ndarray:
+    """The output RMSNorm of test_full_model_logits.c:944-948 (restated)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    gamma = np.ascontiguousarray(gamma, dtype=np.float32)
+    fn = _lib().oracle_output_norm
+    if fn.argtypes is None:
+        fn.argtypes = [_fp, _fp, _i, _f, _fp]
+        fn.restype = None
+    out = np.zeros_like(x)
+    fn(_fptr(x), _fptr(gamma), x.size, eps, _fptr(out))
+    return out
+
+
+def greedy_pick(logits: np.ndarray) -> int:
+    """The server's host argmax (qwen_server.c:998-1005, restated)."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    fn = _lib().oracle_greedy_pick
+    if fn.argtypes is None:
+        fn.argtypes = [_fp, _i]
+        fn.restype = _i
+    return int(fn(_fptr(logits), logits.size))
+
+
+def ref_token_embedding(table: np.ndarray, token: int) -> np.ndarray:
+    """The reference's own get_token_embedding on a Q4_0 table."""
+    table = np.ascontiguousarray(table, dtype=np.uint8).reshape(-1)
+    lib = _load(REF_MODEL_SO)
+    fn = lib.ref_token_embedding
+    if fn.argtypes is None:
+        fn.argtypes = [ctypes.c_void_p, ctypes.c_longlong, _i, _fp]
+        fn.restype = _i
+    out = np.zeros(1536, dtype=np.float32)
+    rc = fn(table.ctypes.data, table.size, token, _fptr(out))
+    if rc != 0:
+        raise ValueError(f"reference embedding lookup failed ({rc})")
+    return out
+
+
+def _head_lib():
+    lib = _load(REF_HEAD_SO)
+    if lib.ref_gemv_q6_k.argtypes is None:
+        lib.ref_gemv_q6_k.argtypes = [ctypes.c_void_p, _fp, _fp, _i]
+        lib.ref_gemv_q6_k.restype = None
+        lib.ref_dequant_q6_k.argtypes = [ctypes.c_void_p, _fp]
+        lib.ref_dequant_q6_k.restype = None
+    return lib
+
+
+def ref_gemv_q6_k(w: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """The reference's cpu_gemv_q6_k_ref: y[r] = dequant(row r) . x in fp32,
+    rows of 1260 bytes (GGUF order)."""
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+    assert w.size % Q6_K_ROW_BYTES == 0
+    m = w.size // Q6_K_ROW_BYTES
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    assert x.size == 1536
+    y = np.zeros(m, dtype=np.float32)
+    _head_lib().ref_gemv_q6_k(w.ctypes.data, _fptr(x), _fptr(y), m)
+    return y
+
+
+def ref_dequant_q6_k(row: np.ndarray) -> np.ndarray:
+    """dequantize_row_q6_k_ref of one 1260-byte row (1536 floats)."""
+    row = np.ascontiguousarray(row, dtype=np.uint8).reshape(-1)
+    assert row.size == Q6_K_ROW_BYTES
+    y = np.zeros(1536, dtype=np.float32)
+    _head_lib().ref_dequant_q6_k(row.ctypes.data, _fptr(y))
+    return y
+
+
+def ref_lm_head(state: np.ndarray, gamma: np.ndarray, w: np.ndarray):
+    """Output norm + the reference's Q6_K GEMV + greedy pick: (logits, token)."""
+    logits = ref_gemv_q6_k(w, output_norm(state, gamma))
+    return logits, greedy_pick(logits)
+
+
+def ref_decode_token(table, layers, kv, gamma_out, w_head, token: int, pos: int):
+    """One greedy step of the whole model on the CPU: embedding of `token`,
+    ref_decoder_layer for every layer (layers[l] = (attn, ffn), kv[l] =
+    (k_cache, v_cache) updated in place at row pos), output norm, Q6_K head,
+    pick.  Returns (logits, next token)."""
+    x = token_embedding(table, token)
+    for (attn, ffn), (kc, vc) in zip(layers, kv):
+        x = ref_decoder_layer(x, attn, ffn, kc, vc, pos, pos + 1)
+    return ref_lm_head(x, gamma_out, w_head)
