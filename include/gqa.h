@@ -302,7 +302,8 @@ GQA_API int gqa_decoder_layers(gqa_ctx *ctx, gqa_stream_t stream, int n_layers,
 #define GQA_Q6_K_BLOCK_BYTES 210  /* block_q6_K: 256 weights */
 
 /* Bytes that gqa_lm_head_pack writes for n_rows rows of 1536 inputs: the
- * size of the GGUF tensor itself, n_rows * 1260. */
+ * size of the GGUF tensor itself with the rows rounded up to a multiple of 4,
+ * 1260 * ((n_rows + 3) / 4 * 4) (for the 151936-row head exactly its size). */
 GQA_API long long gqa_lm_head_packed_bytes(int n_rows);
 
 /* Lays a Q6_K matrix out for gqa_lm_head.  q6k: device, n_rows rows of
@@ -310,7 +311,8 @@ GQA_API long long gqa_lm_head_packed_bytes(int n_rows);
  * the bytes of the GGUF tensor output.weight that qwen_server.c uploads whole
  * (:586-588, d_W_head); packed: device, 16-byte aligned,
  * gqa_lm_head_packed_bytes(n_rows).  The same bytes in four planes (ql, qh,
- * scales, d) whose rows are aligned; run once when the weights are loaded. */
+ * scales, d) whose rows are aligned, padding rows zero; run once when the
+ * weights are loaded. */
 GQA_API int gqa_lm_head_pack(gqa_ctx *ctx, gqa_stream_t stream, const void *q6k, int n_rows,
                              void *packed);
 

@@ -61,9 +61,11 @@ size_t lm_head_packed_bytes(long long n_rows);
 int lm_head_grid(int n_sm);
 size_t lm_head_best_bytes(int grid);
 cudaError_t launch_q6k_pack(const void* src, int n_rows, void* dst, cudaStream_t st);
+cudaError_t prepare_head_kernels();
 cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, const float* state,
-                           float* logits, int* token, void* best, unsigned* done, int grid,
-                           cudaStream_t st, bool pdl);
+                           float* logits, int* token, void* best, unsigned* done, int* status,
+                           int grid, int variant, cudaStream_t st, bool pdl);
+int lm_head_variant_count();
 cudaError_t launch_embed_q4(const void* table, int n_rows, const int* token, float* state,
                             int* status, cudaStream_t st, bool pdl);
 }  // namespace gqa
@@ -117,6 +119,7 @@ struct gqa_ctx {
   float* blk_h = nullptr;     // FFN workspace: silu(gate) * up
   void* head_best = nullptr;  // LM head: per-CTA greedy picks
   int head_grid = 0;          // LM head CTAs
+  int head_variant = 1;       // LM head code-to-float variant (csrc/gqa_head.cu)
   __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
   size_t prefill_cap = 0;                // elements
   float2* rope_cs = nullptr;             // prefill RoPE table [rope_cap][64] (cos, sin)
@@ -489,6 +492,7 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->blk_attn, sizeof(float) * cfg->n_heads_q * kHeadDim);
   if (e == cudaSuccess) e = cudaMalloc(&c->blk_h, sizeof(float) * block_d_ffn());
   if (e == cudaSuccess) e = prepare_block_kernels();
+  if (e == cudaSuccess) e = prepare_head_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kCounterSlots);
   if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * kCounterSlots);
   if (e == cudaSuccess) {
@@ -541,6 +545,11 @@ int gqa_set_option(gqa_ctx* c, int option, long long value) {
       return GQA_OK;
     case 6: /* GQA_OPT_CLUSTER (internal tuning knob) */
       c->cluster = value ? 1 : 0;
+      return GQA_OK;
+    case 7: /* GQA_OPT_HEAD_VARIANT (internal tuning knob) */
+      if (value < 0 || value >= lm_head_variant_count())
+        return fail(GQA_ERR_INVALID_ARG, "head variant out of range");
+      c->head_variant = (int)value;
       return GQA_OK;
     case 4: /* GQA_OPT_KERNEL_VARIANT (internal tuning knob) */
       if (value < -1 || value >= decode_variant_count())
@@ -959,8 +968,8 @@ int gqa_lm_head(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
   if (!logits && !token) return fail(GQA_ERR_INVALID_ARG, "gqa_lm_head: no output requested");
   DeviceGuard g(c->device);
   GQA_CUDA(launch_lm_head(packed, n_rows, gamma, state, logits, token, c->head_best,
-                          reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot), c->head_grid,
-                          (cudaStream_t)stream, c->pdl != 0));
+                          reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot), c->status,
+                          c->head_grid, c->head_variant, (cudaStream_t)stream, c->pdl != 0));
   return GQA_OK;
 }
 
@@ -1006,7 +1015,7 @@ int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float*
   }
   GQA_CUDA(launch_lm_head(m->lm_head, m->vocab, m->gamma_output, state, logits, d_token,
                           c->head_best, reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot),
-                          c->head_grid, st, pdl));
+                          c->status, c->head_grid, c->head_variant, st, pdl));
   GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, pdl));
   return GQA_OK;
 }

@@ -29,8 +29,9 @@
 // in each pass, the low (h = 0) or high (h = 1) nibbles of block i + 16 * pass,
 // i.e. 16 weights: the block's scale and codes come from five aligned 32-bit
 // shared loads (the 18-byte blocks sit at 2 or 0 mod 4), the inputs from four
-// float4 loads; the 32 partial sums meet by shuffles.  Dependents are released
-// after the wait, not before.
+// float4 loads; codes turn into floats four to a word through byte_perm and
+// the products run as f32x2 pairs; the 32 partial sums meet by shuffles.
+// Dependents are released after the wait, not before.
 #include <cuda_fp16.h>
 
 #include "gqa_common.cuh"
@@ -76,11 +77,6 @@ struct GemvShape {
   static constexpr size_t kSmem = (size_t)kWBytes + sizeof(float) * K + 64 + 16;
 };
 
-// Exact float of (code - 8) for a 4-bit code: 2^23 + code, minus 2^23 + 8.
-__device__ __forceinline__ float q4_weight(uint32_t code) {
-  return __uint_as_float(0x4B000000u | code) - 8388616.0f;
-}
-
 // The reference's stable_silu (test_28_layers_real.c:53-60).
 __device__ __forceinline__ float silu_ref(float x) {
   if (x >= 0.0f) return x / (1.0f + expf(-x));
@@ -95,10 +91,14 @@ __device__ __forceinline__ int z_index(int j) {
 }
 
 // Dot product of blocks [b_begin, b_end) of one Q4_0 row held in shared
-// memory (row start 16-byte aligned) with z, by one warp.
+// memory (row start 16-byte aligned) with z, by one warp.  The lane's 16 codes
+// of a block come as four words of four nibbles, one per byte; each code
+// becomes an exact float by byte_perm into 2^23 + code minus 2^23 + 8, and
+// the products run as f32x2 pairs.
 __device__ __forceinline__ float warp_row_dot(const uint8_t* wrow, const float* z, int lane,
                                               int b_begin, int b_end) {
   const int half = lane & 1, shift = 4 * half;
+  const float2 code_off = make_float2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
   float acc = 0.f;
 #pragma unroll 3
   for (int b = b_begin + (lane >> 1); b < b_end; b += 16) {
@@ -116,19 +116,24 @@ __device__ __forceinline__ float warp_row_dot(const uint8_t* wrow, const float* 
                            odd ? w3 : __funnelshift_r(w2, w3, 16),
                            odd ? w4 : __funnelshift_r(w3, w4, 16)};
     const int zb = b << 5;
-    float a = 0.f;
+    float2 a = make_float2(0.f, 0.f);
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
+      // byte e of Q: the code of weight 4m + e of this half (low nibble of
+      // code byte 4m + e for half 0, high nibble for half 1)
+      const uint32_t Q = (q[m] >> shift) & 0x0F0F0F0Fu;
       const float4 zz =
           *reinterpret_cast<const float4*>(z + zb + ((16 * half + 4 * m + 4 * b) & 31));
-      // weights 4m .. 4m+3 of this half: byte 4m+e holds weight 4m+e (low
-      // nibble, half 0) or 16+4m+e (high nibble, half 1)
-      a = fmaf(q4_weight((q[m] >> shift) & 15u), zz.x, a);
-      a = fmaf(q4_weight((q[m] >> (8 + shift)) & 15u), zz.y, a);
-      a = fmaf(q4_weight((q[m] >> (16 + shift)) & 15u), zz.z, a);
-      a = fmaf(q4_weight((q[m] >> (24 + shift)) & 15u), zz.w, a);
+      const float2 w01 = __fadd2_rn(
+          make_float2(__uint_as_float(__byte_perm(Q, 0x4B00u, 0x5440u)),
+                      __uint_as_float(__byte_perm(Q, 0x4B00u, 0x5441u))), code_off);
+      const float2 w23 = __fadd2_rn(
+          make_float2(__uint_as_float(__byte_perm(Q, 0x4B00u, 0x5442u)),
+                      __uint_as_float(__byte_perm(Q, 0x4B00u, 0x5443u))), code_off);
+      a = __ffma2_rn(w01, make_float2(zz.x, zz.y), a);
+      a = __ffma2_rn(w23, make_float2(zz.z, zz.w), a);
     }
-    acc = fmaf(d, a, acc);
+    acc = fmaf(d, a.x + a.y, acc);
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);

@@ -20,20 +20,31 @@
 //
 // A row of 1536 inputs is 6 superblocks, 1260 bytes, so rows and the 210-byte
 // superblocks start on 2-byte boundaries only.  gqa_lm_head_pack therefore
-// lays the same bytes out once, at load time, as four planes:
-//   ql [rows][768]  qh [rows][384]  scales [rows][96]  d [rows][6] (fp16)
-// -- 1260 bytes per row as before, every plane row 4-byte (scales 8-byte)
-// aligned.  Half-superblock hh = 2 * superblock + n of a row is then ql bytes
-// [64hh, 64hh + 64), qh bytes [32hh, 32hh + 32) and scale bytes [8hh, 8hh + 8).
+// lays the same bytes out once, at load time, as four planes over the rows
+// rounded up to a multiple of 4 (Np):
+//   ql [Np][768]  qh [Np][384]  scales [Np][96]  d [Np][6] (fp16)
+// -- 1260 bytes per row as before.  Half-superblock hh = 2 * superblock + n of
+// a row owns ql bytes [64hh, 64hh + 64), qh bytes [32hh, 32hh + 32) and scale
+// bytes [8hh, 8hh + 8); within its ql bytes the two 32-byte halves (quarters
+// 0/2 and 1/3) are swapped when hh & 2, so that the warp's loads below hit 32
+// different shared-memory banks, and its scale bytes are reordered so that
+// scales[8n + 2c + g] sits at 8hh + 4g + c, XOR-ed with 0x80 (offset binary):
+// a lane's four scales are one 32-bit word.  Any run of rows starting on a
+// multiple of 4 is then four 16-byte-aligned runs of bytes.
 //
-// One warp per row, rows interleaved over all warps of the grid.  Lane
-// (hh0 = lane / 8, q = lane % 8) owns, in every row, the three 16-weight units
-// hh = hh0 + 4u (u = 0, 1, 2), l = 4q .. 4q + 3, all four quarters: the units'
-// 48 inputs stay in registers for the whole kernel.  Per unit the lane loads
-// two ql words, one qh word, the half's 8 scale bytes and d; four code words
-// (one byte per weight) come from three AND/OR steps each; each code becomes
-// an exact float by byte_perm into 2^23 + code and a subtraction of 2^23 + 32
-// (the q4 kernels' trick), and the products run as f32x2 pairs.
+// The head kernel is a bulk-copy pipeline: one CTA per SM, a producer warp
+// that copies stages of 16 rows (the four planes' runs, 20160 bytes) into an
+// 8-deep ring of shared-memory stages, starting before the programmatic
+// dependency wait (the weights do not depend on the previous kernel), and 16
+// consumer warps that each take one row of a stage.  Stages go to CTAs
+// round-robin.  Lane (hh0 = lane / 8, q = lane % 8) owns, in every row, the
+// three 16-weight units hh = hh0 + 4u (u = 0, 1, 2), l = 4q .. 4q + 3, all
+// four quarters: the units' 48 inputs stay in registers for the whole kernel.
+// Per unit the lane reads two ql words, one qh word, the half's 8 scale bytes
+// and d; four code words (one byte per weight) come from AND/OR steps; each
+// code becomes an exact float by byte_perm into 2^23 + code minus 2^23 + 32,
+// each scale likewise (2^23 + (scale ^ 0x80) minus 2^23 + 128, no int-to-float
+// unit), and the products run as f32x2 pairs.
 #include <cuda_fp16.h>
 
 #include "gqa_common.cuh"
@@ -48,16 +59,37 @@ constexpr int kQlRow = kQ6Supers * 128;            // plane row bytes
 constexpr int kQhRow = kQ6Supers * 64;
 constexpr int kScRow = kQ6Supers * 16;
 constexpr int kDRow = kQ6Supers * 2;
-constexpr int kHeadThreads = 256;
-constexpr int kHeadWarps = kHeadThreads / 32;
+constexpr int kHeadConsumerWarps = 16;
+constexpr int kHeadConsumers = 32 * kHeadConsumerWarps;
+constexpr int kHeadThreads = kHeadConsumers + 32;  // + the producer warp
+constexpr int kStageRows = kHeadConsumerWarps;     // a row per consumer warp
+constexpr int kHeadStages = 8;
+constexpr int kStQl = kStageRows * kQlRow;
+constexpr int kStQh = kStageRows * kQhRow;
+constexpr int kStSc = kStageRows * kScRow;
+constexpr int kStD = kStageRows * kDRow;
+constexpr int kStageBytes = kStQl + kStQh + kStSc + kStD;  // 20160
 constexpr float kHeadRmsEps = 1e-6f;               // EPSILON of the reference
 constexpr float kNoPick = -1e30f;                  // best_val start of the greedy loop
+constexpr long long kHeadWaitBudget = 2000000000LL;
 constexpr int kEmbedThreads = 256;
 constexpr int kQ4Bytes = 18;
+static_assert(kStageBytes % 16 == 0 && kStQl % 16 == 0 && kStQh % 16 == 0 && kStSc % 16 == 0,
+              "stage runs must stay 16-byte aligned");
 
 struct HeadBest {
   float v;
   int i;
+};
+
+struct HeadSmem {
+  alignas(128) uint8_t stage[kHeadStages][kStageBytes];
+  alignas(16) float sz[kHeadK];
+  float red[kHeadConsumerWarps];
+  HeadBest best[kHeadConsumerWarps];
+  uint64_t full[kHeadStages];
+  uint64_t empty[kHeadStages];
+  int last;
 };
 
 struct HeadParams {
@@ -69,60 +101,60 @@ struct HeadParams {
   int* token;             // greedy pick, or null
   HeadBest* best;         // [gridDim.x] per-CTA picks
   unsigned* done;         // CTA arrival counter, zero between launches
+  int* status;
 };
 
-size_t lm_head_packed_bytes(long long n_rows) { return (size_t)n_rows * kQ6RowBytes; }
+__host__ __device__ constexpr long long head_padded_rows(long long n_rows) {
+  return (n_rows + 3) / 4 * 4;
+}
+
+size_t lm_head_packed_bytes(long long n_rows) {
+  return (size_t)head_padded_rows(n_rows) * kQ6RowBytes;
+}
 
 // ---------------------------------------------------------------------------
-// GGUF rows -> planes (one CTA per row; a load-time step)
+// GGUF rows -> planes (one CTA per row; a load-time step).  Padding rows are
+// written as zeros.
 // ---------------------------------------------------------------------------
 __global__ void q6k_pack_kernel(const uint8_t* __restrict__ src, int n_rows,
                                 uint8_t* __restrict__ dst) {
   const long long r = blockIdx.x;
-  const uint8_t* row = src + r * kQ6RowBytes;
+  const long long np = head_padded_rows(n_rows);
   uint8_t* ql = dst + r * kQlRow;
-  uint8_t* qh = dst + (size_t)n_rows * kQlRow + r * kQhRow;
-  uint8_t* sc = dst + (size_t)n_rows * (kQlRow + kQhRow) + r * kScRow;
-  uint8_t* dd = dst + (size_t)n_rows * (kQlRow + kQhRow + kScRow) + r * kDRow;
+  uint8_t* qh = dst + np * kQlRow + r * kQhRow;
+  uint8_t* sc = dst + np * (kQlRow + kQhRow) + r * kScRow;
+  uint8_t* dd = dst + np * (kQlRow + kQhRow + kScRow) + r * kDRow;
   for (int i = threadIdx.x; i < kQ6RowBytes; i += blockDim.x) {
     const int s = i / kQ6SuperBytes, o = i % kQ6SuperBytes;
-    const uint8_t v = row[i];
-    if (o < 128) ql[128 * s + o] = v;
-    else if (o < 192) qh[64 * s + (o - 128)] = v;
-    else if (o < 208) sc[16 * s + (o - 192)] = v;
-    else dd[2 * s + (o - 208)] = v;
+    const uint8_t v = r < n_rows ? src[r * kQ6RowBytes + i] : 0;
+    if (o < 128) {
+      const int hh = 2 * s + (o >> 6), b = o & 63;
+      ql[64 * hh + (b ^ ((hh & 2) ? 32 : 0))] = v;
+    } else if (o < 192) {
+      qh[64 * s + (o - 128)] = v;
+    } else if (o < 208) {
+      // scales[8n + 2c + g] -> byte 8hh + 4g + c, stored as scale ^ 0x80
+      const int j = o - 192, n = j >> 3, c = (j & 7) >> 1, g = j & 1;
+      sc[8 * (2 * s + n) + 4 * g + c] = v ^ 0x80;
+    } else {
+      dd[2 * s + (o - 208)] = v;
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 // Output RMSNorm + Q6_K LM head + greedy pick
 // ---------------------------------------------------------------------------
-// Exact float of (code - 32) for a code byte of w picked by `sel`
-// (byte_perm selector 0x5440 + byte): 2^23 + code, minus 2^23 + 32.
-constexpr float kQ6Magic = 8388640.0f;
-
-__device__ __forceinline__ float code_f(uint32_t w, uint32_t sel) {
+__device__ __forceinline__ float magic_f(uint32_t w, uint32_t sel) {
   return __uint_as_float(__byte_perm(w, 0x4B00u, sel));
 }
 
-__device__ __forceinline__ void pair_add(float& d0, float& d1, float a0, float a1, float b0,
-                                         float b1) {
-  asm("{\n\t.reg .b64 a, b, d;\n\t"
-      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
-      "add.rn.f32x2 d, a, b;\n\t"
-      "mov.b64 {%0, %1}, d;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+__device__ __forceinline__ void head_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
-__device__ __forceinline__ void pair_fma(float& d0, float& d1, float a0, float a1, float b0,
-                                         float b1, float c0, float c1) {
-  asm("{\n\t.reg .b64 a, b, c, d;\n\t"
-      "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
-      "fma.rn.f32x2 d, a, b, c;\n\t"
-      "mov.b64 {%0, %1}, d;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kHeadConsumers) : "memory");
 }
 
 // Better pick of two: larger value, then smaller row (the host loop's first
@@ -131,147 +163,224 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
-template <int kBatch>
-__global__ void __launch_bounds__(kHeadThreads) lm_head_kernel(const HeadParams p) {
-  __shared__ __align__(16) float sz[kHeadK];
-  __shared__ float red[kHeadWarps];
-  __shared__ HeadBest s_best[kHeadWarps];
-  __shared__ int s_last;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q = lane & 7, hh0 = lane >> 3;
-  const int gsh = (q >> 2) * 8;  // this lane's scale byte within each scale pair
-  const int n_rows = p.n_rows;
-  const uint32_t* ql = reinterpret_cast<const uint32_t*>(p.planes);
-  const uint32_t* qh = reinterpret_cast<const uint32_t*>(p.planes + (size_t)n_rows * kQlRow);
-  const uint2* sc =
-      reinterpret_cast<const uint2*>(p.planes + (size_t)n_rows * (kQlRow + kQhRow));
-  const unsigned short* dd = reinterpret_cast<const unsigned short*>(
-      p.planes + (size_t)n_rows * (kQlRow + kQhRow + kScRow));
+// The consumer lane's fixed part of the row arithmetic.
+struct LaneConst {
+  int hh0, q, o0, o1;   // unit base, 4-weight group, word offsets of W0 / W1
+  int g;                // which 16 of the 32 l values: scale word 2hh + g
+};
 
-  constexpr int kPer = kHeadK / kHeadThreads;
+// Exact floats of the four bytes of w minus `off`: 2^23 + byte through
+// byte_perm, then one f32x2 subtraction per pair (variant 0), or fp16
+// 1024 + byte for a pair per byte_perm, widened with the subtraction (1).
+template <int kVariant>
+__device__ __forceinline__ void bytes_to_floats(uint32_t w, float off, float2& p01, float2& p23) {
+  if (kVariant == 0) {
+    const float2 o = make_float2(-(8388608.0f + off), -(8388608.0f + off));
+    p01 = __fadd2_rn(make_float2(magic_f(w, 0x5440u), magic_f(w, 0x5441u)), o);
+    p23 = __fadd2_rn(make_float2(magic_f(w, 0x5442u), magic_f(w, 0x5443u)), o);
+  } else {
+    const uint32_t b01 = __byte_perm(w, 0x6464u, 0x4140u), b23 = __byte_perm(w, 0x6464u, 0x4342u);
+    const __half2 h01 = *reinterpret_cast<const __half2*>(&b01);
+    const __half2 h23 = *reinterpret_cast<const __half2*>(&b23);
+    const float o = -(1024.0f + off);
+    p01 = make_float2(__low2float(h01) + o, __high2float(h01) + o);
+    p23 = make_float2(__low2float(h23) + o, __high2float(h23) + o);
+  }
+}
+
+// Dot product of one row held in a stage with the lane's inputs (lane's
+// partial sum; the caller reduces over the warp).  x[u][c] holds the inputs
+// of weights 4q .. 4q + 3 of unit u, quarter c, as two pairs.
+template <int kVariant>
+__device__ __forceinline__ float row_dot(const uint8_t* sb, int j, const LaneConst& lc,
+                                         const float2 (&x)[3][4][2]) {
+  const uint32_t* qlw = reinterpret_cast<const uint32_t*>(sb) + j * (kQlRow / 4);
+  const uint32_t* qhw = reinterpret_cast<const uint32_t*>(sb + kStQl) + j * (kQhRow / 4);
+  const uint32_t* scw = reinterpret_cast<const uint32_t*>(sb + kStQl + kStQh) + j * (kScRow / 4);
+  const unsigned short* dw =
+      reinterpret_cast<const unsigned short*>(sb + kStQl + kStQh + kStSc) + j * (kDRow / 2);
+  float acc = 0.f;
+#pragma unroll
+  for (int u = 0; u < 3; ++u) {
+    const int hh = lc.hh0 + 4 * u;
+    const uint32_t W0 = qlw[16 * hh + lc.o0 + lc.q], W1 = qlw[16 * hh + lc.o1 + lc.q];
+    const uint32_t H = qhw[8 * hh + lc.q];
+    const uint32_t sv = scw[2 * hh + lc.g];
+    const float d = __half2float(__ushort_as_half(dw[hh >> 1]));
+    // byte e of Q[c] = 6-bit code of weight (quarter c, l = 4q + e)
+    uint32_t Q[4];
+    Q[0] = (W0 & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
+    Q[1] = (W1 & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
+    Q[2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
+    Q[3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
+    float2 sc01, sc23;  // the quarters' scales (stored offset by 128)
+    bytes_to_floats<kVariant>(sv, 128.0f, sc01, sc23);
+    const float scs[4] = {sc01.x, sc01.y, sc23.x, sc23.y};
+    float2 t = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float2 w01, w23;  // code - 32
+      bytes_to_floats<kVariant>(Q[c], 32.0f, w01, w23);
+      const float2 a = __ffma2_rn(w23, x[u][c][1], __fmul2_rn(w01, x[u][c][0]));
+      t = __ffma2_rn(a, make_float2(scs[c], scs[c]), t);
+    }
+    acc = fmaf(d, t.x + t.y, acc);
+  }
+  return acc;
+}
+
+template <int kVariant>
+__global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadParams p) {
+  extern __shared__ __align__(128) unsigned char head_smem_raw[];
+  HeadSmem& sm = *reinterpret_cast<HeadSmem*>(head_smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_rows = p.n_rows;
+  const long long np = head_padded_rows(n_rows);
+  const int n_stages = (int)((np + kStageRows - 1) / kStageRows);
+  const int grid = gridDim.x;
+  if (tid == 0) {
+    for (int s = 0; s < kHeadStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kHeadConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kHeadConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint8_t* ql = p.planes;
+      const uint8_t* qh = p.planes + np * kQlRow;
+      const uint8_t* sc = p.planes + np * (kQlRow + kQhRow);
+      const uint8_t* dd = p.planes + np * (kQlRow + kQhRow + kScRow);
+      const uint64_t pol = l2_policy_evict_first();
+      int k = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_stages; t += grid, ++k) {
+        const int s = k % kHeadStages;
+        if (k >= kHeadStages &&
+            !mbar_wait_bounded(&sm.empty[s], ((k / kHeadStages) - 1) & 1, kHeadWaitBudget)) {
+          ok = false;
+          break;
+        }
+        const long long r0 = (long long)t * kStageRows;
+        const int nr = (int)min((long long)kStageRows, np - r0);
+        uint8_t* st = sm.stage[s];
+        mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(nr * kQ6RowBytes));
+        bulk_copy_g2s(st, ql + r0 * kQlRow, nr * kQlRow, &sm.full[s], pol);
+        bulk_copy_g2s(st + kStQl, qh + r0 * kQhRow, nr * kQhRow, &sm.full[s], pol);
+        bulk_copy_g2s(st + kStQl + kStQh, sc + r0 * kScRow, nr * kScRow, &sm.full[s], pol);
+        bulk_copy_g2s(st + kStQl + kStQh + kStSc, dd + r0 * kDRow, nr * kDRow, &sm.full[s], pol);
+        if (k == kHeadStages - 1) {
+          pdl_wait();
+          pdl_launch_dependents();
+        }
+      }
+      if (k < kHeadStages) {
+        pdl_wait();
+        pdl_launch_dependents();
+      }
+      if (!ok) atomicOr(p.status, kStatusWaitTimeout);
+      // Every copy issued has landed before the CTA may exit: wait for the
+      // last use of each stage (a no-op when the consumers already did).
+      for (int kk = max(0, k - kHeadStages); kk < k; ++kk)
+        mbar_wait_bounded(&sm.full[kk % kHeadStages], (kk / kHeadStages) & 1, kHeadWaitBudget);
+    } else {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  constexpr int kPer = kHeadK / kHeadConsumers;
   float gm[kPer];
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) gm[k] = p.gamma[tid + k * kHeadThreads];
+  for (int k = 0; k < kPer; ++k) gm[k] = p.gamma[tid + k * kHeadConsumers];
   pdl_wait();
   pdl_launch_dependents();
 
-  // ---- z = rmsnorm(state) * gamma (test_full_model_logits.c:944-948) ----
+  // z = rmsnorm(state) * gamma (test_full_model_logits.c:944-948)
   float xv[kPer];
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
-    xv[k] = p.state[tid + k * kHeadThreads];
+    xv[k] = p.state[tid + k * kHeadConsumers];
     ss += xv[k] * xv[k];
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  if (lane == 0) red[warp] = ss;
-  __syncthreads();
+  if (lane == 0) sm.red[warp] = ss;
+  consumers_sync();
   float tot = 0.f;
 #pragma unroll
-  for (int k = 0; k < kHeadWarps; ++k) tot += red[k];
+  for (int k = 0; k < kHeadConsumerWarps; ++k) tot += sm.red[k];
   const float scale = 1.0f / sqrtf(tot / (float)kHeadK + kHeadRmsEps);
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) sz[tid + k * kHeadThreads] = xv[k] * scale * gm[k];
-  __syncthreads();
+  for (int k = 0; k < kPer; ++k) sm.sz[tid + k * kHeadConsumers] = xv[k] * scale * gm[k];
+  consumers_sync();
 
-  // ---- this lane's 48 inputs: unit u, quarter c, weights 4q .. 4q + 3 ----
-  float x[3][4][4];
+  LaneConst lc;
+  lc.hh0 = lane >> 3;
+  lc.q = lane & 7;
+  lc.o0 = (lc.hh0 & 2) ? 8 : 0;  // the pack swapped the halves of these units
+  lc.o1 = 8 - lc.o0;
+  lc.g = (lane & 7) >> 2;
+  float2 x[3][4][2];
 #pragma unroll
   for (int u = 0; u < 3; ++u)
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const float4 v = *reinterpret_cast<const float4*>(sz + 128 * (hh0 + 4 * u) + 32 * c + 4 * q);
-      x[u][c][0] = v.x;
-      x[u][c][1] = v.y;
-      x[u][c][2] = v.z;
-      x[u][c][3] = v.w;
+      const float4 v =
+          *reinterpret_cast<const float4*>(sm.sz + 128 * (lc.hh0 + 4 * u) + 32 * c + 4 * lc.q);
+      x[u][c][0] = make_float2(v.x, v.y);
+      x[u][c][1] = make_float2(v.z, v.w);
     }
 
-  const int wg = blockIdx.x * kHeadWarps + warp, nw = gridDim.x * kHeadWarps;
   float best_v = kNoPick;
   int best_i = 0;
-  for (int r0 = wg; r0 < n_rows; r0 += nw * kBatch) {
-    uint32_t w0[kBatch][3], w1[kBatch][3], hq[kBatch][3];
-    uint2 s8[kBatch][3];
-    unsigned short dv[kBatch][3];
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      const int r = r0 + b * nw;
-      const bool ok = r < n_rows;
-      const size_t rq = ok ? (size_t)r : 0;
-#pragma unroll
-      for (int u = 0; u < 3; ++u) {
-        const int hh = hh0 + 4 * u;
-        w0[b][u] = __ldg(ql + rq * (kQlRow / 4) + 16 * hh + q);
-        w1[b][u] = __ldg(ql + rq * (kQlRow / 4) + 16 * hh + 8 + q);
-        hq[b][u] = __ldg(qh + rq * (kQhRow / 4) + 8 * hh + q);
-        s8[b][u] = __ldg(sc + rq * (kScRow / 8) + hh);
-        dv[b][u] = __ldg(dd + rq * (kDRow / 2) + (hh >> 1));
-      }
+  bool ok = true;
+  int k = 0;
+  for (int t = blockIdx.x; t < n_stages; t += grid, ++k) {
+    const int s = k % kHeadStages;
+    if (!mbar_wait_bounded(&sm.full[s], (k / kHeadStages) & 1, kHeadWaitBudget)) {
+      ok = false;
+      break;
     }
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      float acc = 0.f;
-#pragma unroll
-      for (int u = 0; u < 3; ++u) {
-        const uint32_t W0 = w0[b][u], W1 = w1[b][u], H = hq[b][u];
-        // byte e of Q[c] = 6-bit code of weight (quarter c, l = 4q + e)
-        uint32_t Q[4];
-        Q[0] = (W0 & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
-        Q[1] = (W1 & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
-        Q[2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
-        Q[3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
-        // scales[8n + 2c + g] of this lane's g: byte 0 / 2 of each 32-bit half
-        const uint32_t slo = s8[b][u].x >> gsh, shi = s8[b][u].y >> gsh;
-        const float scf[4] = {(float)(signed char)(slo & 0xFFu),
-                              (float)(signed char)((slo >> 16) & 0xFFu),
-                              (float)(signed char)(shi & 0xFFu),
-                              (float)(signed char)((shi >> 16) & 0xFFu)};
-        float t0 = 0.f, t1 = 0.f;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float v0, v1, v2, v3;
-          pair_add(v0, v1, code_f(Q[c], 0x5440u), code_f(Q[c], 0x5441u), -kQ6Magic, -kQ6Magic);
-          pair_add(v2, v3, code_f(Q[c], 0x5442u), code_f(Q[c], 0x5443u), -kQ6Magic, -kQ6Magic);
-          float a0, a1;
-          pair_fma(a0, a1, v0, v1, x[u][c][0], x[u][c][1], 0.f, 0.f);
-          pair_fma(a0, a1, v2, v3, x[u][c][2], x[u][c][3], a0, a1);
-          pair_fma(t0, t1, a0, a1, scf[c], scf[c], t0, t1);
-        }
-        const float d = __half2float(__ushort_as_half(dv[b][u]));
-        acc = fmaf(d, t0 + t1, acc);
-      }
+    const int r = t * kStageRows + warp;
+    if (r < n_rows) {
+      float acc = row_dot<kVariant>(sm.stage[s], warp, lc, x);
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-      const int r = r0 + b * nw;
-      if (r < n_rows) {
-        if (p.logits && lane == 0) p.logits[r] = acc;
-        if (acc > best_v) {  // rows rise within a warp: the first maximum stays
-          best_v = acc;
-          best_i = r;
-        }
+      if (p.logits && lane == 0) p.logits[r] = acc;
+      if (acc > best_v) {  // rows rise within a warp: the first maximum stays
+        best_v = acc;
+        best_i = r;
       }
     }
+    __syncwarp();
+    if (lane == 0) head_arrive(&sm.empty[s]);
   }
+  if (!ok && lane == 0) atomicOr(p.status, kStatusWaitTimeout);
   if (!p.token) return;
 
   // ---- greedy pick: warp -> CTA -> grid (the last CTA to arrive) ----
-  if (lane == 0) s_best[warp] = HeadBest{best_v, best_i};
-  __syncthreads();
+  if (lane == 0) sm.best[warp] = HeadBest{best_v, best_i};
+  consumers_sync();
   if (tid == 0) {
-    HeadBest b = s_best[0];
-    for (int w = 1; w < kHeadWarps; ++w)
-      if (better(s_best[w].v, s_best[w].i, b.v, b.i)) b = s_best[w];
+    HeadBest b = sm.best[0];
+    for (int w = 1; w < kHeadConsumerWarps; ++w)
+      if (better(sm.best[w].v, sm.best[w].i, b.v, b.i)) b = sm.best[w];
     p.best[blockIdx.x] = b;
     __threadfence();
-    s_last = atomicAdd(p.done, 1u) == gridDim.x - 1;
+    sm.last = atomicAdd(p.done, 1u) == (unsigned)grid - 1;
   }
-  __syncthreads();
-  if (!s_last) return;
+  consumers_sync();
+  if (!sm.last) return;
   __threadfence();
   HeadBest b{kNoPick, 0};
-  for (int i = tid; i < (int)gridDim.x; i += kHeadThreads) {
+  for (int i = tid; i < grid; i += kHeadConsumers) {
     const float v = __ldcg(&p.best[i].v);
     const int idx = __ldcg(&p.best[i].i);
     if (better(v, idx, b.v, b.i)) b = HeadBest{v, idx};
@@ -282,12 +391,12 @@ __global__ void __launch_bounds__(kHeadThreads) lm_head_kernel(const HeadParams 
     const int idx = __shfl_xor_sync(0xffffffffu, b.i, off);
     if (better(v, idx, b.v, b.i)) b = HeadBest{v, idx};
   }
-  __syncthreads();  // s_best reads above are done
-  if (lane == 0) s_best[warp] = b;
-  __syncthreads();
+  consumers_sync();  // the reads of sm.best above are done
+  if (lane == 0) sm.best[warp] = b;
+  consumers_sync();
   if (tid == 0) {
-    for (int w = 1; w < kHeadWarps; ++w)
-      if (better(s_best[w].v, s_best[w].i, b.v, b.i)) b = s_best[w];
+    for (int w = 1; w < kHeadConsumerWarps; ++w)
+      if (better(sm.best[w].v, sm.best[w].i, b.v, b.i)) b = sm.best[w];
     *p.token = b.i;
     *p.done = 0u;  // ready for the next launch
   }
@@ -321,26 +430,34 @@ __global__ void __launch_bounds__(kEmbedThreads) embed_q4_kernel(const uint8_t* 
 // ---------------------------------------------------------------------------
 // Launchers
 // ---------------------------------------------------------------------------
-constexpr int kHeadBatch = 2;
+int lm_head_grid(int n_sm) { return n_sm; }
 
-int lm_head_grid(int n_sm) {
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, lm_head_kernel<kHeadBatch>,
-                                                    kHeadThreads, 0) != cudaSuccess ||
-      per_sm < 1)
-    per_sm = 1;
-  return n_sm * per_sm;
+constexpr int kHeadVariants = 2;
+using HeadKernel = void (*)(const HeadParams);
+static const HeadKernel kHeadKernels[kHeadVariants] = {lm_head_kernel<0>, lm_head_kernel<1>};
+
+int lm_head_variant_count() { return kHeadVariants; }
+
+cudaError_t prepare_head_kernels() {
+  for (int v = 0; v < kHeadVariants; ++v) {
+    cudaError_t e = cudaFuncSetAttribute((const void*)kHeadKernels[v],
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sizeof(HeadSmem));
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_q6k_pack(const void* src, int n_rows, void* dst, cudaStream_t st) {
-  q6k_pack_kernel<<<n_rows, 256, 0, st>>>(static_cast<const uint8_t*>(src), n_rows,
-                                          static_cast<uint8_t*>(dst));
+  q6k_pack_kernel<<<(unsigned)head_padded_rows(n_rows), 256, 0, st>>>(
+      static_cast<const uint8_t*>(src), n_rows, static_cast<uint8_t*>(dst));
   return cudaGetLastError();
 }
 
 cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, const float* state,
-                           float* logits, int* token, void* best, unsigned* done, int grid,
-                           cudaStream_t st, bool pdl) {
+                           float* logits, int* token, void* best, unsigned* done, int* status,
+                           int grid, int variant, cudaStream_t st, bool pdl) {
+  if (variant < 0 || variant >= kHeadVariants) return cudaErrorInvalidValue;
   HeadParams p{};
   p.planes = static_cast<const uint8_t*>(planes);
   p.n_rows = n_rows;
@@ -350,9 +467,11 @@ cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, c
   p.token = token;
   p.best = static_cast<HeadBest*>(best);
   p.done = done;
+  p.status = status;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kHeadThreads);
+  cfg.dynamicSmemBytes = sizeof(HeadSmem);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -360,7 +479,7 @@ cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, c
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   void* args[] = {&p};
-  return cudaLaunchKernelExC(&cfg, (const void*)lm_head_kernel<kHeadBatch>, args);
+  return cudaLaunchKernelExC(&cfg, (const void*)kHeadKernels[variant], args);
 }
 
 size_t lm_head_best_bytes(int grid) { return sizeof(HeadBest) * (size_t)grid; }

@@ -181,11 +181,23 @@ def q6_k_dequant(blocks: np.ndarray, rows: int, cols: int = 1536) -> np.ndarray:
 
 
 def q6_k_planes(blocks: np.ndarray, rows: int) -> np.ndarray:
-    """The byte layout gqa_lm_head_pack writes: ql [rows][768], qh [rows][384],
-    scales [rows][96], d [rows][12] (superblock order kept within each plane)."""
-    b = np.asarray(blocks, dtype=np.uint8).reshape(rows, 6, Q6_K_BLOCK_BYTES)
-    return np.concatenate([b[:, :, :128].reshape(-1), b[:, :, 128:192].reshape(-1),
-                           b[:, :, 192:208].reshape(-1), b[:, :, 208:].reshape(-1)])
+    """The byte layout gqa_lm_head_pack writes, over the rows rounded up to a
+    multiple of 4 (padding rows zero): ql [Np][768], qh [Np][384], scales
+    [Np][96], d [Np][12], superblock order kept within each plane, except that
+    the two 32-byte halves of half-superblock hh's 64 ql bytes are swapped
+    when hh & 2, and that scales[8n + 2c + g] of a superblock moves to byte
+    8hh + 4g + c of the row (hh = 2 * superblock + n) as scale ^ 0x80."""
+    np_rows = (rows + 3) // 4 * 4
+    b = np.zeros((np_rows, 6, Q6_K_BLOCK_BYTES), dtype=np.uint8)
+    b[:rows] = np.asarray(blocks, dtype=np.uint8).reshape(rows, 6, Q6_K_BLOCK_BYTES)
+    ql = b[:, :, :128].reshape(np_rows, 12, 2, 32).copy()  # [row][hh][half][32]
+    swap = (np.arange(12) & 2) != 0
+    ql[:, swap] = ql[:, swap][:, :, ::-1]
+    sc = b[:, :, 192:208].reshape(np_rows, 6, 2, 4, 2)  # [row][sb][n][c][g]
+    sc = (sc.transpose(0, 1, 2, 4, 3) ^ np.uint8(0x80))      # [row][sb][n][g][c]
+    sc[rows:] = 0
+    return np.concatenate([ql.reshape(-1), b[:, :, 128:192].reshape(-1),
+                           sc.reshape(-1), b[:, :, 208:].reshape(-1)])
 
 
 def head_inputs(seed: int, vocab: int = 151936, d_model: int = 1536):
