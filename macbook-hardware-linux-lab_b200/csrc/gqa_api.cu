@@ -64,8 +64,7 @@ cudaError_t launch_q6k_pack(const void* src, int n_rows, void* dst, cudaStream_t
 cudaError_t prepare_head_kernels();
 cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, const float* state,
                            float* logits, int* token, void* best, unsigned* done, int* status,
-                           int grid, int variant, cudaStream_t st, bool pdl);
-int lm_head_variant_count();
+                           int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_embed_q4(const void* table, int n_rows, const int* token, float* state,
                             int* status, cudaStream_t st, bool pdl);
 }  // namespace gqa
@@ -119,7 +118,6 @@ struct gqa_ctx {
   float* blk_h = nullptr;     // FFN workspace: silu(gate) * up
   void* head_best = nullptr;  // LM head: per-CTA greedy picks
   int head_grid = 0;          // LM head CTAs
-  int head_variant = 1;       // LM head code-to-float variant (csrc/gqa_head.cu)
   __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
   size_t prefill_cap = 0;                // elements
   float2* rope_cs = nullptr;             // prefill RoPE table [rope_cap][64] (cos, sin)
@@ -546,11 +544,6 @@ int gqa_set_option(gqa_ctx* c, int option, long long value) {
     case 6: /* GQA_OPT_CLUSTER (internal tuning knob) */
       c->cluster = value ? 1 : 0;
       return GQA_OK;
-    case 7: /* GQA_OPT_HEAD_VARIANT (internal tuning knob) */
-      if (value < 0 || value >= lm_head_variant_count())
-        return fail(GQA_ERR_INVALID_ARG, "head variant out of range");
-      c->head_variant = (int)value;
-      return GQA_OK;
     case 4: /* GQA_OPT_KERNEL_VARIANT (internal tuning knob) */
       if (value < -1 || value >= decode_variant_count())
         return fail(GQA_ERR_INVALID_ARG, "kernel variant out of range (-1 = automatic)");
@@ -969,7 +962,7 @@ int gqa_lm_head(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
   DeviceGuard g(c->device);
   GQA_CUDA(launch_lm_head(packed, n_rows, gamma, state, logits, token, c->head_best,
                           reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot), c->status,
-                          c->head_grid, c->head_variant, (cudaStream_t)stream, c->pdl != 0));
+                          c->head_grid, (cudaStream_t)stream, c->pdl != 0));
   return GQA_OK;
 }
 
@@ -1015,7 +1008,7 @@ int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float*
   }
   GQA_CUDA(launch_lm_head(m->lm_head, m->vocab, m->gamma_output, state, logits, d_token,
                           c->head_best, reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot),
-                          c->status, c->head_grid, c->head_variant, st, pdl));
+                          c->status, c->head_grid, st, pdl));
   GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, pdl));
   return GQA_OK;
 }

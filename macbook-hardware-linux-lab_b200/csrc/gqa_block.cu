@@ -41,8 +41,6 @@ namespace gqa {
 constexpr int kQ4BlockBytes = 18;
 constexpr int kDModel = 1536;
 constexpr int kDFfn = 8960;
-constexpr int kGemvRows = 8;                  // rows per CTA, a warp each
-constexpr int kGemvThreads = 32 * kGemvRows;
 constexpr float kRmsEps = 1e-6f;              // EPSILON of the reference
 constexpr long long kGemvWaitBudget = 2000000000LL;
 
@@ -66,15 +64,22 @@ struct GemvShape {
   static constexpr int K = kMode == kDown ? kDFfn : kDModel;
   static constexpr int kRowBytes = q4_row_bytes_of(K);
   static constexpr int kMats = kMode == kGateUp ? 2 : 1;
-  static constexpr int kSplitK = kMode == kDown ? 2 : 1;       // warps per row
-  static constexpr int kRows = kGemvRows / kSplitK;            // rows per CTA
+  // The down projection (K = 8960) splits each row over 5 warps, 4 rows per
+  // CTA, for enough warps per SM; the others take a row (or a gate/up pair)
+  // per warp, 8 per CTA.
+  static constexpr int kWarps = kMode == kDown ? 20 : 8;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kSplitK = kMode == kDown ? 5 : 1;       // warps per row
+  static constexpr int kRows = kWarps / kSplitK;               // rows per CTA
   static constexpr int kWBytes = kMats * kRows * kRowBytes + 16;  // + tail for 32-bit reads
-  static constexpr int kInPerThread = K / kGemvThreads;
+  static constexpr int kInPerThread = K / kThreads;
   static constexpr int kBlocks = K / 32;
   static constexpr bool kNorm = kMode == kQkv || kMode == kGateUp;
   static constexpr bool kAdd = kMode == kWo || kMode == kDown;
-  // dynamic shared memory: weights | z[K] | red[16] | full barrier
-  static constexpr size_t kSmem = (size_t)kWBytes + sizeof(float) * K + 64 + 16;
+  static_assert(K % kThreads == 0 && kBlocks % kSplitK == 0, "even split");
+  // dynamic shared memory: weights | z[K] | red[2 * kWarps] | full barrier
+  static constexpr size_t kRedBytes = (sizeof(float) * 2 * kWarps + 15) / 16 * 16;
+  static constexpr size_t kSmem = (size_t)kWBytes + sizeof(float) * K + kRedBytes + 16;
 };
 
 // The reference's stable_silu (test_28_layers_real.c:53-60).
@@ -90,64 +95,74 @@ __device__ __forceinline__ int z_index(int j) {
   return (b << 5) + (((j & 31) + 4 * b) & 31);
 }
 
-// Dot product of blocks [b_begin, b_end) of one Q4_0 row held in shared
-// memory (row start 16-byte aligned) with z, by one warp.  The lane's 16 codes
-// of a block come as four words of four nibbles, one per byte; each code
-// becomes an exact float by byte_perm into 2^23 + code minus 2^23 + 8, and
-// the products run as f32x2 pairs.
-__device__ __forceinline__ float warp_row_dot(const uint8_t* wrow, const float* z, int lane,
-                                              int b_begin, int b_end) {
+// Dot products of blocks [b_begin, b_end) of kN Q4_0 rows held in shared
+// memory (rows 16-byte aligned, row_stride bytes apart) with z, by one warp;
+// the rows share the input loads.  The lane's 16 codes of a block come as
+// four words of four nibbles, one per byte; each code becomes an exact float
+// by byte_perm into 2^23 + code minus 2^23 + 8, and the products run as f32x2
+// pairs.  out[i] is the full sum for row i in every lane.
+template <int kN>
+__device__ __forceinline__ void warp_rows_dot(const uint8_t* wrow, int row_stride, const float* z,
+                                              int lane, int b_begin, int b_end, float (&out)[kN]) {
   const int half = lane & 1, shift = 4 * half;
   const float2 code_off = make_float2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
-  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < kN; ++i) out[i] = 0.f;
 #pragma unroll 3
   for (int b = b_begin + (lane >> 1); b < b_end; b += 16) {
     // Block b spans bytes [18b, 18b + 18); words from the 4-byte boundary at
     // or below 18b: an even block starts on it, an odd one 2 bytes past it.
     const int off = b * kQ4BlockBytes;
-    const uint32_t* wp = reinterpret_cast<const uint32_t*>(wrow + (off & ~3));
-    const uint32_t w0 = wp[0], w1 = wp[1], w2 = wp[2], w3 = wp[3], w4 = wp[4];
     const bool odd = (off & 3) != 0;
-    const float d = __half2float(__ushort_as_half((unsigned short)(odd ? (w0 >> 16) : w0)));
-    // codes byte 4m .. 4m+3 (block bytes 2 + 4m ..): word m+1 for an odd
-    // block, the upper half of word m and lower half of word m+1 otherwise
-    const uint32_t q[4] = {odd ? w1 : __funnelshift_r(w0, w1, 16),
-                           odd ? w2 : __funnelshift_r(w1, w2, 16),
-                           odd ? w3 : __funnelshift_r(w2, w3, 16),
-                           odd ? w4 : __funnelshift_r(w3, w4, 16)};
     const int zb = b << 5;
-    float2 a = make_float2(0.f, 0.f);
+    float4 zz[4];
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      // byte e of Q: the code of weight 4m + e of this half (low nibble of
-      // code byte 4m + e for half 0, high nibble for half 1)
-      const uint32_t Q = (q[m] >> shift) & 0x0F0F0F0Fu;
-      const float4 zz =
-          *reinterpret_cast<const float4*>(z + zb + ((16 * half + 4 * m + 4 * b) & 31));
-      const float2 w01 = __fadd2_rn(
-          make_float2(__uint_as_float(__byte_perm(Q, 0x4B00u, 0x5440u)),
-                      __uint_as_float(__byte_perm(Q, 0x4B00u, 0x5441u))), code_off);
-      const float2 w23 = __fadd2_rn(
-          make_float2(__uint_as_float(__byte_perm(Q, 0x4B00u, 0x5442u)),
-                      __uint_as_float(__byte_perm(Q, 0x4B00u, 0x5443u))), code_off);
-      a = __ffma2_rn(w01, make_float2(zz.x, zz.y), a);
-      a = __ffma2_rn(w23, make_float2(zz.z, zz.w), a);
+    for (int m = 0; m < 4; ++m)
+      zz[m] = *reinterpret_cast<const float4*>(z + zb + ((16 * half + 4 * m + 4 * b) & 31));
+#pragma unroll
+    for (int i = 0; i < kN; ++i) {
+      const uint32_t* wp = reinterpret_cast<const uint32_t*>(wrow + i * row_stride + (off & ~3));
+      const uint32_t w0 = wp[0], w1 = wp[1], w2 = wp[2], w3 = wp[3], w4 = wp[4];
+      const float d = __half2float(__ushort_as_half((unsigned short)(odd ? (w0 >> 16) : w0)));
+      // codes byte 4m .. 4m+3 (block bytes 2 + 4m ..): word m+1 for an odd
+      // block, the upper half of word m and lower half of word m+1 otherwise
+      const uint32_t q[4] = {odd ? w1 : __funnelshift_r(w0, w1, 16),
+                             odd ? w2 : __funnelshift_r(w1, w2, 16),
+                             odd ? w3 : __funnelshift_r(w2, w3, 16),
+                             odd ? w4 : __funnelshift_r(w3, w4, 16)};
+      float2 a = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        // byte e of Q: the code of weight 4m + e of this half (low nibble of
+        // code byte 4m + e for half 0, high nibble for half 1)
+        const uint32_t Q = (q[m] >> shift) & 0x0F0F0F0Fu;
+        const float2 w01 = __fadd2_rn(
+            make_float2(__uint_as_float(__byte_perm(Q, 0x4B00u, 0x5440u)),
+                        __uint_as_float(__byte_perm(Q, 0x4B00u, 0x5441u))), code_off);
+        const float2 w23 = __fadd2_rn(
+            make_float2(__uint_as_float(__byte_perm(Q, 0x4B00u, 0x5442u)),
+                        __uint_as_float(__byte_perm(Q, 0x4B00u, 0x5443u))), code_off);
+        a = __ffma2_rn(w01, make_float2(zz[m].x, zz[m].y), a);
+        a = __ffma2_rn(w23, make_float2(zz[m].z, zz[m].w), a);
+      }
+      out[i] = fmaf(d, a.x + a.y, out[i]);
     }
-    acc = fmaf(d, a.x + a.y, acc);
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  return acc;
+  for (int i = 0; i < kN; ++i)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) out[i] += __shfl_xor_sync(0xffffffffu, out[i], off);
 }
 
 template <int kMode>
-__global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GemvShape<kMode>::kThreads) gemv_q4_kernel(const GemvParams p) {
   using S = GemvShape<kMode>;
   extern __shared__ __align__(128) unsigned char gemv_smem[];
   uint8_t* sw = gemv_smem;
   float* sz = reinterpret_cast<float*>(gemv_smem + S::kWBytes);
   float* red = sz + S::K;
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + 16);
+  uint64_t* full = reinterpret_cast<uint64_t*>(gemv_smem + S::kWBytes + sizeof(float) * S::K +
+                                               S::kRedBytes);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int row = warp / S::kSplitK, part = warp % S::kSplitK;
   const int r0 = blockIdx.x * S::kRows;
@@ -169,7 +184,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
   float gm[S::kInPerThread];
   if (S::kNorm) {
 #pragma unroll
-    for (int k = 0; k < S::kInPerThread; ++k) gm[k] = p.gamma[tid + k * kGemvThreads];
+    for (int k = 0; k < S::kInPerThread; ++k) gm[k] = p.gamma[tid + k * S::kThreads];
   }
   const float bias = (kMode == kQkv && lane == 0 && part == 0) ? p.bias[r0 + row] : 0.f;
   // Dependents are released only once this grid runs for real: launched
@@ -182,7 +197,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
   // ---- the input vector (RMSNorm'ed for the QKV and gate/up projections) ----
   float xv[S::kInPerThread];
 #pragma unroll
-  for (int k = 0; k < S::kInPerThread; ++k) xv[k] = p.x[tid + k * kGemvThreads];
+  for (int k = 0; k < S::kInPerThread; ++k) xv[k] = p.x[tid + k * S::kThreads];
   if (S::kNorm) {
     float ss = 0.f;
 #pragma unroll
@@ -193,13 +208,13 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
     __syncthreads();
     float tot = 0.f;
 #pragma unroll
-    for (int k = 0; k < kGemvThreads / 32; ++k) tot += red[k];
+    for (int k = 0; k < S::kWarps; ++k) tot += red[k];
     const float scale = 1.0f / sqrtf(tot / (float)S::K + kRmsEps);
 #pragma unroll
     for (int k = 0; k < S::kInPerThread; ++k) xv[k] = xv[k] * scale * gm[k];
   }
 #pragma unroll
-  for (int k = 0; k < S::kInPerThread; ++k) sz[z_index(tid + k * kGemvThreads)] = xv[k];
+  for (int k = 0; k < S::kInPerThread; ++k) sz[z_index(tid + k * S::kThreads)] = xv[k];
   __syncthreads();
 
   // ---- weights landed? (bounded wait; the copy always completes) ----
@@ -210,23 +225,25 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvParams 
   }
 
   constexpr int kPartBlocks = S::kBlocks / S::kSplitK;
-  float acc = warp_row_dot(sw + row * S::kRowBytes, sz, lane, part * kPartBlocks,
-                           (part + 1) * kPartBlocks);
+  float acc[S::kMats];
+  warp_rows_dot<S::kMats>(sw + row * S::kRowBytes, S::kRows * S::kRowBytes, sz, lane,
+                          part * kPartBlocks, (part + 1) * kPartBlocks, acc);
   if (S::kSplitK > 1) {
-    // the other half of the row's blocks, from the partner warp
-    if (lane == 0) red[8 + warp] = acc;
+    // the other parts of the row's blocks, from the row's other warps
+    if (lane == 0) red[S::kWarps + warp] = acc[0];
     __syncthreads();
     if (part != 0) return;
-    if (lane == 0) acc += red[8 + warp + 1];
+    if (lane == 0)
+#pragma unroll
+      for (int k = 1; k < S::kSplitK; ++k) acc[0] += red[S::kWarps + warp + k];
   }
   float out;
   if (kMode == kGateUp) {
-    const float up = warp_row_dot(sw + (S::kRows + row) * S::kRowBytes, sz, lane, 0, S::kBlocks);
-    out = silu_ref(acc) * up;
+    out = silu_ref(acc[0]) * acc[S::kMats - 1];
   } else if (kMode == kQkv) {
-    out = acc + bias;
+    out = acc[0] + bias;
   } else {
-    out = resid + acc;
+    out = resid + acc[0];
   }
   if (lane == 0) p.y[r0 + row] = out;
 }
@@ -236,7 +253,7 @@ static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t st, bool pdl) {
   if (p.M % GemvShape<kMode>::kRows) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.M / GemvShape<kMode>::kRows);
-  cfg.blockDim = dim3(kGemvThreads);
+  cfg.blockDim = dim3(GemvShape<kMode>::kThreads);
   cfg.dynamicSmemBytes = GemvShape<kMode>::kSmem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

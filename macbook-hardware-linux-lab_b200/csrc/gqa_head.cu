@@ -170,28 +170,19 @@ struct LaneConst {
 };
 
 // Exact floats of the four bytes of w minus `off`: 2^23 + byte through
-// byte_perm, then one f32x2 subtraction per pair (variant 0), or fp16
-// 1024 + byte for a pair per byte_perm, widened with the subtraction (1).
-template <int kVariant>
+// byte_perm, then one f32x2 subtraction per pair.  (An fp16 form -- 1024 +
+// byte, two bytes per byte_perm, widened with the subtraction -- halves the
+// byte_perm count but measured slower on B200: 59.4 against 55.5 us per
+// head, the widening moving the load onto the FMA pipe.)
 __device__ __forceinline__ void bytes_to_floats(uint32_t w, float off, float2& p01, float2& p23) {
-  if (kVariant == 0) {
-    const float2 o = make_float2(-(8388608.0f + off), -(8388608.0f + off));
-    p01 = __fadd2_rn(make_float2(magic_f(w, 0x5440u), magic_f(w, 0x5441u)), o);
-    p23 = __fadd2_rn(make_float2(magic_f(w, 0x5442u), magic_f(w, 0x5443u)), o);
-  } else {
-    const uint32_t b01 = __byte_perm(w, 0x6464u, 0x4140u), b23 = __byte_perm(w, 0x6464u, 0x4342u);
-    const __half2 h01 = *reinterpret_cast<const __half2*>(&b01);
-    const __half2 h23 = *reinterpret_cast<const __half2*>(&b23);
-    const float o = -(1024.0f + off);
-    p01 = make_float2(__low2float(h01) + o, __high2float(h01) + o);
-    p23 = make_float2(__low2float(h23) + o, __high2float(h23) + o);
-  }
+  const float2 o = make_float2(-(8388608.0f + off), -(8388608.0f + off));
+  p01 = __fadd2_rn(make_float2(magic_f(w, 0x5440u), magic_f(w, 0x5441u)), o);
+  p23 = __fadd2_rn(make_float2(magic_f(w, 0x5442u), magic_f(w, 0x5443u)), o);
 }
 
 // Dot product of one row held in a stage with the lane's inputs (lane's
 // partial sum; the caller reduces over the warp).  x[u][c] holds the inputs
 // of weights 4q .. 4q + 3 of unit u, quarter c, as two pairs.
-template <int kVariant>
 __device__ __forceinline__ float row_dot(const uint8_t* sb, int j, const LaneConst& lc,
                                          const float2 (&x)[3][4][2]) {
   const uint32_t* qlw = reinterpret_cast<const uint32_t*>(sb) + j * (kQlRow / 4);
@@ -214,13 +205,13 @@ __device__ __forceinline__ float row_dot(const uint8_t* sb, int j, const LaneCon
     Q[2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
     Q[3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
     float2 sc01, sc23;  // the quarters' scales (stored offset by 128)
-    bytes_to_floats<kVariant>(sv, 128.0f, sc01, sc23);
+    bytes_to_floats(sv, 128.0f, sc01, sc23);
     const float scs[4] = {sc01.x, sc01.y, sc23.x, sc23.y};
     float2 t = make_float2(0.f, 0.f);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       float2 w01, w23;  // code - 32
-      bytes_to_floats<kVariant>(Q[c], 32.0f, w01, w23);
+      bytes_to_floats(Q[c], 32.0f, w01, w23);
       const float2 a = __ffma2_rn(w23, x[u][c][1], __fmul2_rn(w01, x[u][c][0]));
       t = __ffma2_rn(a, make_float2(scs[c], scs[c]), t);
     }
@@ -229,7 +220,6 @@ __device__ __forceinline__ float row_dot(const uint8_t* sb, int j, const LaneCon
   return acc;
 }
 
-template <int kVariant>
 __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadParams p) {
   extern __shared__ __align__(128) unsigned char head_smem_raw[];
   HeadSmem& sm = *reinterpret_cast<HeadSmem*>(head_smem_raw);
@@ -350,7 +340,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
     }
     const int r = t * kStageRows + warp;
     if (r < n_rows) {
-      float acc = row_dot<kVariant>(sm.stage[s], warp, lc, x);
+      float acc = row_dot(sm.stage[s], warp, lc, x);
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
       if (p.logits && lane == 0) p.logits[r] = acc;
@@ -432,20 +422,10 @@ __global__ void __launch_bounds__(kEmbedThreads) embed_q4_kernel(const uint8_t* 
 // ---------------------------------------------------------------------------
 int lm_head_grid(int n_sm) { return n_sm; }
 
-constexpr int kHeadVariants = 2;
-using HeadKernel = void (*)(const HeadParams);
-static const HeadKernel kHeadKernels[kHeadVariants] = {lm_head_kernel<0>, lm_head_kernel<1>};
-
-int lm_head_variant_count() { return kHeadVariants; }
-
 cudaError_t prepare_head_kernels() {
-  for (int v = 0; v < kHeadVariants; ++v) {
-    cudaError_t e = cudaFuncSetAttribute((const void*)kHeadKernels[v],
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)sizeof(HeadSmem));
-    if (e != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+  return cudaFuncSetAttribute((const void*)lm_head_kernel,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)sizeof(HeadSmem));
 }
 
 cudaError_t launch_q6k_pack(const void* src, int n_rows, void* dst, cudaStream_t st) {
@@ -456,8 +436,7 @@ cudaError_t launch_q6k_pack(const void* src, int n_rows, void* dst, cudaStream_t
 
 cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, const float* state,
                            float* logits, int* token, void* best, unsigned* done, int* status,
-                           int grid, int variant, cudaStream_t st, bool pdl) {
-  if (variant < 0 || variant >= kHeadVariants) return cudaErrorInvalidValue;
+                           int grid, cudaStream_t st, bool pdl) {
   HeadParams p{};
   p.planes = static_cast<const uint8_t*>(planes);
   p.n_rows = n_rows;
@@ -479,7 +458,7 @@ cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, c
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   void* args[] = {&p};
-  return cudaLaunchKernelExC(&cfg, (const void*)kHeadKernels[variant], args);
+  return cudaLaunchKernelExC(&cfg, (const void*)lm_head_kernel, args);
 }
 
 size_t lm_head_best_bytes(int grid) { return sizeof(HeadBest) * (size_t)grid; }

@@ -84,16 +84,13 @@ def _gamma_for_unit(orc, i, target=32.0):
     raise AssertionError("no gamma gives an exact unit")
 
 
-@pytest.mark.parametrize("variant", [0, 1])
-def test_head_basis_vectors_bit_exact(pkg, orc, cuda, head_w, variant):
+def test_head_basis_vectors_bit_exact(pkg, orc, cuda, head_w):
     """Unit inputs at the reference test's columns: every logit is one
-    dequantised weight times 32, bit for bit the reference's (both
-    code-to-float variants)."""
+    dequantised weight times 32, bit for bit the reference's."""
     torch = cuda
     n = 8192
     w = head_w[:n * ROW]
     with pkg.Context() as ctx:
-        ctx.set_option(pkg.gqa.GQA_OPT_HEAD_VARIANT, variant)
         packed = _packed(torch, ctx, pkg, w, n)
         for i in BASIS:
             state, gamma = _gamma_for_unit(orc, i)
@@ -105,15 +102,14 @@ def test_head_basis_vectors_bit_exact(pkg, orc, cuda, head_w, variant):
         assert ctx.device_status() == 0
 
 
-@pytest.mark.parametrize("seed,variant", [(0, 1), (1, 1), (2, 1), (0, 0)])
-def test_head_full_vocab_matches_reference(pkg, orc, cuda, head_w, seed, variant):
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_head_full_vocab_matches_reference(pkg, orc, cuda, head_w, seed):
     torch = cuda
     state = pkg.seeded.normal(100 + seed, pkg.seeded.STATE, 1536) * (1 + seed)
     gamma = (1.0 + 0.1 * pkg.seeded.normal(100 + seed, pkg.seeded.GAMMA_OUT, 1536)).astype(
         np.float32)
     want, want_tok = orc.ref_lm_head(state, gamma, head_w)
     with pkg.Context() as ctx:
-        ctx.set_option(pkg.gqa.GQA_OPT_HEAD_VARIANT, variant)
         packed = _packed(torch, ctx, pkg, head_w, VOCAB)
         got, tok = _run_head(torch, ctx, packed, VOCAB, gamma, state)
         assert ctx.device_status() == 0
