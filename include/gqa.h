@@ -365,6 +365,84 @@ GQA_API int gqa_decode_token(gqa_ctx *ctx, gqa_stream_t stream, const gqa_model 
                              float *state, int *d_token, int *d_pos, float *logits, int wrap_lo,
                              int wrap_hi);
 
+/* ---- GGUF model files and the server's requests -------------------------- */
+
+/* A GGUF file opened for reading (v2 or v3): the tensor table, the integer
+ * metadata, general.alignment and tokenizer.ggml.tokens -- what qwen_server.c
+ * gets from parse_gguf_tensors (:113-178) and load_tokenizer_tokens
+ * (:203-266).  Unlike the reference, every length is checked against the
+ * file size, general.alignment is honoured (the reference assumes 32, the
+ * default) and a damaged file is an error, never an exit. */
+typedef struct gqa_gguf gqa_gguf;
+
+typedef struct {
+    const char *name;            /* owned by the gqa_gguf */
+    int n_dims;
+    long long ne[4];             /* ne[0] is the innermost dimension */
+    int type;                    /* GGUF tensor type: 0 F32, 2 Q4_0, 14 Q6_K, ... */
+    unsigned long long offset;   /* absolute file offset of the data */
+    unsigned long long bytes;    /* size of the data (0 for a type not sized here) */
+} gqa_gguf_tensor;
+
+GQA_API int gqa_gguf_open(const char *path, gqa_gguf **out);
+GQA_API int gqa_gguf_close(gqa_gguf *g);
+GQA_API int gqa_gguf_tensor_count(const gqa_gguf *g);
+GQA_API int gqa_gguf_tensor_at(const gqa_gguf *g, int i, gqa_gguf_tensor *out);
+/* get_tensor_offset (:180-186) with an error instead of exit when absent. */
+GQA_API int gqa_gguf_find(const gqa_gguf *g, const char *name, gqa_gguf_tensor *out);
+/* Reads a tensor's bytes (or any in-file range given as a gqa_gguf_tensor). */
+GQA_API int gqa_gguf_read(const gqa_gguf *g, const gqa_gguf_tensor *t, void *host_dst);
+GQA_API int gqa_gguf_meta_int(const gqa_gguf *g, const char *key, long long *out);
+/* Number of tokenizer.ggml.tokens entries (0 if absent) and one entry's raw
+ * string (copied with a terminating NUL; returns its full length). */
+GQA_API int gqa_gguf_vocab_size(const gqa_gguf *g);
+GQA_API int gqa_gguf_token_string(const gqa_gguf *g, int id, char *out, int cap);
+
+/* Device copies of one model's weights, laid out as the server lays them
+ * out (qwen_server.c:525-588): per layer W_qkv = attn_q | attn_k | attn_v rows
+ * and b_qkv likewise, attn_output, ffn_gate/up/down and both norm weights;
+ * token_embd.weight; output_norm.weight; output.weight through
+ * gqa_lm_head_pack.  Types and shapes are checked (Q4_0 projections and
+ * embedding, Q6_K head, F32 norms and biases, Qwen2.5-1.5B shapes).
+ * n_layers <= 0 takes qwen2.block_count from the file.  Allocates on the
+ * current device, which must be the context's. */
+typedef struct gqa_model_weights gqa_model_weights;
+GQA_API int gqa_model_load(gqa_ctx *ctx, const gqa_gguf *g, int n_layers,
+                           gqa_model_weights **out);
+/* A gqa_model over loaded weights and the caller's KV caches (kv may be NULL
+ * for a view without caches). */
+GQA_API int gqa_model_view(const gqa_model_weights *w, const gqa_layer_kv *kv, gqa_model *out);
+GQA_API int gqa_model_free(gqa_model_weights *w);
+
+/* The server's requests without the socket (qwen_server.c:770-1054): one
+ * conversation state over a model whose caches have at least t_max rows.
+ * eog_ids / n_eog: the end-of-generation tokens (NULL: the reference's
+ * 151643 and 151645).  Errors carry the server's reply text in
+ * gqa_last_error_string(): ERR_BAD_REQUEST, ERR_INVALID_TOKEN,
+ * ERR_CONTEXT_FULL, ERR_NOT_READY, ERR_RAW_NOT_ALLOWED_WHEN_BASE_ACTIVE,
+ * ERR_GPU_FAILURE. */
+typedef struct gqa_session gqa_session;
+GQA_API int gqa_session_create(gqa_ctx *ctx, const gqa_model *model, int t_max,
+                               const int *eog_ids, int n_eog, gqa_session **out);
+GQA_API int gqa_session_destroy(gqa_session *s);
+/* SET_BASE: the tokens through every layer at positions 0 .. n-1, one token
+ * at a time as the server does; then base_pos = n, base_hash = FNV-1a of the
+ * ids, base_generation + 1, state READY. */
+GQA_API int gqa_session_set_base(gqa_session *s, const int *tokens, int n);
+/* QUERY (raw = 0, from base_pos; needs READY) or RAW_QUERY (raw = 1, from
+ * position 0; refused while a base is active): the prompt through the layers,
+ * the head on its last token, then greedy generation of at most max_new
+ * tokens, stopping before an end-of-generation token.  out_tokens receives
+ * the generated ids (room for max_new), *n_out their count.  Positions past
+ * base_pos are scratch for the next request, as in the server. */
+GQA_API int gqa_session_query(gqa_session *s, const int *tokens, int n, int max_new, int raw,
+                              int *out_tokens, int *n_out);
+/* STATUS: base_pos, base_hash, base_generation and whether the state is
+ * READY (any pointer may be NULL). */
+GQA_API int gqa_session_status(const gqa_session *s, int *base_pos,
+                               unsigned long long *base_hash, int *base_generation,
+                               int *ready);
+
 /* ---- prefill ---------------------------------------------------------- */
 
 /* Causal attention over whole prompts on the tensor cores (bf16 operands,

@@ -12,6 +12,6 @@ The directory name contains hyphens, so it is loaded by path (see
 ``__graft_entry__.load_package``) under the module name ``gqa_b200``.
 """
 from . import seeded, shard  # noqa: F401
-from .gqa import (BlockWeights, Context, Exchange, FfnWeights, GqaError, Graph,  # noqa: F401
-                  LayerKV, Model, ModelHandle, block_weights_of, ffn_weights_of, header_functions,
-                  kv_of, last_error, lib)
+from .gqa import (BlockWeights, Context, Exchange, FfnWeights, Gguf, GqaError,  # noqa: F401
+                  Graph, LayerKV, LoadedModel, Model, ModelHandle, Session, block_weights_of,
+                  ffn_weights_of, header_functions, kv_of, last_error, lib)

@@ -1,4 +1,4 @@
-"""Builds the sm_100a CUDA library in-tree: csrc/*.cu -> libgqa_b200.so.
+"""Builds the sm_100a CUDA library in-tree: csrc/*.cu + csrc/*.cpp -> libgqa_b200.so.
 
 nvcc cross-compiles for sm_100a without a GPU.  The library links the CUDA
 runtime statically and exports only the C ABI of include/gqa.h.
@@ -24,7 +24,8 @@ NVCC_FLAGS = [
 
 
 def sources() -> list[str]:
-    return sorted(glob.glob(os.path.join(HERE, "csrc", "*.cu")))
+    return sorted(glob.glob(os.path.join(HERE, "csrc", "*.cu")) +
+                  glob.glob(os.path.join(HERE, "csrc", "*.cpp")))
 
 
 def needs_rebuild() -> bool:

@@ -73,6 +73,12 @@ class LayerKV(ctypes.Structure):
     _fields_ = [("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p)]
 
 
+class GgufTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("n_dims", ctypes.c_int),
+                ("ne", ctypes.c_longlong * 4), ("type", ctypes.c_int),
+                ("offset", ctypes.c_ulonglong), ("bytes", ctypes.c_ulonglong)]
+
+
 class Model(ctypes.Structure):
     """gqa_model: everything one whole-model decode step reads."""
     _fields_ = [("n_layers", ctypes.c_int), ("attn", ctypes.POINTER(BlockWeights)),
@@ -129,6 +135,24 @@ _SIGNATURES = {
     "gqa_lm_head": [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp],
     "gqa_token_embedding": [_vp, _vp, _vp, _i, _vp, _vp],
     "gqa_decode_token": [_vp, _vp, ctypes.POINTER(Model), _vp, _vp, _vp, _vp, _i, _i],
+    "gqa_gguf_open": [ctypes.c_char_p, ctypes.POINTER(_vp)],
+    "gqa_gguf_close": [_vp],
+    "gqa_gguf_tensor_count": [_vp],
+    "gqa_gguf_tensor_at": [_vp, _i, ctypes.POINTER(GgufTensor)],
+    "gqa_gguf_find": [_vp, ctypes.c_char_p, ctypes.POINTER(GgufTensor)],
+    "gqa_gguf_read": [_vp, ctypes.POINTER(GgufTensor), _vp],
+    "gqa_gguf_meta_int": [_vp, ctypes.c_char_p, ctypes.POINTER(_ll)],
+    "gqa_gguf_vocab_size": [_vp],
+    "gqa_gguf_token_string": [_vp, _i, ctypes.c_char_p, _i],
+    "gqa_model_load": [_vp, _vp, _i, ctypes.POINTER(_vp)],
+    "gqa_model_view": [_vp, _vp, ctypes.POINTER(Model)],
+    "gqa_model_free": [_vp],
+    "gqa_session_create": [_vp, ctypes.POINTER(Model), _i, _vp, _i, ctypes.POINTER(_vp)],
+    "gqa_session_destroy": [_vp],
+    "gqa_session_set_base": [_vp, _vp, _i],
+    "gqa_session_query": [_vp, _vp, _i, _i, _i, _vp, ctypes.POINTER(_i)],
+    "gqa_session_status": [_vp, ctypes.POINTER(_i), ctypes.POINTER(_ull), ctypes.POINTER(_i),
+                           ctypes.POINTER(_i)],
     "gqa_prefill_bf16": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
     "gqa_fill_normal": [_vp, _vp, _vp, _ll, _ull, _ull, _ll],
     "gqa_inv_freq": [_vp, ctypes.POINTER(ctypes.c_float)],
@@ -277,6 +301,146 @@ class Exchange:
     def destroy(self) -> None:
         if getattr(self, "_h", None):
             lib().gqa_exchange_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+class Gguf:
+    """A GGUF file opened by the library's reader (host only, no GPU needed)."""
+
+    def __init__(self, path: str):
+        h = _vp()
+        _check(lib().gqa_gguf_open(str(path).encode(), ctypes.byref(h)))
+        self._h = h.value
+
+    def close(self) -> None:
+        if self._h:
+            lib().gqa_gguf_close(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @staticmethod
+    def _info(t: GgufTensor) -> dict:
+        return {"name": t.name.decode(), "n_dims": t.n_dims, "ne": list(t.ne)[:t.n_dims],
+                "type": t.type, "offset": t.offset, "bytes": t.bytes}
+
+    def tensors(self) -> list[dict]:
+        out = []
+        for i in range(lib().gqa_gguf_tensor_count(self._h)):
+            t = GgufTensor()
+            _check(lib().gqa_gguf_tensor_at(self._h, i, ctypes.byref(t)))
+            out.append(self._info(t))
+        return out
+
+    def find(self, name: str) -> dict:
+        t = GgufTensor()
+        _check(lib().gqa_gguf_find(self._h, name.encode(), ctypes.byref(t)))
+        return self._info(t)
+
+    def read(self, name: str) -> np.ndarray:
+        t = GgufTensor()
+        _check(lib().gqa_gguf_find(self._h, name.encode(), ctypes.byref(t)))
+        out = np.empty(t.bytes, dtype=np.uint8)
+        _check(lib().gqa_gguf_read(self._h, ctypes.byref(t), out.ctypes.data))
+        return out
+
+    def meta_int(self, key: str) -> int:
+        v = _ll()
+        _check(lib().gqa_gguf_meta_int(self._h, key.encode(), ctypes.byref(v)))
+        return v.value
+
+    def vocab_size(self) -> int:
+        return lib().gqa_gguf_vocab_size(self._h)
+
+    def token(self, i: int) -> bytes:
+        buf = ctypes.create_string_buffer(1024)
+        n = lib().gqa_gguf_token_string(self._h, i, buf, len(buf))
+        if n < 0:
+            _check(n)
+        return buf.raw[:min(n, len(buf) - 1)]
+
+
+class LoadedModel:
+    """gqa_model_load's device weights; view(kvs) gives the gqa_model."""
+
+    def __init__(self, ctx: "Context", gguf: Gguf, n_layers: int = 0):
+        h = _vp()
+        _check(lib().gqa_model_load(ctx._h, gguf._h, n_layers, ctypes.byref(h)))
+        self._h = h.value
+        m = Model()
+        _check(lib().gqa_model_view(self._h, None, ctypes.byref(m)))
+        self.n_layers, self.vocab = m.n_layers, m.vocab
+
+    def view(self, kvs) -> Model:
+        n = len(kvs)
+        assert n == self.n_layers
+        self._kv = (LayerKV * n)(*kvs)
+        m = Model()
+        _check(lib().gqa_model_view(self._h, self._kv, ctypes.byref(m)))
+        return m
+
+    def free(self) -> None:
+        if self._h:
+            lib().gqa_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class Session:
+    """The server's SET_BASE / QUERY / RAW_QUERY / STATUS over a model."""
+
+    def __init__(self, ctx: "Context", model: Model, t_max: int, eog=None):
+        h = _vp()
+        self._keep = (ctx, model)
+        eog_arr = (ctypes.c_int * len(eog))(*eog) if eog is not None else None
+        _check(lib().gqa_session_create(ctx._h, ctypes.byref(model), t_max, eog_arr,
+                                        len(eog) if eog is not None else 0, ctypes.byref(h)))
+        self._h = h.value
+
+    def set_base(self, tokens) -> None:
+        arr = (ctypes.c_int * len(tokens))(*tokens)
+        _check(lib().gqa_session_set_base(self._h, arr, len(tokens)))
+
+    def query(self, tokens, max_new: int, raw: bool = False) -> list[int]:
+        arr = (ctypes.c_int * max(len(tokens), 1))(*tokens)
+        out = (ctypes.c_int * max(max_new, 1))()
+        n = _i()
+        _check(lib().gqa_session_query(self._h, arr, len(tokens), max_new, int(raw), out,
+                                       ctypes.byref(n)))
+        return list(out[:n.value])
+
+    def status(self) -> dict:
+        bp, gen, ready = _i(), _i(), _i()
+        hsh = _ull()
+        _check(lib().gqa_session_status(self._h, ctypes.byref(bp), ctypes.byref(hsh),
+                                        ctypes.byref(gen), ctypes.byref(ready)))
+        return {"base_pos": bp.value, "base_hash": hsh.value, "base_generation": gen.value,
+                "ready": bool(ready.value)}
+
+    def destroy(self) -> None:
+        if self._h:
+            lib().gqa_session_destroy(self._h)
             self._h = None
 
     def __del__(self):

@@ -9,9 +9,11 @@ bench.py, as the checker (never as the thing measured or shipped).
   ``_ref/libgqa_ref_head.so`` / ``_ref/libgqa_ref_model.so`` -- the
   reference's own cpu_attention_gqa_pipeline (attention_gqa_benchmark.c:
   109-216), cpu_decoder_layer_step (test_28_layers_real.c:192-318), Q6_K
-  LM-head GEMV cpu_gemv_q6_k_ref (test_gemv_q6_k.c:46-94) and token embedding
-  lookup get_token_embedding (test_full_model_logits.c:584-597), compiled
-  unmodified from its sources by oracle/Makefile.  They exist only where the
+  LM-head GEMV cpu_gemv_q6_k_ref (test_gemv_q6_k.c:46-94), token embedding
+  lookup get_token_embedding (test_full_model_logits.c:584-597) and the
+  server's GGUF reading parse_gguf_tensors / load_tokenizer_tokens
+  (qwen_server.c:113-266, ``_ref/libgqa_ref_server.so``), compiled unmodified
+  from its sources by oracle/Makefile.  They exist only where the
   reference sources were present at build time; REF_T_MAX = 4096 is their
   compile-time cache stride.
 """
@@ -28,6 +30,7 @@ REF_BENCH_SO = os.path.join(HERE, "_ref", "libgqa_ref_bench.so")
 REF_LAYER_SO = os.path.join(HERE, "_ref", "libgqa_ref_layer.so")
 REF_HEAD_SO = os.path.join(HERE, "_ref", "libgqa_ref_head.so")
 REF_MODEL_SO = os.path.join(HERE, "_ref", "libgqa_ref_model.so")
+REF_SERVER_SO = os.path.join(HERE, "_ref", "libgqa_ref_server.so")
 REF_T_MAX = 4096
 
 _f = ctypes.c_float
@@ -54,7 +57,8 @@ def _load(path: str) -> ctypes.CDLL:
 
 
 def have_reference() -> bool:
-    return all(os.path.exists(p) for p in (REF_BENCH_SO, REF_LAYER_SO, REF_HEAD_SO, REF_MODEL_SO))
+    return all(os.path.exists(p) for p in (REF_BENCH_SO, REF_LAYER_SO, REF_HEAD_SO, REF_MODEL_SO,
+                                           REF_SERVER_SO))
 
 
 def _fptr(a: np.ndarray):
@@ -379,3 +383,93 @@ def ref_decode_token(table, layers, kv, gamma_out, w_head, token: int, pos: int)
     for (attn, ffn), (kc, vc) in zip(layers, kv):
         x = ref_decoder_layer(x, attn, ffn, kc, vc, pos, pos + 1)
     return ref_lm_head(x, gamma_out, w_head)
+
+
+# ---- the server: GGUF reading (compiled) and its request loop (restated) -----
+
+def ref_gguf_parse(path: str, max_tensors: int = 4096):
+    """The reference's parse_gguf_tensors on a file: (tensors, data_start) with
+    tensors = [{"name", "n_dims", "ne", "type", "offset"}] (absolute offsets)."""
+    lib = _load(REF_SERVER_SO)
+    fn = lib.ref_gguf_parse
+    if fn.argtypes is None:
+        _u32p = ctypes.POINTER(ctypes.c_uint32)
+        _u64p = ctypes.POINTER(ctypes.c_uint64)
+        fn.argtypes = [ctypes.c_char_p, _i, ctypes.c_char_p, _u32p, _u64p, _u32p, _u64p, _u64p]
+        fn.restype = _i
+    names = ctypes.create_string_buffer(64 * max_tensors)
+    n_dims = (ctypes.c_uint32 * max_tensors)()
+    ne = (ctypes.c_uint64 * (4 * max_tensors))()
+    types = (ctypes.c_uint32 * max_tensors)()
+    offs = (ctypes.c_uint64 * max_tensors)()
+    start = ctypes.c_uint64()
+    n = fn(str(path).encode(), max_tensors, names, n_dims, ne, types, offs, ctypes.byref(start))
+    if n < 0:
+        raise ValueError(f"reference parser failed ({n})")
+    out = []
+    for i in range(n):
+        raw = names.raw[64 * i:64 * i + 64]
+        out.append({"name": raw.split(b"\0", 1)[0].decode(), "n_dims": n_dims[i],
+                    "ne": [ne[4 * i + d] for d in range(n_dims[i])], "type": types[i],
+                    "offset": offs[i]})
+    return out, start.value
+
+
+def ref_gguf_token(path: str, token: int) -> bytes:
+    """The reference's load_tokenizer_tokens, one entry."""
+    lib = _load(REF_SERVER_SO)
+    fn = lib.ref_gguf_token
+    if fn.argtypes is None:
+        fn.argtypes = [ctypes.c_char_p, _i, ctypes.c_char_p, _i]
+        fn.restype = _i
+    buf = ctypes.create_string_buffer(1024)
+    rc = fn(str(path).encode(), token, buf, len(buf))
+    if rc < 0:
+        raise ValueError(f"reference tokenizer read failed ({rc})")
+    return buf.value
+
+
+def ref_server_query(table, layers, kv, gamma_out, w_head, tokens, cur_pos: int, max_new: int,
+                     eog=(151643, 151645), t_max: int = REF_T_MAX, margins=None):
+    """The server's QUERY loop (qwen_server.c:957-1049), restated over the
+    compiled pieces: every prompt token through the layers at cur_pos + p (the
+    head only after the last), then greedy picks -- stop before an
+    end-of-generation id, emit, stop at max_new or t_max, else run the pick
+    through the layers and the head.  kv[l] = (k_cache, v_cache) updated in
+    place.  Returns the emitted ids; `margins`, when a list, receives the gap
+    between the two largest logits of every pick."""
+    logits = None
+    for p, tok in enumerate(tokens):
+        x = token_embedding(table, tok)
+        for (attn, ffn), (kc, vc) in zip(layers, kv):
+            x = ref_decoder_layer(x, attn, ffn, kc, vc, cur_pos + p, cur_pos + p + 1)
+        if p == len(tokens) - 1:
+            logits, _ = ref_lm_head(x, gamma_out, w_head)
+    out = []
+    next_pos = cur_pos + len(tokens)
+    for gen in range(max_new):
+        best = greedy_pick(logits)
+        if margins is not None:  # gap between the two largest logits of each pick
+            top = np.sort(logits)[-2:]
+            margins.append(float(top[1] - top[0]))
+        if best in eog:
+            break
+        out.append(best)
+        if gen + 1 >= max_new or next_pos >= t_max:
+            break
+        logits, _ = ref_decode_token(table, layers, kv, gamma_out, w_head, best, next_pos)
+        next_pos += 1
+    return out
+
+
+def ref_server_set_base(table, layers, kv, tokens):
+    """SET_BASE (qwen_server.c:815-860): the tokens through the layers at
+    positions 0 .. n-1; returns the FNV-1a hash of the ids."""
+    h = 14695981039346656037
+    for p, tok in enumerate(tokens):
+        h ^= tok
+        h = (h * 1099511628211) & ((1 << 64) - 1)
+        x = token_embedding(table, tok)
+        for (attn, ffn), (kc, vc) in zip(layers, kv):
+            x = ref_decoder_layer(x, attn, ffn, kc, vc, p, p + 1)
+    return h
