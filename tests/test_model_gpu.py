@@ -75,9 +75,9 @@ def test_raw_query_matches_reference(pkg, orc, cuda, loaded):
     s = pkg.Session(ctx, model.view(kvs), 4096)
     try:
         got = s.query(prompt, 5, raw=True)
-        if not _close_call(margins):
-            assert got == want
-        assert len(got) == 5
+        if _close_call(margins):
+            pytest.skip("near-tie in the reference's picks")
+        assert got == want and len(got) == 5
         assert s.status() == {"base_pos": 0, "base_hash": 0, "base_generation": 0,
                               "ready": False}
     finally:
@@ -99,8 +99,7 @@ def test_set_base_then_queries(pkg, orc, cuda, loaded):
         for prompt, max_new in (([7, 7, 100], 4), ([1500], 3)):
             want, margins = _ref_query(orc, arrays, layers, kv, prompt, len(base), max_new)
             got = s.query(prompt, max_new)
-            if not _close_call(margins):
-                assert got == want
+            assert _close_call(margins) or got == want
         with pytest.raises(pkg.GqaError, match="ERR_RAW_NOT_ALLOWED_WHEN_BASE_ACTIVE"):
             s.query([1], 2, raw=True)
         with pytest.raises(pkg.GqaError, match="ERR_INVALID_TOKEN"):
