@@ -54,6 +54,9 @@ WORKLOADS = {
     "layer28": dict(layers=28, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1),
     "head": dict(layers=0, t_max=1, seqs=1, vocab=151936),
     "token28": dict(layers=28, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1, vocab=151936),
+    # Qwen2.5-0.5B attention shape (head_dim 64, 14 q / 2 KV heads), 24 layers
+    "resident05b": dict(layers=24, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1, n_q=14, n_kv=2,
+                        d=64),
 }
 
 BLOCK_METRIC = ("GQA attention block (RMSNorm, Q4_0 QKV + bias, attention, Q4_0 Wo + residual): "
@@ -243,6 +246,34 @@ def cpu_reference_run(steps, warmup, budget_s, pos_lo=3840, layers=28):
     return nbytes / dt / 1e9, cores, sample, kind, done / dt
 
 
+def cpu_port_05b_run(budget_s, pos_lo=3840, layers=24):
+    """The reference has no CPU attention for the 0.5B shape: the restatement
+    (oracle/gqa_oracle.c, its loops at head_dim 64, group 7), one thread, per
+    step the 24 layer calls."""
+    import __graft_entry__
+    orc = __graft_entry__.load_oracle()
+    rng = np.random.default_rng(0)
+    T, nq, nkv, d = 4096, 14, 2, 64
+    kcs = [rng.standard_normal((nkv, T, d), dtype=np.float32) for _ in range(layers)]
+    vcs = [rng.standard_normal((nkv, T, d), dtype=np.float32) for _ in range(layers)]
+    qkvs = [rng.standard_normal((nq + 2 * nkv) * d, dtype=np.float32) for _ in range(layers)]
+    t0 = time.perf_counter()
+    done, nbytes = 0, 0
+    while True:
+        pos = pos_lo + done % 256
+        for l in range(layers):
+            orc.layer_attention(qkvs[l].copy(), kcs[l], vcs[l], pos, pos + 1, n_heads_q=nq,
+                                n_heads_kv=nkv, head_dim=d)
+        nbytes += layers * 2 * nkv * d * 4 * (pos + 1)
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    sample = (f"{done} decode step(s) x {layers} layers at positions {pos_lo}.."
+              f"{pos_lo + min(done, 256) - 1}, the C restatement on 1 thread")
+    return nbytes / dt / 1e9, 1, sample, "port", done / dt
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -301,6 +332,14 @@ def workload_config(name, exchange="peer"):
                 "bytes_per_layer": "2048*(pos+1) KV + %d weights" % BLOCK_WEIGHT_BYTES,
                 "l2": "KV 235 MB + weights 87 MB per GPU > 126 MB L2; no flush",
                 "parallelism": "sequence-sharded replicas"}
+    if name == "resident05b":
+        return {"workload": "resident05b: 24-layer resident decode attention of the Qwen2.5-0.5B "
+                            "shape (head_dim 64, 14 q / 2 KV heads, 7 per KV head), 1 sequence "
+                            "per GPU, fp32 KV t_max=4096 per layer (50 MB), steps at positions "
+                            "3840..4095 (window wraps), shape-generic kernels",
+                "layers": 24, "t_max": 4096, "positions": [3840, 4095], "global_batch": None,
+                "l2": "KV 50 MB per GPU < 126 MB L2: read from L2 after the first pass",
+                "parallelism": "sequence-sharded replicas"}
     if name == "resident28":
         return {"workload": "resident28: 28-layer resident decode attention, 1 sequence per GPU, "
                             "12 q / 2 KV heads, d=128, fp32 KV t_max=4096 per layer (235 MB), "
@@ -340,28 +379,32 @@ def run_resident(args, g, ctx, rank, world, local):
     import torch
     wl = WORKLOADS[args.workload]
     L_layers, t_max, pos_lo, pos_hi = wl["layers"], wl["t_max"], wl["pos_lo"], wl["pos_hi"]
+    n_q, n_kv, d = wl.get("n_q", N_Q), wl.get("n_kv", N_KV), wl.get("d", D)
+    qkv_w, out_w, row_bytes = (n_q + 2 * n_kv) * d, n_q * d, 2 * n_kv * d * 4
+    generic = d != D
     seed = 4242 + 1000 * rank
-    caches = torch.empty((L_layers, 2, 2, t_max, D), device="cuda")  # [layer][k/v][h][t][d]
+    caches = torch.empty((L_layers, 2, n_kv, t_max, d), device="cuda")  # [layer][k/v][h][t][d]
     ctx.fill_normal(caches, caches.numel(), seed, g.seeded.K_CACHE)
     kvs = [g.kv_of(caches[l, 0], caches[l, 1]) for l in range(L_layers)]
     n_slots = 8
-    qkv_slots = torch.empty((n_slots, L_layers, QKV_W), device="cuda")
+    qkv_slots = torch.empty((n_slots, L_layers, qkv_w), device="cuda")
     ctx.fill_normal(qkv_slots, qkv_slots.numel(), seed, g.seeded.QKV)
-    out = torch.empty((L_layers, OUT_W), device="cuda")
+    out = torch.empty((L_layers, out_w), device="cuda")
     d_pos = torch.tensor([pos_lo], dtype=torch.int32, device="cuda")
-    graphs = [ctx.graph_create_layers(kvs, qkv_slots[s], QKV_W, out, OUT_W, d_pos, advance=True,
+    ctx.reserve(1, t_max)
+    graphs = [ctx.graph_create_layers(kvs, qkv_slots[s], qkv_w, out, out_w, d_pos, advance=True,
                                       wrap_lo=pos_lo, wrap_hi=pos_hi) for s in range(n_slots)]
     # e2e: host-buffer steps through the C ABI (gqa_graph_step_host)
-    d_qkv_e2e = torch.empty((L_layers, QKV_W), device="cuda")
-    g_e2e = ctx.graph_create_layers(kvs, d_qkv_e2e, QKV_W, out, OUT_W, d_pos, advance=True,
+    d_qkv_e2e = torch.empty((L_layers, qkv_w), device="cuda")
+    g_e2e = ctx.graph_create_layers(kvs, d_qkv_e2e, qkv_w, out, out_w, d_pos, advance=True,
                                     wrap_lo=pos_lo, wrap_hi=pos_hi)
     h_qkv = qkv_slots.cpu().pin_memory()
-    h_out = torch.empty((n_slots, L_layers, OUT_W)).pin_memory()
+    h_out = torch.empty((n_slots, L_layers, out_w)).pin_memory()
     n_window = pos_hi - pos_lo
 
     def step_bytes(i):
         pos = pos_lo + i % n_window
-        return L_layers * ROW_BYTES * (pos + 1)
+        return L_layers * row_bytes * (pos + 1)
 
     stream = torch.cuda.current_stream()
     for i in range(args.warmup):
@@ -403,16 +446,24 @@ def run_resident(args, g, ctx, rank, world, local):
 
     # mirrors the library's split plan for pos read from the device (planned for t_max)
     n_sm = torch.cuda.get_device_properties(local).multi_processor_count
-    target = args.target_ctas or n_sm
-    quant = g.gqa.VARIANT_QUANT[3 if args.variant < 0 else args.variant]
-    n_splits = min(-(-target // N_KV), -(-t_max // quant))
-    kernels_per_step = L_layers * (2 if n_splits > 1 else 1) + 1
+    if generic:  # append, split, merge per layer (csrc/gqa_generic.cu)
+        kernels_per_step = L_layers * 3 + 1
+    else:
+        target = args.target_ctas or n_sm
+        quant = g.gqa.VARIANT_QUANT[3 if args.variant < 0 else args.variant]
+        n_splits = min(-(-target // n_kv), -(-t_max // quant))
+        kernels_per_step = L_layers * (2 if n_splits > 1 else 1) + 1
     for gr in graphs + [g_e2e]:
         gr.destroy()
-    return dict(t=t_local, t_e2e=t_e2e_local, bytes=total_bytes, clocks=clk.summary(),
-                launches=kernels_per_step * args.steps, launches_per_step=kernels_per_step,
-                h2d=L_layers * QKV_W * 4, d2h=L_layers * OUT_W * 4, tokens=args.steps,
-                dominant_launches=L_layers * args.steps)
+    res = dict(t=t_local, t_e2e=t_e2e_local, bytes=total_bytes, clocks=clk.summary(),
+               launches=kernels_per_step * args.steps, launches_per_step=kernels_per_step,
+               h2d=L_layers * qkv_w * 4, d2h=L_layers * out_w * 4, tokens=args.steps,
+               dominant_launches=L_layers * args.steps)
+    if generic:
+        res.update(kernel="split_generic_kernel<64, 7> (+ append and merge)",
+                   data="synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal), "
+                        "Qwen2.5-0.5B attention shape")
+    return res
 
 
 def run_block(args, g, ctx, rank, world, local):
@@ -935,7 +986,8 @@ def run_ours(args):
     t_max = wl.get("t_max") or (wl["len_hi"] + wl["window"])
     if args.workload == "long1":
         t_max = max(n for _, n in g.shard.plan_kv_ranges(t_max, world))
-    ctx = g.Context(t_max=t_max, device=local)
+    ctx = g.Context(n_heads_q=wl.get("n_q", N_Q), n_heads_kv=wl.get("n_kv", N_KV),
+                    head_dim=wl.get("d", D), t_max=t_max, device=local)
     if args.variant >= 0:
         ctx.set_option(g.gqa.GQA_OPT_KERNEL_VARIANT, args.variant)
     if args.target_ctas:
@@ -949,7 +1001,7 @@ def run_ours(args):
         r = run_block(args, g, ctx, rank, world, local)
     elif args.workload in ("head", "token28"):
         r = run_head(args, g, ctx, rank, world, local)
-    elif args.workload in ("resident28", "single"):
+    elif args.workload in ("resident28", "single", "resident05b"):
         r = run_resident(args, g, ctx, rank, world, local)
     elif args.workload == "long1":
         r = run_long1(args, g, ctx, rank, world, local)
@@ -970,6 +1022,8 @@ def run_ours(args):
             res = cpu_block_run(budget_s=12.0, full=args.workload == "layer28")
         elif args.workload in ("head", "token28"):
             res = cpu_head_run(budget_s=12.0, whole=args.workload == "token28")
+        elif args.workload == "resident05b":
+            res = cpu_port_05b_run(budget_s=12.0)
         else:
             res = cpu_reference_run(10 ** 6, 1, budget_s=12.0)
         if res is not None:
@@ -983,7 +1037,7 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t / args.steps * 1e3, 5), "higher_is_better": True,
             "scaling": "weak" if args.workload in ("resident28", "single", "block28", "layer28",
-                                                   "head", "token28")
+                                                   "head", "token28", "resident05b")
             else "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": r.get("data", "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)"),

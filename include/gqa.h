@@ -49,7 +49,7 @@ typedef enum {
 typedef struct {
     int n_heads_q;     /* 12 */
     int n_heads_kv;    /* 2 */
-    int head_dim;      /* 128 (only value built) */
+    int head_dim;      /* 128 with 6 q heads per KV head; or 64 with 7 (Qwen2.5-0.5B) */
     int t_max;         /* cache rows per KV head (reference: 4096) */
     float rope_theta;  /* 1e6 */
 } gqa_config;
@@ -64,7 +64,12 @@ typedef struct {
 /* ---- context ---------------------------------------------------------- */
 
 /* Creates a context on `device` (makes it current).  Replaces the OpenCL
- * context/queue/program set-up of qwen_server.c:560-640. */
+ * context/queue/program set-up of qwen_server.c:560-640.  Two shapes are
+ * built: head_dim 128 with 6 q heads per KV head (Qwen2.5-1.5B, every entry
+ * point) and head_dim 64 with 7 (Qwen2.5-0.5B, generate_stream_05b.c:19-31:
+ * gqa_kv_alloc/free, gqa_reserve, gqa_layer_attention(_out),
+ * gqa_decode_layers and the layer graphs, on shape-generic kernels; the other
+ * entry points return GQA_ERR_UNSUPPORTED for it). */
 GQA_API int gqa_create(const gqa_config *cfg, int device, gqa_ctx **out);
 GQA_API int gqa_destroy(gqa_ctx *ctx);
 

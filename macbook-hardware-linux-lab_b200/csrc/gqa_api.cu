@@ -57,6 +57,14 @@ size_t exchange_inbox_bytes(int world, int n_rows);
 cudaError_t launch_exchange_combine(const CombineParams& local, uint2* const* inbox,
                                     unsigned* epoch, int rank, int world, float* out, int* status,
                                     cudaStream_t st, bool pdl);
+bool generic_shape_built(int head_dim, int group);
+int generic_max_splits();
+int generic_plan_splits(int n_kv, int plan_len, int n_sm);
+cudaError_t launch_generic_attention(const float* qkv, float* q_rot, float* out, float* k_cache,
+                                     float* v_cache, Lengths len, int t_max, int n_q, int n_kv,
+                                     int head_dim, int n_splits, int plan_len,
+                                     const float* inv_freq, float* part_o, float* part_ml,
+                                     int* status, cudaStream_t st, bool pdl_first, bool pdl);
 size_t lm_head_packed_bytes(long long n_rows);
 int lm_head_grid(int n_sm);
 size_t lm_head_best_bytes(int grid);
@@ -116,6 +124,8 @@ struct gqa_ctx {
   float* blk_qkv = nullptr;   // attention block workspace: qkv of the token
   float* blk_attn = nullptr;  // attention block workspace: attention output
   float* blk_h = nullptr;     // FFN workspace: silu(gate) * up
+  bool generic = false;       // a shape the tuned kernels are not built for (gqa_generic.cu)
+  float* gen_q = nullptr;     // generic path: rotated q of the step [n_q][head_dim]
   void* head_best = nullptr;  // LM head: per-CTA greedy picks
   int head_grid = 0;          // LM head CTAs
   __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
@@ -305,13 +315,37 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
   return GQA_OK;
 }
 
+// The decode step on the shape-generic kernels (gqa_generic.cu): RoPE +
+// append into the context's q scratch and the cache, split partials, merge.
+int run_generic(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
+                Lengths len, int plan_len, float* out, bool pdl_first) {
+  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
+  const int n_splits = generic_plan_splits(nkv, plan_len, c->n_sm);
+  int rc = ensure_scratch(c, (long long)nq * n_splits, st);
+  if (rc != GQA_OK) return rc;
+  GQA_CUDA(launch_generic_attention(qkv, c->gen_q, out, kv->k_cache, kv->v_cache, len,
+                                    c->cfg.t_max, nq, nkv, c->cfg.head_dim, n_splits, plan_len,
+                                    c->inv_freq, c->part_o, c->part_ml, c->status, st, pdl_first,
+                                    c->layers_pdl != 0));
+  return GQA_OK;
+}
+
+// Entry points built only for the tuned shape (head_dim 128, group 6).
+int tuned_only(const gqa_ctx* c, const char* what) {
+  if (c->generic)
+    return fail(GQA_ERR_UNSUPPORTED, "%s: built for head_dim 128 with 6 q heads per KV head "
+                "only (this context: head_dim %d, %d per KV head)", what, c->cfg.head_dim,
+                c->cfg.n_heads_q / c->cfg.n_heads_kv);
+  return GQA_OK;
+}
+
 int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* kv,
                 const float* qkv, long long qkv_stride, float* out, long long out_stride,
                 int* d_pos, int advance, int wrap_lo, int wrap_hi) {
   if (n_layers < 1 || !kv || !qkv || !out || !d_pos)
     return fail(GQA_ERR_INVALID_ARG, "gqa_decode_layers: null argument or n_layers < 1");
-  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
-  if (qkv_stride < (long long)(nq + 2 * nkv) * kHeadDim || out_stride < (long long)nq * kHeadDim)
+  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv, hd = c->cfg.head_dim;
+  if (qkv_stride < (long long)(nq + 2 * nkv) * hd || out_stride < (long long)nq * hd)
     return fail(GQA_ERR_INVALID_ARG, "layer strides smaller than one layer's qkv / output");
   if ((qkv_stride & 3) || (out_stride & 3) || !aligned16(qkv) || !aligned16(out))
     return fail(GQA_ERR_INVALID_ARG, "qkv/out and their layer strides must be 16-byte aligned");
@@ -325,9 +359,12 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
     // Layer 0 may follow the kernel that advanced *d_pos: it reads pos only
     // after its dependency wait.  Later layers follow a combine/split of
     // the previous layer, which never writes pos or this layer's cache.
-    int rc = run_single(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max, true,
-                        out + l * out_stride, /*pdl_first=*/c->layers_pdl != 0,
-                        /*lengths_stable=*/l > 0);
+    int rc = c->generic
+                 ? run_generic(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max,
+                               out + l * out_stride, c->layers_pdl != 0)
+                 : run_single(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max, true,
+                              out + l * out_stride, /*pdl_first=*/c->layers_pdl != 0,
+                              /*lengths_stable=*/l > 0);
     if (rc != GQA_OK) return rc;
   }
   if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
@@ -452,11 +489,15 @@ const char* gqa_version(void) { return "gqa-b200 0.1 (sm_100a)"; }
 int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (!cfg || !out) return fail(GQA_ERR_INVALID_ARG, "gqa_create: null argument");
   *out = nullptr;
-  if (cfg->head_dim != kHeadDim)
-    return fail(GQA_ERR_UNSUPPORTED, "head_dim %d not built (only 128)", cfg->head_dim);
-  if (cfg->n_heads_kv < 1 || cfg->n_heads_q != 6 * cfg->n_heads_kv)
-    return fail(GQA_ERR_UNSUPPORTED, "n_heads_q must be 6 * n_heads_kv (got %d / %d)",
+  if (cfg->n_heads_kv < 1 || cfg->n_heads_q % cfg->n_heads_kv)
+    return fail(GQA_ERR_INVALID_ARG, "n_heads_q must be a multiple of n_heads_kv (got %d / %d)",
                 cfg->n_heads_q, cfg->n_heads_kv);
+  const int group = cfg->n_heads_q / cfg->n_heads_kv;
+  const bool tuned = cfg->head_dim == kHeadDim && group == 6;
+  if (!tuned && !generic_shape_built(cfg->head_dim, group))
+    return fail(GQA_ERR_UNSUPPORTED,
+                "shape not built: head_dim %d with %d q heads per KV head (built: 128 / 6, "
+                "64 / 7)", cfg->head_dim, group);
   if (cfg->t_max < 1 || !(cfg->rope_theta > 0.f))
     return fail(GQA_ERR_INVALID_ARG, "t_max must be >= 1 and rope_theta > 0");
   if ((long long)cfg->n_heads_kv * cfg->t_max * kHeadDim > (1LL << 40))
@@ -479,8 +520,11 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   // attention_gqa_benchmark.c:143: powf(ROPE_BASE, -2.0f * (float)tid / (float)HEAD_DIM),
   // evaluated once here with the host libm so the device multiplies the very
   // same fp32 inverse frequency by pos.
+  c->generic = !tuned;
   for (int i = 0; i < kHalf; ++i)
-    c->h_inv_freq[i] = powf(cfg->rope_theta, -2.0f * (float)i / (float)kHeadDim);
+    c->h_inv_freq[i] =
+        i < cfg->head_dim / 2 ? powf(cfg->rope_theta, -2.0f * (float)i / (float)cfg->head_dim)
+                              : 0.f;
   cudaError_t e = prepare_decode_kernels();
   if (e == cudaSuccess) e = prepare_prefill_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->inv_freq, sizeof(float) * kHalf);
@@ -491,6 +535,8 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->blk_h, sizeof(float) * block_d_ffn());
   if (e == cudaSuccess) e = prepare_block_kernels();
   if (e == cudaSuccess) e = prepare_head_kernels();
+  if (e == cudaSuccess && c->generic)
+    e = cudaMalloc(&c->gen_q, sizeof(float) * cfg->n_heads_q * cfg->head_dim);
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kCounterSlots);
   if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * kCounterSlots);
   if (e == cudaSuccess) {
@@ -518,6 +564,7 @@ int gqa_destroy(gqa_ctx* c) {
   if (c->blk_attn) cudaFree(c->blk_attn);
   if (c->blk_h) cudaFree(c->blk_h);
   if (c->head_best) cudaFree(c->head_best);
+  if (c->gen_q) cudaFree(c->gen_q);
   if (c->prefill_img) cudaFree(c->prefill_img);
   if (c->rope_cs) cudaFree(c->rope_cs);
   if (c->part_o) cudaFree(c->part_o);
@@ -557,6 +604,10 @@ int gqa_reserve(gqa_ctx* c, int n_seq, int max_len) {
   if (!c || n_seq < 1 || max_len < 1 || max_len > c->cfg.t_max)
     return fail(GQA_ERR_INVALID_ARG, "gqa_reserve: bad arguments");
   DeviceGuard g(c->device);
+  if (c->generic)
+    return ensure_scratch(c, (long long)n_seq * c->cfg.n_heads_q *
+                                 generic_plan_splits(c->cfg.n_heads_kv, max_len, c->n_sm),
+                          nullptr);
   const int single = ((plan_splits_single(c, c->cfg.n_heads_kv, max_len) + kCluster - 1) /
                       kCluster) * kCluster;
   const int batched = ceil_div(max_len, batch_chunk(c, max_len));
@@ -576,7 +627,8 @@ int gqa_device_status(gqa_ctx* c, int* status, int clear) {
 int gqa_kv_alloc(gqa_ctx* c, int n_layers, gqa_layer_kv* out) {
   if (!c || !out || n_layers < 1) return fail(GQA_ERR_INVALID_ARG, "gqa_kv_alloc: bad arguments");
   DeviceGuard g(c->device);
-  const size_t bytes = sizeof(float) * (size_t)c->cfg.n_heads_kv * c->cfg.t_max * kHeadDim;
+  const size_t bytes =
+      sizeof(float) * (size_t)c->cfg.n_heads_kv * c->cfg.t_max * c->cfg.head_dim;
   for (int l = 0; l < n_layers; ++l) out[l].k_cache = out[l].v_cache = nullptr;
   for (int l = 0; l < n_layers; ++l) {
     if (cudaMalloc(&out[l].k_cache, bytes) != cudaSuccess ||
@@ -616,6 +668,8 @@ int gqa_layer_attention_out(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv*
   Lengths len{};
   len.pos_imm = pos;
   len.seqlen_imm = seq_len;
+  if (c->generic) return run_generic(c, (cudaStream_t)stream, kv, qkv, len, seq_len, out,
+                                     c->pdl != 0);
   return run_single(c, (cudaStream_t)stream, kv, qkv, len, seq_len, true, out, c->pdl != 0,
                     true);
 }
@@ -710,6 +764,7 @@ int gqa_graph_destroy(gqa_graph* gr) {
 int gqa_rope_kv_append(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, float* q,
                        const float* k, const float* v, int pos) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_rope_kv_append") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_kv(c, kv);
   if (rc != GQA_OK) return rc;
   if (!q || !k || !v) return fail(GQA_ERR_INVALID_ARG, "null q/k/v");
@@ -735,6 +790,7 @@ int gqa_rope_kv_append(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, 
 int gqa_decode(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, const float* q_rot,
                int seq_len, float* out) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_decode") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_kv(c, kv);
   if (rc != GQA_OK) return rc;
   if (!q_rot || !out || !aligned16(q_rot) || !aligned16(out))
@@ -753,6 +809,7 @@ int gqa_decode_batched(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const*
                        float* const* v_caches, const float* qkv, long long qkv_stride,
                        const int* seq_lens, int max_len, float* out, long long out_stride) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_decode_batched") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_seq < 1 || n_seq > 65535 || !k_caches || !v_caches || !qkv || !seq_lens || !out)
     return fail(GQA_ERR_INVALID_ARG, "gqa_decode_batched: null argument or n_seq out of range");
   if (max_len < 1 || max_len > c->cfg.t_max)
@@ -800,6 +857,7 @@ int gqa_decode_split_partial(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv
                              const float* q_rot, int t_begin, int t_end, float* m, float* l,
                              float* o) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_decode_split_partial") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_kv(c, kv);
   if (rc != GQA_OK) return rc;
   if (!q_rot || !m || !l || !o || !aligned16(q_rot))
@@ -843,6 +901,7 @@ int gqa_decode_kv_shard(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
                         const float* qkv, int pos, int shard_begin, int shard_rows, float* m,
                         float* l, float* o) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_decode_kv_shard") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (!m || !l || !o) return fail(GQA_ERR_INVALID_ARG, "null argument");
   DeviceGuard g(c->device);
   cudaStream_t st = (cudaStream_t)stream;
@@ -859,6 +918,7 @@ int gqa_decode_kv_shard(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
 int gqa_attention_block(gqa_ctx* c, gqa_stream_t stream, const gqa_block_weights* w,
                         const gqa_layer_kv* kv, float* state, int pos, int seq_len) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_attention_block") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_block_weights(c, w);
   if (rc != GQA_OK) return rc;
   rc = check_kv(c, kv);
@@ -878,6 +938,7 @@ int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
                                const gqa_block_weights* w, const gqa_layer_kv* kv, float* state,
                                int* d_pos, int advance, int wrap_lo, int wrap_hi) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_attention_block_layers") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_layers < 1 || !w || !kv || !d_pos || !state || !aligned16(state))
     return fail(GQA_ERR_INVALID_ARG, "gqa_attention_block_layers: bad arguments");
   for (int l = 0; l < n_layers; ++l) {
@@ -903,6 +964,7 @@ int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
 
 int gqa_ffn_block(gqa_ctx* c, gqa_stream_t stream, const gqa_ffn_weights* w, float* state) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_ffn_block") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_ffn_weights(c, w);
   if (rc != GQA_OK) return rc;
   if (!state || !aligned16(state)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned state");
@@ -914,6 +976,7 @@ int gqa_decoder_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers, const gqa_
                        const gqa_ffn_weights* ffn, const gqa_layer_kv* kv, float* state,
                        int* d_pos, int advance, int wrap_lo, int wrap_hi) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_decoder_layers") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_layers < 1 || !attn || !ffn || !kv || !d_pos || !state || !aligned16(state))
     return fail(GQA_ERR_INVALID_ARG, "gqa_decoder_layers: bad arguments");
   for (int l = 0; l < n_layers; ++l) {
@@ -955,6 +1018,7 @@ int gqa_lm_head_pack(gqa_ctx* c, gqa_stream_t stream, const void* q6k, int n_row
 int gqa_lm_head(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
                 const float* gamma, const float* state, float* logits, int* token) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_lm_head") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_head(c, packed, n_rows, gamma);
   if (rc != GQA_OK) return rc;
   if (!state || !aligned16(state)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned state");
@@ -969,6 +1033,7 @@ int gqa_lm_head(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
 int gqa_token_embedding(gqa_ctx* c, gqa_stream_t stream, const void* table, int n_rows,
                         const int* d_token, float* state) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_token_embedding") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (c->cfg.n_heads_q * kHeadDim != block_d_model())
     return fail(GQA_ERR_UNSUPPORTED, "embedding built for d_model %d", block_d_model());
   if (!table || !d_token || !state || n_rows < 1)
@@ -982,6 +1047,7 @@ int gqa_token_embedding(gqa_ctx* c, gqa_stream_t stream, const void* table, int 
 int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float* state,
                      int* d_token, int* d_pos, float* logits, int wrap_lo, int wrap_hi) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_decode_token") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (!m || m->n_layers < 1 || !m->attn || !m->ffn || !m->kv || !m->token_embd || !d_token ||
       !d_pos || !state || !aligned16(state))
     return fail(GQA_ERR_INVALID_ARG, "gqa_decode_token: bad arguments");
@@ -1015,6 +1081,7 @@ int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float*
 
 int gqa_exchange_create(gqa_ctx* c, int rank, int world, gqa_exchange** out, void* ipc_handle) {
   if (!c || !out || !ipc_handle) return fail(GQA_ERR_INVALID_ARG, "null argument");
+  if (tuned_only(c, "gqa_exchange_create") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   *out = nullptr;
   if (world < 1 || world > kMaxExchangeWorld || rank < 0 || rank >= world)
     return fail(GQA_ERR_INVALID_ARG, "rank %d / world %d invalid (world <= %d)", rank, world,
@@ -1075,6 +1142,7 @@ int gqa_decode_kv_shard_exchange(gqa_ctx* c, gqa_exchange* x, gqa_stream_t strea
                                  const gqa_layer_kv* kv, const float* qkv, int pos,
                                  int shard_begin, int shard_rows, float* out) {
   if (!c || !x || !out) return fail(GQA_ERR_INVALID_ARG, "null argument");
+  if (tuned_only(c, "gqa_decode_kv_shard_exchange") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (x->ctx != c || !x->opened)
     return fail(GQA_ERR_INVALID_ARG, "exchange belongs to another context or is not opened");
   if (!aligned16(out)) return fail(GQA_ERR_INVALID_ARG, "out must be 16-byte aligned");
@@ -1103,6 +1171,7 @@ int gqa_exchange_destroy(gqa_exchange* x) {
 int gqa_lse_combine(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows, const float* m,
                     const float* l, const float* o, float* out) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_lse_combine") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_parts < 0 || n_parts > 4096 || n_rows < 1 || n_rows > 65535 || !m || !l || !o || !out)
     return fail(GQA_ERR_INVALID_ARG, "gqa_lse_combine: bad arguments");
   DeviceGuard g(c->device);
@@ -1124,6 +1193,7 @@ int gqa_lse_combine(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows, co
 int gqa_lse_combine_packed(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows,
                            const float* packed, long long part_stride, float* out) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_lse_combine_packed") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_parts < 0 || n_parts > 4096 || n_rows < 1 || n_rows > 65535 || !packed || !out ||
       part_stride < (long long)n_rows * (2 + kHeadDim))
     return fail(GQA_ERR_INVALID_ARG, "gqa_lse_combine_packed: bad arguments");
@@ -1146,6 +1216,7 @@ int gqa_lse_combine_packed(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_r
 int gqa_prefill_bf16(gqa_ctx* c, gqa_stream_t stream, int n_seq, int seq_len, const float* qkv,
                      float* out, float* const* k_caches, float* const* v_caches) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (tuned_only(c, "gqa_prefill_bf16") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_seq < 1 || n_seq > 65535 || !qkv || !out)
     return fail(GQA_ERR_INVALID_ARG, "gqa_prefill_bf16: null argument or n_seq out of range");
   if (seq_len < 128 || seq_len % 128 != 0 || seq_len > 65535 * 128)

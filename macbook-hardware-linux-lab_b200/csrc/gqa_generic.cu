@@ -1,0 +1,326 @@
+// The GQA decode step for model shapes other than the one the tuned kernels
+// are built for (head_dim 128, 6 query heads per KV head, gqa_decode.cu):
+// Qwen2.5-0.5B's head_dim 64 with 7 query heads per KV head
+// (generate_stream_05b.c:19-31; its attention kernels,
+// kernel_decoder_layer_05b.cl:142-380, are the 1.5B ones at these sizes).
+// Same math as the reference: RoPE on pairs (i, i + D/2) with
+// theta_i = pos * base^(-2i/D), the new K row (rotated) and V row appended at
+// pos, s = (q . k) * (1 / sqrt(D)) over rows t < seq_len, a stable softmax and
+// the PV product; here split over KV ranges and merged by log-sum-exp.
+//
+//   rope_append_generic_kernel  one CTA of D/2 threads: rotated q heads into a
+//                               scratch row (the caller's qkv stays as given),
+//                               K/V rows into the caches (the reference's
+//                               kernel_rope_and_kv_append, one thread per pair)
+//   split_generic_kernel        one CTA per (split, KV head): its rows in tiles
+//                               of 64 staged in shared memory by coalesced
+//                               float4 loads; scores of the G heads per row
+//                               (thread = row x head set, float4 reads rotated
+//                               per row so a warp's 32 rows hit different banks),
+//                               a per-tile max and exp, then PV with one thread
+//                               per (head, dim) output; running (m, l, o) per head
+//   merge_generic_kernel        one CTA per q head: the splits' (m, l, o) merged
+//                               by log-sum-exp into the output row
+#include "gqa_common.cuh"
+
+#include <math_constants.h>
+
+namespace gqa {
+
+constexpr int kGenThreads = 256;
+constexpr int kGenTile = 64;            // rows per shared-memory tile
+constexpr int kGenMaxSplits = 1024;
+
+template <int D, int G>
+struct GenShape {
+  static constexpr int kChunks = D / 4;                 // float4 per row
+  static constexpr int kOut = G * D;                    // outputs per KV head
+  static constexpr int kOutPerThread = (kOut + kGenThreads - 1) / kGenThreads;
+  static constexpr int kHeadSets = kGenThreads / kGenTile;          // 4
+  static constexpr int kHeadsPerThread = (G + kHeadSets - 1) / kHeadSets;
+  static_assert(D % 4 == 0 && D <= 128, "head_dim");
+  static_assert(kGenThreads % kGenTile == 0, "tile");
+};
+
+struct GenParams {
+  const float* q;    // [n_q][D] new token, before RoPE
+  float* q_rot;      // [n_q][D] scratch: q after RoPE
+  const float* k;    // [n_kv][D] new token
+  const float* v;
+  float* k_cache;    // [n_kv][t_max][D]
+  float* v_cache;
+  Lengths len;
+  int t_max, n_q, n_kv, n_splits, rows_per_split;
+  const float* inv_freq;  // [D / 2]
+  float scale;            // 1 / sqrt(D)
+  float* part_o;          // [n_q][n_splits][D]
+  float* part_ml;         // [n_q][n_splits][2]
+  float* out;             // [n_q][D]
+  int* status;
+};
+
+// pos and seq_len of the step (from device memory when len.pos_dev is set,
+// seq_len = pos + 1 then); false when they leave the cache.
+__device__ __forceinline__ bool gen_lengths(const GenParams& p, int& pos, int& seq_len) {
+  if (p.len.pos_dev) {
+    pos = *p.len.pos_dev;
+    seq_len = pos + 1;
+  } else {
+    pos = p.len.pos_imm;
+    seq_len = p.len.seqlen_imm;
+  }
+  return pos >= 0 && pos < p.t_max && seq_len >= 1 && seq_len <= p.t_max;
+}
+
+template <int D>
+__global__ void __launch_bounds__(D / 2) rope_append_generic_kernel(const GenParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  int pos, seq_len;
+  if (!gen_lengths(p, pos, seq_len)) {
+    if (threadIdx.x == 0) atomicOr(p.status, kStatusBadLength);
+    return;
+  }
+  constexpr int H = D / 2;
+  const int i = threadIdx.x;
+  float sn, cs;
+  sincosf((float)pos * p.inv_freq[i], &sn, &cs);
+  for (int h = 0; h < p.n_q; ++h) {
+    const float* qh = p.q + (long long)h * D;
+    const float q0 = qh[i], q1 = qh[i + H];
+    p.q_rot[(long long)h * D + i] = q0 * cs - q1 * sn;
+    p.q_rot[(long long)h * D + i + H] = q0 * sn + q1 * cs;
+  }
+  for (int h = 0; h < p.n_kv; ++h) {
+    const float k0 = p.k[h * D + i], k1 = p.k[h * D + i + H];
+    const long long row = ((long long)h * p.t_max + pos) * D;
+    p.k_cache[row + i] = k0 * cs - k1 * sn;
+    p.k_cache[row + i + H] = k0 * sn + k1 * cs;
+    p.v_cache[row + i] = p.v[h * D + i];
+    p.v_cache[row + i + H] = p.v[h * D + i + H];
+  }
+}
+
+template <int D, int G>
+struct GenSmem {
+  float q[G][D];
+  float k[kGenTile][D];
+  float v[kGenTile][D];
+  float s[G][kGenTile];     // scores, then weights e^(s - m)
+  float m[G], corr[G];      // running max per head, rescale of this tile
+};
+
+template <int D, int G>
+__global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenParams p) {
+  using S = GenShape<D, G>;
+  __shared__ __align__(16) GenSmem<D, G> sm;
+  pdl_wait();
+  pdl_launch_dependents();
+  int pos, seq_len;
+  if (!gen_lengths(p, pos, seq_len)) return;  // the append kernel reported it
+  const int split = blockIdx.x, hkv = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t0 = split * p.rows_per_split;
+  const int t1 = min(seq_len, t0 + p.rows_per_split);
+  const float* kc = p.k_cache + (long long)hkv * p.t_max * D;
+  const float* vc = p.v_cache + (long long)hkv * p.t_max * D;
+  for (int i = tid; i < G * D; i += kGenThreads)
+    (&sm.q[0][0])[i] = p.q_rot[(long long)hkv * G * D + i];
+  if (tid < G) sm.m[tid] = -CUDART_INF_F;
+  float o[S::kOutPerThread], l_run = 0.f;  // l_run: thread tid < G holds head tid's l
+#pragma unroll
+  for (int k = 0; k < S::kOutPerThread; ++k) o[k] = 0.f;
+  __syncthreads();
+
+  for (int tb = t0; tb < t1; tb += kGenTile) {
+    const int nrow = min(kGenTile, t1 - tb);
+    // ---- stage the tile's K and V rows ----
+    for (int i = tid; i < nrow * S::kChunks; i += kGenThreads) {
+      const int r = i / S::kChunks, c = i % S::kChunks;
+      reinterpret_cast<float4*>(&sm.k[r][0])[c] =
+          __ldcs(reinterpret_cast<const float4*>(kc + (long long)(tb + r) * D) + c);
+      reinterpret_cast<float4*>(&sm.v[r][0])[c] =
+          __ldcs(reinterpret_cast<const float4*>(vc + (long long)(tb + r) * D) + c);
+    }
+    __syncthreads();
+    // ---- scores: thread (set, r) takes heads set, set + 4, ... of row r ----
+    {
+      const int r = tid % kGenTile, set = tid / kGenTile;
+      float acc[S::kHeadsPerThread];
+#pragma unroll
+      for (int j = 0; j < S::kHeadsPerThread; ++j) acc[j] = 0.f;
+      if (r < nrow) {
+#pragma unroll 4
+        for (int cc = 0; cc < S::kChunks; ++cc) {
+          const int c = (cc + r) % S::kChunks;  // rotated: the warp's rows on different banks
+          const float4 kv = reinterpret_cast<const float4*>(&sm.k[r][0])[c];
+#pragma unroll
+          for (int j = 0; j < S::kHeadsPerThread; ++j) {
+            const int g = set + j * S::kHeadSets;
+            if (g < G) {
+              const float4 qv = reinterpret_cast<const float4*>(&sm.q[g][0])[c];
+              acc[j] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, acc[j]))));
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < S::kHeadsPerThread; ++j) {
+        const int g = set + j * S::kHeadSets;
+        if (g < G) sm.s[g][r] = r < nrow ? acc[j] * p.scale : -CUDART_INF_F;
+      }
+    }
+    __syncthreads();
+    // ---- per-head tile max -> new running max and the rescale factor ----
+    for (int g = warp; g < G; g += kGenThreads / 32) {
+      float mx = fmaxf(sm.s[g][lane], sm.s[g][lane + 32]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      if (lane == 0) {
+        const float m_new = fmaxf(sm.m[g], mx);
+        sm.corr[g] = sm.m[g] == -CUDART_INF_F ? 0.f : expf(sm.m[g] - m_new);
+        sm.m[g] = m_new;
+      }
+    }
+    __syncthreads();
+    // ---- weights e^(s - m) ----
+    for (int i = tid; i < G * kGenTile; i += kGenThreads) {
+      const int g = i / kGenTile, r = i % kGenTile;
+      const float sv = sm.s[g][r];
+      sm.s[g][r] = sv == -CUDART_INF_F ? 0.f : expf(sv - sm.m[g]);
+    }
+    __syncthreads();
+    // ---- l and PV: thread owns outputs tid + k * kGenThreads = (g, d) ----
+    if (tid < G) {
+      float ls = 0.f;
+      for (int r = 0; r < nrow; ++r) ls += sm.s[tid][r];
+      l_run = l_run * sm.corr[tid] + ls;
+    }
+#pragma unroll
+    for (int k = 0; k < S::kOutPerThread; ++k) {
+      const int idx = tid + k * kGenThreads;
+      if (idx < S::kOut) {
+        const int g = idx / D, d = idx % D;
+        float acc = o[k] * sm.corr[g];
+        for (int r = 0; r < nrow; ++r) acc = fmaf(sm.s[g][r], sm.v[r][d], acc);
+        o[k] = acc;
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- the split's partial: (m, l, un-normalised o) per q head ----
+  const int qh0 = hkv * G;
+#pragma unroll
+  for (int k = 0; k < S::kOutPerThread; ++k) {
+    const int idx = tid + k * kGenThreads;
+    if (idx < S::kOut) {
+      const int g = idx / D, d = idx % D;
+      p.part_o[((long long)(qh0 + g) * p.n_splits + split) * D + d] = o[k];
+    }
+  }
+  if (tid < G) {
+    float* ml = p.part_ml + ((long long)(qh0 + tid) * p.n_splits + split) * 2;
+    ml[0] = t1 > t0 ? sm.m[tid] : -CUDART_INF_F;
+    ml[1] = t1 > t0 ? l_run : 0.f;
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(D) merge_generic_kernel(const GenParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  int pos, seq_len;
+  if (!gen_lengths(p, pos, seq_len)) return;
+  const int h = blockIdx.x, d = threadIdx.x;
+  const float* ml = p.part_ml + (long long)h * p.n_splits * 2;
+  float M = -CUDART_INF_F;
+  for (int i = 0; i < p.n_splits; ++i)
+    if (ml[2 * i + 1] > 0.f) M = fmaxf(M, ml[2 * i]);
+  float L = 0.f, O = 0.f;
+  if (M != -CUDART_INF_F) {
+    const float* po = p.part_o + (long long)h * p.n_splits * D + d;
+    for (int i = 0; i < p.n_splits; ++i) {
+      const float li = ml[2 * i + 1];
+      if (li > 0.f) {
+        const float w = expf(ml[2 * i] - M);
+        L = fmaf(w, li, L);
+        O = fmaf(w, po[(long long)i * D], O);
+      }
+    }
+  }
+  p.out[(long long)h * D + d] = L > 0.f ? O / L : 0.f;
+}
+
+// ---------------------------------------------------------------------------
+// Launcher: append, split, merge, chained by programmatic dependent launch.
+// ---------------------------------------------------------------------------
+template <typename K>
+static cudaError_t gen_launch(K kernel, dim3 grid, dim3 block, const GenParams& p,
+                              cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  GenParams copy = p;
+  void* args[] = {&copy};
+  return cudaLaunchKernelExC(&cfg, (const void*)kernel, args);
+}
+
+bool generic_shape_built(int head_dim, int group) { return head_dim == 64 && group == 7; }
+
+int generic_max_splits() { return kGenMaxSplits; }
+
+// Splits for a cache of up to plan_len rows: at least one tile each, enough
+// CTAs to cover the device twice.
+int generic_plan_splits(int n_kv, int plan_len, int n_sm) {
+  int by_rows = (plan_len + kGenTile - 1) / kGenTile;
+  int by_sms = (2 * n_sm + n_kv - 1) / n_kv;
+  int s = by_rows < by_sms ? by_rows : by_sms;
+  if (s < 1) s = 1;
+  return s > kGenMaxSplits ? kGenMaxSplits : s;
+}
+
+cudaError_t launch_generic_attention(const float* qkv, float* q_rot, float* out, float* k_cache,
+                                     float* v_cache, Lengths len, int t_max, int n_q, int n_kv,
+                                     int head_dim, int n_splits, int plan_len,
+                                     const float* inv_freq, float* part_o, float* part_ml,
+                                     int* status, cudaStream_t st, bool pdl_first, bool pdl) {
+  if (head_dim != 64 || n_q != 7 * n_kv) return cudaErrorInvalidValue;
+  constexpr int D = 64, G = 7;
+  GenParams p{};
+  p.q = qkv;
+  p.q_rot = q_rot;
+  p.k = qkv + (long long)n_q * D;
+  p.v = p.k + (long long)n_kv * D;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.len = len;
+  p.t_max = t_max;
+  p.n_q = n_q;
+  p.n_kv = n_kv;
+  p.n_splits = n_splits;
+  // rows per split: whole tiles, covering plan_len rows
+  const int per = (plan_len + n_splits - 1) / n_splits;
+  p.rows_per_split = (per + kGenTile - 1) / kGenTile * kGenTile;
+  p.inv_freq = inv_freq;
+  p.scale = 1.0f / sqrtf((float)D);
+  p.part_o = part_o;
+  p.part_ml = part_ml;
+  p.out = out;
+  p.status = status;
+  cudaError_t e =
+      gen_launch(rope_append_generic_kernel<D>, dim3(1), dim3(D / 2), p, st, pdl_first);
+  if (e == cudaSuccess)
+    e = gen_launch(split_generic_kernel<D, G>, dim3(n_splits, n_kv), dim3(kGenThreads), p, st,
+                   pdl);
+  if (e == cudaSuccess) e = gen_launch(merge_generic_kernel<D>, dim3(n_q), dim3(D), p, st, pdl);
+  return e;
+}
+
+}  // namespace gqa

@@ -99,11 +99,13 @@ def inv_freq(rope_base: float = 1e6, head_dim: int = 128) -> np.ndarray:
 
 def layer_attention(qkv: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, pos: int,
                     seq_len: int, n_heads_q: int = 12, n_heads_kv: int = 2,
-                    rope_base: float = 1e6) -> None:
-    """In place: caches [n_kv][t_max][128] get row pos, qkv[:n_q*128] becomes attn_out."""
+                    rope_base: float = 1e6, head_dim: int = 128) -> None:
+    """In place: caches [n_kv][t_max][head_dim] get row pos, qkv[:n_q*head_dim]
+    becomes attn_out.  The restatement's loops take any head_dim; at 128 it is
+    pinned to the compiled reference bit for bit."""
     t_max = k_cache.shape[1]
     _lib().oracle_layer_attention(_fptr(qkv), _fptr(k_cache), _fptr(v_cache), pos, seq_len, t_max,
-                                  n_heads_q, n_heads_kv, 128, rope_base)
+                                  n_heads_q, n_heads_kv, head_dim, rope_base)
 
 
 def rope_kv_append(q, k, v, k_cache, v_cache, pos, n_heads_q=12, n_heads_kv=2, rope_base=1e6):
