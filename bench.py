@@ -446,8 +446,8 @@ def run_resident(args, g, ctx, rank, world, local):
 
     # mirrors the library's split plan for pos read from the device (planned for t_max)
     n_sm = torch.cuda.get_device_properties(local).multi_processor_count
-    if generic:  # append, split, merge per layer (csrc/gqa_generic.cu)
-        kernels_per_step = L_layers * 3 + 1
+    if generic:  # split (RoPE + append fused), merge per layer (csrc/gqa_generic.cu)
+        kernels_per_step = L_layers * 2 + 1
     else:
         target = args.target_ctas or n_sm
         quant = g.gqa.VARIANT_QUANT[3 if args.variant < 0 else args.variant]
@@ -460,7 +460,7 @@ def run_resident(args, g, ctx, rank, world, local):
                h2d=L_layers * qkv_w * 4, d2h=L_layers * out_w * 4, tokens=args.steps,
                dominant_launches=L_layers * args.steps)
     if generic:
-        res.update(kernel="split_generic_kernel<64, 7> (+ append and merge)",
+        res.update(kernel="split_generic_kernel<64, 7> (+ merge)",
                    data="synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal), "
                         "Qwen2.5-0.5B attention shape")
     return res

@@ -60,11 +60,11 @@ cudaError_t launch_exchange_combine(const CombineParams& local, uint2* const* in
 bool generic_shape_built(int head_dim, int group);
 int generic_max_splits();
 int generic_plan_splits(int n_kv, int plan_len, int n_sm);
-cudaError_t launch_generic_attention(const float* qkv, float* q_rot, float* out, float* k_cache,
-                                     float* v_cache, Lengths len, int t_max, int n_q, int n_kv,
-                                     int head_dim, int n_splits, int plan_len,
-                                     const float* inv_freq, float* part_o, float* part_ml,
-                                     int* status, cudaStream_t st, bool pdl_first, bool pdl);
+cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cache, float* v_cache,
+                                     Lengths len, int t_max, int n_q, int n_kv, int head_dim,
+                                     int n_splits, int plan_len, const float* inv_freq,
+                                     float* part_o, float* part_ml, int* status, cudaStream_t st,
+                                     bool pdl_first, bool pdl);
 size_t lm_head_packed_bytes(long long n_rows);
 int lm_head_grid(int n_sm);
 size_t lm_head_best_bytes(int grid);
@@ -125,7 +125,6 @@ struct gqa_ctx {
   float* blk_attn = nullptr;  // attention block workspace: attention output
   float* blk_h = nullptr;     // FFN workspace: silu(gate) * up
   bool generic = false;       // a shape the tuned kernels are not built for (gqa_generic.cu)
-  float* gen_q = nullptr;     // generic path: rotated q of the step [n_q][head_dim]
   void* head_best = nullptr;  // LM head: per-CTA greedy picks
   int head_grid = 0;          // LM head CTAs
   __nv_bfloat16* prefill_img = nullptr;  // bf16 tile images for the prefill
@@ -315,17 +314,17 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
   return GQA_OK;
 }
 
-// The decode step on the shape-generic kernels (gqa_generic.cu): RoPE +
-// append into the context's q scratch and the cache, split partials, merge.
+// The decode step on the shape-generic kernels (gqa_generic.cu): split
+// partials (RoPE and the append fused), then the merge.
 int run_generic(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
                 Lengths len, int plan_len, float* out, bool pdl_first) {
   const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
   const int n_splits = generic_plan_splits(nkv, plan_len, c->n_sm);
   int rc = ensure_scratch(c, (long long)nq * n_splits, st);
   if (rc != GQA_OK) return rc;
-  GQA_CUDA(launch_generic_attention(qkv, c->gen_q, out, kv->k_cache, kv->v_cache, len,
-                                    c->cfg.t_max, nq, nkv, c->cfg.head_dim, n_splits, plan_len,
-                                    c->inv_freq, c->part_o, c->part_ml, c->status, st, pdl_first,
+  GQA_CUDA(launch_generic_attention(qkv, out, kv->k_cache, kv->v_cache, len, c->cfg.t_max, nq,
+                                    nkv, c->cfg.head_dim, n_splits, plan_len, c->inv_freq,
+                                    c->part_o, c->part_ml, c->status, st, pdl_first,
                                     c->layers_pdl != 0));
   return GQA_OK;
 }
@@ -535,8 +534,6 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->blk_h, sizeof(float) * block_d_ffn());
   if (e == cudaSuccess) e = prepare_block_kernels();
   if (e == cudaSuccess) e = prepare_head_kernels();
-  if (e == cudaSuccess && c->generic)
-    e = cudaMalloc(&c->gen_q, sizeof(float) * cfg->n_heads_q * cfg->head_dim);
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kCounterSlots);
   if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * kCounterSlots);
   if (e == cudaSuccess) {
@@ -564,7 +561,6 @@ int gqa_destroy(gqa_ctx* c) {
   if (c->blk_attn) cudaFree(c->blk_attn);
   if (c->blk_h) cudaFree(c->blk_h);
   if (c->head_best) cudaFree(c->head_best);
-  if (c->gen_q) cudaFree(c->gen_q);
   if (c->prefill_img) cudaFree(c->prefill_img);
   if (c->rope_cs) cudaFree(c->rope_cs);
   if (c->part_o) cudaFree(c->part_o);

@@ -8,11 +8,13 @@
 // pos, s = (q . k) * (1 / sqrt(D)) over rows t < seq_len, a stable softmax and
 // the PV product; here split over KV ranges and merged by log-sum-exp.
 //
-//   rope_append_generic_kernel  one CTA of D/2 threads: rotated q heads into a
-//                               scratch row (the caller's qkv stays as given),
-//                               K/V rows into the caches (the reference's
-//                               kernel_rope_and_kv_append, one thread per pair)
-//   split_generic_kernel        one CTA per (split, KV head): its rows in tiles
+//   split_generic_kernel        one CTA per (split, KV head): RoPE of its KV
+//                               head's q heads into shared memory (the
+//                               caller's qkv stays as given), and on the CTA
+//                               whose range holds pos the new K (rotated) and
+//                               V rows into the caches -- the reference's
+//                               kernel_rope_and_kv_append, one thread per pair;
+//                               then its rows in tiles
 //                               of 64 staged in shared memory by coalesced
 //                               float4 loads; scores of the G heads per row
 //                               (thread = row x head set, float4 reads rotated
@@ -44,7 +46,6 @@ struct GenShape {
 
 struct GenParams {
   const float* q;    // [n_q][D] new token, before RoPE
-  float* q_rot;      // [n_q][D] scratch: q after RoPE
   const float* k;    // [n_kv][D] new token
   const float* v;
   float* k_cache;    // [n_kv][t_max][D]
@@ -72,38 +73,11 @@ __device__ __forceinline__ bool gen_lengths(const GenParams& p, int& pos, int& s
   return pos >= 0 && pos < p.t_max && seq_len >= 1 && seq_len <= p.t_max;
 }
 
-template <int D>
-__global__ void __launch_bounds__(D / 2) rope_append_generic_kernel(const GenParams p) {
-  pdl_wait();
-  pdl_launch_dependents();
-  int pos, seq_len;
-  if (!gen_lengths(p, pos, seq_len)) {
-    if (threadIdx.x == 0) atomicOr(p.status, kStatusBadLength);
-    return;
-  }
-  constexpr int H = D / 2;
-  const int i = threadIdx.x;
-  float sn, cs;
-  sincosf((float)pos * p.inv_freq[i], &sn, &cs);
-  for (int h = 0; h < p.n_q; ++h) {
-    const float* qh = p.q + (long long)h * D;
-    const float q0 = qh[i], q1 = qh[i + H];
-    p.q_rot[(long long)h * D + i] = q0 * cs - q1 * sn;
-    p.q_rot[(long long)h * D + i + H] = q0 * sn + q1 * cs;
-  }
-  for (int h = 0; h < p.n_kv; ++h) {
-    const float k0 = p.k[h * D + i], k1 = p.k[h * D + i + H];
-    const long long row = ((long long)h * p.t_max + pos) * D;
-    p.k_cache[row + i] = k0 * cs - k1 * sn;
-    p.k_cache[row + i + H] = k0 * sn + k1 * cs;
-    p.v_cache[row + i] = p.v[h * D + i];
-    p.v_cache[row + i + H] = p.v[h * D + i + H];
-  }
-}
-
 template <int D, int G>
 struct GenSmem {
-  float q[G][D];
+  float q[G][D];            // rotated q of the KV head's G q heads
+  float knew[D], vnew[D];   // the new row (owner CTA only)
+  float rope[D / 2][2];     // (cos, sin) per pair
   float k[kGenTile][D];
   float v[kGenTile][D];
   float s[G][kGenTile];     // scores, then weights e^(s - m)
@@ -117,15 +91,51 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
   pdl_wait();
   pdl_launch_dependents();
   int pos, seq_len;
-  if (!gen_lengths(p, pos, seq_len)) return;  // the append kernel reported it
+  if (!gen_lengths(p, pos, seq_len)) {
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+      atomicOr(p.status, kStatusBadLength);
+    return;
+  }
+  constexpr int H = D / 2;
   const int split = blockIdx.x, hkv = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t0 = split * p.rows_per_split;
   const int t1 = min(seq_len, t0 + p.rows_per_split);
-  const float* kc = p.k_cache + (long long)hkv * p.t_max * D;
-  const float* vc = p.v_cache + (long long)hkv * p.t_max * D;
-  for (int i = tid; i < G * D; i += kGenThreads)
-    (&sm.q[0][0])[i] = p.q_rot[(long long)hkv * G * D + i];
+  float* kc = p.k_cache + (long long)hkv * p.t_max * D;
+  float* vc = p.v_cache + (long long)hkv * p.t_max * D;
+  // The split whose range holds pos (the last one when pos lies past them
+  // all) appends the new row; only it may attend that row.
+  const bool owner = split == min(pos / p.rows_per_split, p.n_splits - 1);
+
+  // ---- RoPE: theta_i = pos * inv_freq[i], pairs (i, i + D/2) ----
+  if (tid < H) {
+    float sn, cs;
+    sincosf((float)pos * p.inv_freq[tid], &sn, &cs);
+    sm.rope[tid][0] = cs;
+    sm.rope[tid][1] = sn;
+  }
+  __syncthreads();
+  for (int i = tid; i < G * H; i += kGenThreads) {
+    const int g = i / H, j = i % H;
+    const float* qh = p.q + (long long)(hkv * G + g) * D;
+    const float q0 = qh[j], q1 = qh[j + H], cs = sm.rope[j][0], sn = sm.rope[j][1];
+    sm.q[g][j] = q0 * cs - q1 * sn;
+    sm.q[g][j + H] = q0 * sn + q1 * cs;
+  }
+  if (owner && tid < H) {
+    const float k0 = p.k[hkv * D + tid], k1 = p.k[hkv * D + tid + H];
+    const float cs = sm.rope[tid][0], sn = sm.rope[tid][1];
+    const float kr0 = k0 * cs - k1 * sn, kr1 = k0 * sn + k1 * cs;
+    const float v0 = p.v[hkv * D + tid], v1 = p.v[hkv * D + tid + H];
+    kc[(long long)pos * D + tid] = kr0;
+    kc[(long long)pos * D + tid + H] = kr1;
+    vc[(long long)pos * D + tid] = v0;
+    vc[(long long)pos * D + tid + H] = v1;
+    sm.knew[tid] = kr0;
+    sm.knew[tid + H] = kr1;
+    sm.vnew[tid] = v0;
+    sm.vnew[tid + H] = v1;
+  }
   if (tid < G) sm.m[tid] = -CUDART_INF_F;
   float o[S::kOutPerThread], l_run = 0.f;  // l_run: thread tid < G holds head tid's l
 #pragma unroll
@@ -143,6 +153,13 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
           __ldcs(reinterpret_cast<const float4*>(vc + (long long)(tb + r) * D) + c);
     }
     __syncthreads();
+    if (owner && pos >= tb && pos < tb + nrow) {  // the row just appended, as written
+      for (int i = tid; i < D; i += kGenThreads) {
+        sm.k[pos - tb][i] = sm.knew[i];
+        sm.v[pos - tb][i] = sm.vnew[i];
+      }
+      __syncthreads();
+    }
     // ---- scores: thread (set, r) takes heads set, set + 4, ... of row r ----
     {
       const int r = tid % kGenTile, set = tid / kGenTile;
@@ -253,7 +270,8 @@ __global__ void __launch_bounds__(D) merge_generic_kernel(const GenParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// Launcher: append, split, merge, chained by programmatic dependent launch.
+// Launcher: split (with RoPE and the append), merge, chained by programmatic
+// dependent launch.
 // ---------------------------------------------------------------------------
 template <typename K>
 static cudaError_t gen_launch(K kernel, dim3 grid, dim3 block, const GenParams& p,
@@ -286,16 +304,15 @@ int generic_plan_splits(int n_kv, int plan_len, int n_sm) {
   return s > kGenMaxSplits ? kGenMaxSplits : s;
 }
 
-cudaError_t launch_generic_attention(const float* qkv, float* q_rot, float* out, float* k_cache,
-                                     float* v_cache, Lengths len, int t_max, int n_q, int n_kv,
-                                     int head_dim, int n_splits, int plan_len,
-                                     const float* inv_freq, float* part_o, float* part_ml,
-                                     int* status, cudaStream_t st, bool pdl_first, bool pdl) {
+cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cache, float* v_cache,
+                                     Lengths len, int t_max, int n_q, int n_kv, int head_dim,
+                                     int n_splits, int plan_len, const float* inv_freq,
+                                     float* part_o, float* part_ml, int* status, cudaStream_t st,
+                                     bool pdl_first, bool pdl) {
   if (head_dim != 64 || n_q != 7 * n_kv) return cudaErrorInvalidValue;
   constexpr int D = 64, G = 7;
   GenParams p{};
   p.q = qkv;
-  p.q_rot = q_rot;
   p.k = qkv + (long long)n_q * D;
   p.v = p.k + (long long)n_kv * D;
   p.k_cache = k_cache;
@@ -314,11 +331,8 @@ cudaError_t launch_generic_attention(const float* qkv, float* q_rot, float* out,
   p.part_ml = part_ml;
   p.out = out;
   p.status = status;
-  cudaError_t e =
-      gen_launch(rope_append_generic_kernel<D>, dim3(1), dim3(D / 2), p, st, pdl_first);
-  if (e == cudaSuccess)
-    e = gen_launch(split_generic_kernel<D, G>, dim3(n_splits, n_kv), dim3(kGenThreads), p, st,
-                   pdl);
+  cudaError_t e = gen_launch(split_generic_kernel<D, G>, dim3(n_splits, n_kv),
+                             dim3(kGenThreads), p, st, pdl_first);
   if (e == cudaSuccess) e = gen_launch(merge_generic_kernel<D>, dim3(n_q), dim3(D), p, st, pdl);
   return e;
 }
