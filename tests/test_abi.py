@@ -49,9 +49,9 @@ def test_null_arguments_are_rejected(pkg):
 def test_unsupported_shapes_are_rejected_before_touching_the_device(pkg):
     lib = pkg.lib()
     h = ctypes.c_void_p()
-    bad = pkg.gqa.Config(12, 2, 64, 4096, 1e6)  # head_dim 64 not built
+    bad = pkg.gqa.Config(12, 2, 64, 4096, 1e6)  # head_dim 64 is built with 7 per KV head only
     assert lib.gqa_create(ctypes.byref(bad), 0, ctypes.byref(h)) == pkg.gqa.GQA_ERR_UNSUPPORTED
-    bad = pkg.gqa.Config(14, 2, 128, 4096, 1e6)  # group 7 not built
+    bad = pkg.gqa.Config(14, 2, 128, 4096, 1e6)  # group 7 is built at head_dim 64 only
     assert lib.gqa_create(ctypes.byref(bad), 0, ctypes.byref(h)) == pkg.gqa.GQA_ERR_UNSUPPORTED
     bad = pkg.gqa.Config(12, 2, 128, 0, 1e6)
     assert lib.gqa_create(ctypes.byref(bad), 0, ctypes.byref(h)) == pkg.gqa.GQA_ERR_INVALID_ARG
