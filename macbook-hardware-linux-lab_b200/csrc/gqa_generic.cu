@@ -22,7 +22,8 @@
 //                               a per-tile max and exp, then PV with one thread
 //                               per (head, dim) output; running (m, l, o) per head
 //   merge_generic_kernel        one CTA per q head: the splits' (m, l, o) merged
-//                               by log-sum-exp into the output row
+//                               by log-sum-exp into the output row, all loads
+//                               of a round in flight at once
 #include "gqa_common.cuh"
 
 #include <math_constants.h>
@@ -77,7 +78,6 @@ template <int D, int G>
 struct GenSmem {
   float q[G][D];            // rotated q of the KV head's G q heads
   float knew[D], vnew[D];   // the new row (owner CTA only)
-  float rope[D / 2][2];     // (cos, sin) per pair
   float k[kGenTile][D];
   float v[kGenTile][D];
   float s[G][kGenTile];     // scores, then weights e^(s - m)
@@ -107,24 +107,22 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
   // all) appends the new row; only it may attend that row.
   const bool owner = split == min(pos / p.rows_per_split, p.n_splits - 1);
 
-  // ---- RoPE: theta_i = pos * inv_freq[i], pairs (i, i + D/2) ----
-  if (tid < H) {
-    float sn, cs;
-    sincosf((float)pos * p.inv_freq[tid], &sn, &cs);
-    sm.rope[tid][0] = cs;
-    sm.rope[tid][1] = sn;
-  }
-  __syncthreads();
+  // ---- RoPE: theta_i = pos * inv_freq[i], pairs (i, i + D/2); each thread
+  // takes its own angles, so these loads share a round trip with the first
+  // tile's (the tile's barrier publishes sm.q) ----
   for (int i = tid; i < G * H; i += kGenThreads) {
     const int g = i / H, j = i % H;
     const float* qh = p.q + (long long)(hkv * G + g) * D;
-    const float q0 = qh[j], q1 = qh[j + H], cs = sm.rope[j][0], sn = sm.rope[j][1];
+    const float q0 = qh[j], q1 = qh[j + H];
+    float sn, cs;
+    sincosf((float)pos * p.inv_freq[j], &sn, &cs);
     sm.q[g][j] = q0 * cs - q1 * sn;
     sm.q[g][j + H] = q0 * sn + q1 * cs;
   }
   if (owner && tid < H) {
     const float k0 = p.k[hkv * D + tid], k1 = p.k[hkv * D + tid + H];
-    const float cs = sm.rope[tid][0], sn = sm.rope[tid][1];
+    float sn, cs;
+    sincosf((float)pos * p.inv_freq[tid], &sn, &cs);
     const float kr0 = k0 * cs - k1 * sn, kr1 = k0 * sn + k1 * cs;
     const float v0 = p.v[hkv * D + tid], v1 = p.v[hkv * D + tid + H];
     kc[(long long)pos * D + tid] = kr0;
@@ -140,7 +138,6 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
   float o[S::kOutPerThread], l_run = 0.f;  // l_run: thread tid < G holds head tid's l
 #pragma unroll
   for (int k = 0; k < S::kOutPerThread; ++k) o[k] = 0.f;
-  __syncthreads();
 
   for (int tb = t0; tb < t1; tb += kGenTile) {
     const int nrow = min(kGenTile, t1 - tb);
@@ -243,30 +240,83 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
   }
 }
 
+// One CTA of kGenThreads per q head: every split's (m, l) loaded at once by
+// the first threads, the weights e^(m_i - M) formed in shared memory while
+// each group of D threads has its splits' o values in flight, then the groups'
+// sums added.
 template <int D>
-__global__ void __launch_bounds__(D) merge_generic_kernel(const GenParams p) {
+__global__ void __launch_bounds__(kGenThreads) merge_generic_kernel(const GenParams p) {
+  constexpr int kGroups = kGenThreads / D;
+  constexpr int kInFlight = 16;                    // o loads in flight per thread
+  __shared__ float w[kGenMaxSplits];
+  __shared__ float osum[kGroups][D];
+  __shared__ float wmax[kGenThreads / 32], wsum[kGenThreads / 32];
   pdl_wait();
   pdl_launch_dependents();
   int pos, seq_len;
   if (!gen_lengths(p, pos, seq_len)) return;
-  const int h = blockIdx.x, d = threadIdx.x;
-  const float* ml = p.part_ml + (long long)h * p.n_splits * 2;
-  float M = -CUDART_INF_F;
-  for (int i = 0; i < p.n_splits; ++i)
-    if (ml[2 * i + 1] > 0.f) M = fmaxf(M, ml[2 * i]);
-  float L = 0.f, O = 0.f;
-  if (M != -CUDART_INF_F) {
-    const float* po = p.part_o + (long long)h * p.n_splits * D + d;
-    for (int i = 0; i < p.n_splits; ++i) {
-      const float li = ml[2 * i + 1];
-      if (li > 0.f) {
-        const float w = expf(ml[2 * i] - M);
-        L = fmaf(w, li, L);
-        O = fmaf(w, po[(long long)i * D], O);
-      }
+  const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int d = tid % D, grp = tid / D, n = p.n_splits;
+  const float* ml = p.part_ml + (long long)h * n * 2;
+  const float* po = p.part_o + (long long)h * n * D + d;
+  // this thread's first o values (splits grp, grp + kGroups, ...), in flight
+  float ov[kInFlight];
+#pragma unroll
+  for (int u = 0; u < kInFlight; ++u) {
+    const int i = grp + u * kGroups;
+    ov[u] = i < n ? __ldcg(po + (long long)i * D) : 0.f;
+  }
+  // M = max m_i over splits with l_i > 0
+  float mx = -CUDART_INF_F;
+  for (int i = tid; i < n; i += kGenThreads)
+    if (__ldcg(ml + 2 * i + 1) > 0.f) mx = fmaxf(mx, __ldcg(ml + 2 * i));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  if (lane == 0) wmax[warp] = mx;
+  __syncthreads();
+  float M = wmax[0];
+#pragma unroll
+  for (int k = 1; k < kGenThreads / 32; ++k) M = fmaxf(M, wmax[k]);
+  // weights and L = sum w_i l_i
+  float ls = 0.f;
+  for (int i = tid; i < n; i += kGenThreads) {
+    const float li = __ldcg(ml + 2 * i + 1);
+    const float wi = (li > 0.f && M != -CUDART_INF_F) ? expf(__ldcg(ml + 2 * i) - M) : 0.f;
+    w[i] = wi;
+    ls = fmaf(wi, li, ls);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+  if (lane == 0) wsum[warp] = ls;
+  __syncthreads();
+  float O = 0.f;
+#pragma unroll
+  for (int u = 0; u < kInFlight; ++u) {
+    const int i = grp + u * kGroups;
+    if (i < n && w[i] != 0.f) O = fmaf(w[i], ov[u], O);
+  }
+  for (int i0 = kInFlight * kGroups; i0 < n; i0 += kInFlight * kGroups) {
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      const int i = i0 + grp + u * kGroups;
+      ov[u] = i < n ? __ldcg(po + (long long)i * D) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < kInFlight; ++u) {
+      const int i = i0 + grp + u * kGroups;
+      if (i < n && w[i] != 0.f) O = fmaf(w[i], ov[u], O);
     }
   }
-  p.out[(long long)h * D + d] = L > 0.f ? O / L : 0.f;
+  osum[grp][d] = O;
+  __syncthreads();
+  if (grp == 0) {
+    float L = 0.f, S = 0.f;
+#pragma unroll
+    for (int k = 0; k < kGenThreads / 32; ++k) L += wsum[k];
+#pragma unroll
+    for (int k = 0; k < kGroups; ++k) S += osum[k][d];
+    p.out[(long long)h * D + d] = L > 0.f ? S / L : 0.f;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -333,7 +383,8 @@ cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cach
   p.status = status;
   cudaError_t e = gen_launch(split_generic_kernel<D, G>, dim3(n_splits, n_kv),
                              dim3(kGenThreads), p, st, pdl_first);
-  if (e == cudaSuccess) e = gen_launch(merge_generic_kernel<D>, dim3(n_q), dim3(D), p, st, pdl);
+  if (e == cudaSuccess)
+    e = gen_launch(merge_generic_kernel<D>, dim3(n_q), dim3(kGenThreads), p, st, pdl);
   return e;
 }
 
