@@ -57,6 +57,10 @@ WORKLOADS = {
     # Qwen2.5-0.5B attention shape (head_dim 64, 14 q / 2 KV heads), 24 layers
     "resident05b": dict(layers=24, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1, n_q=14, n_kv=2,
                         d=64),
+    # the Qwen2.5-0.5B model's ends (Q8_0 head) and its whole greedy step
+    "head05b": dict(layers=0, t_max=1, seqs=1, vocab=151936, n_q=14, n_kv=2, d=64, model="0.5b"),
+    "token24_05b": dict(layers=24, t_max=4096, pos_lo=3840, pos_hi=4096, seqs=1, vocab=151936,
+                        n_q=14, n_kv=2, d=64, model="0.5b"),
 }
 
 BLOCK_METRIC = ("GQA attention block (RMSNorm, Q4_0 QKV + bias, attention, Q4_0 Wo + residual): "
@@ -75,6 +79,17 @@ HEAD_METRIC = ("Q6_K LM head (output RMSNorm, 151936x1536 GEMV, greedy pick): HB
                "weights and logits/s")
 TOKEN_METRIC = ("whole-model greedy decode step (Q4_0 embedding, 28 decoder layers, Q6_K LM head, "
                 "pick): tok/s and HBM GB/s of KV + weights")
+# Qwen2.5-0.5B sizes (generate_stream_05b.c:19-35)
+D05, QKV05, DFFN05 = 896, 1152, 4864
+Q4_ROW05 = (D05 // 32) * 18
+ROW05 = 2 * 2 * 64 * 4  # K + V bytes of one attended position, both KV heads (1024)
+BLOCK05_BYTES = (QKV05 + D05) * Q4_ROW05 + (QKV05 + D05) * 4
+FFN05_BYTES = 2 * DFFN05 * Q4_ROW05 + D05 * (DFFN05 // 32) * 18 + D05 * 4
+HEAD05_BYTES = VOCAB * 952 + D05 * 4 * 2  # Q8_0 output.weight, gamma_output, state
+HEAD05_METRIC = ("Q8_0 LM head of Qwen2.5-0.5B (output RMSNorm, 151936x896 GEMV, greedy pick): "
+                 "HBM GB/s of weights and logits/s")
+TOKEN05_METRIC = ("Qwen2.5-0.5B whole-model greedy decode step (Q4_0 embedding, 24 decoder layers, "
+                  "Q8_0 LM head, pick): tok/s and HBM GB/s of KV + weights")
 
 
 def measured_peak():
@@ -313,6 +328,24 @@ def workload_config(name, exchange="peer"):
                 "bytes_per_step": "28*(2048*(pos+1) + %d) + %d"
                                   % (BLOCK_WEIGHT_BYTES + FFN_WEIGHT_BYTES, HEAD_BYTES + Q4_ROW),
                 "l2": "KV 235 MB + weights 928 MB per GPU > 126 MB L2; no flush",
+                "parallelism": "sequence-sharded replicas"}
+    if name == "head05b":
+        return {"workload": "head05b: output RMSNorm + Q8_0 LM head 151936x896 (145 MB) of "
+                            "Qwen2.5-0.5B + greedy pick, one token's state per step",
+                "vocab": VOCAB, "bytes_per_step": HEAD05_BYTES,
+                "l2": "two copies of the head weights used alternately (289 MB > 126 MB L2); "
+                      "no flush",
+                "parallelism": "replicas"}
+    if name == "token24_05b":
+        return {"workload": "token24_05b: one greedy decode step of the whole Qwen2.5-0.5B model "
+                            "per step -- Q4_0 embedding of the previous pick, 24 decoder layers "
+                            "(d_model 896, 14 q / 2 KV heads of 64, d_ffn 4864, Q4_0), output "
+                            "RMSNorm, Q8_0 LM head 151936x896, pick -- token and position kept "
+                            "on the device, one CUDA graph per step",
+                "layers": 24, "t_max": 4096, "positions": [3840, 4095], "vocab": VOCAB,
+                "bytes_per_step": "24*(1024*(pos+1) + %d) + %d"
+                                  % (BLOCK05_BYTES + FFN05_BYTES, HEAD05_BYTES + Q4_ROW05),
+                "l2": "KV 50 MB + weights 346 MB per GPU > 126 MB L2; no flush",
                 "parallelism": "sequence-sharded replicas"}
     if name == "layer28":
         return {"workload": "layer28: 28 whole decoder layers per token (attention block as in "
@@ -569,64 +602,80 @@ def run_block(args, g, ctx, rank, world, local):
 
 
 def run_head(args, g, ctx, rank, world, local):
-    """The LM head alone ("head") or the whole greedy decode step ("token28")."""
+    """The LM head alone ("head", "head05b") or the whole greedy decode step
+    ("token28", "token24_05b"): Qwen2.5-1.5B with its Q6_K head, or
+    Qwen2.5-0.5B with its Q8_0 head."""
     import torch
     wl = WORKLOADS[args.workload]
-    whole = args.workload == "token28"
+    whole = args.workload in ("token28", "token24_05b")
+    small = wl.get("model") == "0.5b"
+    d_model, qkv_w, d_ffn = (D05, QKV05, DFFN05) if small else (OUT_W, QKV_W, D_FFN)
+    hd, n_kv = wl.get("d", D), wl.get("n_kv", N_KV)
+    head_bytes = HEAD05_BYTES if small else HEAD_BYTES
     seed = 6464 + 1000 * rank
     s = g.seeded
-    w_head, gamma_out, embd = s.head_inputs(seed, VOCAB, OUT_W)
+    if small:
+        w_head, gamma_out, embd = s.head_q8_inputs(seed, VOCAB, d_model)
+        packed_bytes, pack, head = (g.Context.lm_head_q8_0_packed_bytes, ctx.lm_head_q8_0_pack,
+                                    ctx.lm_head_q8_0)
+    else:
+        w_head, gamma_out, embd = s.head_inputs(seed, VOCAB, d_model)
+        packed_bytes, pack, head = g.Context.lm_head_packed_bytes, ctx.lm_head_pack, ctx.lm_head
     n_copies = 1 if whole else 2
     packed = []
     raw = torch.from_numpy(w_head).cuda()
     for _ in range(n_copies):
-        p = torch.empty(g.Context.lm_head_packed_bytes(VOCAB), dtype=torch.uint8, device="cuda")
-        ctx.lm_head_pack(raw, VOCAB, p)
+        p = torch.empty(packed_bytes(VOCAB), dtype=torch.uint8, device="cuda")
+        pack(raw, VOCAB, p)
         packed.append(p)
     del raw
     d_gamma = torch.from_numpy(gamma_out).cuda()
     d_embd = torch.from_numpy(embd).cuda()
     d_tok = torch.tensor([17], dtype=torch.int32, device="cuda")
     logits = torch.empty(VOCAB, device="cuda")
-    state0 = torch.empty(OUT_W, device="cuda")
-    ctx.fill_normal(state0, OUT_W, seed, s.STATE)
+    state0 = torch.empty(d_model, device="cuda")
+    ctx.fill_normal(state0, d_model, seed, s.STATE)
     state = state0.clone()
     keep = []
     if whole:
         L_layers, t_max, pos_lo, pos_hi = wl["layers"], wl["t_max"], wl["pos_lo"], wl["pos_hi"]
-        caches = torch.empty((L_layers, 2, 2, t_max, D), device="cuda")
+        caches = torch.empty((L_layers, 2, n_kv, t_max, hd), device="cuda")
         ctx.fill_normal(caches, caches.numel(), seed, s.K_CACHE)
         kvs = [g.kv_of(caches[l, 0], caches[l, 1]) for l in range(L_layers)]
-        scale = 1.0 / (4.6 * np.sqrt(OUT_W))
+        scale = 1.0 / (4.6 * np.sqrt(d_model))
         ws, fws = [], []
         for l in range(L_layers):
-            wq = s.q4_0_matrix(seed + l, s.W_QKV, QKV_W, OUT_W, scale)
-            wo = s.q4_0_matrix(seed + l, s.W_O, OUT_W, OUT_W, scale)
-            bq = (0.1 * s.normal(seed + l, s.B_QKV, QKV_W)).astype(np.float32)
-            gm = (1.0 + 0.1 * s.normal(seed + l, s.GAMMA, OUT_W)).astype(np.float32)
+            wq = s.q4_0_matrix(seed + l, s.W_QKV, qkv_w, d_model, scale)
+            wo = s.q4_0_matrix(seed + l, s.W_O, d_model, d_model, scale)
+            bq = (0.1 * s.normal(seed + l, s.B_QKV, qkv_w)).astype(np.float32)
+            gm = (1.0 + 0.1 * s.normal(seed + l, s.GAMMA, d_model)).astype(np.float32)
             dev = [torch.from_numpy(a).cuda() for a in (wq, bq, wo, gm)]
-            fdev = [torch.from_numpy(a).cuda() for a in s.ffn_block_inputs(seed + l)]
+            fdev = [torch.from_numpy(a).cuda()
+                    for a in s.ffn_block_inputs(seed + l, d_model=d_model, d_ffn=d_ffn)]
             keep += dev + fdev
             ws.append(g.block_weights_of(*dev))
             fws.append(g.ffn_weights_of(*fdev))
-        model = g.ModelHandle(ws, fws, kvs, d_embd, d_gamma, packed[0], VOCAB)
+        model = g.ModelHandle(ws, fws, kvs, d_embd, d_gamma, packed[0], VOCAB,
+                              g.gqa.HEAD_Q8_0 if small else g.gqa.HEAD_Q6_K)
         d_pos = torch.tensor([pos_lo], dtype=torch.int32, device="cuda")
         ctx.reserve(1, t_max)
         n_window = pos_hi - pos_lo
-        w_bytes = BLOCK_WEIGHT_BYTES + FFN_WEIGHT_BYTES
+        w_bytes = (BLOCK05_BYTES + FFN05_BYTES) if small else (BLOCK_WEIGHT_BYTES + FFN_WEIGHT_BYTES)
+        row_bytes = 2 * n_kv * hd * 4
+        embd_row = (d_model // 32) * 18
 
         def step_bytes(i):
             pos = pos_lo + i % n_window
-            return L_layers * (ROW_BYTES * (pos + 1) + w_bytes) + HEAD_BYTES + Q4_ROW
+            return L_layers * (row_bytes * (pos + 1) + w_bytes) + head_bytes + embd_row
 
         def graph_body(i):
             ctx.decode_token(model, state, d_tok, d_pos, logits, pos_lo, pos_hi)
     else:
         def step_bytes(i):
-            return HEAD_BYTES
+            return head_bytes
 
         def graph_body(i):
-            ctx.lm_head(packed[i % n_copies], VOCAB, d_gamma, state, logits, d_tok)
+            head(packed[i % n_copies], VOCAB, d_gamma, state, logits, d_tok)
 
     stream = torch.cuda.current_stream()
     for i in range(args.warmup):
@@ -684,15 +733,21 @@ def run_head(args, g, ctx, rank, world, local):
     del graphs
     # embedding, per layer 6 kernels, head, position advance
     per_step = (1 + 6 * wl["layers"] + 2) if whole else 1
+    if small:
+        metric = TOKEN05_METRIC if whole else HEAD05_METRIC
+        data = ("synthetic: seeded Q8_0 head (uniform int8 codes, fp16 d ~ 2^-8), seeded Q4_0 "
+                "embedding/layer weights at the Qwen2.5-0.5B sizes, N(0,1) state and KV caches")
+    else:
+        metric = TOKEN_METRIC if whole else HEAD_METRIC
+        data = ("synthetic: seeded Q6_K head (uniform codes/scales, fp16 d ~ 2^-12), seeded "
+                "Q4_0 embedding/layer weights, N(0,1) state and KV caches")
     return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3, bytes=total_bytes,
                 clocks=clk.summary(), launches=per_step * args.steps,
                 launches_per_step=per_step, h2d=4, d2h=4, tokens=args.steps,
-                dominant_launches=args.steps,
-                metric=TOKEN_METRIC if whole else HEAD_METRIC,
-                kernel="whole decode step" if whole else "lm_head_kernel",
-                head_bytes=HEAD_BYTES,
-                data="synthetic: seeded Q6_K head (uniform codes/scales, fp16 d ~ 2^-12), seeded "
-                     "Q4_0 embedding/layer weights, N(0,1) state and KV caches")
+                dominant_launches=args.steps, metric=metric,
+                kernel="whole decode step" if whole else
+                ("lm_head_q8_kernel" if small else "lm_head_kernel"),
+                head_bytes=head_bytes, data=data)
 
 
 def cpu_head_run(budget_s, whole=False, pos_lo=3840, layers=28):
@@ -737,6 +792,50 @@ def cpu_head_run(budget_s, whole=False, pos_lo=3840, layers=28):
             if whole else "LM head call(s): output norm, Q6_K GEMV over 151936 rows, pick")
     sample = (f"{done} {what}; the reference's OpenMP GEMVs on {os.cpu_count()} threads")
     return nbytes / dt / 1e9, os.cpu_count() or 1, sample, "reference", done / dt
+
+
+def cpu_head05b_run(budget_s, whole=False, pos_lo=3840, layers=24):
+    """The 0.5B model's step on the host cores.  The reference runs it only
+    in OpenCL (generate_stream_05b.c), so this is the oracle: the reference's
+    compiled OpenMP GEMVs for every projection, the restated Q8_0 head
+    (gemv_q8_0) and attention, one thread for the restated parts."""
+    import __graft_entry__
+    g = __graft_entry__.load_package()
+    orc = __graft_entry__.load_oracle()
+    if not orc.have_reference():
+        return None
+    s = g.seeded
+    w_head = s.q8_0_matrix(901, s.W_HEAD, VOCAB, D05)
+    gamma = (1.0 + 0.1 * s.normal(901, s.GAMMA_OUT, D05)).astype(np.float32)
+    state = s.normal(901, s.STATE, D05)
+    if whole:
+        table = s.q4_0_matrix(901, s.TOKEN_EMBD, VOCAB, D05, 1.0 / 4.6)
+        blocks = [s.attention_block_inputs(900 + l, d_model=D05, n_heads_kv=2, head_dim=64)
+                  for l in range(layers)]
+        ffns = [s.ffn_block_inputs(900 + l, d_model=D05, d_ffn=DFFN05) for l in range(layers)]
+        lay = [((L[1], L[2], L[3], L[4]), f) for L, f in zip(blocks, ffns)]
+        kv = [(L[5], L[6]) for L in blocks]
+    tok = 17
+    t0 = time.perf_counter()
+    done, nbytes = 0, 0
+    while True:
+        if whole:
+            pos = pos_lo + done % 256
+            _, tok = orc.ref_decode_token(table, lay, kv, gamma, w_head, tok, pos, model="0.5b")
+            nbytes += (layers * (ROW05 * (pos + 1) + BLOCK05_BYTES + FFN05_BYTES) +
+                       HEAD05_BYTES + Q4_ROW05)
+        else:
+            _, tok = orc.lm_head_q8_0(state, gamma, w_head, VOCAB)
+            nbytes += HEAD05_BYTES
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    what = ("whole 0.5B decode step(s): embedding, 24 decoder layers, output norm, Q8_0 head, "
+            "pick" if whole else "Q8_0 LM head call(s) over 151936 rows with the pick")
+    sample = (f"{done} {what}; the reference's compiled OpenMP GEMVs on {os.cpu_count()} "
+              "threads, the restated Q8_0 head and attention on one")
+    return nbytes / dt / 1e9, os.cpu_count() or 1, sample, "port", done / dt
 
 
 def cpu_block_run(budget_s, pos_lo=3840, layers=28, full=False):
@@ -999,7 +1098,7 @@ def run_ours(args):
                               world)
     if args.workload in ("block28", "layer28"):
         r = run_block(args, g, ctx, rank, world, local)
-    elif args.workload in ("head", "token28"):
+    elif args.workload in ("head", "token28", "head05b", "token24_05b"):
         r = run_head(args, g, ctx, rank, world, local)
     elif args.workload in ("resident28", "single", "resident05b"):
         r = run_resident(args, g, ctx, rank, world, local)
@@ -1024,6 +1123,8 @@ def run_ours(args):
             res = cpu_head_run(budget_s=12.0, whole=args.workload == "token28")
         elif args.workload == "resident05b":
             res = cpu_port_05b_run(budget_s=12.0)
+        elif args.workload in ("head05b", "token24_05b"):
+            res = cpu_head05b_run(budget_s=12.0, whole=args.workload == "token24_05b")
         else:
             res = cpu_reference_run(10 ** 6, 1, budget_s=12.0)
         if res is not None:
@@ -1037,7 +1138,8 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t / args.steps * 1e3, 5), "higher_is_better": True,
             "scaling": "weak" if args.workload in ("resident28", "single", "block28", "layer28",
-                                                   "head", "token28", "resident05b")
+                                                   "head", "token28", "resident05b",
+                                                   "head05b", "token24_05b")
             else "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": r.get("data", "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)"),

@@ -251,10 +251,18 @@ GQA_API int gqa_decode_kv_shard_exchange(gqa_ctx *ctx, gqa_exchange *x, gqa_stre
  * each row d_model / 32 blocks. */
 #define GQA_Q4_0_BLOCK_BYTES 18
 
+/* The decoder sizes the projections are built for, by the context's shape:
+ *   Qwen2.5-1.5B  head_dim 128, 12 q / 2 KV heads: d_model 1536, d_ffn 8960
+ *                 (qwen_server.c);
+ *   Qwen2.5-0.5B  head_dim 64, 14 q / 2 KV heads:  d_model 896,  d_ffn 4864
+ *                 (generate_stream_05b.c:19-26).
+ * The block, FFN, embedding and token-step calls report GQA_ERR_UNSUPPORTED
+ * for any other shape. */
+
 /* Device pointers of one layer's attention weights (16-byte aligned). */
 typedef struct {
-    const void *w_qkv;   /* Q4_0 [(n_heads_q + 2 n_heads_kv) * 128][d_model / 32] */
-    const float *b_qkv;  /* [(n_heads_q + 2 n_heads_kv) * 128] */
+    const void *w_qkv;   /* Q4_0 [(n_heads_q + 2 n_heads_kv) * head_dim][d_model / 32] */
+    const float *b_qkv;  /* [(n_heads_q + 2 n_heads_kv) * head_dim] */
     const void *w_o;     /* Q4_0 [d_model][d_model / 32] */
     const float *gamma;  /* [d_model] weight of the attention RMSNorm */
 } gqa_block_weights;
@@ -263,7 +271,9 @@ typedef struct {
  * the attention half of gpu_decoder_layer_step (qwen_server.c:444-453:
  * k_rmsnorm_attn, k_qkv_gemv, the five attention kernels, k_wo_residual),
  * with the KV append at pos as in gqa_layer_attention.  d_model =
- * n_heads_q * 128 must be 1536; the RMSNorm epsilon is the reference's 1e-6.
+ * n_heads_q * head_dim (1536 or 896, above); the RMSNorm epsilon is the
+ * reference's 1e-6 (the 0.5B generator's gpu_decoder_layer_step,
+ * generate_stream_05b.c:364-476, is the same chain at its sizes).
  * state: [d_model] device floats, updated in place. */
 GQA_API int gqa_attention_block(gqa_ctx *ctx, gqa_stream_t stream, const gqa_block_weights *w,
                                 const gqa_layer_kv *kv, float *state, int pos, int seq_len);
@@ -289,7 +299,7 @@ typedef struct {
 /* state += W_down * (silu(W_gate * z) * (W_up * z)), z = rmsnorm(state, gamma):
  * the FFN half of gpu_decoder_layer_step (qwen_server.c k_rmsnorm_ffn,
  * k_swiglu_fused, k_down_res; CPU test_28_layers_real.c:298-317), with the
- * reference's stable SiLU.  d_model = 1536, d_ffn = 8960. */
+ * reference's stable SiLU.  d_model / d_ffn: 1536 / 8960 or 896 / 4864. */
 GQA_API int gqa_ffn_block(gqa_ctx *ctx, gqa_stream_t stream, const gqa_ffn_weights *w,
                           float *state);
 
@@ -332,18 +342,46 @@ GQA_API int gqa_lm_head_pack(gqa_ctx *ctx, gqa_stream_t stream, const void *q6k,
 GQA_API int gqa_lm_head(gqa_ctx *ctx, gqa_stream_t stream, const void *packed, int n_rows,
                         const float *gamma, const float *state, float *logits, int *token);
 
-/* state = row *d_token of a Q4_0 embedding table [n_rows][1536 / 32 blocks]
+/* state = row *d_token of a Q4_0 embedding table [n_rows][d_model / 32 blocks]
  * (device, the bytes of token_embd.weight): get_token_embedding
- * (qwen_server.c:188-201) done on the device, so that the token id never
+ * (qwen_server.c:188-201; generate_stream_05b.c:200-213 with d_model 896)
+ * done on the device, so that the token id never
  * leaves it.  An id outside [0, n_rows) sets GQA_STATUS_BAD_TOKEN in the
  * device status word and leaves state unchanged. */
 GQA_API int gqa_token_embedding(gqa_ctx *ctx, gqa_stream_t stream, const void *table, int n_rows,
                                 const int *d_token, float *state);
 
+/* The Qwen2.5-0.5B head: Q8_0 blocks (block_q8_0, generate_stream_05b.c:
+ * 42-45), an IEEE fp16 scale d then 32 int8 codes; weight j = d * qs[j]. */
+#define GQA_Q8_0_BLOCK_BYTES 34
+
+/* Bytes that gqa_lm_head_q8_0_pack writes for n_rows rows of 896 inputs:
+ * 952 * ((n_rows + 3) / 4 * 4) (for the 151936-row head exactly its size). */
+GQA_API long long gqa_lm_head_q8_0_packed_bytes(int n_rows);
+
+/* Lays a Q8_0 matrix out for gqa_lm_head_q8_0.  q8: device, n_rows rows of
+ * 28 blocks of 34 bytes (the bytes of output.weight that
+ * generate_stream_05b.c uploads whole, :687, d_W_head); packed: device,
+ * 16-byte aligned, gqa_lm_head_q8_0_packed_bytes(n_rows).  The same bytes in
+ * two planes (codes, scales) whose rows are aligned; run once at load time. */
+GQA_API int gqa_lm_head_q8_0_pack(gqa_ctx *ctx, gqa_stream_t stream, const void *q8, int n_rows,
+                                  void *packed);
+
+/* gqa_lm_head for the Qwen2.5-0.5B shape (d_model 896): k_output_norm and
+ * the gemv_q8_0 LM head (kernel_q8_0.cl:10-61, generate_stream_05b.c:
+ * 845-864), logits and/or the greedy pick of the host loop at :872-878
+ * (the first row whose logit is the largest one above -1e30). */
+GQA_API int gqa_lm_head_q8_0(gqa_ctx *ctx, gqa_stream_t stream, const void *packed, int n_rows,
+                             const float *gamma, const float *state, float *logits, int *token);
+
 /* Device status bits (gqa_device_status). */
 #define GQA_STATUS_BAD_LENGTH 1   /* a device-side pos / seq_len was out of range */
 #define GQA_STATUS_WAIT_TIMEOUT 2 /* a bounded device wait gave up */
 #define GQA_STATUS_BAD_TOKEN 8    /* a device-side token id was outside the vocabulary */
+
+/* gqa_model.lm_head_type */
+#define GQA_HEAD_Q6_K 0  /* gqa_lm_head_pack layout (Qwen2.5-1.5B, d_model 1536) */
+#define GQA_HEAD_Q8_0 1  /* gqa_lm_head_q8_0_pack layout (Qwen2.5-0.5B, d_model 896) */
 
 /* Everything one decode step of the whole model reads (device pointers in
  * host arrays). */
@@ -352,10 +390,11 @@ typedef struct {
     const gqa_block_weights *attn;  /* [n_layers] */
     const gqa_ffn_weights *ffn;     /* [n_layers] */
     const gqa_layer_kv *kv;         /* [n_layers] */
-    const void *token_embd;         /* Q4_0 [vocab][48 blocks] */
-    const float *gamma_output;      /* [1536] output_norm.weight */
-    const void *lm_head;            /* gqa_lm_head_pack layout of output.weight */
+    const void *token_embd;         /* Q4_0 [vocab][d_model / 32 blocks] */
+    const float *gamma_output;      /* [d_model] output_norm.weight */
+    const void *lm_head;            /* packed output.weight, layout by lm_head_type */
     int vocab;                      /* rows of token_embd and of the head */
+    int lm_head_type;               /* GQA_HEAD_Q6_K or GQA_HEAD_Q8_0 */
 } gqa_model;
 
 /* One greedy decode step of the whole model without leaving the device: the
@@ -363,7 +402,9 @@ typedef struct {
  * decoder layers at position *d_pos, output norm, LM head, greedy pick -- with
  * the pick written back to *d_token and *d_pos advanced (wrapping to wrap_lo
  * at wrap_hi when wrap_hi > 0), so that steps chain on the device and one step
- * can be captured as a graph.  state: [1536] device workspace; logits: [vocab]
+ * can be captured as a graph (the 0.5B generator's loop, generate_stream_05b.c:
+ * 823-897, is the same step with the Q8_0 head).  state: [d_model] device
+ * workspace; logits: [vocab]
  * device, or NULL.  The end-of-generation check (:1008) and the position
  * limit (:1014) stay with the caller, which reads *d_token. */
 GQA_API int gqa_decode_token(gqa_ctx *ctx, gqa_stream_t stream, const gqa_model *model,

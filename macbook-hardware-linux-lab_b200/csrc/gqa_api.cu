@@ -40,19 +40,20 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
                            __nv_bfloat16* kimg, __nv_bfloat16* vimg, float* const* k_caches,
                            float* const* v_caches, int t_max, float* out, int* status,
                            int* sched, int n_sm, cudaStream_t st);
-int block_d_model();
-int block_d_ffn();
+int block_d_model(int model);
+int block_d_ffn(int model);
+int block_max_d_ffn();
 cudaError_t prepare_block_kernels();
-cudaError_t launch_gateup_gemv(const void* w_gate, const void* w_up, const float* gamma,
-                               const float* state, float* h, int* status, cudaStream_t st,
-                               bool pdl);
-cudaError_t launch_down_gemv(const void* w_down, const float* h, float* state, int* status,
-                             cudaStream_t st, bool pdl);
-cudaError_t launch_qkv_gemv(const void* w, const float* bias, const float* gamma,
+cudaError_t launch_gateup_gemv(int model, const void* w_gate, const void* w_up,
+                               const float* gamma, const float* state, float* h, int* status,
+                               cudaStream_t st, bool pdl);
+cudaError_t launch_down_gemv(int model, const void* w_down, const float* h, float* state,
+                             int* status, cudaStream_t st, bool pdl);
+cudaError_t launch_qkv_gemv(int model, const void* w, const float* bias, const float* gamma,
                             const float* state, float* qkv, int M, int* status, cudaStream_t st,
                             bool pdl);
-cudaError_t launch_wo_gemv(const void* w, const float* attn, float* state, int M, int* status,
-                           cudaStream_t st, bool pdl);
+cudaError_t launch_wo_gemv(int model, const void* w, const float* attn, float* state, int M,
+                           int* status, cudaStream_t st, bool pdl);
 size_t exchange_inbox_bytes(int world, int n_rows);
 cudaError_t launch_exchange_combine(const CombineParams& local, uint2* const* inbox,
                                     unsigned* epoch, int rank, int world, float* out, int* status,
@@ -66,15 +67,17 @@ cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cach
                                      float* part_o, float* part_ml, int* status, cudaStream_t st,
                                      bool pdl_first, bool pdl);
 size_t lm_head_packed_bytes(long long n_rows);
+size_t lm_head_q8_packed_bytes(long long n_rows);
+cudaError_t launch_q8_pack(const void* src, int n_rows, void* dst, cudaStream_t st);
 int lm_head_grid(int n_sm);
 size_t lm_head_best_bytes(int grid);
 cudaError_t launch_q6k_pack(const void* src, int n_rows, void* dst, cudaStream_t st);
 cudaError_t prepare_head_kernels();
-cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, const float* state,
-                           float* logits, int* token, void* best, unsigned* done, int* status,
-                           int grid, cudaStream_t st, bool pdl);
-cudaError_t launch_embed_q4(const void* table, int n_rows, const int* token, float* state,
-                            int* status, cudaStream_t st, bool pdl);
+cudaError_t launch_lm_head(bool q8, const void* planes, int n_rows, const float* gamma,
+                           const float* state, float* logits, int* token, void* best,
+                           unsigned* done, int* status, int grid, cudaStream_t st, bool pdl);
+cudaError_t launch_embed_q4(const void* table, int n_rows, int d_model, const int* token,
+                            float* state, int* status, cudaStream_t st, bool pdl);
 }  // namespace gqa
 
 using namespace gqa;
@@ -370,14 +373,33 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
   return GQA_OK;
 }
 
+// The decoder sizes of the context's shape: 0 for Qwen2.5-1.5B (head_dim 128,
+// 12 / 2 heads: d_model 1536, d_ffn 8960), 1 for Qwen2.5-0.5B (head_dim 64,
+// 14 / 2 heads: d_model 896, d_ffn 4864), -1 for a shape whose projections
+// are not built.
+int block_model(const gqa_ctx* c) {
+  const int dm = c->cfg.n_heads_q * c->cfg.head_dim;
+  if (!c->generic && dm == block_d_model(0)) return 0;
+  if (c->generic && c->cfg.head_dim == 64 && c->cfg.n_heads_kv == 2 && dm == block_d_model(1))
+    return 1;
+  return -1;
+}
+
+int need_block_model(const gqa_ctx* c, const char* what) {
+  if (block_model(c) < 0)
+    return fail(GQA_ERR_UNSUPPORTED, "%s built for the Qwen2.5-1.5B (128-dim heads, 12 / 2, "
+                "d_model 1536) and Qwen2.5-0.5B (64-dim heads, 14 / 2, d_model 896) shapes only "
+                "(this context: head_dim %d, %d / %d heads)", what, c->cfg.head_dim,
+                c->cfg.n_heads_q, c->cfg.n_heads_kv);
+  return GQA_OK;
+}
+
 // One attention block: QKV projection (with RMSNorm) -> split-KV attention
 // (RoPE + append fused) and merge -> Wo projection into the state.
 int check_block_weights(const gqa_ctx* c, const gqa_block_weights* w) {
   if (!w || !w->w_qkv || !w->b_qkv || !w->w_o || !w->gamma)
     return fail(GQA_ERR_INVALID_ARG, "null block weight pointer");
-  if (c->cfg.n_heads_q * kHeadDim != block_d_model())
-    return fail(GQA_ERR_UNSUPPORTED, "attention block built for d_model %d (n_heads_q * 128 = %d)",
-                block_d_model(), c->cfg.n_heads_q * kHeadDim);
+  if (need_block_model(c, "attention block") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (!aligned16(w->w_qkv) || !aligned16(w->w_o) || !aligned16(w->b_qkv) || !aligned16(w->gamma))
     return fail(GQA_ERR_INVALID_ARG, "block weights must be 16-byte aligned");
   return GQA_OK;
@@ -385,30 +407,34 @@ int check_block_weights(const gqa_ctx* c, const gqa_block_weights* w) {
 
 int block_impl(gqa_ctx* c, cudaStream_t st, const gqa_block_weights* w, const gqa_layer_kv* kv,
                float* state, Lengths len, int plan_len, bool pdl_first, bool lengths_stable) {
-  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
-  GQA_CUDA(launch_qkv_gemv(w->w_qkv, w->b_qkv, w->gamma, state, c->blk_qkv,
-                           (nq + 2 * nkv) * kHeadDim, c->status, st, pdl_first));
-  int rc = run_single(c, st, kv, c->blk_qkv, len, plan_len, true, c->blk_attn, true,
-                      lengths_stable);
+  const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv, hd = c->cfg.head_dim;
+  const int model = block_model(c);
+  GQA_CUDA(launch_qkv_gemv(model, w->w_qkv, w->b_qkv, w->gamma, state, c->blk_qkv,
+                           (nq + 2 * nkv) * hd, c->status, st, pdl_first));
+  int rc = c->generic ? run_generic(c, st, kv, c->blk_qkv, len, plan_len, c->blk_attn, true)
+                      : run_single(c, st, kv, c->blk_qkv, len, plan_len, true, c->blk_attn, true,
+                                   lengths_stable);
   if (rc != GQA_OK) return rc;
-  GQA_CUDA(launch_wo_gemv(w->w_o, c->blk_attn, state, nq * kHeadDim, c->status, st, true));
+  GQA_CUDA(launch_wo_gemv(model, w->w_o, c->blk_attn, state, nq * hd, c->status, st, true));
   return GQA_OK;
 }
 
 int check_ffn_weights(const gqa_ctx* c, const gqa_ffn_weights* w) {
   if (!w || !w->w_gate || !w->w_up || !w->w_down || !w->gamma)
     return fail(GQA_ERR_INVALID_ARG, "null FFN weight pointer");
-  if (c->cfg.n_heads_q * kHeadDim != block_d_model())
-    return fail(GQA_ERR_UNSUPPORTED, "FFN block built for d_model %d", block_d_model());
+  if (need_block_model(c, "FFN block") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (!aligned16(w->w_gate) || !aligned16(w->w_up) || !aligned16(w->w_down) ||
       !aligned16(w->gamma))
     return fail(GQA_ERR_INVALID_ARG, "FFN weights must be 16-byte aligned");
   return GQA_OK;
 }
 
-int check_head(const gqa_ctx* c, const void* packed, int n_rows, const float* gamma) {
-  if (c->cfg.n_heads_q * kHeadDim != block_d_model())
-    return fail(GQA_ERR_UNSUPPORTED, "LM head built for d_model %d", block_d_model());
+// q8: the Q8_0 head (built for d_model 896), else the Q6_K head (d_model 1536).
+int check_head(const gqa_ctx* c, bool q8, const void* packed, int n_rows, const float* gamma) {
+  if (block_model(c) != (q8 ? 1 : 0))
+    return fail(GQA_ERR_UNSUPPORTED, "the %s LM head is built for d_model %d only (this context: "
+                "%d)", q8 ? "Q8_0" : "Q6_K", block_d_model(q8 ? 1 : 0),
+                c->cfg.n_heads_q * c->cfg.head_dim);
   if (!packed || !gamma || n_rows < 1)
     return fail(GQA_ERR_INVALID_ARG, "LM head: null weights or n_rows %d", n_rows);
   if (!aligned16(packed) || !aligned16(gamma))
@@ -416,9 +442,10 @@ int check_head(const gqa_ctx* c, const void* packed, int n_rows, const float* ga
   return GQA_OK;
 }
 int ffn_impl(gqa_ctx* c, cudaStream_t st, const gqa_ffn_weights* w, float* state, bool pdl_first) {
-  GQA_CUDA(launch_gateup_gemv(w->w_gate, w->w_up, w->gamma, state, c->blk_h, c->status, st,
-                              pdl_first));
-  GQA_CUDA(launch_down_gemv(w->w_down, c->blk_h, state, c->status, st, true));
+  const int model = block_model(c);
+  GQA_CUDA(launch_gateup_gemv(model, w->w_gate, w->w_up, w->gamma, state, c->blk_h, c->status,
+                              st, pdl_first));
+  GQA_CUDA(launch_down_gemv(model, w->w_down, c->blk_h, state, c->status, st, true));
   return GQA_OK;
 }
 
@@ -477,6 +504,9 @@ int set_error(int code, const char* fmt, ...) {
   va_end(ap);
   return code;
 }
+
+// The context's decoder sizes (block_model above), for the model loader.
+int ctx_block_model(const gqa_ctx* c) { return block_model(c); }
 }  // namespace gqa
 
 extern "C" {
@@ -531,7 +561,7 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess)
     e = cudaMalloc(&c->blk_qkv, sizeof(float) * (cfg->n_heads_q + 2 * cfg->n_heads_kv) * kHeadDim);
   if (e == cudaSuccess) e = cudaMalloc(&c->blk_attn, sizeof(float) * cfg->n_heads_q * kHeadDim);
-  if (e == cudaSuccess) e = cudaMalloc(&c->blk_h, sizeof(float) * block_d_ffn());
+  if (e == cudaSuccess) e = cudaMalloc(&c->blk_h, sizeof(float) * block_max_d_ffn());
   if (e == cudaSuccess) e = prepare_block_kernels();
   if (e == cudaSuccess) e = prepare_head_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kCounterSlots);
@@ -914,7 +944,6 @@ int gqa_decode_kv_shard(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
 int gqa_attention_block(gqa_ctx* c, gqa_stream_t stream, const gqa_block_weights* w,
                         const gqa_layer_kv* kv, float* state, int pos, int seq_len) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
-  if (tuned_only(c, "gqa_attention_block") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_block_weights(c, w);
   if (rc != GQA_OK) return rc;
   rc = check_kv(c, kv);
@@ -934,7 +963,6 @@ int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
                                const gqa_block_weights* w, const gqa_layer_kv* kv, float* state,
                                int* d_pos, int advance, int wrap_lo, int wrap_hi) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
-  if (tuned_only(c, "gqa_attention_block_layers") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_layers < 1 || !w || !kv || !d_pos || !state || !aligned16(state))
     return fail(GQA_ERR_INVALID_ARG, "gqa_attention_block_layers: bad arguments");
   for (int l = 0; l < n_layers; ++l) {
@@ -960,7 +988,6 @@ int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
 
 int gqa_ffn_block(gqa_ctx* c, gqa_stream_t stream, const gqa_ffn_weights* w, float* state) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
-  if (tuned_only(c, "gqa_ffn_block") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_ffn_weights(c, w);
   if (rc != GQA_OK) return rc;
   if (!state || !aligned16(state)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned state");
@@ -972,7 +999,6 @@ int gqa_decoder_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers, const gqa_
                        const gqa_ffn_weights* ffn, const gqa_layer_kv* kv, float* state,
                        int* d_pos, int advance, int wrap_lo, int wrap_hi) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
-  if (tuned_only(c, "gqa_decoder_layers") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_layers < 1 || !attn || !ffn || !kv || !d_pos || !state || !aligned16(state))
     return fail(GQA_ERR_INVALID_ARG, "gqa_decoder_layers: bad arguments");
   for (int l = 0; l < n_layers; ++l) {
@@ -1014,13 +1040,41 @@ int gqa_lm_head_pack(gqa_ctx* c, gqa_stream_t stream, const void* q6k, int n_row
 int gqa_lm_head(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
                 const float* gamma, const float* state, float* logits, int* token) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
-  if (tuned_only(c, "gqa_lm_head") != GQA_OK) return GQA_ERR_UNSUPPORTED;
-  int rc = check_head(c, packed, n_rows, gamma);
+  int rc = check_head(c, false, packed, n_rows, gamma);
   if (rc != GQA_OK) return rc;
   if (!state || !aligned16(state)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned state");
   if (!logits && !token) return fail(GQA_ERR_INVALID_ARG, "gqa_lm_head: no output requested");
   DeviceGuard g(c->device);
-  GQA_CUDA(launch_lm_head(packed, n_rows, gamma, state, logits, token, c->head_best,
+  GQA_CUDA(launch_lm_head(false, packed, n_rows, gamma, state, logits, token, c->head_best,
+                          reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot), c->status,
+                          c->head_grid, (cudaStream_t)stream, c->pdl != 0));
+  return GQA_OK;
+}
+
+long long gqa_lm_head_q8_0_packed_bytes(int n_rows) {
+  return n_rows < 1 ? 0 : (long long)lm_head_q8_packed_bytes(n_rows);
+}
+
+int gqa_lm_head_q8_0_pack(gqa_ctx* c, gqa_stream_t stream, const void* q8, int n_rows,
+                          void* packed) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (!q8 || !packed || n_rows < 1)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_lm_head_q8_0_pack: null buffer or n_rows %d", n_rows);
+  if (!aligned16(packed)) return fail(GQA_ERR_INVALID_ARG, "packed head must be 16-byte aligned");
+  DeviceGuard g(c->device);
+  GQA_CUDA(launch_q8_pack(q8, n_rows, packed, (cudaStream_t)stream));
+  return GQA_OK;
+}
+
+int gqa_lm_head_q8_0(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
+                     const float* gamma, const float* state, float* logits, int* token) {
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  int rc = check_head(c, true, packed, n_rows, gamma);
+  if (rc != GQA_OK) return rc;
+  if (!state || !aligned16(state)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned state");
+  if (!logits && !token) return fail(GQA_ERR_INVALID_ARG, "gqa_lm_head_q8_0: no output requested");
+  DeviceGuard g(c->device);
+  GQA_CUDA(launch_lm_head(true, packed, n_rows, gamma, state, logits, token, c->head_best,
                           reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot), c->status,
                           c->head_grid, (cudaStream_t)stream, c->pdl != 0));
   return GQA_OK;
@@ -1029,25 +1083,25 @@ int gqa_lm_head(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
 int gqa_token_embedding(gqa_ctx* c, gqa_stream_t stream, const void* table, int n_rows,
                         const int* d_token, float* state) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
-  if (tuned_only(c, "gqa_token_embedding") != GQA_OK) return GQA_ERR_UNSUPPORTED;
-  if (c->cfg.n_heads_q * kHeadDim != block_d_model())
-    return fail(GQA_ERR_UNSUPPORTED, "embedding built for d_model %d", block_d_model());
+  if (need_block_model(c, "gqa_token_embedding") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (!table || !d_token || !state || n_rows < 1)
     return fail(GQA_ERR_INVALID_ARG, "gqa_token_embedding: null argument or n_rows %d", n_rows);
   DeviceGuard g(c->device);
-  GQA_CUDA(launch_embed_q4(table, n_rows, d_token, state, c->status, (cudaStream_t)stream,
-                           c->pdl != 0));
+  GQA_CUDA(launch_embed_q4(table, n_rows, block_d_model(block_model(c)), d_token, state,
+                           c->status, (cudaStream_t)stream, c->pdl != 0));
   return GQA_OK;
 }
 
 int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float* state,
                      int* d_token, int* d_pos, float* logits, int wrap_lo, int wrap_hi) {
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
-  if (tuned_only(c, "gqa_decode_token") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (!m || m->n_layers < 1 || !m->attn || !m->ffn || !m->kv || !m->token_embd || !d_token ||
       !d_pos || !state || !aligned16(state))
     return fail(GQA_ERR_INVALID_ARG, "gqa_decode_token: bad arguments");
-  int rc = check_head(c, m->lm_head, m->vocab, m->gamma_output);
+  if (m->lm_head_type != GQA_HEAD_Q6_K && m->lm_head_type != GQA_HEAD_Q8_0)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_decode_token: lm_head_type %d", m->lm_head_type);
+  const bool q8 = m->lm_head_type == GQA_HEAD_Q8_0;
+  int rc = check_head(c, q8, m->lm_head, m->vocab, m->gamma_output);
   if (rc != GQA_OK) return rc;
   for (int l = 0; l < m->n_layers; ++l) {
     rc = check_block_weights(c, &m->attn[l]);
@@ -1058,7 +1112,8 @@ int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float*
   DeviceGuard g(c->device);
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = c->layers_pdl != 0;
-  GQA_CUDA(launch_embed_q4(m->token_embd, m->vocab, d_token, state, c->status, st, pdl));
+  GQA_CUDA(launch_embed_q4(m->token_embd, m->vocab, block_d_model(block_model(c)), d_token, state,
+                           c->status, st, pdl));
   Lengths len{};
   len.pos_dev = d_pos;
   for (int l = 0; l < m->n_layers; ++l) {
@@ -1068,7 +1123,7 @@ int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float*
     if (rc == GQA_OK) rc = ffn_impl(c, st, &m->ffn[l], state, pdl);
     if (rc != GQA_OK) return rc;
   }
-  GQA_CUDA(launch_lm_head(m->lm_head, m->vocab, m->gamma_output, state, logits, d_token,
+  GQA_CUDA(launch_lm_head(q8, m->lm_head, m->vocab, m->gamma_output, state, logits, d_token,
                           c->head_best, reinterpret_cast<unsigned*>(c->counters + kHeadDoneSlot),
                           c->status, c->head_grid, st, pdl));
   GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, pdl));

@@ -16,12 +16,14 @@
 // weights per 18-byte block, an fp16 scale d followed by 16 bytes of 4-bit
 // codes; weight j < 16 is d * ((qs[j] & 15) - 8), weight j + 16 is
 // d * ((qs[j] >> 4) - 8).  A row of K inputs is K / 32 blocks: 864 bytes for
-// K = d_model = 1536, 5040 bytes for K = d_ffn = 8960 (both multiples of 16,
-// so a CTA's rows are whole 1-D bulk copies).
+// K = d_model = 1536, 5040 bytes for K = d_ffn = 8960 (Qwen2.5-1.5B); 504 and
+// 2736 bytes for the Qwen2.5-0.5B sizes 896 and 4864 (generate_stream_05b.c:
+// 22-26).  A CTA's rows are one 1-D bulk copy, so rows per CTA x row bytes is
+// a multiple of 16 for every instance.
 //
 // Each CTA owns 8 consecutive output rows, one warp per row (two rows --
-// gate and up -- for kGateUp; for kDown 4 rows, two warps per row, each
-// taking half of K).  It copies their weights into shared memory (and the
+// gate and up -- for kGateUp; for kDown 4 rows, several warps per row, each
+// taking a part of K).  It copies their weights into shared memory (and the
 // RMSNorm weights into registers) before its programmatic-dependency wait --
 // the weights do not depend on the previous kernel -- then reads the input
 // vector into shared memory, block b's 32 values rotated by 4b so that the
@@ -39,12 +41,25 @@
 namespace gqa {
 
 constexpr int kQ4BlockBytes = 18;
-constexpr int kDModel = 1536;
-constexpr int kDFfn = 8960;
 constexpr float kRmsEps = 1e-6f;              // EPSILON of the reference
 constexpr long long kGemvWaitBudget = 2000000000LL;
 
 enum GemvMode { kQkv = 0, kWo = 1, kGateUp = 2, kDown = 3 };
+
+// The decoder sizes each instance is built for: model 0 is Qwen2.5-1.5B
+// (qwen_server.c), model 1 Qwen2.5-0.5B (generate_stream_05b.c:22-26).
+template <int kModel>
+struct ModelDims;
+template <>
+struct ModelDims<0> {
+  static constexpr int kDModel = 1536, kDFfn = 8960;
+  static constexpr int kDownWarps = 20, kDownSplit = 5;  // 4 rows x 5 parts of 56 blocks
+};
+template <>
+struct ModelDims<1> {
+  static constexpr int kDModel = 896, kDFfn = 4864;
+  static constexpr int kDownWarps = 16, kDownSplit = 4;  // 4 rows x 4 parts of 38 blocks
+};
 
 constexpr int q4_row_bytes_of(int k) { return (k / 32) * kQ4BlockBytes; }
 
@@ -52,31 +67,34 @@ struct GemvParams {
   const uint8_t* w;     // Q4_0 rows (kGateUp: gate)
   const uint8_t* w2;    // kGateUp: up; else unused
   const float* bias;    // kQkv: [M]; else unused
-  const float* gamma;   // kQkv / kGateUp: RMSNorm weight [kDModel]
+  const float* gamma;   // kQkv / kGateUp: RMSNorm weight [d_model]
   const float* x;       // input vector [K]
   float* y;             // kQkv: qkv, kGateUp: h (written); kWo / kDown: state (added to)
   int M;
   int* status;
 };
 
-template <int kMode>
+template <int kMode, int kModel>
 struct GemvShape {
-  static constexpr int K = kMode == kDown ? kDFfn : kDModel;
+  using M = ModelDims<kModel>;
+  static constexpr int K = kMode == kDown ? M::kDFfn : M::kDModel;
   static constexpr int kRowBytes = q4_row_bytes_of(K);
   static constexpr int kMats = kMode == kGateUp ? 2 : 1;
-  // The down projection (K = 8960) splits each row over 5 warps, 4 rows per
-  // CTA, for enough warps per SM; the others take a row (or a gate/up pair)
-  // per warp, 8 per CTA.
-  static constexpr int kWarps = kMode == kDown ? 20 : 8;
+  // The down projection (K = d_ffn) splits each row over several warps, 4
+  // rows per CTA, for enough warps per SM; the others take a row (or a
+  // gate/up pair) per warp, 8 per CTA.
+  static constexpr int kWarps = kMode == kDown ? M::kDownWarps : 8;
   static constexpr int kThreads = 32 * kWarps;
-  static constexpr int kSplitK = kMode == kDown ? 5 : 1;       // warps per row
-  static constexpr int kRows = kWarps / kSplitK;               // rows per CTA
+  static constexpr int kSplitK = kMode == kDown ? M::kDownSplit : 1;  // warps per row
+  static constexpr int kRows = kWarps / kSplitK;                      // rows per CTA
   static constexpr int kWBytes = kMats * kRows * kRowBytes + 16;  // + tail for 32-bit reads
-  static constexpr int kInPerThread = K / kThreads;
+  static constexpr int kInPerThread = (K + kThreads - 1) / kThreads;
+  static constexpr bool kEvenIn = K % kThreads == 0;
   static constexpr int kBlocks = K / 32;
   static constexpr bool kNorm = kMode == kQkv || kMode == kGateUp;
   static constexpr bool kAdd = kMode == kWo || kMode == kDown;
-  static_assert(K % kThreads == 0 && kBlocks % kSplitK == 0, "even split");
+  static_assert(K % 32 == 0 && kBlocks % kSplitK == 0 && kWarps % kSplitK == 0, "even split");
+  static_assert((kRows * kRowBytes) % 16 == 0, "a CTA's rows must be one bulk copy");
   // dynamic shared memory: weights | z[K] | red[2 * kWarps] | full barrier
   static constexpr size_t kRedBytes = (sizeof(float) * 2 * kWarps + 15) / 16 * 16;
   static constexpr size_t kSmem = (size_t)kWBytes + sizeof(float) * K + kRedBytes + 16;
@@ -154,9 +172,10 @@ __device__ __forceinline__ void warp_rows_dot(const uint8_t* wrow, int row_strid
     for (int off = 16; off > 0; off >>= 1) out[i] += __shfl_xor_sync(0xffffffffu, out[i], off);
 }
 
-template <int kMode>
-__global__ void __launch_bounds__(GemvShape<kMode>::kThreads) gemv_q4_kernel(const GemvParams p) {
-  using S = GemvShape<kMode>;
+template <int kMode, int kModel>
+__global__ void __launch_bounds__(GemvShape<kMode, kModel>::kThreads)
+    gemv_q4_kernel(const GemvParams p) {
+  using S = GemvShape<kMode, kModel>;
   extern __shared__ __align__(128) unsigned char gemv_smem[];
   uint8_t* sw = gemv_smem;
   float* sz = reinterpret_cast<float*>(gemv_smem + S::kWBytes);
@@ -181,10 +200,13 @@ __global__ void __launch_bounds__(GemvShape<kMode>::kThreads) gemv_q4_kernel(con
             "r"(S::kRows * S::kRowBytes), "r"(smem_addr(full)) : "memory");
     }
   }
+  // input j = tid + k * kThreads of this thread exists when in_range(k)
+  auto in_range = [&](int k) { return S::kEvenIn || tid + k * S::kThreads < S::K; };
   float gm[S::kInPerThread];
   if (S::kNorm) {
 #pragma unroll
-    for (int k = 0; k < S::kInPerThread; ++k) gm[k] = p.gamma[tid + k * S::kThreads];
+    for (int k = 0; k < S::kInPerThread; ++k)
+      gm[k] = in_range(k) ? p.gamma[tid + k * S::kThreads] : 0.f;
   }
   const float bias = (kMode == kQkv && lane == 0 && part == 0) ? p.bias[r0 + row] : 0.f;
   // Dependents are released only once this grid runs for real: launched
@@ -197,7 +219,7 @@ __global__ void __launch_bounds__(GemvShape<kMode>::kThreads) gemv_q4_kernel(con
   // ---- the input vector (RMSNorm'ed for the QKV and gate/up projections) ----
   float xv[S::kInPerThread];
 #pragma unroll
-  for (int k = 0; k < S::kInPerThread; ++k) xv[k] = p.x[tid + k * S::kThreads];
+  for (int k = 0; k < S::kInPerThread; ++k) xv[k] = in_range(k) ? p.x[tid + k * S::kThreads] : 0.f;
   if (S::kNorm) {
     float ss = 0.f;
 #pragma unroll
@@ -214,7 +236,8 @@ __global__ void __launch_bounds__(GemvShape<kMode>::kThreads) gemv_q4_kernel(con
     for (int k = 0; k < S::kInPerThread; ++k) xv[k] = xv[k] * scale * gm[k];
   }
 #pragma unroll
-  for (int k = 0; k < S::kInPerThread; ++k) sz[z_index(tid + k * S::kThreads)] = xv[k];
+  for (int k = 0; k < S::kInPerThread; ++k)
+    if (in_range(k)) sz[z_index(tid + k * S::kThreads)] = xv[k];
   __syncthreads();
 
   // ---- weights landed? (bounded wait; the copy always completes) ----
@@ -248,13 +271,14 @@ __global__ void __launch_bounds__(GemvShape<kMode>::kThreads) gemv_q4_kernel(con
   if (lane == 0) p.y[r0 + row] = out;
 }
 
-template <int kMode>
-static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t st, bool pdl) {
-  if (p.M % GemvShape<kMode>::kRows) return cudaErrorInvalidValue;
+template <int kMode, int kModel>
+static cudaError_t launch_gemv_model(const GemvParams& p, cudaStream_t st, bool pdl) {
+  using S = GemvShape<kMode, kModel>;
+  if (p.M % S::kRows) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.M / GemvShape<kMode>::kRows);
-  cfg.blockDim = dim3(GemvShape<kMode>::kThreads);
-  cfg.dynamicSmemBytes = GemvShape<kMode>::kSmem;
+  cfg.gridDim = dim3(p.M / S::kRows);
+  cfg.blockDim = dim3(S::kThreads);
+  cfg.dynamicSmemBytes = S::kSmem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -263,48 +287,72 @@ static cudaError_t launch_gemv(const GemvParams& p, cudaStream_t st, bool pdl) {
   cfg.numAttrs = pdl ? 1 : 0;
   GemvParams copy = p;
   void* args[] = {&copy};
-  return cudaLaunchKernelExC(&cfg, (const void*)gemv_q4_kernel<kMode>, args);
+  return cudaLaunchKernelExC(&cfg, (const void*)gemv_q4_kernel<kMode, kModel>, args);
 }
 
-int block_d_model() { return kDModel; }
-int block_d_ffn() { return kDFfn; }
+template <int kMode>
+static cudaError_t launch_gemv(int model, const GemvParams& p, cudaStream_t st, bool pdl) {
+  switch (model) {
+    case 0: return launch_gemv_model<kMode, 0>(p, st, pdl);
+    case 1: return launch_gemv_model<kMode, 1>(p, st, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int block_d_model(int model) {
+  return model == 0 ? ModelDims<0>::kDModel : model == 1 ? ModelDims<1>::kDModel : 0;
+}
+int block_d_ffn(int model) {
+  return model == 0 ? ModelDims<0>::kDFfn : model == 1 ? ModelDims<1>::kDFfn : 0;
+}
+int block_max_d_ffn() { return ModelDims<0>::kDFfn > ModelDims<1>::kDFfn ? ModelDims<0>::kDFfn
+                                                                         : ModelDims<1>::kDFfn; }
+
+template <int kMode, int kModel>
+static cudaError_t allow_smem() {
+  return cudaFuncSetAttribute((const void*)gemv_q4_kernel<kMode, kModel>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)GemvShape<kMode, kModel>::kSmem);
+}
 
 cudaError_t prepare_block_kernels() {
-  return cudaFuncSetAttribute((const void*)gemv_q4_kernel<kDown>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)GemvShape<kDown>::kSmem);
+  cudaError_t e = allow_smem<kDown, 0>();
+  if (e == cudaSuccess) e = allow_smem<kDown, 1>();
+  if (e == cudaSuccess) e = allow_smem<kGateUp, 0>();
+  if (e == cudaSuccess) e = allow_smem<kGateUp, 1>();
+  return e;
 }
 
 // state -> RMSNorm -> W_qkv (+ bias) -> qkv[M]
-cudaError_t launch_qkv_gemv(const void* w, const float* bias, const float* gamma,
+cudaError_t launch_qkv_gemv(int model, const void* w, const float* bias, const float* gamma,
                             const float* state, float* qkv, int M, int* status, cudaStream_t st,
                             bool pdl) {
   GemvParams p{static_cast<const uint8_t*>(w), nullptr, bias, gamma, state, qkv, M, status};
-  return launch_gemv<kQkv>(p, st, pdl);
+  return launch_gemv<kQkv>(model, p, st, pdl);
 }
 
 // state[M] += W_o * attn
-cudaError_t launch_wo_gemv(const void* w, const float* attn, float* state, int M, int* status,
-                           cudaStream_t st, bool pdl) {
+cudaError_t launch_wo_gemv(int model, const void* w, const float* attn, float* state, int M,
+                           int* status, cudaStream_t st, bool pdl) {
   GemvParams p{static_cast<const uint8_t*>(w), nullptr, nullptr, nullptr, attn, state, M, status};
-  return launch_gemv<kWo>(p, st, pdl);
+  return launch_gemv<kWo>(model, p, st, pdl);
 }
 
 // state -> RMSNorm -> h[d_ffn] = silu(W_gate z) * (W_up z)
-cudaError_t launch_gateup_gemv(const void* w_gate, const void* w_up, const float* gamma,
-                               const float* state, float* h, int* status, cudaStream_t st,
-                               bool pdl) {
+cudaError_t launch_gateup_gemv(int model, const void* w_gate, const void* w_up,
+                               const float* gamma, const float* state, float* h, int* status,
+                               cudaStream_t st, bool pdl) {
   GemvParams p{static_cast<const uint8_t*>(w_gate), static_cast<const uint8_t*>(w_up), nullptr,
-               gamma, state, h, kDFfn, status};
-  return launch_gemv<kGateUp>(p, st, pdl);
+               gamma, state, h, block_d_ffn(model), status};
+  return launch_gemv<kGateUp>(model, p, st, pdl);
 }
 
 // state[d_model] += W_down * h
-cudaError_t launch_down_gemv(const void* w_down, const float* h, float* state, int* status,
-                             cudaStream_t st, bool pdl) {
-  GemvParams p{static_cast<const uint8_t*>(w_down), nullptr, nullptr, nullptr, h, state, kDModel,
-               status};
-  return launch_gemv<kDown>(p, st, pdl);
+cudaError_t launch_down_gemv(int model, const void* w_down, const float* h, float* state,
+                             int* status, cudaStream_t st, bool pdl) {
+  GemvParams p{static_cast<const uint8_t*>(w_down), nullptr, nullptr, nullptr, h, state,
+               block_d_model(model), status};
+  return launch_gemv<kDown>(model, p, st, pdl);
 }
 
 }  // namespace gqa

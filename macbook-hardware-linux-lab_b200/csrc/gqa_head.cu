@@ -163,6 +163,51 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
 
+// Greedy pick, warp -> CTA -> grid, run by the consumer threads of a head
+// kernel: (best_v, best_i) is the warp's pick (lane 0's is used).  The CTA's
+// pick goes to gbest[blockIdx.x]; the last CTA to arrive (an atomic counter)
+// reduces all of them with the tie rule of `better`, writes *token and
+// resets the counter for the next launch.
+__device__ __forceinline__ void head_pick(float best_v, int best_i, HeadBest* sbest, int* slast,
+                                          HeadBest* gbest, unsigned* done, int* token) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int grid = gridDim.x;
+  if (lane == 0) sbest[warp] = HeadBest{best_v, best_i};
+  consumers_sync();
+  if (tid == 0) {
+    HeadBest b = sbest[0];
+    for (int w = 1; w < kHeadConsumerWarps; ++w)
+      if (better(sbest[w].v, sbest[w].i, b.v, b.i)) b = sbest[w];
+    gbest[blockIdx.x] = b;
+    __threadfence();
+    *slast = atomicAdd(done, 1u) == (unsigned)grid - 1;
+  }
+  consumers_sync();
+  if (!*slast) return;
+  __threadfence();
+  HeadBest b{kNoPick, 0};
+  for (int i = tid; i < grid; i += kHeadConsumers) {
+    const float v = __ldcg(&gbest[i].v);
+    const int idx = __ldcg(&gbest[i].i);
+    if (better(v, idx, b.v, b.i)) b = HeadBest{v, idx};
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, b.v, off);
+    const int idx = __shfl_xor_sync(0xffffffffu, b.i, off);
+    if (better(v, idx, b.v, b.i)) b = HeadBest{v, idx};
+  }
+  consumers_sync();  // the reads of sbest above are done
+  if (lane == 0) sbest[warp] = b;
+  consumers_sync();
+  if (tid == 0) {
+    for (int w = 1; w < kHeadConsumerWarps; ++w)
+      if (better(sbest[w].v, sbest[w].i, b.v, b.i)) b = sbest[w];
+    *token = b.i;
+    *done = 0u;  // ready for the next launch
+  }
+}
+
 // The consumer lane's fixed part of the row arithmetic.
 struct LaneConst {
   int hh0, q, o0, o1;   // unit base, 4-weight group, word offsets of W0 / W1
@@ -355,49 +400,262 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
   if (!ok && lane == 0) atomicOr(p.status, kStatusWaitTimeout);
   if (!p.token) return;
 
-  // ---- greedy pick: warp -> CTA -> grid (the last CTA to arrive) ----
-  if (lane == 0) sm.best[warp] = HeadBest{best_v, best_i};
-  consumers_sync();
-  if (tid == 0) {
-    HeadBest b = sm.best[0];
-    for (int w = 1; w < kHeadConsumerWarps; ++w)
-      if (better(sm.best[w].v, sm.best[w].i, b.v, b.i)) b = sm.best[w];
-    p.best[blockIdx.x] = b;
-    __threadfence();
-    sm.last = atomicAdd(p.done, 1u) == (unsigned)grid - 1;
+  head_pick(best_v, best_i, sm.best, &sm.last, p.best, p.done, p.token);
+}
+
+// ---------------------------------------------------------------------------
+// Output RMSNorm + Q8_0 LM head + greedy pick (Qwen2.5-0.5B)
+//
+// The 0.5B generator's head is Q8_0 over 896 inputs (gemv_q8_0,
+// kernel_q8_0.cl:10-61; generate_stream_05b.c:845-864): 28 blocks of 34
+// bytes per row (fp16 d, then 32 int8 codes q), logit = sum_b d_b * sum_j
+// q_bj * z_32b+j.  952-byte rows start on 8-byte boundaries only, so
+// gqa_lm_head_q8_0_pack lays them out once, at load time, as two planes over
+// the rows rounded up to a multiple of 4 (Np):
+//   qs [Np][896]  codes XOR 0x80 (offset binary), reordered per row so that
+//                 block b = li + 14s (li < 14, s < 2), codes 16mq .. 16mq + 15
+//                 (mq < 2), sit at the 16 bytes from 16 * ((2s + mq) * 14 + li)
+//   d  [Np][28]   the fp16 scales
+// -- 952 bytes per row as before.  The kernel is the Q6_K head's pipeline with
+// stages of 32 rows: a consumer warp takes two rows, one per half-warp; lane li
+// of a half owns blocks li and li + 14 (lanes 14 and 15 idle), their 64 inputs
+// held in registers for the whole kernel, and reads a block's codes as two
+// 16-byte words -- the half-warp for the second row reads its blocks in the
+// other order, so the two rows' loads fall on different banks.  Codes become
+// exact floats by byte_perm into 2^23 + (q + 128) minus 2^23 + 128; each
+// block's sum is scaled by d once.
+// ---------------------------------------------------------------------------
+constexpr int kQ8K = 896;
+constexpr int kQ8Blocks = kQ8K / 32;                   // 28
+constexpr int kQ8BlockBytes = 34;
+constexpr int kQ8RowBytes = kQ8Blocks * kQ8BlockBytes;  // 952
+constexpr int kQ8Lanes = kQ8Blocks / 2;                 // lanes with blocks, per half-warp
+constexpr int kQ8DRow = kQ8Blocks * 2;                  // 56
+constexpr int kQ8StageRows = 2 * kHeadConsumerWarps;    // 32
+constexpr int kQ8StQs = kQ8StageRows * kQ8K;
+constexpr int kQ8StageBytes = kQ8StQs + kQ8StageRows * kQ8DRow;  // 30464
+constexpr int kQ8Stages = 6;
+static_assert(kQ8StQs % 16 == 0 && kQ8StageBytes % 16 == 0 && (4 * kQ8DRow) % 16 == 0,
+              "stage runs must stay 16-byte aligned");
+
+struct Q8Smem {
+  alignas(128) uint8_t stage[kQ8Stages][kQ8StageBytes];
+  alignas(16) float sz[kQ8K];
+  float red[kHeadConsumerWarps];
+  HeadBest best[kHeadConsumerWarps];
+  uint64_t full[kQ8Stages];
+  uint64_t empty[kQ8Stages];
+  int last;
+};
+
+size_t lm_head_q8_packed_bytes(long long n_rows) {
+  return (size_t)head_padded_rows(n_rows) * kQ8RowBytes;
+}
+
+// GGUF rows -> planes (one CTA per padded row; load time).  Padding rows get
+// code 0 and scale 0.
+__global__ void q8_pack_kernel(const uint8_t* __restrict__ src, int n_rows,
+                               uint8_t* __restrict__ dst) {
+  const long long r = blockIdx.x;
+  const long long np = head_padded_rows(n_rows);
+  uint8_t* qs = dst + r * kQ8K;
+  uint8_t* dd = dst + np * kQ8K + r * kQ8DRow;
+  for (int i = threadIdx.x; i < kQ8RowBytes; i += blockDim.x) {
+    const int b = i / kQ8BlockBytes, o = i % kQ8BlockBytes;
+    if (o < 2) {
+      dd[2 * b + o] = r < n_rows ? src[r * kQ8RowBytes + i] : 0;
+    } else {
+      const int j = o - 2, sl = b / kQ8Lanes, li = b % kQ8Lanes;
+      const int at = 16 * ((2 * sl + (j >> 4)) * kQ8Lanes + li) + (j & 15);
+      qs[at] = r < n_rows ? (uint8_t)(src[r * kQ8RowBytes + i] ^ 0x80) : (uint8_t)0x80;
+    }
   }
-  consumers_sync();
-  if (!sm.last) return;
-  __threadfence();
-  HeadBest b{kNoPick, 0};
-  for (int i = tid; i < grid; i += kHeadConsumers) {
-    const float v = __ldcg(&p.best[i].v);
-    const int idx = __ldcg(&p.best[i].i);
-    if (better(v, idx, b.v, b.i)) b = HeadBest{v, idx};
+}
+
+// One row of a stage, lane's part: blocks b_u = li + 14 (u ^ h) for u = 0, 1.
+// z[u][m] holds the inputs of codes 4m .. 4m + 3 of block b_u.
+__device__ __forceinline__ float q8_row_dot(const uint8_t* sb, int jrow, const int (&qoff)[2],
+                                            const int (&boff)[2], const float4 (&z)[2][8]) {
+  const uint8_t* qs = sb + jrow * kQ8K;
+  const unsigned short* dd =
+      reinterpret_cast<const unsigned short*>(sb + kQ8StQs) + jrow * kQ8Blocks;
+  // The second half-warp visits the lane's two blocks in the other order, so
+  // each block's term is rounded on its own and the pair is summed with a
+  // plain (commutative) add: a row's logit does not depend on which half-warp
+  // computes it, and equal rows give equal logits for the tie rule.
+  float v[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    float2 t0 = make_float2(0.f, 0.f), t1 = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int mq = 0; mq < 2; ++mq) {
+      const uint4 w = *reinterpret_cast<const uint4*>(qs + qoff[u] + 16 * kQ8Lanes * mq);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        float2 p01, p23;  // q = (q + 128) - 128, exact
+        bytes_to_floats(ws[m], 128.0f, p01, p23);
+        const float4 zz = z[u][4 * mq + m];
+        t0 = __ffma2_rn(p01, make_float2(zz.x, zz.y), t0);
+        t1 = __ffma2_rn(p23, make_float2(zz.z, zz.w), t1);
+      }
+    }
+    const float d = __half2float(__ushort_as_half(dd[boff[u]]));
+    const float2 t = __fadd2_rn(t0, t1);
+    v[u] = __fmul_rn(d, __fadd_rn(t.x, t.y));
+  }
+  return __fadd_rn(v[0], v[1]);
+}
+
+__global__ void __launch_bounds__(kHeadThreads, 1) lm_head_q8_kernel(const HeadParams p) {
+  extern __shared__ __align__(128) unsigned char head_smem_raw[];
+  Q8Smem& sm = *reinterpret_cast<Q8Smem*>(head_smem_raw);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_rows = p.n_rows;
+  const long long np = head_padded_rows(n_rows);
+  const int n_stages = (int)((np + kQ8StageRows - 1) / kQ8StageRows);
+  const int grid = gridDim.x;
+  if (tid == 0) {
+    for (int s = 0; s < kQ8Stages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kHeadConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kHeadConsumerWarps) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint8_t* qs = p.planes;
+      const uint8_t* dd = p.planes + np * kQ8K;
+      const uint64_t pol = l2_policy_evict_first();
+      int k = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < n_stages; t += grid, ++k) {
+        const int s = k % kQ8Stages;
+        if (k >= kQ8Stages &&
+            !mbar_wait_bounded(&sm.empty[s], ((k / kQ8Stages) - 1) & 1, kHeadWaitBudget)) {
+          ok = false;
+          break;
+        }
+        const long long r0 = (long long)t * kQ8StageRows;
+        const int nr = (int)min((long long)kQ8StageRows, np - r0);  // a multiple of 4
+        uint8_t* st = sm.stage[s];
+        mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(nr * kQ8RowBytes));
+        bulk_copy_g2s(st, qs + r0 * kQ8K, nr * kQ8K, &sm.full[s], pol);
+        bulk_copy_g2s(st + kQ8StQs, dd + r0 * kQ8DRow, nr * kQ8DRow, &sm.full[s], pol);
+        if (k == kQ8Stages - 1) {
+          pdl_wait();
+          pdl_launch_dependents();
+        }
+      }
+      if (k < kQ8Stages) {
+        pdl_wait();
+        pdl_launch_dependents();
+      }
+      if (!ok) atomicOr(p.status, kStatusWaitTimeout);
+      // Every copy issued has landed before the CTA may exit.
+      for (int kk = max(0, k - kQ8Stages); kk < k; ++kk)
+        mbar_wait_bounded(&sm.full[kk % kQ8Stages], (kk / kQ8Stages) & 1, kHeadWaitBudget);
+    } else {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  constexpr int kPer = (kQ8K + kHeadConsumers - 1) / kHeadConsumers;
+  auto in_range = [&](int k) { return tid + k * kHeadConsumers < kQ8K; };
+  float gm[kPer];
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) gm[k] = in_range(k) ? p.gamma[tid + k * kHeadConsumers] : 0.f;
+  pdl_wait();
+  pdl_launch_dependents();
+
+  // z = rmsnorm(state) * gamma (the k_output_norm step, generate_stream_05b.c:845-851)
+  float xv[kPer];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    xv[k] = in_range(k) ? p.state[tid + k * kHeadConsumers] : 0.f;
+    ss += xv[k] * xv[k];
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    const float v = __shfl_xor_sync(0xffffffffu, b.v, off);
-    const int idx = __shfl_xor_sync(0xffffffffu, b.i, off);
-    if (better(v, idx, b.v, b.i)) b = HeadBest{v, idx};
-  }
-  consumers_sync();  // the reads of sm.best above are done
-  if (lane == 0) sm.best[warp] = b;
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if (lane == 0) sm.red[warp] = ss;
   consumers_sync();
-  if (tid == 0) {
-    for (int w = 1; w < kHeadConsumerWarps; ++w)
-      if (better(sm.best[w].v, sm.best[w].i, b.v, b.i)) b = sm.best[w];
-    *p.token = b.i;
-    *p.done = 0u;  // ready for the next launch
+  float tot = 0.f;
+#pragma unroll
+  for (int k = 0; k < kHeadConsumerWarps; ++k) tot += sm.red[k];
+  const float scale = 1.0f / sqrtf(tot / (float)kQ8K + kHeadRmsEps);
+#pragma unroll
+  for (int k = 0; k < kPer; ++k)
+    if (in_range(k)) sm.sz[tid + k * kHeadConsumers] = xv[k] * scale * gm[k];
+  consumers_sync();
+
+  const int h = lane >> 4, li = lane & 15;
+  const bool active = li < kQ8Lanes;
+  int qoff[2], boff[2];
+  float4 z[2][8];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int sl = u ^ h;
+    const int b = active ? li + kQ8Lanes * sl : 0;
+    qoff[u] = 16 * (2 * sl * kQ8Lanes + (active ? li : 0));
+    boff[u] = b;
+#pragma unroll
+    for (int m = 0; m < 8; ++m)
+      z[u][m] = active ? *reinterpret_cast<const float4*>(sm.sz + 32 * b + 4 * m)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
   }
+
+  float best_v = kNoPick;
+  int best_i = 0;
+  bool ok = true;
+  int k = 0;
+  for (int t = blockIdx.x; t < n_stages; t += grid, ++k) {
+    const int s = k % kQ8Stages;
+    if (!mbar_wait_bounded(&sm.full[s], (k / kQ8Stages) & 1, kHeadWaitBudget)) {
+      ok = false;
+      break;
+    }
+    const int jrow = 2 * warp + h;
+    const int r = t * kQ8StageRows + jrow;
+    float acc = 0.f;
+    if (active && r < n_rows) acc = q8_row_dot(sm.stage[s], jrow, qoff, boff, z);
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (li == 0 && r < n_rows) {
+      if (p.logits) p.logits[r] = acc;
+      if (acc > best_v) {  // rows rise within a half-warp: the first maximum stays
+        best_v = acc;
+        best_i = r;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) head_arrive(&sm.empty[s]);
+  }
+  if (!ok && lane == 0) atomicOr(p.status, kStatusWaitTimeout);
+  if (!p.token) return;
+  {  // the two half-warps' picks meet in lane 0
+    const float v = __shfl_down_sync(0xffffffffu, best_v, 16);
+    const int idx = __shfl_down_sync(0xffffffffu, best_i, 16);
+    if (better(v, idx, best_v, best_i)) {
+      best_v = v;
+      best_i = idx;
+    }
+  }
+  head_pick(best_v, best_i, sm.best, &sm.last, p.best, p.done, p.token);
 }
 
 // ---------------------------------------------------------------------------
 // Token embedding: state = Q4_0 row *token of the table
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kEmbedThreads) embed_q4_kernel(const uint8_t* table, int n_rows,
-                                                                 const int* token, float* state,
-                                                                 int* status) {
+                                                                 int d_model, const int* token,
+                                                                 float* state, int* status) {
   pdl_wait();
   pdl_launch_dependents();
   const int t = *token;
@@ -405,8 +663,8 @@ __global__ void __launch_bounds__(kEmbedThreads) embed_q4_kernel(const uint8_t* 
     if (threadIdx.x == 0) atomicOr(status, kStatusBadToken);
     return;
   }
-  const uint8_t* row = table + (size_t)t * (kHeadK / 32) * kQ4Bytes;
-  for (int j = threadIdx.x; j < kHeadK; j += kEmbedThreads) {
+  const uint8_t* row = table + (size_t)t * (d_model / 32) * kQ4Bytes;
+  for (int j = threadIdx.x; j < d_model; j += kEmbedThreads) {
     const uint8_t* blk = row + (j >> 5) * kQ4Bytes;
     const int w = j & 31;
     const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
@@ -423,9 +681,19 @@ __global__ void __launch_bounds__(kEmbedThreads) embed_q4_kernel(const uint8_t* 
 int lm_head_grid(int n_sm) { return n_sm; }
 
 cudaError_t prepare_head_kernels() {
-  return cudaFuncSetAttribute((const void*)lm_head_kernel,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)sizeof(HeadSmem));
+  cudaError_t e = cudaFuncSetAttribute((const void*)lm_head_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(HeadSmem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void*)lm_head_q8_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Q8Smem));
+  return e;
+}
+
+cudaError_t launch_q8_pack(const void* src, int n_rows, void* dst, cudaStream_t st) {
+  q8_pack_kernel<<<(unsigned)head_padded_rows(n_rows), 256, 0, st>>>(
+      static_cast<const uint8_t*>(src), n_rows, static_cast<uint8_t*>(dst));
+  return cudaGetLastError();
 }
 
 cudaError_t launch_q6k_pack(const void* src, int n_rows, void* dst, cudaStream_t st) {
@@ -434,9 +702,10 @@ cudaError_t launch_q6k_pack(const void* src, int n_rows, void* dst, cudaStream_t
   return cudaGetLastError();
 }
 
-cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, const float* state,
-                           float* logits, int* token, void* best, unsigned* done, int* status,
-                           int grid, cudaStream_t st, bool pdl) {
+// q8: the Q8_0 head (lm_head_q8_kernel) instead of the Q6_K one.
+cudaError_t launch_lm_head(bool q8, const void* planes, int n_rows, const float* gamma,
+                           const float* state, float* logits, int* token, void* best,
+                           unsigned* done, int* status, int grid, cudaStream_t st, bool pdl) {
   HeadParams p{};
   p.planes = static_cast<const uint8_t*>(planes);
   p.n_rows = n_rows;
@@ -450,7 +719,7 @@ cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, c
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kHeadThreads);
-  cfg.dynamicSmemBytes = sizeof(HeadSmem);
+  cfg.dynamicSmemBytes = q8 ? sizeof(Q8Smem) : sizeof(HeadSmem);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -458,13 +727,14 @@ cudaError_t launch_lm_head(const void* planes, int n_rows, const float* gamma, c
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   void* args[] = {&p};
-  return cudaLaunchKernelExC(&cfg, (const void*)lm_head_kernel, args);
+  return cudaLaunchKernelExC(&cfg, q8 ? (const void*)lm_head_q8_kernel : (const void*)lm_head_kernel,
+                             args);
 }
 
 size_t lm_head_best_bytes(int grid) { return sizeof(HeadBest) * (size_t)grid; }
 
-cudaError_t launch_embed_q4(const void* table, int n_rows, const int* token, float* state,
-                            int* status, cudaStream_t st, bool pdl) {
+cudaError_t launch_embed_q4(const void* table, int n_rows, int d_model, const int* token,
+                            float* state, int* status, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(kEmbedThreads);
@@ -475,7 +745,7 @@ cudaError_t launch_embed_q4(const void* table, int n_rows, const int* token, flo
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   const uint8_t* tb = static_cast<const uint8_t*>(table);
-  void* args[] = {&tb, &n_rows, &token, &state, &status};
+  void* args[] = {&tb, &n_rows, &d_model, &token, &state, &status};
   return cudaLaunchKernelExC(&cfg, (const void*)embed_q4_kernel, args);
 }
 

@@ -11,7 +11,9 @@
 //                  out (:525-588): per layer W_qkv = attn_q | attn_k | attn_v
 //                  rows and b_qkv = the three biases, W_o, the FFN weights and
 //                  both norms; token_embd.weight; output_norm.weight; and
-//                  output.weight, laid out for the head by gqa_lm_head_pack.
+//                  output.weight, laid out for the head by gqa_lm_head_pack
+//                  (Q6_K) or gqa_lm_head_q8_0_pack (Q8_0, the 0.5B model of
+//                  generate_stream_05b.c:553-615), at the context's sizes.
 //                  Tensor types and shapes are checked (the server trusts them).
 //   gqa_session_*  SET_BASE / QUERY / RAW_QUERY / STATUS of the server
 //                  (:770-1054) without the socket: the same validation, the
@@ -38,20 +40,19 @@
 
 namespace gqa {
 int set_error(int code, const char* fmt, ...);
+int ctx_block_model(const gqa_ctx* c);
+int block_d_model(int model);
+int block_d_ffn(int model);
 }
 
 namespace {
 
 using gqa::set_error;
 
-constexpr int kDModel = 1536;
-constexpr int kDQkv = 2048;
-constexpr int kDKv = 256;
-constexpr int kDFfn = 8960;
 constexpr int kQ4Block = 18;
 constexpr int kEogDefault[2] = {151643, 151645};  // <|endoftext|>, <|im_end|> (:1007-1008)
 
-enum GgufType : uint32_t { kF32 = 0, kQ4_0 = 2, kQ6_K = 14 };
+enum GgufType : uint32_t { kF32 = 0, kQ4_0 = 2, kQ8_0 = 8, kQ6_K = 14 };
 
 // Bytes of n elements of a GGUF tensor type; 0 for a type this reader does
 // not size.
@@ -192,6 +193,7 @@ struct gqa_model_weights {
   void* token_embd = nullptr;
   float* gamma_output = nullptr;
   void* lm_head = nullptr;
+  int lm_head_type = GQA_HEAD_Q6_K;
 };
 
 // ---------------------------------------------------------------------------
@@ -206,7 +208,7 @@ struct gqa_session {
   gqa_model model{};
   std::vector<int> eog;
   cudaStream_t stream = nullptr;
-  float* state = nullptr;        // device [1536]
+  float* state = nullptr;        // device [d_model]
   int* d_tok = nullptr;          // device: token in, pick out
   int* d_pos = nullptr;          // device: next position
   int* h_buf = nullptr;          // pinned: prompt tokens (t_max) + pick + position
@@ -420,40 +422,57 @@ int load_impl(gqa_ctx* ctx, const gqa_gguf* g, int n_layers, gqa_model_weights* 
               size_t stage_bytes) {
   gqa_gguf_tensor t;
   int rc;
-  // token_embd.weight: Q4_0 [1536][vocab]; output.weight: Q6_K [1536][vocab]
-  if ((rc = expect(g, "token_embd.weight", kQ4_0, kDModel, -1, &t)) != GQA_OK) return rc;
+  // The sizes of the context's shape: Qwen2.5-1.5B (qwen_server.c:525-588) or
+  // Qwen2.5-0.5B (generate_stream_05b.c:553-615).
+  const int model = gqa::ctx_block_model(ctx);
+  if (model < 0)
+    return set_error(GQA_ERR_UNSUPPORTED,
+                     "gqa_model_load: the context's shape has no built decoder sizes");
+  const long long d_model = gqa::block_d_model(model), d_ffn = gqa::block_d_ffn(model);
+  const long long d_kv = d_model / (model == 0 ? 6 : 7);  // n_heads_kv * head_dim
+  const long long d_qkv = d_model + 2 * d_kv;
+  // token_embd.weight: Q4_0 [d_model][vocab]; output.weight: Q6_K (1.5B) or
+  // Q8_0 (0.5B) [d_model][vocab]
+  if ((rc = expect(g, "token_embd.weight", kQ4_0, d_model, -1, &t)) != GQA_OK) return rc;
   m->vocab = (int)t.ne[1];
   if ((rc = model_alloc(m, &m->token_embd, t.bytes)) != GQA_OK) return rc;
   if ((rc = upload(g, t, m->token_embd, stage, stage_bytes)) != GQA_OK) return rc;
-  if ((rc = expect(g, "output_norm.weight", kF32, kDModel, 1, &t)) != GQA_OK) return rc;
+  if ((rc = expect(g, "output_norm.weight", kF32, d_model, 1, &t)) != GQA_OK) return rc;
   if ((rc = model_alloc(m, (void**)&m->gamma_output, t.bytes)) != GQA_OK) return rc;
   if ((rc = upload(g, t, m->gamma_output, stage, stage_bytes)) != GQA_OK) return rc;
-  if ((rc = expect(g, "output.weight", kQ6_K, kDModel, m->vocab, &t)) != GQA_OK) return rc;
+  const bool q8 = model == 1;
+  m->lm_head_type = q8 ? GQA_HEAD_Q8_0 : GQA_HEAD_Q6_K;
+  if ((rc = expect(g, "output.weight", q8 ? kQ8_0 : kQ6_K, d_model, m->vocab, &t)) != GQA_OK)
+    return rc;
   {
     void* raw = nullptr;
     MODEL_CUDA(cudaMalloc(&raw, t.bytes));
     rc = upload(g, t, raw, stage, stage_bytes);
-    if (rc == GQA_OK) rc = model_alloc(m, &m->lm_head, (size_t)gqa_lm_head_packed_bytes(m->vocab));
-    if (rc == GQA_OK) rc = gqa_lm_head_pack(ctx, nullptr, raw, m->vocab, m->lm_head);
+    const long long packed =
+        q8 ? gqa_lm_head_q8_0_packed_bytes(m->vocab) : gqa_lm_head_packed_bytes(m->vocab);
+    if (rc == GQA_OK) rc = model_alloc(m, &m->lm_head, (size_t)packed);
+    if (rc == GQA_OK)
+      rc = q8 ? gqa_lm_head_q8_0_pack(ctx, nullptr, raw, m->vocab, m->lm_head)
+              : gqa_lm_head_pack(ctx, nullptr, raw, m->vocab, m->lm_head);
     if (rc == GQA_OK && cudaDeviceSynchronize() != cudaSuccess)
       rc = set_error(GQA_ERR_CUDA, "LM head pack failed");
     cudaFree(raw);
     if (rc != GQA_OK) return rc;
   }
 
-  const size_t q4_row = (size_t)(kDModel / 32) * kQ4Block;
-  const size_t q4_row_ffn = (size_t)(kDFfn / 32) * kQ4Block;
+  const size_t q4_row = (size_t)(d_model / 32) * kQ4Block;
+  const size_t q4_row_ffn = (size_t)(d_ffn / 32) * kQ4Block;
   for (int l = 0; l < n_layers; ++l) {
     const std::string b = "blk." + std::to_string(l) + ".";
     void *w_qkv, *b_qkv, *w_o, *g_attn, *w_gate, *w_up, *w_down, *g_ffn;
-    if ((rc = model_alloc(m, &w_qkv, kDQkv * q4_row)) != GQA_OK ||
-        (rc = model_alloc(m, &b_qkv, sizeof(float) * kDQkv)) != GQA_OK ||
-        (rc = model_alloc(m, &w_o, kDModel * q4_row)) != GQA_OK ||
-        (rc = model_alloc(m, &g_attn, sizeof(float) * kDModel)) != GQA_OK ||
-        (rc = model_alloc(m, &w_gate, kDFfn * q4_row)) != GQA_OK ||
-        (rc = model_alloc(m, &w_up, kDFfn * q4_row)) != GQA_OK ||
-        (rc = model_alloc(m, &w_down, kDModel * q4_row_ffn)) != GQA_OK ||
-        (rc = model_alloc(m, &g_ffn, sizeof(float) * kDModel)) != GQA_OK)
+    if ((rc = model_alloc(m, &w_qkv, d_qkv * q4_row)) != GQA_OK ||
+        (rc = model_alloc(m, &b_qkv, sizeof(float) * d_qkv)) != GQA_OK ||
+        (rc = model_alloc(m, &w_o, d_model * q4_row)) != GQA_OK ||
+        (rc = model_alloc(m, &g_attn, sizeof(float) * d_model)) != GQA_OK ||
+        (rc = model_alloc(m, &w_gate, d_ffn * q4_row)) != GQA_OK ||
+        (rc = model_alloc(m, &w_up, d_ffn * q4_row)) != GQA_OK ||
+        (rc = model_alloc(m, &w_down, d_model * q4_row_ffn)) != GQA_OK ||
+        (rc = model_alloc(m, &g_ffn, sizeof(float) * d_model)) != GQA_OK)
       return rc;
     struct Piece {
       const char* name;
@@ -461,21 +480,22 @@ int load_impl(gqa_ctx* ctx, const gqa_gguf* g, int n_layers, gqa_model_weights* 
       long long ne0, ne1;
       void* dst;
     };
-    // W_qkv = attn_q | attn_k | attn_v rows, b_qkv likewise (qwen_server.c:551-567)
+    // W_qkv = attn_q | attn_k | attn_v rows, b_qkv likewise (qwen_server.c:551-567,
+    // generate_stream_05b.c:583-596)
     const Piece pieces[] = {
-        {"attn_norm.weight", kF32, kDModel, 1, g_attn},
-        {"ffn_norm.weight", kF32, kDModel, 1, g_ffn},
-        {"attn_q.bias", kF32, kDModel, 1, b_qkv},
-        {"attn_k.bias", kF32, kDKv, 1, static_cast<float*>(b_qkv) + kDModel},
-        {"attn_v.bias", kF32, kDKv, 1, static_cast<float*>(b_qkv) + kDModel + kDKv},
-        {"attn_q.weight", kQ4_0, kDModel, kDModel, w_qkv},
-        {"attn_k.weight", kQ4_0, kDModel, kDKv, static_cast<char*>(w_qkv) + kDModel * q4_row},
-        {"attn_v.weight", kQ4_0, kDModel, kDKv,
-         static_cast<char*>(w_qkv) + (kDModel + kDKv) * q4_row},
-        {"attn_output.weight", kQ4_0, kDModel, kDModel, w_o},
-        {"ffn_gate.weight", kQ4_0, kDModel, kDFfn, w_gate},
-        {"ffn_up.weight", kQ4_0, kDModel, kDFfn, w_up},
-        {"ffn_down.weight", kQ4_0, kDFfn, kDModel, w_down},
+        {"attn_norm.weight", kF32, d_model, 1, g_attn},
+        {"ffn_norm.weight", kF32, d_model, 1, g_ffn},
+        {"attn_q.bias", kF32, d_model, 1, b_qkv},
+        {"attn_k.bias", kF32, d_kv, 1, static_cast<float*>(b_qkv) + d_model},
+        {"attn_v.bias", kF32, d_kv, 1, static_cast<float*>(b_qkv) + d_model + d_kv},
+        {"attn_q.weight", kQ4_0, d_model, d_model, w_qkv},
+        {"attn_k.weight", kQ4_0, d_model, d_kv, static_cast<char*>(w_qkv) + d_model * q4_row},
+        {"attn_v.weight", kQ4_0, d_model, d_kv,
+         static_cast<char*>(w_qkv) + (d_model + d_kv) * q4_row},
+        {"attn_output.weight", kQ4_0, d_model, d_model, w_o},
+        {"ffn_gate.weight", kQ4_0, d_model, d_ffn, w_gate},
+        {"ffn_up.weight", kQ4_0, d_model, d_ffn, w_up},
+        {"ffn_down.weight", kQ4_0, d_ffn, d_model, w_down},
     };
     for (const Piece& p : pieces) {
       if ((rc = expect(g, b + p.name, p.type, p.ne0, p.ne1, &t)) != GQA_OK) return rc;
@@ -532,6 +552,7 @@ int gqa_model_view(const gqa_model_weights* m, const gqa_layer_kv* kv, gqa_model
   out->gamma_output = m->gamma_output;
   out->lm_head = m->lm_head;
   out->vocab = m->vocab;
+  out->lm_head_type = m->lm_head_type;
   return GQA_OK;
 }
 
@@ -641,7 +662,12 @@ int gqa_session_create(gqa_ctx* ctx, const gqa_model* model, int t_max, const in
       rc = set_error(GQA_ERR_CUDA, "gqa_session_create: %s: %s", what, cudaGetErrorString(e));
   };
   cu(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking), "stream");
-  cu(cudaMalloc(&s->state, sizeof(float) * kDModel), "state");
+  const int model_sizes = gqa::ctx_block_model(ctx);
+  if (model_sizes < 0)
+    rc = set_error(GQA_ERR_UNSUPPORTED, "gqa_session_create: the context's shape has no built "
+                   "decoder sizes");
+  cu(cudaMalloc(&s->state, sizeof(float) * (model_sizes < 0 ? 1 : gqa::block_d_model(model_sizes))),
+     "state");
   cu(cudaMalloc(&s->d_tok, sizeof(int)), "token");
   cu(cudaMalloc(&s->d_pos, sizeof(int)), "position");
   cu(cudaMallocHost(&s->h_buf, sizeof(int) * ((size_t)t_max + 2)), "pinned buffer");

@@ -45,6 +45,9 @@ STATUS_BAD_LENGTH = 1
 STATUS_WAIT_TIMEOUT = 2
 STATUS_BAD_TOKEN = 8
 
+HEAD_Q6_K = 0   # gqa_model.lm_head_type: gqa_lm_head_pack layout (Qwen2.5-1.5B)
+HEAD_Q8_0 = 1   # gqa_lm_head_q8_0_pack layout (Qwen2.5-0.5B)
+
 
 class GqaError(RuntimeError):
     def __init__(self, code: int, message: str):
@@ -84,7 +87,8 @@ class Model(ctypes.Structure):
     _fields_ = [("n_layers", ctypes.c_int), ("attn", ctypes.POINTER(BlockWeights)),
                 ("ffn", ctypes.POINTER(FfnWeights)), ("kv", ctypes.POINTER(LayerKV)),
                 ("token_embd", ctypes.c_void_p), ("gamma_output", ctypes.c_void_p),
-                ("lm_head", ctypes.c_void_p), ("vocab", ctypes.c_int)]
+                ("lm_head", ctypes.c_void_p), ("vocab", ctypes.c_int),
+                ("lm_head_type", ctypes.c_int)]
 
 
 _vp = ctypes.c_void_p
@@ -133,6 +137,9 @@ _SIGNATURES = {
     "gqa_lm_head_packed_bytes": [_i],
     "gqa_lm_head_pack": [_vp, _vp, _vp, _i, _vp],
     "gqa_lm_head": [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp],
+    "gqa_lm_head_q8_0_packed_bytes": [_i],
+    "gqa_lm_head_q8_0_pack": [_vp, _vp, _vp, _i, _vp],
+    "gqa_lm_head_q8_0": [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp],
     "gqa_token_embedding": [_vp, _vp, _vp, _i, _vp, _vp],
     "gqa_decode_token": [_vp, _vp, ctypes.POINTER(Model), _vp, _vp, _vp, _vp, _i, _i],
     "gqa_gguf_open": [ctypes.c_char_p, ctypes.POINTER(_vp)],
@@ -161,7 +168,8 @@ _SIGNATURES = {
                                    _i],
 }
 _RESTYPES = {"gqa_last_error_string": ctypes.c_char_p, "gqa_version": ctypes.c_char_p,
-             "gqa_lm_head_packed_bytes": ctypes.c_longlong}
+             "gqa_lm_head_packed_bytes": ctypes.c_longlong,
+             "gqa_lm_head_q8_0_packed_bytes": ctypes.c_longlong}
 
 _lib = None
 
@@ -453,7 +461,8 @@ class Session:
 class ModelHandle:
     """A gqa_model together with the ctypes arrays it points into."""
 
-    def __init__(self, attn, ffn, kvs, token_embd, gamma_output, lm_head_packed, vocab: int):
+    def __init__(self, attn, ffn, kvs, token_embd, gamma_output, lm_head_packed, vocab: int,
+                 lm_head_type: int = 0):
         n = len(attn)
         assert len(ffn) == n and len(kvs) == n
         self._attn = (BlockWeights * n)(*attn)
@@ -461,7 +470,7 @@ class ModelHandle:
         self._kv = (LayerKV * n)(*kvs)
         self._keep = (token_embd, gamma_output, lm_head_packed)
         self.struct = Model(n, self._attn, self._ffn, self._kv, _ptr(token_embd),
-                            _ptr(gamma_output), _ptr(lm_head_packed), vocab)
+                            _ptr(gamma_output), _ptr(lm_head_packed), vocab, lm_head_type)
 
 
 class Context:
@@ -616,6 +625,19 @@ class Context:
                 stream=None) -> None:
         _check(lib().gqa_lm_head(self._h, _stream(stream), _ptr(packed), n_rows, _ptr(gamma),
                                  _ptr(state), _ptr(logits), _ptr(token)))
+
+    @staticmethod
+    def lm_head_q8_0_packed_bytes(n_rows: int) -> int:
+        return int(lib().gqa_lm_head_q8_0_packed_bytes(n_rows))
+
+    def lm_head_q8_0_pack(self, q8, n_rows: int, packed, stream=None) -> None:
+        _check(lib().gqa_lm_head_q8_0_pack(self._h, _stream(stream), _ptr(q8), n_rows,
+                                           _ptr(packed)))
+
+    def lm_head_q8_0(self, packed, n_rows: int, gamma, state, logits=None, token=None,
+                     stream=None) -> None:
+        _check(lib().gqa_lm_head_q8_0(self._h, _stream(stream), _ptr(packed), n_rows, _ptr(gamma),
+                                      _ptr(state), _ptr(logits), _ptr(token)))
 
     def token_embedding(self, table, n_rows: int, d_token, state, stream=None) -> None:
         _check(lib().gqa_token_embedding(self._h, _stream(stream), _ptr(table), n_rows,

@@ -33,6 +33,7 @@ W_HEAD, GAMMA_OUT, TOKEN_EMBD, HEAD_X = 17, 18, 19, 20
 
 Q4_0_BLOCK_BYTES = 18
 Q6_K_BLOCK_BYTES = 210
+Q8_0_BLOCK_BYTES = 34
 
 
 def _mix(z: np.ndarray) -> np.ndarray:
@@ -200,6 +201,47 @@ def q6_k_planes(blocks: np.ndarray, rows: int) -> np.ndarray:
                            sc.reshape(-1), b[:, :, 208:].reshape(-1)])
 
 
+def q8_0_matrix(seed: int, stream_id: int, rows: int, cols: int = 896,
+                scale: float = 2.0 ** -8) -> np.ndarray:
+    """A Q8_0 matrix [rows][cols / 32 blocks] as bytes (the reference's
+    block_q8_0, generate_stream_05b.c:42-45: little-endian fp16 d, then 32
+    int8 codes).  Block b takes splitmix64 outputs 5b .. 5b+4 of the stream:
+    the first sets d = scale * (0.5 + u), u uniform in [0, 1), the other four
+    are the codes.  With the default scale, rows dotted with a unit-RMS input
+    give logits of about 8 RMS."""
+    nb = rows * (cols // 32)
+    u = uniform_u64(seed, stream_id, 5 * nb).reshape(nb, 5)
+    frac = (u[:, 0] >> np.uint64(11)).astype(np.float64) / float(1 << 53)
+    d = (scale * (0.5 + frac)).astype(np.float16)
+    out = np.empty((nb, Q8_0_BLOCK_BYTES), dtype=np.uint8)
+    out[:, 0:2] = d.view(np.uint8).reshape(nb, 2)
+    out[:, 2:] = np.ascontiguousarray(u[:, 1:]).astype("<u8").view(np.uint8).reshape(nb, 32)
+    return out.reshape(-1)
+
+
+def q8_0_dequant(blocks: np.ndarray, rows: int, cols: int = 896) -> np.ndarray:
+    """Dense float32 [rows][cols] of a Q8_0 byte matrix (w = d * q)."""
+    b = np.asarray(blocks, dtype=np.uint8).reshape(rows * (cols // 32), Q8_0_BLOCK_BYTES)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
+    q = b[:, 2:].view(np.int8).astype(np.float32)
+    return (q * d).reshape(rows, cols)
+
+
+def q8_0_planes(blocks: np.ndarray, rows: int) -> np.ndarray:
+    """The byte layout gqa_lm_head_q8_0_pack writes for 896-wide rows, over the
+    rows rounded up to a multiple of 4: codes [Np][896] then scales [Np][28]
+    (fp16).  In a row, the codes of block b = li + 14 s (li < 14, s < 2), 16
+    at a time (half mq < 2), sit at byte 16 ((2s + mq) 14 + li) XOR-ed with
+    0x80; padding rows hold code 0x80 and scale 0."""
+    np_rows = (rows + 3) // 4 * 4
+    b = np.zeros((np_rows, 28, Q8_0_BLOCK_BYTES), dtype=np.uint8)
+    b[:rows] = np.asarray(blocks, dtype=np.uint8).reshape(rows, 28, Q8_0_BLOCK_BYTES)
+    q = b[:, :, 2:] ^ np.uint8(0x80)                          # [row][b][32]
+    q[rows:] = 0x80
+    q = q.reshape(np_rows, 2, 14, 2, 16).transpose(0, 1, 3, 2, 4)  # [row][s][mq][li][16]
+    return np.concatenate([np.ascontiguousarray(q).reshape(-1), b[:, :, 0:2].reshape(-1)])
+
+
 def head_inputs(seed: int, vocab: int = 151936, d_model: int = 1536):
     """(w_head Q6_K bytes, gamma_out, token_embd Q4_0 bytes) of the model's
     ends: gamma_out ~ 1 + N(0, 0.1^2); embedding rows of unit RMS."""
@@ -209,20 +251,30 @@ def head_inputs(seed: int, vocab: int = 151936, d_model: int = 1536):
     return w_head, gamma, embd
 
 
-def attention_block_inputs(seed: int, t_max: int = 4096, d_model: int = 1536, n_heads_kv: int = 2):
+def head_q8_inputs(seed: int, vocab: int = 151936, d_model: int = 896):
+    """(w_head Q8_0 bytes, gamma_out, token_embd Q4_0 bytes) of the 0.5B
+    model's ends, drawn from the same streams as head_inputs."""
+    w_head = q8_0_matrix(seed, W_HEAD, vocab, d_model)
+    gamma = (1.0 + 0.1 * normal(seed, GAMMA_OUT, d_model)).astype(np.float32)
+    embd = q4_0_matrix(seed, TOKEN_EMBD, vocab, d_model, 1.0 / 4.6)
+    return w_head, gamma, embd
+
+
+def attention_block_inputs(seed: int, t_max: int = 4096, d_model: int = 1536, n_heads_kv: int = 2,
+                           head_dim: int = 128):
     """(state, w_qkv, b_qkv, w_o, gamma, k_cache, v_cache) of one layer's
     attention block: state, caches N(0, 1); Q4_0 weights scaled so each
     projection has unit-RMS rows; b_qkv ~ N(0, 0.1^2); gamma ~ 1 + N(0, 0.1^2)."""
-    n_qkv = d_model + 2 * n_heads_kv * 128
+    n_qkv = d_model + 2 * n_heads_kv * head_dim
     scale = 1.0 / (4.6 * np.sqrt(d_model))  # RMS of (code - 8) is ~4.6
     state = normal(seed, STATE, d_model)
     w_qkv = q4_0_matrix(seed, W_QKV, n_qkv, d_model, scale)
     b_qkv = (0.1 * normal(seed, B_QKV, n_qkv)).astype(np.float32)
     w_o = q4_0_matrix(seed, W_O, d_model, d_model, scale)
     gamma = (1.0 + 0.1 * normal(seed, GAMMA, d_model)).astype(np.float32)
-    n = n_heads_kv * t_max * 128
-    kc = normal(seed, K_CACHE, n).reshape(n_heads_kv, t_max, 128)
-    vc = normal(seed, V_CACHE, n).reshape(n_heads_kv, t_max, 128)
+    n = n_heads_kv * t_max * head_dim
+    kc = normal(seed, K_CACHE, n).reshape(n_heads_kv, t_max, head_dim)
+    vc = normal(seed, V_CACHE, n).reshape(n_heads_kv, t_max, head_dim)
     return state, w_qkv, b_qkv, w_o, gamma, kc, vc
 
 

@@ -346,6 +346,30 @@ void oracle_output_norm(const float *x, const float *gamma, int n, float eps, fl
     for (int i = 0; i < n; i++) z[i] = x[i] * scale * gamma[i];
 }
 
+/* The Qwen2.5-0.5B LM head, gemv_q8_0 (kernel_q8_0.cl:10-61), restated on
+ * the CPU (the reference has no CPU path for it).  For each row, lane l of
+ * the kernel's 32-lane group accumulates d_b * q_bl * x[32b + l] over the row's
+ * k / 32 blocks in block order (:30-37); the 32 lane sums then meet by the
+ * kernel's tree, halves 16, 8, 4, 2, 1 (:40-53).  w: n_rows rows of k / 32
+ * block_q8_0 (fp16 d, 32 int8 codes; 34 bytes each). */
+void oracle_gemv_q8_0(const uint8_t *w, const float *x, int n_rows, int k, float *y) {
+    const int nb = k / 32;
+    for (int r = 0; r < n_rows; r++) {
+        const uint8_t *row = w + (size_t)r * nb * 34;
+        float acc[32];
+        for (int l = 0; l < 32; l++) acc[l] = 0.0f;
+        for (int b = 0; b < nb; b++) {
+            const uint8_t *blk = row + b * 34;
+            const float d = oracle_fp16_to_float((uint16_t)(blk[0] | (blk[1] << 8)));
+            for (int l = 0; l < 32; l++)
+                acc[l] += d * (float)(int8_t)blk[2 + l] * x[b * 32 + l];
+        }
+        for (int s = 16; s > 0; s >>= 1)
+            for (int l = 0; l < s; l++) acc[l] += acc[l + s];
+        y[r] = acc[0];
+    }
+}
+
 /* The server's greedy pick (qwen_server.c:998-1005): best_val starts at
  * -1e30, a logit replaces it only when strictly larger, so the first row of
  * the maximum wins, NaN never does, and 0 comes back when nothing beats -1e30. */

@@ -282,9 +282,69 @@ def ref_decoder_layer(x_in, attn, ffn, k_cache, v_cache, pos, seq_len) -> np.nda
     return out
 
 
+def ref_gemv_q4_0(w, x, bias, M: int, K: int) -> np.ndarray:
+    """The reference's own cpu_gemv_q4_0_bias (test_28_layers_real.c:90-108) at
+    any size: y = W x (+ bias), W Q4_0 bytes [M][K / 32 blocks]."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    assert w.size == M * (K // 32) * 18
+    fn = _load(REF_LAYER_SO).ref_gemv_q4_0_bias
+    if fn.argtypes is None:
+        fn.argtypes = [ctypes.c_void_p, _fp, _fp, _fp, _i, _i]
+        fn.restype = None
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    y = np.zeros(M, dtype=np.float32)
+    fn(w.ctypes.data, _fptr(x), None if b is None else _fptr(b), _fptr(y), M, K)
+    return y
+
+
+def ref_swiglu(w_gate, w_up, x, M: int, K: int) -> np.ndarray:
+    """The reference's own cpu_swiglu_fused (test_28_layers_real.c:110-131):
+    h = silu(W_gate x) * (W_up x) with its stable SiLU."""
+    wg = np.ascontiguousarray(w_gate, dtype=np.uint8)
+    wu = np.ascontiguousarray(w_up, dtype=np.uint8)
+    assert wg.size == wu.size == M * (K // 32) * 18
+    fn = _load(REF_LAYER_SO).ref_swiglu_fused
+    if fn.argtypes is None:
+        fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _fp, _fp, _i, _i]
+        fn.restype = None
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    h = np.zeros(M, dtype=np.float32)
+    fn(wg.ctypes.data, wu.ctypes.data, _fptr(x), _fptr(h), M, K)
+    return h
+
+
+def decoder_layer_sized(x_in, attn, ffn, k_cache, v_cache, pos: int, seq_len: int,
+                        n_heads_q: int, n_heads_kv: int, head_dim: int, d_ffn: int) -> np.ndarray:
+    """One decoder layer at any size, in the order of cpu_decoder_layer_step
+    (test_28_layers_real.c:192-318) and of the 0.5B generator's layer step
+    (generate_stream_05b.c:364-476): RMSNorm, the reference's compiled Q4_0
+    GEMV + bias, RoPE + append + attention (the shape-generic restatement),
+    W_o GEMV + residual, RMSNorm, the reference's compiled fused SwiGLU GEMV,
+    down GEMV + residual.  At the 1.5B sizes it equals the compiled
+    cpu_decoder_layer_step (checked by the CPU tests).  Caches are updated in
+    place at row pos."""
+    w_qkv, b_qkv, w_o, g_a = attn
+    w_gate, w_up, w_down, g_f = ffn
+    d_model = n_heads_q * head_dim
+    d_qkv = d_model + 2 * n_heads_kv * head_dim
+    x = np.ascontiguousarray(x_in, dtype=np.float32)
+    z1 = output_norm(x, g_a)
+    qkv = ref_gemv_q4_0(w_qkv, z1, b_qkv, d_qkv, d_model)
+    layer_attention(qkv, k_cache, v_cache, pos, seq_len, n_heads_q, n_heads_kv,
+                    head_dim=head_dim)
+    r = ref_gemv_q4_0(w_o, qkv[:d_model], None, d_model, d_model)
+    r = (r + x).astype(np.float32)
+    z2 = output_norm(r, g_f)
+    h = ref_swiglu(w_gate, w_up, z2, d_ffn, d_model)
+    y = ref_gemv_q4_0(w_down, h, None, d_model, d_ffn)
+    return (y + r).astype(np.float32)
+
+
 # ---- around the decoder layers: embedding, output norm, LM head, pick -------
 
 Q6_K_ROW_BYTES = 1260  # 6 superblocks of 210 bytes per 1536-wide row
+D05B_MODEL, D05B_FFN = 896, 4864  # Qwen2.5-0.5B (generate_stream_05b.c:22-26)
 
 
 def token_embedding(table: np.ndarray, token: int, d_model: int = 1536) -> np.ndarray:
@@ -321,6 +381,29 @@ def greedy_pick(logits: np.ndarray) -> int:
         fn.argtypes = [_fp, _i]
         fn.restype = _i
     return int(fn(_fptr(logits), logits.size))
+
+
+def gemv_q8_0(w: np.ndarray, x: np.ndarray, n_rows: int, k: int = 896) -> np.ndarray:
+    """The 0.5B model's Q8_0 LM head GEMV (kernel_q8_0.cl:10-61), restated in
+    gqa_oracle.c with the kernel's lane sums and reduction tree."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    assert w.size >= n_rows * (k // 32) * 34
+    fn = _lib().oracle_gemv_q8_0
+    if fn.argtypes is None:
+        fn.argtypes = [ctypes.c_void_p, _fp, _i, _i, _fp]
+        fn.restype = None
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(n_rows, dtype=np.float32)
+    fn(w.ctypes.data, _fptr(x), n_rows, k, _fptr(y))
+    return y
+
+
+def lm_head_q8_0(state, gamma, w, n_rows: int):
+    """(logits, pick) of the 0.5B generator's step end (generate_stream_05b.c:
+    845-878): output RMSNorm, the Q8_0 GEMV, the host argmax."""
+    z = output_norm(state, gamma)
+    logits = gemv_q8_0(w, z, n_rows, z.size)
+    return logits, greedy_pick(logits)
 
 
 def ref_token_embedding(table: np.ndarray, token: int) -> np.ndarray:
@@ -376,11 +459,19 @@ def ref_lm_head(state: np.ndarray, gamma: np.ndarray, w: np.ndarray):
     return logits, greedy_pick(logits)
 
 
-def ref_decode_token(table, layers, kv, gamma_out, w_head, token: int, pos: int):
+def ref_decode_token(table, layers, kv, gamma_out, w_head, token: int, pos: int,
+                     model: str = "1.5b"):
     """One greedy step of the whole model on the CPU: embedding of `token`,
-    ref_decoder_layer for every layer (layers[l] = (attn, ffn), kv[l] =
-    (k_cache, v_cache) updated in place at row pos), output norm, Q6_K head,
-    pick.  Returns (logits, next token)."""
+    the decoder layer for every layer (layers[l] = (attn, ffn), kv[l] =
+    (k_cache, v_cache) updated in place at row pos), output norm, head, pick.
+    model "1.5b": the compiled cpu_decoder_layer_step and Q6_K GEMV; "0.5b":
+    decoder_layer_sized at the Qwen2.5-0.5B sizes and the Q8_0 head
+    (generate_stream_05b.c:836-878).  Returns (logits, next token)."""
+    if model == "0.5b":
+        x = token_embedding(table, token, D05B_MODEL)
+        for (attn, ffn), (kc, vc) in zip(layers, kv):
+            x = decoder_layer_sized(x, attn, ffn, kc, vc, pos, pos + 1, 14, 2, 64, D05B_FFN)
+        return lm_head_q8_0(x, gamma_out, w_head, len(w_head) // (D05B_MODEL // 32 * 34))
     x = token_embedding(table, token)
     for (attn, ffn), (kc, vc) in zip(layers, kv):
         x = ref_decoder_layer(x, attn, ffn, kc, vc, pos, pos + 1)
@@ -432,21 +523,30 @@ def ref_gguf_token(path: str, token: int) -> bytes:
 
 
 def ref_server_query(table, layers, kv, gamma_out, w_head, tokens, cur_pos: int, max_new: int,
-                     eog=(151643, 151645), t_max: int = REF_T_MAX, margins=None):
+                     eog=(151643, 151645), t_max: int = REF_T_MAX, margins=None,
+                     model: str = "1.5b"):
     """The server's QUERY loop (qwen_server.c:957-1049), restated over the
     compiled pieces: every prompt token through the layers at cur_pos + p (the
     head only after the last), then greedy picks -- stop before an
     end-of-generation id, emit, stop at max_new or t_max, else run the pick
     through the layers and the head.  kv[l] = (k_cache, v_cache) updated in
     place.  Returns the emitted ids; `margins`, when a list, receives the gap
-    between the two largest logits of every pick."""
+    between the two largest logits of every pick.  model "0.5b" runs the same
+    loop over the Qwen2.5-0.5B pieces (ref_decode_token)."""
     logits = None
     for p, tok in enumerate(tokens):
-        x = token_embedding(table, tok)
-        for (attn, ffn), (kc, vc) in zip(layers, kv):
-            x = ref_decoder_layer(x, attn, ffn, kc, vc, cur_pos + p, cur_pos + p + 1)
         if p == len(tokens) - 1:
-            logits, _ = ref_lm_head(x, gamma_out, w_head)
+            logits, _ = ref_decode_token(table, layers, kv, gamma_out, w_head, tok, cur_pos + p,
+                                         model)
+        elif model == "0.5b":
+            x = token_embedding(table, tok, D05B_MODEL)
+            for (attn, ffn), (kc, vc) in zip(layers, kv):
+                x = decoder_layer_sized(x, attn, ffn, kc, vc, cur_pos + p, cur_pos + p + 1, 14, 2,
+                                        64, D05B_FFN)
+        else:
+            x = token_embedding(table, tok)
+            for (attn, ffn), (kc, vc) in zip(layers, kv):
+                x = ref_decoder_layer(x, attn, ffn, kc, vc, cur_pos + p, cur_pos + p + 1)
     out = []
     next_pos = cur_pos + len(tokens)
     for gen in range(max_new):
@@ -459,7 +559,7 @@ def ref_server_query(table, layers, kv, gamma_out, w_head, tokens, cur_pos: int,
         out.append(best)
         if gen + 1 >= max_new or next_pos >= t_max:
             break
-        logits, _ = ref_decode_token(table, layers, kv, gamma_out, w_head, best, next_pos)
+        logits, _ = ref_decode_token(table, layers, kv, gamma_out, w_head, best, next_pos, model)
         next_pos += 1
     return out
 

@@ -117,3 +117,18 @@ int ref_decoder_layer(const float *x_in, const void *w_qkv, const float *b_qkv, 
     cpu_decoder_layer_step(x_in, &w, &kv, pos, seq_len, y_out);
     return 0;
 }
+
+/* The reference's own Q4_0 GEMV with bias and its fused gate/up GEMV with the
+ * stable SiLU (test_28_layers_real.c:90-131).  Both take their sizes as
+ * arguments, so the Qwen2.5-0.5B decoder layer (d_model 896, d_ffn 4864,
+ * generate_stream_05b.c:364-476), which the reference only has as OpenCL, is
+ * checked against a composition of these compiled pieces.  w: row-major
+ * block_q4_0 [M][K / 32]; bias may be NULL. */
+void ref_gemv_q4_0_bias(const void *w, const float *x, const float *bias, float *y, int M, int K) {
+    cpu_gemv_q4_0_bias((const block_q4_0 *)w, x, bias, y, M, K);
+}
+
+void ref_swiglu_fused(const void *w_gate, const void *w_up, const float *x, float *h, int M,
+                      int K) {
+    cpu_swiglu_fused((const block_q4_0 *)w_gate, (const block_q4_0 *)w_up, x, h, M, K);
+}

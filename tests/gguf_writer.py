@@ -67,21 +67,26 @@ def write(path, metadata, tensors, alignment: int = 32, version: int = 3,
     return {name: start + off for (name, _, _, _), off in zip(tensors, offsets)}
 
 
-def qwen_model(path, seeded, n_layers: int, vocab: int, seed: int, tokens=None):
+def qwen_model(path, seeded, n_layers: int, vocab: int, seed: int, tokens=None,
+               model: str = "1.5b"):
     """A Qwen2.5-1.5B-shaped GGUF (Q4_0 projections and embedding, Q6_K head,
     F32 norms and biases) with seeded weights, and the same weights as arrays:
     (offsets, {"embd", "head", "gamma_out", "layers": [((w_qkv, b_qkv, w_o, g_attn),
-    (w_gate, w_up, w_down, g_ffn))]})."""
-    d, dkv, dffn = 1536, 256, 8960
+    (w_gate, w_up, w_down, g_ffn))]}).  model "0.5b": the Qwen2.5-0.5B sizes
+    (d_model 896, 14 / 2 heads of 64, d_ffn 4864) with a Q8_0 head, the tensors
+    generate_stream_05b.c:553-615 reads."""
+    small = model == "0.5b"
+    d, dkv, dffn = (896, 128, 4864) if small else (1536, 256, 8960)
     s_in = 1.0 / (4.6 * np.sqrt(d))
     s_down = 1.0 / (4.6 * np.sqrt(dffn))
     f32 = lambda a: np.ascontiguousarray(a, dtype=np.float32).tobytes()
     embd = seeded.q4_0_matrix(seed, seeded.TOKEN_EMBD, vocab, d, 1.0 / 4.6)
-    head = seeded.q6_k_matrix(seed, seeded.W_HEAD, vocab, d)
+    head = (seeded.q8_0_matrix(seed, seeded.W_HEAD, vocab, d) if small
+            else seeded.q6_k_matrix(seed, seeded.W_HEAD, vocab, d))
     gamma_out = (1.0 + 0.1 * seeded.normal(seed, seeded.GAMMA_OUT, d)).astype(np.float32)
     tensors = [("token_embd.weight", T_Q4_0, [d, vocab], embd),
                ("output_norm.weight", T_F32, [d], f32(gamma_out)),
-               ("output.weight", T_Q6_K, [d, vocab], head)]
+               ("output.weight", T_Q8_0 if small else T_Q6_K, [d, vocab], head)]
     layers = []
     for l in range(n_layers):
         ls = seed * 100 + l
@@ -109,7 +114,8 @@ def qwen_model(path, seeded, n_layers: int, vocab: int, seed: int, tokens=None):
                     (b + "ffn_down.weight", T_Q4_0, [dffn, d], w_down)]
         layers.append(((w_qkv, b_qkv, w_o, g_attn), (w_gate, w_up, w_down, g_ffn)))
     meta = [("general.architecture", STR, "qwen2"), ("qwen2.block_count", U32, n_layers),
-            ("qwen2.embedding_length", U32, d), ("qwen2.attention.head_count", U32, 12),
+            ("qwen2.embedding_length", U32, d),
+            ("qwen2.attention.head_count", U32, 14 if small else 12),
             ("qwen2.attention.head_count_kv", U32, 2), ("qwen2.rope.freq_base", F32, 1e6),
             ("tokenizer.ggml.tokens", ARR,
              (STR, tokens if tokens is not None else [f"t{i}" for i in range(vocab)]))]
