@@ -417,11 +417,12 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
 //                 (mq < 2), sit at the 16 bytes from 16 * ((2s + mq) * 14 + li)
 //   d  [Np][28]   the fp16 scales
 // -- 952 bytes per row as before.  The kernel is the Q6_K head's pipeline with
-// stages of 32 rows: a consumer warp takes two rows, one per half-warp; lane li
-// of a half owns blocks li and li + 14 (lanes 14 and 15 idle), their 64 inputs
-// held in registers for the whole kernel, and reads a block's codes as two
-// 16-byte words -- the half-warp for the second row reads its blocks in the
-// other order, so the two rows' loads fall on different banks.  Codes become
+// stages of 64 rows (3 deep) over a contiguous, balanced row range per CTA: a
+// consumer warp takes four rows of a stage, two per half-warp, computed side by
+// side; lane li of a half owns blocks li and li + 14 (lanes 14 and 15 idle),
+// their 64 inputs held in registers for the whole kernel, and reads a block's
+// codes as two 16-byte words -- the second half-warp reads its blocks in the
+// other order, so the two halves' loads fall on different banks.  Codes become
 // exact floats by byte_perm into 2^23 + (q + 128) minus 2^23 + 128; each
 // block's sum is scaled by d once.
 // ---------------------------------------------------------------------------
@@ -431,10 +432,10 @@ constexpr int kQ8BlockBytes = 34;
 constexpr int kQ8RowBytes = kQ8Blocks * kQ8BlockBytes;  // 952
 constexpr int kQ8Lanes = kQ8Blocks / 2;                 // lanes with blocks, per half-warp
 constexpr int kQ8DRow = kQ8Blocks * 2;                  // 56
-constexpr int kQ8StageRows = 2 * kHeadConsumerWarps;    // 32
+constexpr int kQ8StageRows = 4 * kHeadConsumerWarps;    // 64: two rows per half-warp
 constexpr int kQ8StQs = kQ8StageRows * kQ8K;
-constexpr int kQ8StageBytes = kQ8StQs + kQ8StageRows * kQ8DRow;  // 30464
-constexpr int kQ8Stages = 6;
+constexpr int kQ8StageBytes = kQ8StQs + kQ8StageRows * kQ8DRow;  // 60928
+constexpr int kQ8Stages = 3;
 static_assert(kQ8StQs % 16 == 0 && kQ8StageBytes % 16 == 0 && (4 * kQ8DRow) % 16 == 0,
               "stage runs must stay 16-byte aligned");
 
@@ -472,39 +473,61 @@ __global__ void q8_pack_kernel(const uint8_t* __restrict__ src, int n_rows,
   }
 }
 
-// One row of a stage, lane's part: blocks b_u = li + 14 (u ^ h) for u = 0, 1.
-// z[u][m] holds the inputs of codes 4m .. 4m + 3 of block b_u.
-__device__ __forceinline__ float q8_row_dot(const uint8_t* sb, int jrow, const int (&qoff)[2],
-                                            const int (&boff)[2], const float4 (&z)[2][8]) {
-  const uint8_t* qs = sb + jrow * kQ8K;
-  const unsigned short* dd =
-      reinterpret_cast<const unsigned short*>(sb + kQ8StQs) + jrow * kQ8Blocks;
-  // The second half-warp visits the lane's two blocks in the other order, so
-  // each block's term is rounded on its own and the pair is summed with a
-  // plain (commutative) add: a row's logit does not depend on which half-warp
-  // computes it, and equal rows give equal logits for the tie rule.
-  float v[2];
+// Rows ja and jb of a stage, lane's part: blocks b_u = li + 14 (u ^ h) for
+// u = 0, 1.  z[u][m] holds the inputs of codes 4m .. 4m + 3 of block b_u,
+// shared by both rows; the two rows' chains are independent, which is what
+// keeps the lane's pipes busy.  The second half-warp visits the lane's two
+// blocks in the other order, so each block's term is rounded on its own and
+// the pair is summed with a plain (commutative) add: a row's logit does not
+// depend on which half-warp computes it, and equal rows give equal logits for
+// the tie rule.
+__device__ __forceinline__ void q8_rows_dot(const uint8_t* sb, int ja, int jb,
+                                            const int (&qoff)[2], const int (&boff)[2],
+                                            const float4 (&z)[2][8], float& out_a,
+                                            float& out_b) {
+  const uint8_t* qa = sb + ja * kQ8K;
+  const uint8_t* qb = sb + jb * kQ8K;
+  const unsigned short* dsc = reinterpret_cast<const unsigned short*>(sb + kQ8StQs);
+  float va[2], vb[2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
-    float2 t0 = make_float2(0.f, 0.f), t1 = make_float2(0.f, 0.f);
+    float2 a0 = make_float2(0.f, 0.f), a1 = a0, b0 = a0, b1 = a0;
 #pragma unroll
     for (int mq = 0; mq < 2; ++mq) {
-      const uint4 w = *reinterpret_cast<const uint4*>(qs + qoff[u] + 16 * kQ8Lanes * mq);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      const uint4 wa = *reinterpret_cast<const uint4*>(qa + qoff[u] + 16 * kQ8Lanes * mq);
+      const uint4 wb = *reinterpret_cast<const uint4*>(qb + qoff[u] + 16 * kQ8Lanes * mq);
+      const uint32_t wsa[4] = {wa.x, wa.y, wa.z, wa.w};
+      const uint32_t wsb[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        float2 p01, p23;  // q = (q + 128) - 128, exact
-        bytes_to_floats(ws[m], 128.0f, p01, p23);
         const float4 zz = z[u][4 * mq + m];
-        t0 = __ffma2_rn(p01, make_float2(zz.x, zz.y), t0);
-        t1 = __ffma2_rn(p23, make_float2(zz.z, zz.w), t1);
+        const float2 z01 = make_float2(zz.x, zz.y), z23 = make_float2(zz.z, zz.w);
+        float2 p01, p23;  // q = (q + 128) - 128, exact
+        bytes_to_floats(wsa[m], 128.0f, p01, p23);
+        a0 = __ffma2_rn(p01, z01, a0);
+        a1 = __ffma2_rn(p23, z23, a1);
+        bytes_to_floats(wsb[m], 128.0f, p01, p23);
+        b0 = __ffma2_rn(p01, z01, b0);
+        b1 = __ffma2_rn(p23, z23, b1);
       }
     }
-    const float d = __half2float(__ushort_as_half(dd[boff[u]]));
-    const float2 t = __fadd2_rn(t0, t1);
-    v[u] = __fmul_rn(d, __fadd_rn(t.x, t.y));
+    const float da = __half2float(__ushort_as_half(dsc[ja * kQ8Blocks + boff[u]]));
+    const float db = __half2float(__ushort_as_half(dsc[jb * kQ8Blocks + boff[u]]));
+    const float2 ta = __fadd2_rn(a0, a1), tb = __fadd2_rn(b0, b1);
+    va[u] = __fmul_rn(da, __fadd_rn(ta.x, ta.y));
+    vb[u] = __fmul_rn(db, __fadd_rn(tb.x, tb.y));
   }
-  return __fadd_rn(v[0], v[1]);
+  out_a = __fadd_rn(va[0], va[1]);
+  out_b = __fadd_rn(vb[0], vb[1]);
+}
+
+// The CTA's rows: a contiguous range of the padded rows, cut on multiples of
+// 4 so that every stage's runs stay 16-byte multiples; ranges differ by at
+// most 4 rows, so no CTA does a whole stage more than another.
+__device__ __forceinline__ void q8_cta_rows(long long np, long long& r_begin, long long& r_end) {
+  const long long units = np / 4;
+  r_begin = units * blockIdx.x / gridDim.x * 4;
+  r_end = units * (blockIdx.x + 1) / gridDim.x * 4;
 }
 
 __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_q8_kernel(const HeadParams p) {
@@ -513,8 +536,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_q8_kernel(const HeadP
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_rows = p.n_rows;
   const long long np = head_padded_rows(n_rows);
-  const int n_stages = (int)((np + kQ8StageRows - 1) / kQ8StageRows);
-  const int grid = gridDim.x;
+  long long r_begin, r_end;
+  q8_cta_rows(np, r_begin, r_end);
+  const int n_stages = (int)((r_end - r_begin + kQ8StageRows - 1) / kQ8StageRows);
   if (tid == 0) {
     for (int s = 0; s < kQ8Stages; ++s) {
       mbar_init(&sm.full[s], 1);
@@ -532,15 +556,15 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_q8_kernel(const HeadP
       const uint64_t pol = l2_policy_evict_first();
       int k = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < n_stages; t += grid, ++k) {
+      for (; k < n_stages; ++k) {
         const int s = k % kQ8Stages;
         if (k >= kQ8Stages &&
             !mbar_wait_bounded(&sm.empty[s], ((k / kQ8Stages) - 1) & 1, kHeadWaitBudget)) {
           ok = false;
           break;
         }
-        const long long r0 = (long long)t * kQ8StageRows;
-        const int nr = (int)min((long long)kQ8StageRows, np - r0);  // a multiple of 4
+        const long long r0 = r_begin + (long long)k * kQ8StageRows;
+        const int nr = (int)min((long long)kQ8StageRows, r_end - r0);  // a multiple of 4
         uint8_t* st = sm.stage[s];
         mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(nr * kQ8RowBytes));
         bulk_copy_g2s(st, qs + r0 * kQ8K, nr * kQ8K, &sm.full[s], pol);
@@ -614,24 +638,40 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_q8_kernel(const HeadP
   float best_v = kNoPick;
   int best_i = 0;
   bool ok = true;
-  int k = 0;
-  for (int t = blockIdx.x; t < n_stages; t += grid, ++k) {
+  const long long r_stop = min(r_end, (long long)n_rows);  // padding rows are never output
+  const int ja = 2 * warp + h, jb = ja + kQ8StageRows / 2;
+  for (int k = 0; k < n_stages; ++k) {
     const int s = k % kQ8Stages;
     if (!mbar_wait_bounded(&sm.full[s], (k / kQ8Stages) & 1, kHeadWaitBudget)) {
       ok = false;
       break;
     }
-    const int jrow = 2 * warp + h;
-    const int r = t * kQ8StageRows + jrow;
-    float acc = 0.f;
-    if (active && r < n_rows) acc = q8_row_dot(sm.stage[s], jrow, qoff, boff, z);
+    const long long r0 = r_begin + (long long)k * kQ8StageRows;
+    float acc_a = 0.f, acc_b = 0.f;
+    // (jb > ja: a half-warp whose first row is past the CTA's rows has none;
+    // the rows past a short last stage hold stale bytes and are not output)
+    if (active && r0 + ja < r_stop) q8_rows_dot(sm.stage[s], ja, jb, qoff, boff, z, acc_a, acc_b);
 #pragma unroll
-    for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (li == 0 && r < n_rows) {
-      if (p.logits) p.logits[r] = acc;
-      if (acc > best_v) {  // rows rise within a half-warp: the first maximum stays
-        best_v = acc;
-        best_i = r;
+    for (int off = 8; off > 0; off >>= 1) {
+      acc_a += __shfl_xor_sync(0xffffffffu, acc_a, off);
+      acc_b += __shfl_xor_sync(0xffffffffu, acc_b, off);
+    }
+    if (li == 0) {
+      // rows rise within a half-warp (ja < jb, stages in order): the first
+      // maximum stays
+      if (r0 + ja < r_stop) {
+        if (p.logits) p.logits[r0 + ja] = acc_a;
+        if (acc_a > best_v) {
+          best_v = acc_a;
+          best_i = (int)(r0 + ja);
+        }
+      }
+      if (r0 + jb < r_stop) {
+        if (p.logits) p.logits[r0 + jb] = acc_b;
+        if (acc_b > best_v) {
+          best_v = acc_b;
+          best_i = (int)(r0 + jb);
+        }
       }
     }
     __syncwarp();
