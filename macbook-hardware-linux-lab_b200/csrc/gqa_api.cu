@@ -65,7 +65,7 @@ cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cach
                                      Lengths len, int t_max, int n_q, int n_kv, int head_dim,
                                      int n_splits, int plan_len, const float* inv_freq,
                                      float* part_o, float* part_ml, int* status, cudaStream_t st,
-                                     bool pdl_first, bool pdl);
+                                     bool pdl_first, bool pdl, bool lengths_stable);
 size_t lm_head_packed_bytes(long long n_rows);
 size_t lm_head_q8_packed_bytes(long long n_rows);
 cudaError_t launch_q8_pack(const void* src, int n_rows, void* dst, cudaStream_t st);
@@ -319,8 +319,10 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
 
 // The decode step on the shape-generic kernels (gqa_generic.cu): split
 // partials (RoPE and the append fused), then the merge.
+// lengths_stable: pos / seq_len are not produced by the preceding kernel (see
+// split_generic_kernel).
 int run_generic(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
-                Lengths len, int plan_len, float* out, bool pdl_first) {
+                Lengths len, int plan_len, float* out, bool pdl_first, bool lengths_stable) {
   const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
   const int n_splits = generic_plan_splits(nkv, plan_len, c->n_sm);
   int rc = ensure_scratch(c, (long long)nq * n_splits, st);
@@ -328,7 +330,7 @@ int run_generic(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float
   GQA_CUDA(launch_generic_attention(qkv, out, kv->k_cache, kv->v_cache, len, c->cfg.t_max, nq,
                                     nkv, c->cfg.head_dim, n_splits, plan_len, c->inv_freq,
                                     c->part_o, c->part_ml, c->status, st, pdl_first,
-                                    c->layers_pdl != 0));
+                                    c->layers_pdl != 0, lengths_stable));
   return GQA_OK;
 }
 
@@ -363,7 +365,7 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
     // the previous layer, which never writes pos or this layer's cache.
     int rc = c->generic
                  ? run_generic(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max,
-                               out + l * out_stride, c->layers_pdl != 0)
+                               out + l * out_stride, c->layers_pdl != 0, /*lengths_stable=*/l > 0)
                  : run_single(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max, true,
                               out + l * out_stride, /*pdl_first=*/c->layers_pdl != 0,
                               /*lengths_stable=*/l > 0);
@@ -411,7 +413,8 @@ int block_impl(gqa_ctx* c, cudaStream_t st, const gqa_block_weights* w, const gq
   const int model = block_model(c);
   GQA_CUDA(launch_qkv_gemv(model, w->w_qkv, w->b_qkv, w->gamma, state, c->blk_qkv,
                            (nq + 2 * nkv) * hd, c->status, st, pdl_first));
-  int rc = c->generic ? run_generic(c, st, kv, c->blk_qkv, len, plan_len, c->blk_attn, true)
+  int rc = c->generic ? run_generic(c, st, kv, c->blk_qkv, len, plan_len, c->blk_attn, true,
+                                    lengths_stable)
                       : run_single(c, st, kv, c->blk_qkv, len, plan_len, true, c->blk_attn, true,
                                    lengths_stable);
   if (rc != GQA_OK) return rc;
@@ -695,7 +698,7 @@ int gqa_layer_attention_out(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv*
   len.pos_imm = pos;
   len.seqlen_imm = seq_len;
   if (c->generic) return run_generic(c, (cudaStream_t)stream, kv, qkv, len, seq_len, out,
-                                     c->pdl != 0);
+                                     c->pdl != 0, true);
   return run_single(c, (cudaStream_t)stream, kv, qkv, len, seq_len, true, out, c->pdl != 0,
                     true);
 }

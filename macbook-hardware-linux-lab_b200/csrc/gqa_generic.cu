@@ -8,15 +8,19 @@
 // pos, s = (q . k) * (1 / sqrt(D)) over rows t < seq_len, a stable softmax and
 // the PV product; here split over KV ranges and merged by log-sum-exp.
 //
-//   split_generic_kernel        one CTA per (split, KV head): RoPE of its KV
-//                               head's q heads into shared memory (the
+//   split_generic_kernel        one CTA per (split, KV head): its first tile's
+//                               cache rows requested (cp.async) before the
+//                               dependency wait when the step's position is
+//                               not produced by the preceding kernel -- rows
+//                               below pos are never written by it; RoPE of its
+//                               KV head's q heads into shared memory (the
 //                               caller's qkv stays as given), and on the CTA
 //                               whose range holds pos the new K (rotated) and
 //                               V rows into the caches -- the reference's
 //                               kernel_rope_and_kv_append, one thread per pair;
 //                               then its rows in tiles
 //                               of 64 staged in shared memory by coalesced
-//                               float4 loads; scores of the G heads per row
+//                               16-byte async copies; scores of the G heads per row
 //                               (thread = row x head set, float4 reads rotated
 //                               per row so a warp's 32 rows hit different banks),
 //                               a per-tile max and exp, then PV with one thread
@@ -53,6 +57,7 @@ struct GenParams {
   float* v_cache;
   Lengths len;
   int t_max, n_q, n_kv, n_splits, rows_per_split;
+  int lengths_stable;     // pos / seq_len not written by the preceding kernel
   const float* inv_freq;  // [D / 2]
   float scale;            // 1 / sqrt(D)
   float* part_o;          // [n_q][n_splits][D]
@@ -84,14 +89,40 @@ struct GenSmem {
   float m[G], corr[G];      // running max per head, rescale of this tile
 };
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
+               : "memory");
+}
+
+// Rows [tb, tb + nrow) of the KV head's K and V into the tile buffers, as
+// 16-byte async copies (one commit group; cp.async.wait_all completes it).
+template <int D, int G>
+__device__ __forceinline__ void gen_issue_tile(GenSmem<D, G>& sm, const float* kc,
+                                               const float* vc, int tb, int nrow, int tid) {
+  using S = GenShape<D, G>;
+  for (int i = tid; i < nrow * S::kChunks; i += kGenThreads) {
+    const int r = i / S::kChunks, c = i % S::kChunks;
+    cp_async16(&sm.k[r][4 * c], kc + (long long)(tb + r) * D + 4 * c);
+    cp_async16(&sm.v[r][4 * c], vc + (long long)(tb + r) * D + 4 * c);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
 template <int D, int G>
 __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenParams p) {
   using S = GenShape<D, G>;
   __shared__ __align__(16) GenSmem<D, G> sm;
-  pdl_wait();
-  pdl_launch_dependents();
+  // With stable lengths the first tile is requested before the dependency
+  // wait: the preceding kernel (the previous layer's merge, a projection, the
+  // embedding) writes neither pos nor this layer's cache, and the split that
+  // wrote row pos - 1 finished before it could start.  Row pos itself, which
+  // this kernel appends, is replaced in shared memory below.
+  const bool early = p.lengths_stable != 0;
+  if (!early) pdl_wait();
   int pos, seq_len;
   if (!gen_lengths(p, pos, seq_len)) {
+    if (early) pdl_wait();
+    pdl_launch_dependents();
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
       atomicOr(p.status, kStatusBadLength);
     return;
@@ -106,6 +137,9 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
   // The split whose range holds pos (the last one when pos lies past them
   // all) appends the new row; only it may attend that row.
   const bool owner = split == min(pos / p.rows_per_split, p.n_splits - 1);
+  if (t0 < t1) gen_issue_tile(sm, kc, vc, t0, min(kGenTile, t1 - t0), tid);
+  if (early) pdl_wait();
+  pdl_launch_dependents();
 
   // ---- RoPE: theta_i = pos * inv_freq[i], pairs (i, i + D/2); each thread
   // takes its own angles, so these loads share a round trip with the first
@@ -141,14 +175,10 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
 
   for (int tb = t0; tb < t1; tb += kGenTile) {
     const int nrow = min(kGenTile, t1 - tb);
-    // ---- stage the tile's K and V rows ----
-    for (int i = tid; i < nrow * S::kChunks; i += kGenThreads) {
-      const int r = i / S::kChunks, c = i % S::kChunks;
-      reinterpret_cast<float4*>(&sm.k[r][0])[c] =
-          __ldcs(reinterpret_cast<const float4*>(kc + (long long)(tb + r) * D) + c);
-      reinterpret_cast<float4*>(&sm.v[r][0])[c] =
-          __ldcs(reinterpret_cast<const float4*>(vc + (long long)(tb + r) * D) + c);
-    }
+    // ---- the tile's K and V rows (the first tile's were requested above;
+    // the previous tile's buffers are free after the loop's last barrier) ----
+    if (tb != t0) gen_issue_tile(sm, kc, vc, tb, nrow, tid);
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
     if (owner && pos >= tb && pos < tb + nrow) {  // the row just appended, as written
       for (int i = tid; i < D; i += kGenThreads) {
@@ -358,7 +388,7 @@ cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cach
                                      Lengths len, int t_max, int n_q, int n_kv, int head_dim,
                                      int n_splits, int plan_len, const float* inv_freq,
                                      float* part_o, float* part_ml, int* status, cudaStream_t st,
-                                     bool pdl_first, bool pdl) {
+                                     bool pdl_first, bool pdl, bool lengths_stable) {
   if (head_dim != 64 || n_q != 7 * n_kv) return cudaErrorInvalidValue;
   constexpr int D = 64, G = 7;
   GenParams p{};
@@ -375,6 +405,7 @@ cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cach
   // rows per split: whole tiles, covering plan_len rows
   const int per = (plan_len + n_splits - 1) / n_splits;
   p.rows_per_split = (per + kGenTile - 1) / kGenTile * kGenTile;
+  p.lengths_stable = lengths_stable ? 1 : 0;
   p.inv_freq = inv_freq;
   p.scale = 1.0f / sqrtf((float)D);
   p.part_o = part_o;
