@@ -412,19 +412,23 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
 // q_bj * z_32b+j.  952-byte rows start on 8-byte boundaries only, so
 // gqa_lm_head_q8_0_pack lays them out once, at load time, as two planes over
 // the rows rounded up to a multiple of 4 (Np):
-//   qs [Np][896]  codes XOR 0x80 (offset binary), reordered per row so that
-//                 block b = li + 14s (li < 14, s < 2), codes 16mq .. 16mq + 15
+//   qs [Np][896]  the int8 codes, reordered per row so that block
+//                 b = li + 14s (li < 14, s < 2), codes 16mq .. 16mq + 15
 //                 (mq < 2), sit at the 16 bytes from 16 * ((2s + mq) * 14 + li)
 //   d  [Np][28]   the fp16 scales
 // -- 952 bytes per row as before.  The kernel is the Q6_K head's pipeline with
 // stages of 64 rows (3 deep) over a contiguous, balanced row range per CTA: a
 // consumer warp takes four rows of a stage, two per half-warp, computed side by
-// side; lane li of a half owns blocks li and li + 14 (lanes 14 and 15 idle),
-// their 64 inputs held in registers for the whole kernel, and reads a block's
-// codes as two 16-byte words -- the second half-warp reads its blocks in the
-// other order, so the two halves' loads fall on different banks.  Codes become
-// exact floats by byte_perm into 2^23 + (q + 128) minus 2^23 + 128; each
-// block's sum is scaled by d once.
+// side; lane li of a half owns blocks li and li + 14 (lanes 14 and 15 idle) and
+// reads a block's codes as two 16-byte words -- the second half-warp reads its
+// blocks in the other order, so the two halves' loads fall on different banks.
+// The products are integer: once per launch each lane splits its 64
+// normalised inputs, per block of 32 with s = max|z| / 127, into three signed
+// 8-bit digits, z = s (e1 + e2 / 254 + e3 / 254^2) to about 1e-7 of max|z|;
+// per row, dp4a gives the exact int32 sums I_k = sum_j q_j e_kj, which become
+// floats exactly (|I_k| < 2^22: 2^23 + 2^22 magic), and the block's term is
+// d * s * (I_1 + I_2 / 254 + I_3 / 254^2): three dp4a per 4 weights instead of
+// four byte_perm, two f32x2 adds and two f32x2 FMAs.
 // ---------------------------------------------------------------------------
 constexpr int kQ8K = 896;
 constexpr int kQ8Blocks = kQ8K / 32;                   // 28
@@ -442,6 +446,11 @@ static_assert(kQ8StQs % 16 == 0 && kQ8StageBytes % 16 == 0 && (4 * kQ8DRow) % 16
 struct Q8Smem {
   alignas(128) uint8_t stage[kQ8Stages][kQ8StageBytes];
   alignas(16) float sz[kQ8K];
+  // the inputs' digits: word (k, mq, b, m4) packs digit k of inputs
+  // 16mq + 4m4 .. + 3 of block b -- a lane's four words of one (k, mq) are one
+  // 16-byte load, the 14 lanes of a half-warp on consecutive ones
+  alignas(16) uint32_t dig[3][2][kQ8Blocks][4];
+  float bscale[kQ8Blocks], binv[kQ8Blocks];
   float red[kHeadConsumerWarps];
   HeadBest best[kHeadConsumerWarps];
   uint64_t full[kQ8Stages];
@@ -468,54 +477,62 @@ __global__ void q8_pack_kernel(const uint8_t* __restrict__ src, int n_rows,
     } else {
       const int j = o - 2, sl = b / kQ8Lanes, li = b % kQ8Lanes;
       const int at = 16 * ((2 * sl + (j >> 4)) * kQ8Lanes + li) + (j & 15);
-      qs[at] = r < n_rows ? (uint8_t)(src[r * kQ8RowBytes + i] ^ 0x80) : (uint8_t)0x80;
+      qs[at] = r < n_rows ? src[r * kQ8RowBytes + i] : (uint8_t)0;
     }
   }
 }
 
+// Exact float of an int32 below 2^22 in magnitude: 2^23 + 2^22 + i as bits,
+// minus the same.
+__device__ __forceinline__ float small_int_to_float(int i) {
+  return __fsub_rn(__int_as_float(0x4B400000 + i), 12582912.0f);
+}
+
 // Rows ja and jb of a stage, lane's part: blocks b_u = li + 14 (u ^ h) for
-// u = 0, 1.  z[u][m] holds the inputs of codes 4m .. 4m + 3 of block b_u,
-// shared by both rows; the two rows' chains are independent, which is what
-// keeps the lane's pipes busy.  The second half-warp visits the lane's two
-// blocks in the other order, so each block's term is rounded on its own and
-// the pair is summed with a plain (commutative) add: a row's logit does not
-// depend on which half-warp computes it, and equal rows give equal logits for
-// the tie rule.
+// u = 0, 1.  e[u][k][m] packs the k-th digits of the inputs of codes
+// 4m .. 4m + 3 of block b_u (four int8), s[u] the block's digit scale; both
+// rows use them, and their chains are independent.  The second half-warp
+// visits the lane's two blocks in the other order, so each block's term is
+// rounded on its own and the pair summed with a plain (commutative) add: a
+// row's logit does not depend on which half-warp computes it, and equal rows
+// give equal logits for the tie rule.
 __device__ __forceinline__ void q8_rows_dot(const uint8_t* sb, int ja, int jb,
                                             const int (&qoff)[2], const int (&boff)[2],
-                                            const float4 (&z)[2][8], float& out_a,
-                                            float& out_b) {
+                                            const int (&e)[2][3][8], const float (&s)[2],
+                                            float& out_a, float& out_b) {
   const uint8_t* qa = sb + ja * kQ8K;
   const uint8_t* qb = sb + jb * kQ8K;
   const unsigned short* dsc = reinterpret_cast<const unsigned short*>(sb + kQ8StQs);
   float va[2], vb[2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
-    float2 a0 = make_float2(0.f, 0.f), a1 = a0, b0 = a0, b1 = a0;
+    int a1 = 0, a2 = 0, a3 = 0, b1 = 0, b2 = 0, b3 = 0;
 #pragma unroll
     for (int mq = 0; mq < 2; ++mq) {
       const uint4 wa = *reinterpret_cast<const uint4*>(qa + qoff[u] + 16 * kQ8Lanes * mq);
       const uint4 wb = *reinterpret_cast<const uint4*>(qb + qoff[u] + 16 * kQ8Lanes * mq);
-      const uint32_t wsa[4] = {wa.x, wa.y, wa.z, wa.w};
-      const uint32_t wsb[4] = {wb.x, wb.y, wb.z, wb.w};
+      const int wsa[4] = {(int)wa.x, (int)wa.y, (int)wa.z, (int)wa.w};
+      const int wsb[4] = {(int)wb.x, (int)wb.y, (int)wb.z, (int)wb.w};
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        const float4 zz = z[u][4 * mq + m];
-        const float2 z01 = make_float2(zz.x, zz.y), z23 = make_float2(zz.z, zz.w);
-        float2 p01, p23;  // q = (q + 128) - 128, exact
-        bytes_to_floats(wsa[m], 128.0f, p01, p23);
-        a0 = __ffma2_rn(p01, z01, a0);
-        a1 = __ffma2_rn(p23, z23, a1);
-        bytes_to_floats(wsb[m], 128.0f, p01, p23);
-        b0 = __ffma2_rn(p01, z01, b0);
-        b1 = __ffma2_rn(p23, z23, b1);
+        const int k = 4 * mq + m;
+        a1 = __dp4a(wsa[m], e[u][0][k], a1);
+        a2 = __dp4a(wsa[m], e[u][1][k], a2);
+        a3 = __dp4a(wsa[m], e[u][2][k], a3);
+        b1 = __dp4a(wsb[m], e[u][0][k], b1);
+        b2 = __dp4a(wsb[m], e[u][1][k], b2);
+        b3 = __dp4a(wsb[m], e[u][2][k], b3);
       }
     }
+    constexpr float kD1 = 1.0f / 254.0f, kD2 = 1.0f / 64516.0f;
+    const float fa = __fmaf_rn(small_int_to_float(a3), kD2,
+                               __fmaf_rn(small_int_to_float(a2), kD1, small_int_to_float(a1)));
+    const float fb = __fmaf_rn(small_int_to_float(b3), kD2,
+                               __fmaf_rn(small_int_to_float(b2), kD1, small_int_to_float(b1)));
     const float da = __half2float(__ushort_as_half(dsc[ja * kQ8Blocks + boff[u]]));
     const float db = __half2float(__ushort_as_half(dsc[jb * kQ8Blocks + boff[u]]));
-    const float2 ta = __fadd2_rn(a0, a1), tb = __fadd2_rn(b0, b1);
-    va[u] = __fmul_rn(da, __fadd_rn(ta.x, ta.y));
-    vb[u] = __fmul_rn(db, __fadd_rn(tb.x, tb.y));
+    va[u] = __fmul_rn(__fmul_rn(da, s[u]), fa);
+    vb[u] = __fmul_rn(__fmul_rn(db, s[u]), fb);
   }
   out_a = __fadd_rn(va[0], va[1]);
   out_b = __fadd_rn(vb[0], vb[1]);
@@ -619,20 +636,67 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_q8_kernel(const HeadP
     if (in_range(k)) sm.sz[tid + k * kHeadConsumers] = xv[k] * scale * gm[k];
   consumers_sync();
 
+  // ---- the inputs as three 8-bit digits per block of 32:
+  // z = s (e1 + e2 / 254 + e3 / 254^2), s = max|z| / 127 ----
+  for (int b = warp; b < kQ8Blocks; b += kHeadConsumerWarps) {
+    float mx = fabsf(sm.sz[32 * b + lane]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) {
+      sm.bscale[b] = mx / 127.0f;
+      sm.binv[b] = mx > 0.f ? 127.0f / mx : 0.f;
+    }
+  }
+  consumers_sync();
+  if (tid < kQ8K / 4) {  // one word of four inputs per thread
+    const int b = tid >> 3, m = tid & 7;
+    const float4 zz = *reinterpret_cast<const float4*>(sm.sz + 4 * tid);
+    const float inv = sm.binv[b];
+    const float xs[4] = {zz.x * inv, zz.y * inv, zz.z * inv, zz.w * inv};
+    uint32_t by[3][4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      // round to nearest by 1.5 * 2^23 (|x| <= 127): the sum's low byte is the
+      // digit, the difference its value
+      constexpr float kMagic = 12582912.0f;
+      const float t1 = __fadd_rn(xs[c], kMagic);
+      const float r1 = __fmul_rn(__fsub_rn(xs[c], __fsub_rn(t1, kMagic)), 254.0f);
+      const float t2 = __fadd_rn(r1, kMagic);
+      const float r2 = __fmul_rn(__fsub_rn(r1, __fsub_rn(t2, kMagic)), 254.0f);
+      const float t3 = __fadd_rn(r2, kMagic);
+      by[0][c] = __float_as_uint(t1);
+      by[1][c] = __float_as_uint(t2);
+      by[2][c] = __float_as_uint(t3);
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      sm.dig[k][m >> 2][b][m & 3] = __byte_perm(__byte_perm(by[k][0], by[k][1], 0x0040),
+                                                __byte_perm(by[k][2], by[k][3], 0x0040), 0x5410);
+  }
+  consumers_sync();
+
   const int h = lane >> 4, li = lane & 15;
   const bool active = li < kQ8Lanes;
   int qoff[2], boff[2];
-  float4 z[2][8];
+  int e[2][3][8];  // the lane's inputs as three 8-bit digits, four per word
+  float sc[2];     // their scale per block
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const int sl = u ^ h;
     const int b = active ? li + kQ8Lanes * sl : 0;
     qoff[u] = 16 * (2 * sl * kQ8Lanes + (active ? li : 0));
     boff[u] = b;
+    sc[u] = sm.bscale[b];
 #pragma unroll
-    for (int m = 0; m < 8; ++m)
-      z[u][m] = active ? *reinterpret_cast<const float4*>(sm.sz + 32 * b + 4 * m)
-                       : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < 3; ++k)
+#pragma unroll
+      for (int mq = 0; mq < 2; ++mq) {
+        const uint4 w = *reinterpret_cast<const uint4*>(&sm.dig[k][mq][b][0]);
+        e[u][k][4 * mq + 0] = (int)w.x;
+        e[u][k][4 * mq + 1] = (int)w.y;
+        e[u][k][4 * mq + 2] = (int)w.z;
+        e[u][k][4 * mq + 3] = (int)w.w;
+      }
   }
 
   float best_v = kNoPick;
@@ -650,7 +714,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_q8_kernel(const HeadP
     float acc_a = 0.f, acc_b = 0.f;
     // (jb > ja: a half-warp whose first row is past the CTA's rows has none;
     // the rows past a short last stage hold stale bytes and are not output)
-    if (active && r0 + ja < r_stop) q8_rows_dot(sm.stage[s], ja, jb, qoff, boff, z, acc_a, acc_b);
+    if (active && r0 + ja < r_stop) q8_rows_dot(sm.stage[s], ja, jb, qoff, boff, e, sc, acc_a, acc_b);
 #pragma unroll
     for (int off = 8; off > 0; off >>= 1) {
       acc_a += __shfl_xor_sync(0xffffffffu, acc_a, off);

@@ -230,14 +230,13 @@ def q8_0_dequant(blocks: np.ndarray, rows: int, cols: int = 896) -> np.ndarray:
 def q8_0_planes(blocks: np.ndarray, rows: int) -> np.ndarray:
     """The byte layout gqa_lm_head_q8_0_pack writes for 896-wide rows, over the
     rows rounded up to a multiple of 4: codes [Np][896] then scales [Np][28]
-    (fp16).  In a row, the codes of block b = li + 14 s (li < 14, s < 2), 16
-    at a time (half mq < 2), sit at byte 16 ((2s + mq) 14 + li) XOR-ed with
-    0x80; padding rows hold code 0x80 and scale 0."""
+    (fp16).  In a row, the int8 codes of block b = li + 14 s (li < 14, s < 2),
+    16 at a time (half mq < 2), sit at byte 16 ((2s + mq) 14 + li); padding rows
+    hold code 0 and scale 0."""
     np_rows = (rows + 3) // 4 * 4
     b = np.zeros((np_rows, 28, Q8_0_BLOCK_BYTES), dtype=np.uint8)
     b[:rows] = np.asarray(blocks, dtype=np.uint8).reshape(rows, 28, Q8_0_BLOCK_BYTES)
-    q = b[:, :, 2:] ^ np.uint8(0x80)                          # [row][b][32]
-    q[rows:] = 0x80
+    q = b[:, :, 2:]                                            # [row][b][32]
     q = q.reshape(np_rows, 2, 14, 2, 16).transpose(0, 1, 3, 2, 4)  # [row][s][mq][li][16]
     return np.concatenate([np.ascontiguousarray(q).reshape(-1), b[:, :, 0:2].reshape(-1)])
 

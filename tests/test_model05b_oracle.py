@@ -80,9 +80,9 @@ def test_q8_0_planes_layout(pkg):
         for mq in range(2):
             at = 16 * ((2 * s + mq) * 14 + li)
             dense[:, 32 * b + 16 * mq:32 * b + 16 * mq + 16] = \
-                (qs[:, at:at + 16].astype(np.int32) - 128) * d[:, b:b + 1].astype(np.float32)
+                qs[:, at:at + 16].view(np.int8).astype(np.float32) * d[:, b:b + 1].astype(np.float32)
     assert np.array_equal(dense[:n], S.q8_0_dequant(w, n))
-    assert (qs[n:] == 0x80).all() and (d[n:] == 0).all()
+    assert (qs[n:] == 0).all() and (d[n:] == 0).all()
 
 
 def test_gguf_05b_file(pkg, orc, tmp_path):
