@@ -47,6 +47,36 @@ def test_layer_attention_05b(pkg, orc, cuda, pos, seq_len):
         assert np.array_equal(d_qkv[NQ * D:].cpu().numpy(), qkv[NQ * D:])
 
 
+def test_token_by_token_with_pdl_05b(pkg, orc, cuda):
+    """Single layer calls one token after another on one cache with
+    programmatic dependent launch on: each call's split kernel requests its
+    first cache rows before its dependency wait, and must still see the row
+    the previous call appended (the prompt walk of generate_stream_05b.c:
+    744-753, one layer)."""
+    torch = cuda
+    pos0, n_tok = 190, 6   # crosses the 64-row tile and split boundary at 192
+    _, kc, vc = _inputs(pkg, 7300)
+    rows = [pkg.seeded.normal(7301 + t, pkg.seeded.QKV, (NQ + 2 * NKV) * D) for t in range(n_tok)]
+    rk, rv = kc.copy(), vc.copy()
+    want = []
+    for t, row in enumerate(rows):
+        r = row.copy()
+        orc.layer_attention(r, rk, rv, pos0 + t, pos0 + t + 1, n_heads_q=NQ, n_heads_kv=NKV,
+                            head_dim=D)
+        want.append(r[:NQ * D].copy())
+    with pkg.Context(n_heads_q=NQ, n_heads_kv=NKV, head_dim=D, t_max=T_MAX) as ctx:
+        ctx.set_option(pkg.gqa.GQA_OPT_PDL, 1)
+        k, v = torch.from_numpy(kc.copy()).cuda(), torch.from_numpy(vc.copy()).cuda()
+        bufs = [torch.from_numpy(r.copy()).cuda() for r in rows]
+        for t in range(n_tok):  # queued back to back, no host synchronisation
+            ctx.layer_attention(pkg.kv_of(k, v), bufs[t], pos0 + t, pos0 + t + 1)
+        torch.cuda.synchronize()
+        assert ctx.device_status() == 0
+        for t in range(n_tok):
+            assert nerr(bufs[t][:NQ * D].cpu().numpy(), want[t]) <= TOL
+        assert np.array_equal(v[:, pos0:pos0 + n_tok].cpu().numpy(), rv[:, pos0:pos0 + n_tok])
+
+
 def test_decode_layers_graph_05b(pkg, orc, cuda):
     """Three layers per step, position on the device, two steps; the second
     from a graph replay; the layer inputs stay unrotated between replays."""
