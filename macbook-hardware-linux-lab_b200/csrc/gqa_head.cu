@@ -28,9 +28,10 @@
 // bytes [8hh, 8hh + 8); within its ql bytes the two 32-byte halves (quarters
 // 0/2 and 1/3) are swapped when hh & 2, so that the warp's loads below hit 32
 // different shared-memory banks, and its scale bytes are reordered so that
-// scales[8n + 2c + g] sits at 8hh + 4g + c, XOR-ed with 0x80 (offset binary):
-// a lane's four scales are one 32-bit word.  Any run of rows starting on a
-// multiple of 4 is then four 16-byte-aligned runs of bytes.
+// scales[8n + 2c + g] sits at 8hh + 4g + c: a lane's four scales are one
+// 32-bit word; the qh bytes are stored XOR 0xAA (the high bit of each 2-bit
+// field flipped), so that an assembled code byte is code ^ 32.  Any run of rows
+// starting on a multiple of 4 is then four 16-byte-aligned runs of bytes.
 //
 // The head kernel is a bulk-copy pipeline: one CTA per SM, a producer warp
 // that copies stages of 16 rows (the four planes' runs, 20160 bytes) into an
@@ -40,11 +41,18 @@
 // round-robin.  Lane (hh0 = lane / 8, q = lane % 8) owns, in every row, the
 // three 16-weight units hh = hh0 + 4u (u = 0, 1, 2), l = 4q .. 4q + 3, all
 // four quarters: the units' 48 inputs stay in registers for the whole kernel.
-// Per unit the lane reads two ql words, one qh word, the half's 8 scale bytes
-// and d; four code words (one byte per weight) come from AND/OR steps; each
-// code becomes an exact float by byte_perm into 2^23 + code minus 2^23 + 32,
-// each scale likewise (2^23 + (scale ^ 0x80) minus 2^23 + 128, no int-to-float
-// unit), and the products run as f32x2 pairs.
+// Per unit the lane reads two ql words, one qh word, its four scale bytes and
+// d; four code words (one byte per weight, 0..63) come from AND/OR steps.  The
+// products are integer: once per launch the CTA splits each unit's 16
+// normalised inputs, with a power-of-two scale s >= max|z| / 63, into three
+// signed digits in [-63, 63], z = s (e1 + e2 / 126 + e3 / 126^2); per row, the
+// code bytes become code - 32 as signed bytes (y = code ^ 32 from the packed qh,
+// plus 6 (y & 32): two instructions per word), dp4a against the digit words
+// gives exact int32 sums, the quarters' int8 scales combine them exactly
+// (|K| < 2^22), and the unit's term
+// is (d s) (K1 + K2 / 126 + K3 / 126^2).  With z = 32 e_i (a power of two) the
+// digits are exact and a logit is d * (scale * (code - 32) * 32) with one
+// rounding, as in the reference's order (d * scale is exact).
 #include <cuda_fp16.h>
 
 #include "gqa_common.cuh"
@@ -82,9 +90,16 @@ struct HeadBest {
   int i;
 };
 
+constexpr int kHeadUnits = kHeadK / 16;  // 16-weight units of a row (96)
+
 struct HeadSmem {
   alignas(128) uint8_t stage[kHeadStages][kStageBytes];
   alignas(16) float sz[kHeadK];
+  // the inputs' digits: word (k, unit, c) packs digit k of the unit's four
+  // inputs of quarter c; a lane's four quarters of a (k, unit) are one
+  // 16-byte load, consecutive units on consecutive lanes
+  alignas(16) uint32_t dig[3][kHeadUnits][4];
+  float uscale[kHeadUnits];
   float red[kHeadConsumerWarps];
   HeadBest best[kHeadConsumerWarps];
   uint64_t full[kHeadStages];
@@ -131,11 +146,12 @@ __global__ void q6k_pack_kernel(const uint8_t* __restrict__ src, int n_rows,
       const int hh = 2 * s + (o >> 6), b = o & 63;
       ql[64 * hh + (b ^ ((hh & 2) ? 32 : 0))] = v;
     } else if (o < 192) {
-      qh[64 * s + (o - 128)] = v;
+      // the high bit of each 2-bit field flipped: assembled codes are code ^ 32
+      qh[64 * s + (o - 128)] = r < n_rows ? (uint8_t)(v ^ 0xAA) : (uint8_t)0;
     } else if (o < 208) {
-      // scales[8n + 2c + g] -> byte 8hh + 4g + c, stored as scale ^ 0x80
+      // scales[8n + 2c + g] -> byte 8hh + 4g + c
       const int j = o - 192, n = j >> 3, c = (j & 7) >> 1, g = j & 1;
-      sc[8 * (2 * s + n) + 4 * g + c] = v ^ 0x80;
+      sc[8 * (2 * s + n) + 4 * g + c] = v;
     } else {
       dd[2 * s + (o - 208)] = v;
     }
@@ -145,10 +161,6 @@ __global__ void q6k_pack_kernel(const uint8_t* __restrict__ src, int n_rows,
 // ---------------------------------------------------------------------------
 // Output RMSNorm + Q6_K LM head + greedy pick
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float magic_f(uint32_t w, uint32_t sel) {
-  return __uint_as_float(__byte_perm(w, 0x4B00u, sel));
-}
-
 __device__ __forceinline__ void head_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
@@ -214,22 +226,24 @@ struct LaneConst {
   int g;                // which 16 of the 32 l values: scale word 2hh + g
 };
 
-// Exact floats of the four bytes of w minus `off`: 2^23 + byte through
-// byte_perm, then one f32x2 subtraction per pair.  (An fp16 form -- 1024 +
-// byte, two bytes per byte_perm, widened with the subtraction -- halves the
-// byte_perm count but measured slower on B200: 59.4 against 55.5 us per
-// head, the widening moving the load onto the FMA pipe.)
-__device__ __forceinline__ void bytes_to_floats(uint32_t w, float off, float2& p01, float2& p23) {
-  const float2 o = make_float2(-(8388608.0f + off), -(8388608.0f + off));
-  p01 = __fadd2_rn(make_float2(magic_f(w, 0x5440u), magic_f(w, 0x5441u)), o);
-  p23 = __fadd2_rn(make_float2(magic_f(w, 0x5442u), magic_f(w, 0x5443u)), o);
+// Exact float of an int32 below 2^22 in magnitude: 2^23 + 2^22 + i as bits,
+// minus the same.
+__device__ __forceinline__ float small_int_to_float(int i) {
+  return __fsub_rn(__int_as_float(0x4B400000 + i), 12582912.0f);
 }
 
+// The lane's inputs as digits (see the file comment): for unit u, quarter c
+// and digit k, e[u][c][k] packs the digits of weights 4q .. 4q + 3; s[u] is
+// the unit's power-of-two scale.
+struct LaneDigits {
+  int e[3][4][3];
+  float s[3];
+};
+
 // Dot product of one row held in a stage with the lane's inputs (lane's
-// partial sum; the caller reduces over the warp).  x[u][c] holds the inputs
-// of weights 4q .. 4q + 3 of unit u, quarter c, as two pairs.
+// partial sum; the caller reduces over the warp).
 __device__ __forceinline__ float row_dot(const uint8_t* sb, int j, const LaneConst& lc,
-                                         const float2 (&x)[3][4][2]) {
+                                         const LaneDigits& x) {
   const uint32_t* qlw = reinterpret_cast<const uint32_t*>(sb) + j * (kQlRow / 4);
   const uint32_t* qhw = reinterpret_cast<const uint32_t*>(sb + kStQl) + j * (kQhRow / 4);
   const uint32_t* scw = reinterpret_cast<const uint32_t*>(sb + kStQl + kStQh) + j * (kScRow / 4);
@@ -243,24 +257,31 @@ __device__ __forceinline__ float row_dot(const uint8_t* sb, int j, const LaneCon
     const uint32_t H = qhw[8 * hh + lc.q];
     const uint32_t sv = scw[2 * hh + lc.g];
     const float d = __half2float(__ushort_as_half(dw[hh >> 1]));
-    // byte e of Q[c] = 6-bit code of weight (quarter c, l = 4q + e)
+    // byte e of Q[c] = (6-bit code of weight (quarter c, l = 4q + e)) ^ 32
     uint32_t Q[4];
     Q[0] = (W0 & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
     Q[1] = (W1 & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
     Q[2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
     Q[3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
-    float2 sc01, sc23;  // the quarters' scales (stored offset by 128)
-    bytes_to_floats(sv, 128.0f, sc01, sc23);
-    const float scs[4] = {sc01.x, sc01.y, sc23.x, sc23.y};
-    float2 t = make_float2(0.f, 0.f);
+    int K[3] = {0, 0, 0};
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      float2 w01, w23;  // code - 32
-      bytes_to_floats(Q[c], 32.0f, w01, w23);
-      const float2 a = __ffma2_rn(w23, x[u][c][1], __fmul2_rn(w01, x[u][c][0]));
-      t = __ffma2_rn(a, make_float2(scs[c], scs[c]), t);
+      // code - 32 as a signed byte: y when y < 32, y - 64 (= y | 0xC0) otherwise
+      const int v = (int)((Q[c] & 0x20202020u) * 6u + Q[c]);
+      // the quarter's int8 scale, sign-extended: PTX prmt replicates the
+      // selected byte's sign bit when bit 3 of a selector nibble is set (the
+      // __byte_perm intrinsic reads only bits 0-2 of each nibble)
+      int sc;
+      asm("prmt.b32 %0, %1, 0, %2;"
+          : "=r"(sc)
+          : "r"(sv), "r"(c | (8 + c) << 4 | (8 + c) << 8 | (8 + c) << 12));
+#pragma unroll
+      for (int k = 0; k < 3; ++k) K[k] += sc * __dp4a(v, x.e[u][c][k], 0);
     }
-    acc = fmaf(d, t.x + t.y, acc);
+    constexpr float kB1 = 1.0f / 126.0f, kB2 = 1.0f / 15876.0f;
+    const float f = __fmaf_rn(small_int_to_float(K[2]), kB2,
+                              __fmaf_rn(small_int_to_float(K[1]), kB1, small_int_to_float(K[0])));
+    acc = __fmaf_rn(__fmul_rn(d, x.s[u]), f, acc);
   }
   return acc;
 }
@@ -356,22 +377,65 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
   for (int k = 0; k < kPer; ++k) sm.sz[tid + k * kHeadConsumers] = xv[k] * scale * gm[k];
   consumers_sync();
 
+  // ---- the inputs as digits, one word (unit, quarter) per thread: unit
+  // (hh, q) holds inputs 128hh + 32c + 4q + e, c, e < 4 ----
+  if (tid < kHeadUnits * 4) {
+    const int unit = tid >> 2, c = tid & 3, hh = unit >> 3, q = unit & 7;
+    const float4 zz = *reinterpret_cast<const float4*>(sm.sz + 128 * hh + 32 * c + 4 * q);
+    float mx = fmaxf(fmaxf(fabsf(zz.x), fabsf(zz.y)), fmaxf(fabsf(zz.z), fabsf(zz.w)));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // the unit's four words are
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));  // four consecutive lanes
+    // s = the smallest power of two >= mx / 63 (1 when the unit is all zero)
+    const uint32_t mb = __float_as_uint(mx / 63.0f);
+    const uint32_t sb = (mb & 0x007FFFFFu) ? (mb & 0x7F800000u) + 0x00800000u : mb;
+    const float sunit = mx > 0.f ? __uint_as_float(sb) : 1.0f;
+    const float inv = __frcp_rn(sunit);  // exact: a power of two
+    const float xs[4] = {zz.x * inv, zz.y * inv, zz.z * inv, zz.w * inv};
+    uint32_t by[3][4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      // round to nearest by 1.5 * 2^23 (|x| <= 63): the sum's low byte is the
+      // digit, the difference its value
+      constexpr float kMagic = 12582912.0f;
+      const float t1 = __fadd_rn(xs[e], kMagic);
+      const float d1 = __fsub_rn(t1, kMagic);
+      const float r1 = __fmul_rn(__fsub_rn(xs[e], d1), 126.0f);
+      const float t2 = __fadd_rn(r1, kMagic);
+      const float d2 = __fsub_rn(t2, kMagic);
+      const float r2 = __fmul_rn(__fsub_rn(r1, d2), 126.0f);
+      const float t3 = __fadd_rn(r2, kMagic);
+      by[0][e] = __float_as_uint(t1);
+      by[1][e] = __float_as_uint(t2);
+      by[2][e] = __float_as_uint(t3);
+    }
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      sm.dig[k][unit][c] = __byte_perm(__byte_perm(by[k][0], by[k][1], 0x0040),
+                                       __byte_perm(by[k][2], by[k][3], 0x0040), 0x5410);
+    if (c == 0) sm.uscale[unit] = sunit;
+  }
+  consumers_sync();
+
   LaneConst lc;
   lc.hh0 = lane >> 3;
   lc.q = lane & 7;
   lc.o0 = (lc.hh0 & 2) ? 8 : 0;  // the pack swapped the halves of these units
   lc.o1 = 8 - lc.o0;
   lc.g = (lane & 7) >> 2;
-  float2 x[3][4][2];
+  LaneDigits x;
 #pragma unroll
-  for (int u = 0; u < 3; ++u)
+  for (int u = 0; u < 3; ++u) {
+    const int unit = 8 * (lc.hh0 + 4 * u) + lc.q;  // = lane + 32u: consecutive per lane
+    x.s[u] = sm.uscale[unit];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const float4 v =
-          *reinterpret_cast<const float4*>(sm.sz + 128 * (lc.hh0 + 4 * u) + 32 * c + 4 * lc.q);
-      x[u][c][0] = make_float2(v.x, v.y);
-      x[u][c][1] = make_float2(v.z, v.w);
+    for (int k = 0; k < 3; ++k) {
+      const uint4 w = *reinterpret_cast<const uint4*>(&sm.dig[k][unit][0]);
+      x.e[u][0][k] = (int)w.x;
+      x.e[u][1][k] = (int)w.y;
+      x.e[u][2][k] = (int)w.z;
+      x.e[u][3][k] = (int)w.w;
     }
+  }
 
   float best_v = kNoPick;
   int best_i = 0;
@@ -480,12 +544,6 @@ __global__ void q8_pack_kernel(const uint8_t* __restrict__ src, int n_rows,
       qs[at] = r < n_rows ? src[r * kQ8RowBytes + i] : (uint8_t)0;
     }
   }
-}
-
-// Exact float of an int32 below 2^22 in magnitude: 2^23 + 2^22 + i as bits,
-// minus the same.
-__device__ __forceinline__ float small_int_to_float(int i) {
-  return __fsub_rn(__int_as_float(0x4B400000 + i), 12582912.0f);
 }
 
 // Rows ja and jb of a stage, lane's part: blocks b_u = li + 14 (u ^ h) for

@@ -186,8 +186,10 @@ def q6_k_planes(blocks: np.ndarray, rows: int) -> np.ndarray:
     multiple of 4 (padding rows zero): ql [Np][768], qh [Np][384], scales
     [Np][96], d [Np][12], superblock order kept within each plane, except that
     the two 32-byte halves of half-superblock hh's 64 ql bytes are swapped
-    when hh & 2, and that scales[8n + 2c + g] of a superblock moves to byte
-    8hh + 4g + c of the row (hh = 2 * superblock + n) as scale ^ 0x80."""
+    when hh & 2, that scales[8n + 2c + g] of a superblock moves to byte
+    8hh + 4g + c of the row (hh = 2 * superblock + n), and that the qh bytes
+    of real rows are stored XOR 0xAA (the high bit of each 2-bit field
+    flipped)."""
     np_rows = (rows + 3) // 4 * 4
     b = np.zeros((np_rows, 6, Q6_K_BLOCK_BYTES), dtype=np.uint8)
     b[:rows] = np.asarray(blocks, dtype=np.uint8).reshape(rows, 6, Q6_K_BLOCK_BYTES)
@@ -195,9 +197,10 @@ def q6_k_planes(blocks: np.ndarray, rows: int) -> np.ndarray:
     swap = (np.arange(12) & 2) != 0
     ql[:, swap] = ql[:, swap][:, :, ::-1]
     sc = b[:, :, 192:208].reshape(np_rows, 6, 2, 4, 2)  # [row][sb][n][c][g]
-    sc = (sc.transpose(0, 1, 2, 4, 3) ^ np.uint8(0x80))      # [row][sb][n][g][c]
-    sc[rows:] = 0
-    return np.concatenate([ql.reshape(-1), b[:, :, 128:192].reshape(-1),
+    sc = np.ascontiguousarray(sc.transpose(0, 1, 2, 4, 3))   # [row][sb][n][g][c]
+    qh = b[:, :, 128:192].copy()
+    qh[:rows] ^= np.uint8(0xAA)
+    return np.concatenate([ql.reshape(-1), qh.reshape(-1),
                            sc.reshape(-1), b[:, :, 208:].reshape(-1)])
 
 

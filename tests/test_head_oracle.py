@@ -108,8 +108,8 @@ def test_greedy_pick_rules(orc):
 
 def test_planes_layout(pkg):
     """Planes over 4 rows (3 real + 1 zero padding row); ql halves of the
-    half-superblocks hh with hh & 2 swapped; scales regrouped per (hh, g) and
-    stored offset by 128."""
+    half-superblocks hh with hh & 2 swapped; qh bytes XOR 0xAA; scales
+    regrouped per (hh, g)."""
     w = pkg.seeded.q6_k_matrix(25, pkg.seeded.W_HEAD, 3)
     p = pkg.seeded.q6_k_planes(w, 3)
     n = 4
@@ -121,12 +121,12 @@ def test_planes_layout(pkg):
         want = np.concatenate([src[32:], src[:32]]) if hh & 2 else src
         assert np.array_equal(row0_ql[hh], want), hh
     assert not p[3 * 768:4 * 768].any()                                   # padding row
-    assert np.array_equal(p[n * 768 + 384:n * 768 + 768], b[1, :, 128:192].reshape(-1))
+    assert np.array_equal(p[n * 768 + 384:n * 768 + 768], b[1, :, 128:192].reshape(-1) ^ 0xAA)
     sc_row2 = p[n * 1152 + 96 * 2:n * 1152 + 96 * 3].reshape(12, 2, 4)  # [hh][g][c]
     for hh in range(12):
         for g in range(2):
             for c in range(4):
-                want = b[2, hh // 2, 192 + 8 * (hh % 2) + 2 * c + g] ^ 0x80
+                want = b[2, hh // 2, 192 + 8 * (hh % 2) + 2 * c + g]
                 assert sc_row2[hh, g, c] == want
     assert not p[n * 1152 + 96 * 3:n * 1152 + 96 * 4].any()             # padding row
     assert np.array_equal(p[n * 1248:n * 1248 + 12], b[0, :, 208:].reshape(-1))
