@@ -87,6 +87,7 @@ struct GenSmem {
   float v[kGenTile][D];
   float s[G][kGenTile];     // scores, then weights e^(s - m)
   float m[G], corr[G];      // running max per head, rescale of this tile
+  float l[G];               // running sum of the weights per head
 };
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -168,8 +169,11 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
     sm.vnew[tid] = v0;
     sm.vnew[tid + H] = v1;
   }
-  if (tid < G) sm.m[tid] = -CUDART_INF_F;
-  float o[S::kOutPerThread], l_run = 0.f;  // l_run: thread tid < G holds head tid's l
+  if (tid < G) {
+    sm.m[tid] = -CUDART_INF_F;
+    sm.l[tid] = 0.f;
+  }
+  float o[S::kOutPerThread];
 #pragma unroll
   for (int k = 0; k < S::kOutPerThread; ++k) o[k] = 0.f;
 
@@ -234,20 +238,30 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
       sm.s[g][r] = sv == -CUDART_INF_F ? 0.f : expf(sv - sm.m[g]);
     }
     __syncthreads();
-    // ---- l and PV: thread owns outputs tid + k * kGenThreads = (g, d) ----
-    if (tid < G) {
-      float ls = 0.f;
-      for (int r = 0; r < nrow; ++r) ls += sm.s[tid][r];
-      l_run = l_run * sm.corr[tid] + ls;
+    // ---- l: warp g sums head g's weights (rows past nrow weigh 0) ----
+    for (int g = warp; g < G; g += kGenThreads / 32) {
+      float ls = sm.s[g][lane] + sm.s[g][lane + 32];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+      if (lane == 0) sm.l[g] = sm.l[g] * sm.corr[g] + ls;
     }
+    // ---- PV: thread owns outputs tid + k * kGenThreads = (g, d); four
+    // independent chains over the rows ----
 #pragma unroll
     for (int k = 0; k < S::kOutPerThread; ++k) {
       const int idx = tid + k * kGenThreads;
       if (idx < S::kOut) {
         const int g = idx / D, d = idx % D;
-        float acc = o[k] * sm.corr[g];
-        for (int r = 0; r < nrow; ++r) acc = fmaf(sm.s[g][r], sm.v[r][d], acc);
-        o[k] = acc;
+        float a0 = o[k] * sm.corr[g], a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int r = 0;
+        for (; r + 4 <= nrow; r += 4) {
+          a0 = fmaf(sm.s[g][r], sm.v[r][d], a0);
+          a1 = fmaf(sm.s[g][r + 1], sm.v[r + 1][d], a1);
+          a2 = fmaf(sm.s[g][r + 2], sm.v[r + 2][d], a2);
+          a3 = fmaf(sm.s[g][r + 3], sm.v[r + 3][d], a3);
+        }
+        for (; r < nrow; ++r) a0 = fmaf(sm.s[g][r], sm.v[r][d], a0);
+        o[k] = (a0 + a1) + (a2 + a3);
       }
     }
     __syncthreads();
@@ -266,7 +280,7 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
   if (tid < G) {
     float* ml = p.part_ml + ((long long)(qh0 + tid) * p.n_splits + split) * 2;
     ml[0] = t1 > t0 ? sm.m[tid] : -CUDART_INF_F;
-    ml[1] = t1 > t0 ? l_run : 0.f;
+    ml[1] = t1 > t0 ? sm.l[tid] : 0.f;
   }
 }
 
