@@ -407,8 +407,15 @@ int check_block_weights(const gqa_ctx* c, const gqa_block_weights* w) {
   return GQA_OK;
 }
 
+// The split kernel's immediate predecessor is the QKV projection, which writes
+// neither pos nor a cache, and every kernel of the library releases its
+// dependents only after its own dependency wait: by the time the split kernel
+// starts, the kernel that advanced a device-side pos (two launches back at the
+// nearest) has finished, so the split may read the lengths and stream its cache
+// rows before its wait, in every layer.
 int block_impl(gqa_ctx* c, cudaStream_t st, const gqa_block_weights* w, const gqa_layer_kv* kv,
-               float* state, Lengths len, int plan_len, bool pdl_first, bool lengths_stable) {
+               float* state, Lengths len, int plan_len, bool pdl_first) {
+  const bool lengths_stable = true;
   const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv, hd = c->cfg.head_dim;
   const int model = block_model(c);
   GQA_CUDA(launch_qkv_gemv(model, w->w_qkv, w->b_qkv, w->gamma, state, c->blk_qkv,
@@ -959,7 +966,7 @@ int gqa_attention_block(gqa_ctx* c, gqa_stream_t stream, const gqa_block_weights
   Lengths len{};
   len.pos_imm = pos;
   len.seqlen_imm = seq_len;
-  return block_impl(c, (cudaStream_t)stream, w, kv, state, len, seq_len, c->pdl != 0, false);
+  return block_impl(c, (cudaStream_t)stream, w, kv, state, len, seq_len, c->pdl != 0);
 }
 
 int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
@@ -978,11 +985,9 @@ int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
   Lengths len{};
   len.pos_dev = d_pos;
   for (int l = 0; l < n_layers; ++l) {
-    // Layer 0 may follow the kernel that advanced *d_pos; its split kernel
-    // reads pos only after its wait.  Every later kernel starts after layer
-    // 0's split kernel has passed its wait.
-    int rc = block_impl(c, st, &w[l], &kv[l], state, len, c->cfg.t_max,
-                        c->layers_pdl != 0, l > 0);
+    // Layer 0's QKV projection may follow the kernel that advanced *d_pos;
+    // the split kernel after it reads pos early (see block_impl).
+    int rc = block_impl(c, st, &w[l], &kv[l], state, len, c->cfg.t_max, c->layers_pdl != 0);
     if (rc != GQA_OK) return rc;
   }
   if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
@@ -1015,10 +1020,8 @@ int gqa_decoder_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers, const gqa_
   Lengths len{};
   len.pos_dev = d_pos;
   for (int l = 0; l < n_layers; ++l) {
-    // Layer 0's split kernel reads pos only after its wait (see
-    // gqa_attention_block_layers); every later kernel starts after it.
-    int rc = block_impl(c, st, &attn[l], &kv[l], state, len, c->cfg.t_max, c->layers_pdl != 0,
-                        l > 0);
+    // (the split kernels read pos early: see block_impl)
+    int rc = block_impl(c, st, &attn[l], &kv[l], state, len, c->cfg.t_max, c->layers_pdl != 0);
     if (rc == GQA_OK) rc = ffn_impl(c, st, &ffn[l], state, true);
     if (rc != GQA_OK) return rc;
   }
@@ -1120,9 +1123,8 @@ int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float*
   Lengths len{};
   len.pos_dev = d_pos;
   for (int l = 0; l < m->n_layers; ++l) {
-    // Layer 0's split kernel reads pos only after its wait (see
-    // gqa_attention_block_layers); every later kernel starts after it.
-    rc = block_impl(c, st, &m->attn[l], &m->kv[l], state, len, c->cfg.t_max, pdl, l > 0);
+    // (the split kernels read pos early: see block_impl)
+    rc = block_impl(c, st, &m->attn[l], &m->kv[l], state, len, c->cfg.t_max, pdl);
     if (rc == GQA_OK) rc = ffn_impl(c, st, &m->ffn[l], state, pdl);
     if (rc != GQA_OK) return rc;
   }
