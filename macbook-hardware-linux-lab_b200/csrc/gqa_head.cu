@@ -33,12 +33,12 @@
 // field flipped), so that an assembled code byte is code ^ 32.  Any run of rows
 // starting on a multiple of 4 is then four 16-byte-aligned runs of bytes.
 //
-// The head kernel is a bulk-copy pipeline: one CTA per SM, a producer warp
-// that copies stages of 16 rows (the four planes' runs, 20160 bytes) into an
-// 8-deep ring of shared-memory stages, starting before the programmatic
-// dependency wait (the weights do not depend on the previous kernel), and 16
-// consumer warps that each take one row of a stage.  Stages go to CTAs
-// round-robin.  Lane (hh0 = lane / 8, q = lane % 8) owns, in every row, the
+// The head kernel is a bulk-copy pipeline: one CTA per SM over a contiguous,
+// balanced range of rows, a producer warp that copies stages of 32 rows (the
+// four planes' runs, 40320 bytes) into a 4-deep ring of shared-memory stages,
+// starting before the programmatic dependency wait (the weights do not depend
+// on the previous kernel), and 16 consumer warps that each take two rows of a
+// stage, computed side by side.  Lane (hh0 = lane / 8, q = lane % 8) owns, in every row, the
 // three 16-weight units hh = hh0 + 4u (u = 0, 1, 2), l = 4q .. 4q + 3, all
 // four quarters: the units' 48 inputs stay in registers for the whole kernel.
 // Per unit the lane reads two ql words, one qh word, its four scale bytes and
@@ -70,13 +70,13 @@ constexpr int kDRow = kQ6Supers * 2;
 constexpr int kHeadConsumerWarps = 16;
 constexpr int kHeadConsumers = 32 * kHeadConsumerWarps;
 constexpr int kHeadThreads = kHeadConsumers + 32;  // + the producer warp
-constexpr int kStageRows = kHeadConsumerWarps;     // a row per consumer warp
-constexpr int kHeadStages = 8;
+constexpr int kStageRows = 2 * kHeadConsumerWarps;  // two rows per consumer warp
+constexpr int kHeadStages = 4;
 constexpr int kStQl = kStageRows * kQlRow;
 constexpr int kStQh = kStageRows * kQhRow;
 constexpr int kStSc = kStageRows * kScRow;
 constexpr int kStD = kStageRows * kDRow;
-constexpr int kStageBytes = kStQl + kStQh + kStSc + kStD;  // 20160
+constexpr int kStageBytes = kStQl + kStQh + kStSc + kStD;  // 40320
 constexpr float kHeadRmsEps = 1e-6f;               // EPSILON of the reference
 constexpr float kNoPick = -1e30f;                  // best_val start of the greedy loop
 constexpr long long kHeadWaitBudget = 2000000000LL;
@@ -240,50 +240,68 @@ struct LaneDigits {
   float s[3];
 };
 
-// Dot product of one row held in a stage with the lane's inputs (lane's
-// partial sum; the caller reduces over the warp).
-__device__ __forceinline__ float row_dot(const uint8_t* sb, int j, const LaneConst& lc,
-                                         const LaneDigits& x) {
+// Unit u's term of row j of a stage for this lane: (d s) (K1 + K2/126 + K3/126^2).
+__device__ __forceinline__ float unit_term(const uint8_t* sb, int j, int u, const LaneConst& lc,
+                                           const LaneDigits& x) {
   const uint32_t* qlw = reinterpret_cast<const uint32_t*>(sb) + j * (kQlRow / 4);
   const uint32_t* qhw = reinterpret_cast<const uint32_t*>(sb + kStQl) + j * (kQhRow / 4);
   const uint32_t* scw = reinterpret_cast<const uint32_t*>(sb + kStQl + kStQh) + j * (kScRow / 4);
   const unsigned short* dw =
       reinterpret_cast<const unsigned short*>(sb + kStQl + kStQh + kStSc) + j * (kDRow / 2);
-  float acc = 0.f;
+  const int hh = lc.hh0 + 4 * u;
+  const uint32_t W0 = qlw[16 * hh + lc.o0 + lc.q], W1 = qlw[16 * hh + lc.o1 + lc.q];
+  const uint32_t H = qhw[8 * hh + lc.q];
+  const uint32_t sv = scw[2 * hh + lc.g];
+  const float d = __half2float(__ushort_as_half(dw[hh >> 1]));
+  // byte e of Q[c] = (6-bit code of weight (quarter c, l = 4q + e)) ^ 32
+  uint32_t Q[4];
+  Q[0] = (W0 & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
+  Q[1] = (W1 & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
+  Q[2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
+  Q[3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
+  int K[3] = {0, 0, 0};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    // code - 32 as a signed byte: y when y < 32, y - 64 (= y | 0xC0) otherwise
+    const int v = (int)((Q[c] & 0x20202020u) * 6u + Q[c]);
+    // the quarter's int8 scale, sign-extended: PTX prmt replicates the
+    // selected byte's sign bit when bit 3 of a selector nibble is set (the
+    // __byte_perm intrinsic reads only bits 0-2 of each nibble)
+    int sc;
+    asm("prmt.b32 %0, %1, 0, %2;"
+        : "=r"(sc)
+        : "r"(sv), "r"(c | (8 + c) << 4 | (8 + c) << 8 | (8 + c) << 12));
+#pragma unroll
+    for (int k = 0; k < 3; ++k) K[k] += sc * __dp4a(v, x.e[u][c][k], 0);
+  }
+  constexpr float kB1 = 1.0f / 126.0f, kB2 = 1.0f / 15876.0f;
+  const float f = __fmaf_rn(small_int_to_float(K[2]), kB2,
+                            __fmaf_rn(small_int_to_float(K[1]), kB1, small_int_to_float(K[0])));
+  return f * __fmul_rn(d, x.s[u]);  // (d s) exact: s is a power of two
+}
+
+// Rows ja and jb of a stage with the lane's inputs (lane's partial sums; the
+// caller reduces over the warp): two independent chains sharing the digits.
+__device__ __forceinline__ void rows_dot(const uint8_t* sb, int ja, int jb, const LaneConst& lc,
+                                         const LaneDigits& x, float& acc_a, float& acc_b) {
+  acc_a = 0.f;
+  acc_b = 0.f;
 #pragma unroll
   for (int u = 0; u < 3; ++u) {
-    const int hh = lc.hh0 + 4 * u;
-    const uint32_t W0 = qlw[16 * hh + lc.o0 + lc.q], W1 = qlw[16 * hh + lc.o1 + lc.q];
-    const uint32_t H = qhw[8 * hh + lc.q];
-    const uint32_t sv = scw[2 * hh + lc.g];
-    const float d = __half2float(__ushort_as_half(dw[hh >> 1]));
-    // byte e of Q[c] = (6-bit code of weight (quarter c, l = 4q + e)) ^ 32
-    uint32_t Q[4];
-    Q[0] = (W0 & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
-    Q[1] = (W1 & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
-    Q[2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
-    Q[3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
-    int K[3] = {0, 0, 0};
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      // code - 32 as a signed byte: y when y < 32, y - 64 (= y | 0xC0) otherwise
-      const int v = (int)((Q[c] & 0x20202020u) * 6u + Q[c]);
-      // the quarter's int8 scale, sign-extended: PTX prmt replicates the
-      // selected byte's sign bit when bit 3 of a selector nibble is set (the
-      // __byte_perm intrinsic reads only bits 0-2 of each nibble)
-      int sc;
-      asm("prmt.b32 %0, %1, 0, %2;"
-          : "=r"(sc)
-          : "r"(sv), "r"(c | (8 + c) << 4 | (8 + c) << 8 | (8 + c) << 12));
-#pragma unroll
-      for (int k = 0; k < 3; ++k) K[k] += sc * __dp4a(v, x.e[u][c][k], 0);
-    }
-    constexpr float kB1 = 1.0f / 126.0f, kB2 = 1.0f / 15876.0f;
-    const float f = __fmaf_rn(small_int_to_float(K[2]), kB2,
-                              __fmaf_rn(small_int_to_float(K[1]), kB1, small_int_to_float(K[0])));
-    acc = __fmaf_rn(__fmul_rn(d, x.s[u]), f, acc);
+    const float ta = unit_term(sb, ja, u, lc, x);
+    const float tb = unit_term(sb, jb, u, lc, x);
+    acc_a = __fadd_rn(acc_a, ta);
+    acc_b = __fadd_rn(acc_b, tb);
   }
-  return acc;
+}
+
+// The CTA's rows: a contiguous range of the padded rows, cut on multiples of
+// 4 so that every stage's runs stay 16-byte multiples; ranges differ by at
+// most 4 rows, so no CTA does a whole stage more than another.
+__device__ __forceinline__ void head_cta_rows(long long np, long long& r_begin, long long& r_end) {
+  const long long units = np / 4;
+  r_begin = units * blockIdx.x / gridDim.x * 4;
+  r_end = units * (blockIdx.x + 1) / gridDim.x * 4;
 }
 
 __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadParams p) {
@@ -292,8 +310,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_rows = p.n_rows;
   const long long np = head_padded_rows(n_rows);
-  const int n_stages = (int)((np + kStageRows - 1) / kStageRows);
-  const int grid = gridDim.x;
+  long long r_begin, r_end;
+  head_cta_rows(np, r_begin, r_end);
+  const int n_stages = (int)((r_end - r_begin + kStageRows - 1) / kStageRows);
   if (tid == 0) {
     for (int s = 0; s < kHeadStages; ++s) {
       mbar_init(&sm.full[s], 1);
@@ -313,15 +332,15 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
       const uint64_t pol = l2_policy_evict_first();
       int k = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < n_stages; t += grid, ++k) {
+      for (; k < n_stages; ++k) {
         const int s = k % kHeadStages;
         if (k >= kHeadStages &&
             !mbar_wait_bounded(&sm.empty[s], ((k / kHeadStages) - 1) & 1, kHeadWaitBudget)) {
           ok = false;
           break;
         }
-        const long long r0 = (long long)t * kStageRows;
-        const int nr = (int)min((long long)kStageRows, np - r0);
+        const long long r0 = r_begin + (long long)k * kStageRows;
+        const int nr = (int)min((long long)kStageRows, r_end - r0);  // a multiple of 4
         uint8_t* st = sm.stage[s];
         mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(nr * kQ6RowBytes));
         bulk_copy_g2s(st, ql + r0 * kQlRow, nr * kQlRow, &sm.full[s], pol);
@@ -440,22 +459,37 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
   float best_v = kNoPick;
   int best_i = 0;
   bool ok = true;
-  int k = 0;
-  for (int t = blockIdx.x; t < n_stages; t += grid, ++k) {
+  const long long r_stop = min(r_end, (long long)n_rows);  // padding rows are never output
+  const int ja = warp, jb = warp + kStageRows / 2;
+  for (int k = 0; k < n_stages; ++k) {
     const int s = k % kHeadStages;
     if (!mbar_wait_bounded(&sm.full[s], (k / kHeadStages) & 1, kHeadWaitBudget)) {
       ok = false;
       break;
     }
-    const int r = t * kStageRows + warp;
-    if (r < n_rows) {
-      float acc = row_dot(sm.stage[s], warp, lc, x);
+    const long long r0 = r_begin + (long long)k * kStageRows;
+    // (jb > ja: a warp whose first row is past the CTA's rows has none; the
+    // rows past a short last stage hold stale bytes and are not output)
+    if (r0 + ja < r_stop) {
+      float acc_a, acc_b;
+      rows_dot(sm.stage[s], ja, jb, lc, x, acc_a, acc_b);
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-      if (p.logits && lane == 0) p.logits[r] = acc;
-      if (acc > best_v) {  // rows rise within a warp: the first maximum stays
-        best_v = acc;
-        best_i = r;
+      for (int off = 16; off > 0; off >>= 1) {
+        acc_a += __shfl_xor_sync(0xffffffffu, acc_a, off);
+        acc_b += __shfl_xor_sync(0xffffffffu, acc_b, off);
+      }
+      // rows rise within a warp (ja < jb, stages in order): the first maximum stays
+      if (p.logits && lane == 0) p.logits[r0 + ja] = acc_a;
+      if (acc_a > best_v) {
+        best_v = acc_a;
+        best_i = (int)(r0 + ja);
+      }
+      if (r0 + jb < r_stop) {
+        if (p.logits && lane == 0) p.logits[r0 + jb] = acc_b;
+        if (acc_b > best_v) {
+          best_v = acc_b;
+          best_i = (int)(r0 + jb);
+        }
       }
     }
     __syncwarp();
@@ -596,15 +630,6 @@ __device__ __forceinline__ void q8_rows_dot(const uint8_t* sb, int ja, int jb,
   out_b = __fadd_rn(vb[0], vb[1]);
 }
 
-// The CTA's rows: a contiguous range of the padded rows, cut on multiples of
-// 4 so that every stage's runs stay 16-byte multiples; ranges differ by at
-// most 4 rows, so no CTA does a whole stage more than another.
-__device__ __forceinline__ void q8_cta_rows(long long np, long long& r_begin, long long& r_end) {
-  const long long units = np / 4;
-  r_begin = units * blockIdx.x / gridDim.x * 4;
-  r_end = units * (blockIdx.x + 1) / gridDim.x * 4;
-}
-
 __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_q8_kernel(const HeadParams p) {
   extern __shared__ __align__(128) unsigned char head_smem_raw[];
   Q8Smem& sm = *reinterpret_cast<Q8Smem*>(head_smem_raw);
@@ -612,7 +637,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_q8_kernel(const HeadP
   const int n_rows = p.n_rows;
   const long long np = head_padded_rows(n_rows);
   long long r_begin, r_end;
-  q8_cta_rows(np, r_begin, r_end);
+  head_cta_rows(np, r_begin, r_end);
   const int n_stages = (int)((r_end - r_begin + kQ8StageRows - 1) / kQ8StageRows);
   if (tid == 0) {
     for (int s = 0; s < kQ8Stages; ++s) {
