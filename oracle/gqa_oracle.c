@@ -20,6 +20,12 @@
  *   oracle_*_batched()          the same per-sequence math over many sequences,
  *                               OpenMP-parallel over (sequence, q head); each
  *                               head's arithmetic is identical to the serial loop.
+ *
+ * And the caller's step around the path where the reference's CPU code cannot
+ * be compiled for it: the token embedding, the output RMSNorm and the greedy
+ * pick (restated from qwen_server.c / test_full_model_logits.c), and the
+ * Qwen2.5-0.5B head oracle_gemv_q8_0() (kernel_q8_0.cl:10-61, which the
+ * reference has only as OpenCL: parity for it is unpinned).
  */
 #include <immintrin.h>
 #include <math.h>

@@ -15,7 +15,10 @@ bench.py, as the checker (never as the thing measured or shipped).
   (qwen_server.c:113-266, ``_ref/libgqa_ref_server.so``), compiled unmodified
   from its sources by oracle/Makefile.  They exist only where the
   reference sources were present at build time; REF_T_MAX = 4096 is their
-  compile-time cache stride.
+  compile-time cache stride.  The layer library also exports the reference's
+  size-generic cpu_gemv_q4_0_bias / cpu_swiglu_fused (test_28_layers_real.c:
+  90-131), from which decoder_layer_sized() composes the Qwen2.5-0.5B layer
+  (pinned bit for bit to cpu_decoder_layer_step at the 1.5B sizes).
 """
 from __future__ import annotations
 
