@@ -448,8 +448,10 @@ GQA_API int gqa_gguf_token_string(const gqa_gguf *g, int id, char *out, int cap)
  * out (qwen_server.c:525-588): per layer W_qkv = attn_q | attn_k | attn_v rows
  * and b_qkv likewise, attn_output, ffn_gate/up/down and both norm weights;
  * token_embd.weight; output_norm.weight; output.weight through
- * gqa_lm_head_pack.  Types and shapes are checked (Q4_0 projections and
- * embedding, Q6_K head, F32 norms and biases, Qwen2.5-1.5B shapes).
+ * gqa_lm_head_pack.  The sizes come from the context's shape: Qwen2.5-1.5B
+ * (Q6_K head) or Qwen2.5-0.5B (Q8_0 head through gqa_lm_head_q8_0_pack, the
+ * tensors generate_stream_05b.c:553-615 reads); types and shapes are checked
+ * (Q4_0 projections and embedding, the head's type, F32 norms and biases).
  * n_layers <= 0 takes qwen2.block_count from the file.  Allocates on the
  * current device, which must be the context's. */
 typedef struct gqa_model_weights gqa_model_weights;
