@@ -38,21 +38,21 @@
 // four planes' runs, 40320 bytes) into a 4-deep ring of shared-memory stages,
 // starting before the programmatic dependency wait (the weights do not depend
 // on the previous kernel), and 16 consumer warps that each take two rows of a
-// stage, computed side by side.  Lane (hh0 = lane / 8, q = lane % 8) owns, in every row, the
-// three 16-weight units hh = hh0 + 4u (u = 0, 1, 2), l = 4q .. 4q + 3, all
-// four quarters: the units' 48 inputs stay in registers for the whole kernel.
-// Per unit the lane reads two ql words, one qh word, its four scale bytes and
-// d; four code words (one byte per weight, 0..63) come from AND/OR steps.  The
-// products are integer: once per launch the CTA splits each unit's 16
-// normalised inputs, with a power-of-two scale s >= max|z| / 63, into three
-// signed digits in [-63, 63], z = s (e1 + e2 / 126 + e3 / 126^2); per row, the
-// code bytes become code - 32 as signed bytes (y = code ^ 32 from the packed qh,
-// plus 6 (y & 32): two instructions per word), dp4a against the digit words
-// gives exact int32 sums, the quarters' int8 scales combine them exactly
-// (|K| < 2^22), and the unit's term
-// is (d s) (K1 + K2 / 126 + K3 / 126^2).  With z = 32 e_i (a power of two) the
-// digits are exact and a logit is d * (scale * (code - 32) * 32) with one
-// rounding, as in the reference's order (d * scale is exact).
+// stage, computed side by side.  Lane (hh0 = lane / 8, q = lane % 8) owns, in
+// every row, the three 16-weight units hh = hh0 + 4u (u = 0, 1, 2),
+// l = 4q .. 4q + 3, all four quarters; the digit words of the units' 48 inputs
+// (below) stay in registers for the whole kernel.  Per unit the lane reads two
+// ql words, one qh word, its four scale bytes and d; four code words (one byte
+// per weight) come from AND/OR steps.  The products are integer: once per
+// launch the CTA splits each unit's 16 normalised inputs, with a power-of-two
+// scale s >= max|z| / 63, into three signed digits in [-63, 63],
+// z = s (e1 + e2 / 126 + e3 / 126^2); per row, the code bytes become code - 32
+// as signed bytes (y = code ^ 32 from the packed qh, plus 6 (y & 32): two
+// instructions per word), dp4a against the digit words gives exact int32
+// sums, the quarters' int8 scales combine them exactly (|K| < 2^22), and the
+// unit's term is (d s) (K1 + K2 / 126 + K3 / 126^2).  With z = 32 e_i (a power
+// of two) the digits are exact and a logit is d * (scale * (code - 32) * 32)
+// with one rounding, as in the reference's order (d * scale is exact).
 #include <cuda_fp16.h>
 
 #include "gqa_common.cuh"
