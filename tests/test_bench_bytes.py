@@ -1,0 +1,50 @@
+"""The algorithmic byte counts behind bench.py's GB/s and roofline figures,
+recomputed from the sizes of the arrays the workloads are generated from (no
+GPU): KV rows, Q4_0 projection and FFN weights, biases and norms, and the two
+LM heads at both model sizes."""
+import os
+import sys
+
+import numpy as np
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import bench  # noqa: E402
+
+
+def _nbytes(*arrays):
+    return sum(np.asarray(a).nbytes for a in arrays)
+
+
+def test_kv_row_bytes():
+    # K and V of one attended position, both KV heads, fp32
+    assert bench.ROW_BYTES == 2 * 2 * 128 * 4 == 2048
+    assert bench.ROW05 == 2 * 2 * 64 * 4 == 1024
+
+
+def test_layer_weight_bytes_15b(pkg):
+    s = pkg.seeded
+    _, w_qkv, b_qkv, w_o, gamma, _, _ = s.attention_block_inputs(1, t_max=8)
+    assert bench.BLOCK_WEIGHT_BYTES == _nbytes(w_qkv, b_qkv, w_o, gamma)
+    assert bench.FFN_WEIGHT_BYTES == _nbytes(*s.ffn_block_inputs(1))
+
+
+def test_layer_weight_bytes_05b(pkg):
+    s = pkg.seeded
+    _, w_qkv, b_qkv, w_o, gamma, _, _ = s.attention_block_inputs(1, t_max=8, d_model=896,
+                                                                 n_heads_kv=2, head_dim=64)
+    assert bench.BLOCK05_BYTES == _nbytes(w_qkv, b_qkv, w_o, gamma)
+    assert bench.FFN05_BYTES == _nbytes(*s.ffn_block_inputs(1, d_model=896, d_ffn=4864))
+    assert bench.Q4_ROW05 == 896 // 32 * 18
+
+
+def test_head_bytes(pkg):
+    s = pkg.seeded
+    rows = 64
+    # per vocabulary row, as generated; plus gamma_output and the state
+    q6 = s.q6_k_matrix(1, s.W_HEAD, rows, 1536).nbytes // rows
+    q8 = s.q8_0_matrix(1, s.W_HEAD, rows, 896).nbytes // rows
+    assert bench.HEAD_BYTES == bench.VOCAB * q6 + 1536 * 4 * 2
+    assert bench.HEAD05_BYTES == bench.VOCAB * q8 + 896 * 4 * 2
+    # the packed layouts hold exactly the tensor's bytes for the full vocabulary
+    assert pkg.Context.lm_head_packed_bytes(bench.VOCAB) == bench.VOCAB * q6
+    assert pkg.Context.lm_head_q8_0_packed_bytes(bench.VOCAB) == bench.VOCAB * q8
