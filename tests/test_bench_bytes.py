@@ -48,3 +48,13 @@ def test_head_bytes(pkg):
     # the packed layouts hold exactly the tensor's bytes for the full vocabulary
     assert pkg.Context.lm_head_packed_bytes(bench.VOCAB) == bench.VOCAB * q6
     assert pkg.Context.lm_head_q8_0_packed_bytes(bench.VOCAB) == bench.VOCAB * q8
+
+
+def test_packed_sizes_edges(pkg):
+    """Rows are rounded up to a multiple of 4; no rows, no bytes."""
+    C = pkg.Context
+    for n in (-1, 0):
+        assert C.lm_head_packed_bytes(n) == 0 and C.lm_head_q8_0_packed_bytes(n) == 0
+    for n, padded in ((1, 4), (3, 4), (4, 4), (5, 8), (151936, 151936)):
+        assert C.lm_head_packed_bytes(n) == padded * 1260
+        assert C.lm_head_q8_0_packed_bytes(n) == padded * 952
