@@ -263,10 +263,12 @@ def cpu_reference_run(steps, warmup, budget_s, pos_lo=3840, layers=28):
 
 def cpu_port_05b_run(budget_s, pos_lo=3840, layers=24):
     """The reference has no CPU attention for the 0.5B shape: the restatement
-    (oracle/gqa_oracle.c, its loops at head_dim 64, group 7), one thread, per
-    step the 24 layer calls."""
+    (oracle/gqa_oracle.c, its loops at head_dim 64, group 7); per step the 24
+    layer calls (independent inputs) spread over all host threads, as the
+    reference's own function is timed for the 1.5B shape."""
     import __graft_entry__
     orc = __graft_entry__.load_oracle()
+    cores = os.cpu_count() or 1
     rng = np.random.default_rng(0)
     T, nq, nkv, d = 4096, 14, 2, 64
     kcs = [rng.standard_normal((nkv, T, d), dtype=np.float32) for _ in range(layers)]
@@ -276,17 +278,17 @@ def cpu_port_05b_run(budget_s, pos_lo=3840, layers=24):
     done, nbytes = 0, 0
     while True:
         pos = pos_lo + done % 256
-        for l in range(layers):
-            orc.layer_attention(qkvs[l].copy(), kcs[l], vcs[l], pos, pos + 1, n_heads_q=nq,
-                                n_heads_kv=nkv, head_dim=d)
+        orc.decode_batched([q.copy() for q in qkvs], kcs, vcs, [pos + 1] * layers, n_heads_q=nq,
+                           n_heads_kv=nkv, n_threads=cores, head_dim=d)
         nbytes += layers * 2 * nkv * d * 4 * (pos + 1)
         done += 1
         if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
     sample = (f"{done} decode step(s) x {layers} layers at positions {pos_lo}.."
-              f"{pos_lo + min(done, 256) - 1}, the C restatement on 1 thread")
-    return nbytes / dt / 1e9, 1, sample, "port", done / dt
+              f"{pos_lo + min(done, 256) - 1}, the C restatement, layer calls spread over "
+              f"{cores} threads")
+    return nbytes / dt / 1e9, cores, sample, "port", done / dt
 
 
 def run_reference_arm(args):

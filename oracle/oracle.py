@@ -129,14 +129,14 @@ def _ptr_array(arrs):
 
 
 def decode_batched(qkv: list, k_caches: list, v_caches: list, seq_lens, n_heads_q=12,
-                   n_heads_kv=2, rope_base=1e6, n_threads=None) -> list:
+                   n_heads_kv=2, rope_base=1e6, n_threads=None, head_dim=128) -> list:
     """One new token per sequence; caches appended in place; returns attn_out per sequence."""
     n = len(qkv)
-    outs = [np.zeros(n_heads_q * 128, dtype=np.float32) for _ in range(n)]
+    outs = [np.zeros(n_heads_q * head_dim, dtype=np.float32) for _ in range(n)]
     lens = (ctypes.c_int * n)(*[int(x) for x in seq_lens])
     _lib().oracle_decode_batched(n, _ptr_array(qkv), _ptr_array(k_caches), _ptr_array(v_caches),
-                                 lens, k_caches[0].shape[1], n_heads_q, n_heads_kv, 128, rope_base,
-                                 _ptr_array(outs), n_threads or os.cpu_count())
+                                 lens, k_caches[0].shape[1], n_heads_q, n_heads_kv, head_dim,
+                                 rope_base, _ptr_array(outs), n_threads or os.cpu_count())
     return outs
 
 
