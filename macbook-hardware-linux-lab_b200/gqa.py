@@ -198,7 +198,8 @@ def lib() -> ctypes.CDLL:
 
 
 def last_error() -> str:
-    return (lib().gqa_last_error_string() or b"").decode()
+    # (a message can quote a name from a damaged file: never fail on its bytes)
+    return (lib().gqa_last_error_string() or b"").decode("utf-8", "replace")
 
 
 def _check(rc: int) -> None:
@@ -345,7 +346,10 @@ class Gguf:
 
     @staticmethod
     def _info(t: GgufTensor) -> dict:
-        return {"name": t.name.decode(), "n_dims": t.n_dims, "ne": list(t.ne)[:t.n_dims],
+        # names are bytes in the file (the reference reads them as char arrays):
+        # undecodable bytes survive as surrogates and round-trip into find()
+        return {"name": t.name.decode("utf-8", "surrogateescape"), "n_dims": t.n_dims,
+                "ne": list(t.ne)[:t.n_dims],
                 "type": t.type, "offset": t.offset, "bytes": t.bytes}
 
     def tensors(self) -> list[dict]:
@@ -358,19 +362,22 @@ class Gguf:
 
     def find(self, name: str) -> dict:
         t = GgufTensor()
-        _check(lib().gqa_gguf_find(self._h, name.encode(), ctypes.byref(t)))
+        _check(lib().gqa_gguf_find(self._h, name.encode("utf-8", "surrogateescape"),
+                                   ctypes.byref(t)))
         return self._info(t)
 
     def read(self, name: str) -> np.ndarray:
         t = GgufTensor()
-        _check(lib().gqa_gguf_find(self._h, name.encode(), ctypes.byref(t)))
+        _check(lib().gqa_gguf_find(self._h, name.encode("utf-8", "surrogateescape"),
+                                   ctypes.byref(t)))
         out = np.empty(t.bytes, dtype=np.uint8)
         _check(lib().gqa_gguf_read(self._h, ctypes.byref(t), out.ctypes.data))
         return out
 
     def meta_int(self, key: str) -> int:
         v = _ll()
-        _check(lib().gqa_gguf_meta_int(self._h, key.encode(), ctypes.byref(v)))
+        _check(lib().gqa_gguf_meta_int(self._h, key.encode("utf-8", "surrogateescape"),
+                                       ctypes.byref(v)))
         return v.value
 
     def vocab_size(self) -> int:

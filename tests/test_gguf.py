@@ -115,3 +115,55 @@ def test_qwen_shaped_file(pkg, orc, tmp_path):
             ref, _ = orc.ref_gguf_parse(str(path))
             assert [(r["name"], r["offset"]) for r in ref] == \
                    [(x["name"], x["offset"]) for x in g.tensors()]
+
+
+def test_names_are_bytes(pkg, tmp_path):
+    """A tensor name that is not UTF-8 (the format says UTF-8; the reference
+    reads names as bytes) is listed, found and read by the same name."""
+    path = tmp_path / "n.gguf"
+    name = b"blk.0.\xff\xfe.weight"
+    data = np.arange(4, dtype=np.float32)
+    gw.write(path, [("general.architecture", gw.STR, "qwen2")],
+             [(name, gw.T_F32, [4], data.tobytes())])
+    with pkg.Gguf(str(path)) as g:
+        (t,) = g.tensors()
+        assert t["name"].encode("utf-8", "surrogateescape") == name
+        assert np.array_equal(g.read(t["name"]).view(np.float32), data)
+
+
+def test_mutated_files_are_read_or_refused(pkg, tmp_path):
+    """300 seeded mutations of a small model file -- bytes changed in the
+    header, metadata and tensor table, 32-bit fields set to extreme values,
+    truncations anywhere: each file is either read or refused with GqaError;
+    nothing crashes or reads past the end."""
+    path = tmp_path / "m.gguf"
+    gw.qwen_model(path, pkg.seeded, n_layers=1, vocab=64, seed=2, model="0.5b")
+    good = path.read_bytes()
+    rng = np.random.default_rng(2024)
+    bad = tmp_path / "bad.gguf"
+    refused = 0
+    for it in range(300):
+        b = bytearray(good)
+        if it % 3 == 0:
+            for _ in range(int(rng.integers(1, 8))):
+                b[int(rng.integers(0, min(len(b), 4096)))] = int(rng.integers(0, 256))
+        elif it % 3 == 1:
+            i = int(rng.integers(0, min(len(b), 4096) - 4)) & ~3
+            v = int(rng.choice([0, 1, 0x7FFFFFFF, 0xFFFFFFFF, 0x80000000]))
+            b[i:i + 4] = v.to_bytes(4, "little")
+        else:
+            b = b[:int(rng.integers(0, len(b)))]
+        bad.write_bytes(bytes(b))
+        try:
+            with pkg.Gguf(str(bad)) as g:
+                for t in g.tensors():
+                    assert t["offset"] + t["bytes"] <= len(b)
+                for i in range(min(g.vocab_size(), 8)):
+                    g.token(i)
+                try:
+                    g.read("output.weight")
+                except pkg.GqaError:
+                    pass
+        except pkg.GqaError:
+            refused += 1
+    assert refused > 0
