@@ -1095,6 +1095,8 @@ def run_ours(args):
         ctx.set_option(g.gqa.GQA_OPT_TARGET_CTAS, args.target_ctas)
     if args.batch_chunk:
         ctx.set_option(g.gqa.GQA_OPT_BATCH_CHUNK, args.batch_chunk)
+    if not args.grid_merge:
+        ctx.set_option(g.gqa.GQA_OPT_GRID_MERGE, 0)
     if args.workload == "prefill":
         return report_prefill(args, run_prefill(args, g, ctx, rank, world, local), ctx, rank,
                               world)
@@ -1223,6 +1225,7 @@ def main():
     ap.add_argument("--variant", type=int, default=-1, help=argparse.SUPPRESS)
     ap.add_argument("--target-ctas", type=int, default=0, help=argparse.SUPPRESS)
     ap.add_argument("--batch-chunk", type=int, default=0, help=argparse.SUPPRESS)
+    ap.add_argument("--grid-merge", type=int, default=1, help=argparse.SUPPRESS)
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer", help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.warmup < 3:

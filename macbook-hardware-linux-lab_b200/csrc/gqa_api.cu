@@ -23,6 +23,8 @@ cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cu
                                 bool pdl, int variant);
 int decode_variant_count();
 int decode_variant_quant(int variant);
+int decode_variant_grid_quant(int variant);
+int decode_grid_ctas_per_sm(int variant);
 cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl);
 cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k_ptrs,
                                float* const* v_ptrs, float* k_base, float* v_base,
@@ -124,6 +126,12 @@ struct gqa_ctx {
   // the final merge).
   int cluster = 0;
   int* counters = nullptr;  // [kCounterSlots] arrival / item counters, kept at zero
+  // Grid-merged single-sequence decode (one launch per layer call, the merge
+  // done by the split kernel's CTAs after a barrier on grid_bar).  On by
+  // default; off falls back to split kernel + combine kernel.
+  int grid_merge = 1;
+  int grid_ctas_per_sm = 0;                 // resident CTAs of the grid instance per SM
+  unsigned long long* grid_bar = nullptr;   // device barrier counter (only grows)
   float* blk_qkv = nullptr;   // attention block workspace: qkv of the token
   float* blk_attn = nullptr;  // attention block workspace: attention output
   float* blk_h = nullptr;     // FFN workspace: silu(gate) * up
@@ -241,6 +249,29 @@ int plan_splits_single(const gqa_ctx* c, int rows_kv, int len) {
   return want < 1 ? 1 : want;
 }
 
+// The grid-merged kernel shape: the forced variant if it has a grid instance,
+// else variant 0 (8 warps x 4-row stages; two CTAs fit on an SM, so the next
+// layer's CTAs can become resident beside the running ones).
+int grid_variant(const gqa_ctx* c) { return c->variant >= 0 ? c->variant : 0; }
+
+// Splits of a grid-merged single-sequence decode over `len` rows, or 0 when
+// the grid merge cannot be used: at least 6 splits (one merge slice per q
+// head), at most kGridMaxSplits, and every CTA of the launch resident at once
+// with room for the next launch's CTAs (at most one CTA per SM when two fit).
+constexpr int kGridMaxSplits = 256;  // = kGridMaxParts of the kernel
+int plan_splits_grid(const gqa_ctx* c, int rows_kv, int len) {
+  if (!c->grid_merge || c->generic || c->grid_ctas_per_sm < 1) return 0;
+  const int quant = decode_variant_grid_quant(grid_variant(c));
+  const int per_sm = c->grid_ctas_per_sm >= 2 ? 1 : c->grid_ctas_per_sm;
+  const int cap = c->n_sm * per_sm;
+  const int target = c->target_ctas > 0 && c->target_ctas < cap ? c->target_ctas : cap;
+  int want = target / rows_kv;
+  const int most = ceil_div(len, quant);
+  if (want > most) want = most;
+  if (want > kGridMaxSplits) want = kGridMaxSplits;
+  return want >= 6 ? want : 0;
+}
+
 int batch_chunk(const gqa_ctx* c, int max_len) {
   const int q = decode_variant_quant(batch_variant(c));
   int want = c->batch_chunk > 0 ? c->batch_chunk : (max_len > 8192 ? 1024 : 256);
@@ -285,11 +316,49 @@ int check_kv(const gqa_ctx* c, const gqa_layer_kv* kv) {
   return GQA_OK;
 }
 
-// One sequence: split kernel (+ combine when split), result to `out`.
+// Position advance folded into a grid-merged launch (see DecodeParams).
+struct Advance {
+  int* pos = nullptr;
+  int wrap_lo = 0, wrap_hi = 0;
+};
+
+// One sequence: split kernel (+ combine when split), result to `out`.  When
+// the grid merge applies, one launch does both; it then also brings
+// `next_kv`'s rows (if any) into L2 and performs `adv` (if any), and
+// *advanced is set.  Otherwise the caller still owes the advance.
 int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
                Lengths len, int plan_len, bool fused, float* out, bool pdl_first,
-               bool lengths_stable) {
+               bool lengths_stable, const gqa_layer_kv* next_kv = nullptr,
+               const Advance* adv = nullptr, bool* advanced = nullptr) {
   const int n_kv = c->cfg.n_heads_kv;
+  if (advanced) *advanced = false;
+  const int grid_splits = (fused && out != nullptr) ? plan_splits_grid(c, n_kv, plan_len) : 0;
+  if (grid_splits > 0) {
+    int rc = ensure_scratch(c, (long long)c->cfg.n_heads_q * grid_splits, st);
+    if (rc != GQA_OK) return rc;
+    DecodeParams p = base_params(c);
+    p.k_base = kv->k_cache;
+    p.v_base = kv->v_cache;
+    p.qkv = qkv;
+    p.len = len;
+    p.lengths_stable = lengths_stable ? 1 : 0;
+    p.n_splits = grid_splits;
+    p.min_chunk = decode_variant_grid_quant(grid_variant(c));
+    p.out = out;
+    p.grid_bar = c->grid_bar;
+    if (next_kv) {
+      p.pf_k = next_kv->k_cache;
+      p.pf_v = next_kv->v_cache;
+    }
+    if (adv && adv->pos) {
+      p.advance_pos = adv->pos;
+      p.wrap_lo = adv->wrap_lo;
+      p.wrap_hi = adv->wrap_hi;
+      if (advanced) *advanced = true;
+    }
+    GQA_CUDA(launch_decode_split(p, 1, true, st, pdl_first, grid_variant(c)));
+    return GQA_OK;
+  }
   int n_splits = plan_splits_single(c, n_kv, plan_len);
   // Enough splits for whole clusters: reduce in-kernel (no combine launch).
   const bool use_cluster = fused && c->cluster && n_splits >= kCluster && n_kv <= kMaxCounters;
@@ -359,19 +428,30 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
   }
   Lengths len{};
   len.pos_dev = d_pos;
+  Advance adv;
+  adv.pos = advance ? d_pos : nullptr;
+  adv.wrap_lo = wrap_lo;
+  adv.wrap_hi = wrap_hi;
+  bool advanced = false;
   for (int l = 0; l < n_layers; ++l) {
-    // Layer 0 may follow the kernel that advanced *d_pos: it reads pos only
-    // after its dependency wait.  Later layers follow a combine/split of
-    // the previous layer, which never writes pos or this layer's cache.
+    // Layer 0 is launched without programmatic overlap, so whatever advanced
+    // *d_pos before it has finished and it may read pos (and stream its
+    // cache rows) at once.  Later layers follow a kernel of the previous
+    // layer, which never writes pos or this layer's cache (the advance, when
+    // folded into the last layer, happens after all of that layer's CTAs
+    // have read pos).
+    const bool pdl = l > 0 && c->layers_pdl != 0;
+    const bool last = l == n_layers - 1;
     int rc = c->generic
                  ? run_generic(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max,
-                               out + l * out_stride, c->layers_pdl != 0, /*lengths_stable=*/l > 0)
+                               out + l * out_stride, pdl, /*lengths_stable=*/true)
                  : run_single(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max, true,
-                              out + l * out_stride, /*pdl_first=*/c->layers_pdl != 0,
-                              /*lengths_stable=*/l > 0);
+                              out + l * out_stride, pdl, /*lengths_stable=*/true,
+                              last ? nullptr : &kv[l + 1], last ? &adv : nullptr,
+                              last ? &advanced : nullptr);
     if (rc != GQA_OK) return rc;
   }
-  if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
+  if (advance && !advanced) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
   return GQA_OK;
 }
 
@@ -576,6 +656,9 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess) e = prepare_head_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kCounterSlots);
   if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * kCounterSlots);
+  if (e == cudaSuccess) e = cudaMalloc(&c->grid_bar, sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(c->grid_bar, 0, sizeof(unsigned long long));
+  if (e == cudaSuccess) c->grid_ctas_per_sm = decode_grid_ctas_per_sm(grid_variant(c));
   if (e == cudaSuccess) {
     c->head_grid = lm_head_grid(c->n_sm);
     e = cudaMalloc(&c->head_best, lm_head_best_bytes(c->head_grid));
@@ -597,6 +680,7 @@ int gqa_destroy(gqa_ctx* c) {
   if (c->inv_freq) cudaFree(c->inv_freq);
   if (c->status) cudaFree(c->status);
   if (c->counters) cudaFree(c->counters);
+  if (c->grid_bar) cudaFree(c->grid_bar);
   if (c->blk_qkv) cudaFree(c->blk_qkv);
   if (c->blk_attn) cudaFree(c->blk_attn);
   if (c->blk_h) cudaFree(c->blk_h);
@@ -627,10 +711,14 @@ int gqa_set_option(gqa_ctx* c, int option, long long value) {
     case 6: /* GQA_OPT_CLUSTER (internal tuning knob) */
       c->cluster = value ? 1 : 0;
       return GQA_OK;
+    case 7: /* GQA_OPT_GRID_MERGE (internal tuning knob) */
+      c->grid_merge = value ? 1 : 0;
+      return GQA_OK;
     case 4: /* GQA_OPT_KERNEL_VARIANT (internal tuning knob) */
       if (value < -1 || value >= decode_variant_count())
         return fail(GQA_ERR_INVALID_ARG, "kernel variant out of range (-1 = automatic)");
       c->variant = (int)value;
+      c->grid_ctas_per_sm = decode_grid_ctas_per_sm(grid_variant(c));
       return GQA_OK;
     default: return fail(GQA_ERR_INVALID_ARG, "unknown option %d", option);
   }
@@ -644,8 +732,10 @@ int gqa_reserve(gqa_ctx* c, int n_seq, int max_len) {
     return ensure_scratch(c, (long long)n_seq * c->cfg.n_heads_q *
                                  generic_plan_splits(c->cfg.n_heads_kv, max_len, c->n_sm),
                           nullptr);
-  const int single = ((plan_splits_single(c, c->cfg.n_heads_kv, max_len) + kCluster - 1) /
-                      kCluster) * kCluster;
+  int single = ((plan_splits_single(c, c->cfg.n_heads_kv, max_len) + kCluster - 1) /
+                kCluster) * kCluster;
+  const int grid = plan_splits_grid(c, c->cfg.n_heads_kv, max_len);
+  if (grid > single) single = grid;
   const int batched = ceil_div(max_len, batch_chunk(c, max_len));
   const int splits = single > batched ? single : batched;
   return ensure_scratch(c, (long long)n_seq * c->cfg.n_heads_q * splits, nullptr);

@@ -123,6 +123,19 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Asks the memory system to bring [p, p + bytes) into L2 (no shared memory, no
+// completion to wait for).  p 16-byte aligned, bytes a multiple of 16.  L2 is
+// the point of coherence, so a line brought in early still sees later writes.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // ---------------------------------------------------------------------------
 // Kernel parameter blocks
 // ---------------------------------------------------------------------------
@@ -197,6 +210,26 @@ struct DecodeParams {
   // and is left at zero -- merges them into `out`.
   int cluster;
   int* counters;
+
+  // Grid merge (single-sequence launches, the GRID instance).  Every CTA
+  // publishes its partial, arrives on *grid_bar and waits (bounded) until all
+  // CTAs of the launch have arrived; each CTA then merges one slice of the
+  // outputs, so the launch leaves the final output and no combine launch is
+  // needed.  grid_bar only grows: a launch of N CTAs takes it from a multiple
+  // of N to the next one, so it never needs resetting.  The launcher makes
+  // sure every CTA of the grid can be resident at once.
+  unsigned long long* grid_bar;
+  // Cache rows of the next layer (same t_max and split plan) to bring into L2
+  // while this launch runs; null for none.  Those rows are never written by
+  // this launch, so fetching them early cannot read stale data.
+  const float* pf_k;
+  const float* pf_v;
+  // When set, CTA 0 stores the next position (pos + 1, wrapping from wrap_hi
+  // back to wrap_lo when wrap_hi > wrap_lo) after every CTA has read pos: the
+  // device-side position advance of a replayed step, folded into its last
+  // layer.
+  int* advance_pos;
+  int wrap_lo, wrap_hi;
 };
 
 struct CombineParams {

@@ -35,6 +35,8 @@ constexpr float kRescaleThresh = 8.0f;           // log2 units
 constexpr long long kWaitBudget = 2000000000LL;  // ~1 s of SM clocks per wait
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kG = 6;                            // q heads per KV head
+constexpr int kGridMaxParts = 256;               // splits per KV head in a grid-merged launch
+constexpr int kGridChunk = 8;                    // partial o loads in flight per thread
 
 // Kernel shape: NW streaming warps per CTA, each with a private ring of NS
 // stages of ST cache rows (K and V).  Instantiated shapes are listed in
@@ -52,8 +54,12 @@ struct DecodeSmem {
   float wla[NW][kG];  // weight * l per warp
   float hm[kG];       // CTA max per head (log2 units)
   float hl[kG];       // CTA sum per head (cluster reduction input)
+  float gw[kGridMaxParts];  // grid merge: weight of every part of the merged head
+  float gred[NW * 32];      // grid merge: per-thread sums
+  float gL;                 // grid merge: the head's L
   uint64_t full[NW][NS];
   int err;
+  int gok;                  // grid merge: every CTA arrived in time
 };
 
 __device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
@@ -261,7 +267,136 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeParams& p, float (*
   if (tid == 0) p.counters[seq * p.n_kv + hkv] = 0;
 }
 
-template <int NW, int ST, int NS, bool FUSED, bool CLUSTER = false>
+// Grid merge of one single-sequence launch (GRID instance).  Every CTA has
+// stored its partial (m in log2 units, l, un-normalised o) for its split and
+// its 6 q heads at part_ml / part_o [q head][split].  The CTAs meet at a
+// barrier on p.grid_bar (one arrival each, bounded wait); then CTA b merges
+// dims [d0, d0 + nd) of q head b / per_head over all splits: warp 0 forms the
+// maximum, the weights and L from every (m, l) while every thread already has
+// its o loads in flight (one L2 round trip), and the sums meet in shared
+// memory.  All q heads are covered when n_splits >= 6 (per_head >= 1); the
+// launcher guarantees that and that every CTA of the grid can be resident at
+// once (the barrier needs all of them running).
+template <int NW, int ST, int NS>
+__device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<NW, ST, NS>& sm,
+                                              int pos) {
+  constexpr int NT = NW * 32;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const unsigned n_cta = gridDim.x * gridDim.y;
+  const int b = (int)(blockIdx.y * gridDim.x + blockIdx.x);
+  __syncthreads();  // every thread's partial stores are issued
+  if (tid == 0) {
+    int ok = 1;
+    __threadfence();
+    const unsigned long long old = atomicAdd(p.grid_bar, 1ULL);
+    const unsigned long long target = (old / n_cta + 1ULL) * n_cta;
+    if (ld_acquire_gpu_u64(p.grid_bar) < target) {
+      const long long start = clock64();
+      while (ld_acquire_gpu_u64(p.grid_bar) < target) {
+        if (clock64() - start > kWaitBudget) {
+          ok = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+    if (!ok) atomicOr(p.status, kStatusWaitTimeout);
+    sm.gok = ok;
+  }
+  __syncthreads();
+  if (!sm.gok) return;
+  if (p.advance_pos && b == 0 && tid == 0) {
+    int nxt = pos + 1;
+    if (p.wrap_hi > p.wrap_lo && nxt >= p.wrap_hi) nxt = p.wrap_lo;
+    *p.advance_pos = nxt;
+  }
+
+  const int n_q = p.n_kv * kG;
+  const int S = p.n_splits;
+  const int per_head = (int)n_cta / n_q;
+  if (per_head < 1) return;
+  const int head = b / per_head;
+  if (head >= n_q) return;
+  const int dps = (kHeadDim + per_head - 1) / per_head;
+  const int d0 = (b % per_head) * dps;
+  const int nd = min(dps, kHeadDim - d0);
+  if (nd <= 0) return;
+  const long long r0 = (long long)head * S;  // this head's first (split) row
+  const int ng = NT / nd;                    // thread groups over the parts
+  const int gi = tid / nd, dd = tid % nd;
+  const float* o_col = p.part_o + r0 * kHeadDim + d0 + dd;
+
+  float ov[kGridChunk];
+#pragma unroll
+  for (int u = 0; u < kGridChunk; ++u) {
+    const int i = gi + u * ng;
+    ov[u] = (gi < ng && i < S) ? __ldcg(o_col + (long long)i * kHeadDim) : 0.f;
+  }
+  if (tid < 32) {
+    constexpr int kPer = kGridMaxParts / 32;
+    float mr[kPer], lr[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = lane + 32 * k;
+      mr[k] = i < S ? __ldcg(p.part_ml + (r0 + i) * 2) : -CUDART_INF_F;
+      lr[k] = i < S ? __ldcg(p.part_ml + (r0 + i) * 2 + 1) : 0.f;
+    }
+    float mx = -CUDART_INF_F;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+      if (lr[k] > 0.f) mx = fmaxf(mx, mr[k]);
+    mx = warp_max(mx);
+    float ls = 0.f;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = lane + 32 * k;
+      if (i < S) {
+        const float w = lr[k] > 0.f ? exp2f(mr[k] - mx) : 0.f;
+        sm.gw[i] = w;
+        ls += w * lr[k];
+      }
+    }
+    ls = warp_sum(ls);
+    if (lane == 0) sm.gL = ls;
+  }
+  __syncthreads();
+  float acc = 0.f;
+  if (gi < ng) {
+#pragma unroll
+    for (int u = 0; u < kGridChunk; ++u) {
+      const int i = gi + u * ng;
+      if (i < S) {
+        const float w = sm.gw[i];
+        if (w != 0.f) acc += w * ov[u];
+      }
+    }
+    for (int i0 = ng * kGridChunk; i0 < S; i0 += ng * kGridChunk) {
+#pragma unroll
+      for (int u = 0; u < kGridChunk; ++u) {
+        const int i = i0 + gi + u * ng;
+        ov[u] = i < S ? __ldcg(o_col + (long long)i * kHeadDim) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kGridChunk; ++u) {
+        const int i = i0 + gi + u * ng;
+        if (i < S) {
+          const float w = sm.gw[i];
+          if (w != 0.f) acc += w * ov[u];
+        }
+      }
+    }
+  }
+  sm.gred[tid] = acc;
+  __syncthreads();
+  if (tid < nd) {
+    float s = 0.f;
+    for (int g = 0; g < ng; ++g) s += sm.gred[g * nd + tid];
+    const float L = sm.gL;
+    p.out[(long long)head * kHeadDim + d0 + tid] = L > 0.f ? s / L : 0.f;
+  }
+}
+
+template <int NW, int ST, int NS, bool FUSED, bool CLUSTER = false, bool GRID = false>
 __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     decode_split_kernel(const DecodeParams p) {
   constexpr int G = kG;
@@ -280,6 +415,11 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   // preceding kernel, e.g. the device pos advanced at the end of a step).
   // The unfused kernel usually follows rope_append, which writes row pos.
   const bool early = FUSED && p.lengths_stable != 0;
+  // A grid-merged launch lets the next kernel's CTAs become resident (and
+  // start their own cache streaming) while it runs: they are launched only
+  // once every CTA of this grid is running, so they can never keep one of
+  // this grid's CTAs (and with it the merge barrier) waiting for an SM.
+  if constexpr (GRID) pdl_launch_dependents();
   if (!early) pdl_wait();
 
   int pos, seq_len;
@@ -300,10 +440,10 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   const int c1 = min(c0 + chunk, r_end);
   const long long prow = ((long long)seq * n_q + hkv * G) * p.n_splits + split;
 
-  if (!CLUSTER && c0 >= r_end) {
+  if (!CLUSTER && !GRID && c0 >= r_end) {
     // Empty split (short sequence in a batch planned for the longest one).
-    // (In cluster mode empty CTAs run through with no rows: they must still
-    // take part in the cluster barriers.)
+    // (In cluster and grid-merge modes empty CTAs run through with no rows:
+    // they must still take part in the barriers and the merge.)
     if (early) pdl_wait();
     pdl_launch_dependents();
     if (tid < G) {
@@ -356,6 +496,22 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   if (lane == 0) {
     for (int s = 0; s < NS && s < n_it; ++s) issue(s, s);
   }
+  if constexpr (GRID) {
+    // The next layer's rows of this warp's range, into L2 (its own launch
+    // then streams them from L2), and this launch's q and new row, which are
+    // read right after the dependency wait.
+    if (lane == 0 && p.pf_k != nullptr && n_tok > 0 && early) {
+      const long long off = ((long long)hkv * p.t_max + w0) * kHeadDim;
+      bulk_prefetch_l2(p.pf_k + off, (uint32_t)n_tok * kRowBytes);
+      bulk_prefetch_l2(p.pf_v + off, (uint32_t)n_tok * kRowBytes);
+    }
+    if (tid == 32 && early) {
+      const float* qin = p.qkv + (long long)seq * p.qkv_stride;
+      bulk_prefetch_l2(qin + (long long)hkv * G * kHeadDim, G * kRowBytes);
+      bulk_prefetch_l2(qin + (long long)(n_q + hkv) * kHeadDim, kRowBytes);
+      bulk_prefetch_l2(qin + (long long)(n_q + p.n_kv + hkv) * kHeadDim, kRowBytes);
+    }
+  }
 
   // RoPE angle table (cos, sin per rotation pair).  When pos is known before
   // the dependency wait, it is built while the previous kernel finishes.
@@ -370,7 +526,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   };
   if (FUSED && early) rope_table();
   if (early) pdl_wait();
-  pdl_launch_dependents();
+  if constexpr (!GRID) pdl_launch_dependents();
   if (FUSED && !early) rope_table();
 
   // ---- q (and the new k/v row) straight into registers --------------------
@@ -621,7 +777,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     reinterpret_cast<float4*>(ow + h * kHeadDim)[lane] =
         make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
   __syncthreads();
-  if (!CLUSTER && sm.err) return;
+  if (!CLUSTER && !GRID && sm.err) return;
 
   // ---- merge the warps: weights once per (warp, head), then one pass ----
   if (tid < NW * G) {
@@ -665,6 +821,15 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
       // is free by now) for the cluster reduction below.
       sm.q[h][d] = O;
       if (d == 0) sm.hl[h] = (sm.err || M == -CUDART_INF_F) ? 0.f : Lsum;
+    } else if constexpr (GRID) {
+      // Log2 units: the grid merge below is the only reader.  A CTA that
+      // failed publishes an empty partial (l = 0) but still takes part.
+      const long long r = ((long long)(hkv * G + h)) * p.n_splits + split;
+      p.part_o[r * kHeadDim + d] = O;
+      if (d == 0) {
+        p.part_ml[r * 2 + 0] = M;
+        p.part_ml[r * 2 + 1] = (sm.err || M == -CUDART_INF_F) ? 0.f : Lsum;
+      }
     } else if (p.out != nullptr && p.n_splits == 1) {
       p.out[(long long)seq * p.out_stride + (long long)(hkv * G + h) * kHeadDim + d] =
           Lsum > 0.f ? O / Lsum : 0.f;
@@ -678,6 +843,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     }
   }
   if constexpr (CLUSTER) cluster_epilogue<NT>(p, sm.q, sm.hm, sm.hl, seq, hkv);
+  if constexpr (GRID) grid_epilogue<NW, ST, NS>(p, sm, pos);
 }
 
 // Log-sum-exp merge of n_parts partials per output row (merge_partials in
@@ -795,26 +961,32 @@ struct Variant {
   const void* fused;
   const void* unfused;
   const void* fused_cluster;
+  const void* fused_grid;  // grid-merged instance (null where not built)
   int threads;
   int quant;
+  int grid_quant;          // row quantum of a grid-merged split
   size_t smem;
 };
 
-template <int NW, int ST, int NS>
+template <int NW, int ST, int NS, bool WITH_GRID = false>
 static Variant make_variant() {
   Variant v;
   v.fused = (const void*)decode_split_kernel<NW, ST, NS, true>;
   v.unfused = (const void*)decode_split_kernel<NW, ST, NS, false>;
   v.fused_cluster = (const void*)decode_split_kernel<NW, ST, NS, true, true>;
+  v.fused_grid = nullptr;
+  if constexpr (WITH_GRID)
+    v.fused_grid = (const void*)decode_split_kernel<NW, ST, NS, true, false, true>;
   v.threads = NW * 32;
   v.quant = NW * ST > 32 ? NW * ST : 32;
+  v.grid_quant = ST > 8 ? ST : 8;
   v.smem = sizeof(DecodeSmem<NW, ST, NS>);
   return v;
 }
 
 static const Variant& decode_variant(int i) {
   static const Variant table[] = {
-      make_variant<8, 4, 3>(),  // 0: 256 threads, 12 KB ring per warp, 2 CTAs/SM
+      make_variant<8, 4, 3, true>(),  // 0: 256 threads, 12 KB ring per warp, 2 CTAs/SM
       make_variant<4, 8, 3>(),  // 1: 128 threads, 24 KB ring per warp, 2 CTAs/SM
       make_variant<4, 4, 4>(),  // 2: 128 threads, 16 KB ring per warp, 3 CTAs/SM
       make_variant<8, 8, 2>(),  // 3: 256 threads, 32 KB ring per warp, 1 CTA/SM
@@ -828,6 +1000,22 @@ static const Variant& decode_variant(int i) {
 
 int decode_variant_count() { return 7; }
 int decode_variant_quant(int i) { return decode_variant(i).quant; }
+int decode_variant_grid_quant(int i) { return decode_variant(i).grid_quant; }
+
+// CTAs of the grid-merged instance of variant i that fit on one SM (0: not
+// built).  The grid merge's barrier needs every CTA of a launch resident at
+// once, so a launch may use at most n_sm x this many CTAs.
+int decode_grid_ctas_per_sm(int i) {
+  const Variant& v = decode_variant(i);
+  if (!v.fused_grid) return 0;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, v.fused_grid, v.threads, v.smem) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
 
 static cudaError_t launch_ex(const void* fn, dim3 grid, dim3 block, size_t smem,
                              cudaStream_t st, bool pdl, void** args) {
@@ -855,6 +1043,9 @@ cudaError_t prepare_decode_kernels() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(v.fused_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)v.smem);
+    if (e == cudaSuccess && v.fused_grid)
+      e = cudaFuncSetAttribute(v.fused_grid, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)v.smem);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -867,6 +1058,14 @@ cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cu
   DecodeParams copy = p;
   copy.quant = v.quant;
   void* args[] = {&copy};
+  if (p.grid_bar != nullptr) {
+    // Grid-merged single-sequence launch: the output is final when it ends.
+    if (!fused || n_seq != 1 || !v.fused_grid || p.n_splits < kG ||
+        p.n_splits > kGridMaxParts || p.out == nullptr)
+      return cudaErrorInvalidValue;
+    copy.quant = v.grid_quant;
+    return launch_ex(v.fused_grid, grid, dim3(v.threads), v.smem, st, pdl, args);
+  }
   if (p.cluster > 1) {
     if (!fused || p.n_splits % p.cluster != 0 || p.cluster > 8) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};

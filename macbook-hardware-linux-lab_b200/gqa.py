@@ -38,6 +38,9 @@ GQA_OPT_PDL = 1
 GQA_OPT_TARGET_CTAS = 2
 GQA_OPT_BATCH_CHUNK = 3
 GQA_OPT_KERNEL_VARIANT = 4
+GQA_OPT_LAYERS_PDL = 5   # tuning knobs (internal): PDL inside the layer loop,
+GQA_OPT_CLUSTER = 6      # the cluster reduction,
+GQA_OPT_GRID_MERGE = 7   # the grid-merged single-sequence decode (default on)
 # rows per split quantum of each decode kernel variant (csrc/gqa_decode.cu)
 VARIANT_QUANT = {0: 32, 1: 32, 2: 32, 3: 64, 4: 32, 5: 64, 6: 32}
 

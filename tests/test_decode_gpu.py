@@ -394,7 +394,8 @@ def test_cluster_reduction_matches_oracle(pkg, orc, cuda, variant, cluster):
     t_max = 4096
     with pkg.Context(t_max=t_max) as ctx:
         ctx.set_option(pkg.gqa.GQA_OPT_KERNEL_VARIANT, variant)
-        ctx.set_option(6, cluster)
+        ctx.set_option(pkg.gqa.GQA_OPT_GRID_MERGE, 0)
+        ctx.set_option(pkg.gqa.GQA_OPT_CLUSTER, cluster)
         for pos, seq_len in [(4095, 4096), (3000, 3001), (300, 301), (256, 257), (4000, 2000)]:
             for rep in range(2):
                 qkv, kc, vc = pkg.seeded.decode_inputs(7000 + pos + rep, t_max)
@@ -405,4 +406,30 @@ def test_cluster_reduction_matches_oracle(pkg, orc, cuda, variant, cluster):
                 torch.cuda.synchronize()
                 assert nerr(d_qkv[:1536].cpu().numpy(), rq[:1536]) <= TOL, (pos, seq_len, rep)
                 assert np.abs(d_k[:, pos].cpu().numpy() - rk[:, pos]).max() <= 1e-5
+        assert ctx.device_status() == 0
+
+
+@pytest.mark.parametrize("target_ctas", [0, 12, 40, 148])
+def test_grid_merge_matches_oracle(pkg, orc, cuda, target_ctas):
+    """Single-sequence decode merged inside the split kernel (grid barrier, one
+    merge slice per CTA): lengths from below the 6-split minimum (which falls
+    back to split + combine) to t_max, a row appended outside the attended
+    range, and repeated calls so the barrier counter keeps counting."""
+    torch = cuda
+    t_max = 4096
+    with pkg.Context(t_max=t_max) as ctx:
+        if target_ctas:
+            ctx.set_option(pkg.gqa.GQA_OPT_TARGET_CTAS, target_ctas)
+        for pos, seq_len in [(4095, 4096), (3840, 3841), (1000, 1001), (47, 48), (40, 41),
+                             (4000, 2000), (0, 1)]:
+            for rep in range(2):
+                qkv, kc, vc = pkg.seeded.decode_inputs(9100 + pos + rep, t_max)
+                rq, rk, rv = qkv.copy(), kc.copy(), vc.copy()
+                orc.layer_attention(rq, rk, rv, pos, seq_len)
+                d_qkv, d_k, d_v = to_dev(torch, qkv), to_dev(torch, kc), to_dev(torch, vc)
+                ctx.layer_attention(pkg.kv_of(d_k, d_v), d_qkv, pos, seq_len)
+                torch.cuda.synchronize()
+                assert nerr(d_qkv[:1536].cpu().numpy(), rq[:1536]) <= TOL, (pos, seq_len, rep)
+                assert np.abs(d_k[:, pos].cpu().numpy() - rk[:, pos]).max() <= 1e-5
+                assert np.array_equal(d_v[:, pos].cpu().numpy(), rv[:, pos])
         assert ctx.device_status() == 0
