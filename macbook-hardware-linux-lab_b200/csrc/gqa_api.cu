@@ -26,6 +26,7 @@ int decode_variant_quant(int variant);
 int decode_variant_grid_quant(int variant);
 int decode_grid_ctas_per_sm(int variant);
 cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl);
+cudaError_t launch_combine_wide(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl);
 cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k_ptrs,
                                float* const* v_ptrs, float* k_base, float* v_base,
                                long long seq_stride, Lengths len, int t_max, int n_q, int n_kv,
@@ -126,12 +127,13 @@ struct gqa_ctx {
   // the final merge).
   int cluster = 0;
   int* counters = nullptr;  // [kCounterSlots] arrival / item counters, kept at zero
-  // Grid-merged single-sequence decode (one launch per layer call, the merge
-  // done by the split kernel's CTAs after a barrier on grid_bar).  On by
-  // default; off falls back to split kernel + combine kernel.
+  // Grid-merged single-sequence decode (one launch per layer call: the split
+  // kernel's CTAs merge each other's epoch-tagged partials).  On by default;
+  // off falls back to split kernel + combine kernel.
   int grid_merge = 1;
-  int grid_ctas_per_sm = 0;                 // resident CTAs of the grid instance per SM
-  unsigned long long* grid_bar = nullptr;   // device barrier counter (only grows)
+  int grid_ctas_per_sm = 0;                   // resident CTAs of the grid instance per SM
+  unsigned* grid_epoch = nullptr;             // [kGridEpochWords] per-KV-head launch epochs
+  unsigned long long* grid_words = nullptr;   // tagged partials [n_q][kGridMaxParts][row]
   float* blk_qkv = nullptr;   // attention block workspace: qkv of the token
   float* blk_attn = nullptr;  // attention block workspace: attention output
   float* blk_h = nullptr;     // FFN workspace: silu(gate) * up
@@ -258,9 +260,10 @@ int grid_variant(const gqa_ctx* c) { return c->variant >= 0 ? c->variant : 0; }
 // the grid merge cannot be used: at least 6 splits (one merge slice per q
 // head), at most kGridMaxSplits, and every CTA of the launch resident at once
 // with room for the next launch's CTAs (at most one CTA per SM when two fit).
-constexpr int kGridMaxSplits = 256;  // = kGridMaxParts of the kernel
 int plan_splits_grid(const gqa_ctx* c, int rows_kv, int len) {
-  if (!c->grid_merge || c->generic || c->grid_ctas_per_sm < 1) return 0;
+  if (!c->grid_merge || c->generic || c->grid_ctas_per_sm < 1 || !c->grid_words ||
+      rows_kv > kGridEpochWords)
+    return 0;
   const int quant = decode_variant_grid_quant(grid_variant(c));
   const int per_sm = c->grid_ctas_per_sm >= 2 ? 1 : c->grid_ctas_per_sm;
   const int cap = c->n_sm * per_sm;
@@ -268,7 +271,7 @@ int plan_splits_grid(const gqa_ctx* c, int rows_kv, int len) {
   int want = target / rows_kv;
   const int most = ceil_div(len, quant);
   if (want > most) want = most;
-  if (want > kGridMaxSplits) want = kGridMaxSplits;
+  if (want > kGridMaxParts) want = kGridMaxParts;
   return want >= 6 ? want : 0;
 }
 
@@ -316,26 +319,15 @@ int check_kv(const gqa_ctx* c, const gqa_layer_kv* kv) {
   return GQA_OK;
 }
 
-// Position advance folded into a grid-merged launch (see DecodeParams).
-struct Advance {
-  int* pos = nullptr;
-  int wrap_lo = 0, wrap_hi = 0;
-};
-
 // One sequence: split kernel (+ combine when split), result to `out`.  When
-// the grid merge applies, one launch does both; it then also brings
-// `next_kv`'s rows (if any) into L2 and performs `adv` (if any), and
-// *advanced is set.  Otherwise the caller still owes the advance.
+// the grid merge applies, one launch does both, and it also brings
+// `next_kv`'s rows (if any) into L2 for the next layer's launch.
 int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
                Lengths len, int plan_len, bool fused, float* out, bool pdl_first,
-               bool lengths_stable, const gqa_layer_kv* next_kv = nullptr,
-               const Advance* adv = nullptr, bool* advanced = nullptr) {
+               bool lengths_stable, const gqa_layer_kv* next_kv = nullptr) {
   const int n_kv = c->cfg.n_heads_kv;
-  if (advanced) *advanced = false;
   const int grid_splits = (fused && out != nullptr) ? plan_splits_grid(c, n_kv, plan_len) : 0;
   if (grid_splits > 0) {
-    int rc = ensure_scratch(c, (long long)c->cfg.n_heads_q * grid_splits, st);
-    if (rc != GQA_OK) return rc;
     DecodeParams p = base_params(c);
     p.k_base = kv->k_cache;
     p.v_base = kv->v_cache;
@@ -345,16 +337,11 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
     p.n_splits = grid_splits;
     p.min_chunk = decode_variant_grid_quant(grid_variant(c));
     p.out = out;
-    p.grid_bar = c->grid_bar;
+    p.grid_epoch = c->grid_epoch;
+    p.grid_words = c->grid_words;
     if (next_kv) {
       p.pf_k = next_kv->k_cache;
       p.pf_v = next_kv->v_cache;
-    }
-    if (adv && adv->pos) {
-      p.advance_pos = adv->pos;
-      p.wrap_lo = adv->wrap_lo;
-      p.wrap_hi = adv->wrap_hi;
-      if (advanced) *advanced = true;
     }
     GQA_CUDA(launch_decode_split(p, 1, true, st, pdl_first, grid_variant(c)));
     return GQA_OK;
@@ -381,7 +368,7 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
   if (n_splits > 1 && !use_cluster) {
     CombineParams cp = combine_from_scratch(c, n_splits);
     cp.out = out;
-    GQA_CUDA(launch_combine(cp, 1, st, c->layers_pdl != 0));
+    GQA_CUDA(launch_combine_wide(cp, 1, st, c->layers_pdl != 0));
   }
   return GQA_OK;
 }
@@ -428,18 +415,11 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
   }
   Lengths len{};
   len.pos_dev = d_pos;
-  Advance adv;
-  adv.pos = advance ? d_pos : nullptr;
-  adv.wrap_lo = wrap_lo;
-  adv.wrap_hi = wrap_hi;
-  bool advanced = false;
   for (int l = 0; l < n_layers; ++l) {
     // Layer 0 is launched without programmatic overlap, so whatever advanced
     // *d_pos before it has finished and it may read pos (and stream its
     // cache rows) at once.  Later layers follow a kernel of the previous
-    // layer, which never writes pos or this layer's cache (the advance, when
-    // folded into the last layer, happens after all of that layer's CTAs
-    // have read pos).
+    // layer, which never writes pos or this layer's cache.
     const bool pdl = l > 0 && c->layers_pdl != 0;
     const bool last = l == n_layers - 1;
     int rc = c->generic
@@ -447,11 +427,10 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
                                out + l * out_stride, pdl, /*lengths_stable=*/true)
                  : run_single(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max, true,
                               out + l * out_stride, pdl, /*lengths_stable=*/true,
-                              last ? nullptr : &kv[l + 1], last ? &adv : nullptr,
-                              last ? &advanced : nullptr);
+                              last ? nullptr : &kv[l + 1]);
     if (rc != GQA_OK) return rc;
   }
-  if (advance && !advanced) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
+  if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
   return GQA_OK;
 }
 
@@ -656,8 +635,14 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess) e = prepare_head_kernels();
   if (e == cudaSuccess) e = cudaMalloc(&c->counters, sizeof(int) * kCounterSlots);
   if (e == cudaSuccess) e = cudaMemset(c->counters, 0, sizeof(int) * kCounterSlots);
-  if (e == cudaSuccess) e = cudaMalloc(&c->grid_bar, sizeof(unsigned long long));
-  if (e == cudaSuccess) e = cudaMemset(c->grid_bar, 0, sizeof(unsigned long long));
+  // Epoch-tagged grid-merge partials: zeroed here and written by nothing else,
+  // so no stale word ever carries a current epoch.
+  const size_t grid_words_bytes =
+      sizeof(unsigned long long) * (size_t)cfg->n_heads_q * kGridMaxParts * kGridRowWords;
+  if (e == cudaSuccess) e = cudaMalloc(&c->grid_epoch, kGridEpochWords * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(c->grid_epoch, 0, kGridEpochWords * sizeof(unsigned));
+  if (e == cudaSuccess && tuned) e = cudaMalloc(&c->grid_words, grid_words_bytes);
+  if (e == cudaSuccess && tuned) e = cudaMemset(c->grid_words, 0, grid_words_bytes);
   if (e == cudaSuccess) c->grid_ctas_per_sm = decode_grid_ctas_per_sm(grid_variant(c));
   if (e == cudaSuccess) {
     c->head_grid = lm_head_grid(c->n_sm);
@@ -680,7 +665,8 @@ int gqa_destroy(gqa_ctx* c) {
   if (c->inv_freq) cudaFree(c->inv_freq);
   if (c->status) cudaFree(c->status);
   if (c->counters) cudaFree(c->counters);
-  if (c->grid_bar) cudaFree(c->grid_bar);
+  if (c->grid_epoch) cudaFree(c->grid_epoch);
+  if (c->grid_words) cudaFree(c->grid_words);
   if (c->blk_qkv) cudaFree(c->blk_qkv);
   if (c->blk_attn) cudaFree(c->blk_attn);
   if (c->blk_h) cudaFree(c->blk_h);

@@ -130,9 +130,29 @@ __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) 
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+// One 64-bit word {float bits (low half), tag (high half)}, stored and loaded
+// whole: a scalar 64-bit access is single-copy atomic, so a reader that sees
+// the tag of a store also sees its value.  No fence is implied.
+__device__ __forceinline__ void st_tagged(unsigned long long* p, float v, unsigned tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+__device__ __forceinline__ unsigned tag_of(unsigned long long w) { return (unsigned)(w >> 32); }
+__device__ __forceinline__ float value_of(unsigned long long w) {
+  return __uint_as_float((unsigned)w);
+}
+
+__device__ __forceinline__ void st_relaxed_gpu(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_relaxed_gpu_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
@@ -151,6 +171,13 @@ struct Lengths {
   int pos_imm;
   int seqlen_imm;
 };
+
+// Grid-merged partials: per (q head, split) one row of kGridRowWords tagged
+// words, o[0..127] then m and l; 144 words (1152 bytes, 9 x 128) keep every
+// 16-dim slice of a row inside one 128-byte line.
+constexpr int kGridRowWords = 144;
+constexpr int kGridMaxParts = 128;   // splits per KV head in a grid-merged launch
+constexpr int kGridEpochWords = 64;  // per-KV-head epochs of one context (n_kv <= 64)
 
 struct DecodeParams {
   // KV caches.  Per sequence s the cache is k_ptrs[s] (device array of
@@ -212,24 +239,24 @@ struct DecodeParams {
   int* counters;
 
   // Grid merge (single-sequence launches, the GRID instance).  Every CTA
-  // publishes its partial, arrives on *grid_bar and waits (bounded) until all
-  // CTAs of the launch have arrived; each CTA then merges one slice of the
-  // outputs, so the launch leaves the final output and no combine launch is
-  // needed.  grid_bar only grows: a launch of N CTAs takes it from a multiple
-  // of N to the next one, so it never needs resetting.  The launcher makes
-  // sure every CTA of the grid can be resident at once.
-  unsigned long long* grid_bar;
+  // stores its partial as tagged words (value, epoch) in grid_words
+  // [q head][split][kGridRowWords]; each CTA then merges a slice of the
+  // outputs, polling (bounded) the words it needs until they carry this
+  // launch's epoch, so the launch leaves the final output with no barrier,
+  // fence or combine launch.  The epoch of KV head h is grid_epoch[h] + 1,
+  // read after the dependency wait; a merging CTA stores it back once it has
+  // seen every split of its KV head, i.e. once every CTA of that KV head has
+  // read the old value.  Both buffers start at zero and are used by no other
+  // path, so a stale word never carries a current epoch.  The launcher makes
+  // sure every CTA of the grid can be resident at once (mergers wait on the
+  // others).
+  unsigned* grid_epoch;
+  unsigned long long* grid_words;
   // Cache rows of the next layer (same t_max and split plan) to bring into L2
   // while this launch runs; null for none.  Those rows are never written by
   // this launch, so fetching them early cannot read stale data.
   const float* pf_k;
   const float* pf_v;
-  // When set, CTA 0 stores the next position (pos + 1, wrapping from wrap_hi
-  // back to wrap_lo when wrap_hi > wrap_lo) after every CTA has read pos: the
-  // device-side position advance of a replayed step, folded into its last
-  // layer.
-  int* advance_pos;
-  int wrap_lo, wrap_hi;
 };
 
 struct CombineParams {

@@ -35,8 +35,6 @@ constexpr float kRescaleThresh = 8.0f;           // log2 units
 constexpr long long kWaitBudget = 2000000000LL;  // ~1 s of SM clocks per wait
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kG = 6;                            // q heads per KV head
-constexpr int kGridMaxParts = 256;               // splits per KV head in a grid-merged launch
-constexpr int kGridChunk = 8;                    // partial o loads in flight per thread
 
 // Kernel shape: NW streaming warps per CTA, each with a private ring of NS
 // stages of ST cache rows (K and V).  Instantiated shapes are listed in
@@ -54,12 +52,11 @@ struct DecodeSmem {
   float wla[NW][kG];  // weight * l per warp
   float hm[kG];       // CTA max per head (log2 units)
   float hl[kG];       // CTA sum per head (cluster reduction input)
-  float gw[kGridMaxParts];  // grid merge: weight of every part of the merged head
-  float gred[NW * 32];      // grid merge: per-thread sums
-  float gL;                 // grid merge: the head's L
+  SliceSmem<kGridMaxParts> slice;  // grid merge
   uint64_t full[NW][NS];
   int err;
-  int gok;                  // grid merge: every CTA arrived in time
+  int gok;                  // grid merge: every word of the slice arrived in time
+  unsigned gep;             // grid merge: this launch's epoch
 };
 
 __device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
@@ -268,131 +265,132 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeParams& p, float (*
 }
 
 // Grid merge of one single-sequence launch (GRID instance).  Every CTA has
-// stored its partial (m in log2 units, l, un-normalised o) for its split and
-// its 6 q heads at part_ml / part_o [q head][split].  The CTAs meet at a
-// barrier on p.grid_bar (one arrival each, bounded wait); then CTA b merges
-// dims [d0, d0 + nd) of q head b / per_head over all splits: warp 0 forms the
-// maximum, the weights and L from every (m, l) while every thread already has
-// its o loads in flight (one L2 round trip), and the sums meet in shared
-// memory.  All q heads are covered when n_splits >= 6 (per_head >= 1); the
-// launcher guarantees that and that every CTA of the grid can be resident at
-// once (the barrier needs all of them running).
+// stored its partial for its split and its 6 q heads as tagged words (value,
+// epoch) at grid_words [q head][split][kGridRowWords] (o[128], m in log2
+// units, l).  The 48 slices (6 q heads x 8 slices of 16 dims) of a KV head are
+// merged by that KV head's CTAs, CTA `split` taking slices split, split +
+// n_splits, ...  A merging thread polls (bounded) the words it needs until
+// all carry this launch's epoch -- there is no barrier and no fence: a word
+// whose tag is current holds its value (one 64-bit store).  Half-warp hw
+// takes parts hw, hw + 16, ... of dim d0 + (lane & 15) (coalesced 128-byte
+// rows); warp 0 settles every (m, l) word and forms the maximum, the weights
+// and L; the sums meet by one shuffle and in shared memory.  Once warp 0 has
+// seen every split's (m, l), every CTA of the KV head has read the epoch, so
+// the merging CTA may store it back for the next launch.
 template <int NW, int ST, int NS>
 __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<NW, ST, NS>& sm,
-                                              int pos) {
-  constexpr int NT = NW * 32;
-  const int tid = threadIdx.x, lane = tid & 31;
-  const unsigned n_cta = gridDim.x * gridDim.y;
-  const int b = (int)(blockIdx.y * gridDim.x + blockIdx.x);
-  __syncthreads();  // every thread's partial stores are issued
-  if (tid == 0) {
-    int ok = 1;
-    __threadfence();
-    const unsigned long long old = atomicAdd(p.grid_bar, 1ULL);
-    const unsigned long long target = (old / n_cta + 1ULL) * n_cta;
-    if (ld_acquire_gpu_u64(p.grid_bar) < target) {
-      const long long start = clock64();
-      while (ld_acquire_gpu_u64(p.grid_bar) < target) {
-        if (clock64() - start > kWaitBudget) {
-          ok = 0;
-          break;
-        }
-      }
-    }
-    __threadfence();
-    if (!ok) atomicOr(p.status, kStatusWaitTimeout);
-    sm.gok = ok;
-  }
-  __syncthreads();
-  if (!sm.gok) return;
-  if (p.advance_pos && b == 0 && tid == 0) {
-    int nxt = pos + 1;
-    if (p.wrap_hi > p.wrap_lo && nxt >= p.wrap_hi) nxt = p.wrap_lo;
-    *p.advance_pos = nxt;
-  }
-
-  const int n_q = p.n_kv * kG;
+                                              int hkv, int split, unsigned ep) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hw = tid >> 4, j = tid & 15;
+  constexpr int kGroups = kSliceThreads / 16;
+  static_assert(NW * 32 == kSliceThreads, "the grid merge maps 256 threads");
+  static_assert(kGroups * kSliceChunk == kGridMaxParts, "parts held in registers");
+  constexpr int kSlices = kHeadDim / kSliceDims;
   const int S = p.n_splits;
-  const int per_head = (int)n_cta / n_q;
-  if (per_head < 1) return;
-  const int head = b / per_head;
-  if (head >= n_q) return;
-  const int dps = (kHeadDim + per_head - 1) / per_head;
-  const int d0 = (b % per_head) * dps;
-  const int nd = min(dps, kHeadDim - d0);
-  if (nd <= 0) return;
-  const long long r0 = (long long)head * S;  // this head's first (split) row
-  const int ng = NT / nd;                    // thread groups over the parts
-  const int gi = tid / nd, dd = tid % nd;
-  const float* o_col = p.part_o + r0 * kHeadDim + d0 + dd;
+  for (int s = split; s < kG * kSlices; s += S) {
+    const int head = hkv * kG + s / kSlices;
+    const int d0 = (s % kSlices) * kSliceDims;
+    const unsigned long long* rows = p.grid_words + (long long)head * S * kGridRowWords;
+    if (s != split) __syncthreads();  // the previous slice's shared memory is free
+    if (tid == 0) sm.gok = 1;
 
-  float ov[kGridChunk];
+    unsigned long long wo[kSliceChunk];
 #pragma unroll
-  for (int u = 0; u < kGridChunk; ++u) {
-    const int i = gi + u * ng;
-    ov[u] = (gi < ng && i < S) ? __ldcg(o_col + (long long)i * kHeadDim) : 0.f;
-  }
-  if (tid < 32) {
+    for (int k = 0; k < kSliceChunk; ++k) {
+      const int i = hw + kGroups * k;
+      wo[k] = i < S ? ld_tagged(rows + (long long)i * kGridRowWords + d0 + j) : 0ull;
+    }
     constexpr int kPer = kGridMaxParts / 32;
-    float mr[kPer], lr[kPer];
+    unsigned long long wm[kPer], wl[kPer];
+    if (warp == 0) {
 #pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int i = lane + 32 * k;
-      mr[k] = i < S ? __ldcg(p.part_ml + (r0 + i) * 2) : -CUDART_INF_F;
-      lr[k] = i < S ? __ldcg(p.part_ml + (r0 + i) * 2 + 1) : 0.f;
-    }
-    float mx = -CUDART_INF_F;
-#pragma unroll
-    for (int k = 0; k < kPer; ++k)
-      if (lr[k] > 0.f) mx = fmaxf(mx, mr[k]);
-    mx = warp_max(mx);
-    float ls = 0.f;
-#pragma unroll
-    for (int k = 0; k < kPer; ++k) {
-      const int i = lane + 32 * k;
-      if (i < S) {
-        const float w = lr[k] > 0.f ? exp2f(mr[k] - mx) : 0.f;
-        sm.gw[i] = w;
-        ls += w * lr[k];
+      for (int k = 0; k < kPer; ++k) {
+        const int i = lane + 32 * k;
+        wm[k] = i < S ? ld_tagged(rows + (long long)i * kGridRowWords + kHeadDim) : 0ull;
+        wl[k] = i < S ? ld_tagged(rows + (long long)i * kGridRowWords + kHeadDim + 1) : 0ull;
       }
     }
-    ls = warp_sum(ls);
-    if (lane == 0) sm.gL = ls;
-  }
-  __syncthreads();
-  float acc = 0.f;
-  if (gi < ng) {
+    bool ok = true;
+    const long long t0 = clock64();
+    for (;;) {
+      bool fresh = true;
 #pragma unroll
-    for (int u = 0; u < kGridChunk; ++u) {
-      const int i = gi + u * ng;
-      if (i < S) {
-        const float w = sm.gw[i];
-        if (w != 0.f) acc += w * ov[u];
-      }
-    }
-    for (int i0 = ng * kGridChunk; i0 < S; i0 += ng * kGridChunk) {
-#pragma unroll
-      for (int u = 0; u < kGridChunk; ++u) {
-        const int i = i0 + gi + u * ng;
-        ov[u] = i < S ? __ldcg(o_col + (long long)i * kHeadDim) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < kGridChunk; ++u) {
-        const int i = i0 + gi + u * ng;
-        if (i < S) {
-          const float w = sm.gw[i];
-          if (w != 0.f) acc += w * ov[u];
+      for (int k = 0; k < kSliceChunk; ++k) {
+        const int i = hw + kGroups * k;
+        if (i < S && tag_of(wo[k]) != ep) {
+          fresh = false;
+          wo[k] = ld_tagged(rows + (long long)i * kGridRowWords + d0 + j);
         }
       }
+      if (warp == 0) {
+#pragma unroll
+        for (int k = 0; k < kPer; ++k) {
+          const int i = lane + 32 * k;
+          if (i < S && tag_of(wm[k]) != ep) {
+            fresh = false;
+            wm[k] = ld_tagged(rows + (long long)i * kGridRowWords + kHeadDim);
+          }
+          if (i < S && tag_of(wl[k]) != ep) {
+            fresh = false;
+            wl[k] = ld_tagged(rows + (long long)i * kGridRowWords + kHeadDim + 1);
+          }
+        }
+      }
+      if (fresh) break;
+      if (clock64() - t0 > kWaitBudget) {
+        ok = false;
+        break;
+      }
     }
-  }
-  sm.gred[tid] = acc;
-  __syncthreads();
-  if (tid < nd) {
-    float s = 0.f;
-    for (int g = 0; g < ng; ++g) s += sm.gred[g * nd + tid];
-    const float L = sm.gL;
-    p.out[(long long)head * kHeadDim + d0 + tid] = L > 0.f ? s / L : 0.f;
+    if (!ok) sm.gok = 0;  // benign race: every writer stores 0
+    if (warp == 0) {
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int k = 0; k < kPer; ++k)
+        if (lane + 32 * k < S && value_of(wl[k]) > 0.f) mx = fmaxf(mx, value_of(wm[k]));
+      mx = warp_max(mx);
+      float ls = 0.f;
+#pragma unroll
+      for (int k = 0; k < kPer; ++k) {
+        const int i = lane + 32 * k;
+        if (i < S) {
+          const float l = value_of(wl[k]);
+          const float w = l > 0.f ? exp2f(value_of(wm[k]) - mx) : 0.f;
+          sm.slice.w[i] = w;
+          ls += w * l;
+        }
+      }
+      ls = warp_sum(ls);
+      if (lane == 0) sm.slice.L = ls;
+    }
+    __syncthreads();
+    if (!sm.gok) {
+      if (tid == 0) atomicOr(p.status, kStatusWaitTimeout);
+      return;
+    }
+    // Every split of this KV head has stored its (m, l): all of its CTAs have
+    // read the epoch, which may now advance (every merging CTA stores the
+    // same value).
+    if (tid == 0) st_relaxed_gpu(p.grid_epoch + hkv, ep);
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < kSliceChunk; ++k) {
+      const int i = hw + kGroups * k;
+      if (i < S) {
+        const float w = sm.slice.w[i];
+        if (w != 0.f) acc += w * value_of(wo[k]);
+      }
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+    if (lane < 16) sm.slice.red[warp][j] = acc;
+    __syncthreads();
+    if (tid < kSliceDims) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kSliceThreads / 32; ++w) sum += sm.slice.red[w][tid];
+      const float L = sm.slice.L;
+      p.out[(long long)head * kHeadDim + d0 + tid] = L > 0.f ? sum / L : 0.f;
+    }
   }
 }
 
@@ -539,6 +537,9 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     for (int i = tid; i < G * kHeadDim / 4; i += NT)
       reinterpret_cast<float4*>(&sm.q[0][0])[i] = __ldcg(qg + i);
   }
+  // This launch's epoch for the tagged partials (read after the wait: the
+  // previous launch, which may have advanced it, has finished).
+  if (GRID && tid == 0) sm.gep = ld_relaxed_gpu_u32(p.grid_epoch + hkv) + 1u;
   const bool pos_attended = pos >= p.t_begin && pos < r_end;
   const bool row_writer = has_row && (pos_attended ? (pos >= w0 && pos < w1)
                                                    : (split == 0 && warp == 0));
@@ -822,13 +823,15 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
       sm.q[h][d] = O;
       if (d == 0) sm.hl[h] = (sm.err || M == -CUDART_INF_F) ? 0.f : Lsum;
     } else if constexpr (GRID) {
-      // Log2 units: the grid merge below is the only reader.  A CTA that
-      // failed publishes an empty partial (l = 0) but still takes part.
-      const long long r = ((long long)(hkv * G + h)) * p.n_splits + split;
-      p.part_o[r * kHeadDim + d] = O;
+      // Tagged words, m in log2 units: the grid merge below is the only
+      // reader.  A CTA that failed publishes an empty partial (l = 0).
+      unsigned long long* row =
+          p.grid_words + ((long long)(hkv * G + h) * p.n_splits + split) * kGridRowWords;
+      const unsigned ep = sm.gep;
+      st_tagged(row + d, O, ep);
       if (d == 0) {
-        p.part_ml[r * 2 + 0] = M;
-        p.part_ml[r * 2 + 1] = (sm.err || M == -CUDART_INF_F) ? 0.f : Lsum;
+        st_tagged(row + kHeadDim, M, ep);
+        st_tagged(row + kHeadDim + 1, (sm.err || M == -CUDART_INF_F) ? 0.f : Lsum, ep);
       }
     } else if (p.out != nullptr && p.n_splits == 1) {
       p.out[(long long)seq * p.out_stride + (long long)(hkv * G + h) * kHeadDim + d] =
@@ -843,7 +846,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     }
   }
   if constexpr (CLUSTER) cluster_epilogue<NT>(p, sm.q, sm.hm, sm.hl, seq, hkv);
-  if constexpr (GRID) grid_epilogue<NW, ST, NS>(p, sm, pos);
+  if constexpr (GRID) grid_epilogue<NW, ST, NS>(p, sm, hkv, split, sm.gep);
 }
 
 // Log-sum-exp merge of n_parts partials per output row (merge_partials in
@@ -873,6 +876,24 @@ __global__ void __launch_bounds__(kHeadDim * kMergeGroups) combine_kernel(const 
   } else {
     dst[d] = L > 0.f ? O / L : 0.f;
   }
+}
+
+// Single-sequence combine over many CTAs: CTA (slice, q head, sequence)
+// merges dims [16 slice, +16) of that head's output over its split partials
+// (merge_slice16: coalesced loads, one L2 round trip).  Used where there are
+// few output rows, so that the merge's loads spread over 8 x rows CTAs.
+__global__ void __launch_bounds__(kSliceThreads) combine_wide_kernel(const CombineParams c) {
+  __shared__ SliceSmem<kMergeMaxParts> sm;
+  const int slice = blockIdx.x, h = blockIdx.y, seq = blockIdx.z;
+  const long long r = (long long)seq * c.rows_per_seq + h;
+  pdl_wait();  // released after the wait, as combine_kernel
+  pdl_launch_dependents();
+  const int d0 = slice * kSliceDims;
+  merge_slice16<kMergeMaxParts>(c.o + r * c.o_row_stride + d0, c.o_part_stride,
+                                c.m + r * c.ml_row_stride, c.l + r * c.ml_row_stride,
+                                c.ml_part_stride, c.n_parts, 1.4426950408889634f, sm,
+                                c.out + (long long)seq * c.out_stride + (long long)h * kHeadDim +
+                                    d0);
 }
 
 // RoPE on every q head (in place) and every k head of one new token per
@@ -1058,7 +1079,7 @@ cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cu
   DecodeParams copy = p;
   copy.quant = v.quant;
   void* args[] = {&copy};
-  if (p.grid_bar != nullptr) {
+  if (p.grid_words != nullptr) {
     // Grid-merged single-sequence launch: the output is final when it ends.
     if (!fused || n_seq != 1 || !v.fused_grid || p.n_splits < kG ||
         p.n_splits > kGridMaxParts || p.out == nullptr)
@@ -1093,6 +1114,14 @@ cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, b
   void* args[] = {&copy};
   return launch_ex((const void*)combine_kernel, grid, dim3(kHeadDim * kMergeGroups), 0, st, pdl,
                    args);
+}
+
+cudaError_t launch_combine_wide(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl) {
+  if (c.out_m != nullptr || c.n_parts > kMergeMaxParts) return cudaErrorInvalidValue;
+  dim3 grid(kHeadDim / kSliceDims, c.rows_per_seq, n_seq);
+  CombineParams copy = c;
+  void* args[] = {&copy};
+  return launch_ex((const void*)combine_wide_kernel, grid, dim3(kSliceThreads), 0, st, pdl, args);
 }
 
 cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k_ptrs,

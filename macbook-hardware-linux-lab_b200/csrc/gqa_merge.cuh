@@ -134,4 +134,113 @@ __device__ __forceinline__ void merge_partials(const CombineParams& c, long long
   }
 }
 
+// ---------------------------------------------------------------------------
+// Slice merge: dims [d0, d0 + 16) of one row over its S partials, by one
+// block of 256 threads.  Every access is coalesced: half-warp hw takes parts
+// hw, hw + 16, ... and its lane j dim d0 + j (one 64-byte segment per part),
+// with the first kSliceChunk parts of every thread in flight before the
+// weights are known; warp 0 meanwhile forms the maximum, the weights (in
+// shared memory) and L from every (m, l).  The two half-warps of a warp meet
+// by one shuffle and the 8 warps in shared memory.  m is in log2 units when
+// m_scale is 1 and in natural-log units when it is log2(e).
+constexpr int kSliceDims = 16;
+constexpr int kSliceThreads = 256;
+constexpr int kSliceChunk = 8;
+
+template <int MAXP>
+struct SliceSmem {
+  float w[MAXP];
+  float red[kSliceThreads / 32][kSliceDims];
+  float L;
+};
+
+template <int MAXP>
+__device__ __forceinline__ void merge_slice16(const float* o_row, long long o_part_stride,
+                                              const float* m_row, const float* l_row,
+                                              long long ml_part_stride, int S, float m_scale,
+                                              SliceSmem<MAXP>& sm, float* out) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hw = tid >> 4, j = tid & 15;
+  constexpr int kGroups = kSliceThreads / 16;
+  const float* oc = o_row + j;
+  float ov[kSliceChunk];
+#pragma unroll
+  for (int k = 0; k < kSliceChunk; ++k) {
+    const int i = hw + kGroups * k;
+    ov[k] = i < S ? __ldcg(oc + (long long)i * o_part_stride) : 0.f;
+  }
+  if (warp == 0) {
+    constexpr int kPer = 8;
+    float mr[kPer], lr[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = lane + 32 * k;
+      mr[k] = i < S ? __ldcg(m_row + (long long)i * ml_part_stride) : -CUDART_INF_F;
+      lr[k] = i < S ? __ldcg(l_row + (long long)i * ml_part_stride) : 0.f;
+    }
+    float mx = -CUDART_INF_F;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k)
+      if (lr[k] > 0.f) mx = fmaxf(mx, mr[k]);
+    for (int i = lane + 32 * kPer; i < S; i += 32)
+      if (__ldcg(l_row + (long long)i * ml_part_stride) > 0.f)
+        mx = fmaxf(mx, __ldcg(m_row + (long long)i * ml_part_stride));
+    mx = warp_max(mx);
+    float ls = 0.f;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = lane + 32 * k;
+      if (i < S) {
+        const float w = lr[k] > 0.f ? exp2f((mr[k] - mx) * m_scale) : 0.f;
+        sm.w[i] = w;
+        ls += w * lr[k];
+      }
+    }
+    for (int i = lane + 32 * kPer; i < S; i += 32) {
+      const float li = __ldcg(l_row + (long long)i * ml_part_stride);
+      const float w =
+          li > 0.f ? exp2f((__ldcg(m_row + (long long)i * ml_part_stride) - mx) * m_scale) : 0.f;
+      sm.w[i] = w;
+      ls += w * li;
+    }
+    ls = warp_sum(ls);
+    if (lane == 0) sm.L = ls;
+  }
+  __syncthreads();
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < kSliceChunk; ++k) {
+    const int i = hw + kGroups * k;
+    if (i < S) {
+      const float w = sm.w[i];
+      if (w != 0.f) acc += w * ov[k];
+    }
+  }
+  for (int i0 = kGroups * kSliceChunk; i0 < S; i0 += kGroups * kSliceChunk) {
+#pragma unroll
+    for (int k = 0; k < kSliceChunk; ++k) {
+      const int i = i0 + hw + kGroups * k;
+      ov[k] = i < S ? __ldcg(oc + (long long)i * o_part_stride) : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < kSliceChunk; ++k) {
+      const int i = i0 + hw + kGroups * k;
+      if (i < S) {
+        const float w = sm.w[i];
+        if (w != 0.f) acc += w * ov[k];
+      }
+    }
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+  if (lane < 16) sm.red[warp][j] = acc;
+  __syncthreads();
+  if (tid < kSliceDims) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kSliceThreads / 32; ++w) s += sm.red[w][tid];
+    const float L = sm.L;
+    out[tid] = L > 0.f ? s / L : 0.f;
+  }
+}
+
 }  // namespace gqa
