@@ -283,7 +283,9 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hw = tid >> 4, j = tid & 15;
   constexpr int kGroups = kSliceThreads / 16;
-  static_assert(NW * 32 == kSliceThreads, "the grid merge maps 256 threads");
+  static_assert(NW * 32 >= kSliceThreads, "the grid merge maps 256 threads");
+  // Threads beyond the first 256 only take part in the CTA barriers.
+  const bool merger = tid < kSliceThreads;
   static_assert(kGroups * kSliceChunk == kGridMaxParts, "parts held in registers");
   constexpr int kSlices = kHeadDim / kSliceDims;
   const int S = p.n_splits;
@@ -298,7 +300,7 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
 #pragma unroll
     for (int k = 0; k < kSliceChunk; ++k) {
       const int i = hw + kGroups * k;
-      wo[k] = i < S ? ld_tagged(rows + (long long)i * kGridRowWords + d0 + j) : 0ull;
+      wo[k] = merger && i < S ? ld_tagged(rows + (long long)i * kGridRowWords + d0 + j) : 0ull;
     }
     constexpr int kPer = kGridMaxParts / 32;
     unsigned long long wm[kPer], wl[kPer];
@@ -317,7 +319,7 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
 #pragma unroll
       for (int k = 0; k < kSliceChunk; ++k) {
         const int i = hw + kGroups * k;
-        if (i < S && tag_of(wo[k]) != ep) {
+        if (merger && i < S && tag_of(wo[k]) != ep) {
           fresh = false;
           wo[k] = ld_tagged(rows + (long long)i * kGridRowWords + d0 + j);
         }
@@ -372,17 +374,19 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
     // read the epoch, which may now advance (every merging CTA stores the
     // same value).
     if (tid == 0) st_relaxed_gpu(p.grid_epoch + hkv, ep);
-    float acc = 0.f;
+    if (merger) {
+      float acc = 0.f;
 #pragma unroll
-    for (int k = 0; k < kSliceChunk; ++k) {
-      const int i = hw + kGroups * k;
-      if (i < S) {
-        const float w = sm.slice.w[i];
-        if (w != 0.f) acc += w * value_of(wo[k]);
+      for (int k = 0; k < kSliceChunk; ++k) {
+        const int i = hw + kGroups * k;
+        if (i < S) {
+          const float w = sm.slice.w[i];
+          if (w != 0.f) acc += w * value_of(wo[k]);
+        }
       }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+      if (lane < 16) sm.slice.red[warp][j] = acc;
     }
-    acc += __shfl_xor_sync(0xffffffffu, acc, 16);
-    if (lane < 16) sm.slice.red[warp][j] = acc;
     __syncthreads();
     if (tid < kSliceDims) {
       float sum = 0.f;
@@ -522,20 +526,46 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
       sm.cs[tid][1] = sn;
     }
   };
-  if (FUSED && early) rope_table();
+  if (FUSED && early) {
+    rope_table();
+    __syncthreads();  // angle table complete (before the wait, off the critical path)
+  }
   if (early) pdl_wait();
   if constexpr (!GRID) pdl_launch_dependents();
-  if (FUSED && !early) rope_table();
+  if (FUSED && !early) {
+    rope_table();
+    __syncthreads();
+  }
 
-  // ---- q (and the new k/v row) straight into registers --------------------
-  // Lane l holds dims 4l..4l+3 of every head; the RoPE partner dims (+-64)
-  // live in lane l^16, one shuffle away.
+  // ---- q, rotated and scaled once per CTA ----------------------------------
+  // Thread 16h + k (k < 16) loads dims 4k..4k+3 and their RoPE partners
+  // 64+4k..64+4k+3 of head h, applies the reference's half rotation
+  // (a' = a c - b s, b' = a s + b c for the pair (i, i + 64)) and the softmax
+  // scale, and stores both to sm.q; each warp then reads its lanes' dims.
   const float* qin = p.qkv + (long long)seq * p.qkv_stride;
-  // One cooperative load of the group's q (6 x 128 floats) per CTA.
-  {
-    const float4* qg = reinterpret_cast<const float4*>(qin + (long long)hkv * G * kHeadDim);
-    for (int i = tid; i < G * kHeadDim / 4; i += NT)
-      reinterpret_cast<float4*>(&sm.q[0][0])[i] = __ldcg(qg + i);
+  if (tid < G * 16) {
+    const int h = tid >> 4, k = tid & 15;
+    const float4* qg = reinterpret_cast<const float4*>(qin + (long long)(hkv * G + h) * kHeadDim);
+    const float4 x = __ldcg(qg + k), y = __ldcg(qg + 16 + k);
+    float4 xa, ya;
+    if (FUSED) {
+      float c[4], s[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 t = *reinterpret_cast<const float2*>(sm.cs[4 * k + j]);
+        c[j] = t.x;
+        s[j] = t.y;
+      }
+      xa = make_float4((x.x * c[0] - y.x * s[0]) * p.q_scale, (x.y * c[1] - y.y * s[1]) * p.q_scale,
+                       (x.z * c[2] - y.z * s[2]) * p.q_scale, (x.w * c[3] - y.w * s[3]) * p.q_scale);
+      ya = make_float4((x.x * s[0] + y.x * c[0]) * p.q_scale, (x.y * s[1] + y.y * c[1]) * p.q_scale,
+                       (x.z * s[2] + y.z * c[2]) * p.q_scale, (x.w * s[3] + y.w * c[3]) * p.q_scale);
+    } else {
+      xa = make_float4(x.x * p.q_scale, x.y * p.q_scale, x.z * p.q_scale, x.w * p.q_scale);
+      ya = make_float4(y.x * p.q_scale, y.y * p.q_scale, y.z * p.q_scale, y.w * p.q_scale);
+    }
+    reinterpret_cast<float4*>(sm.q[h])[k] = xa;
+    reinterpret_cast<float4*>(sm.q[h])[16 + k] = ya;
   }
   // This launch's epoch for the tagged partials (read after the wait: the
   // previous launch, which may have advanced it, has finished).
@@ -543,45 +573,27 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   const bool pos_attended = pos >= p.t_begin && pos < r_end;
   const bool row_writer = has_row && (pos_attended ? (pos >= w0 && pos < w1)
                                                    : (split == 0 && warp == 0));
-  float4 nk = make_float4(0.f, 0.f, 0.f, 0.f), nv = nk, nkp = nk;
+  float4 nk = make_float4(0.f, 0.f, 0.f, 0.f), nv = nk;
   if (row_writer) {
+    // The new row: lane l holds dims 4l..4l+3; the RoPE partner dims (+-64)
+    // are in lane l ^ 16's load.
     const float4* kh = reinterpret_cast<const float4*>(qin + (long long)(n_q + hkv) * kHeadDim);
     nk = __ldcg(kh + lane);
-    nkp = __ldcg(kh + (lane ^ 16));
+    const float4 nkp = __ldcg(kh + (lane ^ 16));
     nv = __ldcg(reinterpret_cast<const float4*>(qin + (long long)(n_q + p.n_kv + hkv) *
                                                 kHeadDim) + lane);
-  }
-  __syncthreads();  // q staged, angle table complete
-
-  float4 qv[G], qp[G];  // own dims and the RoPE partner dims (+-64)
+    if (FUSED) {
+      float c[4], sn[4];
 #pragma unroll
-  for (int h = 0; h < G; ++h) {
-    qv[h] = reinterpret_cast<const float4*>(sm.q[h])[lane];
-    qp[h] = reinterpret_cast<const float4*>(sm.q[h])[lane ^ 16];
-  }
-  float qr[G][4];
-  if (FUSED) {
-    float c[4], sn[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 t = *reinterpret_cast<const float2*>(sm.cs[4 * (lane & 15) + j]);
-      c[j] = t.x;
-      sn[j] = t.y;
-    }
-    const bool lo = lane < 16;
-    // lo lanes: x' = x c - y s (dims < 64); hi lanes: x' = y s + x c (dims >= 64),
-    // with y the partner value: the reference's half rotation.
-    auto rot = [&](float x, float y, int j) {
-      return lo ? (x * c[j] - y * sn[j]) : (y * sn[j] + x * c[j]);
-    };
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      qr[h][0] = rot(qv[h].x, qp[h].x, 0) * p.q_scale;
-      qr[h][1] = rot(qv[h].y, qp[h].y, 1) * p.q_scale;
-      qr[h][2] = rot(qv[h].z, qp[h].z, 2) * p.q_scale;
-      qr[h][3] = rot(qv[h].w, qp[h].w, 3) * p.q_scale;
-    }
-    if (row_writer) {
+      for (int j = 0; j < 4; ++j) {
+        const float2 t = *reinterpret_cast<const float2*>(sm.cs[4 * (lane & 15) + j]);
+        c[j] = t.x;
+        sn[j] = t.y;
+      }
+      const bool lo = lane < 16;
+      auto rot = [&](float x, float y, int j) {
+        return lo ? (x * c[j] - y * sn[j]) : (y * sn[j] + x * c[j]);
+      };
       nk = make_float4(rot(nk.x, nkp.x, 0), rot(nk.y, nkp.y, 1), rot(nk.z, nkp.z, 2),
                        rot(nk.w, nkp.w, 3));
       if (!pos_attended) {
@@ -589,14 +601,6 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
         reinterpret_cast<float4*>(kc + (long long)pos * kHeadDim)[lane] = nk;
         reinterpret_cast<float4*>(vc + (long long)pos * kHeadDim)[lane] = nv;
       }
-    }
-  } else {
-#pragma unroll
-    for (int h = 0; h < G; ++h) {
-      qr[h][0] = qv[h].x * p.q_scale;
-      qr[h][1] = qv[h].y * p.q_scale;
-      qr[h][2] = qv[h].z * p.q_scale;
-      qr[h][3] = qv[h].w * p.q_scale;
     }
   }
 
@@ -612,15 +616,20 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   const int hb = B::head0(lane);     // first of this lane's three heads
   const bool hi = hb != 0;
   const bool own = B::owner(lane);   // one lane per (token, head triple) writes p
+  __syncthreads();  // rotated q staged
   // Partials are stored in a lane-dependent order -- position (tp, hp) holds
   // token tp ^ tt and head hp with its triple swapped when `hi` -- so that
   // every butterfly exchange keeps the lower half and sends the upper half
   // with no select (Bfly::run_permuted).  The q registers are swapped once.
   float qs[G][4];
 #pragma unroll
-  for (int h = 0; h < G; ++h)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) qs[h][j] = hi ? qr[(h + 3) % G][j] : qr[h][j];
+  for (int h = 0; h < G; ++h) {
+    const float4 t = reinterpret_cast<const float4*>(sm.q[hi ? (h + 3) % G : h])[lane];
+    qs[h][0] = t.x;
+    qs[h][1] = t.y;
+    qs[h][2] = t.z;
+    qs[h][3] = t.w;
+  }
   float lown[3] = {0.f, 0.f, 0.f};  // this owner lane's share of l for its heads
   int consumed = 0;
   bool failed = false;
@@ -1010,9 +1019,9 @@ static const Variant& decode_variant(int i) {
       make_variant<8, 4, 3, true>(),  // 0: 256 threads, 12 KB ring per warp, 2 CTAs/SM
       make_variant<4, 8, 3>(),  // 1: 128 threads, 24 KB ring per warp, 2 CTAs/SM
       make_variant<4, 4, 4>(),  // 2: 128 threads, 16 KB ring per warp, 3 CTAs/SM
-      make_variant<8, 8, 2>(),  // 3: 256 threads, 32 KB ring per warp, 1 CTA/SM
+      make_variant<8, 8, 2, true>(),  // 3: 256 threads, 32 KB ring per warp, 1 CTA/SM
       make_variant<8, 2, 4>(),  // 4: 256 threads,  8 KB ring per warp, 2-3 CTAs/SM
-      make_variant<16, 4, 2>(), // 5: 512 threads,  8 KB ring per warp, 1 CTA/SM
+      make_variant<16, 4, 2, true>(), // 5: 512 threads,  8 KB ring per warp, 1 CTA/SM
       make_variant<16, 2, 3>(), // 6: 512 threads,  6 KB ring per warp, 1 CTA/SM
   };
   constexpr int n = sizeof(table) / sizeof(table[0]);
