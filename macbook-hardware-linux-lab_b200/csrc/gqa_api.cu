@@ -257,15 +257,19 @@ int plan_splits_single(const gqa_ctx* c, int rows_kv, int len) {
 int grid_variant(const gqa_ctx* c) { return c->variant >= 0 ? c->variant : 0; }
 
 // Splits of a grid-merged single-sequence decode over `len` rows, or 0 when
-// the grid merge cannot be used: at least 6 splits (one merge slice per q
-// head), at most kGridMaxSplits, and every CTA of the launch resident at once
-// with room for the next launch's CTAs (at most one CTA per SM when two fit).
+// the grid merge cannot be used: at least 6 splits, at most kGridMaxParts,
+// and every CTA of the launch resident at once (its mergers wait on the other
+// CTAs): one CTA per SM.  (The next launch's CTAs are released only once all
+// of this launch's are running, so they can never take a slot this launch
+// still needs.  Two CTAs per SM of one launch measured slower: the second
+// wave waits for the previous launch's CTAs to leave, and the merge waits
+// for it.)
 int plan_splits_grid(const gqa_ctx* c, int rows_kv, int len) {
   if (!c->grid_merge || c->generic || c->grid_ctas_per_sm < 1 || !c->grid_words ||
       rows_kv > kGridEpochWords)
     return 0;
   const int quant = decode_variant_grid_quant(grid_variant(c));
-  const int per_sm = c->grid_ctas_per_sm >= 2 ? 1 : c->grid_ctas_per_sm;
+  const int per_sm = c->grid_ctas_per_sm >= 1 ? 1 : 0;
   const int cap = c->n_sm * per_sm;
   const int target = c->target_ctas > 0 && c->target_ctas < cap ? c->target_ctas : cap;
   int want = target / rows_kv;
@@ -320,13 +324,17 @@ int check_kv(const gqa_ctx* c, const gqa_layer_kv* kv) {
 }
 
 // One sequence: split kernel (+ combine when split), result to `out`.  When
-// the grid merge applies, one launch does both, and it also brings
-// `next_kv`'s rows (if any) into L2 for the next layer's launch.
+// the grid merge applies (and `grid_ok`), one launch does both, and it also
+// brings `next_kv`'s rows (if any) into L2 for the next layer's launch.  The
+// attention blocks pass grid_ok = false: between the projections the split
+// kernel + combine measured faster (block28 339 vs 385 us per token).
 int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
                Lengths len, int plan_len, bool fused, float* out, bool pdl_first,
-               bool lengths_stable, const gqa_layer_kv* next_kv = nullptr) {
+               bool lengths_stable, const gqa_layer_kv* next_kv = nullptr,
+               bool grid_ok = true) {
   const int n_kv = c->cfg.n_heads_kv;
-  const int grid_splits = (fused && out != nullptr) ? plan_splits_grid(c, n_kv, plan_len) : 0;
+  const int grid_splits =
+      (grid_ok && fused && out != nullptr) ? plan_splits_grid(c, n_kv, plan_len) : 0;
   if (grid_splits > 0) {
     DecodeParams p = base_params(c);
     p.k_base = kv->k_cache;
@@ -482,7 +490,7 @@ int block_impl(gqa_ctx* c, cudaStream_t st, const gqa_block_weights* w, const gq
   int rc = c->generic ? run_generic(c, st, kv, c->blk_qkv, len, plan_len, c->blk_attn, true,
                                     lengths_stable)
                       : run_single(c, st, kv, c->blk_qkv, len, plan_len, true, c->blk_attn, true,
-                                   lengths_stable);
+                                   lengths_stable, nullptr, /*grid_ok=*/false);
   if (rc != GQA_OK) return rc;
   GQA_CUDA(launch_wo_gemv(model, w->w_o, c->blk_attn, state, nq * hd, c->status, st, true));
   return GQA_OK;

@@ -833,14 +833,16 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
       if (d == 0) sm.hl[h] = (sm.err || M == -CUDART_INF_F) ? 0.f : Lsum;
     } else if constexpr (GRID) {
       // Tagged words, m in log2 units: the grid merge below is the only
-      // reader.  A CTA that failed publishes an empty partial (l = 0).
+      // reader.  A CTA that failed publishes an empty partial (m = -inf,
+      // l = 0), which the merge gives weight 0.
       unsigned long long* row =
           p.grid_words + ((long long)(hkv * G + h) * p.n_splits + split) * kGridRowWords;
       const unsigned ep = sm.gep;
+      const bool empty = sm.err || M == -CUDART_INF_F;
       st_tagged(row + d, O, ep);
       if (d == 0) {
-        st_tagged(row + kHeadDim, M, ep);
-        st_tagged(row + kHeadDim + 1, (sm.err || M == -CUDART_INF_F) ? 0.f : Lsum, ep);
+        st_tagged(row + kHeadDim, empty ? -CUDART_INF_F : M, ep);
+        st_tagged(row + kHeadDim + 1, empty ? 0.f : Lsum, ep);
       }
     } else if (p.out != nullptr && p.n_splits == 1) {
       p.out[(long long)seq * p.out_stride + (long long)(hkv * G + h) * kHeadDim + d] =
@@ -1009,7 +1011,7 @@ static Variant make_variant() {
     v.fused_grid = (const void*)decode_split_kernel<NW, ST, NS, true, false, true>;
   v.threads = NW * 32;
   v.quant = NW * ST > 32 ? NW * ST : 32;
-  v.grid_quant = ST > 8 ? ST : 8;
+  v.grid_quant = ST;
   v.smem = sizeof(DecodeSmem<NW, ST, NS>);
   return v;
 }
