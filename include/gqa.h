@@ -515,14 +515,23 @@ GQA_API int gqa_prefill_bf16(gqa_ctx *ctx, gqa_stream_t stream, int n_seq, int s
  * split-KV scratch is a static device array inside the library (about
  * 2.03 MiB per device that loads the library, held until exit, room for 4096
  * q-head x split partials; a call needing more is rejected with
- * GQA_ERR_INVALID_ARG).  The first call on a device, and any call with a new
- * rope_theta, does a one-time set-up that includes a synchronous copy, so make
- * it before any stream capture.  Calls share the array: calls on one device
- * that may overlap on the GPU race and must be ordered by the caller.  It
- * calls no cudaMalloc, cudaFree or allocating library routine. */
+ * GQA_ERR_INVALID_ARG).  The first call on a device does a one-time set-up
+ * that includes synchronous copies, so make it before any stream capture.  A
+ * call whose rope_theta differs from the previous call's writes the new RoPE
+ * table with an asynchronous copy on `stream`, ordered like the calls
+ * themselves.  Calls share the array: calls on one device that may overlap on
+ * the GPU race and must be ordered by the caller (one stream, or events).
+ * Errors the kernels detect on the device (a bad length, a wait that ran out)
+ * are not in the return value; read them with gqa_static_status.  It calls no
+ * cudaMalloc, cudaFree or allocating library routine. */
 GQA_API int gqa_layer_attention_static(const gqa_config *cfg, gqa_stream_t stream,
                                        const gqa_layer_kv *kv, float *qkv, int pos,
                                        int seq_len);
+
+/* Device status word of the allocation-free layer calls on `device` (bitmask,
+ * 0 = fine; the bits of gqa_device_status); clear != 0 zeroes it.  Waits for
+ * all work on that device first.  No counterpart in the reference. */
+GQA_API int gqa_static_status(int device, int *status, int clear);
 
 /* ---- utilities -------------------------------------------------------- */
 

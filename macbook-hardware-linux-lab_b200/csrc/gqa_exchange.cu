@@ -8,11 +8,12 @@
 //      (merge_partials, as in combine_kernel);
 //   2. stores that triple straight into the inbox of every GPU of the group
 //      (peer memory mapped through CUDA IPC, stores over NVLink), each value
-//      as one 8-byte word {value, step epoch};
+//      as one 64-bit word {value, step epoch};
 //   3. polls (bounded) its own inbox until every source's words carry this
 //      step's epoch, and merges the world triples into the head's output.
-// An aligned 8-byte store is never seen half-written, so a word whose epoch
-// is current holds its value: no fence and no separate flag is needed.
+// Each word is written and read by one 64-bit scalar access, which is
+// single-copy atomic, so a word whose epoch is current holds its value: no
+// fence and no separate flag is needed.
 // This is the reference's split-K segment reduce (kernel_attention_gqa.cl:
 // 378-397) stretched over several GPUs, with the all-gather done by the
 // merging kernel itself instead of a collective library call.
@@ -44,17 +45,20 @@ struct ExchangeParams {
   int* status;
 };
 
-// One word {value, epoch}, stored and loaded whole at system scope.
+// One word {value (low half), epoch (high half)}, stored and loaded as a single
+// 64-bit scalar at system scope.  A scalar access is single-copy atomic, so a
+// reader that sees the epoch of a store sees its value too.  (A .v2.u32 pair
+// would not do: the memory model treats a vector access as separate scalar
+// accesses, so a reader could pair a new epoch with an old value.)
 __device__ __forceinline__ void st_word(uint2* p, float v, unsigned e) {
-  asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)),
-               "r"(e) : "memory");
+  const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
 __device__ __forceinline__ uint2 ld_word(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p)
-               : "memory");
-  return v;
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return make_uint2((unsigned)w, (unsigned)(w >> 32));
 }
 
 // Reloads word w from p until its epoch reaches e; false if that takes past

@@ -17,8 +17,9 @@
 // share it; it keeps the last call's contents.  Calls on one device that can
 // overlap on the GPU (issued to different streams without ordering between
 // them) race on it, so the caller must order them (one stream, or events).
-// Nothing in the array needs to start at zero: every partial a call reads was
-// written earlier in the same call.
+// The partials need no clearing: every partial a call reads was written
+// earlier in the same call.  The status word is cleared at set-up and read
+// (and cleared) with gqa_static_status.
 #include <cmath>
 #include <cstdio>
 #include <mutex>
@@ -61,10 +62,14 @@ StaticDevice g_dev[kMaxDevices];
 std::mutex g_mu;
 
 // First call on a device (with that device current): look up the array's
-// device address and prepare the kernels; whenever rope_theta differs from
-// the loaded one, write the new inverse-frequency table (a synchronous copy,
-// so such a call must not happen during stream capture).
-int setup_device(int dev, float theta, StaticDevice** out) {
+// device address, prepare the kernels and clear the status word (synchronous
+// copies, so this first call must come before any stream capture).  Whenever
+// rope_theta differs from the one last written, the new inverse-frequency
+// table is written with an asynchronous copy on the caller's stream, so it is
+// ordered like the calls themselves: calls ordered on one stream (or by
+// events) each see their own table.  Calls that may overlap on the GPU race on
+// the table as on the rest of the array.
+int setup_device(int dev, float theta, cudaStream_t st, StaticDevice** out) {
   std::lock_guard<std::mutex> lock(g_mu);
   StaticDevice& s = g_dev[dev];
   if (!s.ready) {
@@ -74,18 +79,22 @@ int setup_device(int dev, float theta, StaticDevice** out) {
                        cudaGetErrorString(e));
     e = prepare_decode_kernels();
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&s.n_sm, cudaDevAttrMultiProcessorCount, dev);
+    const float zero[1] = {0.f};
+    if (e == cudaSuccess)
+      e = cudaMemcpyToSymbol(g_noalloc_scratch, zero, sizeof(zero), sizeof(float) * kOffStatus,
+                             cudaMemcpyHostToDevice);
     if (e != cudaSuccess)
       return set_error(GQA_ERR_CUDA, "static-scratch set-up failed: %s", cudaGetErrorString(e));
     s.ready = true;
   }
   if (!(s.theta == theta)) {
-    float table[kHalf + 1];
+    float table[kHalf];
     // attention_gqa_benchmark.c:143 evaluated once on the host, as the
     // context path does.
     for (int i = 0; i < kHalf; ++i) table[i] = powf(theta, -2.0f * (float)i / (float)kHeadDim);
-    table[kHalf] = 0.f;  // status word starts clear
-    cudaError_t e = cudaMemcpyToSymbol(g_noalloc_scratch, table, sizeof(table),
-                                       sizeof(float) * kOffInvFreq, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMemcpyToSymbolAsync(g_noalloc_scratch, table, sizeof(table),
+                                            sizeof(float) * kOffInvFreq, cudaMemcpyHostToDevice,
+                                            st);
     if (e != cudaSuccess)
       return set_error(GQA_ERR_CUDA, "writing the RoPE table failed: %s", cudaGetErrorString(e));
     s.theta = theta;
@@ -118,7 +127,7 @@ extern "C" int gqa_layer_attention_static(const gqa_config* cfg, gqa_stream_t st
   if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return set_error(GQA_ERR_CUDA, "no usable current device");
   StaticDevice* s = nullptr;
-  int rc = setup_device(dev, cfg->rope_theta, &s);
+  int rc = setup_device(dev, cfg->rope_theta, (cudaStream_t)stream, &s);
   if (rc != GQA_OK) return rc;
 
   // Same split plan as the context path: one CTA per SM over the KV heads,
@@ -171,5 +180,38 @@ extern "C" int gqa_layer_attention_static(const gqa_config* cfg, gqa_stream_t st
   if (e != cudaSuccess)
     return set_error(GQA_ERR_CUDA, "gqa_layer_attention_static launch failed: %s",
                      cudaGetErrorString(e));
+  return GQA_OK;
+}
+
+// Reads (and with `clear` zeroes) the status word of the allocation-free
+// calls on `device`: the bits the kernels raise (bad length, wait timeout) in
+// place of a return value.  It waits for all work on that device first.  A
+// device that never ran such a call reads 0.
+extern "C" int gqa_static_status(int device, int* status, int clear) {
+  if (!status) return set_error(GQA_ERR_INVALID_ARG, "gqa_static_status: null status");
+  *status = 0;
+  if (device < 0 || device >= kMaxDevices)
+    return set_error(GQA_ERR_INVALID_ARG, "gqa_static_status: no device %d", device);
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_dev[device].ready) return GQA_OK;
+  }
+  int prev = -1;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e == cudaSuccess && prev != device) e = cudaSetDevice(device);
+  int word = 0;
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess)
+    e = cudaMemcpyFromSymbol(&word, g_noalloc_scratch, sizeof(int), sizeof(float) * kOffStatus,
+                             cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_noalloc_scratch, &zero, sizeof(int), sizeof(float) * kOffStatus,
+                           cudaMemcpyHostToDevice);
+  }
+  if (prev >= 0 && prev != device) cudaSetDevice(prev);
+  if (e != cudaSuccess)
+    return set_error(GQA_ERR_CUDA, "gqa_static_status: %s", cudaGetErrorString(e));
+  *status = word;
   return GQA_OK;
 }

@@ -169,6 +169,7 @@ _SIGNATURES = {
     "gqa_version": [],
     "gqa_layer_attention_static": [ctypes.POINTER(Config), _vp, ctypes.POINTER(LayerKV), _vp, _i,
                                    _i],
+    "gqa_static_status": [_i, ctypes.POINTER(_i), _i],
 }
 _RESTYPES = {"gqa_last_error_string": ctypes.c_char_p, "gqa_version": ctypes.c_char_p,
              "gqa_lm_head_packed_bytes": ctypes.c_longlong,

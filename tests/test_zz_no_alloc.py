@@ -69,3 +69,44 @@ def test_static_scratch_call_rejects_bad_arguments(pkg, cuda):
     bad = pkg.gqa.Config(12, 2, 64, 256, 1e6)
     assert lib.gqa_layer_attention_static(ctypes.byref(bad), stream, ctypes.byref(kv),
                                           qkv.data_ptr(), 0, 1) == pkg.gqa.GQA_ERR_UNSUPPORTED
+
+
+def test_static_scratch_theta_changes_are_stream_ordered(pkg, orc, cuda):
+    """Calls queued back to back on one non-blocking stream, alternating two
+    rope_theta values, with no synchronisation between them: each call must
+    use its own RoPE table (the table is rewritten on the caller's stream)."""
+    torch = cuda
+    lib = pkg.lib()
+    t_max = 1024
+    cases = [(61, 1e6, 1000), (62, 1e4, 700), (63, 1e6, 1023), (64, 1e4, 300)]
+    stream = torch.cuda.Stream()
+    bufs = []
+    for seed, theta, pos in cases:
+        qkv, kc, vc = pkg.seeded.decode_inputs(seed, t_max)
+        d = (torch.from_numpy(qkv.copy()).cuda(), torch.from_numpy(kc.copy()).cuda(),
+             torch.from_numpy(vc.copy()).cuda())
+        bufs.append((qkv, kc, vc, d))
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for (seed, theta, pos), (_, _, _, d) in zip(cases, bufs):
+            cfg = pkg.gqa.Config(12, 2, 128, t_max, theta)
+            kv = pkg.kv_of(d[1], d[2])
+            rc = lib.gqa_layer_attention_static(ctypes.byref(cfg), stream.cuda_stream,
+                                                ctypes.byref(kv), d[0].data_ptr(), pos, pos + 1)
+            assert rc == 0, pkg.last_error()
+    stream.synchronize()
+    for (seed, theta, pos), (qkv, kc, vc, d) in zip(cases, bufs):
+        rq = qkv.copy()
+        orc.layer_attention(rq, kc.copy(), vc.copy(), pos, pos + 1, rope_base=theta)
+        assert nerr(d[0][:1536].cpu().numpy(), rq[:1536]) <= TOL, (seed, theta)
+    st = ctypes.c_int(-1)
+    assert lib.gqa_static_status(torch.cuda.current_device(), ctypes.byref(st), 1) == 0
+    assert st.value == 0
+
+
+def test_static_status_arguments(pkg, cuda):
+    lib = pkg.lib()
+    st = ctypes.c_int(-1)
+    assert lib.gqa_static_status(0, None, 0) == pkg.gqa.GQA_ERR_INVALID_ARG
+    assert lib.gqa_static_status(-1, ctypes.byref(st), 0) == pkg.gqa.GQA_ERR_INVALID_ARG
+    assert lib.gqa_static_status(0, ctypes.byref(st), 0) == 0 and st.value == 0
