@@ -207,6 +207,39 @@ def max_over_ranks(x, world):
     return float(t.item())
 
 
+MIN_TIMED_S = 0.2    # the K-step region is repeated until this much device time is timed
+MAX_ROUNDS = 200
+
+
+def timed_rounds(body, world, stream, before=None):
+    """Times `body` (which enqueues exactly the K timed steps) in rounds.
+
+    Each round is bracketed by a barrier and a device synchronisation on both
+    sides and timed with CUDA events on `stream`; its time is the maximum over
+    ranks.  The number of rounds is fixed after the first (every rank gets the
+    same maximum, so every rank runs the same rounds): enough for MIN_TIMED_S of
+    timed device time in all.  `before()` (optional) runs untimed before each
+    round.  Returns the per-round times in seconds; callers report the median.
+    """
+    import torch
+    times, n_rounds = [], None
+    while n_rounds is None or len(times) < n_rounds:
+        if before is not None:
+            before()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        body()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        t = max_over_ranks(e0.elapsed_time(e1) / 1e3, world)
+        times.append(t)
+        if n_rounds is None:
+            n_rounds = max(1, min(MAX_ROUNDS, int(-(-MIN_TIMED_S // max(t, 1e-9)))))
+    return times
+
+
 def sum_over_ranks(x, world):
     if world == 1:
         return x
@@ -450,31 +483,38 @@ def run_resident(args, g, ctx, rank, world, local):
     if ctx.device_status() != 0:
         raise RuntimeError("device status set during warm-up")
 
-    # ---- kernel-only timed region ----
-    d_pos.fill_(pos_lo)
-    barrier(world)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        ev0.record(stream)
+    # ---- kernel-only timed region (rounds of K steps, median) ----
+    def reset_pos():
+        d_pos.fill_(pos_lo)
+
+    def body():
         for i in range(args.steps):
             graphs[i % n_slots].launch(stream)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    barrier(world)
-    t_local = ev0.elapsed_time(ev1) / 1e3
+
+    with ClockSampler(local) as clk:
+        rounds = timed_rounds(body, world, stream, before=reset_pos)
+    t_local = statistics.median(rounds)
     total_bytes = sum(step_bytes(i) for i in range(args.steps))
 
+    # ---- the layer kernels' own in-graph time: the same 28 layer calls in a
+    # graph without the position advance, replayed at position pos_lo ----
+    g_layers = ctx.graph_create_layers(kvs, qkv_slots[0], qkv_w, out, out_w, d_pos,
+                                       advance=False)
+    reset_pos()
+    for _ in range(3):
+        g_layers.launch(stream)
+    t_layers = statistics.median(timed_rounds(
+        lambda: [g_layers.launch(stream) for _ in range(args.steps)], world, stream))
+    g_layers.destroy()
+    kernel_s = t_layers / args.steps / L_layers
+    kernel_bytes = row_bytes * (pos_lo + 1)
+
     # ---- e2e timed region (host buffers in, host buffers out) ----
-    d_pos.fill_(pos_lo)
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        g_e2e.step_host(h_qkv[i % n_slots], h_out[i % n_slots], stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    t_e2e_local = e0.elapsed_time(e1) / 1e3
+    def body_e2e():
+        for i in range(args.steps):
+            g_e2e.step_host(h_qkv[i % n_slots], h_out[i % n_slots], stream)
+
+    t_e2e_local = statistics.median(timed_rounds(body_e2e, world, stream, before=reset_pos))
     status = ctx.device_status()
     if status != 0:
         raise RuntimeError(f"device status {status} after the timed regions")
@@ -483,6 +523,9 @@ def run_resident(args, g, ctx, rank, world, local):
     n_sm = torch.cuda.get_device_properties(local).multi_processor_count
     if generic:  # split (RoPE + append fused), merge per layer (csrc/gqa_generic.cu)
         kernels_per_step = L_layers * 2 + 1
+    elif args.grid_merge and args.variant in (-1, 0, 3, 5):
+        # one grid-merged split kernel per layer (csrc/gqa_decode.cu), + the advance
+        kernels_per_step = L_layers + 1
     else:
         target = args.target_ctas or n_sm
         quant = g.gqa.VARIANT_QUANT[3 if args.variant < 0 else args.variant]
@@ -493,7 +536,11 @@ def run_resident(args, g, ctx, rank, world, local):
     res = dict(t=t_local, t_e2e=t_e2e_local, bytes=total_bytes, clocks=clk.summary(),
                launches=kernels_per_step * args.steps, launches_per_step=kernels_per_step,
                h2d=L_layers * qkv_w * 4, d2h=L_layers * out_w * 4, tokens=args.steps,
-               dominant_launches=L_layers * args.steps)
+               dominant_launches=L_layers * args.steps, rounds=len(rounds),
+               timed_s=sum(rounds), kernel_s=kernel_s, kernel_bytes=kernel_bytes,
+               layers=L_layers, kernel_pos=pos_lo,
+               kernel_per_layer="split kernel + merge kernel" if generic or
+               kernels_per_step != L_layers + 1 else "one grid-merged split kernel")
     if generic:
         res.update(kernel="split_generic_kernel<64, 7> (+ merge)",
                    data="synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal), "
@@ -919,37 +966,33 @@ def run_batched(args, g, ctx, rank, world, local):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
-    barrier(world)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        ev0.record(stream)
+
+    def body():
         for i in range(args.steps):
             step(i)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    barrier(world)
-    t_local = ev0.elapsed_time(ev1) / 1e3
+
+    with ClockSampler(local) as clk:
+        rounds = timed_rounds(body, world, stream)
+    t_local = statistics.median(rounds)
     total_bytes = sum(ROW_BYTES * (L + i % window) for i in range(args.steps) for L in lens0)
     # e2e: q/k/v rows from pinned host memory, outputs back, every step
     h_qkv = qkv.cpu().pin_memory()
     h_out = torch.empty((n, OUT_W)).pin_memory()
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        qkv.copy_(h_qkv, non_blocking=True)
-        step(i)
-        h_out.copy_(out, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
+
+    def body_e2e():
+        for i in range(args.steps):
+            qkv.copy_(h_qkv, non_blocking=True)
+            step(i)
+            h_out.copy_(out, non_blocking=True)
+
+    t_e2e = statistics.median(timed_rounds(body_e2e, world, stream))
     status = ctx.device_status()
     if status != 0:
         raise RuntimeError(f"device status {status}")
-    return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3, bytes=total_bytes,
+    return dict(t=t_local, t_e2e=t_e2e, bytes=total_bytes,
                 clocks=clk.summary(), launches=2 * args.steps, launches_per_step=2,
                 h2d=n * QKV_W * 4, d2h=n * OUT_W * 4, tokens=n * args.steps,
-                dominant_launches=args.steps)
+                dominant_launches=args.steps, rounds=len(rounds), timed_s=sum(rounds))
 
 
 def run_long1(args, g, ctx, rank, world, local):
@@ -997,42 +1040,38 @@ def run_long1(args, g, ctx, rank, world, local):
                 dec.step(qkv, pos0 + i, out)
         graph.replay()
         torch.cuda.synchronize()
-    barrier(world)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        ev0.record(stream)
+    def body():
         if graph is not None:
             for _ in range(args.steps // window):
                 graph.replay()
         else:
             for i in range(args.steps):
                 dec.step(qkv, pos0 + i % window, out)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    barrier(world)
-    t_local = ev0.elapsed_time(ev1) / 1e3
+
+    with ClockSampler(local) as clk:
+        rounds = timed_rounds(body, world, stream)
+    t_local = statistics.median(rounds)
     h_qkv = qkv.cpu().pin_memory()
     h_out = torch.empty(OUT_W).pin_memory()
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        qkv.copy_(h_qkv, non_blocking=True)
-        dec.step(qkv, pos0 + i % window, out)
-        h_out.copy_(out, non_blocking=True)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
+
+    def body_e2e():
+        for i in range(args.steps):
+            qkv.copy_(h_qkv, non_blocking=True)
+            dec.step(qkv, pos0 + i % window, out)
+            h_out.copy_(out, non_blocking=True)
+
+    t_e2e = statistics.median(timed_rounds(body_e2e, world, stream))
     if ctx.device_status() != 0:
         raise RuntimeError("device status set")
     if args.exchange == "peer":
         barrier(world)  # no rank unmaps its inbox while a peer may still store into it
         del graph
         dec.close()
-    return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3,
+    return dict(t=t_local, t_e2e=t_e2e,
                 bytes=sum(my_bytes(i) for i in range(args.steps)), clocks=clk.summary(),
                 launches=per_step * args.steps, launches_per_step=per_step, h2d=QKV_W * 4,
-                d2h=OUT_W * 4, tokens=args.steps / world, dominant_launches=args.steps)
+                d2h=OUT_W * 4, tokens=args.steps / world, dominant_launches=args.steps,
+                rounds=len(rounds), timed_s=sum(rounds))
 
 
 def run_prefill(args, g, ctx, rank, world, local):
@@ -1118,7 +1157,21 @@ def run_ours(args):
     gbs = total_bytes / t / 1e9
     gbs_e2e = total_bytes / t_e2e / 1e9
     per_gpu_bytes = r["bytes"] / r["dominant_launches"]
-    achieved = r["bytes"] / r["t"] / 1e9  # this rank's dominant-kernel bytes over its timed region
+    if "kernel_s" in r:
+        # the dominant kernel's own in-graph time (its graph replayed without the advance)
+        achieved = r["kernel_bytes"] / r["kernel_s"] / 1e9
+        per_gpu_bytes = r["kernel_bytes"]
+        basis = (f"in-graph: the {r['layers']} layer calls ({r['kernel_per_layer']}) replayed "
+                 f"as a graph without the position advance, at position {r['kernel_pos']}; "
+                 "median of rounds; per layer")
+    else:
+        achieved = r["bytes"] / r["t"] / 1e9  # this rank's kernel bytes over its timed region
+        basis = ("timed-region device time / launches of the dominant kernel (includes its "
+                 "merge and gaps)")
+    extra = None
+    if args.workload == "resident28" and not args.no_extra:
+        extra = {name: run_extra(args, g, name, rank, world, local)
+                 for name in ("batched", "long1")}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if args.workload in ("block28", "layer28"):
@@ -1147,10 +1200,7 @@ def run_ours(args):
             else "strong",
             "vs_baseline": None, "dtype": "f32",
             "data": r.get("data", "synthetic: seeded N(0,1) q/k/v and KV caches (gqa_fill_normal)"),
-            "config": dict(workload_config(args.workload, args.exchange),
-                           kernel_variant="auto" if args.variant < 0 else args.variant,
-                           target_ctas=args.target_ctas or None,
-                           batch_chunk=args.batch_chunk or None),
+            "config": workload_config(args.workload, args.exchange),
             "tok_per_s": round(tokens / t, 1),
             "hbm_frac_of_measured": round(gbs / world / peak, 4),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
@@ -1158,9 +1208,13 @@ def run_ours(args):
                          "peak_source": f"{peak_kind} hbm_gbs",
                          "kernel": r.get("kernel", "decode_split_kernel"),
                          "algorithmic_bytes_per_launch": round(per_gpu_bytes),
-                         "duration_basis": "timed-region device time / launches of the "
-                                           "dominant kernel (includes its combine and gaps)",
+                         "duration_us": round(per_gpu_bytes / achieved / 1e3, 3),
+                         "duration_basis": basis,
                          "traffic": profile_traffic(args.workload)},
+            "timing": {"rounds": r.get("rounds", 1), "timed_s": round(r.get("timed_s", t), 4),
+                       "statistic": "median over rounds of the K timed steps (each round "
+                                    "barrier + synchronize on both sides, max over ranks); "
+                                    f"rounds until >= {MIN_TIMED_S} s timed"},
             "e2e": {"value": round(gbs_e2e, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
                     "tok_per_s": round(tokens / t_e2e, 1)},
@@ -1168,12 +1222,49 @@ def run_ours(args):
             "clocks": r["clocks"],
             "cpu_baseline": cpu,
         }
+        if extra:
+            line["extra"] = extra
+        if k_nondefault(args):  # tuning knobs away from the library's defaults
+            line["tuning"] = {"kernel_variant": args.variant, "target_ctas": args.target_ctas,
+                              "batch_chunk": args.batch_chunk, "grid_merge": args.grid_merge}
         print(json.dumps(line), flush=True)
     ctx.close()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
         dist.destroy_process_group()
+
+
+def k_nondefault(args):
+    return (args.variant >= 0 or args.target_ctas or args.batch_chunk or not args.grid_merge)
+
+
+def run_extra(args, g, name, rank, world, local):
+    """One of the sharded configurations timed in the default run: `batched`
+    (64 sequences dealt to the ranks, strong scaling) or `long1` (one 32768-row
+    sequence split by KV range over the ranks, merged over peer memory)."""
+    import copy
+    sub = copy.copy(args)
+    sub.workload = name
+    if name == "long1":
+        sub.steps = WORKLOADS["long1"]["window"]  # the peer-exchange graph holds one window
+        t_max = max(n for _, n in g.shard.plan_kv_ranges(WORKLOADS["long1"]["t_max"], world))
+    else:
+        t_max = WORKLOADS[name]["len_hi"] + WORKLOADS[name]["window"]
+    ctx = g.Context(t_max=t_max, device=local)
+    try:
+        r = run_long1(sub, g, ctx, rank, world, local) if name == "long1" else \
+            run_batched(sub, g, ctx, rank, world, local)
+    finally:
+        ctx.close()
+    t = max_over_ranks(r["t"], world)
+    total = sum_over_ranks(r["bytes"], world)
+    tokens = sum_over_ranks(r["tokens"], world)
+    return {"workload": workload_config(name, args.exchange)["workload"],
+            "value": round(total / t / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(t / sub.steps * 1e3, 5), "steps": sub.steps,
+            "tok_per_s": round(tokens / t, 1), "scaling": "strong",
+            "rounds": r["rounds"], "clocks": r["clocks"]}
 
 
 def report_prefill(args, r, ctx, rank, world):
@@ -1221,6 +1312,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="resident28")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the sharded configurations the default run also times")
     # tuning knobs (defaults are the library's own choices)
     ap.add_argument("--variant", type=int, default=-1, help=argparse.SUPPRESS)
     ap.add_argument("--target-ctas", type=int, default=0, help=argparse.SUPPRESS)
