@@ -237,6 +237,8 @@ def timed_rounds(body, world, stream, before=None):
         times.append(t)
         if n_rounds is None:
             n_rounds = max(1, min(MAX_ROUNDS, int(-(-MIN_TIMED_S // max(t, 1e-9)))))
+            if MIN_TIMED_S <= 0:
+                n_rounds = 1
     return times
 
 
@@ -1312,6 +1314,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="resident28")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--min-timed-s", type=float, default=MIN_TIMED_S,
+                    help="repeat the K timed steps until this much device time is timed "
+                         "(0: one round, e.g. under a profiler)")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the sharded configurations the default run also times")
     # tuning knobs (defaults are the library's own choices)
@@ -1321,6 +1326,8 @@ def main():
     ap.add_argument("--grid-merge", type=int, default=1, help=argparse.SUPPRESS)
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer", help=argparse.SUPPRESS)
     args = ap.parse_args()
+    global MIN_TIMED_S
+    MIN_TIMED_S = max(0.0, args.min_timed_s)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":

@@ -12,6 +12,8 @@
 
 #include <cuda_bf16.h>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "gqa.h"
 #include "gqa_common.cuh"
 #include "gqa_merge.cuh"
@@ -174,6 +176,16 @@ int fail(int code, const char* fmt, ...) {
     if (e_ != cudaSuccess)                                                              \
       return fail(GQA_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));      \
   } while (0)
+
+// An NVTX range named after the API call, for the call's host-side extent
+// (what a profiler or a tracing tool shows around the call's launches).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+#define GQA_RANGE(name) NvtxRange gqa_range_(name)
 
 // Makes the context's device current for the duration of an API call.
 struct DeviceGuard {
@@ -776,6 +788,7 @@ int gqa_kv_free(gqa_ctx* c, int n_layers, gqa_layer_kv* kv) {
 
 int gqa_layer_attention_out(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
                             const float* qkv, int pos, int seq_len, float* out) {
+  GQA_RANGE("gqa_layer_attention_out");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   int rc = check_kv(c, kv);
   if (rc != GQA_OK) return rc;
@@ -803,6 +816,7 @@ int gqa_decode_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers, const gqa_l
                       const float* qkv, long long qkv_layer_stride, float* out,
                       long long out_layer_stride, int* d_pos, int advance, int wrap_lo,
                       int wrap_hi) {
+  GQA_RANGE("gqa_decode_layers");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   DeviceGuard g(c->device);
   return layers_impl(c, (cudaStream_t)stream, n_layers, kv, qkv, qkv_layer_stride, out,
@@ -813,6 +827,7 @@ int gqa_graph_create_layers(gqa_ctx* c, int n_layers, const gqa_layer_kv* kv, co
                             long long qkv_layer_stride, float* out, long long out_layer_stride,
                             int* d_pos, int advance, int wrap_lo, int wrap_hi,
                             gqa_graph** out_graph) {
+  GQA_RANGE("gqa_graph_create_layers");
   if (!c || !out_graph) return fail(GQA_ERR_INVALID_ARG, "null argument");
   *out_graph = nullptr;
   DeviceGuard g(c->device);
@@ -855,6 +870,7 @@ int gqa_graph_create_layers(gqa_ctx* c, int n_layers, const gqa_layer_kv* kv, co
 }
 
 int gqa_graph_launch(gqa_graph* gr, gqa_stream_t stream) {
+  GQA_RANGE("gqa_graph_launch");
   if (!gr) return fail(GQA_ERR_INVALID_ARG, "null graph");
   DeviceGuard g(gr->ctx->device);
   GQA_CUDA(cudaGraphLaunch(gr->exec, (cudaStream_t)stream));
@@ -862,6 +878,7 @@ int gqa_graph_launch(gqa_graph* gr, gqa_stream_t stream) {
 }
 
 int gqa_graph_step_host(gqa_graph* gr, gqa_stream_t stream, const float* h_qkv, float* h_out) {
+  GQA_RANGE("gqa_graph_step_host");
   if (!gr || !h_qkv || !h_out) return fail(GQA_ERR_INVALID_ARG, "null argument");
   DeviceGuard g(gr->ctx->device);
   cudaStream_t st = (cudaStream_t)stream;
@@ -883,6 +900,7 @@ int gqa_graph_destroy(gqa_graph* gr) {
 
 int gqa_rope_kv_append(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, float* q,
                        const float* k, const float* v, int pos) {
+  GQA_RANGE("gqa_rope_kv_append");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (tuned_only(c, "gqa_rope_kv_append") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_kv(c, kv);
@@ -909,6 +927,7 @@ int gqa_rope_kv_append(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, 
 
 int gqa_decode(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, const float* q_rot,
                int seq_len, float* out) {
+  GQA_RANGE("gqa_decode");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (tuned_only(c, "gqa_decode") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_kv(c, kv);
@@ -928,6 +947,7 @@ int gqa_decode(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv, const fl
 int gqa_decode_batched(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const* k_caches,
                        float* const* v_caches, const float* qkv, long long qkv_stride,
                        const int* seq_lens, int max_len, float* out, long long out_stride) {
+  GQA_RANGE("gqa_decode_batched");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (tuned_only(c, "gqa_decode_batched") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_seq < 1 || n_seq > 65535 || !k_caches || !v_caches || !qkv || !seq_lens || !out)
@@ -976,6 +996,7 @@ int gqa_decode_batched(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const*
 int gqa_decode_split_partial(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
                              const float* q_rot, int t_begin, int t_end, float* m, float* l,
                              float* o) {
+  GQA_RANGE("gqa_decode_split_partial");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (tuned_only(c, "gqa_decode_split_partial") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   int rc = check_kv(c, kv);
@@ -1020,6 +1041,7 @@ int gqa_decode_split_partial(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv
 int gqa_decode_kv_shard(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
                         const float* qkv, int pos, int shard_begin, int shard_rows, float* m,
                         float* l, float* o) {
+  GQA_RANGE("gqa_decode_kv_shard");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (tuned_only(c, "gqa_decode_kv_shard") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (!m || !l || !o) return fail(GQA_ERR_INVALID_ARG, "null argument");
@@ -1037,6 +1059,7 @@ int gqa_decode_kv_shard(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
 
 int gqa_attention_block(gqa_ctx* c, gqa_stream_t stream, const gqa_block_weights* w,
                         const gqa_layer_kv* kv, float* state, int pos, int seq_len) {
+  GQA_RANGE("gqa_attention_block");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   int rc = check_block_weights(c, w);
   if (rc != GQA_OK) return rc;
@@ -1056,6 +1079,7 @@ int gqa_attention_block(gqa_ctx* c, gqa_stream_t stream, const gqa_block_weights
 int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
                                const gqa_block_weights* w, const gqa_layer_kv* kv, float* state,
                                int* d_pos, int advance, int wrap_lo, int wrap_hi) {
+  GQA_RANGE("gqa_attention_block_layers");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (n_layers < 1 || !w || !kv || !d_pos || !state || !aligned16(state))
     return fail(GQA_ERR_INVALID_ARG, "gqa_attention_block_layers: bad arguments");
@@ -1079,6 +1103,7 @@ int gqa_attention_block_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers,
 }
 
 int gqa_ffn_block(gqa_ctx* c, gqa_stream_t stream, const gqa_ffn_weights* w, float* state) {
+  GQA_RANGE("gqa_ffn_block");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   int rc = check_ffn_weights(c, w);
   if (rc != GQA_OK) return rc;
@@ -1090,6 +1115,7 @@ int gqa_ffn_block(gqa_ctx* c, gqa_stream_t stream, const gqa_ffn_weights* w, flo
 int gqa_decoder_layers(gqa_ctx* c, gqa_stream_t stream, int n_layers, const gqa_block_weights* attn,
                        const gqa_ffn_weights* ffn, const gqa_layer_kv* kv, float* state,
                        int* d_pos, int advance, int wrap_lo, int wrap_hi) {
+  GQA_RANGE("gqa_decoder_layers");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (n_layers < 1 || !attn || !ffn || !kv || !d_pos || !state || !aligned16(state))
     return fail(GQA_ERR_INVALID_ARG, "gqa_decoder_layers: bad arguments");
@@ -1129,6 +1155,7 @@ int gqa_lm_head_pack(gqa_ctx* c, gqa_stream_t stream, const void* q6k, int n_row
 
 int gqa_lm_head(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
                 const float* gamma, const float* state, float* logits, int* token) {
+  GQA_RANGE("gqa_lm_head");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   int rc = check_head(c, false, packed, n_rows, gamma);
   if (rc != GQA_OK) return rc;
@@ -1158,6 +1185,7 @@ int gqa_lm_head_q8_0_pack(gqa_ctx* c, gqa_stream_t stream, const void* q8, int n
 
 int gqa_lm_head_q8_0(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_rows,
                      const float* gamma, const float* state, float* logits, int* token) {
+  GQA_RANGE("gqa_lm_head_q8_0");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   int rc = check_head(c, true, packed, n_rows, gamma);
   if (rc != GQA_OK) return rc;
@@ -1172,6 +1200,7 @@ int gqa_lm_head_q8_0(gqa_ctx* c, gqa_stream_t stream, const void* packed, int n_
 
 int gqa_token_embedding(gqa_ctx* c, gqa_stream_t stream, const void* table, int n_rows,
                         const int* d_token, float* state) {
+  GQA_RANGE("gqa_token_embedding");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (need_block_model(c, "gqa_token_embedding") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (!table || !d_token || !state || n_rows < 1)
@@ -1184,6 +1213,7 @@ int gqa_token_embedding(gqa_ctx* c, gqa_stream_t stream, const void* table, int 
 
 int gqa_decode_token(gqa_ctx* c, gqa_stream_t stream, const gqa_model* m, float* state,
                      int* d_token, int* d_pos, float* logits, int wrap_lo, int wrap_hi) {
+  GQA_RANGE("gqa_decode_token");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (!m || m->n_layers < 1 || !m->attn || !m->ffn || !m->kv || !m->token_embd || !d_token ||
       !d_pos || !state || !aligned16(state))
@@ -1281,6 +1311,7 @@ int gqa_exchange_open(gqa_exchange* x, const void* handles) {
 int gqa_decode_kv_shard_exchange(gqa_ctx* c, gqa_exchange* x, gqa_stream_t stream,
                                  const gqa_layer_kv* kv, const float* qkv, int pos,
                                  int shard_begin, int shard_rows, float* out) {
+  GQA_RANGE("gqa_decode_kv_shard_exchange");
   if (!c || !x || !out) return fail(GQA_ERR_INVALID_ARG, "null argument");
   if (tuned_only(c, "gqa_decode_kv_shard_exchange") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (x->ctx != c || !x->opened)
@@ -1310,6 +1341,7 @@ int gqa_exchange_destroy(gqa_exchange* x) {
 
 int gqa_lse_combine(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows, const float* m,
                     const float* l, const float* o, float* out) {
+  GQA_RANGE("gqa_lse_combine");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (tuned_only(c, "gqa_lse_combine") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_parts < 0 || n_parts > 4096 || n_rows < 1 || n_rows > 65535 || !m || !l || !o || !out)
@@ -1332,6 +1364,7 @@ int gqa_lse_combine(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows, co
 
 int gqa_lse_combine_packed(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_rows,
                            const float* packed, long long part_stride, float* out) {
+  GQA_RANGE("gqa_lse_combine_packed");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (tuned_only(c, "gqa_lse_combine_packed") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_parts < 0 || n_parts > 4096 || n_rows < 1 || n_rows > 65535 || !packed || !out ||
@@ -1355,6 +1388,7 @@ int gqa_lse_combine_packed(gqa_ctx* c, gqa_stream_t stream, int n_parts, int n_r
 
 int gqa_prefill_bf16(gqa_ctx* c, gqa_stream_t stream, int n_seq, int seq_len, const float* qkv,
                      float* out, float* const* k_caches, float* const* v_caches) {
+  GQA_RANGE("gqa_prefill_bf16");
   if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
   if (tuned_only(c, "gqa_prefill_bf16") != GQA_OK) return GQA_ERR_UNSUPPORTED;
   if (n_seq < 1 || n_seq > 65535 || !qkv || !out)
