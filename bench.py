@@ -1307,6 +1307,7 @@ def report_prefill(args, r, ctx, rank, world):
 
 
 def main():
+    global MIN_TIMED_S
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1024)
@@ -1326,7 +1327,6 @@ def main():
     ap.add_argument("--grid-merge", type=int, default=1, help=argparse.SUPPRESS)
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer", help=argparse.SUPPRESS)
     args = ap.parse_args()
-    global MIN_TIMED_S
     MIN_TIMED_S = max(0.0, args.min_timed_s)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
