@@ -336,14 +336,12 @@ int check_kv(const gqa_ctx* c, const gqa_layer_kv* kv) {
 }
 
 // One sequence: split kernel (+ combine when split), result to `out`.  When
-// the grid merge applies (and `grid_ok`), one launch does both, and it also
-// brings `next_kv`'s rows (if any) into L2 for the next layer's launch.  The
+// the grid merge applies (and `grid_ok`), one launch does both.  The
 // attention blocks pass grid_ok = false: between the projections the split
 // kernel + combine measured faster (block28 339 vs 385 us per token).
 int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
                Lengths len, int plan_len, bool fused, float* out, bool pdl_first,
-               bool lengths_stable, const gqa_layer_kv* next_kv = nullptr,
-               bool grid_ok = true) {
+               bool lengths_stable, bool grid_ok = true) {
   const int n_kv = c->cfg.n_heads_kv;
   const int grid_splits =
       (grid_ok && fused && out != nullptr) ? plan_splits_grid(c, n_kv, plan_len) : 0;
@@ -359,10 +357,6 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
     p.out = out;
     p.grid_epoch = c->grid_epoch;
     p.grid_words = c->grid_words;
-    if (next_kv) {
-      p.pf_k = next_kv->k_cache;
-      p.pf_v = next_kv->v_cache;
-    }
     GQA_CUDA(launch_decode_split(p, 1, true, st, pdl_first, grid_variant(c)));
     return GQA_OK;
   }
@@ -441,13 +435,11 @@ int layers_impl(gqa_ctx* c, cudaStream_t st, int n_layers, const gqa_layer_kv* k
     // cache rows) at once.  Later layers follow a kernel of the previous
     // layer, which never writes pos or this layer's cache.
     const bool pdl = l > 0 && c->layers_pdl != 0;
-    const bool last = l == n_layers - 1;
     int rc = c->generic
                  ? run_generic(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max,
                                out + l * out_stride, pdl, /*lengths_stable=*/true)
                  : run_single(c, st, &kv[l], qkv + l * qkv_stride, len, c->cfg.t_max, true,
-                              out + l * out_stride, pdl, /*lengths_stable=*/true,
-                              last ? nullptr : &kv[l + 1]);
+                              out + l * out_stride, pdl, /*lengths_stable=*/true);
     if (rc != GQA_OK) return rc;
   }
   if (advance) GQA_CUDA(launch_advance_pos(d_pos, wrap_lo, wrap_hi, st, true));
@@ -502,7 +494,7 @@ int block_impl(gqa_ctx* c, cudaStream_t st, const gqa_block_weights* w, const gq
   int rc = c->generic ? run_generic(c, st, kv, c->blk_qkv, len, plan_len, c->blk_attn, true,
                                     lengths_stable)
                       : run_single(c, st, kv, c->blk_qkv, len, plan_len, true, c->blk_attn, true,
-                                   lengths_stable, nullptr, /*grid_ok=*/false);
+                                   lengths_stable, /*grid_ok=*/false);
   if (rc != GQA_OK) return rc;
   GQA_CUDA(launch_wo_gemv(model, w->w_o, c->blk_attn, state, nq * hd, c->status, st, true));
   return GQA_OK;

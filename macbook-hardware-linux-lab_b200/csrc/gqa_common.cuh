@@ -252,11 +252,6 @@ struct DecodeParams {
   // others).
   unsigned* grid_epoch;
   unsigned long long* grid_words;
-  // Cache rows of the next layer (same t_max and split plan) to bring into L2
-  // while this launch runs; null for none.  Those rows are never written by
-  // this launch, so fetching them early cannot read stale data.
-  const float* pf_k;
-  const float* pf_v;
 };
 
 struct CombineParams {

@@ -5,22 +5,28 @@
 //   decode_split_kernel : RoPE of q and of the new k (optional), KV append,
 //                         QK^T, online softmax and PV over one token range of
 //                         one KV head for all 6 query heads of its group, so
-//                         every K/V byte is read from HBM exactly once;
-//   combine_kernel      : log-sum-exp merge of the per-range partials.
+//                         every K/V byte is read from HBM exactly once; in its
+//                         grid-merged form (GRID) the same launch also merges
+//                         the ranges' partials into the final output;
+//   combine_kernel /
+//   combine_wide_kernel : log-sum-exp merge of the per-range partials, where
+//                         the split kernel leaves partials (batches, shards,
+//                         the attention blocks).
 //
 // Memory path.  Each CTA owns a contiguous token range of one KV head; each of
-// its 4 warps owns a contiguous quarter of that range and streams it through a
-// private 3-stage ring in shared memory with cp.async.bulk (1-D TMA: one copy
-// per K tile and one per V tile, 8 rows = 4 KB each, evict-first L2 hint).
+// its NW warps owns a contiguous part of that range and streams it through a
+// private ring of NS stages of ST rows in shared memory with cp.async.bulk
+// (1-D TMA: one copy per K tile and one per V tile, evict-first L2 hint),
+// issued before the dependency wait whenever the lengths are known.
 // Consecutive cache rows are contiguous ([h][t][128] layout), so a tile is
 // one linear copy; no tensor map and no multicast is needed.
 //
-// Compute path (per warp, per 8-token stage).  Lane l holds dims 4l..4l+3 of
-// the 6 (scaled, rotated) q heads.  QK^T gives 48 partial dot products per
-// lane; a butterfly reduce-scatter (5 exchange rounds, 48 shuffles in total)
+// Compute path (per warp, per ST-token stage).  q is rotated and scaled once
+// per CTA into shared memory; lane l holds dims 4l..4l+3 of the 6 q heads.
+// QK^T gives ST x 6 partial dot products per lane; a butterfly reduce-scatter
 // leaves each lane 3 complete scores.  Softmax runs in the log2 domain with a
 // lazily updated running max (rescale only when a score exceeds the max by
-// more than 2^8), p is staged through a 256-byte per-warp buffer and PV
+// more than 2^8), p is staged through a small per-warp buffer and PV
 // accumulates o[6][4] per lane.  Warps are merged in shared memory at the end.
 #include "gqa_common.cuh"
 #include "gqa_merge.cuh"
@@ -499,14 +505,8 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     for (int s = 0; s < NS && s < n_it; ++s) issue(s, s);
   }
   if constexpr (GRID) {
-    // The next layer's rows of this warp's range, into L2 (its own launch
-    // then streams them from L2), and this launch's q and new row, which are
-    // read right after the dependency wait.
-    if (lane == 0 && p.pf_k != nullptr && n_tok > 0 && early) {
-      const long long off = ((long long)hkv * p.t_max + w0) * kHeadDim;
-      bulk_prefetch_l2(p.pf_k + off, (uint32_t)n_tok * kRowBytes);
-      bulk_prefetch_l2(p.pf_v + off, (uint32_t)n_tok * kRowBytes);
-    }
+    // This launch's q and new row, read right after the dependency wait, into
+    // L2 (coherent there, so a later write by the preceding kernel still wins).
     if (tid == 32 && early) {
       const float* qin = p.qkv + (long long)seq * p.qkv_stride;
       bulk_prefetch_l2(qin + (long long)hkv * G * kHeadDim, G * kRowBytes);
