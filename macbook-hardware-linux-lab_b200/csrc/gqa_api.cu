@@ -4,6 +4,7 @@
 // plumbing in gpu_decoder_layer_step (qwen_server.c:344-455) with argument
 // validation, a split-KV plan and cudaLaunchKernelEx launches.  Errors are
 // returned as gqa_status codes with a thread-local message; nothing exits.
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -99,7 +100,8 @@ struct gqa_exchange {
   cudaIpcMemHandle_t own{};                // handle of base
   void* peer[kMaxExchangeWorld] = {};      // mapped peer allocations (self: base)
   uint2** d_inbox = nullptr;               // device [world]
-  unsigned* epoch = nullptr;               // device [n_rows]
+  unsigned* epoch = nullptr;               // device [n_rows] (exchange kernel's steps)
+  unsigned* slice_epoch = nullptr;         // device [n_rows * kXSlices] (fused path's steps)
   bool opened = false;
 };
 
@@ -1255,12 +1257,19 @@ int gqa_exchange_create(gqa_ctx* c, int rank, int world, gqa_exchange** out, voi
   x->rank = rank;
   x->world = world;
   x->n_rows = c->cfg.n_heads_q;
-  const size_t bytes = exchange_inbox_bytes(world, x->n_rows);
+  // One inbox serves either form of the merge: the exchange kernel's slots or
+  // the fused split kernel's per-slice slots (kXSlotWords words each).
+  const size_t fused_bytes =
+      sizeof(unsigned long long) * 2ull * world * x->n_rows * kXSlices * kXSlotWords;
+  const size_t bytes = std::max(exchange_inbox_bytes(world, x->n_rows), fused_bytes);
   cudaIpcMemHandle_t h;
   cudaError_t e = cudaMalloc(&x->base, bytes);
   if (e == cudaSuccess) e = cudaMemset(x->base, 0, bytes);
   if (e == cudaSuccess) e = cudaMalloc(&x->epoch, sizeof(unsigned) * x->n_rows);
   if (e == cudaSuccess) e = cudaMemset(x->epoch, 0, sizeof(unsigned) * x->n_rows);
+  if (e == cudaSuccess) e = cudaMalloc(&x->slice_epoch, sizeof(unsigned) * x->n_rows * kXSlices);
+  if (e == cudaSuccess)
+    e = cudaMemset(x->slice_epoch, 0, sizeof(unsigned) * x->n_rows * kXSlices);
   if (e == cudaSuccess) e = cudaMalloc(&x->d_inbox, sizeof(uint2*) * world);
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, x->base);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -1300,6 +1309,63 @@ int gqa_exchange_open(gqa_exchange* x, const void* handles) {
   return GQA_OK;
 }
 
+}  // extern "C"
+
+namespace {
+// One GPU's share of a KV-range-split step as ONE launch: the grid-merged split
+// kernel over this shard's rows (RoPE at the global position, the new row
+// appended only by the shard that holds it), whose merging CTAs merge their
+// slice locally, exchange it with every GPU over peer memory and write the
+// output.  Every rank runs it, also a shard that attends no row (it publishes
+// empty partials), so all ranks take the same steps.
+int shard_exchange_fused(gqa_ctx* c, gqa_exchange* x, cudaStream_t st, const gqa_layer_kv* kv,
+                         const float* qkv, int pos, int shard_begin, int shard_rows, float* out) {
+  int rc = check_kv(c, kv);
+  if (rc != GQA_OK) return rc;
+  if (!qkv || !aligned16(qkv)) return fail(GQA_ERR_INVALID_ARG, "null or unaligned qkv");
+  if (pos < 0 || shard_begin < 0 || shard_rows < 0 || shard_rows > c->cfg.t_max)
+    return fail(GQA_ERR_INVALID_ARG, "pos %d / shard [%d, +%d) invalid (t_max %d)", pos,
+                shard_begin, shard_rows, c->cfg.t_max);
+  const int n_kv = c->cfg.n_heads_kv;
+  long long attended = (long long)pos + 1 - shard_begin;  // global rows [shard_begin, pos]
+  if (attended > shard_rows) attended = shard_rows;
+  if (attended < 0) attended = 0;
+  const bool owns = pos >= shard_begin && pos < shard_begin + shard_rows;
+  const int quant = decode_variant_grid_quant(grid_variant(c));
+  const int target = c->target_ctas > 0 && c->target_ctas < c->n_sm ? c->target_ctas : c->n_sm;
+  int n_splits = target / n_kv;
+  const int most = ceil_div(attended, quant);
+  if (n_splits > most) n_splits = most;
+  if (n_splits > kGridMaxParts) n_splits = kGridMaxParts;
+  if (n_splits < 1) n_splits = 1;
+  DecodeParams p = base_params(c);
+  p.k_base = kv->k_cache;
+  p.v_base = kv->v_cache;
+  p.qkv = qkv;
+  p.rope_override = 1;
+  p.rope_pos = pos;
+  p.skip_append = owns ? 0 : 1;
+  p.len.pos_imm = owns ? pos - shard_begin : 0;
+  p.len.seqlen_imm = (int)attended;
+  p.t_end = (int)attended;
+  p.lengths_stable = 1;
+  p.n_splits = n_splits;
+  p.min_chunk = quant;
+  p.out = out;
+  p.grid_epoch = c->grid_epoch;
+  p.grid_words = c->grid_words;
+  p.allow_empty = 1;
+  p.x_inbox = reinterpret_cast<unsigned long long* const*>(x->d_inbox);
+  p.x_epoch = x->slice_epoch;
+  p.x_rank = x->rank;
+  p.x_world = x->world;
+  GQA_CUDA(launch_decode_split(p, 1, true, st, c->pdl != 0, grid_variant(c)));
+  return GQA_OK;
+}
+}  // namespace
+
+extern "C" {
+
 int gqa_decode_kv_shard_exchange(gqa_ctx* c, gqa_exchange* x, gqa_stream_t stream,
                                  const gqa_layer_kv* kv, const float* qkv, int pos,
                                  int shard_begin, int shard_rows, float* out) {
@@ -1311,6 +1377,8 @@ int gqa_decode_kv_shard_exchange(gqa_ctx* c, gqa_exchange* x, gqa_stream_t strea
   if (!aligned16(out)) return fail(GQA_ERR_INVALID_ARG, "out must be 16-byte aligned");
   DeviceGuard g(c->device);
   cudaStream_t st = (cudaStream_t)stream;
+  if (c->grid_merge && c->grid_ctas_per_sm >= 1 && c->grid_words && x->world <= kXMaxWorld)
+    return shard_exchange_fused(c, x, st, kv, qkv, pos, shard_begin, shard_rows, out);
   CombineParams cp{};
   int rc = shard_partials(c, st, kv, qkv, pos, shard_begin, shard_rows, &cp);
   if (rc != GQA_OK) return rc;
@@ -1326,6 +1394,7 @@ int gqa_exchange_destroy(gqa_exchange* x) {
     if (x->peer[r] && x->peer[r] != x->base) cudaIpcCloseMemHandle(x->peer[r]);
   if (x->d_inbox) cudaFree(x->d_inbox);
   if (x->epoch) cudaFree(x->epoch);
+  if (x->slice_epoch) cudaFree(x->slice_epoch);
   if (x->base) cudaFree(x->base);
   delete x;
   return GQA_OK;

@@ -142,6 +142,16 @@ __device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
+// The same at system scope, for words another GPU stores or polls over NVLink.
+__device__ __forceinline__ void st_tagged_sys(unsigned long long* p, float v, unsigned tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged_sys(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
 __device__ __forceinline__ unsigned tag_of(unsigned long long w) { return (unsigned)(w >> 32); }
 __device__ __forceinline__ float value_of(unsigned long long w) {
   return __uint_as_float((unsigned)w);
@@ -178,6 +188,11 @@ struct Lengths {
 constexpr int kGridRowWords = 144;
 constexpr int kGridMaxParts = 128;   // splits per KV head in a grid-merged launch
 constexpr int kGridEpochWords = 64;  // per-KV-head epochs of one context (n_kv <= 64)
+// Cross-GPU slice exchange of a grid-merged KV-range shard: per (parity, source GPU, q head,
+// 16-dim slice) one slot of kXSlotWords tagged words: M, L, O[16] (padded to 256 bytes).
+constexpr int kXSlotWords = 32;
+constexpr int kXSlices = 8;          // 16-dim slices per q head
+constexpr int kXMaxWorld = 16;
 
 struct DecodeParams {
   // KV caches.  Per sequence s the cache is k_ptrs[s] (device array of
@@ -252,6 +267,23 @@ struct DecodeParams {
   // others).
   unsigned* grid_epoch;
   unsigned long long* grid_words;
+  // With allow_empty set, a launch that attends no row (seq_len 0) is not an
+  // error: every CTA publishes an empty partial (a KV-range shard wholly after
+  // the position still takes part in the exchange).
+  int allow_empty;
+  // Cross-GPU exchange of a KV-range-split sequence (grid-merged launches
+  // only; null x_inbox: none).  Each merging CTA stores its slice's merged
+  // (M, L, O[16]) as tagged words, at system scope, into slot
+  // [parity][x_rank][head][slice] of every GPU's inbox (x_inbox[r]), polls its
+  // own inbox for the x_world sources' words of the step and writes the
+  // output.  The step epoch of (head, slice) is x_epoch[head * 8 + slice] + 1,
+  // stored back by its merging CTA; slots alternate by epoch parity.  A GPU
+  // cannot run two steps ahead of a peer: its step e + 1 waits for the peer's
+  // step-e + 1 words, which the peer stores only after its step-e launch (and
+  // every read of the slots it reuses) has finished.
+  unsigned long long* const* x_inbox;
+  unsigned* x_epoch;
+  int x_rank, x_world;
 };
 
 struct CombineParams {

@@ -63,6 +63,12 @@ struct DecodeSmem {
   int err;
   int gok;                  // grid merge: every word of the slice arrived in time
   unsigned gep;             // grid merge: this launch's epoch
+  // cross-GPU exchange of a merged slice (KV-range shards)
+  float xo[kSliceDims];     // this GPU's un-normalised slice sums
+  float xM;                 // this GPU's slice maximum (log2 units)
+  float xm[kXMaxWorld], xl[kXMaxWorld];
+  float xov[kXMaxWorld][kSliceDims];
+  unsigned xe;              // the slice's step epoch
 };
 
 __device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
@@ -270,6 +276,75 @@ __device__ __forceinline__ void cluster_epilogue(const DecodeParams& p, float (*
   if (tid == 0) p.counters[seq * p.n_kv + hkv] = 0;
 }
 
+// Cross-GPU step of a merged slice (KV-range shards): store this GPU's (M, L,
+// O[16]) into every GPU's inbox as tagged words at system scope, poll this
+// GPU's inbox until every source's words carry the slice's step epoch, and
+// write the merged output.  Thread t publishes / polls word t % 18 of GPU
+// t / 18.  False (status set) when a peer's words did not arrive in time.
+template <int NW, int ST, int NS>
+__device__ __forceinline__ bool exchange_slice(const DecodeParams& p, DecodeSmem<NW, ST, NS>& sm,
+                                               int head, int slice, int slot_id) {
+  constexpr int NT = NW * 32;
+  constexpr int kWords = 2 + kSliceDims;  // M, L, O[16]
+  const int tid = threadIdx.x;
+  const int W = p.x_world, n_q = p.n_kv * kG;
+  const unsigned E = sm.xe;
+  const int par = (int)(E & 1u);
+  auto slot = [&](int src) {
+    return ((((long long)par * W + src) * n_q + head) * kXSlices + slice) * kXSlotWords;
+  };
+  for (int t = tid; t < W * kWords; t += NT) {
+    const int r = t / kWords, w = t % kWords;
+    const float v = w == 0 ? sm.xM : (w == 1 ? sm.slice.L : sm.xo[w - 2]);
+    st_tagged_sys(p.x_inbox[r] + slot(p.x_rank) + w, v, E);
+  }
+  const unsigned long long* own = p.x_inbox[p.x_rank];
+  bool ok = true;
+  for (int t = tid; t < W * kWords; t += NT) {
+    const int src = t / kWords, w = t % kWords;
+    const unsigned long long* a = own + slot(src) + w;
+    unsigned long long v = ld_tagged_sys(a);
+    if (tag_of(v) != E) {
+      const long long t0 = clock64();
+      while (tag_of(v) != E) {
+        if (clock64() - t0 > kWaitBudget) {
+          ok = false;
+          break;
+        }
+        v = ld_tagged_sys(a);
+      }
+    }
+    const float f = value_of(v);
+    if (w == 0)
+      sm.xm[src] = f;
+    else if (w == 1)
+      sm.xl[src] = f;
+    else
+      sm.xov[src][w - 2] = f;
+  }
+  if (!__syncthreads_and(ok)) {
+    // A peer did not arrive: report it, leave the output and the epoch as they are.
+    if (tid == 0) atomicOr(p.status, kStatusWaitTimeout);
+    return false;
+  }
+  if (tid < kSliceDims) {
+    float Mg = -CUDART_INF_F;
+    for (int src = 0; src < W; ++src)
+      if (sm.xl[src] > 0.f) Mg = fmaxf(Mg, sm.xm[src]);
+    float Lg = 0.f, Og = 0.f;
+    for (int src = 0; src < W; ++src) {
+      if (sm.xl[src] > 0.f) {
+        const float w = exp2f(sm.xm[src] - Mg);
+        Lg += w * sm.xl[src];
+        Og += w * sm.xov[src][tid];
+      }
+    }
+    p.out[(long long)head * kHeadDim + slice * kSliceDims + tid] = Lg > 0.f ? Og / Lg : 0.f;
+  }
+  if (tid == 0) st_relaxed_gpu(p.x_epoch + slot_id, E);
+  return true;
+}
+
 // Grid merge of one single-sequence launch (GRID instance).  Every CTA has
 // stored its partial for its split and its 6 q heads as tagged words (value,
 // epoch) at grid_words [q head][split][kGridRowWords] (o[128], m in log2
@@ -301,6 +376,8 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
     const unsigned long long* rows = p.grid_words + (long long)head * S * kGridRowWords;
     if (s != split) __syncthreads();  // the previous slice's shared memory is free
     if (tid == 0) sm.gok = 1;
+    const int slot_id = head * kXSlices + s % kSlices;  // the slice's exchange slot
+    if (tid == 0 && p.x_inbox != nullptr) sm.xe = ld_relaxed_gpu_u32(p.x_epoch + slot_id) + 1u;
 
     unsigned long long wo[kSliceChunk];
 #pragma unroll
@@ -369,7 +446,10 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
         }
       }
       ls = warp_sum(ls);
-      if (lane == 0) sm.slice.L = ls;
+      if (lane == 0) {
+        sm.slice.L = ls;
+        sm.xM = mx;
+      }
     }
     __syncthreads();
     if (!sm.gok) {
@@ -399,7 +479,14 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
 #pragma unroll
       for (int w = 0; w < kSliceThreads / 32; ++w) sum += sm.slice.red[w][tid];
       const float L = sm.slice.L;
-      p.out[(long long)head * kHeadDim + d0 + tid] = L > 0.f ? sum / L : 0.f;
+      if (p.x_inbox == nullptr)
+        p.out[(long long)head * kHeadDim + d0 + tid] = L > 0.f ? sum / L : 0.f;
+      else
+        sm.xo[tid] = sum;
+    }
+    if (p.x_inbox != nullptr) {
+      __syncthreads();  // the slice's sums, L and M are in shared memory
+      if (!exchange_slice<NW, ST, NS>(p, sm, head, s % kSlices, slot_id)) return;
     }
   }
 }
@@ -434,8 +521,11 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   resolve_lengths(p.len, seq, pos, seq_len);
   const int r_end = p.t_end > 0 ? p.t_end : seq_len;
   const bool has_row = FUSED && p.skip_append == 0;  // this launch holds the new token's row
-  const bool bad = seq_len < 1 || seq_len > p.t_max || (has_row && (pos < 0 || pos >= p.t_max)) ||
-                   p.t_begin < 0 || r_end > p.t_max || p.t_begin >= r_end;
+  // An empty KV-range shard (allow_empty, no row attended) is not an error.
+  const bool none = p.allow_empty != 0 && r_end == p.t_begin;
+  const bool bad = (!none && seq_len < 1) || seq_len > p.t_max ||
+                   (has_row && (pos < 0 || pos >= p.t_max)) || p.t_begin < 0 ||
+                   r_end > p.t_max || (!none && p.t_begin >= r_end);
   if (bad) {
     if (early) pdl_wait();
     if (tid == 0) atomicOr(p.status, kStatusBadLength);
@@ -1092,7 +1182,7 @@ cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cu
   void* args[] = {&copy};
   if (p.grid_words != nullptr) {
     // Grid-merged single-sequence launch: the output is final when it ends.
-    if (!fused || n_seq != 1 || !v.fused_grid || p.n_splits < kG ||
+    if (!fused || n_seq != 1 || !v.fused_grid || p.n_splits < 1 ||
         p.n_splits > kGridMaxParts || p.out == nullptr)
       return cudaErrorInvalidValue;
     copy.quant = v.grid_quant;

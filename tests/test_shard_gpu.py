@@ -167,6 +167,9 @@ def test_exchange_absent_peer_times_out(pkg, cuda):
         assert ctx.device_status() == 0
 
 
+TWO_GPU_POSITIONS = [2000, 4095, 4096, 8191]
+
+
 def _exchange_worker(rank, world, port, q):
     import torch
     import torch.distributed as dist
@@ -177,7 +180,9 @@ def _exchange_worker(rank, world, port, q):
                             timeout=datetime.timedelta(seconds=60))
     import __graft_entry__
     g = __graft_entry__.load_package()
-    t_max, positions = 8192, [8188, 8189, 8190, 8191]
+    # 2000 and 4095: rank 1's shard [4096, 8192) attends no row (it still takes
+    # part); 4096: rank 1 holds the new row and attends only it; 8191: both full.
+    t_max, positions = 8192, TWO_GPU_POSITIONS
     qkv, kc, vc = g.seeded.decode_inputs(78, t_max)
     b, n = g.shard.plan_kv_ranges(t_max, world)[rank]
     outs = []
@@ -213,7 +218,7 @@ def test_kv_shards_over_two_gpus_exchange(pkg, orc, cuda):
     for p in procs:
         p.join(120)
         assert p.exitcode == 0
-    _, _, _, ref = _oracle_steps(pkg, orc, 78, 8192, [8188, 8189, 8190, 8191])
+    _, _, _, ref = _oracle_steps(pkg, orc, 78, 8192, TWO_GPU_POSITIONS)
     for r in range(2):
         st, outs = res[r]
         assert st == 0
