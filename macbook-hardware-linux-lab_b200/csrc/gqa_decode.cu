@@ -51,7 +51,7 @@ struct DecodeSmem {
   float v[NW][NS][ST * kHeadDim];
   float cs[kHalf][2];
   float q[kG][kHeadDim];  // raw (pre-RoPE) q of the group, staged once per CTA
-  float p[NW][ST][8];
+  float p[NW][ST][12];    // p of each token's 6 heads, each value twice (f32x2 operands)
   float wm[NW][kG];
   float lp[NW][ST][8];  // per-warp l partials, one row per owner token
   float wa[NW][kG];   // per-warp merge weights
@@ -70,6 +70,14 @@ struct DecodeSmem {
   float xov[kXMaxWorld][kSliceDims];
   unsigned xe;              // the slice's step epoch
 };
+
+// 2^x by the hardware's approximate exponential (ex2.approx.ftz: relative error
+// about 2^-22, 0 for -inf), for softmax weights.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ int ceil_div_i(int a, int b) { return (a + b - 1) / b; }
 __device__ __forceinline__ int round_up_i(int a, int b) { return ceil_div_i(a, b) * b; }
@@ -137,15 +145,34 @@ struct Bfly {
 #pragma unroll
     for (int i = 0; i < N / 2; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i + N / 2], OFF);
   }
+  // The same with the adds paired into f32x2 operations (half the add
+  // instructions; the sums are the same, value for value).
+  template <int N, int OFF>
+  __device__ __forceinline__ static void halve_permuted2(float* v) {
+    constexpr int K = N / 2;
+#pragma unroll
+    for (int i = 0; i + 1 < K; i += 2) {
+      const float2 r = make_float2(__shfl_xor_sync(0xffffffffu, v[i + K], OFF),
+                                   __shfl_xor_sync(0xffffffffu, v[i + 1 + K], OFF));
+      const float2 s = __fadd2_rn(make_float2(v[i], v[i + 1]), r);
+      v[i] = s.x;
+      v[i + 1] = s.y;
+    }
+    if constexpr (K % 2) v[K - 1] += __shfl_xor_sync(0xffffffffu, v[2 * K - 1], OFF);
+  }
   __device__ __forceinline__ static void run_permuted(float* v) {
-    halve_permuted<ST * 6, 16>(v);
-    if constexpr (H >= 2) halve_permuted<ST * 3, 8>(v);
-    if constexpr (H >= 3) halve_permuted<ST * 3 / 2, 4>(v);
-    if constexpr (H >= 4) halve_permuted<ST * 3 / 4, 2>(v);
+    halve_permuted2<ST * 6, 16>(v);
+    if constexpr (H >= 2) halve_permuted2<ST * 3, 8>(v);
+    if constexpr (H >= 3) halve_permuted2<ST * 3 / 2, 4>(v);
+    if constexpr (H >= 4) halve_permuted2<ST * 3 / 4, 2>(v);
 #pragma unroll
     for (int off = 1 << (kLowBits - 1); off > 0; off >>= 1) {
-#pragma unroll
-      for (int i = 0; i < 3; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], off);
+      const float2 r = make_float2(__shfl_xor_sync(0xffffffffu, v[0], off),
+                                   __shfl_xor_sync(0xffffffffu, v[1], off));
+      const float2 s = __fadd2_rn(make_float2(v[0], v[1]), r);
+      v[2] += __shfl_xor_sync(0xffffffffu, v[2], off);
+      v[0] = s.x;
+      v[1] = s.y;
     }
   }
   __device__ __forceinline__ static int token(int lane) { return lane >> (6 - H); }
@@ -694,13 +721,14 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     }
   }
 
-  float o[G][4];
+  // o[h] dims 4l..4l+1 in oa[h], 4l+2..4l+3 in ob[h]: f32x2 accumulators.
+  float2 oa[G], ob[G];
   float m[G];
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     m[h] = -CUDART_INF_F;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o[h][j] = 0.f;
+    oa[h] = make_float2(0.f, 0.f);
+    ob[h] = make_float2(0.f, 0.f);
   }
   const int tt = B::token(lane);     // token this lane's scores belong to
   const int hb = B::head0(lane);     // first of this lane's three heads
@@ -711,14 +739,12 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   // token tp ^ tt and head hp with its triple swapped when `hi` -- so that
   // every butterfly exchange keeps the lower half and sends the upper half
   // with no select (Bfly::run_permuted).  The q registers are swapped once.
-  float qs[G][4];
+  float2 qa[G], qb[G];  // dims 4l..4l+1 and 4l+2..4l+3 of the (swapped) heads
 #pragma unroll
   for (int h = 0; h < G; ++h) {
     const float4 t = reinterpret_cast<const float4*>(sm.q[hi ? (h + 3) % G : h])[lane];
-    qs[h][0] = t.x;
-    qs[h][1] = t.y;
-    qs[h][2] = t.z;
-    qs[h][3] = t.w;
+    qa[h] = make_float2(t.x, t.y);
+    qb[h] = make_float2(t.z, t.w);
   }
   float lown[3] = {0.f, 0.f, 0.f};  // this owner lane's share of l for its heads
   int consumed = 0;
@@ -757,10 +783,12 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
         const int t = tp ^ tt;
         if (decltype(full)::value || t < nt) {
           const float4 kv = reinterpret_cast<const float4*>(ks + t * kHeadDim)[lane];
+          const float2 k01 = make_float2(kv.x, kv.y), k23 = make_float2(kv.z, kv.w);
 #pragma unroll
-          for (int h = 0; h < G; ++h)
-            part[tp * G + h] =
-                qs[h][0] * kv.x + qs[h][1] * kv.y + qs[h][2] * kv.z + qs[h][3] * kv.w;
+          for (int h = 0; h < G; ++h) {
+            const float2 d = __ffma2_rn(qb[h], k23, __fmul2_rn(qa[h], k01));
+            part[tp * G + h] = d.x + d.y;
+          }
         } else {
 #pragma unroll
           for (int h = 0; h < G; ++h) part[tp * G + h] = 0.f;
@@ -800,9 +828,9 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
 #pragma unroll
       for (int h = 0; h < G; ++h) {
         const float mnew = fmaxf(m[h], mx[h]);
-        const float alpha = (mnew == -CUDART_INF_F) ? 1.f : exp2f(m[h] - mnew);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o[h][j] *= alpha;
+        const float alpha = (mnew == -CUDART_INF_F) ? 1.f : fast_exp2(m[h] - mnew);
+        oa[h] = __fmul2_rn(oa[h], make_float2(alpha, alpha));
+        ob[h] = __fmul2_rn(ob[h], make_float2(alpha, alpha));
         if ((h / 3) == (hi ? 1 : 0)) lown[h % 3] *= alpha;
         m[h] = mnew;
       }
@@ -811,12 +839,12 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     }
     float pv[3];
 #pragma unroll
-    for (int i = 0; i < 3; ++i) pv[i] = exp2f(sc[i] - mo[i]);
+    for (int i = 0; i < 3; ++i) pv[i] = fast_exp2(sc[i] - mo[i]);
     if (own) {
 #pragma unroll
       for (int i = 0; i < 3; ++i) {
         lown[i] += pv[i];
-        sm.p[warp][tt][hb + i] = pv[i];
+        *reinterpret_cast<float2*>(&sm.p[warp][tt][2 * (hb + i)]) = make_float2(pv[i], pv[i]);
       }
     }
     __syncwarp();
@@ -826,16 +854,18 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
 #pragma unroll
       for (int t = 0; t < ST; ++t) {
         if (decltype(full)::value || t < nt) {
-          const float4 pa = *reinterpret_cast<const float4*>(&sm.p[warp][t][0]);
-          const float2 pb = *reinterpret_cast<const float2*>(&sm.p[warp][t][4]);
+          const float4 p01 = *reinterpret_cast<const float4*>(&sm.p[warp][t][0]);
+          const float4 p23 = *reinterpret_cast<const float4*>(&sm.p[warp][t][4]);
+          const float4 p45 = *reinterpret_cast<const float4*>(&sm.p[warp][t][8]);
           const float4 vv = reinterpret_cast<const float4*>(vs + t * kHeadDim)[lane];
-          const float pr[6] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y};
+          const float2 v01 = make_float2(vv.x, vv.y), v23 = make_float2(vv.z, vv.w);
+          const float2 pr[6] = {make_float2(p01.x, p01.y), make_float2(p01.z, p01.w),
+                                make_float2(p23.x, p23.y), make_float2(p23.z, p23.w),
+                                make_float2(p45.x, p45.y), make_float2(p45.z, p45.w)};
 #pragma unroll
           for (int h = 0; h < G; ++h) {
-            o[h][0] += pr[h] * vv.x;
-            o[h][1] += pr[h] * vv.y;
-            o[h][2] += pr[h] * vv.z;
-            o[h][3] += pr[h] * vv.w;
+            oa[h] = __ffma2_rn(pr[h], v01, oa[h]);
+            ob[h] = __ffma2_rn(pr[h], v23, ob[h]);
           }
         }
       }
@@ -875,7 +905,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
 #pragma unroll
   for (int h = 0; h < G; ++h)
     reinterpret_cast<float4*>(ow + h * kHeadDim)[lane] =
-        make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
+        make_float4(oa[h].x, oa[h].y, ob[h].x, ob[h].y);
   __syncthreads();
   if (!CLUSTER && !GRID && sm.err) return;
 
