@@ -136,6 +136,7 @@ struct gqa_ctx {
   // off falls back to split kernel + combine kernel.
   int grid_merge = 1;
   int grid_ctas_per_sm = 0;                   // resident CTAs of the grid instance per SM
+  int grid_ctas_per_sm_long = 0;              // the same for the long-range shape (variant 3)
   unsigned* grid_epoch = nullptr;             // [kGridEpochWords] per-KV-head launch epochs
   unsigned long long* grid_words = nullptr;   // tagged partials [n_q][kGridMaxParts][row]
   float* blk_qkv = nullptr;   // attention block workspace: qkv of the token
@@ -270,6 +271,17 @@ int plan_splits_single(const gqa_ctx* c, int rows_kv, int len) {
 // layer's CTAs can become resident beside the running ones).
 int grid_variant(const gqa_ctx* c) { return c->variant >= 0 ? c->variant : 0; }
 
+// The grid-merged shape for `len` rows over n_splits splits: the forced variant,
+// or 8 warps x 8-row stages (variant 3, one CTA per SM) once a warp has more
+// than 16 rows to stream, else variant 0.  Measured: long1 (443 rows per CTA)
+// 15.7 us per step with variant 3 against 18.9 with variant 0; resident28 (56
+// rows per CTA) 163 us per step with variant 0 against 178 with variant 3.
+int grid_variant_for(const gqa_ctx* c, long long len, int n_splits) {
+  if (c->variant >= 0) return c->variant;
+  const long long rows_per_warp = (len + (long long)n_splits * 8 - 1) / ((long long)n_splits * 8);
+  return rows_per_warp > 16 && c->grid_ctas_per_sm_long >= 1 ? 3 : 0;
+}
+
 // Splits of a grid-merged single-sequence decode over `len` rows, or 0 when
 // the grid merge cannot be used: at least 6 splits, at most kGridMaxParts,
 // and every CTA of the launch resident at once (its mergers wait on the other
@@ -355,11 +367,12 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
     p.len = len;
     p.lengths_stable = lengths_stable ? 1 : 0;
     p.n_splits = grid_splits;
-    p.min_chunk = decode_variant_grid_quant(grid_variant(c));
+    const int gv = grid_variant_for(c, plan_len, grid_splits);
+    p.min_chunk = decode_variant_grid_quant(gv);
     p.out = out;
     p.grid_epoch = c->grid_epoch;
     p.grid_words = c->grid_words;
-    GQA_CUDA(launch_decode_split(p, 1, true, st, pdl_first, grid_variant(c)));
+    GQA_CUDA(launch_decode_split(p, 1, true, st, pdl_first, gv));
     return GQA_OK;
   }
   int n_splits = plan_splits_single(c, n_kv, plan_len);
@@ -658,6 +671,7 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
   if (e == cudaSuccess && tuned) e = cudaMalloc(&c->grid_words, grid_words_bytes);
   if (e == cudaSuccess && tuned) e = cudaMemset(c->grid_words, 0, grid_words_bytes);
   if (e == cudaSuccess) c->grid_ctas_per_sm = decode_grid_ctas_per_sm(grid_variant(c));
+  if (e == cudaSuccess) c->grid_ctas_per_sm_long = decode_grid_ctas_per_sm(3);
   if (e == cudaSuccess) {
     c->head_grid = lm_head_grid(c->n_sm);
     e = cudaMalloc(&c->head_best, lm_head_best_bytes(c->head_grid));
@@ -1350,7 +1364,8 @@ int shard_exchange_fused(gqa_ctx* c, gqa_exchange* x, cudaStream_t st, const gqa
   p.t_end = (int)attended;
   p.lengths_stable = 1;
   p.n_splits = n_splits;
-  p.min_chunk = quant;
+  const int gv = grid_variant_for(c, attended, n_splits);
+  p.min_chunk = decode_variant_grid_quant(gv);
   p.out = out;
   p.grid_epoch = c->grid_epoch;
   p.grid_words = c->grid_words;
@@ -1359,7 +1374,7 @@ int shard_exchange_fused(gqa_ctx* c, gqa_exchange* x, cudaStream_t st, const gqa
   p.x_epoch = x->slice_epoch;
   p.x_rank = x->rank;
   p.x_world = x->world;
-  GQA_CUDA(launch_decode_split(p, 1, true, st, c->pdl != 0, grid_variant(c)));
+  GQA_CUDA(launch_decode_split(p, 1, true, st, c->pdl != 0, gv));
   return GQA_OK;
 }
 }  // namespace
