@@ -959,19 +959,31 @@ def run_batched(args, g, ctx, rank, world, local):
     ctx.reserve(n, max_len)
     stream = torch.cuda.current_stream()
 
-    def step(i):
+    def step(i, st=None):
         if i % window == 0:
             dl.copy_(lens_base)
-        ctx.decode_batched(n, kp, vp, qkv, QKV_W, dl, max_len, out, OUT_W, stream)
+        ctx.decode_batched(n, kp, vp, qkv, QKV_W, dl, max_len, out, OUT_W,
+                           st if st is not None else stream)
         dl.add_(1)
 
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
+    # The K timed steps as one CUDA graph (lengths reset at its start, advanced
+    # by one after every step): replays are not bound by the host's launch rate
+    # when a GPU's share of the batch is small.
+    if args.steps > window:
+        raise SystemExit(f"batched: --steps must be at most the window of {window}")
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        cap = torch.cuda.current_stream()
+        for i in range(args.steps):
+            step(i, cap)
+    graph.replay()
+    torch.cuda.synchronize()
 
     def body():
-        for i in range(args.steps):
-            step(i)
+        graph.replay()
 
     with ClockSampler(local) as clk:
         rounds = timed_rounds(body, world, stream)
@@ -991,6 +1003,7 @@ def run_batched(args, g, ctx, rank, world, local):
     status = ctx.device_status()
     if status != 0:
         raise RuntimeError(f"device status {status}")
+    del graph
     return dict(t=t_local, t_e2e=t_e2e, bytes=total_bytes,
                 clocks=clk.summary(), launches=2 * args.steps, launches_per_step=2,
                 h2d=n * QKV_W * 4, d2h=n * OUT_W * 4, tokens=n * args.steps,

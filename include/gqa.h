@@ -544,6 +544,20 @@ GQA_API int gqa_fill_normal(gqa_ctx *ctx, gqa_stream_t stream, float *dst, long 
  * floats): powf(theta, -2*i/head_dim) as in attention_gqa_benchmark.c:143. */
 GQA_API int gqa_inv_freq(const gqa_ctx *ctx, float *out);
 
+/* Phase trace of the split-KV decode kernel, for profiling (no counterpart in
+ * the reference).  Only a library built with -DGQA_PHASE_TRACE records it
+ * (build.py --phase-trace writes libgqa_b200_trace.so); the normal build
+ * returns GQA_ERR_UNSUPPORTED.  Thread 0 of every CTA records 10 words:
+ * {tag = (q pointer << 2) | grid-merged, SM id, globaltimer at start (ns),
+ * clock64 at start, clock64 when the dependency wait returned, when q was
+ * staged, when warp 0's loop ended, when the partial was stored, when the
+ * merged slice's words had all arrived, when the merged slice was stored}
+ * (0 = not reached).  Copies up to max_records records of the current device
+ * to `records`, sets *n_records to the number recorded since the last reset
+ * (at most 65536), and with reset != 0 starts over. */
+GQA_API int gqa_phase_trace_read(unsigned long long *records, int max_records, int reset,
+                                 int *n_records);
+
 /* Version string of the library. */
 GQA_API const char *gqa_version(void);
 

@@ -28,27 +28,34 @@ def sources() -> list[str]:
                   glob.glob(os.path.join(HERE, "csrc", "*.cpp")))
 
 
-def needs_rebuild() -> bool:
-    if not os.path.exists(LIB):
+# The same sources with the split kernel's phase trace compiled in (profiling).
+TRACE_LIB = os.path.join(HERE, "libgqa_b200_trace.so")
+
+
+def needs_rebuild(lib: str = LIB) -> bool:
+    if not os.path.exists(lib):
         return True
-    t = os.path.getmtime(LIB)
+    t = os.path.getmtime(lib)
     deps = sources() + glob.glob(os.path.join(HERE, "csrc", "*.cuh")) + [
         os.path.join(REPO, "include", "gqa.h")]
     return any(os.path.getmtime(d) > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not needs_rebuild():
-        return LIB
-    tmp = LIB + ".tmp"
-    cmd = [NVCC, *NVCC_FLAGS, "-I", os.path.join(REPO, "include"), "-shared", "-o", tmp,
+def build(force: bool = False, verbose: bool = False, phase_trace: bool = False) -> str:
+    lib = TRACE_LIB if phase_trace else LIB
+    if not force and not needs_rebuild(lib):
+        return lib
+    tmp = lib + ".tmp"
+    extra = ["-DGQA_PHASE_TRACE"] if phase_trace else []
+    cmd = [NVCC, *NVCC_FLAGS, *extra, "-I", os.path.join(REPO, "include"), "-shared", "-o", tmp,
            *sources()]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    print(build(force="--force" in sys.argv, verbose=True,
+                phase_trace="--phase-trace" in sys.argv))

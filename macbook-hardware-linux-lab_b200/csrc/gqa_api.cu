@@ -27,6 +27,7 @@ cudaError_t launch_decode_split(const DecodeParams& p, int n_seq, bool fused, cu
 int decode_variant_count();
 int decode_variant_quant(int variant);
 int decode_variant_grid_quant(int variant);
+int phase_trace_read(unsigned long long* host, int max_records, bool reset);
 int decode_grid_ctas_per_sm(int variant);
 cudaError_t launch_combine(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl);
 cudaError_t launch_combine_wide(const CombineParams& c, int n_seq, cudaStream_t st, bool pdl);
@@ -1534,6 +1535,20 @@ int gqa_fill_normal(gqa_ctx* c, gqa_stream_t stream, float* dst, long long n,
   z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
   z = z ^ (z >> 31);
   GQA_CUDA(launch_fill_normal(dst, n, z, offset, c->n_sm, (cudaStream_t)stream));
+  return GQA_OK;
+}
+
+int gqa_phase_trace_read(unsigned long long* records, int max_records, int reset,
+                         int* n_records) {
+  if (!n_records || max_records < 0 || (max_records > 0 && !records))
+    return fail(GQA_ERR_INVALID_ARG, "gqa_phase_trace_read: bad arguments");
+  *n_records = 0;
+  const int n = phase_trace_read(records, max_records, reset != 0);
+  if (n == -1)
+    return fail(GQA_ERR_UNSUPPORTED, "this library was built without the phase trace "
+                "(build with -DGQA_PHASE_TRACE)");
+  if (n < 0) return fail(GQA_ERR_CUDA, "gqa_phase_trace_read: copy failed");
+  *n_records = n;
   return GQA_OK;
 }
 

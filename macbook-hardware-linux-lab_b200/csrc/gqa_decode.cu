@@ -69,7 +69,57 @@ struct DecodeSmem {
   float xm[kXMaxWorld], xl[kXMaxWorld];
   float xov[kXMaxWorld][kSliceDims];
   unsigned xe;              // the slice's step epoch
+  unsigned trace_slot;      // phase-trace record of this CTA (traced builds)
 };
+
+// ---------------------------------------------------------------------------
+// Phase trace (opt-in build with -DGQA_PHASE_TRACE; the stamps compile to
+// nothing otherwise).  Thread 0 of every CTA of the split kernel records one
+// record: {tag, SM id, globaltimer at start, clock64 at start, clock64 at each
+// of kPhaseEvents phase ends}; tag = (q pointer << 2) | grid-merged.  Read
+// with gqa_phase_trace_read; macbook-hardware-linux-lab_b200/phase_trace.py
+// turns a run of the resident decode into a per-phase table.
+// ---------------------------------------------------------------------------
+constexpr int kPhaseEvents = 6;   // wait, q staged, loop, partial stored, poll, merge
+constexpr int kPhaseWords = 4 + kPhaseEvents;
+constexpr int kPhaseRecords = 1 << 16;
+#ifdef GQA_PHASE_TRACE
+static __device__ unsigned long long g_phase_rec[kPhaseRecords * kPhaseWords];
+static __device__ unsigned g_phase_next;
+__device__ __forceinline__ unsigned long long phase_gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define GQA_PHASE_BEGIN(slot, tag)                                                  \
+  do {                                                                              \
+    if (threadIdx.x == 0) {                                                         \
+      unsigned s_ = atomicAdd(&g_phase_next, 1u);                                   \
+      if (s_ >= (unsigned)kPhaseRecords) s_ = kPhaseRecords - 1;                    \
+      unsigned smid_;                                                               \
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid_));                            \
+      unsigned long long* r_ = g_phase_rec + (long long)s_ * kPhaseWords;           \
+      r_[0] = (tag);                                                                \
+      r_[1] = smid_;                                                                \
+      r_[2] = phase_gtime();                                                        \
+      r_[3] = clock64();                                                            \
+      for (int e_ = 0; e_ < kPhaseEvents; ++e_) r_[4 + e_] = 0;                     \
+      (slot) = s_;                                                                  \
+    }                                                                               \
+  } while (0)
+#define GQA_PHASE(slot, ev)                                                         \
+  do {                                                                              \
+    if (threadIdx.x == 0)                                                           \
+      g_phase_rec[(long long)(slot) * kPhaseWords + 3 + (ev)] = clock64();          \
+  } while (0)
+#else
+#define GQA_PHASE_BEGIN(slot, tag) \
+  do {                             \
+  } while (0)
+#define GQA_PHASE(slot, ev) \
+  do {                      \
+  } while (0)
+#endif
 
 // 2^x by the hardware's approximate exponential (ex2.approx.ftz: relative error
 // about 2^-22, 0 for -inf), for softmax weights.
@@ -397,6 +447,7 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
   static_assert(kGroups * kSliceChunk == kGridMaxParts, "parts held in registers");
   constexpr int kSlices = kHeadDim / kSliceDims;
   const int S = p.n_splits;
+  GQA_PHASE(sm.trace_slot, 4);  // partial stored
   for (int s = split; s < kG * kSlices; s += S) {
     const int head = hkv * kG + s / kSlices;
     const int d0 = (s % kSlices) * kSliceDims;
@@ -455,6 +506,7 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
       }
     }
     if (!ok) sm.gok = 0;  // benign race: every writer stores 0
+    if (s == split) GQA_PHASE(sm.trace_slot, 5);  // the slice's words all arrived
     if (warp == 0) {
       float mx = -CUDART_INF_F;
 #pragma unroll
@@ -508,6 +560,7 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
       const float L = sm.slice.L;
       if (p.x_inbox == nullptr)
         p.out[(long long)head * kHeadDim + d0 + tid] = L > 0.f ? sum / L : 0.f;
+      if (s == split) GQA_PHASE(sm.trace_slot, 6);  // merged slice stored
       else
         sm.xo[tid] = sum;
     }
@@ -527,6 +580,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   using B = Bfly<ST>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   DecodeSmem<NW, ST, NS>& sm = *reinterpret_cast<DecodeSmem<NW, ST, NS>*>(smem_raw);
+  GQA_PHASE_BEGIN(sm.trace_slot, ((unsigned long long)(uintptr_t)p.qkv << 2) | (GRID ? 1u : 0u));
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x, hkv = blockIdx.y, seq = blockIdx.z;
@@ -649,6 +703,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   }
   if (early) pdl_wait();
   if constexpr (!GRID) pdl_launch_dependents();
+  GQA_PHASE(sm.trace_slot, 1);  // dependency released
   if (FUSED && !early) {
     rope_table();
     __syncthreads();
@@ -735,6 +790,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
   const bool hi = hb != 0;
   const bool own = B::owner(lane);   // one lane per (token, head triple) writes p
   __syncthreads();  // rotated q staged
+  GQA_PHASE(sm.trace_slot, 2);
   // Partials are stored in a lane-dependent order -- position (tp, hp) holds
   // token tp ^ tt and head hp with its triple swapped when `hi` -- so that
   // every butterfly exchange keeps the lower half and sends the upper half
@@ -878,6 +934,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     }
   }
 
+  GQA_PHASE(sm.trace_slot, 3);  // this warp's loop done (thread 0: warp 0)
   if (failed) {
     // Drain whatever this warp still has in flight (bounded), then report.
     const int issued = min(n_it, consumed + NS);
@@ -1148,6 +1205,31 @@ static const Variant& decode_variant(int i) {
   };
   constexpr int n = sizeof(table) / sizeof(table[0]);
   return table[(i >= 0 && i < n) ? i : 0];
+}
+
+// Copies up to max_records phase-trace records (kPhaseWords words each) to
+// host memory; returns how many were recorded (-1: a build without the trace).
+int phase_trace_read(unsigned long long* host, int max_records, bool reset) {
+#ifdef GQA_PHASE_TRACE
+  unsigned n = 0;
+  if (cudaMemcpyFromSymbol(&n, g_phase_next, sizeof(n)) != cudaSuccess) return -2;
+  if (n > (unsigned)kPhaseRecords) n = kPhaseRecords;
+  const int copy = (int)n < max_records ? (int)n : max_records;
+  if (host && copy > 0 &&
+      cudaMemcpyFromSymbol(host, g_phase_rec, sizeof(unsigned long long) * kPhaseWords * copy) !=
+          cudaSuccess)
+    return -2;
+  if (reset) {
+    const unsigned zero = 0;
+    if (cudaMemcpyToSymbol(g_phase_next, &zero, sizeof(zero)) != cudaSuccess) return -2;
+  }
+  return (int)n;
+#else
+  (void)host;
+  (void)max_records;
+  (void)reset;
+  return -1;
+#endif
 }
 
 int decode_variant_count() { return 7; }

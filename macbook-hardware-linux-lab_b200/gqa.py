@@ -23,7 +23,8 @@ import re
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libgqa_b200.so")
+# GQA_LIB selects another build of the library (e.g. the phase-trace build).
+LIB_PATH = os.environ.get("GQA_LIB") or os.path.join(_HERE, "libgqa_b200.so")
 HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "gqa.h")
 
 GQA_OK = 0
@@ -170,6 +171,7 @@ _SIGNATURES = {
     "gqa_layer_attention_static": [ctypes.POINTER(Config), _vp, ctypes.POINTER(LayerKV), _vp, _i,
                                    _i],
     "gqa_static_status": [_i, ctypes.POINTER(_i), _i],
+    "gqa_phase_trace_read": [_vp, _i, _i, ctypes.POINTER(_i)],
 }
 _RESTYPES = {"gqa_last_error_string": ctypes.c_char_p, "gqa_version": ctypes.c_char_p,
              "gqa_lm_head_packed_bytes": ctypes.c_longlong,
