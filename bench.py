@@ -1185,8 +1185,12 @@ def run_ours(args):
                  "merge and gaps)")
     extra = None
     if args.workload == "resident28" and not args.no_extra:
-        extra = {name: run_extra(args, g, name, rank, world, local)
-                 for name in ("batched", "long1")}
+        extra = {}
+        for name in ("batched", "long1"):
+            try:
+                extra[name] = run_extra(args, g, name, rank, world, local)
+            except Exception as exc:  # a sharded extra never takes the headline line down
+                extra[name] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if args.workload in ("block28", "layer28"):
