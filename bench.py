@@ -1102,16 +1102,14 @@ def run_prefill(args, g, ctx, rank, world, local):
     for _ in range(args.warmup):
         ctx.prefill_bf16(n, S, x, out)
     torch.cuda.synchronize()
-    barrier(world)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        ev0.record(stream)
+
+    def body():
         for _ in range(args.steps):
             ctx.prefill_bf16(n, S, x, out)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-    barrier(world)
-    t_local = ev0.elapsed_time(ev1) / 1e3
+
+    with ClockSampler(local) as clk:
+        rounds = timed_rounds(body, world, stream)
+    t_local = statistics.median(rounds)
     h_x = x.cpu().pin_memory()
     h_out = torch.empty(out.shape).pin_memory()
     barrier(world)
@@ -1129,7 +1127,7 @@ def run_prefill(args, g, ctx, rank, world, local):
     return dict(t=t_local, t_e2e=e0.elapsed_time(e1) / 1e3, flops=flops * args.steps,
                 clocks=clk.summary(), launches=2 * args.steps, launches_per_step=2,
                 h2d=x.numel() * 4, d2h=out.numel() * 4, tokens=n * S * args.steps,
-                dominant_launches=args.steps)
+                dominant_launches=args.steps, rounds=len(rounds), timed_s=sum(rounds))
 
 
 def run_ours(args):
@@ -1186,7 +1184,7 @@ def run_ours(args):
     extra = None
     if args.workload == "resident28" and not args.no_extra:
         extra = {}
-        for name in ("batched", "long1"):
+        for name in ("batched", "long1", "prefill"):
             try:
                 extra[name] = run_extra(args, g, name, rank, world, local)
             except Exception as exc:  # a sharded extra never takes the headline line down
@@ -1260,25 +1258,35 @@ def k_nondefault(args):
 
 def run_extra(args, g, name, rank, world, local):
     """One of the sharded configurations timed in the default run: `batched`
-    (64 sequences dealt to the ranks, strong scaling) or `long1` (one 32768-row
-    sequence split by KV range over the ranks, merged over peer memory)."""
+    (64 sequences dealt to the ranks, strong scaling), `long1` (one 32768-row
+    sequence split by KV range over the ranks, merged over peer memory) or
+    `prefill` (8 prompts of 2048 tokens dealt to the ranks, strong scaling)."""
     import copy
     sub = copy.copy(args)
     sub.workload = name
     if name == "long1":
         sub.steps = WORKLOADS["long1"]["window"]  # the peer-exchange graph holds one window
         t_max = max(n for _, n in g.shard.plan_kv_ranges(WORKLOADS["long1"]["t_max"], world))
+    elif name == "prefill":
+        t_max = WORKLOADS["prefill"]["t_max"]
     else:
         t_max = WORKLOADS[name]["len_hi"] + WORKLOADS[name]["window"]
     ctx = g.Context(t_max=t_max, device=local)
     try:
-        r = run_long1(sub, g, ctx, rank, world, local) if name == "long1" else \
-            run_batched(sub, g, ctx, rank, world, local)
+        runner = {"long1": run_long1, "prefill": run_prefill}.get(name, run_batched)
+        r = runner(sub, g, ctx, rank, world, local)
     finally:
         ctx.close()
     t = max_over_ranks(r["t"], world)
-    total = sum_over_ranks(r["bytes"], world)
     tokens = sum_over_ranks(r["tokens"], world)
+    if name == "prefill":
+        flops = sum_over_ranks(r["flops"], world)
+        return {"workload": workload_config(name)["workload"],
+                "value": round(flops / t / 1e12, 1), "unit": "TFLOP/s",
+                "ms_per_step": round(t / sub.steps * 1e3, 5), "steps": sub.steps,
+                "tok_per_s": round(tokens / t, 1), "scaling": "strong",
+                "rounds": r["rounds"], "clocks": r["clocks"]}
+    total = sum_over_ranks(r["bytes"], world)
     return {"workload": workload_config(name, args.exchange)["workload"],
             "value": round(total / t / 1e9, 2), "unit": "GB/s",
             "ms_per_step": round(t / sub.steps * 1e3, 5), "steps": sub.steps,

@@ -224,3 +224,56 @@ def test_kv_shards_over_two_gpus_exchange(pkg, orc, cuda):
         assert st == 0
         for got, want in zip(outs, ref):
             assert nerr(got, want) <= TOL
+
+
+def _prefill_worker(rank, world, seqs, S, q):
+    import torch
+    torch.cuda.set_device(rank)
+    import __graft_entry__
+    g = __graft_entry__.load_package()
+    mine = g.shard.plan_sequence_shards([S] * seqs, world)[rank]
+    res = {}
+    with g.Context(t_max=S, device=rank) as ctx:
+        for s in mine:
+            x = g.seeded.normal(4400 + s, g.seeded.PREFILL_Q, S * 2048).reshape(1, S, 2048)
+            d_x = torch.from_numpy(x).cuda()
+            out = torch.zeros((1, S, 1536), device="cuda")
+            kc = torch.zeros((1, 2, S, 128), device="cuda")
+            vc = torch.zeros((1, 2, S, 128), device="cuda")
+            kp = torch.tensor([kc.data_ptr()], dtype=torch.int64, device="cuda")
+            vp = torch.tensor([vc.data_ptr()], dtype=torch.int64, device="cuda")
+            ctx.prefill_bf16(1, S, d_x, out, kp, vp)
+            torch.cuda.synchronize()
+            res[s] = (out.cpu().numpy()[0], kc.cpu().numpy()[0], vc.cpu().numpy()[0])
+        status = ctx.device_status()
+    q.put((rank, status, res))
+
+
+def test_prefill_sequences_over_two_gpus(pkg, orc, cuda):
+    """Causal prefill sharded by sequence: four prompts dealt to two GPUs
+    (no collective on the data path), each GPU's outputs and appended cache
+    rows checked against the oracle on the same bf16 operands."""
+    torch = cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import test_prefill_gpu as tp
+    seqs, S = 4, 256
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_prefill_worker, args=(r, 2, seqs, S, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in range(2):
+        rank, st, res = q.get(timeout=300)
+        assert st == 0, rank
+        assert len(res) == seqs // 2, rank  # equal prompts: two per GPU
+        got.update(res)
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    assert sorted(got) == list(range(seqs))
+    for s in range(seqs):
+        x = pkg.seeded.normal(4400 + s, pkg.seeded.PREFILL_Q, S * 2048).reshape(S, 2048)
+        out, kc, vc = got[s]
+        tp.check_sequence(torch, orc, x, out, list(range(0, S, 3)) + [S - 1], kc, vc)
