@@ -72,9 +72,7 @@ cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cach
                                      Lengths len, int t_max, int n_q, int n_kv, int head_dim,
                                      int n_splits, int plan_len, const float* inv_freq,
                                      float* part_o, float* part_ml, int* status, cudaStream_t st,
-                                     bool pdl_first, bool pdl, bool lengths_stable,
-                                     unsigned* grid_epoch, unsigned long long* grid_words);
-int generic_grid_ctas_per_sm();
+                                     bool pdl_first, bool pdl, bool lengths_stable);
 size_t lm_head_packed_bytes(long long n_rows);
 size_t lm_head_q8_packed_bytes(long long n_rows);
 cudaError_t launch_q8_pack(const void* src, int n_rows, void* dst, cudaStream_t st);
@@ -410,29 +408,15 @@ int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float*
 // lengths_stable: pos / seq_len are not produced by the preceding kernel (see
 // split_generic_kernel).
 int run_generic(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
-                Lengths len, int plan_len, float* out, bool pdl_first, bool lengths_stable,
-                bool grid_ok = true) {
+                Lengths len, int plan_len, float* out, bool pdl_first, bool lengths_stable) {
   const int nq = c->cfg.n_heads_q, nkv = c->cfg.n_heads_kv;
-  int n_splits = generic_plan_splits(nkv, plan_len, c->n_sm);
-  // One grid-merged launch when every split's CTA fits on the device at once
-  // (one per SM), as for the tuned shape.
-  const bool grid = grid_ok && c->grid_merge && c->grid_words && c->grid_ctas_per_sm >= 1 &&
-                    nkv <= kGridEpochWords;
-  if (grid) {
-    const int cap = c->n_sm / nkv;
-    if (n_splits > cap) n_splits = cap;
-    if (n_splits > kGridMaxParts) n_splits = kGridMaxParts;
-    if (n_splits < 1) n_splits = 1;
-  } else {
-    int rc = ensure_scratch(c, (long long)nq * n_splits, st);
-    if (rc != GQA_OK) return rc;
-  }
+  const int n_splits = generic_plan_splits(nkv, plan_len, c->n_sm);
+  int rc = ensure_scratch(c, (long long)nq * n_splits, st);
+  if (rc != GQA_OK) return rc;
   GQA_CUDA(launch_generic_attention(qkv, out, kv->k_cache, kv->v_cache, len, c->cfg.t_max, nq,
                                     nkv, c->cfg.head_dim, n_splits, plan_len, c->inv_freq,
                                     c->part_o, c->part_ml, c->status, st, pdl_first,
-                                    c->layers_pdl != 0, lengths_stable,
-                                    grid ? c->grid_epoch : nullptr,
-                                    grid ? c->grid_words : nullptr));
+                                    c->layers_pdl != 0, lengths_stable));
   return GQA_OK;
 }
 
@@ -524,7 +508,7 @@ int block_impl(gqa_ctx* c, cudaStream_t st, const gqa_block_weights* w, const gq
   GQA_CUDA(launch_qkv_gemv(model, w->w_qkv, w->b_qkv, w->gamma, state, c->blk_qkv,
                            (nq + 2 * nkv) * hd, c->status, st, pdl_first));
   int rc = c->generic ? run_generic(c, st, kv, c->blk_qkv, len, plan_len, c->blk_attn, true,
-                                    lengths_stable, /*grid_ok=*/false)
+                                    lengths_stable)
                       : run_single(c, st, kv, c->blk_qkv, len, plan_len, true, c->blk_attn, true,
                                    lengths_stable, /*grid_ok=*/false);
   if (rc != GQA_OK) return rc;
@@ -685,12 +669,10 @@ int gqa_create(const gqa_config* cfg, int device, gqa_ctx** out) {
       sizeof(unsigned long long) * (size_t)cfg->n_heads_q * kGridMaxParts * kGridRowWords;
   if (e == cudaSuccess) e = cudaMalloc(&c->grid_epoch, kGridEpochWords * sizeof(unsigned));
   if (e == cudaSuccess) e = cudaMemset(c->grid_epoch, 0, kGridEpochWords * sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaMalloc(&c->grid_words, grid_words_bytes);
-  if (e == cudaSuccess) e = cudaMemset(c->grid_words, 0, grid_words_bytes);
-  if (e == cudaSuccess)
-    c->grid_ctas_per_sm = c->generic ? generic_grid_ctas_per_sm()
-                                     : decode_grid_ctas_per_sm(grid_variant(c));
-  if (e == cudaSuccess && !c->generic) c->grid_ctas_per_sm_long = decode_grid_ctas_per_sm(3);
+  if (e == cudaSuccess && tuned) e = cudaMalloc(&c->grid_words, grid_words_bytes);
+  if (e == cudaSuccess && tuned) e = cudaMemset(c->grid_words, 0, grid_words_bytes);
+  if (e == cudaSuccess) c->grid_ctas_per_sm = decode_grid_ctas_per_sm(grid_variant(c));
+  if (e == cudaSuccess) c->grid_ctas_per_sm_long = decode_grid_ctas_per_sm(3);
   if (e == cudaSuccess) {
     c->head_grid = lm_head_grid(c->n_sm);
     e = cudaMalloc(&c->head_best, lm_head_best_bytes(c->head_grid));
@@ -751,7 +733,7 @@ int gqa_set_option(gqa_ctx* c, int option, long long value) {
       if (value < -1 || value >= decode_variant_count())
         return fail(GQA_ERR_INVALID_ARG, "kernel variant out of range (-1 = automatic)");
       c->variant = (int)value;
-      if (!c->generic) c->grid_ctas_per_sm = decode_grid_ctas_per_sm(grid_variant(c));
+      c->grid_ctas_per_sm = decode_grid_ctas_per_sm(grid_variant(c));
       return GQA_OK;
     default: return fail(GQA_ERR_INVALID_ARG, "unknown option %d", option);
   }

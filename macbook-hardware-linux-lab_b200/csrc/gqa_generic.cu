@@ -28,14 +28,7 @@
 //   merge_generic_kernel        one CTA per q head: the splits' (m, l, o) merged
 //                               by log-sum-exp into the output row, all loads
 //                               of a round in flight at once
-// For a single-sequence call whose splits all fit on the device at once, the
-// split kernel's GRID instance does both in one launch: every CTA stores its
-// partial as tagged 64-bit words {value, epoch} and then merges 16-dim slices
-// of its KV head's q heads over all splits, polling the words it needs until
-// they carry the launch's epoch (the scheme of the tuned kernel's grid merge,
-// gqa_decode.cu).
 #include "gqa_common.cuh"
-#include "gqa_merge.cuh"
 
 #include <math_constants.h>
 
@@ -44,7 +37,6 @@ namespace gqa {
 constexpr int kGenThreads = 256;
 constexpr int kGenTile = 64;            // rows per shared-memory tile
 constexpr int kGenMaxSplits = 1024;
-constexpr long long kGenWaitBudget = 2000000000LL;  // ~1 s of SM clocks per wait
 
 template <int D, int G>
 struct GenShape {
@@ -66,11 +58,6 @@ struct GenParams {
   Lengths len;
   int t_max, n_q, n_kv, n_splits, rows_per_split;
   int lengths_stable;     // pos / seq_len not written by the preceding kernel
-  // Grid merge (GRID instance): per-KV-head epochs and the tagged partial rows
-  // [n_q][n_splits][gen_row_words<D>()], both zeroed by the context and used by
-  // no other path; null selects the split + merge kernels.
-  unsigned* grid_epoch;
-  unsigned long long* grid_words;
   const float* inv_freq;  // [D / 2]
   float scale;            // 1 / sqrt(D)
   float* part_o;          // [n_q][n_splits][D]
@@ -101,15 +88,7 @@ struct GenSmem {
   float s[G][kGenTile];     // scores, then weights e^(s - m)
   float m[G], corr[G];      // running max per head, rescale of this tile
   float l[G];               // running sum of the weights per head
-  SliceSmem<kGridMaxParts> slice;  // grid merge
-  unsigned gep;             // grid merge: this launch's epoch
-  int gok;                  // grid merge: every word of the slice arrived in time
 };
-
-// Tagged partial row of the grid merge: o[D] then m (natural-log units), l;
-// padded to whole 128-byte lines so a 16-dim slice is one line.
-template <int D>
-__host__ __device__ constexpr int gen_row_words() { return (D + 2 + 15) / 16 * 16; }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src)
@@ -130,162 +109,21 @@ __device__ __forceinline__ void gen_issue_tile(GenSmem<D, G>& sm, const float* k
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// Grid merge of a GRID launch: store this split's partial as tagged words
-// (o, m in natural-log units, l; m = -inf and l = 0 for a split that attends
-// no row), then merge slices split, split + n_splits, ... of the KV head's
-// G * D / 16 slices (16 dims of one q head) over every split: half-warp hw
-// polls parts hw, hw + 16, ... of its dim until their epoch is current, warp
-// 0 also the parts' (m, l) and forms the maximum, the weights and L.  Once
-// warp 0 has seen every split's (m, l), every CTA of the KV head has read the
-// epoch, which the merging CTA may then store back for the next launch.
 template <int D, int G>
-__device__ __forceinline__ void gen_grid_epilogue(const GenParams& p, GenSmem<D, G>& sm,
-                                                  const float* o, int hkv, int split,
-                                                  bool any_row) {
-  using Sh = GenShape<D, G>;
-  constexpr int RW = gen_row_words<D>();
-  constexpr int kSl = D / kSliceDims;
-  constexpr int kGroups = kSliceThreads / 16;
-  constexpr int kChunk = kGridMaxParts / kGroups;
-  constexpr int kPer = kGridMaxParts / 32;
-  static_assert(kGenThreads == kSliceThreads && D % kSliceDims == 0, "slice merge shape");
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hw = tid >> 4, j = tid & 15;
-  const int S = p.n_splits, qh0 = hkv * G;
-  __syncthreads();  // the epoch is in shared memory, the running (m, l) final
-  const unsigned ep = sm.gep;
-#pragma unroll
-  for (int k = 0; k < Sh::kOutPerThread; ++k) {
-    const int idx = tid + k * kGenThreads;
-    if (idx < Sh::kOut) {
-      const int g = idx / D, d = idx % D;
-      st_tagged(p.grid_words + ((long long)(qh0 + g) * S + split) * RW + d, o[k], ep);
-    }
-  }
-  if (tid < G) {
-    unsigned long long* row = p.grid_words + ((long long)(qh0 + tid) * S + split) * RW;
-    st_tagged(row + D, any_row ? sm.m[tid] : -CUDART_INF_F, ep);
-    st_tagged(row + D + 1, any_row ? sm.l[tid] : 0.f, ep);
-  }
-  for (int s = split; s < G * kSl; s += S) {
-    const int head = qh0 + s / kSl, d0 = (s % kSl) * kSliceDims;
-    const unsigned long long* rows = p.grid_words + (long long)head * S * RW;
-    if (s != split) __syncthreads();  // the previous slice's shared memory is free
-    if (tid == 0) sm.gok = 1;
-    unsigned long long wo[kChunk], wm[kPer], wl[kPer];
-#pragma unroll
-    for (int k = 0; k < kChunk; ++k) {
-      const int i = hw + kGroups * k;
-      wo[k] = i < S ? ld_tagged(rows + (long long)i * RW + d0 + j) : 0ull;
-    }
-    if (warp == 0) {
-#pragma unroll
-      for (int k = 0; k < kPer; ++k) {
-        const int i = lane + 32 * k;
-        wm[k] = i < S ? ld_tagged(rows + (long long)i * RW + D) : 0ull;
-        wl[k] = i < S ? ld_tagged(rows + (long long)i * RW + D + 1) : 0ull;
-      }
-    }
-    bool ok = true;
-    const long long t0 = clock64();
-    for (;;) {
-      bool fresh = true;
-#pragma unroll
-      for (int k = 0; k < kChunk; ++k) {
-        const int i = hw + kGroups * k;
-        if (i < S && tag_of(wo[k]) != ep) {
-          fresh = false;
-          wo[k] = ld_tagged(rows + (long long)i * RW + d0 + j);
-        }
-      }
-      if (warp == 0) {
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-          const int i = lane + 32 * k;
-          if (i < S && tag_of(wm[k]) != ep) {
-            fresh = false;
-            wm[k] = ld_tagged(rows + (long long)i * RW + D);
-          }
-          if (i < S && tag_of(wl[k]) != ep) {
-            fresh = false;
-            wl[k] = ld_tagged(rows + (long long)i * RW + D + 1);
-          }
-        }
-      }
-      if (fresh) break;
-      if (clock64() - t0 > kGenWaitBudget) {
-        ok = false;
-        break;
-      }
-    }
-    if (!ok) sm.gok = 0;  // benign race: every writer stores 0
-    if (warp == 0) {
-      float mx = -CUDART_INF_F;
-#pragma unroll
-      for (int k = 0; k < kPer; ++k)
-        if (lane + 32 * k < S && value_of(wl[k]) > 0.f) mx = fmaxf(mx, value_of(wm[k]));
-      mx = warp_max(mx);
-      float ls = 0.f;
-#pragma unroll
-      for (int k = 0; k < kPer; ++k) {
-        const int i = lane + 32 * k;
-        if (i < S) {
-          const float l = value_of(wl[k]);
-          const float w = l > 0.f ? expf(value_of(wm[k]) - mx) : 0.f;
-          sm.slice.w[i] = w;
-          ls += w * l;
-        }
-      }
-      ls = warp_sum(ls);
-      if (lane == 0) sm.slice.L = ls;
-    }
-    __syncthreads();
-    if (!sm.gok) {
-      if (tid == 0) atomicOr(p.status, kStatusWaitTimeout);
-      return;
-    }
-    if (tid == 0) st_relaxed_gpu(p.grid_epoch + hkv, ep);
-    float acc = 0.f;
-#pragma unroll
-    for (int k = 0; k < kChunk; ++k) {
-      const int i = hw + kGroups * k;
-      if (i < S) {
-        const float w = sm.slice.w[i];
-        if (w != 0.f) acc += w * value_of(wo[k]);
-      }
-    }
-    acc += __shfl_xor_sync(0xffffffffu, acc, 16);
-    if (lane < 16) sm.slice.red[warp][j] = acc;
-    __syncthreads();
-    if (tid < kSliceDims) {
-      float sum = 0.f;
-#pragma unroll
-      for (int w = 0; w < kSliceThreads / 32; ++w) sum += sm.slice.red[w][tid];
-      const float L = sm.slice.L;
-      p.out[(long long)head * D + d0 + tid] = L > 0.f ? sum / L : 0.f;
-    }
-  }
-}
-
-template <int D, int G, bool GRID = false>
 __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenParams p) {
   using S = GenShape<D, G>;
   __shared__ __align__(16) GenSmem<D, G> sm;
-  // A grid-merged launch releases the next kernel at once: its CTAs are
-  // launched only when every CTA of this grid runs, so they can never keep a
-  // CTA of this grid (on which the mergers wait) from an SM.
   // With stable lengths the first tile is requested before the dependency
   // wait: the preceding kernel (the previous layer's merge, a projection, the
   // embedding) writes neither pos nor this layer's cache, and the split that
   // wrote row pos - 1 finished before it could start.  Row pos itself, which
   // this kernel appends, is replaced in shared memory below.
   const bool early = p.lengths_stable != 0;
-  if constexpr (GRID) pdl_launch_dependents();
   if (!early) pdl_wait();
   int pos, seq_len;
   if (!gen_lengths(p, pos, seq_len)) {
     if (early) pdl_wait();
-    if constexpr (!GRID) pdl_launch_dependents();
+    pdl_launch_dependents();
     if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0)
       atomicOr(p.status, kStatusBadLength);
     return;
@@ -302,10 +140,7 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
   const bool owner = split == min(pos / p.rows_per_split, p.n_splits - 1);
   if (t0 < t1) gen_issue_tile(sm, kc, vc, t0, min(kGenTile, t1 - t0), tid);
   if (early) pdl_wait();
-  if constexpr (!GRID) pdl_launch_dependents();
-  // The launch's epoch for the tagged partials (read after the wait: the
-  // previous launch, which may have advanced it, has finished).
-  if (GRID && tid == 0) sm.gep = ld_relaxed_gpu_u32(p.grid_epoch + hkv) + 1u;
+  pdl_launch_dependents();
 
   // ---- RoPE: theta_i = pos * inv_freq[i], pairs (i, i + D/2); each thread
   // takes its own angles, so these loads share a round trip with the first
@@ -432,24 +267,20 @@ __global__ void __launch_bounds__(kGenThreads) split_generic_kernel(const GenPar
     __syncthreads();
   }
 
+  // ---- the split's partial: (m, l, un-normalised o) per q head ----
   const int qh0 = hkv * G;
-  if constexpr (GRID) {
-    gen_grid_epilogue<D, G>(p, sm, o, hkv, split, t1 > t0);
-  } else {
-    // ---- the split's partial: (m, l, un-normalised o) per q head ----
 #pragma unroll
-    for (int k = 0; k < S::kOutPerThread; ++k) {
-      const int idx = tid + k * kGenThreads;
-      if (idx < S::kOut) {
-        const int g = idx / D, d = idx % D;
-        p.part_o[((long long)(qh0 + g) * p.n_splits + split) * D + d] = o[k];
-      }
+  for (int k = 0; k < S::kOutPerThread; ++k) {
+    const int idx = tid + k * kGenThreads;
+    if (idx < S::kOut) {
+      const int g = idx / D, d = idx % D;
+      p.part_o[((long long)(qh0 + g) * p.n_splits + split) * D + d] = o[k];
     }
-    if (tid < G) {
-      float* ml = p.part_ml + ((long long)(qh0 + tid) * p.n_splits + split) * 2;
-      ml[0] = t1 > t0 ? sm.m[tid] : -CUDART_INF_F;
-      ml[1] = t1 > t0 ? sm.l[tid] : 0.f;
-    }
+  }
+  if (tid < G) {
+    float* ml = p.part_ml + ((long long)(qh0 + tid) * p.n_splits + split) * 2;
+    ml[0] = t1 > t0 ? sm.m[tid] : -CUDART_INF_F;
+    ml[1] = t1 > t0 ? sm.l[tid] : 0.f;
   }
 }
 
@@ -557,18 +388,6 @@ bool generic_shape_built(int head_dim, int group) { return head_dim == 64 && gro
 
 int generic_max_splits() { return kGenMaxSplits; }
 
-// CTAs of the grid-merged generic kernel that fit on one SM (its mergers need
-// every CTA of a launch resident at once).
-int generic_grid_ctas_per_sm() {
-  int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, split_generic_kernel<64, 7, true>,
-                                                    kGenThreads, 0) != cudaSuccess) {
-    cudaGetLastError();
-    return 0;
-  }
-  return n;
-}
-
 // Splits for a cache of up to plan_len rows: at least one tile each, enough
 // CTAs to cover the device twice.
 int generic_plan_splits(int n_kv, int plan_len, int n_sm) {
@@ -583,8 +402,7 @@ cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cach
                                      Lengths len, int t_max, int n_q, int n_kv, int head_dim,
                                      int n_splits, int plan_len, const float* inv_freq,
                                      float* part_o, float* part_ml, int* status, cudaStream_t st,
-                                     bool pdl_first, bool pdl, bool lengths_stable,
-                                     unsigned* grid_epoch, unsigned long long* grid_words) {
+                                     bool pdl_first, bool pdl, bool lengths_stable) {
   if (head_dim != 64 || n_q != 7 * n_kv) return cudaErrorInvalidValue;
   constexpr int D = 64, G = 7;
   GenParams p{};
@@ -608,14 +426,6 @@ cudaError_t launch_generic_attention(const float* qkv, float* out, float* k_cach
   p.part_ml = part_ml;
   p.out = out;
   p.status = status;
-  if (grid_words != nullptr) {
-    // One grid-merged launch; the caller keeps every CTA resident at once.
-    if (n_splits > kGridMaxParts || !grid_epoch) return cudaErrorInvalidValue;
-    p.grid_epoch = grid_epoch;
-    p.grid_words = grid_words;
-    return gen_launch(split_generic_kernel<D, G, true>, dim3(n_splits, n_kv), dim3(kGenThreads),
-                      p, st, pdl_first);
-  }
   cudaError_t e = gen_launch(split_generic_kernel<D, G>, dim3(n_splits, n_kv),
                              dim3(kGenThreads), p, st, pdl_first);
   if (e == cudaSuccess)
