@@ -80,10 +80,10 @@ struct DecodeSmem {
 // with gqa_phase_trace_read; macbook-hardware-linux-lab_b200/phase_trace.py
 // turns a run of the resident decode into a per-phase table.
 // ---------------------------------------------------------------------------
+#ifdef GQA_PHASE_TRACE
 constexpr int kPhaseEvents = 6;   // wait, q staged, loop, partial stored, poll, merge
 constexpr int kPhaseWords = 4 + kPhaseEvents;
 constexpr int kPhaseRecords = 1 << 16;
-#ifdef GQA_PHASE_TRACE
 static __device__ unsigned long long g_phase_rec[kPhaseRecords * kPhaseWords];
 static __device__ unsigned g_phase_next;
 __device__ __forceinline__ unsigned long long phase_gtime() {
