@@ -558,11 +558,12 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
 #pragma unroll
       for (int w = 0; w < kSliceThreads / 32; ++w) sum += sm.slice.red[w][tid];
       const float L = sm.slice.L;
-      if (p.x_inbox == nullptr)
+      if (p.x_inbox == nullptr) {
         p.out[(long long)head * kHeadDim + d0 + tid] = L > 0.f ? sum / L : 0.f;
-      if (s == split) GQA_PHASE(sm.trace_slot, 6);  // merged slice stored
-      else
+      } else {
         sm.xo[tid] = sum;
+      }
+      if (s == split) GQA_PHASE(sm.trace_slot, 6);  // merged slice stored
     }
     if (p.x_inbox != nullptr) {
       __syncthreads();  // the slice's sums, L and M are in shared memory
