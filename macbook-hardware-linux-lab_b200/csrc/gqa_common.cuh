@@ -137,6 +137,13 @@ __device__ __forceinline__ void st_tagged(unsigned long long* p, float v, unsign
   const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+// Two consecutive tagged words by one vector load (16-byte aligned); each
+// element is its own single-copy-atomic 64-bit access.
+__device__ __forceinline__ void ld_tagged2(const unsigned long long* p, unsigned long long& w0,
+                                           unsigned long long& w1) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(p)
+               : "memory");
+}
 __device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* p) {
   unsigned long long w;
   asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");

@@ -59,6 +59,8 @@ struct DecodeSmem {
   float hm[kG];       // CTA max per head (log2 units)
   float hl[kG];       // CTA sum per head (cluster reduction input)
   SliceSmem<kGridMaxParts> slice;  // grid merge
+  float gm[kSliceThreads / 32];    // grid merge: each merging warp's maximum (log2 units)
+  float gl[kSliceThreads / 32];    // and its sum of l
   uint64_t full[NW][NS];
   int err;
   int gok;                  // grid merge: every word of the slice arrived in time
@@ -81,7 +83,11 @@ struct DecodeSmem {
 // turns a run of the resident decode into a per-phase table.
 // ---------------------------------------------------------------------------
 #ifdef GQA_PHASE_TRACE
-constexpr int kPhaseEvents = 6;   // wait, q staged, loop, partial stored, poll, merge
+// wait, q staged, loop, partial stored, poll, merge; then warp 0's first two
+// stages: rows landed, scores reduced, p stored, PV done (4 stamps each);
+// then the CTA merge (every warp's partial in shared memory, weights formed)
+// and the slice merge (warp 0's sums formed, every warp's sums in shared memory)
+constexpr int kPhaseEvents = 18;
 constexpr int kPhaseWords = 4 + kPhaseEvents;
 constexpr int kPhaseRecords = 1 << 16;
 static __device__ unsigned long long g_phase_rec[kPhaseRecords * kPhaseWords];
@@ -429,108 +435,102 @@ __device__ __forceinline__ bool exchange_slice(const DecodeParams& p, DecodeSmem
 // merged by that KV head's CTAs, CTA `split` taking slices split, split +
 // n_splits, ...  A merging thread polls (bounded) the words it needs until
 // all carry this launch's epoch -- there is no barrier and no fence: a word
-// whose tag is current holds its value (one 64-bit store).  Half-warp hw
-// takes parts hw, hw + 16, ... of dim d0 + (lane & 15) (coalesced 128-byte
-// rows); warp 0 settles every (m, l) word and forms the maximum, the weights
-// and L; the sums meet by one shuffle and in shared memory.  Once warp 0 has
-// seen every split's (m, l), every CTA of the KV head has read the epoch, so
-// the merging CTA may store it back for the next launch.
+// whose tag is current holds its value (each word is one 64-bit access).
+// Warp w takes parts 16w .. 16w + 15, two lanes per part (8 dims each, with
+// the part's m and l): the warp merges its parts against its own maximum by
+// shuffles alone, and the 8 warps' (M, L, O[16]) meet once in shared memory.
+// Once every warp has seen every split's (m, l), every CTA of the KV head has
+// read the epoch, so the merging CTA may store it back for the next launch.
 template <int NW, int ST, int NS>
 __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<NW, ST, NS>& sm,
                                               int hkv, int split, unsigned ep) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int hw = tid >> 4, j = tid & 15;
-  constexpr int kGroups = kSliceThreads / 16;
+  constexpr int kMergeWarps = kSliceThreads / 32;
+  constexpr int kPartsPerWarp = kGridMaxParts / kMergeWarps;
+  static_assert(kPartsPerWarp == 16, "two lanes per part");
+  static_assert(kSliceDims == 16, "8 dims per lane");
   static_assert(NW * 32 >= kSliceThreads, "the grid merge maps 256 threads");
   // Threads beyond the first 256 only take part in the CTA barriers.
   const bool merger = tid < kSliceThreads;
-  static_assert(kGroups * kSliceChunk == kGridMaxParts, "parts held in registers");
   constexpr int kSlices = kHeadDim / kSliceDims;
   const int S = p.n_splits;
+  const int part = warp * kPartsPerWarp + (lane >> 1);
+  const int half = lane & 1;
+  const bool has = merger && part < S;
   GQA_PHASE(sm.trace_slot, 4);  // partial stored
   for (int s = split; s < kG * kSlices; s += S) {
     const int head = hkv * kG + s / kSlices;
     const int d0 = (s % kSlices) * kSliceDims;
-    const unsigned long long* rows = p.grid_words + (long long)head * S * kGridRowWords;
+    const unsigned long long* row =
+        p.grid_words + ((long long)head * S + (has ? part : 0)) * kGridRowWords;
     if (s != split) __syncthreads();  // the previous slice's shared memory is free
     if (tid == 0) sm.gok = 1;
     const int slot_id = head * kXSlices + s % kSlices;  // the slice's exchange slot
     if (tid == 0 && p.x_inbox != nullptr) sm.xe = ld_relaxed_gpu_u32(p.x_epoch + slot_id) + 1u;
 
-    unsigned long long wo[kSliceChunk];
-#pragma unroll
-    for (int k = 0; k < kSliceChunk; ++k) {
-      const int i = hw + kGroups * k;
-      wo[k] = merger && i < S ? ld_tagged(rows + (long long)i * kGridRowWords + d0 + j) : 0ull;
-    }
-    constexpr int kPer = kGridMaxParts / 32;
-    unsigned long long wm[kPer], wl[kPer];
-    if (warp == 0) {
-#pragma unroll
-      for (int k = 0; k < kPer; ++k) {
-        const int i = lane + 32 * k;
-        wm[k] = i < S ? ld_tagged(rows + (long long)i * kGridRowWords + kHeadDim) : 0ull;
-        wl[k] = i < S ? ld_tagged(rows + (long long)i * kGridRowWords + kHeadDim + 1) : 0ull;
-      }
-    }
+    // w[0..7]: o of dims d0 + 8 half + 0..7; w[8], w[9]: m, l.
+    unsigned long long w[10];
     bool ok = true;
-    const long long t0 = clock64();
-    for (;;) {
-      bool fresh = true;
+    if (has) {
+      const unsigned long long* src[5] = {row + d0 + 8 * half, row + d0 + 8 * half + 2,
+                                          row + d0 + 8 * half + 4, row + d0 + 8 * half + 6,
+                                          row + kHeadDim};
 #pragma unroll
-      for (int k = 0; k < kSliceChunk; ++k) {
-        const int i = hw + kGroups * k;
-        if (merger && i < S && tag_of(wo[k]) != ep) {
-          fresh = false;
-          wo[k] = ld_tagged(rows + (long long)i * kGridRowWords + d0 + j);
-        }
-      }
-      if (warp == 0) {
+      for (int k = 0; k < 5; ++k) ld_tagged2(src[k], w[2 * k], w[2 * k + 1]);
+      const long long t0 = clock64();
+      for (;;) {
+        bool fresh = true;
 #pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-          const int i = lane + 32 * k;
-          if (i < S && tag_of(wm[k]) != ep) {
+        for (int k = 0; k < 5; ++k) {
+          if (tag_of(w[2 * k]) != ep || tag_of(w[2 * k + 1]) != ep) {
             fresh = false;
-            wm[k] = ld_tagged(rows + (long long)i * kGridRowWords + kHeadDim);
-          }
-          if (i < S && tag_of(wl[k]) != ep) {
-            fresh = false;
-            wl[k] = ld_tagged(rows + (long long)i * kGridRowWords + kHeadDim + 1);
+            ld_tagged2(src[k], w[2 * k], w[2 * k + 1]);
           }
         }
+        if (fresh) break;
+        if (clock64() - t0 > kWaitBudget) {
+          ok = false;
+          break;
+        }
       }
-      if (fresh) break;
-      if (clock64() - t0 > kWaitBudget) {
-        ok = false;
-        break;
-      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 10; ++k) w[k] = 0ull;
     }
     if (!ok) sm.gok = 0;  // benign race: every writer stores 0
-    if (s == split) GQA_PHASE(sm.trace_slot, 5);  // the slice's words all arrived
-    if (warp == 0) {
-      float mx = -CUDART_INF_F;
+    if (s == split) GQA_PHASE(sm.trace_slot, 5);  // this thread's words all arrived
+
+    if (merger) {  // whole warps
+      const float l = has ? value_of(w[9]) : 0.f;
+      const float m = l > 0.f ? value_of(w[8]) : -CUDART_INF_F;
+      float M = m;  // the two lanes of a part hold the same m
 #pragma unroll
-      for (int k = 0; k < kPer; ++k)
-        if (lane + 32 * k < S && value_of(wl[k]) > 0.f) mx = fmaxf(mx, value_of(wm[k]));
-      mx = warp_max(mx);
-      float ls = 0.f;
+      for (int off = 16; off > 1; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      const float wt = m == -CUDART_INF_F ? 0.f : exp2f(m - M);
+      float Lw = half == 0 ? wt * l : 0.f;
 #pragma unroll
-      for (int k = 0; k < kPer; ++k) {
-        const int i = lane + 32 * k;
-        if (i < S) {
-          const float l = value_of(wl[k]);
-          const float w = l > 0.f ? exp2f(value_of(wm[k]) - mx) : 0.f;
-          sm.slice.w[i] = w;
-          ls += w * l;
-        }
+      for (int off = 16; off > 0; off >>= 1) Lw += __shfl_xor_sync(0xffffffffu, Lw, off);
+      float o[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) o[k] = wt == 0.f ? 0.f : wt * value_of(w[k]);
+      // Sum over the warp's parts (lane bits 4..1), dims scattered as they go:
+      // lane keeps dim 8 half + 4 b4 + 2 b3 + b2 (b = lane bits).
+      bfly_halve<8, 16>(o, lane);
+      bfly_halve<4, 8>(o, lane);
+      bfly_halve<2, 4>(o, lane);
+      o[0] += __shfl_xor_sync(0xffffffffu, o[0], 2);
+      if ((lane & 2) == 0) {
+        const int dim = 8 * half + 4 * ((lane >> 4) & 1) + 2 * ((lane >> 3) & 1) + ((lane >> 2) & 1);
+        sm.slice.red[warp][dim] = o[0];
       }
-      ls = warp_sum(ls);
       if (lane == 0) {
-        sm.slice.L = ls;
-        sm.xM = mx;
+        sm.gm[warp] = M;
+        sm.gl[warp] = Lw;
       }
     }
+    if (s == split) GQA_PHASE(sm.trace_slot, 17);  // this warp's sums formed
     __syncthreads();
+    if (s == split) GQA_PHASE(sm.trace_slot, 18);  // every warp's sums in shared memory
     if (!sm.gok) {
       if (tid == 0) atomicOr(p.status, kStatusWaitTimeout);
       return;
@@ -539,29 +539,28 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
     // read the epoch, which may now advance (every merging CTA stores the
     // same value).
     if (tid == 0) st_relaxed_gpu(p.grid_epoch + hkv, ep);
-    if (merger) {
-      float acc = 0.f;
+    if (tid < kSliceDims) {
+      float Mg = -CUDART_INF_F;
 #pragma unroll
-      for (int k = 0; k < kSliceChunk; ++k) {
-        const int i = hw + kGroups * k;
-        if (i < S) {
-          const float w = sm.slice.w[i];
-          if (w != 0.f) acc += w * value_of(wo[k]);
+      for (int k = 0; k < kMergeWarps; ++k) Mg = fmaxf(Mg, sm.gm[k]);
+      float L = 0.f, O = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMergeWarps; ++k) {
+        const float mk = sm.gm[k];
+        if (mk != -CUDART_INF_F) {
+          const float f = exp2f(mk - Mg);
+          L += f * sm.gl[k];
+          O += f * sm.slice.red[k][tid];
         }
       }
-      acc += __shfl_xor_sync(0xffffffffu, acc, 16);
-      if (lane < 16) sm.slice.red[warp][j] = acc;
-    }
-    __syncthreads();
-    if (tid < kSliceDims) {
-      float sum = 0.f;
-#pragma unroll
-      for (int w = 0; w < kSliceThreads / 32; ++w) sum += sm.slice.red[w][tid];
-      const float L = sm.slice.L;
       if (p.x_inbox == nullptr) {
-        p.out[(long long)head * kHeadDim + d0 + tid] = L > 0.f ? sum / L : 0.f;
+        p.out[(long long)head * kHeadDim + d0 + tid] = L > 0.f ? O / L : 0.f;
       } else {
-        sm.xo[tid] = sum;
+        sm.xo[tid] = O;
+        if (tid == 0) {
+          sm.slice.L = L;
+          sm.xM = Mg;
+        }
       }
       if (s == split) GQA_PHASE(sm.trace_slot, 6);  // merged slice stored
     }
@@ -812,6 +811,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     const uint32_t par = (uint32_t)(it / NS) & 1u;
     bool ok = mbar_wait_bounded(&sm.full[warp][s], par, kWaitBudget);
     ok = __all_sync(0xffffffffu, ok);
+    if (it < 2) GQA_PHASE(sm.trace_slot, 7 + 4 * it);  // rows landed
     if (!ok) {
       failed = true;
       break;
@@ -854,6 +854,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     };
     if (nt == ST) scores(std::true_type{}); else scores(std::false_type{});
     B::run_permuted(part);
+    if (it < 2) GQA_PHASE(sm.trace_slot, 8 + 4 * it);  // scores reduced
 
     float sc[3];
     const bool valid = tt < nt;
@@ -905,6 +906,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
       }
     }
     __syncwarp();
+    if (it < 2) GQA_PHASE(sm.trace_slot, 9 + 4 * it);  // p stored
 
     // ---- o += p . V ----
     auto pv_acc = [&](auto full) {
@@ -928,6 +930,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
       }
     };
     if (nt == ST) pv_acc(std::true_type{}); else pv_acc(std::false_type{});
+    if (it < 2) GQA_PHASE(sm.trace_slot, 10 + 4 * it);  // PV accumulated (issued)
     __syncwarp();
     if (it + NS < n_it && lane == 0) {
       fence_proxy_async_smem();
@@ -965,6 +968,7 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     reinterpret_cast<float4*>(ow + h * kHeadDim)[lane] =
         make_float4(oa[h].x, oa[h].y, ob[h].x, ob[h].y);
   __syncthreads();
+  GQA_PHASE(sm.trace_slot, 15);  // every warp's partial in shared memory
   if (!CLUSTER && !GRID && sm.err) return;
 
   // ---- merge the warps: weights once per (warp, head), then one pass ----

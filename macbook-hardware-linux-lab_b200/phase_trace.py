@@ -22,7 +22,11 @@ from collections import defaultdict
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 PHASES = ["dependency released", "q staged", "warp 0 loop done", "partial stored",
-          "slice words arrived", "merged slice stored"]
+          "slice words arrived", "merged slice stored"] + [
+          f"warp 0 stage {i}: {what}" for i in range(2)
+          for what in ("rows landed", "scores reduced", "p stored", "PV issued")] + [
+          "CTA merge: every warp's partial in shared memory", "CTA merge: weights formed",
+          "slice merge: the warp's sums formed", "slice merge: every warp's sums in shared memory"]
 WORDS = 4 + len(PHASES)
 
 
@@ -99,7 +103,13 @@ def analyse(rec, steps, clock_ghz, layers=28):
         rows.append([np.nanmedian(t[ix, j]) - release[li] for j in range(len(PHASES))])
     rows = np.array(rows) / 1000.0
     period = np.median(np.diff(release[max(first, 1):max(last, 2)])) / 1000.0
-    return np.nanmedian(rows, axis=0), period, len(rows)
+    # Each CTA's own phases after its own release, from clock64 differences
+    # alone (exact; the globaltimer that places CTAs on a common axis ticks
+    # in coarse steps, so the table above moves in those steps).
+    steady = np.concatenate([launches[li] for li in range(max(first, 1), max(last, 2))])
+    own = (ev[steady] - ev[steady, :1]) / clock_ghz / 1000.0
+    own[rec[steady, 4:] == 0] = np.nan
+    return np.nanmedian(rows, axis=0), period, len(rows), np.nanmedian(own, axis=0)
 
 
 def main():
@@ -108,6 +118,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--clock-mhz", type=float, default=0.0,
                     help="SM clock for clock64 stamps (default: the device's maximum)")
+    ap.add_argument("--save", default="", help="also write the raw records (.npy) here")
     args = ap.parse_args()
     sys.path.insert(0, HERE)
     import build  # noqa: E402  (this directory's build.py)
@@ -115,14 +126,17 @@ def main():
     g = _load(trace_lib)
     import torch
     rec = collect(g, args.steps, args.warmup)
+    if args.save:
+        import numpy as np
+        np.save(args.save, rec)
     mhz = args.clock_mhz or max_sm_mhz()
-    med, period, n = analyse(rec, args.steps, mhz / 1000.0)
+    med, period, n, own = analyse(rec, args.steps, mhz / 1000.0)
     print(f"resident28 phase trace: {len(rec)} CTA records, {n} steady-state launches, "
           f"SM clock {mhz:.0f} MHz for clock64 stamps, {torch.cuda.get_device_name(0)}")
-    print("| phase (median CTA, median launch) | us after the dependency release |")
-    print("|---|---|")
-    for name, v in zip(PHASES, med):
-        print(f"| {name} | {v:.2f} |")
+    print("| phase | us after the launch's median release (median CTA) | us after the CTA's own release (median, exact) |")
+    print("|---|---|---|")
+    for name, v, o in zip(PHASES, med, own):
+        print(f"| {name} | {v:.2f} | {o:.3f} |")
     print(f"| layer period (release to next release) | {period:.2f} |")
 
 
