@@ -83,11 +83,7 @@ struct DecodeSmem {
 // turns a run of the resident decode into a per-phase table.
 // ---------------------------------------------------------------------------
 #ifdef GQA_PHASE_TRACE
-// wait, q staged, loop, partial stored, poll, merge; then warp 0's first two
-// stages: rows landed, scores reduced, p stored, PV done (4 stamps each);
-// then the CTA merge (every warp's partial in shared memory, weights formed)
-// and the slice merge (warp 0's sums formed, every warp's sums in shared memory)
-constexpr int kPhaseEvents = 18;
+constexpr int kPhaseEvents = 6;   // wait, q staged, loop, partial stored, poll, merge
 constexpr int kPhaseWords = 4 + kPhaseEvents;
 constexpr int kPhaseRecords = 1 << 16;
 static __device__ unsigned long long g_phase_rec[kPhaseRecords * kPhaseWords];
@@ -498,7 +494,6 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
       for (int k = 0; k < 10; ++k) w[k] = 0ull;
     }
     if (!ok) sm.gok = 0;  // benign race: every writer stores 0
-    if (s == split) GQA_PHASE(sm.trace_slot, 5);  // this thread's words all arrived
 
     if (merger) {  // whole warps
       const float l = has ? value_of(w[9]) : 0.f;
@@ -528,9 +523,8 @@ __device__ __forceinline__ void grid_epilogue(const DecodeParams& p, DecodeSmem<
         sm.gl[warp] = Lw;
       }
     }
-    if (s == split) GQA_PHASE(sm.trace_slot, 17);  // this warp's sums formed
     __syncthreads();
-    if (s == split) GQA_PHASE(sm.trace_slot, 18);  // every warp's sums in shared memory
+    if (s == split) GQA_PHASE(sm.trace_slot, 5);  // every warp's slice sums in shared memory
     if (!sm.gok) {
       if (tid == 0) atomicOr(p.status, kStatusWaitTimeout);
       return;
@@ -811,7 +805,6 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     const uint32_t par = (uint32_t)(it / NS) & 1u;
     bool ok = mbar_wait_bounded(&sm.full[warp][s], par, kWaitBudget);
     ok = __all_sync(0xffffffffu, ok);
-    if (it < 2) GQA_PHASE(sm.trace_slot, 7 + 4 * it);  // rows landed
     if (!ok) {
       failed = true;
       break;
@@ -854,7 +847,6 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     };
     if (nt == ST) scores(std::true_type{}); else scores(std::false_type{});
     B::run_permuted(part);
-    if (it < 2) GQA_PHASE(sm.trace_slot, 8 + 4 * it);  // scores reduced
 
     float sc[3];
     const bool valid = tt < nt;
@@ -906,7 +898,6 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
       }
     }
     __syncwarp();
-    if (it < 2) GQA_PHASE(sm.trace_slot, 9 + 4 * it);  // p stored
 
     // ---- o += p . V ----
     auto pv_acc = [&](auto full) {
@@ -930,7 +921,6 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
       }
     };
     if (nt == ST) pv_acc(std::true_type{}); else pv_acc(std::false_type{});
-    if (it < 2) GQA_PHASE(sm.trace_slot, 10 + 4 * it);  // PV accumulated (issued)
     __syncwarp();
     if (it + NS < n_it && lane == 0) {
       fence_proxy_async_smem();
@@ -968,7 +958,6 @@ __global__ void __launch_bounds__(NW * 32, MinBlocks<NW, ST, NS>::value)
     reinterpret_cast<float4*>(ow + h * kHeadDim)[lane] =
         make_float4(oa[h].x, oa[h].y, ob[h].x, ob[h].y);
   __syncthreads();
-  GQA_PHASE(sm.trace_slot, 15);  // every warp's partial in shared memory
   if (!CLUSTER && !GRID && sm.err) return;
 
   // ---- merge the warps: weights once per (warp, head), then one pass ----

@@ -22,11 +22,7 @@ from collections import defaultdict
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 PHASES = ["dependency released", "q staged", "warp 0 loop done", "partial stored",
-          "slice words arrived", "merged slice stored"] + [
-          f"warp 0 stage {i}: {what}" for i in range(2)
-          for what in ("rows landed", "scores reduced", "p stored", "PV issued")] + [
-          "CTA merge: every warp's partial in shared memory", "CTA merge: weights formed",
-          "slice merge: the warp's sums formed", "slice merge: every warp's sums in shared memory"]
+          "every merging warp's slice sums in shared memory", "merged slice stored"]
 WORDS = 4 + len(PHASES)
 
 
