@@ -25,7 +25,8 @@
  * be compiled for it: the token embedding, the output RMSNorm and the greedy
  * pick (restated from qwen_server.c / test_full_model_logits.c), and the
  * Qwen2.5-0.5B head oracle_gemv_q8_0() (kernel_q8_0.cl:10-61, which the
- * reference has only as OpenCL: parity for it is unpinned).
+ * reference has only as OpenCL; pinned bit for bit to that kernel's source
+ * compiled as C and run by a work-group scheduler, oracle/ref_q8_harness.c).
  */
 #include <immintrin.h>
 #include <math.h>
@@ -357,7 +358,10 @@ void oracle_output_norm(const float *x, const float *gamma, int n, float eps, fl
  * the kernel's 32-lane group accumulates d_b * q_bl * x[32b + l] over the row's
  * k / 32 blocks in block order (:30-37); the 32 lane sums then meet by the
  * kernel's tree, halves 16, 8, 4, 2, 1 (:40-53).  w: n_rows rows of k / 32
- * block_q8_0 (fp16 d, 32 int8 codes; 34 bytes each). */
+ * block_q8_0 (fp16 d, 32 int8 codes; 34 bytes each).  Pinned bit for bit to
+ * the kernel's own source run on the CPU (oracle/ref_q8_harness.c). */
+__attribute__((optimize("fp-contract=off")))  /* each product rounded, then added, as the
+                                                kernel's source reads (no fused multiply-add) */
 void oracle_gemv_q8_0(const uint8_t *w, const float *x, int n_rows, int k, float *y) {
     const int nb = k / 32;
     for (int r = 0; r < n_rows; r++) {

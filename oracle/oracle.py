@@ -34,6 +34,7 @@ REF_LAYER_SO = os.path.join(HERE, "_ref", "libgqa_ref_layer.so")
 REF_HEAD_SO = os.path.join(HERE, "_ref", "libgqa_ref_head.so")
 REF_MODEL_SO = os.path.join(HERE, "_ref", "libgqa_ref_model.so")
 REF_SERVER_SO = os.path.join(HERE, "_ref", "libgqa_ref_server.so")
+REF_Q8_SO = os.path.join(HERE, "_ref", "libgqa_ref_q8.so")
 REF_T_MAX = 4096
 
 _f = ctypes.c_float
@@ -398,6 +399,29 @@ def gemv_q8_0(w: np.ndarray, x: np.ndarray, n_rows: int, k: int = 896) -> np.nda
     x = np.ascontiguousarray(x, dtype=np.float32)
     y = np.zeros(n_rows, dtype=np.float32)
     fn(w.ctypes.data, _fptr(x), n_rows, k, _fptr(y))
+    return y
+
+
+def have_reference_q8() -> bool:
+    return os.path.exists(REF_Q8_SO)
+
+
+def ref_gemv_q8_0(w: np.ndarray, x: np.ndarray, n_rows: int, k: int = 896) -> np.ndarray:
+    """The reference's own gemv_q8_0 (kernel_q8_0.cl:10-61): its OpenCL C
+    compiled as C, every 128-work-item group run by a coroutine scheduler
+    (oracle/ref_q8_harness.c).  Slow (one context switch per work-item per
+    barrier): for a few thousand rows at most."""
+    w = np.ascontiguousarray(w, dtype=np.uint8)
+    assert w.size >= n_rows * (k // 32) * 34 and k == 896
+    lib = _load(REF_Q8_SO)
+    fn = lib.ref_gemv_q8_0
+    if fn.argtypes is None:
+        fn.argtypes = [ctypes.c_void_p, _fp, _fp, _i, _i]
+        fn.restype = _i
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(n_rows, dtype=np.float32)
+    if fn(w.ctypes.data, _fptr(x), _fptr(y), n_rows, k) != 0:
+        raise RuntimeError("ref_gemv_q8_0: coroutine set-up failed")
     return y
 
 

@@ -1,7 +1,8 @@
 """The CPU side of the Qwen2.5-0.5B token step (no GPU): the layer oracle
 composed from the reference's compiled size-generic GEMVs is pinned to the
 compiled cpu_decoder_layer_step at the 1.5B sizes; the Q8_0 head restatement
-(kernel_q8_0.cl:10-61) against a float64 product; the byte layout that
+(kernel_q8_0.cl:10-61) pinned bit for bit to the reference's own kernel source
+run on the CPU, and against a float64 product; the byte layout that
 gqa_lm_head_q8_0_pack writes; and a 0.5B-shaped GGUF file through the reader."""
 import numpy as np
 import pytest
@@ -46,6 +47,31 @@ def test_reference_gemvs_at_05b_sizes(pkg, orc):
     got = orc.ref_gemv_q4_0(wd, h, None, 896, 4864)
     want = S.q4_0_dequant(wd, 896, 4864).astype(np.float64) @ h
     assert np.abs(got - want).max() <= 1e-5 * np.sqrt(np.mean(want ** 2))
+
+
+@pytest.mark.parametrize("seed", [3, 11])
+def test_q8_0_restatement_equals_reference_kernel(pkg, orc, seed):
+    """The restated Q8_0 GEMV == the reference's gemv_q8_0 (kernel_q8_0.cl,
+    its OpenCL C compiled as C, each work-group's 128 work-items run to every
+    barrier in turn), bit for bit: seeded weights and inputs, a row count that
+    leaves a partial last work-group, extreme fp16 scales (subnormal, large,
+    negative zero) and all-zero / saturated code blocks."""
+    if not orc.have_reference_q8():
+        pytest.skip("oracle/_ref not built")
+    S = pkg.seeded
+    n = 203  # 50 full groups of 4 rows and one of 3
+    w = S.q8_0_matrix(seed, S.W_HEAD, n, 896).reshape(n, 28, 34).copy()
+    x = S.normal(seed, S.HEAD_X, 896)
+    w[1, 3, 0:2] = np.frombuffer(np.float16(6.0e-8).tobytes(), np.uint8)   # subnormal d
+    w[2, 5, 0:2] = np.frombuffer(np.float16(-0.0).tobytes(), np.uint8)     # -0 d
+    w[3, 7, 0:2] = np.frombuffer(np.float16(3.0e4).tobytes(), np.uint8)    # large d
+    w[4, 9, 2:] = 0                                                         # zero codes
+    w[5, 11, 2:] = 0x80                                                     # -128 codes
+    w[6, 13, 2:] = 0x7F                                                     # 127 codes
+    w = w.reshape(-1)
+    got = orc.gemv_q8_0(w, x, n)
+    want = orc.ref_gemv_q8_0(w, x, n)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
 
 
 def test_q8_0_head_restatement(pkg, orc):
