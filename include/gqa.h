@@ -174,6 +174,18 @@ GQA_API int gqa_decode_batched(gqa_ctx *ctx, gqa_stream_t stream, int n_seq, flo
                        float *const *v_caches, const float *qkv, long long qkv_stride,
                        const int *seq_lens, int max_len, float *out, long long out_stride);
 
+/* One batched decode step with HOST buffers (the reference's write ->
+ * kernels -> read loop, attention_gqa_benchmark.c:531-545, for a batch):
+ * copies h_qkv (n_seq rows of qkv_stride floats) into the device buffer d_qkv,
+ * runs gqa_decode_batched on it with the other arguments as there, and copies
+ * each sequence's n_heads_q*128 output floats (out_stride apart in d_out) into
+ * h_out, packed row after row.  d_out may equal d_qkv.  Asynchronous on
+ * `stream`; pass page-locked host memory for the copies to run at full rate. */
+GQA_API int gqa_decode_batched_host(gqa_ctx *ctx, gqa_stream_t stream, int n_seq,
+                            float *const *k_caches, float *const *v_caches, const float *h_qkv,
+                            float *d_qkv, long long qkv_stride, const int *seq_lens, int max_len,
+                            float *d_out, long long out_stride, float *h_out);
+
 /* Split-KV partial over cache rows [t_begin, t_end) for already-rotated q:
  * per q head h, a reference value m[h] (natural-log units; scores are
  * q.k / sqrt(128)), l[h] = sum exp(s - m) and o[h][:] = sum exp(s - m) v (not

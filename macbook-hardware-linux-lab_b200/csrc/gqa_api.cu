@@ -1002,6 +1002,33 @@ int gqa_decode_batched(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const*
   return GQA_OK;
 }
 
+int gqa_decode_batched_host(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const* k_caches,
+                            float* const* v_caches, const float* h_qkv, float* d_qkv,
+                            long long qkv_stride, const int* seq_lens, int max_len, float* d_out,
+                            long long out_stride, float* h_out) {
+  GQA_RANGE("gqa_decode_batched_host");
+  if (!c) return fail(GQA_ERR_INVALID_ARG, "null context");
+  if (!h_qkv || !h_out || !d_qkv || !d_out)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_decode_batched_host: null buffer");
+  if (n_seq < 1 || n_seq > 65535 || qkv_stride < 1)
+    return fail(GQA_ERR_INVALID_ARG, "gqa_decode_batched_host: n_seq or qkv_stride out of range");
+  DeviceGuard g(c->device);
+  cudaStream_t st = (cudaStream_t)stream;
+  GQA_CUDA(cudaMemcpyAsync(d_qkv, h_qkv, sizeof(float) * (size_t)qkv_stride * n_seq,
+                           cudaMemcpyHostToDevice, st));
+  const int rc = gqa_decode_batched(c, stream, n_seq, k_caches, v_caches, d_qkv, qkv_stride,
+                                    seq_lens, max_len, d_out, out_stride);
+  if (rc != GQA_OK) return rc;
+  const size_t row = sizeof(float) * (size_t)c->cfg.n_heads_q * kHeadDim;
+  const size_t pitch = sizeof(float) * (size_t)out_stride;
+  if (pitch == row)  // packed rows: one plain copy
+    GQA_CUDA(cudaMemcpyAsync(h_out, d_out, row * (size_t)n_seq, cudaMemcpyDeviceToHost, st));
+  else
+    GQA_CUDA(cudaMemcpy2DAsync(h_out, row, d_out, pitch, row, (size_t)n_seq,
+                               cudaMemcpyDeviceToHost, st));
+  return GQA_OK;
+}
+
 int gqa_decode_split_partial(gqa_ctx* c, gqa_stream_t stream, const gqa_layer_kv* kv,
                              const float* q_rot, int t_begin, int t_end, float* m, float* l,
                              float* o) {

@@ -122,6 +122,7 @@ _SIGNATURES = {
     "gqa_rope_kv_append": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _vp, _vp, _i],
     "gqa_decode": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _vp],
     "gqa_decode_batched": [_vp, _vp, _i, _vp, _vp, _vp, _ll, _vp, _i, _vp, _ll],
+    "gqa_decode_batched_host": [_vp, _vp, _i, _vp, _vp, _vp, _vp, _ll, _vp, _i, _vp, _ll, _vp],
     "gqa_decode_split_partial": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _vp, _vp, _vp],
     "gqa_lse_combine": [_vp, _vp, _i, _i, _vp, _vp, _vp, _vp],
     "gqa_decode_kv_shard": [_vp, _vp, ctypes.POINTER(LayerKV), _vp, _i, _i, _i, _vp, _vp, _vp],
@@ -585,6 +586,17 @@ class Context:
         _check(lib().gqa_decode_batched(self._h, _stream(stream), n_seq, _ptr(k_ptrs),
                                         _ptr(v_ptrs), _ptr(qkv), qkv_stride, _ptr(seq_lens),
                                         max_len, _ptr(out), out_stride))
+
+    def decode_batched_host(self, n_seq: int, k_ptrs, v_ptrs, h_qkv, d_qkv, qkv_stride: int,
+                            seq_lens, max_len: int, d_out, out_stride: int, h_out,
+                            stream=None) -> None:
+        """gqa_decode_batched with host input and output: h_qkv / h_out are
+        host buffers (page-locked tensors or arrays), d_qkv / d_out the device
+        buffers the step runs on; h_out receives n_seq packed output rows."""
+        _check(lib().gqa_decode_batched_host(self._h, _stream(stream), n_seq, _ptr(k_ptrs),
+                                             _ptr(v_ptrs), _ptr(h_qkv), _ptr(d_qkv), qkv_stride,
+                                             _ptr(seq_lens), max_len, _ptr(d_out), out_stride,
+                                             _ptr(h_out)))
 
     def decode_split_partial(self, kv: LayerKV, q_rot, t_begin: int, t_end: int, m, l, o,
                              stream=None) -> None:

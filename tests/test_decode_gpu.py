@@ -205,6 +205,48 @@ def test_batched_matches_oracle(pkg, orc, cuda, lens, t_max):
             assert np.array_equal(d_v[s, :, p].cpu().numpy(), ref_v[s][:, p])
 
 
+def test_batched_host_buffers_match_oracle(pkg, orc, cuda):
+    """gqa_decode_batched_host: page-locked host qkv in, the batched step on a
+    device buffer, packed host outputs back -- the same outputs as the oracle
+    (and the appended rows in the device caches), on a non-blocking stream,
+    two steps in a row, output written in place over the device qkv."""
+    torch = cuda
+    lens, t_max = [1, 40, 300, 1500, 2048], 2048
+    n = len(lens)
+    qkv, kc, vc = _batched_case(pkg, torch, lens, t_max, 1700)
+    ref_q = [qkv[s].copy() for s in range(n)]
+    ref_k = [kc[s].copy() for s in range(n)]
+    ref_v = [vc[s].copy() for s in range(n)]
+    ref = orc.decode_batched(ref_q, ref_k, ref_v, lens)
+    st = torch.cuda.Stream()
+    with pkg.Context(t_max=t_max) as ctx:
+        d_k, d_v = to_dev(torch, kc), to_dev(torch, vc)
+        d_qkv = torch.empty((n, 2048), device="cuda")
+        stride = 2 * t_max * 128 * 4
+        kp = torch.tensor([d_k.data_ptr() + s * stride for s in range(n)], dtype=torch.int64,
+                          device="cuda")
+        vp = torch.tensor([d_v.data_ptr() + s * stride for s in range(n)], dtype=torch.int64,
+                          device="cuda")
+        dl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+        h_qkv = torch.from_numpy(qkv.astype(np.float32)).pin_memory()
+        h_out = torch.full((n, 1536), float("nan")).pin_memory()
+        torch.cuda.synchronize()
+        for _ in range(2):  # the second step appends the same row at the same position
+            ctx.decode_batched_host(n, kp, vp, h_qkv, d_qkv, 2048, dl, max(lens), d_qkv, 2048,
+                                    h_out, st)
+        st.synchronize()
+        assert ctx.device_status() == 0
+        got = h_out.numpy()
+        for s in range(n):
+            assert nerr(got[s], ref[s]) <= TOL, f"sequence {s} (len {lens[s]})"
+            p = lens[s] - 1
+            assert np.abs(d_k[s, :, p].cpu().numpy() - ref_k[s][:, p]).max() <= 1e-5
+            assert np.array_equal(d_v[s, :, p].cpu().numpy(), ref_v[s][:, p])
+        with pytest.raises(pkg.gqa.GqaError):
+            ctx.decode_batched_host(n, kp, vp, None, d_qkv, 2048, dl, max(lens), d_qkv, 2048,
+                                    h_out, st)
+
+
 def test_batched_full_size_workload_sampled(pkg, orc, cuda):
     """The batched workload at full size (64 sequences, lengths uniform in
     [256, 8192], fp32 caches filled on the device); 6 sequences are checked
