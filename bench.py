@@ -957,6 +957,11 @@ def run_batched(args, g, ctx, rank, world, local):
     dl = lens_base.clone()
     max_len = max(lens0) + window - 1
     ctx.reserve(n, max_len)
+    # Consecutive steps overlap their launches (programmatic dependent launch:
+    # the preceding kernel is the previous step's combine, which writes no
+    # cache row), and each step's combine advances the device lengths by one.
+    ctx.set_option(g.gqa.GQA_OPT_PDL, 1)
+    ctx.set_option(g.gqa.GQA_OPT_BATCH_ADVANCE, 1)
     stream = torch.cuda.current_stream()
 
     def step(i, st=None):
@@ -964,7 +969,6 @@ def run_batched(args, g, ctx, rank, world, local):
             dl.copy_(lens_base)
         ctx.decode_batched(n, kp, vp, qkv, QKV_W, dl, max_len, out, OUT_W,
                            st if st is not None else stream)
-        dl.add_(1)
 
     for i in range(args.warmup):
         step(i)
@@ -1000,7 +1004,6 @@ def run_batched(args, g, ctx, rank, world, local):
             # host qkv in, the step, host outputs back: one C-ABI call
             ctx.decode_batched_host(n, kp, vp, h_qkv, qkv, QKV_W, dl, max_len, out, OUT_W, h_out,
                                     stream)
-            dl.add_(1)
 
     t_e2e = statistics.median(timed_rounds(body_e2e, world, stream))
     status = ctx.device_status()

@@ -83,8 +83,12 @@ GQA_API const char *gqa_last_error_string(void);
  * immediately before.  Default 0 for single calls; the multi-layer step and
  * graph APIs always use it between their own launches.
  * GQA_OPT_TARGET_CTAS: CTAs one single-sequence decode aims for (default:
- * the device's SM count). */
-enum { GQA_OPT_PDL = 1, GQA_OPT_TARGET_CTAS = 2 };
+ * the device's SM count).
+ * GQA_OPT_BATCH_ADVANCE: 1 makes gqa_decode_batched(_host) add one to every
+ * seq_lens[s] on the device after the step has used them (the serving
+ * loop's own advance to the next token, done by the step's last kernel
+ * instead of a separate launch); seq_lens is then written.  Default 0. */
+enum { GQA_OPT_PDL = 1, GQA_OPT_TARGET_CTAS = 2, GQA_OPT_BATCH_ADVANCE = 8 };
 GQA_API int gqa_set_option(gqa_ctx *ctx, int option, long long value);
 
 /* Pre-sizes the split-KV scratch for up to n_seq sequences of up to max_len

@@ -37,6 +37,7 @@ cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k
                                const float* inv_freq, int* status, int n_seq, cudaStream_t st,
                                bool pdl);
 cudaError_t launch_advance_pos(int* pos, int wrap_lo, int wrap_hi, cudaStream_t st, bool pdl);
+cudaError_t launch_advance_lens(int* lens, int n, cudaStream_t st, bool pdl);
 cudaError_t launch_fill_normal(float* dst, long long n, uint64_t key, long long offset,
                                int n_sm, cudaStream_t st);
 cudaError_t prepare_prefill_kernels();
@@ -119,6 +120,7 @@ struct gqa_ctx {
   int pdl = 0;
   int target_ctas = 0;
   int batch_chunk = 0;  // tokens per split in batched decode (0 = automatic)
+  int batch_advance = 0;  // GQA_OPT_BATCH_ADVANCE: batched steps advance seq_lens
   int live_graphs = 0;  // graphs hold scratch pointers: no reallocation while > 0
   // Decode kernel shapes (csrc/gqa_decode.cu variant table).  Measured on
   // B200: one sequence (few long CTAs, latency-bound) runs best with 8 warps
@@ -306,9 +308,24 @@ int plan_splits_grid(const gqa_ctx* c, int rows_kv, int len) {
   return want >= 6 ? want : 0;
 }
 
-int batch_chunk(const gqa_ctx* c, int max_len) {
+// Rows per split of a batched decode.  Up to 8192 rows: 512-row splits while
+// the batch still yields 1.5 waves of CTAs with them (a sequence's rows
+// averaging half the longest's), else 256 (a small batch needs the CTAs).
+// Measured, 64 sequences of U[256, 8192] rows dealt to 1/2/4/8 GPUs (one
+// GPU's share): 512 rows 101.7 / 55.7 / 30.2 / 27.9 us per step, 256 rows
+// 109.2 / 61.8 / 33.8 / 20.1 us.
+int batch_chunk(const gqa_ctx* c, int n_seq, int max_len) {
   const int q = decode_variant_quant(batch_variant(c));
-  int want = c->batch_chunk > 0 ? c->batch_chunk : (max_len > 8192 ? 1024 : 256);
+  int want = c->batch_chunk;
+  if (want <= 0) {
+    if (max_len > 8192) {
+      want = 1024;
+    } else {
+      const long long ctas512 =
+          (long long)n_seq * c->cfg.n_heads_kv * ceil_div(max_len, 2 * 512);
+      want = 2 * ctas512 >= 3LL * c->n_sm ? 512 : 256;
+    }
+  }
   const int least = ceil_div(max_len, kMergeMaxParts);  // at most kMergeMaxParts splits
   if (want < least) want = least;
   return ((want + q - 1) / q) * q;
@@ -726,6 +743,9 @@ int gqa_set_option(gqa_ctx* c, int option, long long value) {
     case 6: /* GQA_OPT_CLUSTER (internal tuning knob) */
       c->cluster = value ? 1 : 0;
       return GQA_OK;
+    case GQA_OPT_BATCH_ADVANCE:
+      c->batch_advance = value ? 1 : 0;
+      return GQA_OK;
     case 7: /* GQA_OPT_GRID_MERGE (internal tuning knob) */
       c->grid_merge = value ? 1 : 0;
       return GQA_OK;
@@ -751,7 +771,7 @@ int gqa_reserve(gqa_ctx* c, int n_seq, int max_len) {
                 kCluster) * kCluster;
   const int grid = plan_splits_grid(c, c->cfg.n_heads_kv, max_len);
   if (grid > single) single = grid;
-  const int batched = ceil_div(max_len, batch_chunk(c, max_len));
+  const int batched = ceil_div(max_len, batch_chunk(c, 1, max_len));  // the most splits
   const int splits = single > batched ? single : batched;
   return ensure_scratch(c, (long long)n_seq * c->cfg.n_heads_q * splits, nullptr);
 }
@@ -972,7 +992,7 @@ int gqa_decode_batched(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const*
     return fail(GQA_ERR_INVALID_ARG, "out overlaps qkv without being equal to it");
   DeviceGuard g(c->device);
   cudaStream_t st = (cudaStream_t)stream;
-  const int chunk = batch_chunk(c, max_len);
+  const int chunk = batch_chunk(c, n_seq, max_len);
   const int n_splits = ceil_div(max_len, chunk);
   if (n_splits > 65535) return fail(GQA_ERR_INVALID_ARG, "too many splits");
   if (n_splits > 1) {
@@ -993,11 +1013,17 @@ int gqa_decode_batched(gqa_ctx* c, gqa_stream_t stream, int n_seq, float* const*
   p.out = out;
   p.out_stride = out_stride;
   GQA_CUDA(launch_decode_split(p, n_seq, true, st, c->pdl != 0, batch_variant(c)));
+  // With GQA_OPT_BATCH_ADVANCE the step's last kernel advances the lengths
+  // (the caller's next step), after every read of them.
+  int* advance = c->batch_advance ? const_cast<int*>(seq_lens) : nullptr;
   if (n_splits > 1) {
     CombineParams cp = combine_from_scratch(c, n_splits);
     cp.out = out;
     cp.out_stride = out_stride;
+    cp.advance_lens = advance;
     GQA_CUDA(launch_combine(cp, n_seq, st, true));
+  } else if (advance) {
+    GQA_CUDA(launch_advance_lens(advance, n_seq, st, true));
   }
   return GQA_OK;
 }

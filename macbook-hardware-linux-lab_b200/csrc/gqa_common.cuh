@@ -308,6 +308,9 @@ struct CombineParams {
   // written instead of O / L (a partial over the union of the parts).
   float* out_m;
   float* out_l;
+  // When set, the combine advances every sequence's length by one once the
+  // split kernel before it (which read them) has finished: advance_lens[seq]++.
+  int* advance_lens;
 };
 
 }  // namespace gqa

@@ -1045,6 +1045,8 @@ __global__ void __launch_bounds__(kHeadDim * kMergeGroups) combine_kernel(const 
   // this grid before it reads or writes anything this grid touches.
   pdl_wait();
   pdl_launch_dependents();
+  // The split kernel has finished reading the lengths (the wait above).
+  if (c.advance_lens != nullptr && h == 0 && threadIdx.x == 0) c.advance_lens[seq] += 1;
   float M, L, O;
   merge_partials(c, r, sm, M, L, O);
   if (g != 0) return;
@@ -1116,6 +1118,15 @@ __global__ void __launch_bounds__(kHalf) rope_append_kernel(
     vc[row + i] = v[h * kHeadDim + i];
     vc[row + i + kHalf] = v[h * kHeadDim + i + kHalf];
   }
+}
+
+// Advances every sequence's length by one after a batched step whose split
+// kernel wrote the outputs itself (no combine launch to do it).
+__global__ void advance_lens_kernel(int* lens, int n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    lens[i] += 1;
 }
 
 // Advances the device-side position after a replayed decode step, wrapping
@@ -1339,6 +1350,12 @@ cudaError_t launch_rope_append(float* qkv, long long qkv_stride, float* const* k
   void* args[] = {&qkv, &qkv_stride, (void*)&k_ptrs, (void*)&v_ptrs, &k_base, &v_base,
                   &seq_stride, &len, &t_max, &n_q, &n_kv, (void*)&inv_freq, &status};
   return launch_ex((const void*)rope_append_kernel, dim3(n_seq), dim3(kHalf), 0, st, pdl, args);
+}
+
+cudaError_t launch_advance_lens(int* lens, int n, cudaStream_t st, bool pdl) {
+  void* args[] = {&lens, &n};
+  return launch_ex((const void*)advance_lens_kernel, dim3((n + 255) / 256), dim3(256), 0, st, pdl,
+                   args);
 }
 
 cudaError_t launch_advance_pos(int* pos, int wrap_lo, int wrap_hi, cudaStream_t st, bool pdl) {

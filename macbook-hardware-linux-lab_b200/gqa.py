@@ -42,6 +42,7 @@ GQA_OPT_KERNEL_VARIANT = 4
 GQA_OPT_LAYERS_PDL = 5   # tuning knobs (internal): PDL inside the layer loop,
 GQA_OPT_CLUSTER = 6      # the cluster reduction,
 GQA_OPT_GRID_MERGE = 7   # the grid-merged single-sequence decode (default on)
+GQA_OPT_BATCH_ADVANCE = 8  # batched steps advance seq_lens on the device after use
 # rows per split quantum of each decode kernel variant (csrc/gqa_decode.cu)
 VARIANT_QUANT = {0: 32, 1: 32, 2: 32, 3: 64, 4: 32, 5: 64, 6: 32}
 

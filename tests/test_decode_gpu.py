@@ -205,6 +205,49 @@ def test_batched_matches_oracle(pkg, orc, cuda, lens, t_max):
             assert np.array_equal(d_v[s, :, p].cpu().numpy(), ref_v[s][:, p])
 
 
+@pytest.mark.parametrize("lens", [[1, 40, 300, 1500, 2000], [1, 7, 100, 200]])
+def test_batched_advance_matches_oracle(pkg, orc, cuda, lens):
+    """GQA_OPT_BATCH_ADVANCE with PDL on: two steps in a row, the device
+    lengths advanced by the library after each (by the combine, or by its own
+    small kernel when the plan has one split); each step equals the oracle's
+    step at those lengths, with the rows the first step appended in place."""
+    torch = cuda
+    t_max = 2048
+    n = len(lens)
+    qkv1, kc, vc = _batched_case(pkg, torch, lens, t_max, 2100)
+    qkv2 = np.stack([pkg.seeded.normal(2300 + s, pkg.seeded.QKV, 2048) for s in range(n)])
+    ref_k = [kc[s].copy() for s in range(n)]
+    ref_v = [vc[s].copy() for s in range(n)]
+    ref1 = orc.decode_batched([qkv1[s].copy() for s in range(n)], ref_k, ref_v, lens)
+    ref2 = orc.decode_batched([qkv2[s].copy() for s in range(n)], ref_k, ref_v,
+                              [L + 1 for L in lens])
+    with pkg.Context(t_max=t_max) as ctx:
+        ctx.set_option(pkg.gqa.GQA_OPT_PDL, 1)
+        ctx.set_option(pkg.gqa.GQA_OPT_BATCH_ADVANCE, 1)
+        d_k, d_v = to_dev(torch, kc), to_dev(torch, vc)
+        d1, d2 = to_dev(torch, qkv1), to_dev(torch, qkv2)
+        stride = 2 * t_max * 128 * 4
+        kp = torch.tensor([d_k.data_ptr() + s * stride for s in range(n)], dtype=torch.int64,
+                          device="cuda")
+        vp = torch.tensor([d_v.data_ptr() + s * stride for s in range(n)], dtype=torch.int64,
+                          device="cuda")
+        dl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+        out1 = torch.empty((n, 1536), device="cuda")
+        out2 = torch.empty((n, 1536), device="cuda")
+        ctx.decode_batched(n, kp, vp, d1, 2048, dl, max(lens) + 1, out1, 1536)
+        ctx.decode_batched(n, kp, vp, d2, 2048, dl, max(lens) + 1, out2, 1536)
+        torch.cuda.synchronize()
+        assert ctx.device_status() == 0
+        assert dl.cpu().tolist() == [L + 2 for L in lens]
+        for s in range(n):
+            assert nerr(out1[s].cpu().numpy(), ref1[s]) <= TOL, (s, 1)
+            assert nerr(out2[s].cpu().numpy(), ref2[s]) <= TOL, (s, 2)
+        got_k = d_k.cpu().numpy()
+        for s in range(n):
+            for p in (lens[s] - 1, lens[s]):
+                assert np.abs(got_k[s, :, p] - ref_k[s][:, p]).max() <= 1e-5
+
+
 def test_batched_host_buffers_match_oracle(pkg, orc, cuda):
     """gqa_decode_batched_host: page-locked host qkv in, the batched step on a
     device buffer, packed host outputs back -- the same outputs as the oracle
