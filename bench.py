@@ -1190,7 +1190,7 @@ def run_ours(args):
     extra = None
     if args.workload == "resident28" and not args.no_extra:
         extra = {}
-        for name in ("batched", "long1", "prefill"):
+        for name in ("batched", "long1", "prefill", "token28", "head"):
             try:
                 extra[name] = run_extra(args, g, name, rank, world, local)
             except Exception as exc:  # a sharded extra never takes the headline line down
@@ -1263,13 +1263,31 @@ def k_nondefault(args):
 
 
 def run_extra(args, g, name, rank, world, local):
-    """One of the sharded configurations timed in the default run: `batched`
+    """One of the other configurations timed in the default run: `batched`
     (64 sequences dealt to the ranks, strong scaling), `long1` (one 32768-row
-    sequence split by KV range over the ranks, merged over peer memory) or
-    `prefill` (8 prompts of 2048 tokens dealt to the ranks, strong scaling)."""
+    sequence split by KV range over the ranks, merged over peer memory),
+    `prefill` (8 prompts of 2048 tokens dealt to the ranks, strong scaling),
+    `token28` (the whole greedy decode step of the 28-layer model, one model
+    per rank) or `head` (the output RMSNorm + Q6_K LM head + pick, one per
+    rank)."""
     import copy
     sub = copy.copy(args)
     sub.workload = name
+    if name in ("token28", "head"):
+        wl = WORKLOADS[name]
+        ctx = g.Context(t_max=wl["t_max"], device=local)
+        try:
+            r = run_head(sub, g, ctx, rank, world, local)
+        finally:
+            ctx.close()
+        t = max_over_ranks(r["t"], world)
+        total = sum_over_ranks(r["bytes"], world)
+        tokens = sum_over_ranks(r["tokens"], world)
+        return {"workload": workload_config(name)["workload"],
+                "value": round(total / t / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(t / sub.steps * 1e3, 5), "steps": sub.steps,
+                "tok_per_s": round(tokens / t, 1), "scaling": "weak",
+                "rounds": r.get("rounds", 1), "clocks": r["clocks"]}
     if name == "long1":
         sub.steps = WORKLOADS["long1"]["window"]  # the peer-exchange graph holds one window
         t_max = max(n for _, n in g.shard.plan_kv_ranges(WORKLOADS["long1"]["t_max"], world))
