@@ -23,36 +23,32 @@
 // lays the same bytes out once, at load time, as four planes over the rows
 // rounded up to a multiple of 4 (Np):
 //   ql [Np][768]  qh [Np][384]  scales [Np][96]  d [Np][6] (fp16)
-// -- 1260 bytes per row as before.  Half-superblock hh = 2 * superblock + n of
-// a row owns ql bytes [64hh, 64hh + 64), qh bytes [32hh, 32hh + 32) and scale
-// bytes [8hh, 8hh + 8); within its ql bytes the two 32-byte halves (quarters
-// 0/2 and 1/3) are swapped when hh & 2, so that the warp's loads below hit 32
-// different shared-memory banks, and its scale bytes are reordered so that
-// scales[8n + 2c + g] sits at 8hh + 4g + c: a lane's four scales are one
-// 32-bit word; the qh bytes are stored XOR 0xAA (the high bit of each 2-bit
-// field flipped), so that an assembled code byte is code ^ 32.  Any run of rows
-// starting on a multiple of 4 is then four 16-byte-aligned runs of bytes.
+// -- 1260 bytes per row as before, each plane row the six superblocks' bytes
+// of that kind in order, the ql and qh rows of row r rotated right by
+// 16 (r % 8) bytes so that the eight rows a warp reads at one offset hit eight
+// different groups of shared-memory banks.  Any run of rows starting on a
+// multiple of 4 is then four 16-byte-aligned runs of bytes.
 //
 // The head kernel is a bulk-copy pipeline: one CTA per SM over a contiguous,
-// balanced range of rows, a producer warp that copies stages of 32 rows (the
-// four planes' runs, 40320 bytes) into a 4-deep ring of shared-memory stages,
+// balanced range of rows, a producer warp that copies stages of 64 rows (the
+// four planes' runs, 80640 bytes) into a 2-deep ring of shared-memory stages,
 // starting before the programmatic dependency wait (the weights do not depend
-// on the previous kernel), and 16 consumer warps that each take two rows of a
-// stage, computed side by side.  Lane (hh0 = lane / 8, q = lane % 8) owns, in
-// every row, the three 16-weight units hh = hh0 + 4u (u = 0, 1, 2),
-// l = 4q .. 4q + 3, all four quarters; the digit words of the units' 48 inputs
-// (below) stay in registers for the whole kernel.  Per unit the lane reads two
-// ql words, one qh word, its four scale bytes and d; four code words (one byte
-// per weight) come from AND/OR steps.  The products are integer: once per
-// launch the CTA splits each unit's 16 normalised inputs, with a power-of-two
-// scale s >= max|z| / 63, into three signed digits in [-63, 63],
-// z = s (e1 + e2 / 126 + e3 / 126^2); per row, the code bytes become code - 32
-// as signed bytes (y = code ^ 32 from the packed qh, plus 6 (y & 32): two
-// instructions per word), dp4a against the digit words gives exact int32
-// sums, the quarters' int8 scales combine them exactly (|K| < 2^22), and the
-// unit's term is (d s) (K1 + K2 / 126 + K3 / 126^2).  With z = 32 e_i (a power
-// of two) the digits are exact and a logit is d * (scale * (code - 32) * 32)
-// with one rounding, as in the reference's order (d * scale is exact).
+// on the previous kernel), and 12 consumer warps.  The products run on the
+// tensor cores in 8-bit integers (mma.sync m16n8k16, unsigned codes times
+// signed input digits, int32 accumulators): once per launch the CTA splits
+// the normalised inputs, with one power-of-two scale s >= max|z| / 63, into
+// three signed digits in [-63, 63], z = s (e1 + e2 / 126 + e3 / 126^2), and
+// lays them out as the product's B operand (columns 0-2: the three digits;
+// 3-7 zero), with the accumulator input -32 sum e per column and 16-input
+// chunk, so that D = sum (code - 32) e exactly.  Warp w takes 16 rows (tile
+// w / 3) of a stage over two superblocks (2 (w % 3), 2 (w % 3) + 1): per
+// 16-weight scale group one product, its int32 result times the group's int8
+// scale added into the superblock's sums K_n (|K| < 2^27), and per
+// superblock the term (d s)(K1 + K2 / 126 + K3 / 126^2); the three pairs'
+// terms of a row meet in shared memory, in pair order.  With z = 32 e_i (the
+// reference test's unit columns) the digits are exact and a logit is
+// d * (scale * (code - 32) * 32) with one rounding, as in the reference's
+// order (d * scale is exact).
 #include <cuda_fp16.h>
 
 #include "gqa_common.cuh"
@@ -70,40 +66,52 @@ constexpr int kDRow = kQ6Supers * 2;
 constexpr int kHeadConsumerWarps = 16;
 constexpr int kHeadConsumers = 32 * kHeadConsumerWarps;
 constexpr int kHeadThreads = kHeadConsumers + 32;  // + the producer warp
-constexpr int kStageRows = 2 * kHeadConsumerWarps;  // two rows per consumer warp
-constexpr int kHeadStages = 4;
-constexpr int kStQl = kStageRows * kQlRow;
-constexpr int kStQh = kStageRows * kQhRow;
-constexpr int kStSc = kStageRows * kScRow;
-constexpr int kStD = kStageRows * kDRow;
-constexpr int kStageBytes = kStQl + kStQh + kStSc + kStD;  // 40320
 constexpr float kHeadRmsEps = 1e-6f;               // EPSILON of the reference
 constexpr float kNoPick = -1e30f;                  // best_val start of the greedy loop
 constexpr long long kHeadWaitBudget = 2000000000LL;
 constexpr int kEmbedThreads = 256;
 constexpr int kQ4Bytes = 18;
-static_assert(kStageBytes % 16 == 0 && kStQl % 16 == 0 && kStQh % 16 == 0 && kStSc % 16 == 0,
-              "stage runs must stay 16-byte aligned");
 
 struct HeadBest {
   float v;
   int i;
 };
 
-constexpr int kHeadUnits = kHeadK / 16;  // 16-weight units of a row (96)
 
-struct HeadSmem {
-  alignas(128) uint8_t stage[kHeadStages][kStageBytes];
+// The Q6_K head kernel: 12 consumer warps + a producer warp, stages of 64
+// rows (the four planes' runs, 80640 bytes), two deep.
+constexpr int kQ6Warps = 12;
+constexpr int kQ6Consumers = 32 * kQ6Warps;
+constexpr int kQ6Threads = kQ6Consumers + 32;
+constexpr int kQ6StageRows = 64;
+constexpr int kQ6Stages = 2;
+constexpr int kQ6StQl = kQ6StageRows * kQlRow;
+constexpr int kQ6StQh = kQ6StageRows * kQhRow;
+constexpr int kQ6StSc = kQ6StageRows * kScRow;
+constexpr int kQ6StD = kQ6StageRows * kDRow;
+constexpr int kQ6StageBytes = kQ6StQl + kQ6StQh + kQ6StSc + kQ6StD;  // 80640
+constexpr int kQ6Chunks = kHeadK / 16;  // 16-weight scale groups of a row (96)
+static_assert(kQ6StageBytes % 16 == 0 && kQ6StQl % 16 == 0 && kQ6StQh % 16 == 0 &&
+                  kQ6StSc % 16 == 0 && (4 * kDRow) % 16 == 0,
+              "stage runs must stay 16-byte aligned");
+static_assert(kQ6Consumers == 4 * kQ6Chunks && kHeadK % kQ6Consumers == 0,
+              "one consumer thread per (chunk, 4 inputs)");
+static_assert(kQ6Warps == 3 * (kQ6StageRows / 16), "warp = (16-row tile, superblock pair)");
+
+struct Q6Smem {
+  alignas(128) uint8_t stage[kQ6Stages][kQ6StageBytes];
   alignas(16) float sz[kHeadK];
-  // the inputs' digits: word (k, unit, c) packs digit k of the unit's four
-  // inputs of quarter c; a lane's four quarters of a (k, unit) are one
-  // 16-byte load, consecutive units on consecutive lanes
-  alignas(16) uint32_t dig[3][kHeadUnits][4];
-  float uscale[kHeadUnits];
-  float red[kHeadConsumerWarps];
-  HeadBest best[kHeadConsumerWarps];
-  uint64_t full[kHeadStages];
-  uint64_t empty[kHeadStages];
+  // B operands: word (chunk, n, t) packs digit n of inputs 16 chunk + 4t ..
+  // + 3 (n >= 3: zero columns of the 8-wide product)
+  alignas(16) uint32_t dig[kQ6Chunks][8][4];
+  // accumulator inputs: -32 times the sum of digit n over the chunk's inputs
+  alignas(16) int ncorr[kQ6Chunks][8];
+  float part[2][3][kQ6StageRows];  // (stage parity, superblock pair, row) terms
+  float red[kQ6Warps];
+  float smax[kQ6Warps];
+  HeadBest best[kQ6Warps];
+  uint64_t full[kQ6Stages];
+  uint64_t empty[kQ6Stages];
   int last;
 };
 
@@ -139,22 +147,18 @@ __global__ void q6k_pack_kernel(const uint8_t* __restrict__ src, int n_rows,
   uint8_t* qh = dst + np * kQlRow + r * kQhRow;
   uint8_t* sc = dst + np * (kQlRow + kQhRow) + r * kScRow;
   uint8_t* dd = dst + np * (kQlRow + kQhRow + kScRow) + r * kDRow;
+  const int rot = 16 * (int)(r & 7);  // ql and qh rows rotated right by 16 (r % 8) bytes
   for (int i = threadIdx.x; i < kQ6RowBytes; i += blockDim.x) {
     const int s = i / kQ6SuperBytes, o = i % kQ6SuperBytes;
     const uint8_t v = r < n_rows ? src[r * kQ6RowBytes + i] : 0;
-    if (o < 128) {
-      const int hh = 2 * s + (o >> 6), b = o & 63;
-      ql[64 * hh + (b ^ ((hh & 2) ? 32 : 0))] = v;
-    } else if (o < 192) {
-      // the high bit of each 2-bit field flipped: assembled codes are code ^ 32
-      qh[64 * s + (o - 128)] = r < n_rows ? (uint8_t)(v ^ 0xAA) : (uint8_t)0;
-    } else if (o < 208) {
-      // scales[8n + 2c + g] -> byte 8hh + 4g + c
-      const int j = o - 192, n = j >> 3, c = (j & 7) >> 1, g = j & 1;
-      sc[8 * (2 * s + n) + 4 * g + c] = v;
-    } else {
+    if (o < 128)
+      ql[(128 * s + o + rot) % kQlRow] = v;
+    else if (o < 192)
+      qh[(64 * s + (o - 128) + rot) % kQhRow] = v;
+    else if (o < 208)
+      sc[16 * s + (o - 192)] = v;
+    else
       dd[2 * s + (o - 208)] = v;
-    }
   }
 }
 
@@ -165,8 +169,11 @@ __device__ __forceinline__ void head_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+// Barrier 1 over the NW consumer warps of a head kernel (its producer warp
+// never takes part).
+template <int NW = kHeadConsumerWarps>
 __device__ __forceinline__ void consumers_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kHeadConsumers) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(32 * NW) : "memory");
 }
 
 // Better pick of two: larger value, then smaller row (the host loop's first
@@ -180,25 +187,26 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 // pick goes to gbest[blockIdx.x]; the last CTA to arrive (an atomic counter)
 // reduces all of them with the tie rule of `better`, writes *token and
 // resets the counter for the next launch.
+template <int NW = kHeadConsumerWarps>
 __device__ __forceinline__ void head_pick(float best_v, int best_i, HeadBest* sbest, int* slast,
                                           HeadBest* gbest, unsigned* done, int* token) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int grid = gridDim.x;
   if (lane == 0) sbest[warp] = HeadBest{best_v, best_i};
-  consumers_sync();
+  consumers_sync<NW>();
   if (tid == 0) {
     HeadBest b = sbest[0];
-    for (int w = 1; w < kHeadConsumerWarps; ++w)
+    for (int w = 1; w < NW; ++w)
       if (better(sbest[w].v, sbest[w].i, b.v, b.i)) b = sbest[w];
     gbest[blockIdx.x] = b;
     __threadfence();
     *slast = atomicAdd(done, 1u) == (unsigned)grid - 1;
   }
-  consumers_sync();
+  consumers_sync<NW>();
   if (!*slast) return;
   __threadfence();
   HeadBest b{kNoPick, 0};
-  for (int i = tid; i < grid; i += kHeadConsumers) {
+  for (int i = tid; i < grid; i += 32 * NW) {
     const float v = __ldcg(&gbest[i].v);
     const int idx = __ldcg(&gbest[i].i);
     if (better(v, idx, b.v, b.i)) b = HeadBest{v, idx};
@@ -209,90 +217,21 @@ __device__ __forceinline__ void head_pick(float best_v, int best_i, HeadBest* sb
     const int idx = __shfl_xor_sync(0xffffffffu, b.i, off);
     if (better(v, idx, b.v, b.i)) b = HeadBest{v, idx};
   }
-  consumers_sync();  // the reads of sbest above are done
+  consumers_sync<NW>();  // the reads of sbest above are done
   if (lane == 0) sbest[warp] = b;
-  consumers_sync();
+  consumers_sync<NW>();
   if (tid == 0) {
-    for (int w = 1; w < kHeadConsumerWarps; ++w)
+    for (int w = 1; w < NW; ++w)
       if (better(sbest[w].v, sbest[w].i, b.v, b.i)) b = sbest[w];
     *token = b.i;
     *done = 0u;  // ready for the next launch
   }
 }
 
-// The consumer lane's fixed part of the row arithmetic.
-struct LaneConst {
-  int hh0, q, o0, o1;   // unit base, 4-weight group, word offsets of W0 / W1
-  int g;                // which 16 of the 32 l values: scale word 2hh + g
-};
-
 // Exact float of an int32 below 2^22 in magnitude: 2^23 + 2^22 + i as bits,
 // minus the same.
 __device__ __forceinline__ float small_int_to_float(int i) {
   return __fsub_rn(__int_as_float(0x4B400000 + i), 12582912.0f);
-}
-
-// The lane's inputs as digits (see the file comment): for unit u, quarter c
-// and digit k, e[u][c][k] packs the digits of weights 4q .. 4q + 3; s[u] is
-// the unit's power-of-two scale.
-struct LaneDigits {
-  int e[3][4][3];
-  float s[3];
-};
-
-// Unit u's term of row j of a stage for this lane: (d s) (K1 + K2/126 + K3/126^2).
-__device__ __forceinline__ float unit_term(const uint8_t* sb, int j, int u, const LaneConst& lc,
-                                           const LaneDigits& x) {
-  const uint32_t* qlw = reinterpret_cast<const uint32_t*>(sb) + j * (kQlRow / 4);
-  const uint32_t* qhw = reinterpret_cast<const uint32_t*>(sb + kStQl) + j * (kQhRow / 4);
-  const uint32_t* scw = reinterpret_cast<const uint32_t*>(sb + kStQl + kStQh) + j * (kScRow / 4);
-  const unsigned short* dw =
-      reinterpret_cast<const unsigned short*>(sb + kStQl + kStQh + kStSc) + j * (kDRow / 2);
-  const int hh = lc.hh0 + 4 * u;
-  const uint32_t W0 = qlw[16 * hh + lc.o0 + lc.q], W1 = qlw[16 * hh + lc.o1 + lc.q];
-  const uint32_t H = qhw[8 * hh + lc.q];
-  const uint32_t sv = scw[2 * hh + lc.g];
-  const float d = __half2float(__ushort_as_half(dw[hh >> 1]));
-  // byte e of Q[c] = (6-bit code of weight (quarter c, l = 4q + e)) ^ 32
-  uint32_t Q[4];
-  Q[0] = (W0 & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
-  Q[1] = (W1 & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
-  Q[2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
-  Q[3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
-  int K[3] = {0, 0, 0};
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    // code - 32 as a signed byte: y when y < 32, y - 64 (= y | 0xC0) otherwise
-    const int v = (int)((Q[c] & 0x20202020u) * 6u + Q[c]);
-    // the quarter's int8 scale, sign-extended: PTX prmt replicates the
-    // selected byte's sign bit when bit 3 of a selector nibble is set (the
-    // __byte_perm intrinsic reads only bits 0-2 of each nibble)
-    int sc;
-    asm("prmt.b32 %0, %1, 0, %2;"
-        : "=r"(sc)
-        : "r"(sv), "r"(c | (8 + c) << 4 | (8 + c) << 8 | (8 + c) << 12));
-#pragma unroll
-    for (int k = 0; k < 3; ++k) K[k] += sc * __dp4a(v, x.e[u][c][k], 0);
-  }
-  constexpr float kB1 = 1.0f / 126.0f, kB2 = 1.0f / 15876.0f;
-  const float f = __fmaf_rn(small_int_to_float(K[2]), kB2,
-                            __fmaf_rn(small_int_to_float(K[1]), kB1, small_int_to_float(K[0])));
-  return f * __fmul_rn(d, x.s[u]);  // (d s) exact: s is a power of two
-}
-
-// Rows ja and jb of a stage with the lane's inputs (lane's partial sums; the
-// caller reduces over the warp): two independent chains sharing the digits.
-__device__ __forceinline__ void rows_dot(const uint8_t* sb, int ja, int jb, const LaneConst& lc,
-                                         const LaneDigits& x, float& acc_a, float& acc_b) {
-  acc_a = 0.f;
-  acc_b = 0.f;
-#pragma unroll
-  for (int u = 0; u < 3; ++u) {
-    const float ta = unit_term(sb, ja, u, lc, x);
-    const float tb = unit_term(sb, jb, u, lc, x);
-    acc_a = __fadd_rn(acc_a, ta);
-    acc_b = __fadd_rn(acc_b, tb);
-  }
 }
 
 // The CTA's rows: a contiguous range of the padded rows, cut on multiples of
@@ -304,25 +243,100 @@ __device__ __forceinline__ void head_cta_rows(long long np, long long& r_begin, 
   r_end = units * (blockIdx.x + 1) / gridDim.x * 4;
 }
 
-__global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadParams p) {
+// One m16n8k16 tensor-core product on 8-bit integers: D = A B + C with A
+// 16 x 16 unsigned (a0: row g, a1: row g + 8; bytes k = 4t .. 4t + 3, g =
+// lane / 4, t = lane % 4), B 16 x 8 signed (b0: column g, rows k = 4t ..
+// 4t + 3) and C, D 16 x 8 int32 (d0, d1: row g, columns 2t, 2t + 1; d2, d3:
+// row g + 8).
+__device__ __forceinline__ void mma_u8s8_m16n8k16(int (&d)[4], uint32_t a0, uint32_t a1,
+                                                  uint32_t b0, int c0, int c1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, "
+      "{%7,%8,%9,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0), "r"(c0), "r"(c1), "r"(c0), "r"(c1));
+}
+
+// Byte b of w as a signed int (PTX prmt replicates the selected byte's sign
+// bit when bit 3 of a selector nibble is set).
+__device__ __forceinline__ int sext_byte(uint32_t w, int b) {
+  int r;
+  asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(b | (8 + b) << 4 | (8 + b) << 8 | (8 + b) << 12));
+  return r;
+}
+
+// Rows (row, row + 8) of a stage, superblock sb: the lane's share of the
+// exact integer sums K_n = sum_g scale_g sum_i (code - 32) e_n (digit n's
+// column of the product; the lane holds columns 2t, 2t + 1 of both rows in
+// acc).  The codes come from the un-rotated ql / qh words of the lane's four
+// weights of each group; code - 32 is formed by the accumulator input
+// C = -32 sum e over the group.
+__device__ __forceinline__ void q6_superblock(const uint8_t* st, int row, int rot_a, int rot_b,
+                                              int sb, int lane, const Q6Smem& sm, int (&acc)[4]) {
+  const int t = lane & 3, gcol = lane >> 2;
+  const uint32_t* qlw = reinterpret_cast<const uint32_t*>(st);
+  const uint32_t* qhw = reinterpret_cast<const uint32_t*>(st + kQ6StQl);
+  const uint4* scw = reinterpret_cast<const uint4*>(st + kQ6StQl + kQ6StQh);
+  const uint32_t* ql_a = qlw + row * (kQlRow / 4);
+  const uint32_t* ql_b = qlw + (row + 8) * (kQlRow / 4);
+  const uint32_t* qh_a = qhw + row * (kQhRow / 4);
+  const uint32_t* qh_b = qhw + (row + 8) * (kQhRow / 4);
+  const uint4 sa = scw[row * (kScRow / 16) + sb];
+  const uint4 sb4 = scw[(row + 8) * (kScRow / 16) + sb];
+  const uint32_t swa[4] = {sa.x, sa.y, sa.z, sa.w};
+  const uint32_t swb[4] = {sb4.x, sb4.y, sb4.z, sb4.w};
+#pragma unroll
+  for (int n = 0; n < 2; ++n) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int wq = sb * 32 + 16 * n + 4 * h + t;   // ql word of quarters 0 / 2 (+8: 1 / 3)
+      const int wh = sb * 16 + 8 * n + 4 * h + t;    // qh word of all four quarters
+      const uint32_t w0a = ql_a[(wq + rot_a) % (kQlRow / 4)];
+      const uint32_t w1a = ql_a[(wq + 8 + rot_a) % (kQlRow / 4)];
+      const uint32_t ha = qh_a[(wh + rot_a) % (kQhRow / 4)];
+      const uint32_t w0b = ql_b[(wq + rot_b) % (kQlRow / 4)];
+      const uint32_t w1b = ql_b[(wq + 8 + rot_b) % (kQlRow / 4)];
+      const uint32_t hb = qh_b[(wh + rot_b) % (kQhRow / 4)];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int g = 8 * n + 2 * c + h;  // scale group of the superblock
+        const int chunk = sb * 16 + g;
+        const uint32_t wa = (c & 1) ? w1a : w0a, wb = (c & 1) ? w1b : w0b;
+        const uint32_t qa = ((wa >> (4 * (c >> 1))) & 0x0F0F0F0Fu) | (((ha >> (2 * c)) & 0x03030303u) << 4);
+        const uint32_t qb = ((wb >> (4 * (c >> 1))) & 0x0F0F0F0Fu) | (((hb >> (2 * c)) & 0x03030303u) << 4);
+        const uint32_t b0 = sm.dig[chunk][gcol][t];
+        const int2 cc = *reinterpret_cast<const int2*>(&sm.ncorr[chunk][2 * t]);
+        int d[4];
+        mma_u8s8_m16n8k16(d, qa, qb, b0, cc.x, cc.y);
+        const int sa_g = sext_byte(swa[g >> 2], g & 3), sb_g = sext_byte(swb[g >> 2], g & 3);
+        acc[0] += sa_g * d[0];
+        acc[1] += sa_g * d[1];
+        acc[2] += sb_g * d[2];
+        acc[3] += sb_g * d[3];
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kQ6Threads, 1) lm_head_kernel(const HeadParams p) {
   extern __shared__ __align__(128) unsigned char head_smem_raw[];
-  HeadSmem& sm = *reinterpret_cast<HeadSmem*>(head_smem_raw);
+  Q6Smem& sm = *reinterpret_cast<Q6Smem*>(head_smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_rows = p.n_rows;
   const long long np = head_padded_rows(n_rows);
   long long r_begin, r_end;
   head_cta_rows(np, r_begin, r_end);
-  const int n_stages = (int)((r_end - r_begin + kStageRows - 1) / kStageRows);
+  const int n_stages = (int)((r_end - r_begin + kQ6StageRows - 1) / kQ6StageRows);
   if (tid == 0) {
-    for (int s = 0; s < kHeadStages; ++s) {
+    for (int s = 0; s < kQ6Stages; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], kHeadConsumerWarps);
+      mbar_init(&sm.empty[s], 1);
     }
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == kHeadConsumerWarps) {
+  if (warp == kQ6Warps) {
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint8_t* ql = p.planes;
@@ -333,34 +347,35 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
       int k = 0;
       bool ok = true;
       for (; k < n_stages; ++k) {
-        const int s = k % kHeadStages;
-        if (k >= kHeadStages &&
-            !mbar_wait_bounded(&sm.empty[s], ((k / kHeadStages) - 1) & 1, kHeadWaitBudget)) {
+        const int s = k % kQ6Stages;
+        if (k >= kQ6Stages &&
+            !mbar_wait_bounded(&sm.empty[s], ((k / kQ6Stages) - 1) & 1, kHeadWaitBudget)) {
           ok = false;
           break;
         }
-        const long long r0 = r_begin + (long long)k * kStageRows;
-        const int nr = (int)min((long long)kStageRows, r_end - r0);  // a multiple of 4
+        const long long r0 = r_begin + (long long)k * kQ6StageRows;
+        const int nr = (int)min((long long)kQ6StageRows, r_end - r0);  // a multiple of 4
         uint8_t* st = sm.stage[s];
         mbar_arrive_expect_tx(&sm.full[s], (uint32_t)(nr * kQ6RowBytes));
         bulk_copy_g2s(st, ql + r0 * kQlRow, nr * kQlRow, &sm.full[s], pol);
-        bulk_copy_g2s(st + kStQl, qh + r0 * kQhRow, nr * kQhRow, &sm.full[s], pol);
-        bulk_copy_g2s(st + kStQl + kStQh, sc + r0 * kScRow, nr * kScRow, &sm.full[s], pol);
-        bulk_copy_g2s(st + kStQl + kStQh + kStSc, dd + r0 * kDRow, nr * kDRow, &sm.full[s], pol);
-        if (k == kHeadStages - 1) {
+        bulk_copy_g2s(st + kQ6StQl, qh + r0 * kQhRow, nr * kQhRow, &sm.full[s], pol);
+        bulk_copy_g2s(st + kQ6StQl + kQ6StQh, sc + r0 * kScRow, nr * kScRow, &sm.full[s], pol);
+        bulk_copy_g2s(st + kQ6StQl + kQ6StQh + kQ6StSc, dd + r0 * kDRow, nr * kDRow, &sm.full[s],
+                      pol);
+        if (k == kQ6Stages - 1) {
           pdl_wait();
           pdl_launch_dependents();
         }
       }
-      if (k < kHeadStages) {
+      if (k < kQ6Stages) {
         pdl_wait();
         pdl_launch_dependents();
       }
       if (!ok) atomicOr(p.status, kStatusWaitTimeout);
       // Every copy issued has landed before the CTA may exit: wait for the
       // last use of each stage (a no-op when the consumers already did).
-      for (int kk = max(0, k - kHeadStages); kk < k; ++kk)
-        mbar_wait_bounded(&sm.full[kk % kHeadStages], (kk / kHeadStages) & 1, kHeadWaitBudget);
+      for (int kk = max(0, k - kQ6Stages); kk < k; ++kk)
+        mbar_wait_bounded(&sm.full[kk % kQ6Stages], (kk / kQ6Stages) & 1, kHeadWaitBudget);
     } else {
       pdl_wait();
       pdl_launch_dependents();
@@ -369,10 +384,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
   }
 
   // ---------------- consumers ----------------
-  constexpr int kPer = kHeadK / kHeadConsumers;
+  constexpr int kPer = kHeadK / kQ6Consumers;  // 4
   float gm[kPer];
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) gm[k] = p.gamma[tid + k * kHeadConsumers];
+  for (int k = 0; k < kPer; ++k) gm[k] = p.gamma[tid + k * kQ6Consumers];
   pdl_wait();
   pdl_launch_dependents();
 
@@ -381,36 +396,44 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
-    xv[k] = p.state[tid + k * kHeadConsumers];
+    xv[k] = p.state[tid + k * kQ6Consumers];
     ss += xv[k] * xv[k];
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   if (lane == 0) sm.red[warp] = ss;
-  consumers_sync();
+  consumers_sync<kQ6Warps>();
   float tot = 0.f;
 #pragma unroll
-  for (int k = 0; k < kHeadConsumerWarps; ++k) tot += sm.red[k];
+  for (int k = 0; k < kQ6Warps; ++k) tot += sm.red[k];
   const float scale = 1.0f / sqrtf(tot / (float)kHeadK + kHeadRmsEps);
+  float mz = 0.f;
 #pragma unroll
-  for (int k = 0; k < kPer; ++k) sm.sz[tid + k * kHeadConsumers] = xv[k] * scale * gm[k];
-  consumers_sync();
+  for (int k = 0; k < kPer; ++k) {
+    const float z = xv[k] * scale * gm[k];
+    sm.sz[tid + k * kQ6Consumers] = z;
+    mz = fmaxf(mz, fabsf(z));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mz = fmaxf(mz, __shfl_xor_sync(0xffffffffu, mz, off));
+  if (lane == 0) sm.smax[warp] = mz;
+  consumers_sync<kQ6Warps>();
 
-  // ---- the inputs as digits, one word (unit, quarter) per thread: unit
-  // (hh, q) holds inputs 128hh + 32c + 4q + e, c, e < 4 ----
-  if (tid < kHeadUnits * 4) {
-    const int unit = tid >> 2, c = tid & 3, hh = unit >> 3, q = unit & 7;
-    const float4 zz = *reinterpret_cast<const float4*>(sm.sz + 128 * hh + 32 * c + 4 * q);
-    float mx = fmaxf(fmaxf(fabsf(zz.x), fabsf(zz.y)), fmaxf(fabsf(zz.z), fabsf(zz.w)));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));  // the unit's four words are
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));  // four consecutive lanes
-    // s = the smallest power of two >= mx / 63 (1 when the unit is all zero)
-    const uint32_t mb = __float_as_uint(mx / 63.0f);
-    const uint32_t sb = (mb & 0x007FFFFFu) ? (mb & 0x7F800000u) + 0x00800000u : mb;
-    const float sunit = mx > 0.f ? __uint_as_float(sb) : 1.0f;
-    const float inv = __frcp_rn(sunit);  // exact: a power of two
+  // ---- the inputs as digits: one power-of-two scale s >= max|z| / 63 for
+  // the whole vector; thread (chunk, t) splits inputs 16 chunk + 4t .. + 3 ----
+  float mx = 0.f;
+#pragma unroll
+  for (int k = 0; k < kQ6Warps; ++k) mx = fmaxf(mx, sm.smax[k]);
+  const uint32_t mb = __float_as_uint(mx / 63.0f);
+  const uint32_t sbits = (mb & 0x007FFFFFu) ? (mb & 0x7F800000u) + 0x00800000u : mb;
+  const float s_in = mx > 0.f ? __uint_as_float(sbits) : 1.0f;
+  {
+    const float inv = __frcp_rn(s_in);  // exact: a power of two
+    const int chunk = tid >> 2, t = tid & 3;
+    const float4 zz = *reinterpret_cast<const float4*>(sm.sz + 16 * chunk + 4 * t);
     const float xs[4] = {zz.x * inv, zz.y * inv, zz.z * inv, zz.w * inv};
     uint32_t by[3][4];
+    int sum[3] = {0, 0, 0};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       // round to nearest by 1.5 * 2^23 (|x| <= 63): the sum's low byte is the
@@ -423,82 +446,100 @@ __global__ void __launch_bounds__(kHeadThreads, 1) lm_head_kernel(const HeadPara
       const float d2 = __fsub_rn(t2, kMagic);
       const float r2 = __fmul_rn(__fsub_rn(r1, d2), 126.0f);
       const float t3 = __fadd_rn(r2, kMagic);
+      const float d3 = __fsub_rn(t3, kMagic);
       by[0][e] = __float_as_uint(t1);
       by[1][e] = __float_as_uint(t2);
       by[2][e] = __float_as_uint(t3);
+      sum[0] += (int)d1;
+      sum[1] += (int)d2;
+      sum[2] += (int)d3;
     }
-#pragma unroll
-    for (int k = 0; k < 3; ++k)
-      sm.dig[k][unit][c] = __byte_perm(__byte_perm(by[k][0], by[k][1], 0x0040),
-                                       __byte_perm(by[k][2], by[k][3], 0x0040), 0x5410);
-    if (c == 0) sm.uscale[unit] = sunit;
-  }
-  consumers_sync();
-
-  LaneConst lc;
-  lc.hh0 = lane >> 3;
-  lc.q = lane & 7;
-  lc.o0 = (lc.hh0 & 2) ? 8 : 0;  // the pack swapped the halves of these units
-  lc.o1 = 8 - lc.o0;
-  lc.g = (lane & 7) >> 2;
-  LaneDigits x;
-#pragma unroll
-  for (int u = 0; u < 3; ++u) {
-    const int unit = 8 * (lc.hh0 + 4 * u) + lc.q;  // = lane + 32u: consecutive per lane
-    x.s[u] = sm.uscale[unit];
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
-      const uint4 w = *reinterpret_cast<const uint4*>(&sm.dig[k][unit][0]);
-      x.e[u][0][k] = (int)w.x;
-      x.e[u][1][k] = (int)w.y;
-      x.e[u][2][k] = (int)w.z;
-      x.e[u][3][k] = (int)w.w;
+      sm.dig[chunk][k][t] = __byte_perm(__byte_perm(by[k][0], by[k][1], 0x0040),
+                                        __byte_perm(by[k][2], by[k][3], 0x0040), 0x5410);
+      sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], 1);
+      sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], 2);
+    }
+#pragma unroll
+    for (int k = 3; k < 8; ++k) sm.dig[chunk][k][t] = 0u;
+    if (t == 0) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sm.ncorr[chunk][k] = k < 3 ? -32 * sum[k] : 0;
     }
   }
+  consumers_sync<kQ6Warps>();
 
+  // Warp w takes rows 16 (w / 3) .. + 15 of a stage over superblocks
+  // 2 (w % 3) and 2 (w % 3) + 1; lane (g, t) rows g and g + 8 of those.
+  const int tile = warp / 3, pair = warp % 3, t = lane & 3;
+  const int row = 16 * tile + (lane >> 2);
   float best_v = kNoPick;
   int best_i = 0;
   bool ok = true;
   const long long r_stop = min(r_end, (long long)n_rows);  // padding rows are never output
-  const int ja = warp, jb = warp + kStageRows / 2;
   for (int k = 0; k < n_stages; ++k) {
-    const int s = k % kHeadStages;
-    if (!mbar_wait_bounded(&sm.full[s], (k / kHeadStages) & 1, kHeadWaitBudget)) {
-      ok = false;
-      break;
-    }
-    const long long r0 = r_begin + (long long)k * kStageRows;
-    // (jb > ja: a warp whose first row is past the CTA's rows has none; the
-    // rows past a short last stage hold stale bytes and are not output)
-    if (r0 + ja < r_stop) {
-      float acc_a, acc_b;
-      rows_dot(sm.stage[s], ja, jb, lc, x, acc_a, acc_b);
+    const int s = k % kQ6Stages;
+    if (!mbar_wait_bounded(&sm.full[s], (k / kQ6Stages) & 1, kHeadWaitBudget)) ok = false;
+    ok = __all_sync(0xffffffffu, ok);
+    const long long r0 = r_begin + (long long)k * kQ6StageRows;
+    const int nr = (int)min((long long)kQ6StageRows, r_end - r0);
+    float* part = sm.part[k & 1][pair];
+    if (ok && 16 * tile < nr) {
+      const uint8_t* st = sm.stage[s];
+      const int rot_a = 4 * (int)((r0 + row) & 7), rot_b = 4 * (int)((r0 + row + 8) & 7);
+      const unsigned short* dw =
+          reinterpret_cast<const unsigned short*>(st + kQ6StQl + kQ6StQh + kQ6StSc);
+      float term_a = 0.f, term_b = 0.f;
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        acc_a += __shfl_xor_sync(0xffffffffu, acc_a, off);
-        acc_b += __shfl_xor_sync(0xffffffffu, acc_b, off);
+      for (int q = 0; q < 2; ++q) {
+        const int sb = 2 * pair + q;
+        int acc[4] = {0, 0, 0, 0};
+        q6_superblock(st, row, rot_a, rot_b, sb, lane, sm, acc);
+        // K1, K2 sit in the lanes t == 0 (columns 0, 1), K3 in t == 1 (column 2).
+        const int k3a = __shfl_down_sync(0xffffffffu, acc[0], 1);
+        const int k3b = __shfl_down_sync(0xffffffffu, acc[2], 1);
+        constexpr float kB1 = 1.0f / 126.0f, kB2 = 1.0f / 15876.0f;
+        const float fa = __fmaf_rn((float)k3a, kB2, __fmaf_rn((float)acc[1], kB1, (float)acc[0]));
+        const float fb = __fmaf_rn((float)k3b, kB2, __fmaf_rn((float)acc[3], kB1, (float)acc[2]));
+        const float da = __half2float(__ushort_as_half(dw[row * (kDRow / 2) + sb]));
+        const float db = __half2float(__ushort_as_half(dw[(row + 8) * (kDRow / 2) + sb]));
+        const float ta = fa * __fmul_rn(da, s_in), tb = fb * __fmul_rn(db, s_in);  // (d s) exact
+        term_a = q == 0 ? ta : __fadd_rn(term_a, ta);
+        term_b = q == 0 ? tb : __fadd_rn(term_b, tb);
       }
-      // rows rise within a warp (ja < jb, stages in order): the first maximum stays
-      if (p.logits && lane == 0) p.logits[r0 + ja] = acc_a;
-      if (acc_a > best_v) {
-        best_v = acc_a;
-        best_i = (int)(r0 + ja);
-      }
-      if (r0 + jb < r_stop) {
-        if (p.logits && lane == 0) p.logits[r0 + jb] = acc_b;
-        if (acc_b > best_v) {
-          best_v = acc_b;
-          best_i = (int)(r0 + jb);
-        }
+      if (t == 0) {
+        part[row] = term_a;
+        part[row + 8] = term_b;
       }
     }
-    __syncwarp();
-    if (lane == 0) head_arrive(&sm.empty[s]);
+    consumers_sync<kQ6Warps>();  // every pair's terms of the stage are in place
+    if (tid == 0) head_arrive(&sm.empty[s]);
+    if (tid < kQ6StageRows && tid < nr && r0 + tid < r_stop && ok) {
+      const float* pk = sm.part[k & 1][0];
+      const float v = __fadd_rn(__fadd_rn(pk[tid], pk[kQ6StageRows + tid]),
+                                pk[2 * kQ6StageRows + tid]);
+      if (p.logits) p.logits[r0 + tid] = v;
+      // rows rise within a thread (stages in order): the first maximum stays
+      if (v > best_v) {
+        best_v = v;
+        best_i = (int)(r0 + tid);
+      }
+    }
   }
-  if (!ok && lane == 0) atomicOr(p.status, kStatusWaitTimeout);
+  if (!ok && tid == 0) atomicOr(p.status, kStatusWaitTimeout);
   if (!p.token) return;
-
-  head_pick(best_v, best_i, sm.best, &sm.last, p.best, p.done, p.token);
+  // the lanes' picks meet within each warp first (first maximum on ties)
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float v = __shfl_xor_sync(0xffffffffu, best_v, off);
+    const int idx = __shfl_xor_sync(0xffffffffu, best_i, off);
+    if (better(v, idx, best_v, best_i)) {
+      best_v = v;
+      best_i = idx;
+    }
+  }
+  head_pick<kQ6Warps>(best_v, best_i, sm.best, &sm.last, p.best, p.done, p.token);
 }
 
 // ---------------------------------------------------------------------------
@@ -870,7 +911,7 @@ int lm_head_grid(int n_sm) { return n_sm; }
 cudaError_t prepare_head_kernels() {
   cudaError_t e = cudaFuncSetAttribute((const void*)lm_head_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sizeof(HeadSmem));
+                                       (int)sizeof(Q6Smem));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void*)lm_head_q8_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Q8Smem));
@@ -905,8 +946,8 @@ cudaError_t launch_lm_head(bool q8, const void* planes, int n_rows, const float*
   p.status = status;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kHeadThreads);
-  cfg.dynamicSmemBytes = q8 ? sizeof(Q8Smem) : sizeof(HeadSmem);
+  cfg.blockDim = dim3(q8 ? kHeadThreads : kQ6Threads);
+  cfg.dynamicSmemBytes = q8 ? sizeof(Q8Smem) : sizeof(Q6Smem);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -184,24 +184,23 @@ def q6_k_dequant(blocks: np.ndarray, rows: int, cols: int = 1536) -> np.ndarray:
 def q6_k_planes(blocks: np.ndarray, rows: int) -> np.ndarray:
     """The byte layout gqa_lm_head_pack writes, over the rows rounded up to a
     multiple of 4 (padding rows zero): ql [Np][768], qh [Np][384], scales
-    [Np][96], d [Np][12], superblock order kept within each plane, except that
-    the two 32-byte halves of half-superblock hh's 64 ql bytes are swapped
-    when hh & 2, that scales[8n + 2c + g] of a superblock moves to byte
-    8hh + 4g + c of the row (hh = 2 * superblock + n), and that the qh bytes
-    of real rows are stored XOR 0xAA (the high bit of each 2-bit field
-    flipped)."""
+    [Np][96], d [Np][12], each row the concatenation of its six superblocks'
+    bytes of that kind in their own order, except that row r's ql and qh rows
+    are rotated right by 16 * (r % 8) bytes (byte i of the row is stored at
+    (i + 16 (r % 8)) mod the row length), so that eight consecutive rows read
+    at one offset fall on different shared-memory banks."""
     np_rows = (rows + 3) // 4 * 4
     b = np.zeros((np_rows, 6, Q6_K_BLOCK_BYTES), dtype=np.uint8)
     b[:rows] = np.asarray(blocks, dtype=np.uint8).reshape(rows, 6, Q6_K_BLOCK_BYTES)
-    ql = b[:, :, :128].reshape(np_rows, 12, 2, 32).copy()  # [row][hh][half][32]
-    swap = (np.arange(12) & 2) != 0
-    ql[:, swap] = ql[:, swap][:, :, ::-1]
-    sc = b[:, :, 192:208].reshape(np_rows, 6, 2, 4, 2)  # [row][sb][n][c][g]
-    sc = np.ascontiguousarray(sc.transpose(0, 1, 2, 4, 3))   # [row][sb][n][g][c]
-    qh = b[:, :, 128:192].copy()
-    qh[:rows] ^= np.uint8(0xAA)
-    return np.concatenate([ql.reshape(-1), qh.reshape(-1),
-                           sc.reshape(-1), b[:, :, 208:].reshape(-1)])
+    ql = np.ascontiguousarray(b[:, :, :128]).reshape(np_rows, 768)
+    qh = np.ascontiguousarray(b[:, :, 128:192]).reshape(np_rows, 384)
+    for r in range(min(np_rows, 8)):
+        sel = np.arange(r, np_rows, 8)
+        ql[sel] = np.roll(ql[sel], 16 * r, axis=1)
+        qh[sel] = np.roll(qh[sel], 16 * r, axis=1)
+    sc = np.ascontiguousarray(b[:, :, 192:208]).reshape(np_rows, 96)
+    dd = np.ascontiguousarray(b[:, :, 208:]).reshape(np_rows, 12)
+    return np.concatenate([ql.reshape(-1), qh.reshape(-1), sc.reshape(-1), dd.reshape(-1)])
 
 
 def q8_0_matrix(seed: int, stream_id: int, rows: int, cols: int = 896,

@@ -1,11 +1,11 @@
 """The integer arithmetic of the two LM heads, restated in numpy from the
 packed planes (no GPU): the inputs split into three signed 8-bit digits, the
-exact int32 dot products, and the bounds the kernels rely on -- every digit
-inside its range and every digit sum below 2^22 in magnitude, where the
-2^23 + 2^22 magic conversion to float is exact -- on worst-case weights and
-inputs; with unit inputs z = 32 e_i the Q6_K logits equal the reference's
-compiled GEMV bit for bit (the property tests/test_head_gpu.py checks on the
-device)."""
+exact integer dot products, and the bounds the kernels rely on -- every digit
+inside its range; the Q6_K head's per-superblock sums inside int32, the Q8_0
+head's digit sums below 2^22 in magnitude, where the 2^23 + 2^22 magic
+conversion to float is exact -- on worst-case weights and inputs; with unit
+inputs z = 32 e_i the Q6_K logits equal the reference's compiled GEMV bit for
+bit (the property tests/test_head_gpu.py checks on the device)."""
 import numpy as np
 import pytest
 
@@ -19,19 +19,20 @@ def _round(x):
     return (t - MAGIC).astype(F32)
 
 
-def q6_digits(z_units):
-    """lm_head_kernel's split: per 16-input unit a power-of-two scale
-    s >= max|z| / 63, digits in base 126."""
-    mx = np.abs(z_units).max(axis=1).astype(F32)
-    mb = (mx / F32(63)).astype(F32).view(np.uint32)
-    sb = np.where(mb & 0x007FFFFF, (mb & 0x7F800000) + 0x00800000, mb).astype(np.uint32)
-    s = np.where(mx > 0, sb.view(F32), F32(1)).astype(F32)
-    x = (z_units * (F32(1) / s)[:, None]).astype(F32)
+def q6_digits(z):
+    """lm_head_kernel's split: one power-of-two scale s >= max|z| / 63 for the
+    whole input vector, then three digits in base 126, each in [-63, 63]."""
+    z = np.asarray(z, F32)
+    mx = F32(np.abs(z).max())
+    mb = int(np.array([mx / F32(63)], F32).view(np.uint32)[0])
+    sb = (mb & 0x7F800000) + 0x00800000 if mb & 0x007FFFFF else mb
+    s = np.array([sb], np.uint32).view(F32)[0] if mx > 0 else F32(1)
+    x = (z * (F32(1) / s)).astype(F32)
     d1 = _round(x)
     r1 = ((x - d1).astype(F32) * F32(126)).astype(F32)
     d2 = _round(r1)
     d3 = _round(((r1 - d2).astype(F32) * F32(126)).astype(F32))
-    return s, np.stack([d1, d2, d3], axis=1).astype(np.int64)
+    return F32(s), np.stack([d1, d2, d3]).astype(np.int64)
 
 
 def q8_digits(z_blocks):
@@ -53,55 +54,44 @@ def _fma(a, b, c):
 
 
 def q6_logits(planes, n_rows, z):
-    """The kernel's row arithmetic from the gqa_lm_head_pack planes: lane
-    (hh0, q) owns units hh0 + 4u; code bytes (code ^ 32 from the packed qh)
-    become code - 32; per unit K_k = sum_c scale_c * sum_e (code - 32) e_k;
-    the term (d s)(K1 + K2/126 + K3/126^2); the lane sums by the butterfly.
-    Returns (logits, max |K|)."""
+    """The kernel's row arithmetic from the gqa_lm_head_pack planes: the ql and
+    qh rows un-rotated, 6-bit codes assembled, per superblock and digit the
+    exact integer K_k = sum_g scale_g * sum_i (code - 32) e_k over its 16
+    groups of 16 weights (the tensor-core products, code - 32 by the
+    accumulator's offset), the superblock's term (d s)(K1 + K2/126 +
+    K3/126^2), the terms summed in pairs of superblocks (0+1, 2+3, 4+5, one
+    warp each) and the pairs in order.  Returns (logits, max |K|)."""
     np_rows = (n_rows + 3) // 4 * 4
-    ql = np.ascontiguousarray(planes[:np_rows * 768]).view("<u4").reshape(np_rows, 192)
-    qh = np.ascontiguousarray(planes[np_rows * 768:np_rows * 1152]).view("<u4").reshape(np_rows, 96)
+    ql = np.ascontiguousarray(planes[:np_rows * 768]).reshape(np_rows, 768)[:n_rows].copy()
+    qh = np.ascontiguousarray(planes[np_rows * 768:np_rows * 1152]).reshape(np_rows, 384)[:n_rows].copy()
     sc = np.ascontiguousarray(planes[np_rows * 1152:np_rows * 1248]).view(np.int8).reshape(np_rows, 96)
     dd = np.ascontiguousarray(planes[np_rows * 1248:]).view(np.float16).reshape(np_rows, 6).astype(F32)
-    zu = np.zeros((96, 16), F32)  # unit 8hh + q: inputs 128hh + 32c + 4q + e
-    for hh in range(12):
-        for q in range(8):
-            for c in range(4):
-                zu[8 * hh + q, 4 * c:4 * c + 4] = z[128 * hh + 32 * c + 4 * q:][:4]
-    s, e = q6_digits(zu)
+    for r in range(min(n_rows, 8)):
+        sel = np.arange(r, n_rows, 8)
+        ql[sel] = np.roll(ql[sel], -16 * r, axis=1)
+        qh[sel] = np.roll(qh[sel], -16 * r, axis=1)
+    s, e = q6_digits(z)
     assert np.abs(e).max() <= 63
-    lane = np.zeros((n_rows, 32), F32)
+    j = np.arange(256)
+    n, rr = j // 128, j % 128
+    c, l = rr // 32, rr % 32
     kmax = 0
-    for ln in range(32):
-        hh0, q = ln >> 3, ln & 7
-        o0 = 8 if hh0 & 2 else 0
-        acc = np.zeros(n_rows, F32)
-        for u in range(3):
-            hh = hh0 + 4 * u
-            unit = 8 * hh + q
-            w0 = ql[:n_rows, 16 * hh + o0 + q].astype(np.int64)
-            w1 = ql[:n_rows, 16 * hh + 8 - o0 + q].astype(np.int64)
-            h = qh[:n_rows, 8 * hh + q].astype(np.int64)
-            words = [(w0 & 0x0F0F0F0F) | ((h << 4) & 0x30303030),
-                     (w1 & 0x0F0F0F0F) | ((h << 2) & 0x30303030),
-                     ((w0 >> 4) & 0x0F0F0F0F) | (h & 0x30303030),
-                     ((w1 >> 4) & 0x0F0F0F0F) | ((h >> 2) & 0x30303030)]
-            k = np.zeros((n_rows, 3), np.int64)
-            for c in range(4):
-                v = ((words[c] & 0x20202020) * 6 + words[c]) & 0xFFFFFFFF
-                vb = np.ascontiguousarray(v.astype(np.uint32)).view(np.int8).reshape(n_rows, 4)
-                scale = sc[:n_rows, 8 * hh + 4 * (q >> 2) + c].astype(np.int64)
-                for kk in range(3):
-                    k[:, kk] += scale * (vb.astype(np.int64) * e[unit, kk, 4 * c:4 * c + 4]).sum(1)
-            kmax = max(kmax, int(np.abs(k).max()))
-            f = _fma(k[:, 2].astype(F32), F32(1 / 15876), _fma(k[:, 1].astype(F32), F32(1 / 126),
-                                                              k[:, 0].astype(F32)))
-            term = (f * (dd[:n_rows, hh >> 1] * s[unit]).astype(F32)).astype(F32)
-            acc = (acc + term).astype(F32)
-        lane[:, ln] = acc
-    for off in (16, 8, 4, 2, 1):
-        lane = (lane + lane[:, np.arange(32) ^ off]).astype(F32)
-    return lane[:, 0], kmax
+    terms = []
+    for sb in range(6):
+        lo = ql[:, sb * 128 + 64 * n + 32 * (c & 1) + l].astype(np.int64)
+        hi = qh[:, sb * 64 + 32 * n + l].astype(np.int64)
+        code = ((lo >> (4 * (c >> 1))) & 15) | (((hi >> (2 * c)) & 3) << 4)   # [rows][256]
+        scale = sc[:n_rows, sb * 16:sb * 16 + 16].astype(np.int64)            # [rows][16]
+        k = np.zeros((n_rows, 3), np.int64)
+        for kk in range(3):
+            prod = (code - 32) * e[kk, sb * 256:sb * 256 + 256][None, :]
+            k[:, kk] = (scale * prod.reshape(n_rows, 16, 16).sum(2)).sum(1)
+        kmax = max(kmax, int(np.abs(k).max()))
+        f = _fma(k[:, 2].astype(F32), F32(1 / 15876), _fma(k[:, 1].astype(F32), F32(1 / 126),
+                                                          k[:, 0].astype(F32)))
+        terms.append((f * (dd[:n_rows, sb] * s).astype(F32)).astype(F32))
+    pairs = [(terms[2 * p] + terms[2 * p + 1]).astype(F32) for p in range(3)]
+    return ((pairs[0] + pairs[1]).astype(F32) + pairs[2]).astype(F32), kmax
 
 
 def _worst_q6(pkg, n):
@@ -129,7 +119,7 @@ def test_q6_digits_and_bounds(pkg, orc):
                    ).astype(F32),                                 # mixed powers of two
                   (rng.standard_normal(1536) * 1e-30).astype(F32)):  # tiny inputs
             got, kmax = q6_logits(planes, n, z)
-            assert kmax < LIMIT
+            assert kmax < 2 ** 31 - 1
             want = dense @ z.astype(np.float64)
             err = np.abs(got - want).max() / max(np.sqrt(np.mean(want ** 2)), 1e-300)
             assert err <= 1e-5, err

@@ -107,26 +107,26 @@ def test_greedy_pick_rules(orc):
 
 
 def test_planes_layout(pkg):
-    """Planes over 4 rows (3 real + 1 zero padding row); ql halves of the
-    half-superblocks hh with hh & 2 swapped; qh bytes XOR 0xAA; scales
-    regrouped per (hh, g)."""
-    w = pkg.seeded.q6_k_matrix(25, pkg.seeded.W_HEAD, 3)
-    p = pkg.seeded.q6_k_planes(w, 3)
-    n = 4
+    """Planes over 12 rows (11 real + 1 zero padding row): each row's ql and
+    qh bytes in superblock order, rotated right by 16 * (row % 8) bytes;
+    scales and d in superblock order."""
+    rows = 11
+    w = pkg.seeded.q6_k_matrix(25, pkg.seeded.W_HEAD, rows)
+    p = pkg.seeded.q6_k_planes(w, rows)
+    n = 12
     assert p.size == n * ROW
-    b = w.reshape(3, 6, 210)
-    row0_ql = p[:768].reshape(12, 64)
-    for hh in range(12):
-        src = b[0, hh // 2, 64 * (hh % 2):64 * (hh % 2) + 64]
-        want = np.concatenate([src[32:], src[:32]]) if hh & 2 else src
-        assert np.array_equal(row0_ql[hh], want), hh
-    assert not p[3 * 768:4 * 768].any()                                   # padding row
-    assert np.array_equal(p[n * 768 + 384:n * 768 + 768], b[1, :, 128:192].reshape(-1) ^ 0xAA)
-    sc_row2 = p[n * 1152 + 96 * 2:n * 1152 + 96 * 3].reshape(12, 2, 4)  # [hh][g][c]
-    for hh in range(12):
-        for g in range(2):
-            for c in range(4):
-                want = b[2, hh // 2, 192 + 8 * (hh % 2) + 2 * c + g]
-                assert sc_row2[hh, g, c] == want
-    assert not p[n * 1152 + 96 * 3:n * 1152 + 96 * 4].any()             # padding row
-    assert np.array_equal(p[n * 1248:n * 1248 + 12], b[0, :, 208:].reshape(-1))
+    b = w.reshape(rows, 6, 210)
+    for r in range(rows):
+        ql = p[768 * r:768 * (r + 1)]
+        qh = p[n * 768 + 384 * r:n * 768 + 384 * (r + 1)]
+        rot = 16 * (r % 8)
+        for i in (0, 1, 127, 128, 500, 767):
+            assert ql[(i + rot) % 768] == b[r, i // 128, i % 128], (r, i)
+        for i in (0, 63, 64, 200, 383):
+            assert qh[(i + rot) % 384] == b[r, i // 64, 128 + i % 64], (r, i)
+        assert np.array_equal(p[n * 1152 + 96 * r:n * 1152 + 96 * (r + 1)],
+                              b[r, :, 192:208].reshape(-1))
+        assert np.array_equal(p[n * 1248 + 12 * r:n * 1248 + 12 * (r + 1)],
+                              b[r, :, 208:].reshape(-1))
+    for base, width in ((0, 768), (n * 768, 384), (n * 1152, 96), (n * 1248, 12)):
+        assert not p[base + width * rows:base + width * n].any()             # padding row
