@@ -243,6 +243,11 @@ __device__ __forceinline__ void head_cta_rows(long long np, long long& r_begin, 
   r_end = units * (blockIdx.x + 1) / gridDim.x * 4;
 }
 
+// Barrier 2 + tile over the three consumer warps of a 16-row tile.
+__device__ __forceinline__ void tile_sync(int tile) {
+  asm volatile("bar.sync %0, 96;" ::"r"(2 + tile) : "memory");
+}
+
 // One m16n8k16 tensor-core product on 8-bit integers: D = A B + C with A
 // 16 x 16 unsigned (a0: row g, a1: row g + 8; bytes k = 4t .. 4t + 3, g =
 // lane / 4, t = lane % 4), B 16 x 8 signed (b0: column g, rows k = 4t ..
@@ -272,8 +277,9 @@ __device__ __forceinline__ int sext_byte(uint32_t w, int b) {
 // weights of each group; code - 32 is formed by the accumulator input
 // C = -32 sum e over the group.
 __device__ __forceinline__ void q6_superblock(const uint8_t* st, int row, int rot_a, int rot_b,
-                                              int sb, int lane, const Q6Smem& sm, int (&acc)[4]) {
-  const int t = lane & 3, gcol = lane >> 2;
+                                              int sb, int lane, const Q6Smem& sm,
+                                              const uint32_t (&breg)[16], int (&acc)[4]) {
+  const int t = lane & 3;
   const uint32_t* qlw = reinterpret_cast<const uint32_t*>(st);
   const uint32_t* qhw = reinterpret_cast<const uint32_t*>(st + kQ6StQl);
   const uint4* scw = reinterpret_cast<const uint4*>(st + kQ6StQl + kQ6StQh);
@@ -304,7 +310,7 @@ __device__ __forceinline__ void q6_superblock(const uint8_t* st, int row, int ro
         const uint32_t wa = (c & 1) ? w1a : w0a, wb = (c & 1) ? w1b : w0b;
         const uint32_t qa = ((wa >> (4 * (c >> 1))) & 0x0F0F0F0Fu) | (((ha >> (2 * c)) & 0x03030303u) << 4);
         const uint32_t qb = ((wb >> (4 * (c >> 1))) & 0x0F0F0F0Fu) | (((hb >> (2 * c)) & 0x03030303u) << 4);
-        const uint32_t b0 = sm.dig[chunk][gcol][t];
+        const uint32_t b0 = breg[g];
         const int2 cc = *reinterpret_cast<const int2*>(&sm.ncorr[chunk][2 * t]);
         int d[4];
         mma_u8s8_m16n8k16(d, qa, qb, b0, cc.x, cc.y);
@@ -330,7 +336,7 @@ __global__ void __launch_bounds__(kQ6Threads, 1) lm_head_kernel(const HeadParams
   if (tid == 0) {
     for (int s = 0; s < kQ6Stages; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 1);
+      mbar_init(&sm.empty[s], kQ6StageRows / 16);  // one arrival per 16-row tile
     }
     fence_barrier_init();
   }
@@ -474,6 +480,12 @@ __global__ void __launch_bounds__(kQ6Threads, 1) lm_head_kernel(const HeadParams
   // 2 (w % 3) and 2 (w % 3) + 1; lane (g, t) rows g and g + 8 of those.
   const int tile = warp / 3, pair = warp % 3, t = lane & 3;
   const int row = 16 * tile + (lane >> 2);
+  // The warp's two superblocks never change: their B operands stay in registers.
+  uint32_t breg[2][16];
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int g = 0; g < 16; ++g) breg[q][g] = sm.dig[(2 * pair + q) * 16 + g][lane >> 2][t];
   float best_v = kNoPick;
   int best_i = 0;
   bool ok = true;
@@ -495,7 +507,7 @@ __global__ void __launch_bounds__(kQ6Threads, 1) lm_head_kernel(const HeadParams
       for (int q = 0; q < 2; ++q) {
         const int sb = 2 * pair + q;
         int acc[4] = {0, 0, 0, 0};
-        q6_superblock(st, row, rot_a, rot_b, sb, lane, sm, acc);
+        q6_superblock(st, row, rot_a, rot_b, sb, lane, sm, breg[q], acc);
         // K1, K2 sit in the lanes t == 0 (columns 0, 1), K3 in t == 1 (column 2).
         const int k3a = __shfl_down_sync(0xffffffffu, acc[0], 1);
         const int k3b = __shfl_down_sync(0xffffffffu, acc[2], 1);
@@ -513,17 +525,23 @@ __global__ void __launch_bounds__(kQ6Threads, 1) lm_head_kernel(const HeadParams
         part[row + 8] = term_b;
       }
     }
-    consumers_sync<kQ6Warps>();  // every pair's terms of the stage are in place
-    if (tid == 0) head_arrive(&sm.empty[s]);
-    if (tid < kQ6StageRows && tid < nr && r0 + tid < r_stop && ok) {
-      const float* pk = sm.part[k & 1][0];
-      const float v = __fadd_rn(__fadd_rn(pk[tid], pk[kQ6StageRows + tid]),
-                                pk[2 * kQ6StageRows + tid]);
-      if (p.logits) p.logits[r0 + tid] = v;
-      // rows rise within a thread (stages in order): the first maximum stays
-      if (v > best_v) {
-        best_v = v;
-        best_i = (int)(r0 + tid);
+    // The tile's three warps have their terms in place (and have read the
+    // stage); the last pair's warp sums its tile's rows and frees the stage
+    // for this tile.
+    tile_sync(tile);
+    if (pair == 2) {
+      if (lane == 0) head_arrive(&sm.empty[s]);
+      const int j = 16 * tile + lane;
+      if (lane < 16 && j < nr && r0 + j < r_stop && ok) {
+        const float* pk = sm.part[k & 1][0];
+        const float v = __fadd_rn(__fadd_rn(pk[j], pk[kQ6StageRows + j]),
+                                  pk[2 * kQ6StageRows + j]);
+        if (p.logits) p.logits[r0 + j] = v;
+        // rows rise within a lane (stages in order): the first maximum stays
+        if (v > best_v) {
+          best_v = v;
+          best_i = (int)(r0 + j);
+        }
       }
     }
   }
