@@ -938,7 +938,11 @@ def run_batched(args, g, ctx, rank, world, local):
         n_all, window, t_max = wl["seqs"], wl["window"], wl["t_max"]
         lens_all = [t_max - window] * n_all
     # Sequences are dealt to ranks (longest first to the least-loaded rank).
-    mine = g.shard.plan_sequence_shards(lens_all, world)[rank]
+    # --share-of W (one process): time the share rank 0 gets at W ranks.
+    if args.share_of > 1 and world == 1:
+        mine = g.shard.plan_sequence_shards(lens_all, args.share_of)[0]
+    else:
+        mine = g.shard.plan_sequence_shards(lens_all, world)[rank]
     lens0 = [lens_all[i] for i in mine]
     n = len(lens0)
     k = torch.empty((n, 2, t_max, D), device="cuda")
@@ -973,21 +977,26 @@ def run_batched(args, g, ctx, rank, world, local):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
-    # The K timed steps as one CUDA graph (lengths reset at its start, advanced
-    # by one after every step): replays are not bound by the host's launch rate
-    # when a GPU's share of the batch is small.
-    if args.steps > window:
-        raise SystemExit(f"batched: --steps must be at most the window of {window}")
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        cap = torch.cuda.current_stream()
-        for i in range(args.steps):
-            step(i, cap)
-    graph.replay()
-    torch.cuda.synchronize()
+    # The K timed steps as CUDA graphs of at most one window of steps each
+    # (lengths reset at a graph's start, advanced by one after every step):
+    # replays are not bound by the host's launch rate when a GPU's share of
+    # the batch is small.  K = full * window + rem.
+    def capture(n_steps):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            cap = torch.cuda.current_stream()
+            for i in range(n_steps):
+                step(i, cap)
+        gr.replay()
+        torch.cuda.synchronize()
+        return gr
+
+    full, rem = divmod(args.steps, window)
+    graphs = ([capture(window)] * full) + ([capture(rem)] if rem else [])
 
     def body():
-        graph.replay()
+        for gr in graphs:
+            gr.replay()
 
     with ClockSampler(local) as clk:
         rounds = timed_rounds(body, world, stream)
@@ -1009,7 +1018,7 @@ def run_batched(args, g, ctx, rank, world, local):
     status = ctx.device_status()
     if status != 0:
         raise RuntimeError(f"device status {status}")
-    del graph
+    del graphs
     return dict(t=t_local, t_e2e=t_e2e, bytes=total_bytes,
                 clocks=clk.summary(), launches=2 * args.steps, launches_per_step=2,
                 h2d=n * QKV_W * 4, d2h=n * OUT_W * 4, tokens=n * args.steps,
@@ -1249,7 +1258,8 @@ def run_ours(args):
             line["extra"] = extra
         if k_nondefault(args):  # tuning knobs away from the library's defaults
             line["tuning"] = {"kernel_variant": args.variant, "target_ctas": args.target_ctas,
-                              "batch_chunk": args.batch_chunk, "grid_merge": args.grid_merge}
+                              "batch_chunk": args.batch_chunk, "grid_merge": args.grid_merge,
+                              "share_of": args.share_of}
         print(json.dumps(line), flush=True)
     ctx.close()
     if world > 1:
@@ -1259,7 +1269,8 @@ def run_ours(args):
 
 
 def k_nondefault(args):
-    return (args.variant >= 0 or args.target_ctas or args.batch_chunk or not args.grid_merge)
+    return (args.variant >= 0 or args.target_ctas or args.batch_chunk or not args.grid_merge
+            or args.share_of > 1)
 
 
 def run_extra(args, g, name, rank, world, local):
@@ -1374,6 +1385,7 @@ def main():
     ap.add_argument("--variant", type=int, default=-1, help=argparse.SUPPRESS)
     ap.add_argument("--target-ctas", type=int, default=0, help=argparse.SUPPRESS)
     ap.add_argument("--batch-chunk", type=int, default=0, help=argparse.SUPPRESS)
+    ap.add_argument("--share-of", type=int, default=0, help=argparse.SUPPRESS)
     ap.add_argument("--grid-merge", type=int, default=1, help=argparse.SUPPRESS)
     ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer", help=argparse.SUPPRESS)
     args = ap.parse_args()

@@ -308,23 +308,22 @@ int plan_splits_grid(const gqa_ctx* c, int rows_kv, int len) {
   return want >= 6 ? want : 0;
 }
 
-// Rows per split of a batched decode.  Up to 8192 rows: 512-row splits while
-// the batch still yields 1.5 waves of CTAs with them (a sequence's rows
-// averaging half the longest's), else 256 (a small batch needs the CTAs).
-// Measured, 64 sequences of U[256, 8192] rows dealt to 1/2/4/8 GPUs (one
-// GPU's share): 512 rows 101.7 / 55.7 / 30.2 / 27.9 us per step, 256 rows
-// 109.2 / 61.8 / 33.8 / 20.1 us.
+// Rows per split of a batched decode, by how many waves of CTAs the batch
+// yields (a sequence's rows estimated at half the longest's): 1024 while that
+// still gives two waves, else 512 while it gives 1.5, else 256 (a small batch
+// needs the CTAs).  Measured, 64 sequences of U[256, 8192] rows plus a
+// 256-step window dealt to 1/2/4/8 GPUs (one GPU's share, us per step):
+// 1024 rows 99.8 / 52.3 / 47.3 / 45.5, 512 rows 105.9 / 55.0 / 30.1 / 27.8,
+// 256 rows 112.7 / 60.9 / 33.8 / 20.0.
 int batch_chunk(const gqa_ctx* c, int n_seq, int max_len) {
   const int q = decode_variant_quant(batch_variant(c));
   int want = c->batch_chunk;
   if (want <= 0) {
-    if (max_len > 8192) {
-      want = 1024;
-    } else {
-      const long long ctas512 =
-          (long long)n_seq * c->cfg.n_heads_kv * ceil_div(max_len, 2 * 512);
-      want = 2 * ctas512 >= 3LL * c->n_sm ? 512 : 256;
-    }
+    const auto ctas = [&](int rows) {
+      return (long long)n_seq * c->cfg.n_heads_kv * ceil_div(max_len, 2 * rows);
+    };
+    const long long sms = c->n_sm;
+    want = ctas(1024) >= 2 * sms ? 1024 : 2 * ctas(512) >= 3 * sms ? 512 : 256;
   }
   const int least = ceil_div(max_len, kMergeMaxParts);  // at most kMergeMaxParts splits
   if (want < least) want = least;
