@@ -100,8 +100,12 @@ def measured_peak():
         return HBM_FALLBACK, "fallback"
 
 
-def profile_traffic(workload):
-    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary."""
+def profile_traffic(workload, alg_bytes=None, scale=1.0):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary.
+    Where the summary also gives the algorithmic bytes of the captured launch
+    (`algorithmic_bytes_per_launch`, a sharded workload captured on one GPU),
+    the traffic is scaled to this run's launch by `alg_bytes` / that figure;
+    `scale` multiplies it otherwise (prefill: the share of the sequences)."""
     path = os.path.join(REPO, "profiles", f"traffic_{workload}.txt")
     try:
         vals = {}
@@ -109,7 +113,10 @@ def profile_traffic(workload):
             if "=" in line and not line.startswith("#"):
                 k, v = line.split("=", 1)
                 vals[k.strip()] = v.strip()
-        return float(vals["bytes_per_launch"])
+        traffic = float(vals["bytes_per_launch"])
+        if "algorithmic_bytes_per_launch" in vals and alg_bytes:
+            return round(traffic * alg_bytes / float(vals["algorithmic_bytes_per_launch"]))
+        return round(traffic * scale)
     except Exception:
         return None
 
@@ -1242,7 +1249,7 @@ def run_ours(args):
                          "algorithmic_bytes_per_launch": round(per_gpu_bytes),
                          "duration_us": round(per_gpu_bytes / achieved / 1e3, 3),
                          "duration_basis": basis,
-                         "traffic": profile_traffic(args.workload)},
+                         "traffic": profile_traffic(args.workload, per_gpu_bytes)},
             "timing": {"rounds": r.get("rounds", 1), "timed_s": round(r.get("timed_s", t), 4),
                        "statistic": "median over rounds of the K timed steps (each round "
                                     "barrier + synchronize on both sides, max over ranks); "
@@ -1354,7 +1361,7 @@ def report_prefill(args, r, ctx, rank, world):
                          "peak_source": src, "kernel": "prefill_attn_kernel (+ prep kernel)",
                          "algorithmic_flops_per_step": 4.0 * N_Q * D * 2048 * 2049 / 2 * 8,
                          "achieved_scope": "whole step (prep + attention kernels)",
-                         "traffic": profile_traffic("prefill")},
+                         "traffic": profile_traffic("prefill", scale=1.0 / world)},
             "e2e": {"value": round(flops / t_e2e / 1e12, 1), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
             "gpu_launches": r["launches"], "clocks": r["clocks"], "cpu_baseline": None,
