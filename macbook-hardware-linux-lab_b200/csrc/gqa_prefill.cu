@@ -279,6 +279,9 @@ __device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
 // across neighbouring threads.
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const PrefillPrepParams p) {
   const int unit = blockIdx.x, tile = blockIdx.y, seq = blockIdx.z, tid = threadIdx.x;
+  // The attention kernel may set itself up (barriers, tensor memory) while
+  // this grid finishes; it waits for all of it before it reads an image.
+  pdl_launch_dependents();
   const int width = (p.n_q + 2 * p.n_kv) * kHeadDim;
   const int n_tiles = p.S / kPT;
   const float* base = p.qkv + (long long)seq * p.seq_stride + (long long)tile * kPT * width +
@@ -522,6 +525,8 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // The images and the item counter come from the prep kernel before this one.
+  pdl_wait();
 
   if (warp == 8) {
     // ---- loader ----
@@ -908,8 +913,19 @@ cudaError_t launch_prefill(const float* qkv, long long seq_stride, int n_seq, in
   ap.sched = sched;
   const long long n_items = (long long)(S / kPT) * (n_q / 2) * n_seq;
   const int grid = (int)(n_items < n_sm ? n_items : n_sm);
-  prefill_attn_kernel<<<grid, kPrefillThreads, prefill_smem_bytes(), st>>>(ap);
-  return cudaGetLastError();
+  // Programmatic dependent launch on the prep kernel: the CTAs start as the
+  // prep grid drains and set themselves up before their dependency wait.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kPrefillThreads);
+  cfg.dynamicSmemBytes = prefill_smem_bytes();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prefill_attn_kernel, ap);
 }
 
 }  // namespace gqa
