@@ -58,3 +58,32 @@ def test_packed_sizes_edges(pkg):
     for n, padded in ((1, 4), (3, 4), (4, 4), (5, 8), (151936, 151936)):
         assert C.lm_head_packed_bytes(n) == padded * 1260
         assert C.lm_head_q8_0_packed_bytes(n) == padded * 952
+
+
+def test_batched_traffic_reference_bytes(pkg):
+    """The batched traffic file's algorithmic bytes: the 64 seeded lengths'
+    cache rows (one GPU holding them all) x 2048 B, a few steps into the window."""
+    lens = [int(x) for x in pkg.seeded.uniform_int(777, pkg.seeded.LENGTHS, 64, 256, 8192)]
+    vals = {}
+    for line in open(os.path.join(bench.REPO, "profiles", "traffic_batched.txt")):
+        if "=" in line and not line.startswith("#"):
+            k, v = line.split("=", 1)
+            vals[k.strip()] = float(v)
+    first = bench.ROW_BYTES * sum(lens)
+    alg = vals["algorithmic_bytes_per_launch"]
+    assert first <= alg <= first + 8 * 64 * bench.ROW_BYTES
+
+
+def test_traffic_scaled_to_a_share():
+    """A GPU's share of a sharded workload gets the one-GPU capture's traffic
+    scaled by its own algorithmic bytes (batched) or by the sequence share
+    (prefill); unsharded workloads keep the captured figure."""
+    full = bench.profile_traffic("batched")
+    alg = 542771200
+    assert bench.profile_traffic("batched", alg) == round(full)
+    assert bench.profile_traffic("batched", alg / 4) == round(full / 4)
+    pre = bench.profile_traffic("prefill")
+    assert bench.profile_traffic("prefill", scale=1 / 8) == round(pre / 8)
+    res = bench.profile_traffic("resident28")
+    assert bench.profile_traffic("resident28", 7.9e6) == res
+    assert bench.profile_traffic("no_such_workload", 1e6) is None
