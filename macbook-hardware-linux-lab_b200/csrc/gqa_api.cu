@@ -369,7 +369,8 @@ int check_kv(const gqa_ctx* c, const gqa_layer_kv* kv) {
 // One sequence: split kernel (+ combine when split), result to `out`.  When
 // the grid merge applies (and `grid_ok`), one launch does both.  The
 // attention blocks pass grid_ok = false: between the projections the split
-// kernel + combine measured faster (block28 339 vs 385 us per token).
+// kernel + combine measured faster (block28 332 vs 427 us per token, token28
+// 802 vs 895 us).
 int run_single(gqa_ctx* c, cudaStream_t st, const gqa_layer_kv* kv, const float* qkv,
                Lengths len, int plan_len, bool fused, float* out, bool pdl_first,
                bool lengths_stable, bool grid_ok = true) {
